@@ -1,0 +1,393 @@
+"""Benchmark of the SISA hot path on B200 (one JSON line on rank 0).
+
+Workload: SISA attention forward + backward including the fused preparation,
+B=8, T=4096, H=16, d_head 64, d_state 32, bf16 operands with fp32 g/F, from a fused projection
+``proj`` (B, T, NPAD) and forget logits ``z``. One step = sisa_prep_fwd, sisa_attn_fwd, sisa_attn_bwd,
+sisa_prep_bwd through the C ABI (the same calls the autograd wrapper makes), on buffers allocated
+once. Metric: TFLOP/s on the causal FLOP count, 1152 FLOP per causal (query, key) pair
+(fwd 2(2*64+32), bwd 2(5*64+3*32)). With N ranks each rank runs its own batch (weak scaling, no
+collective on the data path); ``value`` = all ranks' FLOPs / max-over-ranks time.
+
+``e2e``: the same step with host buffers: pinned proj/z/dy copied in, y/d_proj/dz/dlam copied out,
+inside the timed region.
+
+``--impl reference``: the reference's pure-PyTorch CPU algorithm (the oracle port) on the host cores,
+on a bounded sample of the same workload (a subset of (batch, head) units at the full T).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+B, T, H = 8, 4096, 16
+FLOP_PER_PAIR = 1152
+FWD_FLOP_PER_PAIR = 320
+METRIC = "SISA attn fwd+bwd TFLOP/s (T=4096 bf16)"
+
+
+def pairs(b, h, t):
+    return b * h * t * (t + 1) // 2
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("bf16_tflops", 1590.0), d.get("bf16_tflops_sustained", 1400.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 1400.0, 6650.0, "fallback"
+
+
+class Clocks:
+    """Samples nvidia-smi clocks / throttle reasons during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = Path(f"/tmp/sisa_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}",
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path.exists():
+            return None
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) == 7:
+                rows.append(parts)
+        if not rows:
+            return None
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i].lower() == "active"})
+        mx = float(rows[0][1]) if rows[0][1].replace(".", "").isdigit() else None
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def dist_setup(n):
+    if n <= 1 or int(os.environ.get("WORLD_SIZE", "1")) <= 1:
+        return 0, 1, 0
+    import datetime
+
+    import torch.distributed as dist
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return dist.get_rank(), dist.get_world_size(), local
+
+
+class Step:
+    """Buffers and the four C-ABI calls of one fused-layer forward + backward."""
+
+    def __init__(self, dev, b=B, t=T, h=H, seed=0):
+        from sisa_b200 import _lib, backends
+        from sisa_b200.kernels.fused import fused_layout
+
+        self.lib = _lib.load()
+        self._lib = _lib
+        self.dev, self.b, self.t, self.h = dev, b, t, h
+        off = fused_layout(h)
+        self.off = off
+        g = torch.Generator(device=dev).manual_seed(seed)
+        bf = dict(device=dev, dtype=torch.bfloat16)
+        f32 = dict(device=dev, dtype=torch.float32)
+        proj = torch.zeros((b, t, off["NPAD"]), **bf)
+        proj[..., :off["TH"]] = torch.randn((b, t, off["TH"]), generator=g, device=dev).to(torch.bfloat16)
+        proj[..., off["TH"]:off["A"]] = (torch.randn((b, t, h * 16), generator=g, device=dev) * 0.2).to(torch.bfloat16)
+        proj[..., off["A"]:off["NTOT"]] = (torch.randn((b, t, h), generator=g, device=dev) * 0.45 - 5).to(torch.bfloat16)
+        self.proj = proj
+        self.z = torch.randn((b, t, h), generator=g, device=dev) * 0.45 + 4
+        self.lam = torch.nn.functional.softplus(torch.full((h,), -1.0, **f32))
+        self.dy = torch.randn((b, t, h * 64), generator=g, device=dev).to(torch.bfloat16)
+        self.c_rot = torch.empty((b, h, t, 32), **bf)
+        self.b_rot = torch.empty((b, h, t, 32), **bf)
+        self.pos = torch.empty((b, h, t, 4), **f32)
+        self.tot = torch.empty(self.lib.sisa_prep_fwd_workspace(b, h, t), dtype=torch.uint8, device=dev)
+        self.o = torch.empty_strided((b, h, t, 64), (t * h * 64, 64, h * 64, 1), **bf)
+        self.lse = torch.empty((b, h, t), **f32)
+        self.o32 = torch.empty((b, h, t, 64), **f32)
+        self.dproj = torch.empty_like(proj)
+        self.dc = torch.empty((b, h, t, 32), **f32)
+        self.db = torch.empty((b, h, t, 32), **f32)
+        self.dg = torch.empty((b, h, t), **f32)
+        self.dF = torch.empty((b, h, t), **f32)
+        self.dlam = torch.empty((h,), **f32)
+        self.dz = torch.empty((b, t, h), **f32)
+        self.ws = torch.empty(self.lib.sisa_attn_bwd_workspace(b, h, t), dtype=torch.uint8, device=dev)
+        self.bt = torch.empty(self.lib.sisa_prep_bwd_workspace(b, h, t), dtype=torch.uint8, device=dev)
+        self.status = backends.status_word(dev)
+        heads = lambda x, c, w: x[..., c:c + h * w].view(b, t, h, w).transpose(1, 2)  # noqa: E731
+        do = self.dy.view(b, t, h, 64).transpose(1, 2)
+        tens = [heads(proj, off["Q"], 64), heads(proj, off["K"], 64), heads(proj, off["V"], 64), self.c_rot,
+                self.b_rot, self.o, do, heads(self.dproj, off["Q"], 64), heads(self.dproj, off["K"], 64),
+                heads(self.dproj, off["V"], 64), self.dc, self.db]
+        self.views = [_lib.view4(x) for x in tens]
+        self.refs = [_lib.vref(v) for v in self.views]
+        self.launches_per_step = 8   # prep: 2, attn fwd: 1, attn bwd: 3 (dq, dkv, dlam), prep bwd: 2
+
+    def prep_fwd(self, st):
+        L = self.lib
+        rc = L.sisa_prep_fwd(self.proj.data_ptr(), self.b, self.t, self.h, self.proj.stride(0), self.proj.stride(1),
+                             0, self.z.data_ptr(), self.z.stride(0), self.z.stride(1), self.c_rot.data_ptr(),
+                             self.b_rot.data_ptr(), self.pos.data_ptr(), self.tot.data_ptr(), self.status.data_ptr(), st)
+        self._lib.check(rc, "sisa_prep_fwd")
+
+    def attn_fwd(self, st):
+        r = self.refs
+        rc = self.lib.sisa_attn_fwd(r[0], r[1], r[2], r[3], r[4], self.pos.data_ptr(), self.lam.data_ptr(), self.b,
+                                    self.h, self.t, 0, r[5], self.lse.data_ptr(), self.o32.data_ptr(),
+                                    self.status.data_ptr(), st)
+        self._lib.check(rc, "sisa_attn_fwd")
+
+    def attn_bwd(self, st):
+        r = self.refs
+        rc = self.lib.sisa_attn_bwd(r[0], r[1], r[2], r[3], r[4], self.pos.data_ptr(), self.lam.data_ptr(), r[5],
+                                    r[6], self.lse.data_ptr(), self.o32.data_ptr(), self.b, self.h, self.t, 0, r[7],
+                                    r[8], r[9], r[10], r[11], self.dg.data_ptr(), self.dF.data_ptr(),
+                                    self.dlam.data_ptr(), self.ws.data_ptr(), self.status.data_ptr(), st)
+        self._lib.check(rc, "sisa_attn_bwd")
+
+    def prep_bwd(self, st):
+        rc = self.lib.sisa_prep_bwd(self.proj.data_ptr(), self.b, self.t, self.h, self.proj.stride(0),
+                                    self.proj.stride(1), 0, self.z.data_ptr(), self.z.stride(0), self.z.stride(1),
+                                    self.tot.data_ptr(), self.dc.data_ptr(), self.db.data_ptr(), self.dg.data_ptr(),
+                                    self.dF.data_ptr(), self.dproj.data_ptr(), self.dproj.stride(0),
+                                    self.dproj.stride(1), self.dz.data_ptr(), self.bt.data_ptr(),
+                                    self.status.data_ptr(), st)
+        self._lib.check(rc, "sisa_prep_bwd")
+
+    def run(self, st, ev=None):
+        if ev is None:
+            self.prep_fwd(st); self.attn_fwd(st); self.attn_bwd(st); self.prep_bwd(st)  # noqa: E702
+            return
+        ev[0].record(); self.prep_fwd(st)  # noqa: E702
+        ev[1].record(); self.attn_fwd(st)  # noqa: E702
+        ev[2].record(); self.attn_bwd(st)  # noqa: E702
+        ev[3].record(); self.prep_bwd(st)  # noqa: E702
+        ev[4].record()
+
+
+def run_cuda(args):
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    from sisa_b200 import backends
+
+    ok, why = backends.cuda_status(local)
+    if not ok:
+        raise RuntimeError(f"cuda kernels unavailable: {why}")
+    step = Step(dev, seed=1234 + rank)
+    stream = torch.cuda.current_stream(dev)
+    st = stream.cuda_stream
+    for _ in range(args.warmup):
+        step.run(st)
+    torch.cuda.synchronize(dev)
+    backends.check_status(dev)
+    # ---- timed region: K steps, per-call events on the launching stream
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.steps)]
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        start.record()
+        for k in range(args.steps):
+            step.run(st, evs[k])
+        end.record()
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    ms = start.elapsed_time(end)
+    per = {name: statistics.mean(e[i].elapsed_time(e[i + 1]) for e in evs)
+           for i, name in enumerate(["prep_fwd", "attn_fwd", "attn_bwd", "prep_bwd"])}
+    backends.check_status(dev)
+    ms_t = torch.tensor([ms], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    total_flop = FLOP_PER_PAIR * pairs(B, H, T) * args.steps * world
+    value = total_flop / (ms_max * 1e-3) / 1e12
+
+    # ---- e2e: host buffers in and out through the same C-ABI calls
+    e2e = run_e2e(step, dev, args, world)
+
+    if rank == 0:
+        burst, sustained, hbm, src = measured_peaks()
+        att_ms = per["attn_fwd"] + per["attn_bwd"]
+        ach = FLOP_PER_PAIR * pairs(B, H, T) / (att_ms * 1e-3) / 1e12
+        prep_bytes = 302 * B * T * H
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "cfg1: fused prep + SISA attention fwd+bwd (sisa_fused step)", "B": B, "T": T,
+                       "H": H, "d_head": 64, "d_state": 32, "parallelism": f"replicas x{world} (per-rank batch)",
+                       "l2": "inputs larger than L2 (proj %.0f MB)" % (step.proj.numel() * 2 / 1e6),
+                       "flop_per_pair": FLOP_PER_PAIR},
+            "roofline": {"kernel": "sisa_attn_fwd + sisa_attn_bwd (tcgen05)", "bound": "tensor",
+                         "achieved": round(ach, 3), "peak": burst, "unit": "TFLOP/s", "frac": round(ach / burst, 4),
+                         "peak_source": f"{src} bf16 burst", "traffic": None,
+                         "per_call_ms": {k: round(v, 4) for k, v in per.items()},
+                         "attn_fwd_tflops": round(FWD_FLOP_PER_PAIR * pairs(B, H, T) / (per["attn_fwd"] * 1e-3) / 1e12, 3),
+                         "attn_bwd_tflops": round((FLOP_PER_PAIR - FWD_FLOP_PER_PAIR) * pairs(B, H, T) /
+                                                  (per["attn_bwd"] * 1e-3) / 1e12, 3),
+                         "prep_fwd_gbs": round(prep_bytes / (per["prep_fwd"] * 1e-3) / 1e9, 1),
+                         "hbm_peak_gbs": hbm},
+            "e2e": e2e,
+            "gpu_launches": step.launches_per_step * args.steps,
+            "clocks": clk.summary(),
+        }
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args.cpu_sample_heads)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def run_e2e(step, dev, args, world):
+    hp = step.proj.cpu().pin_memory()
+    hz = step.z.cpu().pin_memory()
+    hdy = step.dy.cpu().pin_memory()
+    out_dproj = torch.empty(step.dproj.shape, dtype=step.dproj.dtype, pin_memory=True)
+    out_y = torch.empty((B, T, H * 64), dtype=torch.bfloat16, pin_memory=True)
+    out_dz = torch.empty(step.dz.shape, dtype=torch.float32, pin_memory=True)
+    out_dlam = torch.empty((H,), dtype=torch.float32, pin_memory=True)
+    st = torch.cuda.current_stream(dev).cuda_stream
+    y_view = step.o.transpose(1, 2).reshape(B, T, H * 64)   # view of o's (B, T, H, 64) storage
+
+    def one():
+        step.proj.copy_(hp, non_blocking=True)
+        step.z.copy_(hz, non_blocking=True)
+        step.dy.copy_(hdy, non_blocking=True)
+        step.run(st)
+        out_y.copy_(y_view, non_blocking=True)
+        out_dproj.copy_(step.dproj, non_blocking=True)
+        out_dz.copy_(step.dz, non_blocking=True)
+        out_dlam.copy_(step.dlam, non_blocking=True)
+
+    n = max(1, min(args.steps, 5))
+    for _ in range(2):
+        one()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(n):
+        one()
+    e.record()
+    torch.cuda.synchronize(dev)
+    ms = torch.tensor([s.elapsed_time(e)], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+    ms = float(ms.item())
+    h2d = hp.numel() * 2 + hz.numel() * 4 + hdy.numel() * 2
+    d2h = out_y.numel() * 2 + out_dproj.numel() * 2 + out_dz.numel() * 4 + out_dlam.numel() * 4
+    v = FLOP_PER_PAIR * pairs(B, H, T) * n * world / (ms * 1e-3) / 1e12
+    return {"value": round(v, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": round(ms / n, 3), "steps": n}
+
+
+def cpu_step(heads, seed=0):
+    """One fwd+bwd of the reference's pure-PyTorch algorithm (oracle port, fp32) on B=1, `heads` heads, T=4096."""
+    from oracle import sisa_oracle as O
+
+    proj, z, lam = O.make_proj_inputs(1, T, heads, seed=seed)
+    P = proj.requires_grad_(True)
+    Z = z.requires_grad_(True)
+    LAM = lam.clone().requires_grad_(True)
+    y, _, _ = O.fused_layer(P, Z, LAM, heads, dtype=torch.float32)
+    y.backward(torch.ones_like(y))
+    return FLOP_PER_PAIR * pairs(1, heads, T)
+
+
+def cpu_baseline(heads):
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cpu_step(heads, seed=1)
+    t0 = time.perf_counter()
+    n = 2
+    flop = 0
+    for i in range(n):
+        flop += cpu_step(heads, seed=2 + i)
+    dt = time.perf_counter() - t0
+    return {"value": round(flop / dt / 1e12, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{n} steps of B=1 x H={heads} heads at T=4096 (1/{B * H // heads} of a cfg1 step), fp32, "
+                      f"{dt:.1f} s"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    heads = args.cpu_sample_heads
+    for _ in range(args.warmup):
+        cpu_step(heads, seed=0)
+    t0 = time.perf_counter()
+    flop = 0
+    for k in range(args.steps):
+        flop += cpu_step(heads, seed=1 + k)
+    dt = time.perf_counter() - t0
+    value = flop / dt / 1e12
+    line = {"metric": METRIC, "value": round(value, 5), "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "cfg1: fused prep + SISA attention fwd+bwd (sisa_fused step)", "B": B, "T": T,
+                       "H": H, "d_head": 64, "d_state": 32},
+            "cpu_baseline": {"value": round(value, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                             "sample": f"each step B=1 x H={heads} at T=4096, fp32 pure-PyTorch CPU algorithm"},
+            "e2e": {"value": round(value, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
+    ap.add_argument("--cpu-sample-heads", type=int, default=4)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_cuda(args)
+
+
+if __name__ == "__main__":
+    main()

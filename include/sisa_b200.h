@@ -1,0 +1,128 @@
+/* sisa_b200.h - C ABI of the B200 (sm_100a) SISA hot path.
+ *
+ * Every entry point takes raw device pointers, int64 shapes and element strides, a cudaStream_t
+ * (passed as void*) and a device int32 status word, and returns an int error code (SISA_OK = 0).
+ * Nothing in this library allocates device memory, synchronises the host or throws across the
+ * ABI: the caller owns every output and workspace buffer, and the work is ordered only by the
+ * stream that is passed in. Kernels never trap; run-time conditions are OR-ed into *status
+ * (SISA_ST_* bits) and left for the caller to read.
+ *
+ * Reference interfaces (tlstngud/sisa, paths inside that project) that each entry point
+ * replaces are cited beside it.
+ */
+#ifndef SISA_B200_H
+#define SISA_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- device status bits (OR-ed into the caller's int32 status word) ---- */
+#define SISA_ST_NONFINITE   1  /* NaN/inf reached a score, lse or a block total (fused_prep.py:502-523) */
+#define SISA_ST_NONMONOTONE 2  /* g rose by more than 1e-3 between neighbours (attention.py:123-125,675-683) */
+#define SISA_ST_TIMEOUT     4  /* a bounded device wait gave up; results are invalid */
+#define SISA_ST_BAD_SEED    8  /* linear-CE backward seed differs from the promised grad_scale (linear_ce.py:202-206) */
+
+/* ---- return codes ---- */
+#define SISA_OK              0
+#define SISA_ERR_VALUE       1  /* shape / layout / argument error (Python: ValueError) */
+#define SISA_ERR_TYPE        2  /* dtype error (Python: TypeError) */
+#define SISA_ERR_ALIGN       3  /* pointer or stride alignment the kernels cannot take (ValueError) */
+#define SISA_ERR_CUDA        4  /* a CUDA runtime/driver call failed (RuntimeError) */
+#define SISA_ERR_UNSUPPORTED 5  /* device is not sm_100 (RuntimeError) */
+
+/* ---- element types of low-precision operands ---- */
+#define SISA_BF16 0
+#define SISA_F16  1
+
+/* A (B, H, L, X) view: element strides of the first three axes; the last axis is contiguous. */
+typedef struct sisa_view4 {
+  void* data;
+  int64_t stride_b;
+  int64_t stride_h;
+  int64_t stride_l;
+} sisa_view4;
+
+/* Library version string and the message of the last error returned on this host thread. */
+const char* sisa_version(void);
+const char* sisa_last_error(void);
+
+/* 0 when `device` is an sm_100 GPU this library was built for (else SISA_ERR_UNSUPPORTED). */
+int sisa_device_check(int device);
+
+/* Column layout of the fused projection for n_head heads (d_head 64, d_state 32):
+ * out[0..8] = start columns Q, K, V, B, C, TH, A, then NTOT and NPAD.
+ * Replaces sisa.kernels.fused_prep.fused_layout (src/sisa/kernels/fused_prep.py:71-96). */
+int sisa_fused_layout(int64_t n_head, int64_t* out9);
+
+/* Workspace sizes in bytes for the entry points below (caller allocates; 256-byte aligned). */
+int64_t sisa_prep_fwd_workspace(int64_t B, int64_t H, int64_t L);   /* block totals, fp32 */
+int64_t sisa_prep_bwd_workspace(int64_t B, int64_t H, int64_t L);   /* block totals, fp64 */
+int64_t sisa_attn_bwd_workspace(int64_t B, int64_t H, int64_t L);   /* per-row statistics */
+
+/* Fused preparation, forward (src/sisa/kernels/fused_prep.py:247-352, launched at :527-564):
+ *   g = cumsum(-softplus(alpha)), F = cumsum(logsigmoid(z)), Phi = cumsum(theta),
+ *   c_rot/b_rot = pair rotation R(Phi) of the C/B columns (fp32 math, one rounding).
+ * proj: (B, L, NPAD) in `dtype` with element strides proj_sb, proj_sl (column stride 1).
+ * z: (B, L, H) fp32 with strides z_sb, z_sl (head stride 1), or NULL for no forget gate.
+ * c_rot, b_rot: (B, H, L, 32) contiguous, `dtype`.
+ * pos: (B, H, L, 4) fp32 contiguous, per position {g, F, rowf, colf} where rowf/colf are the
+ *   decay factors relative to the start/end of the position's 64-row block.
+ * workspace: sisa_prep_fwd_workspace(B, H, L) bytes. */
+int sisa_prep_fwd(const void* proj, int64_t B, int64_t L, int64_t H, int64_t proj_sb, int64_t proj_sl,
+                  int dtype, const float* z, int64_t z_sb, int64_t z_sl,
+                  void* c_rot, void* b_rot, float* pos, void* workspace,
+                  int32_t* status, void* stream);
+
+/* Position records for the unfused entry point (src/sisa/kernels/attention.py:129-153):
+ * pos = {g, fgate (0 if NULL), rowf, colf} from g (B, H, L) and fgate (B, H, L) fp32 with the
+ * given element strides; sets SISA_ST_NONMONOTONE when g rises by more than 1e-3. */
+int sisa_pack_positions(const float* g, int64_t g_sb, int64_t g_sh, int64_t g_sl,
+                        const float* fgate, int64_t f_sb, int64_t f_sh, int64_t f_sl,
+                        int64_t B, int64_t H, int64_t L, float* pos, int32_t* status, void* stream);
+
+/* Exact SISA attention forward on tcgen05 (src/sisa/kernels/attention.py:177-296, host 686-727):
+ *   s_ij = q_i.k_j/8 + lam_h exp(g_i-g_j) (c_i.b_j) + (F_i - F_j), j <= i;  o = softmax(s) v.
+ * q, k, v: (B, H, L, 64) views in `dtype`; c, b: (B, H, L, 32) views in `dtype`.
+ * pos: (B, H, L, 4) from sisa_prep_fwd / sisa_pack_positions. lam: (H,) fp32.
+ * o: (B, H, L, 64) view in `dtype`. lse: (B, H, L) fp32 contiguous, log2 units.
+ * o32: (B, H, L, 64) fp32 contiguous self-normalised output for the exact-delta backward,
+ *   or NULL when no backward follows. All views: 16-byte aligned rows, strides multiple of 8. */
+int sisa_attn_fwd(const sisa_view4* q, const sisa_view4* k, const sisa_view4* v,
+                  const sisa_view4* c, const sisa_view4* b, const float* pos, const float* lam,
+                  int64_t B, int64_t H, int64_t L, int dtype,
+                  const sisa_view4* o, float* lse, float* o32, int32_t* status, void* stream);
+
+/* Exact-delta backward on tcgen05 (src/sisa/kernels/attention.py:300-663, host 730-784):
+ * dq, dk, dv: (B, H, L, 64) views in `dtype` (may alias columns of a fused d_proj);
+ * dc, db: (B, H, L, 32) fp32 views; dg, dF: (B, H, L) fp32 contiguous (dF may be NULL when
+ * the forward had no forget gate); dlam: (H,) fp32, summed in fp64 and rounded once.
+ * workspace: sisa_attn_bwd_workspace(B, H, L) bytes. Deterministic (no atomics on data). */
+int sisa_attn_bwd(const sisa_view4* q, const sisa_view4* k, const sisa_view4* v,
+                  const sisa_view4* c, const sisa_view4* b, const float* pos, const float* lam,
+                  const sisa_view4* o, const sisa_view4* dout, const float* lse, const float* o32,
+                  int64_t B, int64_t H, int64_t L, int dtype,
+                  const sisa_view4* dq, const sisa_view4* dk, const sisa_view4* dv,
+                  const sisa_view4* dc, const sisa_view4* db, float* dg, float* dF, float* dlam,
+                  void* workspace, int32_t* status, void* stream);
+
+/* Fused preparation, backward (src/sisa/kernels/fused_prep.py:385-494, launched at :622-633):
+ * reverse scans in fp64 -> d alpha, dz, d theta; inverse rotation of dc/db; zero padding columns.
+ * dproj: (B, L, NPAD) `dtype` with strides dproj_sb, dproj_sl; only the B, C, TH, A and padding
+ * columns are written here (the Q, K, V columns come from sisa_attn_bwd).
+ * dc, db: (B, H, L, 32) fp32 contiguous; dg, dF: (B, H, L) fp32 (dF NULL without z).
+ * dz: (B, L, H) fp32 contiguous (ignored without z). tot: the forward's workspace (block totals).
+ * workspace: sisa_prep_bwd_workspace(B, H, L) bytes. */
+int sisa_prep_bwd(const void* proj, int64_t B, int64_t L, int64_t H, int64_t proj_sb, int64_t proj_sl,
+                  int dtype, const float* z, int64_t z_sb, int64_t z_sl, const void* tot,
+                  const float* dc, const float* db, const float* dg, const float* dF,
+                  void* dproj, int64_t dproj_sb, int64_t dproj_sl, float* dz,
+                  void* workspace, int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SISA_B200_H */

@@ -1,0 +1,130 @@
+"""ctypes binding of ``libsisa_b200.so`` (declared in ``include/sisa_b200.h``).
+
+The library is loaded on first use. If it has not been built, every CUDA entry point raises
+``RuntimeError``: there is no fallback implementation behind this module.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+_LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libsisa_b200.so"
+_LOCK = threading.Lock()
+_LIB = None
+
+# return codes / status bits (sisa_b200.h)
+OK, ERR_VALUE, ERR_TYPE, ERR_ALIGN, ERR_CUDA, ERR_UNSUPPORTED = 0, 1, 2, 3, 4, 5
+ST_NONFINITE, ST_NONMONOTONE, ST_TIMEOUT, ST_BAD_SEED = 1, 2, 4, 8
+BF16, F16 = 0, 1
+
+
+class View4(ctypes.Structure):
+    """``sisa_view4``: a (B, H, L, X) view with element strides of the first three axes."""
+
+    _fields_ = [("data", ctypes.c_void_p), ("stride_b", ctypes.c_int64), ("stride_h", ctypes.c_int64),
+                ("stride_l", ctypes.c_int64)]
+
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I = ctypes.c_int
+_VP = ctypes.POINTER(View4)
+
+# name -> (restype, argtypes); every symbol declared in include/sisa_b200.h
+SIGNATURES = {
+    "sisa_version": (ctypes.c_char_p, []),
+    "sisa_last_error": (ctypes.c_char_p, []),
+    "sisa_device_check": (_I, [_I]),
+    "sisa_fused_layout": (_I, [_I64, ctypes.POINTER(_I64)]),
+    "sisa_prep_fwd_workspace": (_I64, [_I64, _I64, _I64]),
+    "sisa_prep_bwd_workspace": (_I64, [_I64, _I64, _I64]),
+    "sisa_attn_bwd_workspace": (_I64, [_I64, _I64, _I64]),
+    "sisa_prep_fwd": (_I, [_P, _I64, _I64, _I64, _I64, _I64, _I, _P, _I64, _I64, _P, _P, _P, _P, _P, _P]),
+    "sisa_pack_positions": (_I, [_P, _I64, _I64, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P]),
+    "sisa_attn_fwd": (_I, [_VP, _VP, _VP, _VP, _VP, _P, _P, _I64, _I64, _I64, _I, _VP, _P, _P, _P, _P]),
+    "sisa_attn_bwd": (_I, [_VP, _VP, _VP, _VP, _VP, _P, _P, _VP, _VP, _P, _P, _I64, _I64, _I64, _I,
+                           _VP, _VP, _VP, _VP, _VP, _P, _P, _P, _P, _P, _P]),
+    "sisa_prep_bwd": (_I, [_P, _I64, _I64, _I64, _I64, _I64, _I, _P, _I64, _I64, _P, _P, _P, _P, _P,
+                           _P, _I64, _I64, _P, _P, _P, _P]),
+    "sisa_lce_fwd_bwd": (_I, [_P, _I64, _I64, _P, _I64, _I64, _P, _I64, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "sisa_lce_workspace": (_I64, [_I64, _I64, _I64]),
+    "sisa_decode_attn": (_I, [_VP, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I, _P, _P,
+                              _P, _P]),
+    "sisa_decode_workspace": (_I64, [_I64, _I64, _I64]),
+}
+
+
+def lib_path() -> Path:
+    return _LIB_PATH
+
+
+def load():
+    """Load the shared library (once) and attach the prototypes. Raises RuntimeError if it is missing."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    with _LOCK:
+        if _LIB is not None:
+            return _LIB
+        if not _LIB_PATH.exists():
+            raise RuntimeError(f"{_LIB_PATH} is not built; run `python -m sisa_b200.build` (nvcc, sm_100a)")
+        lib = ctypes.CDLL(str(_LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name, None)
+            if fn is None:
+                continue
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = lib
+        return lib
+
+
+def exported_symbols() -> list[str]:
+    lib = load()
+    return [n for n in SIGNATURES if hasattr(lib, n)]
+
+
+def last_error() -> str:
+    return load().sisa_last_error().decode()
+
+
+def check(rc: int, what: str) -> None:
+    """Map a C return code to the reference's exception types."""
+    if rc == OK:
+        return
+    msg = f"{what}: {last_error()}"
+    if rc == ERR_TYPE:
+        raise TypeError(msg)
+    if rc in (ERR_VALUE, ERR_ALIGN):
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def view4(t: torch.Tensor) -> View4:
+    """View4 of a (B, H, L, X) tensor whose last axis is contiguous."""
+    if t.dim() != 4 or t.stride(-1) != 1:
+        raise ValueError(f"expected a 4-D tensor with a contiguous last axis, got {tuple(t.shape)} {t.stride()}")
+    return View4(t.data_ptr(), t.stride(0), t.stride(1), t.stride(2))
+
+
+def vref(v: View4):
+    return ctypes.byref(v)
+
+
+def stream_ptr(device: torch.device | None = None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    if dt == torch.bfloat16:
+        return BF16
+    if dt == torch.float16:
+        return F16
+    raise TypeError(f"the CUDA kernels take bf16 or fp16 operands, got {dt}")

@@ -1,0 +1,62 @@
+// Host-side launch parameters of the tcgen05 attention kernels.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace sisa {
+
+struct FwdParams {
+  CUtensorMap tm_q;    // (64, L, H, B) bf16/fp16, box (64, 128), 128B swizzle
+  CUtensorMap tm_k;    // box (64, 64)
+  CUtensorMap tm_v;    // box (64, 64)
+  CUtensorMap tm_c;    // (32, L, H, B), box (32, 128), 64B swizzle
+  CUtensorMap tm_b;    // box (32, 64)
+  CUtensorMap tm_pos;  // (4, L, B*H) fp32, box (4, 64, 1)
+  const float4* pos;
+  const float* lam;
+  char* o;
+  int64_t o_sb, o_sh, o_sl;
+  float* lse;
+  float* o32;
+  int B, H, L, ntq;
+  int32_t* status;
+};
+
+struct BwdParams {
+  // dq kernel (query-tile owner): Q, dO, C resident (box rows 128); K, V, B streamed (box rows 64)
+  CUtensorMap tm_q128, tm_do128, tm_c128, tm_k64, tm_v64, tm_b64;
+  // dkv kernel (key-tile owner): K, V, B resident (box rows 128); Q, dO, C streamed (box rows 64)
+  CUtensorMap tm_k128, tm_v128, tm_b128, tm_q64, tm_do64, tm_c64;
+  CUtensorMap tm_pos;    // (4, L, B*H) fp32, box (4, 64, 1)
+  CUtensorMap tm_rstat;  // (4, L, B*H) fp32, box (4, 64, 1): {lse, delta, T-delta, dS_tt}
+  const float4* pos;
+  const float* lam;
+  const char* q;  int64_t q_sb, q_sh, q_sl;
+  const char* k;  int64_t k_sb, k_sh, k_sl;
+  const char* bm; int64_t b_sb, b_sh, b_sl;
+  const char* o;  int64_t o_sb, o_sh, o_sl;
+  const char* dout; int64_t do_sb, do_sh, do_sl;
+  const float* lse;
+  const float* o32;
+  char* dq; int64_t dq_sb, dq_sh, dq_sl;
+  char* dk; int64_t dk_sb, dk_sh, dk_sl;
+  char* dv; int64_t dv_sb, dv_sh, dv_sl;
+  float* dc; int64_t dc_sb, dc_sh, dc_sl;
+  float* db; int64_t db_sb, db_sh, db_sl;
+  float* dg;
+  float* dF;
+  float4* rstat;   // (B*H, L)
+  float* rg;       // (B*H, L) row part of dg (times lambda)
+  float* rf;       // row part of dF
+  float* rl;       // per-row dlambda
+  float* dlam;
+  int B, H, L, ntq128, ntq64;
+  int has_f;
+  int32_t* status;
+};
+
+cudaError_t launch_attn_fwd(const FwdParams& p, int dtype, cudaStream_t st);
+cudaError_t launch_attn_bwd(const BwdParams& p, int dtype, cudaStream_t st);
+
+}  // namespace sisa

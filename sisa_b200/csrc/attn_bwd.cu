@@ -1,0 +1,721 @@
+// attn_bwd.cu - exact-delta SISA attention backward on Blackwell tensor cores.
+//
+// Reference semantics: src/sisa/kernels/attention.py:28-78 (numerics (D), (E)), 300-491 (_bwd_dq),
+// 495-663 (_bwd_dkv) and 781-783 (fp64 d lambda). Two kernels, no atomics on data (deterministic):
+//
+//  dq kernel (query-tile owner, 128 rows): recomputes S = QK^T, U = CB~^T, dP = dO V^T per 64-key tile,
+//    P = 2^(x - lse), the FlashAttention-standard dS^ = P (dP - delta'') with delta'' = do.o'' (the
+//    self-normalised fp32 forward output), and accumulates dQ += dS^ K and dC += (dS^ * colf mid) B~ in
+//    TMEM. It also accumulates the row sums of the exact-delta scheme (Z, D, P_tt, dP_tt, the
+//    u-weighted sums) and finishes every row: T^, the delta-free diagonal dS_tt, the row parts of
+//    dg, dF and d lambda, and the per-row statistics {lse, delta, T^-delta, dS_tt} read by the dkv kernel.
+//  dkv kernel (key-tile owner, 128 rows): recomputes S^T, U^T, dP^T per 64-query tile, uses
+//    dS = dS^' - P'(T^ - delta) for dK and the column sums of dg and dF, dS^' for dB (the same delta as
+//    dC, so the Phi_i - Phi_j cancellation of d theta holds), and the dq kernel's dS_tt on the diagonal.
+//
+// Both kernels: 8 compute warps (two warpgroups splitting each tile's 64 columns 32/32; thread =
+// TMEM lane = owned row), one TMA producer warp and one UMMA warp. Per tile the compute warps pull
+// S, U, dP into registers and release TMEM at once, so the next tile's GEMMs overlap their math;
+// the gradient GEMMs read bf16 operands the compute warps wrote to double-buffered, 128B-swizzled
+// shared memory.
+#include <cuda_runtime.h>
+
+#include "attn_common.cuh"
+#include "attn.h"
+
+namespace sisa {
+namespace bwd {
+
+constexpr int NST = 3;
+constexpr int NTHREADS = 320;    // warps 0-7 compute, 8 TMA, 9 MMA
+
+// ----------------------------------------------------------------------------- dq kernel layout
+namespace dqk {
+constexpr uint32_t SZ_Q = 128 * 128, SZ_DO = 128 * 128, SZ_C = 128 * 64;
+constexpr uint32_t SZ_K = 64 * 128, SZ_V = 64 * 128, SZ_B = 64 * 64, SZ_POS = 64 * 16;
+constexpr uint32_t SZ_STAGE = SZ_K + SZ_V + SZ_B + SZ_POS;   // 21504
+constexpr uint32_t SZ_OP = 128 * 128;                          // one 128 x 64 bf16 operand tile
+constexpr uint32_t OFF_Q = 0, OFF_DO = OFF_Q + SZ_Q, OFF_C = OFF_DO + SZ_DO, OFF_ST = OFF_C + SZ_C;
+constexpr uint32_t OFF_OP = OFF_ST + NST * SZ_STAGE;           // [buf][dS, dSC]
+constexpr uint32_t OFF_RED = OFF_OP + 4 * SZ_OP;               // 128 rows x 8 floats
+constexpr uint32_t OFF_BAR = OFF_RED + 128 * 8 * 4;
+constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr int COL_S = 0, COL_U = 64, COL_DP = 128, COL_DQ = 192, COL_DCO = 256, COL_DCD = 288;
+constexpr int B_KVF = 0, B_KVE = 3, B_Q = 6, B_SUF = 7, B_SUE = 8, B_OPF = 9, B_OPE = 11, B_ACC = 13;
+static_assert(OFF_ST % 1024 == 0 && OFF_OP % 1024 == 0, "alignment");
+}  // namespace dqk
+
+// ----------------------------------------------------------------------------- dkv kernel layout
+namespace dkv {
+constexpr uint32_t SZ_K = 128 * 128, SZ_V = 128 * 128, SZ_B = 128 * 64;
+constexpr uint32_t SZ_Q = 64 * 128, SZ_DO = 64 * 128, SZ_C = 64 * 64, SZ_POS = 64 * 16, SZ_RST = 64 * 16;
+constexpr uint32_t SZ_STAGE = SZ_Q + SZ_DO + SZ_C + SZ_POS + SZ_RST;   // 22528
+constexpr uint32_t SZ_OP = 128 * 128;
+constexpr uint32_t OFF_K = 0, OFF_V = OFF_K + SZ_K, OFF_B = OFF_V + SZ_V, OFF_ST = OFF_B + SZ_B;
+constexpr uint32_t OFF_OP = OFF_ST + NST * SZ_STAGE;                   // [buf][P, dS, dSb]
+constexpr uint32_t OFF_RED = OFF_OP + 6 * SZ_OP;                       // 128 rows x 4 floats
+constexpr uint32_t OFF_BAR = OFF_RED + 128 * 4 * 4;
+constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr int COL_S = 0, COL_U = 64, COL_DP = 128, COL_DV = 192, COL_DK = 256, COL_DBD = 320, COL_DBO = 352;
+constexpr int B_KVF = 0, B_KVE = 3, B_K = 6, B_SUF = 7, B_SUE = 8, B_OPF = 9, B_OPE = 11, B_ACC = 13;
+static_assert(OFF_ST % 1024 == 0 && SZ_STAGE % 1024 == 0 && OFF_OP % 1024 == 0, "alignment");
+}  // namespace dkv
+
+constexpr uint32_t TMEM_COLS = 512;
+
+// Write 32 low-precision values (this thread's half of a 64-column operand row) as 4 swizzled chunks.
+__device__ __forceinline__ void st_op_half(uint32_t tile, int row, int wg, const uint32_t* w) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    st_shared_v4(tile + sw128_off(row, wg * 4 + q), w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+}
+
+template <bool kHalf>
+__device__ __forceinline__ float ld_lp_g(const char* base, int64_t i) {
+  if constexpr (kHalf) return __half2float(reinterpret_cast<const __half*>(base)[i]);
+  else return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[i]);
+}
+
+// =============================================================================================
+// dq kernel
+// =============================================================================================
+template <bool kHalf>
+__global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_constant__ BwdParams p) {
+  using namespace dqk;
+  extern __shared__ uint8_t smem_raw[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qt = p.ntq128 - 1 - (int)blockIdx.x;
+  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const int L = p.L;
+  const int m0 = qt * 128;
+  const int ndiag = (m0 + 64 < L) ? 2 : 1;
+  const int ntiles = ndiag + m0 / 64;
+
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t sbase = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (sbase - raw);
+  const uint32_t bar0 = sbase + OFF_BAR;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + 128);
+#define BAR(i) (bar0 + 8u * (uint32_t)(i))
+  if (tid == 0) {
+    for (int s = 0; s < NST; ++s) { mbar_init(BAR(B_KVF + s), 1); mbar_init(BAR(B_KVE + s), 1); }
+    mbar_init(BAR(B_Q), 1);
+    mbar_init(BAR(B_SUF), 1);
+    mbar_init(BAR(B_SUE), 256);
+    for (int i = 0; i < 2; ++i) { mbar_init(BAR(B_OPF + i), 256); mbar_init(BAR(B_OPE + i), 1); }
+    mbar_init(BAR(B_ACC), 1);
+    fence_barrier_init();
+  }
+  if (warp == 9) { tmem_alloc(smem_u32(tmem_slot), TMEM_COLS); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  auto key0 = [&](int n) { return n < ndiag ? m0 + n * 64 : (n - ndiag) * 64; };
+  auto stage_addr = [&](int s) { return sbase + OFF_ST + (uint32_t)s * SZ_STAGE; };
+
+  if (warp == 8) {
+    if (lane == 0) {
+      mbar_expect_tx(BAR(B_Q), SZ_Q + SZ_DO + SZ_C);
+      tma_load_4d(sbase + OFF_Q, &p.tm_q128, BAR(B_Q), 0, m0, h, b);
+      tma_load_4d(sbase + OFF_DO, &p.tm_do128, BAR(B_Q), 0, m0, h, b);
+      tma_load_4d(sbase + OFF_C, &p.tm_c128, BAR(B_Q), 0, m0, h, b);
+      for (int n = 0; n < ntiles; ++n) {
+        const int s = n % NST;
+        if (n >= NST && !mbar_wait(BAR(B_KVE + s), ((n / NST) - 1) & 1, p.status)) break;
+        const int j0 = key0(n);
+        const uint32_t st = stage_addr(s);
+        mbar_expect_tx(BAR(B_KVF + s), SZ_STAGE);
+        tma_load_4d(st, &p.tm_k64, BAR(B_KVF + s), 0, j0, h, b);
+        tma_load_4d(st + SZ_K, &p.tm_v64, BAR(B_KVF + s), 0, j0, h, b);
+        tma_load_4d(st + SZ_K + SZ_V, &p.tm_b64, BAR(B_KVF + s), 0, j0, h, b);
+        tma_load_3d(st + SZ_K + SZ_V + SZ_B, &p.tm_pos, BAR(B_KVF + s), 0, j0, bh);
+      }
+    }
+  } else if (warp == 9) {
+    if (lane == 0) {
+      constexpr uint32_t fmt = kHalf ? 0 : 1;
+      constexpr uint32_t id_s = make_idesc(128, 64, fmt, 0, 0);
+      constexpr uint32_t id_dq = make_idesc(128, 64, fmt, 0, 1);
+      constexpr uint32_t id_dc = make_idesc(128, 32, fmt, 0, 1);
+      const uint32_t sQ = sbase + OFF_Q, sDO = sbase + OFF_DO, sC = sbase + OFF_C;
+      bool ok = mbar_wait(BAR(B_Q), 0, p.status);
+      int ndco = 0, ndcd = 0;   // GEMMs issued into dC_off / dC_diag so far
+      auto issue_grads = [&](int m) -> bool {
+        const int buf = m & 1, s = m % NST;
+        if (!mbar_wait(BAR(B_OPF + buf), (m >> 1) & 1, p.status)) return false;
+        tc_fence_after();
+        const uint32_t sDS = sbase + OFF_OP + (uint32_t)buf * 2 * SZ_OP, sDSC = sDS + SZ_OP;
+        const uint32_t st = stage_addr(s);
+        const bool dg = m < ndiag;
+        const uint32_t tdc = tbase + (dg ? COL_DCD : COL_DCO);
+        int& cnt = dg ? ndcd : ndco;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_ss(tbase + COL_DQ, desc_k128(sDS + k * 32), desc_mn128(st + k * 2048), id_dq, (m > 0 || k > 0));
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_ss(tdc, desc_k128(sDSC + k * 32), desc_mn64(st + SZ_K + SZ_V + k * 1024), id_dc, (cnt > 0 || k > 0));
+        ++cnt;
+        umma_commit(BAR(B_OPE + buf));
+        umma_commit(BAR(B_KVE + s));
+        return true;
+      };
+      for (int n = 0; ok && n < ntiles; ++n) {
+        const int s = n % NST;
+        if (!mbar_wait(BAR(B_KVF + s), (n / NST) & 1, p.status)) { ok = false; break; }
+        if (n > 0 && !mbar_wait(BAR(B_SUE), (n - 1) & 1, p.status)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t st = stage_addr(s);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) umma_ss(tbase + COL_S, desc_k128(sQ + k * 32), desc_k128(st + k * 32), id_s, k > 0);
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+          umma_ss(tbase + COL_U, desc_k64(sC + k * 32), desc_k64(st + SZ_K + SZ_V + k * 32), id_s, k > 0);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_ss(tbase + COL_DP, desc_k128(sDO + k * 32), desc_k128(st + SZ_K + k * 32), id_s, k > 0);
+        umma_commit(BAR(B_SUF));
+        if (n > 0 && !issue_grads(n - 1)) { ok = false; break; }
+      }
+      if (ok) issue_grads(ntiles - 1);
+      // The accumulator of a region that received no GEMM is never read (see the epilogue).
+      umma_commit(BAR(B_ACC));
+    }
+  } else {
+    // ------------------------------------------------------------------ compute warps 0-7
+    const int wg = warp >> 2, quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int row = m0 + r;
+    const bool vrow = row < L;
+    const int64_t rb = (int64_t)bh * L;
+    const float4 pi = p.pos[rb + (vrow ? row : L - 1)];
+    const float gi = pi.x, fi = pi.y;
+    const float ga = p.pos[rb + m0].x;
+    const float lam = p.lam[h];
+    const float rowf = exp2f(fminf((gi - ga) * kLOG2E, 0.f));
+    const float rs = lam * rowf;
+    const float rs2 = rs * kLOG2E;
+    const float lam2 = lam * kLOG2E;
+    const float c1 = kScale * kLOG2E;
+    const float lse = vrow ? p.lse[rb + row] : INFINITY;
+    float* red = reinterpret_cast<float*>(gbase + OFF_RED);
+    bool ok = warp_wait(BAR(B_Q), 0, p.status);
+    // delta'' = do . o'' over this warpgroup's 32 head dims (o'' snaps to the DT output where they agree
+    // to 2^-15, attention.py:341-350), combined across the two warpgroups.
+    float dh = 0.f;
+    if (ok && vrow) {
+      const char* orow = p.o + 2 * ((int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)row * p.o_sl);
+      const float* o32row = p.o32 ? p.o32 + (rb + row) * kD : nullptr;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int chunk = wg * 4 + q;
+        const uint4 dv = *reinterpret_cast<const uint4*>(gbase + OFF_DO + sw128_off(r, chunk));
+        const uint4 ov = *reinterpret_cast<const uint4*>(orow + chunk * 16);
+        const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w}, ow[4] = {ov.x, ov.y, ov.z, ov.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int d = chunk * 8 + 2 * i + e;
+            float o = e ? unpack_hi<kHalf>(ow[i]) : unpack_lo<kHalf>(ow[i]);
+            if (o32row) {
+              const float o3 = o32row[d];
+              o = (fabsf(o3 - o) <= 3.0517578125e-05f * fabsf(o)) ? o : o3;
+            }
+            const float dd = e ? unpack_hi<kHalf>(dw[i]) : unpack_lo<kHalf>(dw[i]);
+            dh = fmaf(o, dd, dh);
+          }
+        }
+      }
+    }
+    // wg 1 hands its partial to wg 0, which forms delta'' and hands it back (identical bits in both)
+    if (wg == 1) red[r * 8 + 7] = dh;
+    named_bar_sync(1, 256);
+    float dl = 0.f;
+    if (wg == 0) {
+      dl = dh + red[r * 8 + 7];
+      red[r * 8 + 6] = dl;
+    }
+    named_bar_sync(1, 256);
+    if (wg == 1) dl = red[r * 8 + 6];
+
+    const uint32_t tS = tmem_addr(tbase, quarter, COL_S + wg * 32);
+    const uint32_t tU = tmem_addr(tbase, quarter, COL_U + wg * 32);
+    const uint32_t tP = tmem_addr(tbase, quarter, COL_DP + wg * 32);
+    float za = 0.f, ya = 0.f, wa = 0.f, xa = 0.f, ptt = 0.f, dptt = 0.f, xd = 0.f, xo = 0.f, yo = 0.f;
+    for (int n = 0; ok && n < ntiles; ++n) {
+      const int s = n % NST;
+      const int j0 = key0(n) + wg * 32;
+      if (!warp_wait(BAR(B_SUF), n & 1, p.status)) { ok = false; break; }
+      tc_fence_after();
+      float sv[32], uv[32], pv[32];
+      tmem_ld32(tS, sv);
+      tmem_ld32(tU, uv);
+      tmem_ld32(tP, pv);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(BAR(B_SUE));
+      const float4* cpos = reinterpret_cast<const float4*>(gbase + OFF_ST + s * SZ_STAGE + SZ_K + SZ_V + SZ_B) + wg * 32;
+      uint32_t wds[16], wdc[16];
+      if (n < ndiag) {
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          float dsv[2], dcv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int cc = c + e;
+            const float4 pj = cpos[cc];
+            const int j = j0 + cc;
+            const bool valid = (j <= row) && (j < L);
+            const float dec = valid ? exp2f(fminf((gi - pj.x) * kLOG2E, 0.f)) : 0.f;
+            const float u = dec * uv[cc];
+            const float x = fmaf(sv[cc], c1, fmaf(fi - pj.y, kLOG2E, lam2 * u));
+            const float pr = valid ? ex2_approx(x - lse) : 0.f;
+            const float ds = pr * (pv[cc] - dl);
+            const bool eye = (j == row);
+            const float dso = eye ? 0.f : ds;
+            if (eye) { ptt += pr; dptt += pv[cc]; xd += uv[cc]; }
+            const float po = eye ? 0.f : pr;
+            za += po;
+            ya = fmaf(po, u, ya);
+            wa += dso;
+            xa = fmaf(dso, u, xa);
+            dsv[e] = dso;
+            dcv[e] = dso * (lam * dec);
+          }
+          wds[c / 2] = pack2<kHalf>(dsv[0], dsv[1]);
+          wdc[c / 2] = pack2<kHalf>(dcv[0], dcv[1]);
+        }
+      } else {
+        const float ge = reinterpret_cast<const float4*>(gbase + OFF_ST + s * SZ_STAGE + SZ_K + SZ_V + SZ_B)[63].x;
+        const float mid = exp2f(fminf((ga - ge) * kLOG2E, 0.f));
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          float dsv[2], dcv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int cc = c + e;
+            const float4 pj = cpos[cc];
+            const float cf = pj.w * mid;
+            const float uc = uv[cc] * cf;
+            const float x = fmaf(sv[cc], c1, fmaf(fi - pj.y, kLOG2E, uc * rs2));
+            const float pr = ex2_approx(x - lse);
+            const float ds = pr * (pv[cc] - dl);
+            xo = fmaf(ds, uc, xo);
+            yo = fmaf(pr, uc, yo);
+            za += pr;
+            wa += ds;
+            dsv[e] = ds;
+            dcv[e] = ds * cf;
+          }
+          wds[c / 2] = pack2<kHalf>(dsv[0], dsv[1]);
+          wdc[c / 2] = pack2<kHalf>(dcv[0], dcv[1]);
+        }
+      }
+      if (n >= 2 && !warp_wait(BAR(B_OPE + (n & 1)), ((n >> 1) - 1) & 1, p.status)) { ok = false; break; }
+      const uint32_t sDS = sbase + OFF_OP + (uint32_t)(n & 1) * 2 * SZ_OP;
+      st_op_half(sDS, r, wg, wds);
+      st_op_half(sDS + SZ_OP, r, wg, wdc);
+      fence_proxy_async_smem();
+      mbar_arrive(BAR(B_OPF + (n & 1)));
+    }
+    xa = fmaf(rowf, xo, xa);
+    ya = fmaf(rowf, yo, ya);
+    // ---- combine the two warpgroups' row sums (wg 1 -> smem -> wg 0)
+    if (wg == 1) {
+      red[r * 8 + 0] = za; red[r * 8 + 1] = ya; red[r * 8 + 2] = wa; red[r * 8 + 3] = xa;
+      red[r * 8 + 4] = ptt; red[r * 8 + 5] = dptt; red[r * 8 + 6] = xd;
+    }
+    named_bar_sync(1, 256);
+    if (wg == 0) {
+      za += red[r * 8 + 0]; ya += red[r * 8 + 1]; wa += red[r * 8 + 2]; xa += red[r * 8 + 3];
+      ptt += red[r * 8 + 4]; dptt += red[r * 8 + 5]; xd += red[r * 8 + 6];
+      // exact delta, delta-free diagonal (attention.py:449-480)
+      float ssum = ptt + za;
+      ssum = ssum > 0.f ? ssum : 1.f;
+      const float x0 = dptt - dl;
+      const float tt = dl + (ptt * x0 + wa) / ssum;
+      const float dstt = ptt * (za * x0 - wa) / ssum;
+      const float dl_row = xa + (dl - tt) * ya;
+      const float dd = tt - dl;
+      if (ok && !warp_wait(BAR(B_ACC), 0, p.status)) ok = false;
+      if (ok) {
+        tc_fence_after();
+        float acc[64], dco[32], dcd[32];
+        tmem_ld32(tmem_addr(tbase, quarter, COL_DQ), acc);
+        tmem_ld32(tmem_addr(tbase, quarter, COL_DQ + 32), acc + 32);
+        tmem_ld32(tmem_addr(tbase, quarter, COL_DCO), dco);
+        tmem_ld32(tmem_addr(tbase, quarter, COL_DCD), dcd);
+        tmem_wait_ld();
+        if (vrow) {
+          p.rstat[rb + row] = make_float4(lse, dl, dd, dstt);
+          p.rl[rb + row] = dl_row + dstt * xd;
+          p.rg[rb + row] = lam * dl_row;
+          p.rf[rb + row] = wa - za * dd;
+          // dq = scale * (sum_{j<t} dS^ k_j + DT(dS_tt) k_t)
+          const float dsr = round_lp<kHalf>(dstt);
+          const char* krow = p.k + 2 * ((int64_t)b * p.k_sb + (int64_t)h * p.k_sh + (int64_t)row * p.k_sl);
+          uint4* dqrow = reinterpret_cast<uint4*>(p.dq + 2 * ((int64_t)b * p.dq_sb + (int64_t)h * p.dq_sh + (int64_t)row * p.dq_sl));
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const uint4 kv = reinterpret_cast<const uint4*>(krow)[q];
+            const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float a0 = fmaf(dsr, unpack_lo<kHalf>(kw[i]), acc[q * 8 + 2 * i]) * kScale;
+              const float a1 = fmaf(dsr, unpack_hi<kHalf>(kw[i]), acc[q * 8 + 2 * i + 1]) * kScale;
+              w[i] = pack2<kHalf>(a0, a1);
+            }
+            dqrow[q] = make_uint4(w[0], w[1], w[2], w[3]);
+          }
+          // dc = dC_diag + lam rowf dC_off + DT(lam dS_tt) b_t   (fp32)
+          const float dsl = round_lp<kHalf>(dstt * lam);
+          const char* brow = p.bm + 2 * ((int64_t)b * p.b_sb + (int64_t)h * p.b_sh + (int64_t)row * p.b_sl);
+          float* dcrow = p.dc + ((int64_t)b * p.dc_sb + (int64_t)h * p.dc_sh + (int64_t)row * p.dc_sl);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint4 bv = reinterpret_cast<const uint4*>(brow)[q];
+            const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+            float o[8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int d = q * 8 + 2 * i;
+              const float d0 = (ndiag > 0 ? dcd[d] : 0.f) + (ntiles > ndiag ? rs * dco[d] : 0.f);
+              const float d1 = (ndiag > 0 ? dcd[d + 1] : 0.f) + (ntiles > ndiag ? rs * dco[d + 1] : 0.f);
+              o[2 * i] = fmaf(dsl, unpack_lo<kHalf>(bw[i]), d0);
+              o[2 * i + 1] = fmaf(dsl, unpack_hi<kHalf>(bw[i]), d1);
+            }
+            reinterpret_cast<float4*>(dcrow)[2 * q] = make_float4(o[0], o[1], o[2], o[3]);
+            reinterpret_cast<float4*>(dcrow)[2 * q + 1] = make_float4(o[4], o[5], o[6], o[7]);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TMEM_COLS);
+  }
+#undef BAR
+}
+
+// =============================================================================================
+// dkv kernel
+// =============================================================================================
+template <bool kHalf>
+__global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_constant__ BwdParams p) {
+  using namespace dkv;
+  extern __shared__ uint8_t smem_raw[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int kt = (int)blockIdx.x;                    // early key tiles carry the most work
+  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const int L = p.L;
+  const int n0 = kt * 128;
+  const int ntiles = (L - n0 + 63) / 64;             // query tiles m0 = n0 + 64 n < L
+  const int ndiag = ntiles < 2 ? ntiles : 2;
+
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t sbase = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (sbase - raw);
+  const uint32_t bar0 = sbase + OFF_BAR;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + 128);
+#define BAR(i) (bar0 + 8u * (uint32_t)(i))
+  if (tid == 0) {
+    for (int s = 0; s < NST; ++s) { mbar_init(BAR(B_KVF + s), 1); mbar_init(BAR(B_KVE + s), 1); }
+    mbar_init(BAR(B_K), 1);
+    mbar_init(BAR(B_SUF), 1);
+    mbar_init(BAR(B_SUE), 256);
+    for (int i = 0; i < 2; ++i) { mbar_init(BAR(B_OPF + i), 256); mbar_init(BAR(B_OPE + i), 1); }
+    mbar_init(BAR(B_ACC), 1);
+    fence_barrier_init();
+  }
+  if (warp == 9) { tmem_alloc(smem_u32(tmem_slot), TMEM_COLS); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  auto stage_addr = [&](int s) { return sbase + OFF_ST + (uint32_t)s * SZ_STAGE; };
+
+  if (warp == 8) {
+    if (lane == 0) {
+      mbar_expect_tx(BAR(B_K), SZ_K + SZ_V + SZ_B);
+      tma_load_4d(sbase + OFF_K, &p.tm_k128, BAR(B_K), 0, n0, h, b);
+      tma_load_4d(sbase + OFF_V, &p.tm_v128, BAR(B_K), 0, n0, h, b);
+      tma_load_4d(sbase + OFF_B, &p.tm_b128, BAR(B_K), 0, n0, h, b);
+      for (int n = 0; n < ntiles; ++n) {
+        const int s = n % NST;
+        if (n >= NST && !mbar_wait(BAR(B_KVE + s), ((n / NST) - 1) & 1, p.status)) break;
+        const int m0 = n0 + 64 * n;
+        const uint32_t st = stage_addr(s);
+        mbar_expect_tx(BAR(B_KVF + s), SZ_STAGE);
+        tma_load_4d(st, &p.tm_q64, BAR(B_KVF + s), 0, m0, h, b);
+        tma_load_4d(st + SZ_Q, &p.tm_do64, BAR(B_KVF + s), 0, m0, h, b);
+        tma_load_4d(st + SZ_Q + SZ_DO, &p.tm_c64, BAR(B_KVF + s), 0, m0, h, b);
+        tma_load_3d(st + SZ_Q + SZ_DO + SZ_C, &p.tm_pos, BAR(B_KVF + s), 0, m0, bh);
+        tma_load_3d(st + SZ_Q + SZ_DO + SZ_C + SZ_POS, &p.tm_rstat, BAR(B_KVF + s), 0, m0, bh);
+      }
+    }
+  } else if (warp == 9) {
+    if (lane == 0) {
+      constexpr uint32_t fmt = kHalf ? 0 : 1;
+      constexpr uint32_t id_s = make_idesc(128, 64, fmt, 0, 0);
+      constexpr uint32_t id_mn64 = make_idesc(128, 64, fmt, 0, 1);
+      constexpr uint32_t id_mn32 = make_idesc(128, 32, fmt, 0, 1);
+      const uint32_t sK = sbase + OFF_K, sV = sbase + OFF_V, sB = sbase + OFF_B;
+      bool ok = mbar_wait(BAR(B_K), 0, p.status);
+      int nbo = 0, nbd = 0;
+      auto issue_grads = [&](int m) -> bool {
+        const int buf = m & 1, s = m % NST;
+        if (!mbar_wait(BAR(B_OPF + buf), (m >> 1) & 1, p.status)) return false;
+        tc_fence_after();
+        const uint32_t sPT = sbase + OFF_OP + (uint32_t)buf * 3 * SZ_OP, sDST = sPT + SZ_OP, sDSB = sDST + SZ_OP;
+        const uint32_t st = stage_addr(s);
+        const bool dg = m < ndiag;
+        int& cnt = dg ? nbd : nbo;
+        const uint32_t tdb = tbase + (dg ? COL_DBD : COL_DBO);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)   // dV += P^T dO
+          umma_ss(tbase + COL_DV, desc_k128(sPT + k * 32), desc_mn128(st + SZ_Q + k * 2048), id_mn64, (m > 0 || k > 0));
+#pragma unroll
+        for (int k = 0; k < 4; ++k)   // dK += dS^T Q
+          umma_ss(tbase + COL_DK, desc_k128(sDST + k * 32), desc_mn128(st + k * 2048), id_mn64, (m > 0 || k > 0));
+#pragma unroll
+        for (int k = 0; k < 4; ++k)   // dB += dSb^T C
+          umma_ss(tdb, desc_k128(sDSB + k * 32), desc_mn64(st + SZ_Q + SZ_DO + k * 1024), id_mn32, (cnt > 0 || k > 0));
+        ++cnt;
+        umma_commit(BAR(B_OPE + buf));
+        umma_commit(BAR(B_KVE + s));
+        return true;
+      };
+      for (int n = 0; ok && n < ntiles; ++n) {
+        const int s = n % NST;
+        if (!mbar_wait(BAR(B_KVF + s), (n / NST) & 1, p.status)) { ok = false; break; }
+        if (n > 0 && !mbar_wait(BAR(B_SUE), (n - 1) & 1, p.status)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t st = stage_addr(s);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) umma_ss(tbase + COL_S, desc_k128(sK + k * 32), desc_k128(st + k * 32), id_s, k > 0);
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+          umma_ss(tbase + COL_U, desc_k64(sB + k * 32), desc_k64(st + SZ_Q + SZ_DO + k * 32), id_s, k > 0);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_ss(tbase + COL_DP, desc_k128(sV + k * 32), desc_k128(st + SZ_Q + k * 32), id_s, k > 0);
+        umma_commit(BAR(B_SUF));
+        if (n > 0 && !issue_grads(n - 1)) { ok = false; break; }
+      }
+      if (ok) issue_grads(ntiles - 1);
+      umma_commit(BAR(B_ACC));
+    }
+  } else {
+    const int wg = warp >> 2, quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int j = n0 + r;                                // owned key row
+    const bool vcol = j < L;
+    const int64_t rb = (int64_t)bh * L;
+    const float4 pjv = p.pos[rb + (vcol ? j : L - 1)];
+    const float gj = pjv.x, fj = pjv.y;
+    const float ge = p.pos[rb + min(n0 + 127, L - 1)].x;
+    const float lam = p.lam[h];
+    const float colf = exp2f(fminf((ge - gj) * kLOG2E, 0.f));     // 128-row key-tile anchor
+    const float rk = lam * colf;
+    const float rk2 = rk * kLOG2E;
+    const float lam2 = lam * kLOG2E;
+    const float c1 = kScale * kLOG2E;
+    const float dstt_j = vcol ? p.rstat[rb + j].w : 0.f;
+    float* red = reinterpret_cast<float*>(gbase + OFF_RED);
+    const uint32_t tS = tmem_addr(tbase, quarter, COL_S + wg * 32);
+    const uint32_t tU = tmem_addr(tbase, quarter, COL_U + wg * 32);
+    const uint32_t tP = tmem_addr(tbase, quarter, COL_DP + wg * 32);
+    float dgu = 0.f, dgo = 0.f, dfs = 0.f;
+    bool ok = true;
+    for (int n = 0; ok && n < ntiles; ++n) {
+      const int s = n % NST;
+      const int i0 = n0 + 64 * n + wg * 32;            // first query column of this thread's half
+      if (!warp_wait(BAR(B_SUF), n & 1, p.status)) { ok = false; break; }
+      tc_fence_after();
+      float sv[32], uv[32], pv[32];
+      tmem_ld32(tS, sv);
+      tmem_ld32(tU, uv);
+      tmem_ld32(tP, pv);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(BAR(B_SUE));
+      const uint8_t* st = gbase + OFF_ST + s * SZ_STAGE;
+      const float4* cpos = reinterpret_cast<const float4*>(st + SZ_Q + SZ_DO + SZ_C) + wg * 32;
+      const float4* crst = reinterpret_cast<const float4*>(st + SZ_Q + SZ_DO + SZ_C + SZ_POS) + wg * 32;
+      uint32_t wp[16], wk[16], wb[16];
+      if (n < ndiag) {
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          float pe[2], ke[2], be[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int cc = c + e;
+            const int i = i0 + cc;
+            const float4 pi = cpos[cc];
+            const float4 ri = crst[cc];
+            const bool valid = (i >= j) && (i < L);
+            const bool strict = valid && (i > j);
+            const bool eye = valid && (i == j);
+            const float dec = valid ? exp2f(fminf((pi.x - gj) * kLOG2E, 0.f)) : 0.f;
+            const float u = dec * uv[cc];
+            const float x = fmaf(sv[cc], c1, fmaf(pi.y - fj, kLOG2E, lam2 * u));
+            const float pr = valid ? ex2_approx(x - ri.x) : 0.f;
+            const float dsh = pr * (pv[cc] - ri.y);
+            const float dsx = fmaf(-pr, ri.z, dsh);
+            const float dso = strict ? dsx : 0.f;
+            dgu = fmaf(dso, u, dgu);
+            dfs += dso;
+            pe[e] = pr;
+            ke[e] = eye ? dstt_j : dso;
+            be[e] = (eye ? dstt_j : (strict ? dsh : 0.f)) * (lam * dec);
+          }
+          wp[c / 2] = pack2<kHalf>(pe[0], pe[1]);
+          wk[c / 2] = pack2<kHalf>(ke[0], ke[1]);
+          wb[c / 2] = pack2<kHalf>(be[0], be[1]);
+        }
+      } else {
+        const float gs = reinterpret_cast<const float4*>(st + SZ_Q + SZ_DO + SZ_C)[0].x;   // query block start
+        const float mid = exp2f(fminf((gs - ge) * kLOG2E, 0.f));
+        const bool tail = (n0 + 64 * n + 64 > L);
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          float pe[2], ke[2], be[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int cc = c + e;
+            const float4 pi = cpos[cc];
+            const float4 ri = crst[cc];
+            const float rq = pi.z * mid;
+            const float uc = uv[cc] * rq;
+            const float x = fmaf(sv[cc], c1, fmaf(pi.y - fj, kLOG2E, uc * rk2));
+            float pr = ex2_approx(x - ri.x);
+            if (tail && (i0 + cc >= L)) pr = 0.f;
+            const float dsh = pr * (pv[cc] - ri.y);
+            const float dsx = fmaf(-pr, ri.z, dsh);
+            dgo = fmaf(dsx, uc, dgo);
+            dfs += dsx;
+            pe[e] = pr;
+            ke[e] = dsx;
+            be[e] = dsh * rq;
+          }
+          wp[c / 2] = pack2<kHalf>(pe[0], pe[1]);
+          wk[c / 2] = pack2<kHalf>(ke[0], ke[1]);
+          wb[c / 2] = pack2<kHalf>(be[0], be[1]);
+        }
+      }
+      if (n >= 2 && !warp_wait(BAR(B_OPE + (n & 1)), ((n >> 1) - 1) & 1, p.status)) { ok = false; break; }
+      const uint32_t sPT = sbase + OFF_OP + (uint32_t)(n & 1) * 3 * SZ_OP;
+      st_op_half(sPT, r, wg, wp);
+      st_op_half(sPT + SZ_OP, r, wg, wk);
+      st_op_half(sPT + 2 * SZ_OP, r, wg, wb);
+      fence_proxy_async_smem();
+      mbar_arrive(BAR(B_OPF + (n & 1)));
+    }
+    dgu = fmaf(colf, dgo, dgu);
+    if (wg == 1) { red[r * 4 + 0] = dgu; red[r * 4 + 1] = dfs; }
+    named_bar_sync(1, 256);
+    if (wg == 0) {
+      dgu += red[r * 4 + 0];
+      dfs += red[r * 4 + 1];
+      if (ok && !warp_wait(BAR(B_ACC), 0, p.status)) ok = false;
+      if (ok) {
+        tc_fence_after();
+        uint4* dkrow = reinterpret_cast<uint4*>(p.dk + 2 * ((int64_t)b * p.dk_sb + (int64_t)h * p.dk_sh + (int64_t)j * p.dk_sl));
+        uint4* dvrow = reinterpret_cast<uint4*>(p.dv + 2 * ((int64_t)b * p.dv_sb + (int64_t)h * p.dv_sh + (int64_t)j * p.dv_sl));
+        // dK and dV, 32 columns at a time (TMEM loads are warp-collective: every lane takes part)
+#pragma unroll 1
+        for (int part = 0; part < 4; ++part) {
+          const int col = (part < 2 ? COL_DK : COL_DV) + (part & 1) * 32;
+          float acc[32];
+          tmem_ld32(tmem_addr(tbase, quarter, col), acc);
+          tmem_wait_ld();
+          const float sc = part < 2 ? kScale : 1.f;
+          uint4* dst = (part < 2 ? dkrow : dvrow) + (part & 1) * 4;
+          if (vcol) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint32_t w4[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) w4[i] = pack2<kHalf>(acc[q * 8 + 2 * i] * sc, acc[q * 8 + 2 * i + 1] * sc);
+              dst[q] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            }
+          }
+        }
+        {
+          float dbo[32], dbd[32];
+          tmem_ld32(tmem_addr(tbase, quarter, COL_DBO), dbo);
+          tmem_ld32(tmem_addr(tbase, quarter, COL_DBD), dbd);
+          tmem_wait_ld();
+          if (vcol) {
+            const bool has_off = ntiles > ndiag;
+            float* dbrow = p.db + ((int64_t)b * p.db_sb + (int64_t)h * p.db_sh + (int64_t)j * p.db_sl);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              float o[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) o[i] = dbd[q * 4 + i] + (has_off ? rk * dbo[q * 4 + i] : 0.f);
+              reinterpret_cast<float4*>(dbrow)[q] = make_float4(o[0], o[1], o[2], o[3]);
+            }
+            p.dg[rb + j] = p.rg[rb + j] - lam * dgu;
+            if (p.dF) p.dF[rb + j] = p.rf[rb + j] - dfs;
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TMEM_COLS);
+  }
+#undef BAR
+}
+
+// d lambda_h = sum over (b, t) of the per-row parts, in fp64 with a fixed reduction tree, rounded once
+// (attention.py:781-783).
+__global__ void __launch_bounds__(256) dlam_kernel(const float* rl, float* dlam, int B, int H, int L) {
+  const int h = blockIdx.x;
+  __shared__ double part[256];
+  double acc = 0.0;
+  for (int bb = 0; bb < B; ++bb) {
+    const float* src = rl + ((int64_t)bb * H + h) * L;
+    for (int t = threadIdx.x; t < L; t += 256) acc += (double)src[t];
+  }
+  part[threadIdx.x] = acc;
+  __syncthreads();
+  for (int w = 128; w > 0; w >>= 1) {
+    if ((int)threadIdx.x < w) part[threadIdx.x] += part[threadIdx.x + w];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) dlam[h] = (float)part[0];
+}
+
+}  // namespace bwd
+
+cudaError_t launch_attn_bwd(const BwdParams& p, int dtype, cudaStream_t st) {
+  using namespace bwd;
+  dim3 gq(p.ntq128, p.B * p.H);
+  dim3 gk(p.ntq128, p.B * p.H);
+  if (dtype == 1) {
+    cudaFuncSetAttribute(attn_bwd_dq_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, dqk::SMEM_BYTES);
+    cudaFuncSetAttribute(attn_bwd_dkv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, dkv::SMEM_BYTES);
+    attn_bwd_dq_kernel<true><<<gq, NTHREADS, dqk::SMEM_BYTES, st>>>(p);
+    attn_bwd_dkv_kernel<true><<<gk, NTHREADS, dkv::SMEM_BYTES, st>>>(p);
+  } else {
+    cudaFuncSetAttribute(attn_bwd_dq_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, dqk::SMEM_BYTES);
+    cudaFuncSetAttribute(attn_bwd_dkv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, dkv::SMEM_BYTES);
+    attn_bwd_dq_kernel<false><<<gq, NTHREADS, dqk::SMEM_BYTES, st>>>(p);
+    attn_bwd_dkv_kernel<false><<<gk, NTHREADS, dkv::SMEM_BYTES, st>>>(p);
+  }
+  dlam_kernel<<<p.H, 256, 0, st>>>(p.rl, p.dlam, p.B, p.H, p.L);
+  return cudaGetLastError();
+}
+
+}  // namespace sisa

@@ -1,0 +1,301 @@
+// attn_fwd.cu - exact SISA attention forward on Blackwell tensor cores (tcgen05 + TMA + TMEM).
+//
+// Reference semantics: src/sisa/kernels/attention.py:177-296 (_fwd) and src/sisa/functional.py:69-103.
+// Outputs: o = softmax(s) v (low precision), lse (log2 units), and the self-normalised fp32 output
+// o'' = sum DT(p) v / sum DT(p) used by the exact-delta backward (attention.py:36-44, 286-293).
+//
+// CTA = one 128-row query tile of one (batch, head). Warp roles:
+//   warps 0-3  softmax: thread r owns query row r = TMEM lane r (row reductions are thread-local),
+//   warp 4     TMA producer: Q and C once, then K, V, B~ and the key position records per 64-key tile,
+//   warp 5     UMMA issuer (one lane) and TMEM owner.
+// Per key tile: S = Q K^T and U = C B~^T (M=128, N=64) land in TMEM; the softmax threads build
+// x = s log2e, write P = 2^(x - m) in bf16 to shared memory (128B-swizzled, K-major) and the MMA
+// warp accumulates O += P V in TMEM. The running maximum is rescaled lazily: O (in TMEM), l and
+// sum DT(p) are corrected only when a row's tile maximum exceeds the reference maximum by more
+// than 2^8, so most tiles need no correction pass. Key tiles are visited diagonal first, then
+// from the start of the sequence. TMEM: 256 columns (S 64 | U 64 | O 64 | spare), so two CTAs
+// share an SM and one CTA's MMAs overlap the other's softmax.
+#include <cuda_runtime.h>
+
+#include "attn_common.cuh"
+#include "attn.h"
+
+namespace sisa {
+namespace fwd {
+
+constexpr int BM = 128, BN = 64, NSTAGE = 2;
+constexpr uint32_t SZ_Q = BM * 128, SZ_C = BM * 64;
+constexpr uint32_t SZ_K = BN * 128, SZ_V = BN * 128, SZ_B = BN * 64, SZ_POS = BN * 16;
+constexpr uint32_t SZ_STAGE = SZ_K + SZ_V + SZ_B + SZ_POS;    // 21504 = 21 KiB
+constexpr uint32_t SZ_P = BM * 128;
+constexpr uint32_t OFF_Q = 0, OFF_C = OFF_Q + SZ_Q, OFF_ST = OFF_C + SZ_C;
+constexpr uint32_t OFF_P = OFF_ST + NSTAGE * SZ_STAGE;
+constexpr uint32_t OFF_BAR = OFF_P + 2 * SZ_P;
+constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr uint32_t TMEM_COLS = 256;
+constexpr int COL_S = 0, COL_U = 64, COL_O = 128;
+// barrier indices
+constexpr int B_Q = 0, B_KVF = 1, B_KVE = 3, B_SUF = 5, B_SUE = 6, B_PF = 7, B_PE = 9, B_O = 11;
+
+static_assert(OFF_ST % 1024 == 0 && SZ_STAGE % 1024 == 0 && OFF_P % 1024 == 0, "swizzle alignment");
+
+template <bool kHalf>
+__global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant__ FwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qt = p.ntq - 1 - (int)blockIdx.x;      // heaviest query tiles first
+  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  const int L = p.L;
+  const int m0 = qt * BM;
+  const int ndiag = (m0 + BN < L) ? 2 : 1;
+  const int ntiles = ndiag + m0 / BN;
+
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t sbase = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (sbase - raw);
+  const uint32_t sQ = sbase + OFF_Q, sC = sbase + OFF_C;
+  const uint32_t bar0 = sbase + OFF_BAR;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + 128);
+#define BAR(i) (bar0 + 8u * (uint32_t)(i))
+
+  if (tid == 0) {
+    mbar_init(BAR(B_Q), 1);
+    for (int s = 0; s < NSTAGE; ++s) { mbar_init(BAR(B_KVF + s), 1); mbar_init(BAR(B_KVE + s), 1); }
+    mbar_init(BAR(B_SUF), 1);
+    mbar_init(BAR(B_SUE), 128);
+    for (int i = 0; i < 2; ++i) { mbar_init(BAR(B_PF + i), 128); mbar_init(BAR(B_PE + i), 1); }
+    mbar_init(BAR(B_O), 1);
+    fence_barrier_init();
+  }
+  if (warp == 5) { tmem_alloc(smem_u32(tmem_slot), TMEM_COLS); tmem_relinquish(); }
+  if (warp == 4 && lane == 0) {
+    tma_prefetch_desc(&p.tm_q); tma_prefetch_desc(&p.tm_k); tma_prefetch_desc(&p.tm_v);
+    tma_prefetch_desc(&p.tm_c); tma_prefetch_desc(&p.tm_b); tma_prefetch_desc(&p.tm_pos);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  auto key0 = [&](int n) { return n < ndiag ? m0 + n * BN : (n - ndiag) * BN; };
+  auto stage_addr = [&](int s) { return sbase + OFF_ST + (uint32_t)s * SZ_STAGE; };
+
+  if (warp == 4) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      mbar_expect_tx(BAR(B_Q), SZ_Q + SZ_C);
+      tma_load_4d(sQ, &p.tm_q, BAR(B_Q), 0, m0, h, b);
+      tma_load_4d(sC, &p.tm_c, BAR(B_Q), 0, m0, h, b);
+      for (int n = 0; n < ntiles; ++n) {
+        const int s = n % NSTAGE;
+        if (n >= NSTAGE && !mbar_wait(BAR(B_KVE + s), ((n / NSTAGE) - 1) & 1, p.status)) break;
+        const int j0 = key0(n);
+        const uint32_t st = stage_addr(s);
+        mbar_expect_tx(BAR(B_KVF + s), SZ_STAGE);
+        tma_load_4d(st, &p.tm_k, BAR(B_KVF + s), 0, j0, h, b);
+        tma_load_4d(st + SZ_K, &p.tm_v, BAR(B_KVF + s), 0, j0, h, b);
+        tma_load_4d(st + SZ_K + SZ_V, &p.tm_b, BAR(B_KVF + s), 0, j0, h, b);
+        tma_load_3d(st + SZ_K + SZ_V + SZ_B, &p.tm_pos, BAR(B_KVF + s), 0, j0, bh);
+      }
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------------ UMMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id_qk = make_idesc(128, 64, kHalf ? 0 : 1, 0, 0);
+      constexpr uint32_t id_pv = make_idesc(128, 64, kHalf ? 0 : 1, 0, 1);
+      const uint32_t tS = tbase + COL_S, tU = tbase + COL_U, tO = tbase + COL_O;
+      bool ok = mbar_wait(BAR(B_Q), 0, p.status);
+      auto issue_pv = [&](int m) -> bool {
+        const int buf = m & 1, s = m % NSTAGE;
+        if (!mbar_wait(BAR(B_PF + buf), (m >> 1) & 1, p.status)) return false;
+        tc_fence_after();
+        const uint32_t sP = sbase + OFF_P + (uint32_t)buf * SZ_P;
+        const uint32_t sV = stage_addr(s) + SZ_K;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_ss(tO, desc_k128(sP + k * 32), desc_mn128(sV + k * 2048), id_pv, (m > 0 || k > 0) ? 1u : 0u);
+        umma_commit(BAR(B_PE + buf));
+        umma_commit(BAR(B_KVE + s));
+        return true;
+      };
+      for (int n = 0; ok && n < ntiles; ++n) {
+        const int s = n % NSTAGE;
+        if (!mbar_wait(BAR(B_KVF + s), (n / NSTAGE) & 1, p.status)) { ok = false; break; }
+        if (n > 0 && !mbar_wait(BAR(B_SUE), (n - 1) & 1, p.status)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t st = stage_addr(s);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) umma_ss(tS, desc_k128(sQ + k * 32), desc_k128(st + k * 32), id_qk, k > 0);
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+          umma_ss(tU, desc_k64(sC + k * 32), desc_k64(st + SZ_K + SZ_V + k * 32), id_qk, k > 0);
+        umma_commit(BAR(B_SUF));
+        if (n > 0 && !issue_pv(n - 1)) { ok = false; break; }
+      }
+      if (ok) issue_pv(ntiles - 1);
+      umma_commit(BAR(B_O));
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax warps 0-3
+    const int r = tid;
+    const int row = m0 + r;
+    const bool vrow = row < L;
+    const float4* posbh = p.pos + (int64_t)bh * L;
+    const float4 pi = posbh[vrow ? row : L - 1];
+    const float gi = pi.x, fi = pi.y;
+    const float ga = posbh[m0].x;
+    const float lam = p.lam[h];
+    const float rs = lam * exp2f(fminf((gi - ga) * kLOG2E, 0.f));   // lam * rowf (128-row anchor)
+    const float lam2 = lam * kLOG2E;
+    const float c1 = kScale * kLOG2E;
+    const uint32_t tS = tmem_addr(tbase, warp, COL_S);
+    const uint32_t tU = tmem_addr(tbase, warp, COL_U);
+    const uint32_t tO = tmem_addr(tbase, warp, COL_O);
+    float m_ref = -INFINITY, l = 0.f, lb = 0.f;
+    bool ok = true;
+    for (int n = 0; n < ntiles; ++n) {
+      const int s = n % NSTAGE;
+      const int j0 = key0(n);
+      if (!warp_wait(BAR(B_SUF), n & 1, p.status)) { ok = false; break; }
+      tc_fence_after();
+      const float4* cpos = reinterpret_cast<const float4*>(gbase + OFF_ST + s * SZ_STAGE + SZ_K + SZ_V + SZ_B);
+      float x[64];
+      if (n < ndiag) {
+        // diagonal tile: pairwise decay, causal mask and sequence end
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          float sv[32], uv[32];
+          tmem_ld32(tS + half * 32, sv);
+          tmem_ld32(tU + half * 32, uv);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int cc = half * 32 + c;
+            const float4 pj = cpos[cc];
+            const float dec = exp2f(fminf((gi - pj.x) * kLOG2E, 0.f));
+            const float xv = fmaf(sv[c], c1, fmaf(fi - pj.y, kLOG2E, lam2 * (dec * uv[c])));
+            const int j = j0 + cc;
+            x[cc] = (j <= row && j < L) ? xv : -INFINITY;
+          }
+        }
+      } else {
+        const float ge = cpos[BN - 1].x;
+        const float rsm = rs * exp2f(fminf((ga - ge) * kLOG2E, 0.f)) * kLOG2E;   // lam rowf mid log2e
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          float sv[32], uv[32];
+          tmem_ld32(tS + half * 32, sv);
+          tmem_ld32(tU + half * 32, uv);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int cc = half * 32 + c;
+            const float4 pj = cpos[cc];
+            x[cc] = fmaf(sv[c], c1, fmaf(fi - pj.y, kLOG2E, (uv[c] * pj.w) * rsm));
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(BAR(B_SUE));            // S and U are in registers: the next tile's GEMMs may start
+
+      float mt = x[0];
+#pragma unroll
+      for (int c = 1; c < 64; ++c) mt = fmaxf(mt, x[c]);
+      const bool need = mt > m_ref + 8.f;
+      const float m_new = need ? mt : m_ref;
+      const float corr = need ? ex2_approx(m_ref - m_new) : 1.f;
+      if (__any_sync(0xffffffffu, need) && n > 0) {
+        // lazy correction of O: wait until O += P V of the previous tile has landed
+        if (!warp_wait(BAR(B_PE + ((n - 1) & 1)), ((n - 1) >> 1) & 1, p.status)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float ov[16];
+          tmem_ld16(tO + q * 16, ov);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) ov[i] *= corr;
+          tmem_st16(tO + q * 16, ov);
+        }
+        tmem_wait_st();
+      }
+      l *= corr;
+      lb *= corr;
+      m_ref = m_new;
+      const float mu = (m_ref == -INFINITY) ? 0.f : m_ref;
+      if (n >= 2 && !warp_wait(BAR(B_PE + (n & 1)), ((n >> 1) - 1) & 1, p.status)) { ok = false; break; }
+      const uint32_t sP = sbase + OFF_P + (uint32_t)(n & 1) * SZ_P;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float p0 = ex2_approx(x[q * 8 + 2 * i] - mu);
+          const float p1 = ex2_approx(x[q * 8 + 2 * i + 1] - mu);
+          l += p0;
+          l += p1;
+          w[i] = pack2<kHalf>(p0, p1);
+          lb += unpack_lo<kHalf>(w[i]);
+          lb += unpack_hi<kHalf>(w[i]);
+        }
+        st_shared_v4(sP + sw128_off(r, q), w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(BAR(B_PF + (n & 1)));
+    }
+    if (ok && !warp_wait(BAR(B_O), 0, p.status)) ok = false;
+    if (ok) {
+      tc_fence_after();
+      float ov[64];
+      tmem_ld32(tO, ov);
+      tmem_ld32(tO + 32, ov + 32);
+      tmem_wait_ld();
+      if (vrow) {
+        const float ls = (l == 0.f) ? 1.f : l;
+        const float lbs = (lb == 0.f) ? 1.f : lb;
+        uint4* orow = reinterpret_cast<uint4*>(p.o + 2 * ((int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)row * p.o_sl));
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          uint32_t w[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) w[i] = pack2<kHalf>(ov[q * 8 + 2 * i] / ls, ov[q * 8 + 2 * i + 1] / ls);
+          orow[q] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        if (p.o32) {
+          float4* o32row = reinterpret_cast<float4*>(p.o32 + ((int64_t)bh * L + row) * kD);
+#pragma unroll
+          for (int q = 0; q < 16; ++q)
+            o32row[q] = make_float4(ov[4 * q] / lbs, ov[4 * q + 1] / lbs, ov[4 * q + 2] / lbs, ov[4 * q + 3] / lbs);
+        }
+        const float lse = ((m_ref == -INFINITY) ? 0.f : m_ref) + log2f(ls);
+        p.lse[(int64_t)bh * L + row] = lse;
+        if (!isfinite(lse) && p.status) atomicOr(p.status, SISA_ST_NONFINITE);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TMEM_COLS);
+  }
+#undef BAR
+}
+
+}  // namespace fwd
+
+cudaError_t launch_attn_fwd(const FwdParams& p, int dtype, cudaStream_t st) {
+  using namespace fwd;
+  dim3 grid(p.ntq, p.B * p.H);
+  if (dtype == 1) {
+    cudaFuncSetAttribute(attn_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attn_fwd_kernel<true><<<grid, 192, SMEM_BYTES, st>>>(p);
+  } else {
+    cudaFuncSetAttribute(attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    attn_fwd_kernel<false><<<grid, 192, SMEM_BYTES, st>>>(p);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace sisa

@@ -1,0 +1,315 @@
+// capi.cu - the extern "C" boundary of libsisa_b200.so: argument validation, TMA tensor-map
+// encoding and kernel launches. No device allocation, no host synchronisation, no exceptions.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "sisa_b200.h"
+#include "attn.h"
+#include "prep.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(SISA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// (X, L, H, B) view of a (B, H, L, X) tensor with element strides; box (X, rows, 1, 1).
+int map_view4(CUtensorMap* m, const sisa_view4* v, int64_t B, int64_t H, int64_t L, int64_t X, int elem_bytes,
+              CUtensorMapDataType dt, int rows, CUtensorMapSwizzle sw, const char* name) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(SISA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[4] = {(cuuint64_t)X, (cuuint64_t)L, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)(v->stride_l * elem_bytes), (cuuint64_t)(v->stride_h * elem_bytes),
+                           (cuuint64_t)(v->stride_b * elem_bytes)};
+  // size-1 axes may carry any stride; give them a legal one
+  if (H == 1) strides[1] = strides[0] * (cuuint64_t)L;
+  if (B == 1) strides[2] = (H == 1 ? strides[1] : strides[1] * (cuuint64_t)H);
+  cuuint32_t box[4] = {(cuuint32_t)X, (cuuint32_t)rows, 1, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = enc(m, dt, 4, v->data, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SISA_ERR_ALIGN, "%s: cuTensorMapEncodeTiled failed (%d)", name, (int)r);
+  return SISA_OK;
+}
+
+// (4, L, B*H) fp32 records, box (4, 64, 1).
+int map_records(CUtensorMap* m, const void* ptr, int64_t BH, int64_t L, const char* name) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(SISA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[3] = {4, (cuuint64_t)L, (cuuint64_t)BH};
+  cuuint64_t strides[2] = {16, (cuuint64_t)(L * 16)};
+  cuuint32_t box[3] = {4, 64, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(ptr), dims, strides, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SISA_ERR_ALIGN, "%s: cuTensorMapEncodeTiled failed (%d)", name, (int)r);
+  return SISA_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_view(const sisa_view4* v, int elem_bytes, const char* name) {
+  if (!v || !v->data) return fail(SISA_ERR_VALUE, "%s: null view", name);
+  if (!aligned16(v->data)) return fail(SISA_ERR_ALIGN, "%s: data pointer is not 16-byte aligned", name);
+  const int64_t unit = 16 / elem_bytes;
+  if (v->stride_l % unit || v->stride_h % unit || v->stride_b % unit)
+    return fail(SISA_ERR_ALIGN, "%s: strides (%lld, %lld, %lld) must be multiples of %lld elements", name,
+                (long long)v->stride_b, (long long)v->stride_h, (long long)v->stride_l, (long long)unit);
+  if (v->stride_l <= 0 || v->stride_h < 0 || v->stride_b < 0)
+    return fail(SISA_ERR_VALUE, "%s: negative or zero strides are not supported", name);
+  return SISA_OK;
+}
+
+int check_dims(int64_t B, int64_t H, int64_t L) {
+  if (B < 1 || H < 1 || L < 1) return fail(SISA_ERR_VALUE, "B, H and L must be >= 1 (got %lld, %lld, %lld)",
+                                           (long long)B, (long long)H, (long long)L);
+  if (L > (1ll << 24) || B * H > (1ll << 20))
+    return fail(SISA_ERR_VALUE, "problem too large (B*H=%lld, L=%lld)", (long long)(B * H), (long long)L);
+  return SISA_OK;
+}
+
+int check_dtype(int dtype) {
+  if (dtype != SISA_BF16 && dtype != SISA_F16) return fail(SISA_ERR_TYPE, "dtype must be SISA_BF16 or SISA_F16");
+  return SISA_OK;
+}
+
+void layout(int64_t H, int64_t* o) {
+  o[0] = 0;                    // Q
+  o[1] = H * 64;               // K
+  o[2] = 2 * H * 64;           // V
+  o[3] = 3 * H * 64;           // B
+  o[4] = o[3] + H * 32;        // C
+  o[5] = o[4] + H * 32;        // TH
+  o[6] = o[5] + H * 16;        // A
+  o[7] = o[6] + H;             // NTOT = 273 H
+  o[8] = (o[7] + 15) / 16 * 16;  // NPAD
+}
+
+int64_t nch64(int64_t L) { return (L + 63) / 64; }
+
+}  // namespace
+
+extern "C" {
+
+const char* sisa_version(void) { return "sisa_b200 0.1.0 (sm_100a)"; }
+const char* sisa_last_error(void) { return g_err.c_str(); }
+
+int sisa_device_check(int device) {
+  cudaDeviceProp prop;
+  cudaError_t e = cudaGetDeviceProperties(&prop, device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
+  if (prop.major != 10 || prop.minor != 0)
+    return fail(SISA_ERR_UNSUPPORTED, "%s is sm_%d%d; this library is built for sm_100a only", prop.name,
+                prop.major, prop.minor);
+  return SISA_OK;
+}
+
+int sisa_fused_layout(int64_t n_head, int64_t* out9) {
+  if (n_head < 1) return fail(SISA_ERR_VALUE, "n_head must be >= 1");
+  if (!out9) return fail(SISA_ERR_VALUE, "out9 is null");
+  layout(n_head, out9);
+  return SISA_OK;
+}
+
+int64_t sisa_prep_fwd_workspace(int64_t B, int64_t H, int64_t L) { return B * H * nch64(L) * 18 * 4; }
+int64_t sisa_prep_bwd_workspace(int64_t B, int64_t H, int64_t L) { return B * H * nch64(L) * 18 * 8; }
+int64_t sisa_attn_bwd_workspace(int64_t B, int64_t H, int64_t L) { return B * H * L * (16 + 3 * 4); }
+
+int sisa_prep_fwd(const void* proj, int64_t B, int64_t L, int64_t H, int64_t proj_sb, int64_t proj_sl, int dtype,
+                  const float* z, int64_t z_sb, int64_t z_sl, void* c_rot, void* b_rot, float* pos, void* workspace,
+                  int32_t* status, void* stream) {
+  int rc;
+  if ((rc = check_dims(B, H, L)) || (rc = check_dtype(dtype))) return rc;
+  if (!proj || !c_rot || !b_rot || !pos || !workspace) return fail(SISA_ERR_VALUE, "sisa_prep_fwd: null pointer");
+  int64_t off[9];
+  layout(H, off);
+  if (proj_sl < off[8]) return fail(SISA_ERR_VALUE, "proj row stride %lld < NPAD %lld", (long long)proj_sl,
+                                    (long long)off[8]);
+  if (!aligned16(proj) || proj_sl % 8 || proj_sb % 8)
+    return fail(SISA_ERR_ALIGN, "proj must be 16-byte aligned with strides that are multiples of 8 elements");
+  if (!aligned16(c_rot) || !aligned16(b_rot) || !aligned16(pos))
+    return fail(SISA_ERR_ALIGN, "c_rot, b_rot and pos must be 16-byte aligned");
+  sisa::PrepFwdLaunch p{};
+  p.proj = proj; p.proj_sb = proj_sb; p.proj_sl = proj_sl; p.dtype = dtype;
+  p.z = z; p.z_sb = z_sb; p.z_sl = z_sl;
+  p.B = B; p.L = L; p.H = H;
+  p.col_b = off[3]; p.col_c = off[4]; p.col_th = off[5]; p.col_a = off[6];
+  p.c_rot = c_rot; p.b_rot = b_rot; p.pos = pos; p.tot = static_cast<float*>(workspace); p.status = status;
+  cudaError_t e = sisa::launch_prep_fwd(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_prep_fwd launch");
+}
+
+int sisa_pack_positions(const float* g, int64_t g_sb, int64_t g_sh, int64_t g_sl, const float* fgate, int64_t f_sb,
+                        int64_t f_sh, int64_t f_sl, int64_t B, int64_t H, int64_t L, float* pos, int32_t* status,
+                        void* stream) {
+  int rc;
+  if ((rc = check_dims(B, H, L))) return rc;
+  if (!g || !pos) return fail(SISA_ERR_VALUE, "sisa_pack_positions: null pointer");
+  if (!aligned16(pos)) return fail(SISA_ERR_ALIGN, "pos must be 16-byte aligned");
+  sisa::PackLaunch p{};
+  p.g = g; p.g_sb = g_sb; p.g_sh = g_sh; p.g_sl = g_sl;
+  p.f = fgate; p.f_sb = f_sb; p.f_sh = f_sh; p.f_sl = f_sl;
+  p.B = B; p.H = H; p.L = L; p.pos = pos; p.status = status;
+  cudaError_t e = sisa::launch_pack_positions(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_pack_positions launch");
+}
+
+int sisa_attn_fwd(const sisa_view4* q, const sisa_view4* k, const sisa_view4* v, const sisa_view4* c,
+                  const sisa_view4* b, const float* pos, const float* lam, int64_t B, int64_t H, int64_t L, int dtype,
+                  const sisa_view4* o, float* lse, float* o32, int32_t* status, void* stream) {
+  int rc;
+  if ((rc = check_dims(B, H, L)) || (rc = check_dtype(dtype))) return rc;
+  if ((rc = check_view(q, 2, "q")) || (rc = check_view(k, 2, "k")) || (rc = check_view(v, 2, "v")) ||
+      (rc = check_view(c, 2, "c")) || (rc = check_view(b, 2, "b")) || (rc = check_view(o, 2, "o")))
+    return rc;
+  if (!pos || !lam || !lse) return fail(SISA_ERR_VALUE, "sisa_attn_fwd: null pos, lam or lse");
+  if (!aligned16(pos) || (o32 && !aligned16(o32))) return fail(SISA_ERR_ALIGN, "pos/o32 must be 16-byte aligned");
+  const CUtensorMapDataType dt = dtype == SISA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  sisa::FwdParams p;
+  memset(&p, 0, sizeof(p));
+  if ((rc = map_view4(&p.tm_q, q, B, H, L, 64, 2, dt, 128, CU_TENSOR_MAP_SWIZZLE_128B, "q")) ||
+      (rc = map_view4(&p.tm_k, k, B, H, L, 64, 2, dt, 64, CU_TENSOR_MAP_SWIZZLE_128B, "k")) ||
+      (rc = map_view4(&p.tm_v, v, B, H, L, 64, 2, dt, 64, CU_TENSOR_MAP_SWIZZLE_128B, "v")) ||
+      (rc = map_view4(&p.tm_c, c, B, H, L, 32, 2, dt, 128, CU_TENSOR_MAP_SWIZZLE_64B, "c")) ||
+      (rc = map_view4(&p.tm_b, b, B, H, L, 32, 2, dt, 64, CU_TENSOR_MAP_SWIZZLE_64B, "b")) ||
+      (rc = map_records(&p.tm_pos, pos, B * H, L, "pos")))
+    return rc;
+  p.pos = reinterpret_cast<const float4*>(pos);
+  p.lam = lam;
+  p.o = static_cast<char*>(o->data); p.o_sb = o->stride_b; p.o_sh = o->stride_h; p.o_sl = o->stride_l;
+  p.lse = lse; p.o32 = o32;
+  p.B = (int)B; p.H = (int)H; p.L = (int)L; p.ntq = (int)((L + 127) / 128);
+  p.status = status;
+  cudaError_t e = sisa::launch_attn_fwd(p, dtype, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_attn_fwd launch");
+}
+
+int sisa_attn_bwd(const sisa_view4* q, const sisa_view4* k, const sisa_view4* v, const sisa_view4* c,
+                  const sisa_view4* b, const float* pos, const float* lam, const sisa_view4* o, const sisa_view4* dout,
+                  const float* lse, const float* o32, int64_t B, int64_t H, int64_t L, int dtype, const sisa_view4* dq,
+                  const sisa_view4* dk, const sisa_view4* dv, const sisa_view4* dc, const sisa_view4* db, float* dg,
+                  float* dF, float* dlam, void* workspace, int32_t* status, void* stream) {
+  int rc;
+  if ((rc = check_dims(B, H, L)) || (rc = check_dtype(dtype))) return rc;
+  if ((rc = check_view(q, 2, "q")) || (rc = check_view(k, 2, "k")) || (rc = check_view(v, 2, "v")) ||
+      (rc = check_view(c, 2, "c")) || (rc = check_view(b, 2, "b")) || (rc = check_view(o, 2, "o")) ||
+      (rc = check_view(dout, 2, "dout")) || (rc = check_view(dq, 2, "dq")) || (rc = check_view(dk, 2, "dk")) ||
+      (rc = check_view(dv, 2, "dv")) || (rc = check_view(dc, 4, "dc")) || (rc = check_view(db, 4, "db")))
+    return rc;
+  if (!pos || !lam || !lse || !dg || !dlam || !workspace)
+    return fail(SISA_ERR_VALUE, "sisa_attn_bwd: null pos, lam, lse, dg, dlam or workspace");
+  if (!aligned16(pos) || !aligned16(workspace) || (o32 && !aligned16(o32)))
+    return fail(SISA_ERR_ALIGN, "pos, o32 and workspace must be 16-byte aligned");
+  const CUtensorMapDataType dt = dtype == SISA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  sisa::BwdParams p;
+  memset(&p, 0, sizeof(p));
+  const CUtensorMapSwizzle s128 = CU_TENSOR_MAP_SWIZZLE_128B, s64 = CU_TENSOR_MAP_SWIZZLE_64B;
+  char* ws = static_cast<char*>(workspace);
+  const int64_t n = B * H * L;
+  p.rstat = reinterpret_cast<float4*>(ws);
+  p.rg = reinterpret_cast<float*>(ws + n * 16);
+  p.rf = p.rg + n;
+  p.rl = p.rf + n;
+  if ((rc = map_view4(&p.tm_q128, q, B, H, L, 64, 2, dt, 128, s128, "q")) ||
+      (rc = map_view4(&p.tm_do128, dout, B, H, L, 64, 2, dt, 128, s128, "dout")) ||
+      (rc = map_view4(&p.tm_c128, c, B, H, L, 32, 2, dt, 128, s64, "c")) ||
+      (rc = map_view4(&p.tm_k64, k, B, H, L, 64, 2, dt, 64, s128, "k")) ||
+      (rc = map_view4(&p.tm_v64, v, B, H, L, 64, 2, dt, 64, s128, "v")) ||
+      (rc = map_view4(&p.tm_b64, b, B, H, L, 32, 2, dt, 64, s64, "b")) ||
+      (rc = map_view4(&p.tm_k128, k, B, H, L, 64, 2, dt, 128, s128, "k")) ||
+      (rc = map_view4(&p.tm_v128, v, B, H, L, 64, 2, dt, 128, s128, "v")) ||
+      (rc = map_view4(&p.tm_b128, b, B, H, L, 32, 2, dt, 128, s64, "b")) ||
+      (rc = map_view4(&p.tm_q64, q, B, H, L, 64, 2, dt, 64, s128, "q")) ||
+      (rc = map_view4(&p.tm_do64, dout, B, H, L, 64, 2, dt, 64, s128, "dout")) ||
+      (rc = map_view4(&p.tm_c64, c, B, H, L, 32, 2, dt, 64, s64, "c")) ||
+      (rc = map_records(&p.tm_pos, pos, B * H, L, "pos")) ||
+      (rc = map_records(&p.tm_rstat, p.rstat, B * H, L, "rstat")))
+    return rc;
+  p.pos = reinterpret_cast<const float4*>(pos);
+  p.lam = lam;
+  p.q = static_cast<const char*>(q->data); p.q_sb = q->stride_b; p.q_sh = q->stride_h; p.q_sl = q->stride_l;
+  p.k = static_cast<const char*>(k->data); p.k_sb = k->stride_b; p.k_sh = k->stride_h; p.k_sl = k->stride_l;
+  p.bm = static_cast<const char*>(b->data); p.b_sb = b->stride_b; p.b_sh = b->stride_h; p.b_sl = b->stride_l;
+  p.o = static_cast<const char*>(o->data); p.o_sb = o->stride_b; p.o_sh = o->stride_h; p.o_sl = o->stride_l;
+  p.dout = static_cast<const char*>(dout->data); p.do_sb = dout->stride_b; p.do_sh = dout->stride_h;
+  p.do_sl = dout->stride_l;
+  p.lse = lse; p.o32 = o32;
+  p.dq = static_cast<char*>(dq->data); p.dq_sb = dq->stride_b; p.dq_sh = dq->stride_h; p.dq_sl = dq->stride_l;
+  p.dk = static_cast<char*>(dk->data); p.dk_sb = dk->stride_b; p.dk_sh = dk->stride_h; p.dk_sl = dk->stride_l;
+  p.dv = static_cast<char*>(dv->data); p.dv_sb = dv->stride_b; p.dv_sh = dv->stride_h; p.dv_sl = dv->stride_l;
+  p.dc = static_cast<float*>(dc->data); p.dc_sb = dc->stride_b; p.dc_sh = dc->stride_h; p.dc_sl = dc->stride_l;
+  p.db = static_cast<float*>(db->data); p.db_sb = db->stride_b; p.db_sh = db->stride_h; p.db_sl = db->stride_l;
+  p.dg = dg; p.dF = dF; p.dlam = dlam;
+  p.B = (int)B; p.H = (int)H; p.L = (int)L;
+  p.ntq128 = (int)((L + 127) / 128); p.ntq64 = (int)((L + 63) / 64);
+  p.has_f = dF != nullptr;
+  p.status = status;
+  cudaError_t e = sisa::launch_attn_bwd(p, dtype, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_attn_bwd launch");
+}
+
+int sisa_prep_bwd(const void* proj, int64_t B, int64_t L, int64_t H, int64_t proj_sb, int64_t proj_sl, int dtype,
+                  const float* z, int64_t z_sb, int64_t z_sl, const void* tot, const float* dc, const float* db,
+                  const float* dg, const float* dF, void* dproj, int64_t dproj_sb, int64_t dproj_sl, float* dz,
+                  void* workspace, int32_t* status, void* stream) {
+  int rc;
+  if ((rc = check_dims(B, H, L)) || (rc = check_dtype(dtype))) return rc;
+  if (!proj || !tot || !dc || !db || !dg || !dproj || !workspace)
+    return fail(SISA_ERR_VALUE, "sisa_prep_bwd: null pointer");
+  if (z && !dz) return fail(SISA_ERR_VALUE, "sisa_prep_bwd: dz is null but z is given");
+  int64_t off[9];
+  layout(H, off);
+  if (proj_sl < off[8] || dproj_sl < off[8]) return fail(SISA_ERR_VALUE, "proj/dproj row stride < NPAD");
+  if (!aligned16(proj) || !aligned16(dproj) || proj_sl % 8 || proj_sb % 8 || dproj_sl % 8 || dproj_sb % 8)
+    return fail(SISA_ERR_ALIGN, "proj/dproj must be 16-byte aligned with strides that are multiples of 8");
+  if (!aligned16(dc) || !aligned16(db)) return fail(SISA_ERR_ALIGN, "dc/db must be 16-byte aligned");
+  sisa::PrepBwdLaunch p{};
+  p.proj = proj; p.proj_sb = proj_sb; p.proj_sl = proj_sl; p.dtype = dtype;
+  p.z = z; p.z_sb = z_sb; p.z_sl = z_sl;
+  p.B = B; p.L = L; p.H = H;
+  p.col_b = off[3]; p.col_c = off[4]; p.col_th = off[5]; p.col_a = off[6]; p.ntot = off[7]; p.npad = off[8];
+  p.tot = static_cast<const float*>(tot); p.dc = dc; p.db = db; p.dg = dg; p.dF = dF;
+  p.dproj = dproj; p.dproj_sb = dproj_sb; p.dproj_sl = dproj_sl; p.dz = dz;
+  p.bt = static_cast<double*>(workspace); p.status = status;
+  cudaError_t e = sisa::launch_prep_bwd(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_prep_bwd launch");
+}
+
+}  // extern "C"

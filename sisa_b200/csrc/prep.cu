@@ -1,0 +1,561 @@
+// prep.cu - fused SISA layer preparation (forward and backward) and the position records of the
+// unfused entry point.
+//
+// Forward (reference: src/sisa/kernels/fused_prep.py:247-352):
+//   g_t   = sum_{s<=t} -softplus(alpha_s)      (softplus threshold 20, torch formula)
+//   F_t   = sum_{s<=t} logsigmoid(z_s)         (min(z,0) - log1p(exp(-|z|)))
+//   Phi_t = sum_{s<=t} theta_s                  (16 pairs per head)
+//   c~_t, b~_t = R(Phi_t) c_t, R(Phi_t) b_t     (interleaved pairs (0,1),(2,3)..., fp32, one rounding)
+// Scans are two-level: a warp scan inside 64-row blocks plus a sequential fp32 sum of the totals of
+// the preceding blocks. The block totals come from the same scan code as the in-block values, so
+// the last g of a block equals the next block's prefix exactly and g stays monotone across blocks.
+//
+// Backward (reference: src/sisa/kernels/fused_prep.py:385-494): reverse cumulative sums in fp64
+// (block totals + in-block warp scans), rounded to fp32 once; inverse rotation of dc~/db~; d theta
+// from both rotations; zero padding columns.
+//
+// Layout: one CTA = one batch row b and one 64-token block; warp w handles heads w, w+8, ...;
+// lane l handles tokens 2l and 2l+1 of the block.
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "sm100.cuh"
+#include "prep.h"
+
+namespace sisa {
+
+constexpr int kBlk = 64;          // rows per scan block (also the rowf/colf grouping)
+constexpr int kS2 = 16;           // rotation pairs per head (d_state / 2)
+constexpr int kTot = 2 + kS2;     // totals per (b, h, block): log alpha, log f, theta[16]
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <bool kHalf>
+__device__ __forceinline__ float ld_lp(const void* p, int64_t i) {
+  if constexpr (kHalf) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  else return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+}
+
+__device__ __forceinline__ float neg_softplus(float a) {       // torch softplus, threshold 20
+  return -(a > 20.f ? a : log1pf(expf(a)));
+}
+__device__ __forceinline__ float softplus_grad(float a) {      // torch softplus_backward
+  if (a > 20.f) return 1.f;
+  const float e = expf(a);
+  return e / (e + 1.f);
+}
+__device__ __forceinline__ float logsigmoid(float z) {         // torch log_sigmoid_forward; NaN propagates
+  const float m = (z != z) ? z : fminf(z, 0.f);
+  return m - log1pf(expf(-fabsf(z)));
+}
+__device__ __forceinline__ float logsigmoid_grad(float z) {    // torch log_sigmoid_backward
+  const float e = expf(-fabsf(z));
+  const float r = e / (1.f + e);
+  return z < 0.f ? 1.f - r : r;
+}
+
+// Inclusive scan of a 64-element sequence held two per lane (x0 = element 2l, x1 = element 2l+1).
+// s0/s1 are the inclusive prefixes of both elements; the block total is lane 31's s1.
+template <typename T>
+__device__ __forceinline__ void scan64(T x0, T x1, T& s0, T& s1) {
+  const int lane = threadIdx.x & 31;
+  T incl = x0 + x1;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const T y = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl = incl + y;
+  }
+  T excl = __shfl_up_sync(0xffffffffu, incl, 1);
+  if (lane == 0) excl = T(0);
+  s0 = excl + x0;
+  s1 = incl;
+}
+
+// Reverse (suffix) inclusive scan of the same 64-element arrangement: r0 = sum_{s>=2l}, r1 = sum_{s>=2l+1};
+// the block total is lane 0's r0.
+template <typename T>
+__device__ __forceinline__ void rscan64(T x0, T x1, T& r0, T& r1) {
+  const int lane = threadIdx.x & 31;
+  T incl = x0 + x1;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const T y = __shfl_down_sync(0xffffffffu, incl, d);
+    if (lane + d < 32) incl = incl + y;
+  }
+  T excl = __shfl_down_sync(0xffffffffu, incl, 1);
+  if (lane == 31) excl = T(0);
+  r1 = excl + x1;
+  r0 = incl;
+}
+
+struct PrepArgs {
+  const void* proj;
+  int64_t proj_sb, proj_sl;
+  const float* z;
+  int64_t z_sb, z_sl;
+  int B, L, H, nch;
+  int col_b, col_c, col_th, col_a;
+  void* c_rot;
+  void* b_rot;
+  float4* pos;
+  float* tot;      // (B*H, nch, kTot)
+  int32_t* status;
+};
+
+// Element values of one head for the two tokens of this lane: log alpha, log f, theta[16].
+template <bool kHalf>
+__device__ __forceinline__ void load_elems(const PrepArgs& a, int b, int h, int t0, float la[2], float lf[2],
+                                           float th[2][kS2]) {
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int t = t0 + r;
+    const bool ok = t < a.L;
+    const int64_t row = (int64_t)b * a.proj_sb + (int64_t)(ok ? t : 0) * a.proj_sl;
+    la[r] = ok ? neg_softplus(ld_lp<kHalf>(a.proj, row + a.col_a + h)) : 0.f;
+    lf[r] = (ok && a.z) ? logsigmoid(a.z[(int64_t)b * a.z_sb + (int64_t)t * a.z_sl + h]) : 0.f;
+    const uint4* tp = reinterpret_cast<const uint4*>(
+        reinterpret_cast<const char*>(a.proj) + (row + a.col_th + h * kS2) * 2);
+    uint4 v0 = make_uint4(0, 0, 0, 0), v1 = make_uint4(0, 0, 0, 0);
+    if (ok) { v0 = tp[0]; v1 = tp[1]; }
+    const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      th[r][2 * i] = unpack_lo<kHalf>(w[i]);
+      th[r][2 * i + 1] = unpack_hi<kHalf>(w[i]);
+    }
+  }
+}
+
+template <bool kHalf>
+__global__ void __launch_bounds__(256) prep_sums_kernel(PrepArgs a) {
+  const int c = blockIdx.x, b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = c * kBlk + 2 * lane;
+  for (int h = warp; h < a.H; h += 8) {
+    float la[2], lf[2], th[2][kS2];
+    load_elems<kHalf>(a, b, h, t0, la, lf, th);
+    float s0, s1, tv[kTot];
+    scan64(la[0], la[1], s0, s1);
+    tv[0] = __shfl_sync(0xffffffffu, s1, 31);
+    scan64(lf[0], lf[1], s0, s1);
+    tv[1] = __shfl_sync(0xffffffffu, s1, 31);
+#pragma unroll
+    for (int p = 0; p < kS2; ++p) {
+      scan64(th[0][p], th[1][p], s0, s1);
+      tv[2 + p] = __shfl_sync(0xffffffffu, s1, 31);
+    }
+    float* dst = a.tot + ((int64_t)(b * a.H + h) * a.nch + c) * kTot;
+    bool bad = false;
+#pragma unroll
+    for (int k = 0; k < kTot; ++k) bad |= !isfinite(tv[k]);
+    if (lane < kTot) {
+      float mine = tv[0];
+#pragma unroll
+      for (int k = 1; k < kTot; ++k) if (lane == k) mine = tv[k];
+      dst[lane] = mine;
+    }
+    if (bad && lane == 0 && a.status) atomicOr(a.status, SISA_ST_NONFINITE);
+  }
+}
+
+// Sequential sum of the totals of blocks [0, c) (component k, computed by lane k, fixed order).
+__device__ __forceinline__ float prefix_total(const float* tot, int64_t bh, int nch, int c, int k) {
+  float acc = 0.f;
+  const float* p = tot + bh * nch * kTot + k;
+#pragma unroll 4
+  for (int cc = 0; cc < c; ++cc) acc += p[(int64_t)cc * kTot];
+  return acc;
+}
+
+template <bool kHalf>
+__global__ void __launch_bounds__(256) prep_fwd_kernel(PrepArgs a) {
+  const int c = blockIdx.x, b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = c * kBlk + 2 * lane;
+  for (int h = warp; h < a.H; h += 8) {
+    const int64_t bh = (int64_t)b * a.H + h;
+    float la[2], lf[2], th[2][kS2];
+    load_elems<kHalf>(a, b, h, t0, la, lf, th);
+    const float mypre = lane < kTot ? prefix_total(a.tot, bh, a.nch, c, lane) : 0.f;
+    float s0, s1;
+    // g, rowf, colf
+    scan64(la[0], la[1], s0, s1);
+    const float pre_g = __shfl_sync(0xffffffffu, mypre, 0);
+    const float g0 = pre_g + s0, g1 = pre_g + s1;
+    const float gs = __shfl_sync(0xffffffffu, g0, 0);
+    const float ge = __shfl_sync(0xffffffffu, g1, 31);   // masked rows add 0: equals the last valid g
+    // F
+    scan64(lf[0], lf[1], s0, s1);
+    const float pre_f = __shfl_sync(0xffffffffu, mypre, 1);
+    const float f0 = pre_f + s0, f1 = pre_f + s1;
+    const float gg[2] = {g0, g1}, ff[2] = {f0, f1};
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int t = t0 + r;
+      if (t < a.L) {
+        const float rowf = exp2f(fminf((gg[r] - gs) * kLog2e, 0.f));
+        const float colf = exp2f(fminf((ge - gg[r]) * kLog2e, 0.f));
+        a.pos[bh * a.L + t] = make_float4(gg[r], ff[r], rowf, colf);
+      }
+    }
+    // Phi and the rotation of C and B
+    float phi[2][kS2];
+#pragma unroll
+    for (int p = 0; p < kS2; ++p) {
+      scan64(th[0][p], th[1][p], s0, s1);
+      const float pre = __shfl_sync(0xffffffffu, mypre, 2 + p);
+      phi[0][p] = pre + s0;
+      phi[1][p] = pre + s1;
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int t = t0 + r;
+      if (t >= a.L) continue;
+      const int64_t row = (int64_t)b * a.proj_sb + (int64_t)t * a.proj_sl;
+      float cs[kS2], sn[kS2];
+#pragma unroll
+      for (int p = 0; p < kS2; ++p) sincosf(phi[r][p], &sn[p], &cs[p]);
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const int col = (which == 0 ? a.col_c : a.col_b) + h * 32;
+        const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.proj) + (row + col) * 2);
+        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(which == 0 ? a.c_rot : a.b_rot) +
+                                              ((bh * a.L + t) * 32) * 2);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 v = src[q];
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+          uint32_t o[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int p = q * 4 + i;
+            const float ze = unpack_lo<kHalf>(w[i]), zo = unpack_hi<kHalf>(w[i]);
+            o[i] = pack2<kHalf>(ze * cs[p] - zo * sn[p], ze * sn[p] + zo * cs[p]);
+          }
+          dst[q] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------ positions
+struct PackArgs {
+  const float* g;
+  int64_t g_sb, g_sh, g_sl;
+  const float* f;
+  int64_t f_sb, f_sh, f_sl;
+  int H, L;
+  float4* pos;
+  int32_t* status;
+};
+
+// One warp per (b*H + h, 64-row block).
+__global__ void __launch_bounds__(256) pack_positions_kernel(PackArgs a, int nch, int64_t nwork) {
+  const int64_t wid = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (wid >= nwork) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t bh = wid / nch;
+  const int c = (int)(wid % nch);
+  const int b = (int)(bh / a.H), h = (int)(bh % a.H);
+  const float* gp = a.g + (int64_t)b * a.g_sb + (int64_t)h * a.g_sh;
+  const float* fp = a.f ? a.f + (int64_t)b * a.f_sb + (int64_t)h * a.f_sh : nullptr;
+  const int base = c * kBlk;
+  const int last = min(base + kBlk - 1, a.L - 1);
+  const float gs = gp[(int64_t)base * a.g_sl];
+  const float ge = gp[(int64_t)last * a.g_sl];
+  bool bad = false;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int t = base + 2 * lane + r;
+    if (t >= a.L) continue;
+    const float g = gp[(int64_t)t * a.g_sl];
+    const float f = fp ? fp[(int64_t)t * a.f_sl] : 0.f;
+    const float rowf = exp2f(fminf((g - gs) * kLog2e, 0.f));
+    const float colf = exp2f(fminf((ge - g) * kLog2e, 0.f));
+    // NaN-propagating clamps, as the reference: a NaN g gives NaN factors.
+    a.pos[bh * a.L + t] = make_float4(g, f, (g != g) ? g : rowf, (g != g) ? g : colf);
+    if (t > 0) {
+      const float inc = g - gp[(int64_t)(t - 1) * a.g_sl];
+      bad |= !(inc <= 1e-3f);
+    }
+  }
+  if (__any_sync(0xffffffffu, bad) && lane == 0 && a.status) atomicOr(a.status, SISA_ST_NONMONOTONE);
+}
+
+// ------------------------------------------------------------------------------------ backward
+struct PrepBwdArgs {
+  const void* proj;
+  int64_t proj_sb, proj_sl;
+  const float* z;
+  int64_t z_sb, z_sl;
+  int B, L, H, nch;
+  int col_b, col_c, col_th, col_a, ntot, npad;
+  const float* tot;        // forward block totals (fp32)
+  const float* dc;         // (B,H,L,32) fp32
+  const float* db;
+  const float* dg;         // (B,H,L)
+  const float* dF;         // (B,H,L) or null
+  void* dproj;
+  int64_t dproj_sb, dproj_sl;
+  float* dz;               // (B,L,H)
+  double* bt;              // (B*H, nch, kTot) fp64
+  int32_t* status;
+};
+
+// Recompute Phi for the two tokens of this lane with the forward's exact code path.
+template <bool kHalf>
+__device__ __forceinline__ void recompute_phi(const PrepBwdArgs& a, int b, int h, int c, int t0, float phi[2][kS2]) {
+  const int lane = threadIdx.x & 31;
+  const int64_t bh = (int64_t)b * a.H + h;
+  float th[2][kS2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int t = t0 + r;
+    const bool ok = t < a.L;
+    const int64_t row = (int64_t)b * a.proj_sb + (int64_t)(ok ? t : 0) * a.proj_sl;
+    const uint4* tp = reinterpret_cast<const uint4*>(
+        reinterpret_cast<const char*>(a.proj) + (row + a.col_th + h * kS2) * 2);
+    uint4 v0 = make_uint4(0, 0, 0, 0), v1 = make_uint4(0, 0, 0, 0);
+    if (ok) { v0 = tp[0]; v1 = tp[1]; }
+    const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      th[r][2 * i] = unpack_lo<kHalf>(w[i]);
+      th[r][2 * i + 1] = unpack_hi<kHalf>(w[i]);
+    }
+  }
+  const float mypre = lane < kTot ? prefix_total(a.tot, bh, a.nch, c, lane) : 0.f;
+#pragma unroll
+  for (int p = 0; p < kS2; ++p) {
+    float s0, s1;
+    scan64(th[0][p], th[1][p], s0, s1);
+    const float pre = __shfl_sync(0xffffffffu, mypre, 2 + p);
+    phi[0][p] = pre + s0;
+    phi[1][p] = pre + s1;
+  }
+}
+
+// d Phi (both rotations) and, when kWrite, the inverse-rotated input gradients of C and B.
+template <bool kHalf, bool kWrite>
+__device__ __forceinline__ void rotation_grads(const PrepBwdArgs& a, int b, int h, int t0, const float phi[2][kS2],
+                                               float dphi[2][kS2]) {
+  const int64_t bh = (int64_t)b * a.H + h;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+#pragma unroll
+    for (int p = 0; p < kS2; ++p) dphi[r][p] = 0.f;
+    const int t = t0 + r;
+    if (t >= a.L) continue;
+    const int64_t row = (int64_t)b * a.proj_sb + (int64_t)t * a.proj_sl;
+    const int64_t drow = (int64_t)b * a.dproj_sb + (int64_t)t * a.dproj_sl;
+    float cs[kS2], sn[kS2];
+#pragma unroll
+    for (int p = 0; p < kS2; ++p) sincosf(phi[r][p], &sn[p], &cs[p]);
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+      const int col = (which == 0 ? a.col_c : a.col_b) + h * 32;
+      const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.proj) + (row + col) * 2);
+      const float4* gsrc = reinterpret_cast<const float4*>((which == 0 ? a.dc : a.db) + (bh * a.L + t) * 32);
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.dproj) + (drow + col) * 2);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 v = src[q];
+        const float4 g0 = gsrc[2 * q], g1 = gsrc[2 * q + 1];
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        const float gd[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int p = q * 4 + i;
+          const float ze = unpack_lo<kHalf>(w[i]), zo = unpack_hi<kHalf>(w[i]);
+          const float oe = ze * cs[p] - zo * sn[p];
+          const float oo = ze * sn[p] + zo * cs[p];
+          const float de = gd[2 * i], dd = gd[2 * i + 1];
+          dphi[r][p] += dd * oe - de * oo;
+          if constexpr (kWrite) o[i] = pack2<kHalf>(de * cs[p] + dd * sn[p], dd * cs[p] - de * sn[p]);
+        }
+        if constexpr (kWrite) dst[q] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+  }
+}
+
+template <bool kHalf>
+__global__ void __launch_bounds__(256) prep_bsums_kernel(PrepBwdArgs a) {
+  const int c = blockIdx.x, b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = c * kBlk + 2 * lane;
+  for (int h = warp; h < a.H; h += 8) {
+    const int64_t bh = (int64_t)b * a.H + h;
+    double x0, x1, r0, r1, tv[kTot];
+    x0 = t0 < a.L ? (double)a.dg[bh * a.L + t0] : 0.0;
+    x1 = t0 + 1 < a.L ? (double)a.dg[bh * a.L + t0 + 1] : 0.0;
+    rscan64(x0, x1, r0, r1);
+    tv[0] = __shfl_sync(0xffffffffu, r0, 0);
+    x0 = (a.dF && t0 < a.L) ? (double)a.dF[bh * a.L + t0] : 0.0;
+    x1 = (a.dF && t0 + 1 < a.L) ? (double)a.dF[bh * a.L + t0 + 1] : 0.0;
+    rscan64(x0, x1, r0, r1);
+    tv[1] = __shfl_sync(0xffffffffu, r0, 0);
+    float phi[2][kS2], dphi[2][kS2];
+    recompute_phi<kHalf>(a, b, h, c, t0, phi);
+    rotation_grads<kHalf, false>(a, b, h, t0, phi, dphi);
+#pragma unroll
+    for (int p = 0; p < kS2; ++p) {
+      rscan64((double)dphi[0][p], (double)dphi[1][p], r0, r1);
+      tv[2 + p] = __shfl_sync(0xffffffffu, r0, 0);
+    }
+    double* dst = a.bt + (bh * a.nch + c) * kTot;
+    if (lane < kTot) {
+      double mine = tv[0];
+#pragma unroll
+      for (int k = 1; k < kTot; ++k) if (lane == k) mine = tv[k];
+      dst[lane] = mine;
+    }
+  }
+}
+
+__device__ __forceinline__ double suffix_total(const double* bt, int64_t bh, int nch, int c, int k) {
+  double acc = 0.0;
+  const double* p = bt + bh * nch * kTot + k;
+#pragma unroll 4
+  for (int cc = c + 1; cc < nch; ++cc) acc += p[(int64_t)cc * kTot];
+  return acc;
+}
+
+template <bool kHalf>
+__device__ __forceinline__ void st_lp(void* p, int64_t i, float v) {
+  if constexpr (kHalf) reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
+  else reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+}
+
+template <bool kHalf>
+__global__ void __launch_bounds__(256) prep_bwd_kernel(PrepBwdArgs a) {
+  const int c = blockIdx.x, b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = c * kBlk + 2 * lane;
+  for (int h = warp; h < a.H; h += 8) {
+    const int64_t bh = (int64_t)b * a.H + h;
+    const double mysuf = lane < kTot ? suffix_total(a.bt, bh, a.nch, c, lane) : 0.0;
+    double x0, x1, r0, r1;
+    // d alpha = -(sum_{s>=t} dg_s) * softplus'(alpha)
+    x0 = t0 < a.L ? (double)a.dg[bh * a.L + t0] : 0.0;
+    x1 = t0 + 1 < a.L ? (double)a.dg[bh * a.L + t0 + 1] : 0.0;
+    rscan64(x0, x1, r0, r1);
+    {
+      const double suf = __shfl_sync(0xffffffffu, mysuf, 0);
+      const double rr[2] = {r0, r1};
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int t = t0 + r;
+        if (t >= a.L) continue;
+        const float dla = (float)(suf + rr[r]);
+        const int64_t row = (int64_t)b * a.proj_sb + (int64_t)t * a.proj_sl;
+        const float al = ld_lp<kHalf>(a.proj, row + a.col_a + h);
+        st_lp<kHalf>(a.dproj, (int64_t)b * a.dproj_sb + (int64_t)t * a.dproj_sl + a.col_a + h,
+                     -dla * softplus_grad(al));
+      }
+    }
+    // dz = (sum_{s>=t} dF_s) * logsigmoid'(z)
+    if (a.z) {
+      x0 = (a.dF && t0 < a.L) ? (double)a.dF[bh * a.L + t0] : 0.0;
+      x1 = (a.dF && t0 + 1 < a.L) ? (double)a.dF[bh * a.L + t0 + 1] : 0.0;
+      rscan64(x0, x1, r0, r1);
+      const double suf = __shfl_sync(0xffffffffu, mysuf, 1);
+      const double rr[2] = {r0, r1};
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int t = t0 + r;
+        if (t >= a.L) continue;
+        const float dlf = (float)(suf + rr[r]);
+        const float zv = a.z[(int64_t)b * a.z_sb + (int64_t)t * a.z_sl + h];
+        a.dz[((int64_t)b * a.L + t) * a.H + h] = dlf * logsigmoid_grad(zv);
+      }
+    }
+    // inverse rotation of C/B, d theta = sum_{s>=t} dPhi_s
+    float phi[2][kS2], dphi[2][kS2];
+    recompute_phi<kHalf>(a, b, h, c, t0, phi);
+    rotation_grads<kHalf, true>(a, b, h, t0, phi, dphi);
+    float dth[2][kS2];
+#pragma unroll
+    for (int p = 0; p < kS2; ++p) {
+      rscan64((double)dphi[0][p], (double)dphi[1][p], r0, r1);
+      const double suf = __shfl_sync(0xffffffffu, mysuf, 2 + p);
+      dth[0][p] = (float)(suf + r0);
+      dth[1][p] = (float)(suf + r1);
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int t = t0 + r;
+      if (t >= a.L) continue;
+      uint32_t o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = pack2<kHalf>(dth[r][2 * i], dth[r][2 * i + 1]);
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.dproj) +
+                                            ((int64_t)b * a.dproj_sb + (int64_t)t * a.dproj_sl + a.col_th + h * kS2) * 2);
+      dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+      dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+    }
+  }
+  // zero the padding columns [ntot, npad) of this block's rows
+  const int npadc = a.npad - a.ntot;
+  if (npadc > 0) {
+    for (int i = threadIdx.x; i < kBlk * npadc; i += blockDim.x) {
+      const int t = c * kBlk + i / npadc;
+      if (t < a.L) st_lp<kHalf>(a.dproj, (int64_t)b * a.dproj_sb + (int64_t)t * a.dproj_sl + a.ntot + i % npadc, 0.f);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------ launchers
+cudaError_t launch_prep_fwd(const PrepFwdLaunch& p, cudaStream_t st) {
+  PrepArgs a;
+  a.proj = p.proj; a.proj_sb = p.proj_sb; a.proj_sl = p.proj_sl;
+  a.z = p.z; a.z_sb = p.z_sb; a.z_sl = p.z_sl;
+  a.B = (int)p.B; a.L = (int)p.L; a.H = (int)p.H; a.nch = (int)((p.L + kBlk - 1) / kBlk);
+  a.col_b = (int)p.col_b; a.col_c = (int)p.col_c; a.col_th = (int)p.col_th; a.col_a = (int)p.col_a;
+  a.c_rot = p.c_rot; a.b_rot = p.b_rot; a.pos = reinterpret_cast<float4*>(p.pos);
+  a.tot = p.tot; a.status = p.status;
+  dim3 grid(a.nch, a.B);
+  if (p.dtype == 1) {
+    prep_sums_kernel<true><<<grid, 256, 0, st>>>(a);
+    prep_fwd_kernel<true><<<grid, 256, 0, st>>>(a);
+  } else {
+    prep_sums_kernel<false><<<grid, 256, 0, st>>>(a);
+    prep_fwd_kernel<false><<<grid, 256, 0, st>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pack_positions(const PackLaunch& p, cudaStream_t st) {
+  PackArgs a;
+  a.g = p.g; a.g_sb = p.g_sb; a.g_sh = p.g_sh; a.g_sl = p.g_sl;
+  a.f = p.f; a.f_sb = p.f_sb; a.f_sh = p.f_sh; a.f_sl = p.f_sl;
+  a.H = (int)p.H; a.L = (int)p.L; a.pos = reinterpret_cast<float4*>(p.pos); a.status = p.status;
+  const int nch = (int)((p.L + kBlk - 1) / kBlk);
+  const int64_t nwork = p.B * p.H * nch;
+  pack_positions_kernel<<<(unsigned)((nwork + 7) / 8), 256, 0, st>>>(a, nch, nwork);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prep_bwd(const PrepBwdLaunch& p, cudaStream_t st) {
+  PrepBwdArgs a;
+  a.proj = p.proj; a.proj_sb = p.proj_sb; a.proj_sl = p.proj_sl;
+  a.z = p.z; a.z_sb = p.z_sb; a.z_sl = p.z_sl;
+  a.B = (int)p.B; a.L = (int)p.L; a.H = (int)p.H; a.nch = (int)((p.L + kBlk - 1) / kBlk);
+  a.col_b = (int)p.col_b; a.col_c = (int)p.col_c; a.col_th = (int)p.col_th; a.col_a = (int)p.col_a;
+  a.ntot = (int)p.ntot; a.npad = (int)p.npad;
+  a.tot = p.tot; a.dc = p.dc; a.db = p.db; a.dg = p.dg; a.dF = p.dF;
+  a.dproj = p.dproj; a.dproj_sb = p.dproj_sb; a.dproj_sl = p.dproj_sl; a.dz = p.dz; a.bt = p.bt;
+  a.status = p.status;
+  dim3 grid(a.nch, a.B);
+  if (p.dtype == 1) {
+    prep_bsums_kernel<true><<<grid, 256, 0, st>>>(a);
+    prep_bwd_kernel<true><<<grid, 256, 0, st>>>(a);
+  } else {
+    prep_bsums_kernel<false><<<grid, 256, 0, st>>>(a);
+    prep_bwd_kernel<false><<<grid, 256, 0, st>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace sisa

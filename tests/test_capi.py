@@ -1,0 +1,69 @@
+"""The C ABI library loads and exports every entry point declared in include/*.h (no GPU calls)."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from sisa_b200 import _lib
+
+INCLUDE = Path(__file__).resolve().parents[1] / "include"
+
+
+def declared_symbols() -> list[str]:
+    names = []
+    for h in sorted(INCLUDE.glob("*.h")):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names += re.findall(r"^\s*(?:const\s+)?\w+\**\s+\**(sisa_\w+)\s*\(", text, flags=re.M)
+    return sorted(set(names))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.load()
+    declared = declared_symbols()
+    assert len(declared) >= 12
+    missing = [n for n in declared if not hasattr(lib, n)]
+    assert not missing, missing
+    # the binding knows every declared symbol (argument types attached)
+    assert set(declared) <= set(_lib.SIGNATURES), sorted(set(declared) - set(_lib.SIGNATURES))
+
+
+def test_version_and_layout():
+    lib = _lib.load()
+    assert b"sm_100a" in lib.sisa_version()
+    out = (ctypes.c_int64 * 9)()
+    for h, npad in ((8, 2192), (12, 3280), (16, 4368)):
+        assert lib.sisa_fused_layout(h, out) == 0
+        assert list(out) == [0, 64 * h, 128 * h, 192 * h, 224 * h, 256 * h, 272 * h, 273 * h, npad]
+    assert lib.sisa_fused_layout(0, out) == _lib.ERR_VALUE
+    assert "n_head" in _lib.last_error()
+
+
+def test_layout_agrees_with_python_and_oracle(golden):
+    from oracle import sisa_oracle as O
+    from sisa_b200.kernels.fused import fused_layout
+
+    for h, lay in golden("known")["layouts"].items():
+        assert fused_layout(h) == lay == O.fused_layout(h)
+
+
+def test_workspace_sizes():
+    lib = _lib.load()
+    assert lib.sisa_prep_fwd_workspace(2, 3, 130) == 2 * 3 * 3 * 18 * 4
+    assert lib.sisa_prep_bwd_workspace(2, 3, 130) == 2 * 3 * 3 * 18 * 8
+    assert lib.sisa_attn_bwd_workspace(2, 3, 130) == 2 * 3 * 130 * 28
+
+
+def test_host_side_argument_errors_need_no_gpu():
+    """Validation happens before any CUDA call: bad shapes return SISA_ERR_VALUE with a message."""
+    lib = _lib.load()
+    rc = lib.sisa_prep_fwd(None, 0, 10, 2, 0, 0, 0, None, 0, 0, None, None, None, None, None, None)
+    assert rc == _lib.ERR_VALUE and "B, H and L" in _lib.last_error()
+    with pytest.raises(ValueError):
+        _lib.check(rc, "sisa_prep_fwd")
+    rc = lib.sisa_prep_fwd(None, 1, 10, 2, 0, 0, 7, None, 0, 0, None, None, None, None, None, None)
+    assert rc == _lib.ERR_TYPE
+    with pytest.raises(TypeError):
+        _lib.check(rc, "sisa_prep_fwd")
