@@ -110,21 +110,33 @@ def attention_grads(q, k, v, c, b, g, lam, fgate, dout, dtype=torch.float64):
     return res
 
 
-def fused_layer(proj, z, lam, n_head, dtype=torch.float64):
-    """y = heads-concatenated attention output of the fused layer core (src/sisa/kernels/fused_prep.py:637-683)."""
+def _round_through(x: torch.Tensor, lowp) -> torch.Tensor:
+    """Value rounded to ``lowp``, gradient passed through: the ``.to(compute_dtype)`` of the reference's
+    torch glue under autocast (src/sisa/modeling.py:197-199)."""
+    if lowp is None:
+        return x
+    return x + (x.detach().to(lowp).to(x.dtype) - x.detach())
+
+
+def fused_layer(proj, z, lam, n_head, dtype=torch.float64, lowp=None):
+    """y = heads-concatenated attention output of the fused layer core (src/sisa/kernels/fused_prep.py:637-683).
+
+    ``lowp`` (e.g. torch.bfloat16) rounds the rotated c/b to the compute dtype as the reference's glue does
+    before the attention; everything else stays in ``dtype``."""
     pr = prep(proj, z, n_head, dtype)
-    o, lse = attention(pr["q"], pr["k"], pr["v"], pr["c"], pr["b"], pr["g"], lam.to(dtype), pr["F"])
+    c, b = _round_through(pr["c"], lowp), _round_through(pr["b"], lowp)
+    o, lse = attention(pr["q"], pr["k"], pr["v"], c, b, pr["g"], lam.to(dtype), pr["F"])
     B, H, L, D = o.shape
     return o.transpose(1, 2).reshape(B, L, H * D), lse, pr
 
 
-def fused_layer_grads(proj, z, lam, n_head, dy, dtype=torch.float64):
+def fused_layer_grads(proj, z, lam, n_head, dy, dtype=torch.float64, lowp=None):
     """fp64 gradients of the fused layer w.r.t. proj, z and lam (the reference's ref64_fused pattern,
-    tests/test_fused_prep.py:173-201, without pass-through values). Returns y, dproj, dz, dlam."""
+    tests/test_fused_prep.py:173-201). Returns y, dproj, dz, dlam."""
     P = proj.detach().to(dtype).requires_grad_(True)
     Z = None if z is None else z.detach().to(dtype).requires_grad_(True)
     LAM = lam.detach().to(dtype).requires_grad_(True)
-    y, _, _ = fused_layer(P, Z, LAM, n_head, dtype)
+    y, _, _ = fused_layer(P, Z, LAM, n_head, dtype, lowp=lowp)
     ins = [P, LAM] + ([Z] if Z is not None else [])
     gr = torch.autograd.grad(y, ins, dy.to(dtype))
     return y.detach(), gr[0], (gr[2] if Z is not None else None), gr[1]

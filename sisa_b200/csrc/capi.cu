@@ -85,6 +85,20 @@ int map_records(CUtensorMap* m, const void* ptr, int64_t BH, int64_t L, const ch
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Tensor-map encoding is a driver call that needs a current context on the calling thread. A thread
+// that has not touched CUDA yet (e.g. an autograd worker) has none, so bind the device that owns the
+// data before encoding. cudaSetDevice initialises that device's primary context if needed.
+int bind_device_of(const void* ptr) {
+  cudaPointerAttributes a;
+  cudaError_t e = cudaPointerGetAttributes(&a, ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaPointerGetAttributes");
+  if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged)
+    return fail(SISA_ERR_VALUE, "tensor data is not device memory");
+  e = cudaSetDevice(a.device);   // makes the primary context current on this thread
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  return SISA_OK;
+}
+
 int check_view(const sisa_view4* v, int elem_bytes, const char* name) {
   if (!v || !v->data) return fail(SISA_ERR_VALUE, "%s: null view", name);
   if (!aligned16(v->data)) return fail(SISA_ERR_ALIGN, "%s: data pointer is not 16-byte aligned", name);
@@ -201,6 +215,7 @@ int sisa_attn_fwd(const sisa_view4* q, const sisa_view4* k, const sisa_view4* v,
     return rc;
   if (!pos || !lam || !lse) return fail(SISA_ERR_VALUE, "sisa_attn_fwd: null pos, lam or lse");
   if (!aligned16(pos) || (o32 && !aligned16(o32))) return fail(SISA_ERR_ALIGN, "pos/o32 must be 16-byte aligned");
+  if ((rc = bind_device_of(q->data))) return rc;
   const CUtensorMapDataType dt = dtype == SISA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   sisa::FwdParams p;
   memset(&p, 0, sizeof(p));
@@ -237,6 +252,7 @@ int sisa_attn_bwd(const sisa_view4* q, const sisa_view4* k, const sisa_view4* v,
     return fail(SISA_ERR_VALUE, "sisa_attn_bwd: null pos, lam, lse, dg, dlam or workspace");
   if (!aligned16(pos) || !aligned16(workspace) || (o32 && !aligned16(o32)))
     return fail(SISA_ERR_ALIGN, "pos, o32 and workspace must be 16-byte aligned");
+  if ((rc = bind_device_of(q->data))) return rc;
   const CUtensorMapDataType dt = dtype == SISA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   sisa::BwdParams p;
   memset(&p, 0, sizeof(p));

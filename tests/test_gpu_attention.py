@@ -126,7 +126,9 @@ def test_fused_layer_grads(cuda_dev, L, H):
     y = sisa_fused(P, Z, LAM, H)
     y.backward(dy.to(cuda_dev))
     torch.cuda.synchronize()
-    y64, dproj64, dz64, dlam64 = O.fused_layer_grads(proj.double(), z.double(), lam.double(), H, dy.double())
+    # truth: fp64 with c~/b~ rounded to bf16 before the attention, as the reference's torch glue does
+    y64, dproj64, dz64, dlam64 = O.fused_layer_grads(proj.double(), z.double(), lam.double(), H, dy.double(),
+                                                     lowp=torch.bfloat16)
     assert max_abs(y.cpu(), y64) <= OUT_MAX_ABS
     off = O.fused_layout(H)
     dP = P.grad.cpu()
