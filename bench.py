@@ -62,7 +62,7 @@ class Clocks:
                 ["nvidia-smi", f"--id={self.index}",
                  "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
                  "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "200"],
+                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
@@ -207,7 +207,7 @@ def run_cuda(args):
     ok, why = backends.cuda_status(local)
     if not ok:
         raise RuntimeError(f"cuda kernels unavailable: {why}")
-    step = Step(dev, seed=1234 + rank)
+    step = Step(dev, b=args.B, t=args.T, h=args.H, seed=1234 + rank)
     stream = torch.cuda.current_stream(dev)
     st = stream.cuda_stream
     for _ in range(args.warmup):
@@ -236,31 +236,32 @@ def run_cuda(args):
     if world > 1:
         torch.distributed.all_reduce(ms_t, op=torch.distributed.ReduceOp.MAX)
     ms_max = float(ms_t.item())
-    total_flop = FLOP_PER_PAIR * pairs(B, H, T) * args.steps * world
+    b_, t_, h_ = args.B, args.T, args.H
+    total_flop = FLOP_PER_PAIR * pairs(b_, h_, t_) * args.steps * world
     value = total_flop / (ms_max * 1e-3) / 1e12
 
     # ---- e2e: host buffers in and out through the same C-ABI calls
-    e2e = run_e2e(step, dev, args, world)
+    e2e = None if args.no_e2e else run_e2e(step, dev, args, world)
 
     if rank == 0:
         burst, sustained, hbm, src = measured_peaks()
         att_ms = per["attn_fwd"] + per["attn_bwd"]
-        ach = FLOP_PER_PAIR * pairs(B, H, T) / (att_ms * 1e-3) / 1e12
-        prep_bytes = 302 * B * T * H
+        ach = FLOP_PER_PAIR * pairs(b_, h_, t_) / (att_ms * 1e-3) / 1e12
+        prep_bytes = 302 * b_ * t_ * h_
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "cfg1: fused prep + SISA attention fwd+bwd (sisa_fused step)", "B": B, "T": T,
-                       "H": H, "d_head": 64, "d_state": 32, "parallelism": f"replicas x{world} (per-rank batch)",
+            "config": {"workload": "cfg1: fused prep + SISA attention fwd+bwd (sisa_fused step)", "B": b_, "T": t_,
+                       "H": h_, "d_head": 64, "d_state": 32, "parallelism": f"replicas x{world} (per-rank batch)",
                        "l2": "inputs larger than L2 (proj %.0f MB)" % (step.proj.numel() * 2 / 1e6),
                        "flop_per_pair": FLOP_PER_PAIR},
             "roofline": {"kernel": "sisa_attn_fwd + sisa_attn_bwd (tcgen05)", "bound": "tensor",
                          "achieved": round(ach, 3), "peak": burst, "unit": "TFLOP/s", "frac": round(ach / burst, 4),
                          "peak_source": f"{src} bf16 burst", "traffic": None,
                          "per_call_ms": {k: round(v, 4) for k, v in per.items()},
-                         "attn_fwd_tflops": round(FWD_FLOP_PER_PAIR * pairs(B, H, T) / (per["attn_fwd"] * 1e-3) / 1e12, 3),
-                         "attn_bwd_tflops": round((FLOP_PER_PAIR - FWD_FLOP_PER_PAIR) * pairs(B, H, T) /
+                         "attn_fwd_tflops": round(FWD_FLOP_PER_PAIR * pairs(b_, h_, t_) / (per["attn_fwd"] * 1e-3) / 1e12, 3),
+                         "attn_bwd_tflops": round((FLOP_PER_PAIR - FWD_FLOP_PER_PAIR) * pairs(b_, h_, t_) /
                                                   (per["attn_bwd"] * 1e-3) / 1e12, 3),
                          "prep_fwd_gbs": round(prep_bytes / (per["prep_fwd"] * 1e-3) / 1e9, 1),
                          "hbm_peak_gbs": hbm},
@@ -281,11 +282,12 @@ def run_e2e(step, dev, args, world):
     hz = step.z.cpu().pin_memory()
     hdy = step.dy.cpu().pin_memory()
     out_dproj = torch.empty(step.dproj.shape, dtype=step.dproj.dtype, pin_memory=True)
-    out_y = torch.empty((B, T, H * 64), dtype=torch.bfloat16, pin_memory=True)
+    b_, t_, h_ = step.b, step.t, step.h
+    out_y = torch.empty((b_, t_, h_ * 64), dtype=torch.bfloat16, pin_memory=True)
     out_dz = torch.empty(step.dz.shape, dtype=torch.float32, pin_memory=True)
-    out_dlam = torch.empty((H,), dtype=torch.float32, pin_memory=True)
+    out_dlam = torch.empty((h_,), dtype=torch.float32, pin_memory=True)
     st = torch.cuda.current_stream(dev).cuda_stream
-    y_view = step.o.transpose(1, 2).reshape(B, T, H * 64)   # view of o's (B, T, H, 64) storage
+    y_view = step.o.transpose(1, 2).reshape(b_, t_, h_ * 64)   # view of o's (B, T, H, 64) storage
 
     def one():
         step.proj.copy_(hp, non_blocking=True)
@@ -315,7 +317,7 @@ def run_e2e(step, dev, args, world):
     ms = float(ms.item())
     h2d = hp.numel() * 2 + hz.numel() * 4 + hdy.numel() * 2
     d2h = out_y.numel() * 2 + out_dproj.numel() * 2 + out_dz.numel() * 4 + out_dlam.numel() * 4
-    v = FLOP_PER_PAIR * pairs(B, H, T) * n * world / (ms * 1e-3) / 1e12
+    v = FLOP_PER_PAIR * pairs(b_, h_, t_) * n * world / (ms * 1e-3) / 1e12
     return {"value": round(v, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": round(ms / n, 3), "steps": n}
 
@@ -377,11 +379,15 @@ def run_reference(args):
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["cuda", "reference"], default="cuda")
     ap.add_argument("--cpu-sample-heads", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--B", type=int, default=B, help="batch (default: config 1)")
+    ap.add_argument("--T", type=int, default=T, help="sequence length (default: config 1)")
+    ap.add_argument("--H", type=int, default=H, help="heads (default: config 1)")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         run_reference(args)
