@@ -121,6 +121,37 @@ int sisa_prep_bwd(const void* proj, int64_t B, int64_t L, int64_t H, int64_t pro
                   void* dproj, int64_t dproj_sb, int64_t dproj_sl, float* dz,
                   void* workspace, int32_t* status, void* stream);
 
+/* Chunked linear + cross-entropy over a tied LM head (src/sisa/kernels/linear_ce.py:60-196).
+ * sisa_lce_logits: logits (R, Vp) = x (R, D) . w (Vp, D)^T on tcgen05, stored in `dtype` (rounded as
+ *   under autocast) at logits (row stride logits_ld), plus per (row, 256-column tile) online
+ *   max/sum-exp over the first V columns and the label's logit, kept in `workspace`
+ *   (sisa_lce_workspace(R, Vp) bytes). D a multiple of 64, Vp >= V a multiple of 256, w rows [V, Vp) zero.
+ * sisa_lce_grad: per row lse, loss_rows[r] = lse - logit[label] (0 for ignore_index), and, when
+ *   compute_grad, G = (softmax - onehot) * (*inv_n) * grad_scale written over the logits in place
+ *   (padding columns 0). inv_n is a device scalar (1 / number of non-ignored rows).
+ * The gradient GEMMs dx = G . w and dw += G^T . x are plain GEMMs left to the caller (cuBLAS). */
+int64_t sisa_lce_workspace(int64_t R, int64_t Vp);
+int sisa_lce_logits(const void* x, int64_t R, int64_t D, int64_t x_ld, const void* w, int64_t V, int64_t Vp,
+                    int64_t w_ld, int dtype, const int64_t* labels, void* logits, int64_t logits_ld,
+                    void* workspace, int32_t* status, void* stream);
+int sisa_lce_grad(void* logits, int64_t logits_ld, int64_t R, int64_t V, int64_t Vp, int dtype,
+                  const int64_t* labels, int64_t ignore_index, const float* inv_n, float grad_scale,
+                  int compute_grad, const void* workspace, float* loss_rows, int32_t* status, void* stream);
+
+/* Incremental decode: one new query row per (batch, head) against N cached keys
+ * (src/sisa/modeling.py:224-238 via src/sisa/functional.py:69-103, src/sisa/generation.py:58-95):
+ *   s_j = q.k_j/8 + lam_h exp(min(g_q - g_j, 0)) (c.b_j) + (F_q - F_j), y = softmax(s) v, in fp32.
+ * q: (B, H, 1, 64) and c: (B, H, 1, 32) views in `dtype`; g_q, f_q: (B, H) fp32 contiguous (f_q may be
+ * NULL, then f_cache must be NULL too). k_cache, v_cache: (B, H, >=N, 64) and b_cache: (B, H, >=N, 32) views;
+ * g_cache, f_cache: fp32 with element (b, h, j) at (b*H + h)*gf_stride + j. y: (B, H, 1, 64) view.
+ * workspace: sisa_decode_workspace(B, H, N) bytes (split-K partials). */
+int64_t sisa_decode_workspace(int64_t B, int64_t H, int64_t N);
+int sisa_decode_attn(const sisa_view4* q, const sisa_view4* c, const float* g_q, const float* f_q,
+                     const sisa_view4* k_cache, const sisa_view4* v_cache, const sisa_view4* b_cache,
+                     const float* g_cache, const float* f_cache, int64_t gf_stride, const float* lam,
+                     int64_t B, int64_t H, int64_t N, int dtype, const sisa_view4* y, void* workspace,
+                     int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,6 +13,8 @@
 #include "sisa_b200.h"
 #include "attn.h"
 #include "prep.h"
+#include "decode.h"
+#include "lce.h"
 
 namespace {
 
@@ -326,6 +328,120 @@ int sisa_prep_bwd(const void* proj, int64_t B, int64_t L, int64_t H, int64_t pro
   p.bt = static_cast<double*>(workspace); p.status = status;
   cudaError_t e = sisa::launch_prep_bwd(p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_prep_bwd launch");
+}
+
+int64_t sisa_decode_workspace(int64_t B, int64_t H, int64_t N) {
+  return (int64_t)sisa::decode_splits(B, H, N) * B * H * 66 * 4;
+}
+
+int sisa_decode_attn(const sisa_view4* q, const sisa_view4* c, const float* g_q, const float* f_q,
+                     const sisa_view4* k_cache, const sisa_view4* v_cache, const sisa_view4* b_cache,
+                     const float* g_cache, const float* f_cache, int64_t gf_stride, const float* lam, int64_t B,
+                     int64_t H, int64_t N, int dtype, const sisa_view4* y, void* workspace, int32_t* status,
+                     void* stream) {
+  int rc;
+  if ((rc = check_dims(B, H, N)) || (rc = check_dtype(dtype))) return rc;
+  if ((rc = check_view(q, 2, "q")) || (rc = check_view(c, 2, "c")) || (rc = check_view(k_cache, 2, "k_cache")) ||
+      (rc = check_view(v_cache, 2, "v_cache")) || (rc = check_view(b_cache, 2, "b_cache")) ||
+      (rc = check_view(y, 2, "y")))
+    return rc;
+  if (!g_q || !g_cache || !lam || !workspace) return fail(SISA_ERR_VALUE, "sisa_decode_attn: null pointer");
+  if ((f_q == nullptr) != (f_cache == nullptr))
+    return fail(SISA_ERR_VALUE, "sisa_decode_attn: f_q and f_cache must both be given or both be null");
+  if (gf_stride < N) return fail(SISA_ERR_VALUE, "g/F cache row stride %lld < N %lld", (long long)gf_stride,
+                                 (long long)N);
+  sisa::DecodeParams p{};
+  p.q = static_cast<const char*>(q->data); p.q_sb = q->stride_b; p.q_sh = q->stride_h;
+  p.c = static_cast<const char*>(c->data); p.c_sb = c->stride_b; p.c_sh = c->stride_h;
+  p.g_q = g_q; p.f_q = f_q;
+  p.k = static_cast<const char*>(k_cache->data); p.k_sb = k_cache->stride_b; p.k_sh = k_cache->stride_h;
+  p.k_sl = k_cache->stride_l;
+  p.v = static_cast<const char*>(v_cache->data); p.v_sb = v_cache->stride_b; p.v_sh = v_cache->stride_h;
+  p.v_sl = v_cache->stride_l;
+  p.bm = static_cast<const char*>(b_cache->data); p.b_sb = b_cache->stride_b; p.b_sh = b_cache->stride_h;
+  p.b_sl = b_cache->stride_l;
+  p.g = g_cache; p.f = f_cache; p.gf_stride = gf_stride; p.lam = lam;
+  p.y = static_cast<char*>(y->data); p.y_sb = y->stride_b; p.y_sh = y->stride_h;
+  p.ws = static_cast<float*>(workspace);
+  p.B = (int)B; p.H = (int)H; p.N = (int)N; p.splits = sisa::decode_splits(B, H, N);
+  p.status = status;
+  cudaError_t e = sisa::launch_decode(p, dtype, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_decode_attn launch");
+}
+
+int64_t sisa_lce_workspace(int64_t R, int64_t Vp) {
+  const int64_t nblk = (Vp + 255) / 256;
+  return R * nblk * 8 + ((R * 4 + 255) / 256) * 256;
+}
+
+int sisa_lce_logits(const void* x, int64_t R, int64_t D, int64_t x_ld, const void* w, int64_t V, int64_t Vp,
+                    int64_t w_ld, int dtype, const int64_t* labels, void* logits, int64_t logits_ld,
+                    void* workspace, int32_t* status, void* stream) {
+  int rc;
+  if ((rc = check_dtype(dtype))) return rc;
+  if (!x || !w || !labels || !logits || !workspace) return fail(SISA_ERR_VALUE, "sisa_lce_logits: null pointer");
+  if (R < 1 || D < 64 || D % 64 || V < 1 || Vp % 256 || Vp < V)
+    return fail(SISA_ERR_VALUE, "sisa_lce_logits: need R >= 1, D a multiple of 64, Vp >= V a multiple of 256 "
+                "(R=%lld D=%lld V=%lld Vp=%lld)", (long long)R, (long long)D, (long long)V, (long long)Vp);
+  if (!aligned16(x) || !aligned16(w) || !aligned16(logits) || x_ld % 8 || w_ld % 8 || logits_ld % 8 ||
+      x_ld < D || w_ld < D || logits_ld < Vp)
+    return fail(SISA_ERR_ALIGN, "sisa_lce_logits: rows must be 16-byte aligned (ld multiple of 8 and >= width)");
+  if ((rc = bind_device_of(x))) return rc;
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(SISA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const CUtensorMapDataType dt = dtype == SISA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  sisa::LceParams p;
+  memset(&p, 0, sizeof(p));
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)R};
+    cuuint64_t strides[1] = {(cuuint64_t)(x_ld * 2)};
+    cuuint32_t box[2] = {64, 128}, es[2] = {1, 1};
+    if (enc(&p.tm_x, dt, 2, const_cast<void*>(x), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+      return fail(SISA_ERR_ALIGN, "x: cuTensorMapEncodeTiled failed");
+  }
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)Vp};
+    cuuint64_t strides[1] = {(cuuint64_t)(w_ld * 2)};
+    cuuint32_t box[2] = {64, 256}, es[2] = {1, 1};
+    if (enc(&p.tm_w, dt, 2, const_cast<void*>(w), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+        CUDA_SUCCESS)
+      return fail(SISA_ERR_ALIGN, "w: cuTensorMapEncodeTiled failed");
+  }
+  const int64_t nblk = Vp / 256;
+  p.logits = static_cast<char*>(logits); p.ld = logits_ld;
+  p.part = static_cast<float2*>(workspace);
+  p.tgt = reinterpret_cast<float*>(static_cast<char*>(workspace) + R * nblk * 8);
+  p.labels = labels;
+  p.R = (int)R; p.D = (int)D; p.V = (int)V; p.Vp = (int)Vp; p.n_mblk = (int)((R + 127) / 128); p.n_nblk = (int)nblk;
+  p.status = status;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaError_t e = sisa::launch_lce_logits(p, dtype, sms, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_lce_logits launch");
+}
+
+int sisa_lce_grad(void* logits, int64_t logits_ld, int64_t R, int64_t V, int64_t Vp, int dtype,
+                  const int64_t* labels, int64_t ignore_index, const float* inv_n, float grad_scale,
+                  int compute_grad, const void* workspace, float* loss_rows, int32_t* status, void* stream) {
+  int rc;
+  if ((rc = check_dtype(dtype))) return rc;
+  if (!logits || !labels || !inv_n || !workspace || !loss_rows) return fail(SISA_ERR_VALUE, "sisa_lce_grad: null pointer");
+  if (R < 1 || Vp % 256 || Vp < V || logits_ld < Vp || logits_ld % 8 || !aligned16(logits))
+    return fail(SISA_ERR_VALUE, "sisa_lce_grad: bad shape or alignment");
+  const int64_t nblk = Vp / 256;
+  sisa::LceGradParams p{};
+  p.logits = static_cast<char*>(logits); p.ld = logits_ld;
+  p.part = static_cast<const float2*>(workspace);
+  p.tgt = reinterpret_cast<const float*>(static_cast<const char*>(workspace) + R * nblk * 8);
+  p.labels = labels; p.inv_n = inv_n; p.gscale = grad_scale; p.loss_rows = loss_rows;
+  p.ignore_index = ignore_index; p.R = (int)R; p.V = (int)V; p.Vp = (int)Vp; p.n_nblk = (int)nblk;
+  p.compute_grad = compute_grad; p.status = status;
+  cudaError_t e = sisa::launch_lce_grad(p, dtype, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_lce_grad launch");
 }
 
 }  // extern "C"

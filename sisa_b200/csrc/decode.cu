@@ -1,0 +1,205 @@
+// decode.cu - incremental-decode attention: one new query row per (batch, head) against the cache.
+//
+// Reference semantics: src/sisa/modeling.py:224-238 (decode step) via src/sisa/functional.py:69-103,
+// computed in fp32 over the low-precision cache: for every cached key j (all j <= the new position)
+//   s_j = q.k_j / 8 + lam_h exp(min(g_q - g_j, 0)) (c.b~_j) + (F_q - F_j),   y = sum_j softmax(s)_j v_j.
+//
+// HBM-bound: per cached key and head it reads k (128 B), v (128 B), b~ (64 B), g and F (8 B).
+// Split-K over the key axis: grid (splits, B*H); each CTA (256 threads) walks its key range in chunks
+// of 256 keys - phase 1 one thread per key computes the score from its k / b~ rows, phase 2 the chunk
+// maximum, phase 3 p = 2^(x - m), phase 4 every warp accumulates p v over its keys with one lane per pair
+// of head dimensions (coalesced 128-byte v rows). A second kernel merges the splits' (m, l, acc).
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "sm100.cuh"
+#include "decode.h"
+
+namespace sisa {
+namespace dec {
+
+constexpr int NT = 256;          // threads per CTA = keys per chunk
+constexpr int NW = NT / 32;
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <bool kHalf>
+__device__ __forceinline__ void load_row(const char* p, int n16, float* out) {
+  // n16 chunks of 16 bytes (8 low-precision values each)
+#pragma unroll
+  for (int i = 0; i < n16; ++i) {
+    const uint4 v = reinterpret_cast<const uint4*>(p)[i];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      out[i * 8 + 2 * e] = unpack_lo<kHalf>(w[e]);
+      out[i * 8 + 2 * e + 1] = unpack_hi<kHalf>(w[e]);
+    }
+  }
+}
+
+template <bool kHalf>
+__global__ void __launch_bounds__(NT) decode_split_kernel(DecodeParams p) {
+  const int split = blockIdx.x, bh = blockIdx.y;
+  const int b = bh / p.H, h = bh % p.H;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int per = (p.N + p.splits - 1) / p.splits;
+  const int j_begin = split * per;
+  const int j_end = min(p.N, j_begin + per);
+
+  __shared__ float s_x[NT];
+  __shared__ float s_red[NW];
+  __shared__ float s_acc[NW][64];
+  __shared__ float s_l[NW];
+
+  // query row and its side values (fp32)
+  float q[64], c[32];
+  load_row<kHalf>(p.q + 2 * ((int64_t)b * p.q_sb + (int64_t)h * p.q_sh), 8, q);
+  load_row<kHalf>(p.c + 2 * ((int64_t)b * p.c_sb + (int64_t)h * p.c_sh), 4, c);
+  const float gq = p.g_q[bh];
+  const float fq = p.f_q ? p.f_q[bh] : 0.f;
+  const float lam = p.lam[h];
+  const float c1 = 0.125f * kLog2e;
+  const float lam2 = lam * kLog2e;
+  const char* kbase = p.k + 2 * ((int64_t)b * p.k_sb + (int64_t)h * p.k_sh);
+  const char* vbase = p.v + 2 * ((int64_t)b * p.v_sb + (int64_t)h * p.v_sh);
+  const char* bbase = p.bm + 2 * ((int64_t)b * p.b_sb + (int64_t)h * p.b_sh);
+  const float* gbase = p.g + (int64_t)bh * p.gf_stride;
+  const float* fbase = p.f ? p.f + (int64_t)bh * p.gf_stride : nullptr;
+
+  float m_run = -INFINITY;       // running maximum (log2 units), identical in every thread
+  float acc0 = 0.f, acc1 = 0.f;  // this lane's two head dims of the warp's partial p.v
+  float lsum = 0.f;              // warp's partial sum of p (kept by every lane)
+  for (int base = j_begin; base < j_end; base += NT) {
+    // ---- phase 1: one key per thread
+    const int j = base + tid;
+    float x = -INFINITY;
+    if (j < j_end) {
+      // stream the k and b~ rows 16 bytes at a time (8 values)
+      float qk = 0.f, cb = 0.f;
+      const uint4* kr = reinterpret_cast<const uint4*>(kbase + 2 * (int64_t)j * p.k_sl);
+      const uint4* br = reinterpret_cast<const uint4*>(bbase + 2 * (int64_t)j * p.b_sl);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint4 v = kr[i];
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          qk = fmaf(q[i * 8 + 2 * e], unpack_lo<kHalf>(w[e]), qk);
+          qk = fmaf(q[i * 8 + 2 * e + 1], unpack_hi<kHalf>(w[e]), qk);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 v = br[i];
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          cb = fmaf(c[i * 8 + 2 * e], unpack_lo<kHalf>(w[e]), cb);
+          cb = fmaf(c[i * 8 + 2 * e + 1], unpack_hi<kHalf>(w[e]), cb);
+        }
+      }
+      const float gj = gbase[j];
+      const float fj = fbase ? fbase[j] : 0.f;
+      const float dec = exp2f(fminf((gq - gj) * kLog2e, 0.f));
+      x = fmaf(qk, c1, fmaf(fq - fj, kLog2e, lam2 * (dec * cb)));
+    }
+    s_x[tid] = x;
+    // ---- phase 2: chunk maximum
+    float mx = x;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) s_red[warp] = mx;
+    __syncthreads();
+    mx = s_red[0];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) mx = fmaxf(mx, s_red[w]);
+    const float m_new = fmaxf(m_run, mx);
+    const float corr = (m_run == -INFINITY) ? 0.f : exp2f(m_run - m_new);
+    m_run = m_new;
+    // ---- phase 3/4: p and p v (warp w takes keys w, w+8, ... of the chunk)
+    acc0 *= corr;
+    acc1 *= corr;
+    lsum *= corr;
+    const int nk = min(NT, j_end - base);
+    for (int t = warp; t < nk; t += NW) {
+      const float pj = exp2f(s_x[t] - m_new);
+      const uint32_t vv = *reinterpret_cast<const uint32_t*>(vbase + 2 * ((int64_t)(base + t) * p.v_sl + 2 * lane));
+      acc0 = fmaf(pj, unpack_lo<kHalf>(vv), acc0);
+      acc1 = fmaf(pj, unpack_hi<kHalf>(vv), acc1);
+      lsum += pj;
+    }
+    __syncthreads();    // s_x / s_red are rewritten by the next chunk
+  }
+  // ---- merge the warps' partials and write this split's (m, l, acc[64])
+  s_acc[warp][2 * lane] = acc0;
+  s_acc[warp][2 * lane + 1] = acc1;
+  if (lane == 0) s_l[warp] = lsum;
+  __syncthreads();
+  float* out = p.ws + ((int64_t)split * p.B * p.H + bh) * 66;
+  if (tid < 64) {
+    float a = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) a += s_acc[w][tid];
+    out[2 + tid] = a;
+  }
+  if (tid == 0) {
+    float l = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) l += s_l[w];
+    out[0] = m_run;
+    out[1] = l;
+  }
+}
+
+// One warp per (batch, head): merge the splits, normalise, write y in the low-precision dtype.
+template <bool kHalf>
+__global__ void __launch_bounds__(256) decode_combine_kernel(DecodeParams p) {
+  const int bh = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (bh >= p.B * p.H) return;
+  const int lane = threadIdx.x & 31;
+  const int b = bh / p.H, h = bh % p.H;
+  const int64_t stride = (int64_t)p.B * p.H * 66;
+  float m = -INFINITY;
+  for (int s = 0; s < p.splits; ++s) m = fmaxf(m, p.ws[s * stride + (int64_t)bh * 66]);
+  float l = 0.f, a0 = 0.f, a1 = 0.f;
+  for (int s = 0; s < p.splits; ++s) {
+    const float* part = p.ws + s * stride + (int64_t)bh * 66;
+    const float ms = part[0];
+    const float w = (ms == -INFINITY) ? 0.f : exp2f(ms - m);
+    l = fmaf(part[1], w, l);
+    a0 = fmaf(part[2 + 2 * lane], w, a0);
+    a1 = fmaf(part[3 + 2 * lane], w, a1);
+  }
+  const float ls = (l == 0.f) ? 1.f : l;
+  uint32_t* y = reinterpret_cast<uint32_t*>(p.y + 2 * ((int64_t)b * p.y_sb + (int64_t)h * p.y_sh));
+  y[lane] = pack2<kHalf>(a0 / ls, a1 / ls);
+  if (lane == 0 && p.status && !isfinite(m + __log2f(ls))) atomicOr(p.status, SISA_ST_NONFINITE);
+}
+
+}  // namespace dec
+
+int decode_splits(int64_t B, int64_t H, int64_t N) {
+  const int64_t target = 148 * 8;
+  const int64_t bh = B * H;
+  int64_t s = (target + bh - 1) / bh;
+  const int64_t maxs = (N + dec::NT - 1) / dec::NT;
+  if (s > maxs) s = maxs;
+  if (s < 1) s = 1;
+  if (s > 64) s = 64;
+  return (int)s;
+}
+
+cudaError_t launch_decode(const DecodeParams& p, int dtype, cudaStream_t st) {
+  dim3 grid(p.splits, p.B * p.H);
+  const unsigned nb = (unsigned)((p.B * p.H + 7) / 8);
+  if (dtype == 1) {
+    dec::decode_split_kernel<true><<<grid, dec::NT, 0, st>>>(p);
+    dec::decode_combine_kernel<true><<<nb, 256, 0, st>>>(p);
+  } else {
+    dec::decode_split_kernel<false><<<grid, dec::NT, 0, st>>>(p);
+    dec::decode_combine_kernel<false><<<nb, 256, 0, st>>>(p);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace sisa

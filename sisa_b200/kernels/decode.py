@@ -1,0 +1,42 @@
+"""Incremental-decode attention on the sm_100a kernel (mirrors the decode step of src/sisa/modeling.py:224-238).
+
+``decode_attention(q, c, g, fgate, state, lam) -> y``: one new query row per (batch, head) against the
+layer's cache (:class:`sisa_b200.generation.LayerState`, which already holds the new position). fp32
+scores and softmax over the bf16/fp16 cache, split-K over the key axis.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import _lib, backends
+
+__all__ = ["decode_attention"]
+
+
+def decode_attention(q: torch.Tensor, c: torch.Tensor, g: torch.Tensor, fgate: torch.Tensor | None, state,
+                     lam: torch.Tensor) -> torch.Tensor:
+    """q: (B, H, 1, 64), c: (B, H, 1, 32) compute dtype; g, fgate: (B, H, 1) fp32; lam: (H,) fp32.
+    Returns y (B, H, 1, 64) in q.dtype."""
+    lib = _lib.load()
+    B, H, M, D = q.shape
+    if M != 1 or D != 64 or c.shape[-1] != 32:
+        raise ValueError(f"decode_attention takes one query row with d_head 64 and d_state 32, got {tuple(q.shape)}")
+    dev = q.device
+    N = state.length
+    if c.dtype != q.dtype:
+        c = c.to(q.dtype)
+    q, c = (t if t.stride(-1) == 1 and t.data_ptr() % 16 == 0 else t.contiguous() for t in (q, c))
+    gq = g.reshape(B, H).float().contiguous()
+    fq = None if fgate is None else fgate.reshape(B, H).float().contiguous()
+    y = torch.empty((B, H, 1, D), device=dev, dtype=q.dtype)
+    ws = torch.empty(max(lib.sisa_decode_workspace(B, H, N), 16), dtype=torch.uint8, device=dev)
+    st = backends.status_word(dev)
+    vs = [_lib.view4(t) for t in (q, c, state.k_buf, state.v_buf, state.b_buf, y)]
+    r = [_lib.vref(x) for x in vs]
+    rc = lib.sisa_decode_attn(r[0], r[1], gq.data_ptr(), _lib.ptr(fq), r[2], r[3], r[4], state.g_buf.data_ptr(),
+                              None if fq is None else state.f_buf.data_ptr(), state.g_buf.shape[2],
+                              lam.float().contiguous().data_ptr(), B, H, N, _lib.dtype_code(q.dtype), r[5],
+                              ws.data_ptr(), st.data_ptr(), _lib.stream_ptr(dev))
+    _lib.check(rc, "sisa_decode_attn")
+    backends.after_call(dev)
+    return y

@@ -1,0 +1,370 @@
+"""SISA language model: pre-norm blocks of SISA attention and SwiGLU, tied embedding
+(mirrors src/sisa/modeling.py; state-dict keys and initialisation are the reference's).
+
+The ``cuda`` implementation runs the fused layer core: one projection GEMM (cuBLAS through
+``F.linear``) into the fused column layout, then the sm_100a preparation and attention kernels
+(:func:`sisa_b200.kernels.fused.sisa_fused`). ``fused_ce=True`` computes the loss with the chunked
+linear + cross-entropy kernels; decoding with a cache uses the incremental-decode kernel.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import TYPE_CHECKING, Any, Iterable
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+from torch import Tensor
+from torch.utils.checkpoint import checkpoint
+
+from .config import ATTN_IMPLS, SISAConfig
+from .functional import _autocast_off, _work_dtype, attend_rows, rotate_pairs, sisa_attention
+
+if TYPE_CHECKING:  # pragma: no cover
+    from .generation import SISACache
+
+__all__ = ["RMSNorm", "SwiGLU", "SISAAttention", "SISABlock", "SISAModel", "SISAForCausalLM", "SISAOutput"]
+
+IGNORE_INDEX = -100
+
+
+class RMSNorm(nn.Module):
+    """RMSNorm computed in fp32; output in the input's dtype (modeling.py:26-36)."""
+
+    def __init__(self, dim: int, eps: float = 1e-6):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(dim))
+        self.eps = eps
+
+    def forward(self, x: Tensor) -> Tensor:
+        norm = torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + self.eps)
+        return ((x.float() * norm) * self.weight.float()).to(x.dtype)
+
+
+class SwiGLU(nn.Module):
+    """``w_down(silu(w_gate x) * w_up x)`` without biases (modeling.py:39-49)."""
+
+    def __init__(self, d_model: int, d_ff: int):
+        super().__init__()
+        self.w_gate = nn.Linear(d_model, d_ff, bias=False)
+        self.w_up = nn.Linear(d_model, d_ff, bias=False)
+        self.w_down = nn.Linear(d_ff, d_model, bias=False)
+
+    def forward(self, x: Tensor) -> Tensor:
+        return self.w_down(F.silu(self.w_gate(x)) * self.w_up(x))
+
+
+def _compute_dtype(x: Tensor) -> torch.dtype:
+    dt = x.device.type
+    try:
+        if torch.is_autocast_enabled(dt):
+            return torch.get_autocast_dtype(dt)
+    except (TypeError, RuntimeError):
+        pass
+    return x.dtype
+
+
+def _resolve_impl(requested: str, x: Tensor, config: SISAConfig) -> str:
+    """``"torch"`` or ``"cuda"`` for layer input ``x`` (modeling.py:60-76)."""
+    if requested not in ATTN_IMPLS:
+        raise ValueError(f"attn_impl must be one of {ATTN_IMPLS}, got {requested!r}")
+    if requested == "torch":
+        return "torch"
+    if x.device.type != "cuda":
+        if requested == "auto":
+            return "torch"
+        raise ValueError(f"attn_impl={requested!r} needs a CUDA tensor, got one on {x.device.type}; "
+                         "use attn_impl='torch' or 'auto'")
+    from . import backends
+
+    return backends.select_impl(requested, x, config)
+
+
+class SISAAttention(nn.Module):
+    """SISA attention sublayer: projections, recurrences, attention and output projection.
+
+    Parameters (paper-checkpoint row layouts, modeling.py:79-141): ``W_Q, W_K, W_V, W_O`` (d -> d);
+    ``W_B, W_C`` (d -> H*d_state); ``alpha_proj`` (d -> H, decay, with bias); ``theta_proj``
+    (d -> H*d_state/2, rotation rate); ``forget_proj`` (d -> H, with bias); ``lambda_raw`` (H),
+    ``lam = softplus(lambda_raw)``, kept in fp32 when the module is cast to bf16/fp16.
+    """
+
+    def __init__(self, config: SISAConfig, layer_idx: int = 0):
+        super().__init__()
+        self.config = config
+        self.layer_idx = layer_idx
+        d, h, s = config.d_model, config.n_head, config.d_state
+        self.W_Q = nn.Linear(d, d, bias=False)
+        self.W_K = nn.Linear(d, d, bias=False)
+        self.W_V = nn.Linear(d, d, bias=False)
+        self.W_O = nn.Linear(d, d, bias=False)
+        self.W_B = nn.Linear(d, h * s, bias=False)
+        self.W_C = nn.Linear(d, h * s, bias=False)
+        self.alpha_proj = nn.Linear(d, h, bias=True)
+        self.theta_proj = nn.Linear(d, h * (s // 2), bias=False)
+        self.forget_proj = nn.Linear(d, h, bias=True)
+        self.lambda_raw = nn.Parameter(torch.full((h,), float(config.lambda_raw_init)))
+        self.reset_parameters()
+
+    @torch.no_grad()
+    def reset_parameters(self) -> None:
+        """Every weight ~ N(0, init_std) except W_C = 0 (zero_init_c) and theta_proj ~ N(0, theta_init_std);
+        alpha bias = decay_bias_init, forget bias = forget_bias_init, lambda_raw = lambda_raw_init."""
+        cfg = self.config
+        for lin in (self.W_Q, self.W_K, self.W_V, self.W_O, self.W_B, self.alpha_proj, self.forget_proj):
+            nn.init.normal_(lin.weight, std=cfg.init_std)
+        if cfg.zero_init_c:
+            nn.init.zeros_(self.W_C.weight)
+        else:
+            nn.init.normal_(self.W_C.weight, std=cfg.init_std)
+        nn.init.normal_(self.theta_proj.weight, std=cfg.theta_init_std)
+        nn.init.constant_(self.alpha_proj.bias, cfg.decay_bias_init)
+        nn.init.constant_(self.forget_proj.bias, cfg.forget_bias_init)
+        self.lambda_raw.fill_(cfg.lambda_raw_init)
+
+    def _apply(self, fn: Any, recurse: bool = True) -> "SISAAttention":
+        low = (torch.float16, torch.bfloat16)
+        old = self.lambda_raw
+        old_data = old.data
+        old_grad = None if old.grad is None else old.grad.data
+        super()._apply(fn, recurse)
+        p = self.lambda_raw
+        if p.dtype in low:
+            src = old_data if old_data.dtype not in low else p.data
+            p.data = src.to(device=p.device, dtype=torch.float32)
+            if p.grad is not None:
+                gsrc = old_grad if old_grad is not None and old_grad.dtype not in low else p.grad
+                p.grad = gsrc.to(device=p.device, dtype=torch.float32)
+        return self
+
+    def lam(self) -> Tensor:
+        return F.softplus(self.lambda_raw).float()
+
+    def _forget_logits(self, x: Tensor) -> Tensor:
+        with _autocast_off(x.device.type):
+            return F.linear(x.float(), self.forget_proj.weight.float(), self.forget_proj.bias.float())
+
+    def fused_weights(self) -> tuple[Tensor, Tensor]:
+        from .kernels.fused import concat_fused_weights
+
+        return concat_fused_weights(self.W_Q.weight, self.W_K.weight, self.W_V.weight, self.W_B.weight,
+                                    self.W_C.weight, self.theta_proj.weight, self.alpha_proj.weight,
+                                    self.alpha_proj.bias)
+
+    def _prepare(self, x: Tensor, state: Any = None):
+        """Torch glue of the unfused path (modeling.py:171-199); with a decode ``state`` the recurrences
+        continue from its last position. Returns q, k, v, c~, b~ (compute dtype) and g, F, Phi (fp32)."""
+        bsz, seq_len, _ = x.shape
+        h, dh, s = self.config.n_head, self.config.d_head, self.config.d_state
+        q = self.W_Q(x).view(bsz, seq_len, h, dh).transpose(1, 2)
+        k = self.W_K(x).view(bsz, seq_len, h, dh).transpose(1, 2)
+        v = self.W_V(x).view(bsz, seq_len, h, dh).transpose(1, 2)
+        b = self.W_B(x).view(bsz, seq_len, h, s).transpose(1, 2)
+        c = self.W_C(x).view(bsz, seq_len, h, s).transpose(1, 2)
+        a = self.alpha_proj(x).transpose(1, 2)
+        theta = self.theta_proj(x).view(bsz, seq_len, h, s // 2).transpose(1, 2)
+        g = torch.cumsum(-F.softplus(a.float()), dim=2)
+        phi = torch.cumsum(theta.float(), dim=2)
+        z = self._forget_logits(x)
+        with _autocast_off(x.device.type):
+            fgate = torch.cumsum(F.logsigmoid(z).transpose(1, 2), dim=2)
+        if state is not None:
+            g = g + state.g_last()
+            phi = phi + state.phi.unsqueeze(2)
+            fgate = fgate + state.f_last()
+        c = rotate_pairs(c.float(), phi)
+        b = rotate_pairs(b.float(), phi)
+        cd = _compute_dtype(x)
+        return q.to(cd), k.to(cd), v.to(cd), c.to(cd), b.to(cd), g, fgate, phi
+
+    def _output(self, y: Tensor) -> Tensor:
+        bsz, h, seq_len, dh = y.shape
+        return self.W_O(y.transpose(1, 2).reshape(bsz, seq_len, h * dh))
+
+    def _forward_fused(self, x: Tensor) -> Tensor:
+        from .kernels.fused import sisa_fused
+
+        bsz, seq_len, d = x.shape
+        weight, bias = self.fused_weights()
+        proj = F.linear(x, weight, bias)
+        y = sisa_fused(proj, self._forget_logits(x), self.lam(), self.config.n_head)
+        return self.W_O(y.reshape(bsz, seq_len, d))
+
+    def _forward_cached(self, x: Tensor, cache: "SISACache", requested: str) -> Tensor:
+        state = cache.get(self.layer_idx)
+        q, k, v, c, b, g, fgate, phi = self._prepare(x, state)
+        if state is None:
+            impl = _resolve_impl(requested, x, self.config)
+            y = sisa_attention(q, k, v, c, b, g, self.lam(), fgate, impl="cuda" if impl == "cuda" else "torch",
+                               block_q=self.config.torch_block_q)
+            cache.update(self.layer_idx, k=k, v=v, b=b, g=g, fgate=fgate, phi=phi[:, :, -1])
+            return self._output(y)
+        start = state.length
+        state = cache.update(self.layer_idx, k=k, v=v, b=b, g=g, fgate=fgate, phi=phi[:, :, -1])
+        impl = _resolve_impl(requested, x, self.config) if x.is_cuda else "torch"
+        if impl == "cuda" and q.shape[2] == 1:
+            from .kernels.decode import decode_attention
+
+            y = decode_attention(q, c, g, fgate, state, self.lam())
+            return self._output(y)
+        wd = _work_dtype(q.dtype)
+        y = attend_rows(q.to(wd), state.k.to(wd), state.v.to(wd), c.to(wd), state.b.to(wd), g.to(wd),
+                        state.g.to(wd), self.lam().to(wd), fgate.to(wd), state.fgate.to(wd), start)
+        return self._output(y.to(q.dtype))
+
+    def forward(self, x: Tensor, *, cache: "SISACache | None" = None, impl: str | None = None) -> Tensor:
+        requested = impl or self.config.attn_impl
+        if cache is not None:
+            return self._forward_cached(x, cache, requested)
+        impl = _resolve_impl(requested, x, self.config)
+        if impl == "cuda":
+            return self._forward_fused(x)
+        q, k, v, c, b, g, fgate, _ = self._prepare(x)
+        y = sisa_attention(q, k, v, c, b, g, self.lam(), fgate, impl="torch", block_q=self.config.torch_block_q)
+        return self._output(y)
+
+
+class SISABlock(nn.Module):
+    """``x + attn(attn_norm(x))`` then ``x + ffn(ffn_norm(x))`` (modeling.py:258-290)."""
+
+    def __init__(self, config: SISAConfig, layer_idx: int = 0):
+        super().__init__()
+        self.config = config
+        self.attn_norm = RMSNorm(config.d_model, config.norm_eps)
+        self.attn = SISAAttention(config, layer_idx)
+        self.ffn_norm = RMSNorm(config.d_model, config.norm_eps)
+        self.ffn = SwiGLU(config.d_model, config.d_ff)
+        self._reset_ffn_and_norms()
+
+    @torch.no_grad()
+    def _reset_ffn_and_norms(self) -> None:
+        for lin in (self.ffn.w_gate, self.ffn.w_up, self.ffn.w_down):
+            nn.init.normal_(lin.weight, std=self.config.init_std)
+        nn.init.ones_(self.attn_norm.weight)
+        nn.init.ones_(self.ffn_norm.weight)
+
+    @torch.no_grad()
+    def reset_parameters(self) -> None:
+        self._reset_ffn_and_norms()
+        self.attn.reset_parameters()
+
+    def forward(self, x: Tensor, cache: "SISACache | None" = None) -> Tensor:
+        x = x + self.attn(self.attn_norm(x), cache=cache)
+        return x + self.ffn(self.ffn_norm(x))
+
+
+@dataclass
+class SISAOutput:
+    loss: Tensor | None = None
+    logits: Tensor | None = None
+
+
+def _lm_head_loss(hidden: Tensor, weight: Tensor, labels: Tensor) -> Tensor:
+    logits = F.linear(hidden, weight)
+    return F.cross_entropy(logits.reshape(-1, logits.shape[-1]).float(), labels.reshape(-1), ignore_index=IGNORE_INDEX)
+
+
+class SISAModel(nn.Module):
+    """Embedding, ``n_layer`` blocks and the final RMSNorm (modeling.py:308-414)."""
+
+    def __init__(self, config: SISAConfig):
+        super().__init__()
+        self.config = config.replace()
+        cfg = self.config
+        self.embed = nn.Embedding(cfg.vocab_size, cfg.d_model)
+        self.layers = nn.ModuleList([SISABlock(cfg, i) for i in range(cfg.n_layer)])
+        self.final_norm = RMSNorm(cfg.d_model, cfg.norm_eps)
+        self._reset_embedding_and_norm()
+
+    @torch.no_grad()
+    def _reset_embedding_and_norm(self) -> None:
+        nn.init.normal_(self.embed.weight, std=self.config.init_std)
+        nn.init.ones_(self.final_norm.weight)
+
+    @torch.no_grad()
+    def reset_parameters(self) -> None:
+        self._reset_embedding_and_norm()
+        for layer in self.layers:
+            layer.reset_parameters()
+
+    def forward(self, input_ids: Tensor, *, cache: "SISACache | None" = None) -> Tensor:
+        x = self.embed(input_ids)
+        use_ckpt = self.config.gradient_checkpointing and self.training and cache is None and torch.is_grad_enabled()
+        for layer in self.layers:
+            x = checkpoint(layer, x, use_reentrant=False) if use_ckpt else layer(x, cache=cache)
+        return self.final_norm(x)
+
+    def set_attn_impl(self, impl: str) -> None:
+        self.config.replace(attn_impl=impl)
+        self.config.attn_impl = impl
+
+    def num_parameters(self, exclude_embeddings: bool = False) -> int:
+        n = sum(p.numel() for p in self.parameters())
+        return n - self.embed.weight.numel() if exclude_embeddings else n
+
+    def param_groups(self, lr: float, weight_decay: float = 0.1, lambda_lr: float | None = None,
+                     no_decay_timescale_biases: bool = True) -> list[dict[str, Any]]:
+        """Optimizer groups "default", "timescale_biases" (alpha/forget biases, no decay) and "lambda"
+        (modeling.py:366-394)."""
+        default, timescale, lam = [], [], []
+        for name, p in self.named_parameters():
+            if not p.requires_grad:
+                continue
+            if name.endswith("lambda_raw"):
+                lam.append(p)
+            elif no_decay_timescale_biases and name.endswith(("alpha_proj.bias", "forget_proj.bias")):
+                timescale.append(p)
+            else:
+                default.append(p)
+        groups = [{"params": default, "lr": lr, "weight_decay": weight_decay, "name": "default"}]
+        if timescale:
+            groups.append({"params": timescale, "lr": lr, "weight_decay": 0.0, "name": "timescale_biases"})
+        if lam:
+            groups.append({"params": lam, "lr": lr if lambda_lr is None else lambda_lr, "weight_decay": 0.0,
+                           "name": "lambda"})
+        return groups
+
+
+class SISAForCausalLM(SISAModel):
+    """:class:`SISAModel` with the tied LM head; labels are shifted internally (HF convention,
+    modeling.py:417-481)."""
+
+    def __init__(self, config: SISAConfig):
+        super().__init__(config)
+        self._loss_fn = _lm_head_loss
+
+    def forward(self, input_ids: Tensor, labels: Tensor | None = None, *, cache: "SISACache | None" = None,
+                fused_ce: bool = False, return_logits: bool = True, logits_to_keep: int = 0) -> SISAOutput:
+        if labels is not None and labels.shape != input_ids.shape:
+            raise ValueError(f"labels shape {tuple(labels.shape)} must match input_ids {tuple(input_ids.shape)}")
+        if labels is not None and logits_to_keep:
+            raise ValueError("logits_to_keep cannot be combined with labels")
+        hidden = super().forward(input_ids, cache=cache)
+        weight = self.embed.weight
+        loss = logits = None
+        fused_ce = fused_ce and labels is not None
+        if fused_ce:
+            if not hidden.is_cuda:
+                raise ValueError("fused_ce=True needs CUDA tensors")
+            from .kernels.linear_ce import linear_cross_entropy
+
+            d = hidden.shape[-1]
+            loss = linear_cross_entropy(hidden[:, :-1].reshape(-1, d), weight, labels[:, 1:].reshape(-1),
+                                        ignore_index=IGNORE_INDEX)
+        elif labels is not None and not return_logits:
+            loss = self._loss_fn(hidden[:, :-1], weight, labels[:, 1:])
+        if return_logits and not fused_ce:
+            logits = F.linear(hidden[:, -logits_to_keep:] if logits_to_keep else hidden, weight)
+            if labels is not None:
+                vocab = logits.shape[-1]
+                loss = F.cross_entropy(logits[:, :-1].reshape(-1, vocab).float(), labels[:, 1:].reshape(-1),
+                                       ignore_index=IGNORE_INDEX)
+        return SISAOutput(loss=loss, logits=logits)
+
+    def generate(self, input_ids: Tensor, max_new_tokens: int, temperature: float = 1.0, top_k: int | None = None,
+                 eos_token_id: int | Iterable[int] | Tensor | None = None, do_sample: bool = False,
+                 **kwargs: Any) -> Tensor:
+        from .generation import generate
+
+        return generate(self, input_ids, max_new_tokens, temperature=temperature, top_k=top_k,
+                        eos_token_id=eos_token_id, do_sample=do_sample, **kwargs)

@@ -1,0 +1,91 @@
+"""Model-level: the cuda implementation (fused layer core, linear-CE) against the torch implementation and
+fp64, under bf16 autocast (the reference's tests/test_model_cuda.py gates)."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+import sisa_b200 as sisa
+from tests.helpers import max_abs, rel_err
+
+pytestmark = pytest.mark.gpu
+
+GROUPS = {"attn": ("attn.W_", "attn.alpha", "attn.theta", "attn.forget", "attn.lambda"),
+          "ffn": ("ffn.",), "embed": ("embed.",), "norm": ("norm.",)}
+
+
+def tiny(seed=0):
+    torch.manual_seed(seed)
+    cfg = sisa.SISAConfig(vocab_size=97, d_model=128, n_layer=2, n_head=2, d_ff=96, zero_init_c=False,
+                          attn_impl="torch")
+    m = sisa.SISAForCausalLM(cfg)
+    gen = torch.Generator().manual_seed(seed + 1)
+    with torch.no_grad():
+        for layer in m.layers:
+            a = layer.attn
+            a.theta_proj.weight.copy_(torch.randn(a.theta_proj.weight.shape, generator=gen) * 0.2)
+            a.alpha_proj.bias.copy_(torch.rand(2, generator=gen) * 3.0 - 4.0)
+            a.forget_proj.bias.copy_(torch.rand(2, generator=gen) * 3.0)
+            a.lambda_raw.copy_(torch.rand(2, generator=gen) * 2.0 - 0.5)
+    return m
+
+
+def run(model, ids, dev, impl, fused_ce=False):
+    m = model.to(dev)
+    m.set_attn_impl(impl)
+    m.zero_grad(set_to_none=True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        out = m(ids.to(dev), labels=ids.to(dev), fused_ce=fused_ce)
+    out.loss.backward()
+    torch.cuda.synchronize()
+    grads = {n: p.grad.detach().float().cpu() for n, p in m.named_parameters()}
+    return out.loss.detach().float().cpu(), (None if out.logits is None else out.logits.detach().float().cpu()), grads
+
+
+def group_err(grads, ref):
+    out = {}
+    for gname, keys in GROUPS.items():
+        names = [n for n in ref if any(k in n for k in keys)]
+        a = torch.cat([grads[n].flatten().double() for n in names])
+        b = torch.cat([ref[n].flatten().double() for n in names])
+        out[gname] = rel_err(a, b)
+    return out
+
+
+def test_cuda_model_matches_torch_and_fp64(cuda_dev):
+    model = tiny()
+    ids = torch.randint(0, 97, (2, 300), generator=torch.Generator().manual_seed(3))
+    m64 = tiny().double()
+    o64 = m64(ids, labels=ids)
+    o64.loss.backward()
+    g64 = {n: p.grad.detach() for n, p in m64.named_parameters()}
+    lt, logt, gt = run(model, ids, cuda_dev, "torch")
+    lc, logc, gc = run(model, ids, cuda_dev, "cuda")
+    d_torch = abs(float(lt) - float(o64.loss))
+    assert abs(float(lc) - float(o64.loss)) <= max(2 * d_torch, 2e-3)
+    e_torch = max_abs(logt, o64.logits)
+    assert max_abs(logc, o64.logits) <= 2 * e_torch + 1e-3
+    et, ec = group_err(gt, g64), group_err(gc, g64)
+    for gname in GROUPS:
+        assert ec[gname] <= 3 * et[gname] + 2e-3, (gname, ec, et)
+
+
+def test_fused_ce_loss_and_grads(cuda_dev):
+    model = tiny(1)
+    ids = torch.randint(0, 97, (2, 257), generator=torch.Generator().manual_seed(4))
+    l1, _, g1 = run(model, ids, cuda_dev, "cuda", fused_ce=False)
+    l2, logits2, g2 = run(model, ids, cuda_dev, "cuda", fused_ce=True)
+    assert logits2 is None
+    assert abs(float(l1) - float(l2)) <= 1e-2
+    e = group_err(g2, g1)
+    assert all(v <= 5e-2 for v in e.values()), e
+
+
+def test_cuda_model_deterministic(cuda_dev):
+    model = tiny(2)
+    ids = torch.randint(0, 97, (2, 200), generator=torch.Generator().manual_seed(5))
+    l1, _, g1 = run(model, ids, cuda_dev, "cuda")
+    l2, _, g2 = run(model, ids, cuda_dev, "cuda")
+    assert torch.equal(l1, l2)
+    for n in g1:
+        assert torch.equal(g1[n], g2[n]), n
