@@ -11,6 +11,11 @@ collective on the data path); ``value`` = all ranks' FLOPs / max-over-ranks time
 ``e2e``: the same step with host buffers: pinned proj/z/dy copied in, y/d_proj/dz/dlam copied out,
 inside the timed region.
 
+``train``: the second half of the metric, 12-layer sisa-152m training (d=768, H=12, d_ff=2744, vocab
+50277, reference initialisation) with per-rank batch 8 x 2048 uniform random ids, bf16 autocast, fused
+AdamW, clipping, fused linear-CE, data-parallel over the N ranks (DDP, NCCL allreduce overlapped with the
+backward). tokens/s = all ranks' input tokens / max-over-ranks step time.
+
 ``--impl reference``: the reference's pure-PyTorch CPU algorithm (the oracle port) on the host cores,
 on a bounded sample of the same workload (a subset of (batch, head) units at the full T).
 """
@@ -242,6 +247,10 @@ def run_cuda(args):
 
     # ---- e2e: host buffers in and out through the same C-ABI calls
     e2e = None if args.no_e2e else run_e2e(step, dev, args, world)
+    proj_mb = step.proj.numel() * 2 / 1e6
+    del step
+    torch.cuda.empty_cache()
+    train = None if args.no_train else run_train(args, rank, world, dev)
 
     if rank == 0:
         burst, sustained, hbm, src = measured_peaks()
@@ -254,7 +263,7 @@ def run_cuda(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "cfg1: fused prep + SISA attention fwd+bwd (sisa_fused step)", "B": b_, "T": t_,
                        "H": h_, "d_head": 64, "d_state": 32, "parallelism": f"replicas x{world} (per-rank batch)",
-                       "l2": "inputs larger than L2 (proj %.0f MB)" % (step.proj.numel() * 2 / 1e6),
+                       "l2": "inputs larger than L2 (proj %.0f MB)" % proj_mb,
                        "flop_per_pair": FLOP_PER_PAIR},
             "roofline": {"kernel": "sisa_attn_fwd + sisa_attn_bwd (tcgen05)", "bound": "tensor",
                          "achieved": round(ach, 3), "peak": burst, "unit": "TFLOP/s", "frac": round(ach / burst, 4),
@@ -266,7 +275,8 @@ def run_cuda(args):
                          "prep_fwd_gbs": round(prep_bytes / (per["prep_fwd"] * 1e-3) / 1e9, 1),
                          "hbm_peak_gbs": hbm},
             "e2e": e2e,
-            "gpu_launches": step.launches_per_step * args.steps,
+            "train": train,
+            "gpu_launches": 8 * args.steps,
             "clocks": clk.summary(),
         }
         if not args.no_cpu_baseline:
@@ -275,6 +285,47 @@ def run_cuda(args):
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
+
+
+TRAIN_FLOP_PER_TOKEN = 6 * 151_878_576 + 1152 * 12 * 1024.5 * 12   # matmul params incl. LM head + attention
+
+
+def run_train(args, rank, world, dev):
+    """cfg3: data-parallel training step of the 12-layer model; returns the ``train`` object (rank 0)."""
+    import sisa_b200 as sisa
+    from sisa_b200 import dp
+
+    cfg = sisa.SISAConfig.preset("sisa-152m", attn_impl="cuda")
+    model = dp.build_model(cfg, dev, seed=0)
+    trainer = dp.Trainer(model)
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    bt, tt = args.train_batch, 2048
+    batches = [torch.randint(0, cfg.vocab_size, (bt, tt), device=dev, generator=g) for _ in range(4)]
+    k_steps = max(3, min(args.train_steps, args.steps))
+    for i in range(max(args.warmup, 3)):
+        trainer.step(batches[i % 4])
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        torch.distributed.barrier()
+    s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_.record()
+    for i in range(k_steps):
+        loss = trainer.step(batches[i % 4])
+    e_.record()
+    torch.cuda.synchronize(dev)
+    ms = torch.tensor([s_.elapsed_time(e_)], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(ms, op=torch.distributed.ReduceOp.MAX)
+    ms = float(ms.item()) / k_steps
+    tok_s = world * bt * tt / (ms * 1e-3)
+    burst, sustained, _, _ = measured_peaks()
+    del trainer, model
+    torch.cuda.empty_cache()
+    return {"metric": "12L train tokens/s", "value": round(tok_s, 1), "unit": "tokens/s", "n_gpus": world,
+            "ms_per_step": round(ms, 3), "steps": k_steps, "per_rank_batch": [bt, tt], "model": "sisa-152m",
+            "params": cfg.num_parameters(), "loss_last": round(float(loss), 4),
+            "mfu_vs_sustained": round(tok_s * TRAIN_FLOP_PER_TOKEN / (world * sustained * 1e12), 4),
+            "parallelism": f"dp{world} (DDP, NCCL allreduce overlapped with backward)"}
 
 
 def run_e2e(step, dev, args, world):
@@ -350,6 +401,93 @@ def cpu_baseline(heads):
                       f"{dt:.1f} s"}
 
 
+def run_lce(args):
+    """cfg2: chunked linear-CE fwd+bwd, hidden [16384 x 1024] bf16 ~ N(0,1), weight [50277 x 1024] fp32 ~ N(0, 0.02^2)
+    under bf16 autocast, labels uniform. Metric: tokens/s (and TFLOP/s on 6 N V D)."""
+    from sisa_b200.kernels.linear_ce import linear_cross_entropy
+
+    dev = torch.device("cuda", 0)
+    N, D, V = 16384, 1024, 50277
+    g = torch.Generator(device=dev).manual_seed(0)
+    h = torch.randn((N, D), generator=g, device=dev).to(torch.bfloat16).requires_grad_(True)
+    w = (torch.randn((V, D), generator=g, device=dev) * 0.02).requires_grad_(True)
+    lab = torch.randint(0, V, (N,), generator=g, device=dev)
+
+    def step():
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = linear_cross_entropy(h, w, lab)
+        loss.backward()
+        h.grad = None
+        w.grad = None
+        return loss
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    base = torch.cuda.memory_allocated()
+    torch.cuda.reset_peak_memory_stats()
+    s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k = max(3, min(args.steps, 30))
+    s_.record()
+    for _ in range(k):
+        step()
+    e_.record()
+    torch.cuda.synchronize()
+    ms = s_.elapsed_time(e_) / k
+    peak = torch.cuda.max_memory_allocated() - base
+    print(json.dumps({"metric": "linear-CE fwd+bwd tokens/s (cfg2)", "value": round(N / (ms * 1e-3), 1),
+                      "unit": "tokens/s", "ms_per_step": round(ms, 3), "tflops": round(6 * N * V * D / (ms * 1e9), 1),
+                      "peak_mem_mb": round(peak / 2**20, 1), "steps": k, "config": {"N": N, "D": D, "V": V}}))
+
+
+def run_decode(args):
+    """cfg4: 12-layer sisa-152m, random init, bf16 weights; batch 64, prompt 8192 ids (id 0 first), greedy decode.
+    Reports prefill tokens/s and per-step decode latency with the cache bytes read per step."""
+    import sisa_b200 as sisa
+    from sisa_b200.generation import SISACache
+
+    dev = torch.device("cuda", 0)
+    Bd, P, S = args.decode_batch, args.decode_prompt, args.decode_steps
+    cfg = sisa.SISAConfig.preset("sisa-152m", attn_impl="cuda")
+    torch.manual_seed(0)
+    model = sisa.SISAForCausalLM(cfg).to(dev).to(torch.bfloat16).eval()
+    g = torch.Generator(device=dev).manual_seed(1)
+    ids = torch.randint(0, cfg.vocab_size, (Bd, P), generator=g, device=dev)
+    ids[:, 0] = 0
+    with torch.no_grad():
+        cache = SISACache(capacity=P + S + 1)
+        model(ids[:, :256], cache=SISACache(capacity=300), logits_to_keep=1)   # warm-up (kernels, allocator)
+        torch.cuda.synchronize()
+        s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_.record()
+        logits = model(ids, cache=cache, logits_to_keep=1).logits[:, -1]
+        e_.record()
+        torch.cuda.synchronize()
+        prefill_ms = s_.elapsed_time(e_)
+        nxt = logits.float().argmax(-1)
+        for _ in range(3):      # warm-up decode steps
+            logits = model(nxt.unsqueeze(1), cache=cache, logits_to_keep=1).logits[:, -1]
+            nxt = logits.float().argmax(-1)
+        torch.cuda.synchronize()
+        n = S - 3
+        s_.record()
+        for _ in range(n):
+            logits = model(nxt.unsqueeze(1), cache=cache, logits_to_keep=1).logits[:, -1]
+            nxt = logits.float().argmax(-1)
+        e_.record()
+        torch.cuda.synchronize()
+        step_ms = s_.elapsed_time(e_) / n
+    L_avg = P + 3 + n / 2
+    per_tok = cfg.n_layer * cfg.n_head * (64 * 2 * 2 + 32 * 2 + 8)   # k, v, b~ (bf16) + g, F (fp32)
+    cache_bytes = Bd * L_avg * per_tok
+    weight_bytes = 2 * (cfg.num_parameters())
+    print(json.dumps({"metric": "decode step latency (cfg4)", "value": round(step_ms, 3), "unit": "ms/step",
+                      "prefill_tokens_s": round(Bd * P / (prefill_ms * 1e-3), 1), "prefill_ms": round(prefill_ms, 1),
+                      "decode_steps_timed": n, "cache_bytes_per_step": int(cache_bytes),
+                      "hbm_gbs": round((cache_bytes + weight_bytes) / (step_ms * 1e-3) / 1e9, 1),
+                      "config": {"batch": Bd, "prompt": P, "new_tokens": S, "model": "sisa-152m"}}))
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -385,12 +523,24 @@ def main(argv=None):
     ap.add_argument("--cpu-sample-heads", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-train", action="store_true")
+    ap.add_argument("--workload", choices=["attn", "lce", "decode"], default="attn",
+                    help="attn (default: config 1 + the config 3 training leg), lce (config 2), decode (config 4)")
+    ap.add_argument("--decode-batch", type=int, default=64)
+    ap.add_argument("--decode-prompt", type=int, default=8192)
+    ap.add_argument("--decode-steps", type=int, default=256)
+    ap.add_argument("--train-steps", type=int, default=20)
+    ap.add_argument("--train-batch", type=int, default=8)
     ap.add_argument("--B", type=int, default=B, help="batch (default: config 1)")
     ap.add_argument("--T", type=int, default=T, help="sequence length (default: config 1)")
     ap.add_argument("--H", type=int, default=H, help="heads (default: config 1)")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "lce":
+        run_lce(args)
+    elif args.workload == "decode":
+        run_decode(args)
     else:
         run_cuda(args)
 

@@ -1,0 +1,107 @@
+"""Data-parallel training step with world_size 2 on CPU (gloo): gradient averaging, replica consistency and
+failure detection (a rank that exits makes the peer's collective fail within the process-group timeout)."""
+from __future__ import annotations
+
+import os
+import socket
+import sys
+import time
+from pathlib import Path
+
+import torch
+import torch.multiprocessing as mp
+
+ROOT = str(Path(__file__).resolve().parents[1])
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _cfg():
+    import sisa_b200 as sisa
+
+    return sisa.SISAConfig(vocab_size=61, d_model=128, n_layer=1, n_head=2, d_ff=64, attn_impl="torch",
+                           zero_init_c=False)
+
+
+def _batch(rank):
+    return torch.randint(0, 61, (2, 24), generator=torch.Generator().manual_seed(10 + rank))
+
+
+def _worker(rank, world, port, mode, q):
+    sys.path.insert(0, ROOT)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    torch.set_num_threads(1)
+    from sisa_b200 import dp
+
+    try:
+        _, _, dev = dp.init_distributed("gloo", timeout_s=15.0)
+        model = dp.build_model(_cfg(), dev, seed=0)
+        # SGD: the update is linear in the averaged gradient, so it can be compared with one process
+        trainer = dp.Trainer(model, torch.optim.SGD(model.parameters(), lr=0.5), fused_ce=False)
+        if mode == "exit" and rank == 1:
+            os._exit(3)                       # leaves between steps, no collective in flight
+        t0 = time.time()
+        loss = trainer.step(_batch(rank))
+        # numpy copies travel by value (tensors would be shared through handles that die with this process)
+        q.put((rank, "ok", float(loss), {n: p.detach().numpy().copy() for n, p in model.named_parameters()},
+               time.time() - t0))
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        q.put((rank, "error", type(e).__name__, str(e)[:200], None))
+    finally:
+        import torch.distributed as dist
+
+        if dist.is_initialized() and mode != "exit":
+            dist.destroy_process_group()
+
+
+def _run(mode, world=2, timeout=120):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = {}
+    expect = world if mode == "ok" else 1
+    t0 = time.time()
+    while len(out) < expect and time.time() - t0 < timeout:
+        try:
+            r = q.get(timeout=5)
+            out[r[0]] = r
+        except Exception:  # noqa: BLE001 - queue.Empty
+            pass
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    return out
+
+
+def test_dp_gloo_gradients_are_averaged_and_replicas_agree():
+    out = _run("ok")
+    assert set(out) == {0, 1} and all(v[1] == "ok" for v in out.values()), out
+    p0 = {n: torch.from_numpy(a) for n, a in out[0][3].items()}
+    p1 = {n: torch.from_numpy(a) for n, a in out[1][3].items()}
+    for n in p0:
+        assert torch.equal(p0[n], p1[n]), n
+    # single process on the concatenated batch gives the same step (equal token counts per rank)
+    sys.path.insert(0, ROOT)
+    from sisa_b200 import dp
+
+    model = dp.build_model(_cfg(), torch.device("cpu"), seed=0)
+    trainer = dp.Trainer(model, torch.optim.SGD(model.parameters(), lr=0.5), fused_ce=False)
+    trainer.step(torch.cat([_batch(0), _batch(1)]))
+    for n, p in model.named_parameters():
+        assert torch.allclose(p.detach(), p0[n], rtol=1e-5, atol=1e-6), n
+
+
+def test_dp_gloo_peer_exit_is_detected():
+    out = _run("exit")
+    assert 0 in out, out
+    rank, status, kind, msg, _ = out[0]
+    assert status == "error", out[0]
