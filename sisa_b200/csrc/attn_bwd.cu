@@ -8,13 +8,14 @@
 //    self-normalised fp32 forward output), and accumulates dQ += dS^ K and dC += (dS^ * colf mid) B~ in
 //    TMEM. It also accumulates the row sums of the exact-delta scheme (Z, D, P_tt, dP_tt, the
 //    u-weighted sums) and finishes every row: T^, the delta-free diagonal dS_tt, the row parts of
-//    dg, dF and d lambda, and the per-row statistics {lse, delta, T^-delta, dS_tt} read by the dkv kernel.
+//    dg, dF and d lambda, and the per-row statistics {-lse, -delta, -(T^-delta), dS_tt} read by the dkv
+//    kernel (negated so that kernel adds them).
 //  dkv kernel (key-tile owner, 128 rows): recomputes S^T, U^T, dP^T per 64-query tile, uses
 //    dS = dS^' - P'(T^ - delta) for dK and the column sums of dg and dF, dS^' for dB (the same delta as
 //    dC, so the Phi_i - Phi_j cancellation of d theta holds), and the dq kernel's dS_tt on the diagonal.
 //
-// Both kernels: 8 compute warps (two warpgroups splitting each tile's 64 columns 32/32; thread =
-// TMEM lane = owned row), one TMA producer warp and one UMMA warp. Per tile the compute warps pull
+// Both kernels: 16 compute warps (four warpgroups splitting each tile's 64 columns 16/16/16/16; thread =
+// TMEM lane = owned row, four compute warps per SM sub-partition), one TMA producer warp and one UMMA warp. Per tile the compute warps pull
 // S, U, dP into registers and release TMEM at once, so the next tile's GEMMs overlap their math;
 // the gradient GEMMs read bf16 operands the compute warps wrote to double-buffered, 128B-swizzled
 // shared memory.
@@ -27,7 +28,12 @@ namespace sisa {
 namespace bwd {
 
 constexpr int NST = 3;
-constexpr int NTHREADS = 320;    // warps 0-7 compute, 8 TMA, 9 MMA
+constexpr int NWG = 4;           // compute warpgroups; each owns 64 / NWG columns of every tile
+constexpr int NCOL = 64 / NWG;   // 16
+constexpr int NCW = 4 * NWG;     // compute warps
+constexpr int NTHREADS = 32 * NCW + 64;    // + one TMA warp + one UMMA warp
+constexpr int WARP_TMA = NCW, WARP_MMA = NCW + 1;
+constexpr int NCT = 32 * NCW;    // compute threads
 
 // ----------------------------------------------------------------------------- dq kernel layout
 namespace dqk {
@@ -37,8 +43,8 @@ constexpr uint32_t SZ_STAGE = SZ_K + SZ_V + SZ_B + SZ_POS;   // 21504
 constexpr uint32_t SZ_OP = 128 * 128;                          // one 128 x 64 bf16 operand tile
 constexpr uint32_t OFF_Q = 0, OFF_DO = OFF_Q + SZ_Q, OFF_C = OFF_DO + SZ_DO, OFF_ST = OFF_C + SZ_C;
 constexpr uint32_t OFF_OP = OFF_ST + NST * SZ_STAGE;           // [buf][dS, dSC]
-constexpr uint32_t OFF_RED = OFF_OP + 4 * SZ_OP;               // 128 rows x 8 floats
-constexpr uint32_t OFF_BAR = OFF_RED + 128 * 8 * 4;
+constexpr uint32_t OFF_RED = OFF_OP + 4 * SZ_OP;               // 128 rows x NWG x 8 floats
+constexpr uint32_t OFF_BAR = OFF_RED + 128 * NWG * 8 * 4;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
 constexpr int COL_S = 0, COL_U = 64, COL_DP = 128, COL_DQ = 192, COL_DCO = 256, COL_DCD = 288;
 constexpr int B_KVF = 0, B_KVE = 3, B_Q = 6, B_SUF = 7, B_SUE = 8, B_OPF = 9, B_OPE = 11, B_ACC = 13;
@@ -53,8 +59,8 @@ constexpr uint32_t SZ_STAGE = SZ_Q + SZ_DO + SZ_C + SZ_POS + SZ_RST;   // 22528
 constexpr uint32_t SZ_OP = 128 * 128;
 constexpr uint32_t OFF_K = 0, OFF_V = OFF_K + SZ_K, OFF_B = OFF_V + SZ_V, OFF_ST = OFF_B + SZ_B;
 constexpr uint32_t OFF_OP = OFF_ST + NST * SZ_STAGE;                   // [buf][P, dS, dSb]
-constexpr uint32_t OFF_RED = OFF_OP + 6 * SZ_OP;                       // 128 rows x 4 floats
-constexpr uint32_t OFF_BAR = OFF_RED + 128 * 4 * 4;
+constexpr uint32_t OFF_RED = OFF_OP + 6 * SZ_OP;                       // 128 rows x NWG x 2 floats
+constexpr uint32_t OFF_BAR = OFF_RED + 128 * NWG * 2 * 4;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
 constexpr int COL_S = 0, COL_U = 64, COL_DP = 128, COL_DV = 192, COL_DK = 256, COL_DBD = 320, COL_DBO = 352;
 constexpr int B_KVF = 0, B_KVE = 3, B_K = 6, B_SUF = 7, B_SUE = 8, B_OPF = 9, B_OPE = 11, B_ACC = 13;
@@ -63,11 +69,11 @@ static_assert(OFF_ST % 1024 == 0 && SZ_STAGE % 1024 == 0 && OFF_OP % 1024 == 0, 
 
 constexpr uint32_t TMEM_COLS = 512;
 
-// Write 32 low-precision values (this thread's half of a 64-column operand row) as 4 swizzled chunks.
-__device__ __forceinline__ void st_op_half(uint32_t tile, int row, int wg, const uint32_t* w) {
+// Write this thread's NCOL low-precision values of a 64-column operand row as NCOL/8 swizzled chunks.
+__device__ __forceinline__ void st_op_part(uint32_t tile, int row, int wg, const uint32_t* w) {
 #pragma unroll
-  for (int q = 0; q < 4; ++q)
-    st_shared_v4(tile + sw128_off(row, wg * 4 + q), w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  for (int q = 0; q < NCOL / 8; ++q)
+    st_shared_v4(tile + sw128_off(row, wg * (NCOL / 8) + q), w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
 }
 
 template <bool kHalf>
@@ -101,12 +107,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
     for (int s = 0; s < NST; ++s) { mbar_init(BAR(B_KVF + s), 1); mbar_init(BAR(B_KVE + s), 1); }
     mbar_init(BAR(B_Q), 1);
     mbar_init(BAR(B_SUF), 1);
-    mbar_init(BAR(B_SUE), 256);
-    for (int i = 0; i < 2; ++i) { mbar_init(BAR(B_OPF + i), 256); mbar_init(BAR(B_OPE + i), 1); }
+    mbar_init(BAR(B_SUE), NCT);
+    for (int i = 0; i < 2; ++i) { mbar_init(BAR(B_OPF + i), NCT); mbar_init(BAR(B_OPE + i), 1); }
     mbar_init(BAR(B_ACC), 1);
     fence_barrier_init();
   }
-  if (warp == 9) { tmem_alloc(smem_u32(tmem_slot), TMEM_COLS); tmem_relinquish(); }
+  if (warp == WARP_MMA) { tmem_alloc(smem_u32(tmem_slot), TMEM_COLS); tmem_relinquish(); }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -114,7 +120,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
   auto key0 = [&](int n) { return n < ndiag ? m0 + n * 64 : (n - ndiag) * 64; };
   auto stage_addr = [&](int s) { return sbase + OFF_ST + (uint32_t)s * SZ_STAGE; };
 
-  if (warp == 8) {
+  if (warp == WARP_TMA) {
     if (lane == 0) {
       mbar_expect_tx(BAR(B_Q), SZ_Q + SZ_DO + SZ_C);
       tma_load_4d(sbase + OFF_Q, &p.tm_q128, BAR(B_Q), 0, m0, h, b);
@@ -132,7 +138,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
         tma_load_3d(st + SZ_K + SZ_V + SZ_B, &p.tm_pos, BAR(B_KVF + s), 0, j0, bh);
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == WARP_MMA) {
     if (lane == 0) {
       constexpr uint32_t fmt = kHalf ? 0 : 1;
       constexpr uint32_t id_s = make_idesc(128, 64, fmt, 0, 0);
@@ -183,7 +189,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
       umma_commit(BAR(B_ACC));
     }
   } else {
-    // ------------------------------------------------------------------ compute warps 0-7
+    // ------------------------------------------------------------------ compute warps
     const int wg = warp >> 2, quarter = warp & 3;
     const int r = quarter * 32 + lane;
     const int row = m0 + r;
@@ -201,15 +207,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
     const float lse = vrow ? p.lse[rb + row] : INFINITY;
     float* red = reinterpret_cast<float*>(gbase + OFF_RED);
     bool ok = warp_wait(BAR(B_Q), 0, p.status);
-    // delta'' = do . o'' over this warpgroup's 32 head dims (o'' snaps to the DT output where they agree
+    // delta'' = do . o'' over this warpgroup's NCOL head dims (o'' snaps to the DT output where they agree
     // to 2^-15, attention.py:341-350), combined across the two warpgroups.
     float dh = 0.f;
     if (ok && vrow) {
       const char* orow = p.o + 2 * ((int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)row * p.o_sl);
       const float* o32row = p.o32 ? p.o32 + (rb + row) * kD : nullptr;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int chunk = wg * 4 + q;
+      for (int q = 0; q < NCOL / 8; ++q) {
+        const int chunk = wg * (NCOL / 8) + q;
         const uint4 dv = *reinterpret_cast<const uint4*>(gbase + OFF_DO + sw128_off(r, chunk));
         const uint4 ov = *reinterpret_cast<const uint4*>(orow + chunk * 16);
         const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w}, ow[4] = {ov.x, ov.y, ov.z, ov.w};
@@ -229,38 +235,43 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
         }
       }
     }
-    // wg 1 hands its partial to wg 0, which forms delta'' and hands it back (identical bits in both)
-    if (wg == 1) red[r * 8 + 7] = dh;
-    named_bar_sync(1, 256);
+    // partial sums of the other warpgroups go to wg 0, which forms delta'' (fixed order) and hands it back
+    float* redr = red + r * (NWG * 8);
+    if (wg > 0) redr[wg * 8 + 7] = dh;
+    named_bar_sync(1, NCT);
     float dl = 0.f;
     if (wg == 0) {
-      dl = dh + red[r * 8 + 7];
-      red[r * 8 + 6] = dl;
+      dl = dh;
+#pragma unroll
+      for (int w = 1; w < NWG; ++w) dl += redr[w * 8 + 7];
+      redr[6] = dl;
     }
-    named_bar_sync(1, 256);
-    if (wg == 1) dl = red[r * 8 + 6];
-
-    const uint32_t tS = tmem_addr(tbase, quarter, COL_S + wg * 32);
-    const uint32_t tU = tmem_addr(tbase, quarter, COL_U + wg * 32);
-    const uint32_t tP = tmem_addr(tbase, quarter, COL_DP + wg * 32);
-    float za = 0.f, ya = 0.f, wa = 0.f, xa = 0.f, ptt = 0.f, dptt = 0.f, xd = 0.f, xo = 0.f, yo = 0.f;
+    named_bar_sync(1, NCT);
+    if (wg > 0) dl = redr[6];
+    const uint32_t tS = tmem_addr(tbase, quarter, COL_S + wg * NCOL);
+    const uint32_t tU = tmem_addr(tbase, quarter, COL_U + wg * NCOL);
+    const uint32_t tP = tmem_addr(tbase, quarter, COL_DP + wg * NCOL);
+    float za = 0.f, ya = 0.f, wa = 0.f, xa = 0.f, ptt = 0.f, dptt = 0.f, xd = 0.f;
+    const float2 c1v = bcast2(c1), l2e = bcast2(kLOG2E), fi2 = bcast2(fi), neg1 = bcast2(-1.f);
+    const float2 nlse2 = bcast2(-lse), ndl2 = bcast2(-dl), rs2v = bcast2(rs2);
+    float2 xo2 = bcast2(0.f), yo2 = bcast2(0.f), za2 = bcast2(0.f), wa2 = bcast2(0.f);
     for (int n = 0; ok && n < ntiles; ++n) {
       const int s = n % NST;
-      const int j0 = key0(n) + wg * 32;
+      const int j0 = key0(n) + wg * NCOL;
       if (!warp_wait(BAR(B_SUF), n & 1, p.status)) { ok = false; break; }
       tc_fence_after();
-      float sv[32], uv[32], pv[32];
-      tmem_ld32(tS, sv);
-      tmem_ld32(tU, uv);
-      tmem_ld32(tP, pv);
+      float sv[NCOL], uv[NCOL], pv[NCOL];
+      tmem_ld16(tS, sv);
+      tmem_ld16(tU, uv);
+      tmem_ld16(tP, pv);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(BAR(B_SUE));
-      const float4* cpos = reinterpret_cast<const float4*>(gbase + OFF_ST + s * SZ_STAGE + SZ_K + SZ_V + SZ_B) + wg * 32;
-      uint32_t wds[16], wdc[16];
+      const float4* cpos = reinterpret_cast<const float4*>(gbase + OFF_ST + s * SZ_STAGE + SZ_K + SZ_V + SZ_B) + wg * NCOL;
+      uint32_t wds[NCOL / 2], wdc[NCOL / 2];
       if (n < ndiag) {
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
+        for (int c = 0; c < NCOL; c += 2) {
           float dsv[2], dcv[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
@@ -289,48 +300,49 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
         }
       } else {
         const float ge = reinterpret_cast<const float4*>(gbase + OFF_ST + s * SZ_STAGE + SZ_K + SZ_V + SZ_B)[63].x;
-        const float mid = exp2f(fminf((ga - ge) * kLOG2E, 0.f));
+        const float2 mid2 = bcast2(exp2f(fminf((ga - ge) * kLOG2E, 0.f)));
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          float dsv[2], dcv[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int cc = c + e;
-            const float4 pj = cpos[cc];
-            const float cf = pj.w * mid;
-            const float uc = uv[cc] * cf;
-            const float x = fmaf(sv[cc], c1, fmaf(fi - pj.y, kLOG2E, uc * rs2));
-            const float pr = ex2_approx(x - lse);
-            const float ds = pr * (pv[cc] - dl);
-            xo = fmaf(ds, uc, xo);
-            yo = fmaf(pr, uc, yo);
-            za += pr;
-            wa += ds;
-            dsv[e] = ds;
-            dcv[e] = ds * cf;
-          }
-          wds[c / 2] = pack2<kHalf>(dsv[0], dsv[1]);
-          wdc[c / 2] = pack2<kHalf>(dcv[0], dcv[1]);
+        for (int c = 0; c < NCOL; c += 2) {
+          const float4 pa = cpos[c], pb = cpos[c + 1];
+          const float2 cf = mul2(make_float2(pa.w, pb.w), mid2);                  // colf mid
+          const float2 uc = mul2(make_float2(uv[c], uv[c + 1]), cf);
+          const float2 t = fma2(make_float2(pa.y, pb.y), neg1, fi2);              // F_i - F_j
+          const float2 y = fma2(uc, rs2v, fma2(t, l2e, nlse2));
+          const float2 x = fma2(make_float2(sv[c], sv[c + 1]), c1v, y);          // x - lse (log2)
+          const float2 pr = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+          const float2 ds = mul2(pr, add2(make_float2(pv[c], pv[c + 1]), ndl2));  // P (dP - delta'')
+          xo2 = fma2(ds, uc, xo2);
+          yo2 = fma2(pr, uc, yo2);
+          za2 = add2(za2, pr);
+          wa2 = add2(wa2, ds);
+          const float2 dsc = mul2(ds, cf);
+          wds[c / 2] = pack2<kHalf>(ds.x, ds.y);
+          wdc[c / 2] = pack2<kHalf>(dsc.x, dsc.y);
         }
       }
       if (n >= 2 && !warp_wait(BAR(B_OPE + (n & 1)), ((n >> 1) - 1) & 1, p.status)) { ok = false; break; }
       const uint32_t sDS = sbase + OFF_OP + (uint32_t)(n & 1) * 2 * SZ_OP;
-      st_op_half(sDS, r, wg, wds);
-      st_op_half(sDS + SZ_OP, r, wg, wdc);
+      st_op_part(sDS, r, wg, wds);
+      st_op_part(sDS + SZ_OP, r, wg, wdc);
       fence_proxy_async_smem();
       mbar_arrive(BAR(B_OPF + (n & 1)));
     }
-    xa = fmaf(rowf, xo, xa);
-    ya = fmaf(rowf, yo, ya);
-    // ---- combine the two warpgroups' row sums (wg 1 -> smem -> wg 0)
-    if (wg == 1) {
-      red[r * 8 + 0] = za; red[r * 8 + 1] = ya; red[r * 8 + 2] = wa; red[r * 8 + 3] = xa;
-      red[r * 8 + 4] = ptt; red[r * 8 + 5] = dptt; red[r * 8 + 6] = xd;
+    za += za2.x + za2.y;
+    wa += wa2.x + wa2.y;
+    xa = fmaf(rowf, xo2.x + xo2.y, xa);
+    ya = fmaf(rowf, yo2.x + yo2.y, ya);
+    // ---- combine the warpgroups' row sums (wg > 0 -> smem -> wg 0, fixed order)
+    if (wg > 0) {
+      redr[wg * 8 + 0] = za; redr[wg * 8 + 1] = ya; redr[wg * 8 + 2] = wa; redr[wg * 8 + 3] = xa;
+      redr[wg * 8 + 4] = ptt; redr[wg * 8 + 5] = dptt; redr[wg * 8 + 6] = xd;
     }
-    named_bar_sync(1, 256);
+    named_bar_sync(1, NCT);
     if (wg == 0) {
-      za += red[r * 8 + 0]; ya += red[r * 8 + 1]; wa += red[r * 8 + 2]; xa += red[r * 8 + 3];
-      ptt += red[r * 8 + 4]; dptt += red[r * 8 + 5]; xd += red[r * 8 + 6];
+#pragma unroll
+      for (int w = 1; w < NWG; ++w) {
+        za += redr[w * 8 + 0]; ya += redr[w * 8 + 1]; wa += redr[w * 8 + 2]; xa += redr[w * 8 + 3];
+        ptt += redr[w * 8 + 4]; dptt += redr[w * 8 + 5]; xd += redr[w * 8 + 6];
+      }
       // exact delta, delta-free diagonal (attention.py:449-480)
       float ssum = ptt + za;
       ssum = ssum > 0.f ? ssum : 1.f;
@@ -342,53 +354,64 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
       if (ok && !warp_wait(BAR(B_ACC), 0, p.status)) ok = false;
       if (ok) {
         tc_fence_after();
-        float acc[64], dco[32], dcd[32];
-        tmem_ld32(tmem_addr(tbase, quarter, COL_DQ), acc);
-        tmem_ld32(tmem_addr(tbase, quarter, COL_DQ + 32), acc + 32);
-        tmem_ld32(tmem_addr(tbase, quarter, COL_DCO), dco);
-        tmem_ld32(tmem_addr(tbase, quarter, COL_DCD), dcd);
-        tmem_wait_ld();
         if (vrow) {
-          p.rstat[rb + row] = make_float4(lse, dl, dd, dstt);
+          p.rstat[rb + row] = make_float4(-lse, -dl, -dd, dstt);   // negated: the dkv kernel adds them
           p.rl[rb + row] = dl_row + dstt * xd;
           p.rg[rb + row] = lam * dl_row;
           p.rf[rb + row] = wa - za * dd;
-          // dq = scale * (sum_{j<t} dS^ k_j + DT(dS_tt) k_t)
-          const float dsr = round_lp<kHalf>(dstt);
-          const char* krow = p.k + 2 * ((int64_t)b * p.k_sb + (int64_t)h * p.k_sh + (int64_t)row * p.k_sl);
-          uint4* dqrow = reinterpret_cast<uint4*>(p.dq + 2 * ((int64_t)b * p.dq_sb + (int64_t)h * p.dq_sh + (int64_t)row * p.dq_sl));
+        }
+        // dq = scale * (sum_{j<t} dS^ k_j + DT(dS_tt) k_t), 32 columns at a time (TMEM loads are warp-wide)
+        const float dsr = round_lp<kHalf>(dstt);
+        const char* krow = p.k + 2 * ((int64_t)b * p.k_sb + (int64_t)h * p.k_sh + (int64_t)(vrow ? row : 0) * p.k_sl);
+        uint4* dqrow = reinterpret_cast<uint4*>(p.dq + 2 * ((int64_t)b * p.dq_sb + (int64_t)h * p.dq_sh + (int64_t)(vrow ? row : 0) * p.dq_sl));
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          float acc[32];
+          tmem_ld32(tmem_addr(tbase, quarter, COL_DQ + half * 32), acc);
+          tmem_wait_ld();
+          if (vrow) {
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const uint4 kv = reinterpret_cast<const uint4*>(krow)[q];
-            const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
-            uint32_t w[4];
+            for (int q = 0; q < 4; ++q) {
+              const uint4 kv = reinterpret_cast<const uint4*>(krow)[half * 4 + q];
+              const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
+              uint32_t w[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float a0 = fmaf(dsr, unpack_lo<kHalf>(kw[i]), acc[q * 8 + 2 * i]) * kScale;
-              const float a1 = fmaf(dsr, unpack_hi<kHalf>(kw[i]), acc[q * 8 + 2 * i + 1]) * kScale;
-              w[i] = pack2<kHalf>(a0, a1);
+              for (int i = 0; i < 4; ++i) {
+                const float a0 = fmaf(dsr, unpack_lo<kHalf>(kw[i]), acc[q * 8 + 2 * i]) * kScale;
+                const float a1 = fmaf(dsr, unpack_hi<kHalf>(kw[i]), acc[q * 8 + 2 * i + 1]) * kScale;
+                w[i] = pack2<kHalf>(a0, a1);
+              }
+              dqrow[half * 4 + q] = make_uint4(w[0], w[1], w[2], w[3]);
             }
-            dqrow[q] = make_uint4(w[0], w[1], w[2], w[3]);
           }
-          // dc = dC_diag + lam rowf dC_off + DT(lam dS_tt) b_t   (fp32)
-          const float dsl = round_lp<kHalf>(dstt * lam);
-          const char* brow = p.bm + 2 * ((int64_t)b * p.b_sb + (int64_t)h * p.b_sh + (int64_t)row * p.b_sl);
-          float* dcrow = p.dc + ((int64_t)b * p.dc_sb + (int64_t)h * p.dc_sh + (int64_t)row * p.dc_sl);
+        }
+        // dc = dC_diag + lam rowf dC_off + DT(lam dS_tt) b_t   (fp32), 16 columns at a time
+        const float dsl = round_lp<kHalf>(dstt * lam);
+        const char* brow = p.bm + 2 * ((int64_t)b * p.b_sb + (int64_t)h * p.b_sh + (int64_t)(vrow ? row : 0) * p.b_sl);
+        float* dcrow = p.dc + ((int64_t)b * p.dc_sb + (int64_t)h * p.dc_sh + (int64_t)(vrow ? row : 0) * p.dc_sl);
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+          float dco[16], dcd[16];
+          tmem_ld16(tmem_addr(tbase, quarter, COL_DCO + half * 16), dco);
+          tmem_ld16(tmem_addr(tbase, quarter, COL_DCD + half * 16), dcd);
+          tmem_wait_ld();
+          if (vrow) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint4 bv = reinterpret_cast<const uint4*>(brow)[q];
-            const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
-            float o[8];
+            for (int q = 0; q < 2; ++q) {
+              const uint4 bv = reinterpret_cast<const uint4*>(brow)[half * 2 + q];
+              const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+              float o[8];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int d = q * 8 + 2 * i;
-              const float d0 = (ndiag > 0 ? dcd[d] : 0.f) + (ntiles > ndiag ? rs * dco[d] : 0.f);
-              const float d1 = (ndiag > 0 ? dcd[d + 1] : 0.f) + (ntiles > ndiag ? rs * dco[d + 1] : 0.f);
-              o[2 * i] = fmaf(dsl, unpack_lo<kHalf>(bw[i]), d0);
-              o[2 * i + 1] = fmaf(dsl, unpack_hi<kHalf>(bw[i]), d1);
+              for (int i = 0; i < 4; ++i) {
+                const int d = q * 8 + 2 * i;
+                const float d0 = (ndiag > 0 ? dcd[d] : 0.f) + (ntiles > ndiag ? rs * dco[d] : 0.f);
+                const float d1 = (ndiag > 0 ? dcd[d + 1] : 0.f) + (ntiles > ndiag ? rs * dco[d + 1] : 0.f);
+                o[2 * i] = fmaf(dsl, unpack_lo<kHalf>(bw[i]), d0);
+                o[2 * i + 1] = fmaf(dsl, unpack_hi<kHalf>(bw[i]), d1);
+              }
+              reinterpret_cast<float4*>(dcrow)[half * 4 + 2 * q] = make_float4(o[0], o[1], o[2], o[3]);
+              reinterpret_cast<float4*>(dcrow)[half * 4 + 2 * q + 1] = make_float4(o[4], o[5], o[6], o[7]);
             }
-            reinterpret_cast<float4*>(dcrow)[2 * q] = make_float4(o[0], o[1], o[2], o[3]);
-            reinterpret_cast<float4*>(dcrow)[2 * q + 1] = make_float4(o[4], o[5], o[6], o[7]);
           }
         }
       }
@@ -396,7 +419,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == WARP_MMA) {
     tc_fence_after();
     tmem_dealloc(tbase, TMEM_COLS);
   }
@@ -428,19 +451,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
     for (int s = 0; s < NST; ++s) { mbar_init(BAR(B_KVF + s), 1); mbar_init(BAR(B_KVE + s), 1); }
     mbar_init(BAR(B_K), 1);
     mbar_init(BAR(B_SUF), 1);
-    mbar_init(BAR(B_SUE), 256);
-    for (int i = 0; i < 2; ++i) { mbar_init(BAR(B_OPF + i), 256); mbar_init(BAR(B_OPE + i), 1); }
+    mbar_init(BAR(B_SUE), NCT);
+    for (int i = 0; i < 2; ++i) { mbar_init(BAR(B_OPF + i), NCT); mbar_init(BAR(B_OPE + i), 1); }
     mbar_init(BAR(B_ACC), 1);
     fence_barrier_init();
   }
-  if (warp == 9) { tmem_alloc(smem_u32(tmem_slot), TMEM_COLS); tmem_relinquish(); }
+  if (warp == WARP_MMA) { tmem_alloc(smem_u32(tmem_slot), TMEM_COLS); tmem_relinquish(); }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
   auto stage_addr = [&](int s) { return sbase + OFF_ST + (uint32_t)s * SZ_STAGE; };
 
-  if (warp == 8) {
+  if (warp == WARP_TMA) {
     if (lane == 0) {
       mbar_expect_tx(BAR(B_K), SZ_K + SZ_V + SZ_B);
       tma_load_4d(sbase + OFF_K, &p.tm_k128, BAR(B_K), 0, n0, h, b);
@@ -459,7 +482,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
         tma_load_3d(st + SZ_Q + SZ_DO + SZ_C + SZ_POS, &p.tm_rstat, BAR(B_KVF + s), 0, m0, bh);
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == WARP_MMA) {
     if (lane == 0) {
       constexpr uint32_t fmt = kHalf ? 0 : 1;
       constexpr uint32_t id_s = make_idesc(128, 64, fmt, 0, 0);
@@ -528,30 +551,32 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
     const float c1 = kScale * kLOG2E;
     const float dstt_j = vcol ? p.rstat[rb + j].w : 0.f;
     float* red = reinterpret_cast<float*>(gbase + OFF_RED);
-    const uint32_t tS = tmem_addr(tbase, quarter, COL_S + wg * 32);
-    const uint32_t tU = tmem_addr(tbase, quarter, COL_U + wg * 32);
-    const uint32_t tP = tmem_addr(tbase, quarter, COL_DP + wg * 32);
-    float dgu = 0.f, dgo = 0.f, dfs = 0.f;
+    const uint32_t tS = tmem_addr(tbase, quarter, COL_S + wg * NCOL);
+    const uint32_t tU = tmem_addr(tbase, quarter, COL_U + wg * NCOL);
+    const uint32_t tP = tmem_addr(tbase, quarter, COL_DP + wg * NCOL);
+    float dgu = 0.f, dfs = 0.f;
+    const float2 c1v = bcast2(c1), l2e = bcast2(kLOG2E), nfj2 = bcast2(-fj), rk2v = bcast2(rk2);
+    float2 dgo2 = bcast2(0.f), dfs2 = bcast2(0.f);
     bool ok = true;
     for (int n = 0; ok && n < ntiles; ++n) {
       const int s = n % NST;
-      const int i0 = n0 + 64 * n + wg * 32;            // first query column of this thread's half
+      const int i0 = n0 + 64 * n + wg * NCOL;          // first query column of this thread's part
       if (!warp_wait(BAR(B_SUF), n & 1, p.status)) { ok = false; break; }
       tc_fence_after();
-      float sv[32], uv[32], pv[32];
-      tmem_ld32(tS, sv);
-      tmem_ld32(tU, uv);
-      tmem_ld32(tP, pv);
+      float sv[NCOL], uv[NCOL], pv[NCOL];
+      tmem_ld16(tS, sv);
+      tmem_ld16(tU, uv);
+      tmem_ld16(tP, pv);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(BAR(B_SUE));
       const uint8_t* st = gbase + OFF_ST + s * SZ_STAGE;
-      const float4* cpos = reinterpret_cast<const float4*>(st + SZ_Q + SZ_DO + SZ_C) + wg * 32;
-      const float4* crst = reinterpret_cast<const float4*>(st + SZ_Q + SZ_DO + SZ_C + SZ_POS) + wg * 32;
-      uint32_t wp[16], wk[16], wb[16];
+      const float4* cpos = reinterpret_cast<const float4*>(st + SZ_Q + SZ_DO + SZ_C) + wg * NCOL;
+      const float4* crst = reinterpret_cast<const float4*>(st + SZ_Q + SZ_DO + SZ_C + SZ_POS) + wg * NCOL;
+      uint32_t wp[NCOL / 2], wk[NCOL / 2], wb[NCOL / 2];
       if (n < ndiag) {
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
+        for (int c = 0; c < NCOL; c += 2) {
           float pe[2], ke[2], be[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
@@ -565,9 +590,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
             const float dec = valid ? exp2f(fminf((pi.x - gj) * kLOG2E, 0.f)) : 0.f;
             const float u = dec * uv[cc];
             const float x = fmaf(sv[cc], c1, fmaf(pi.y - fj, kLOG2E, lam2 * u));
-            const float pr = valid ? ex2_approx(x - ri.x) : 0.f;
-            const float dsh = pr * (pv[cc] - ri.y);
-            const float dsx = fmaf(-pr, ri.z, dsh);
+            const float pr = valid ? ex2_approx(x + ri.x) : 0.f;   // ri = {-lse, -delta, -(T^-delta), dS_tt}
+            const float dsh = pr * (pv[cc] + ri.y);
+            const float dsx = fmaf(pr, ri.z, dsh);
             const float dso = strict ? dsx : 0.f;
             dgu = fmaf(dso, u, dgu);
             dfs += dso;
@@ -581,48 +606,48 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
         }
       } else {
         const float gs = reinterpret_cast<const float4*>(st + SZ_Q + SZ_DO + SZ_C)[0].x;   // query block start
-        const float mid = exp2f(fminf((gs - ge) * kLOG2E, 0.f));
+        const float2 mid2 = bcast2(exp2f(fminf((gs - ge) * kLOG2E, 0.f)));
         const bool tail = (n0 + 64 * n + 64 > L);
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          float pe[2], ke[2], be[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int cc = c + e;
-            const float4 pi = cpos[cc];
-            const float4 ri = crst[cc];
-            const float rq = pi.z * mid;
-            const float uc = uv[cc] * rq;
-            const float x = fmaf(sv[cc], c1, fmaf(pi.y - fj, kLOG2E, uc * rk2));
-            float pr = ex2_approx(x - ri.x);
-            if (tail && (i0 + cc >= L)) pr = 0.f;
-            const float dsh = pr * (pv[cc] - ri.y);
-            const float dsx = fmaf(-pr, ri.z, dsh);
-            dgo = fmaf(dsx, uc, dgo);
-            dfs += dsx;
-            pe[e] = pr;
-            ke[e] = dsx;
-            be[e] = dsh * rq;
+        for (int c = 0; c < NCOL; c += 2) {
+          const float4 pa = cpos[c], pb = cpos[c + 1];
+          const float4 ra = crst[c], rb4 = crst[c + 1];
+          const float2 rq = mul2(make_float2(pa.z, pb.z), mid2);                    // rowf mid
+          const float2 uc = mul2(make_float2(uv[c], uv[c + 1]), rq);
+          const float2 t = add2(make_float2(pa.y, pb.y), nfj2);                     // F_i - F_j
+          const float2 y = fma2(uc, rk2v, fma2(t, l2e, make_float2(ra.x, rb4.x))); // ... - lse_i
+          const float2 x = fma2(make_float2(sv[c], sv[c + 1]), c1v, y);
+          float2 pr = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+          if (tail) {
+            if (i0 + c >= L) pr.x = 0.f;
+            if (i0 + c + 1 >= L) pr.y = 0.f;
           }
-          wp[c / 2] = pack2<kHalf>(pe[0], pe[1]);
-          wk[c / 2] = pack2<kHalf>(ke[0], ke[1]);
-          wb[c / 2] = pack2<kHalf>(be[0], be[1]);
+          const float2 dsh = mul2(pr, add2(make_float2(pv[c], pv[c + 1]), make_float2(ra.y, rb4.y)));
+          const float2 dsx = fma2(pr, make_float2(ra.z, rb4.z), dsh);              // exact dS
+          dgo2 = fma2(dsx, uc, dgo2);
+          dfs2 = add2(dfs2, dsx);
+          const float2 dsb = mul2(dsh, rq);
+          wp[c / 2] = pack2<kHalf>(pr.x, pr.y);
+          wk[c / 2] = pack2<kHalf>(dsx.x, dsx.y);
+          wb[c / 2] = pack2<kHalf>(dsb.x, dsb.y);
         }
       }
       if (n >= 2 && !warp_wait(BAR(B_OPE + (n & 1)), ((n >> 1) - 1) & 1, p.status)) { ok = false; break; }
       const uint32_t sPT = sbase + OFF_OP + (uint32_t)(n & 1) * 3 * SZ_OP;
-      st_op_half(sPT, r, wg, wp);
-      st_op_half(sPT + SZ_OP, r, wg, wk);
-      st_op_half(sPT + 2 * SZ_OP, r, wg, wb);
+      st_op_part(sPT, r, wg, wp);
+      st_op_part(sPT + SZ_OP, r, wg, wk);
+      st_op_part(sPT + 2 * SZ_OP, r, wg, wb);
       fence_proxy_async_smem();
       mbar_arrive(BAR(B_OPF + (n & 1)));
     }
-    dgu = fmaf(colf, dgo, dgu);
-    if (wg == 1) { red[r * 4 + 0] = dgu; red[r * 4 + 1] = dfs; }
-    named_bar_sync(1, 256);
+    dfs += dfs2.x + dfs2.y;
+    dgu = fmaf(colf, dgo2.x + dgo2.y, dgu);
+    float* redr = red + r * (NWG * 2);
+    if (wg > 0) { redr[wg * 2 + 0] = dgu; redr[wg * 2 + 1] = dfs; }
+    named_bar_sync(1, NCT);
     if (wg == 0) {
-      dgu += red[r * 4 + 0];
-      dfs += red[r * 4 + 1];
+#pragma unroll
+      for (int w = 1; w < NWG; ++w) { dgu += redr[w * 2 + 0]; dfs += redr[w * 2 + 1]; }
       if (ok && !warp_wait(BAR(B_ACC), 0, p.status)) ok = false;
       if (ok) {
         tc_fence_after();
@@ -671,7 +696,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == WARP_MMA) {
     tc_fence_after();
     tmem_dealloc(tbase, TMEM_COLS);
   }

@@ -9,12 +9,15 @@
 //   warp 4     TMA producer: Q and C once, then K, V, B~ and the key position records per 64-key tile,
 //   warp 5     UMMA issuer (one lane) and TMEM owner.
 // Per key tile: S = Q K^T and U = C B~^T (M=128, N=64) land in TMEM; the softmax threads build
-// x = s log2e, write P = 2^(x - m) in bf16 to shared memory (128B-swizzled, K-major) and the MMA
-// warp accumulates O += P V in TMEM. The running maximum is rescaled lazily: O (in TMEM), l and
-// sum DT(p) are corrected only when a row's tile maximum exceeds the reference maximum by more
-// than 2^8, so most tiles need no correction pass. Key tiles are visited diagonal first, then
-// from the start of the sequence. TMEM: 256 columns (S 64 | U 64 | O 64 | spare), so two CTAs
-// share an SM and one CTA's MMAs overlap the other's softmax.
+// x = s log2e and write P = 2^(x - m) as packed bf16 straight into tensor memory (one tcgen05.st
+// per thread), from where the MMA warp accumulates O += P V with A read from TMEM - the tensor core
+// reads only V from shared memory, which keeps these small-N UMMAs off the shared-memory bandwidth
+// limit. The running maximum is rescaled lazily: O (in TMEM), l and sum DT(p) are corrected only
+// when a row's tile maximum exceeds the reference maximum by more than 2^8, so most tiles need no
+// correction pass. The per-element arithmetic runs on packed fp32 pairs (FFMA2/FADD2/FMUL2) with
+// tree reductions. Key tiles are visited diagonal first, then from the start of the sequence.
+// TMEM: 256 columns (S 64 | U 64 | O 64 | P 2 x 32), so two CTAs share an SM and one CTA's MMAs
+// overlap the other's softmax.
 #include <cuda_runtime.h>
 
 #include "attn_common.cuh"
@@ -29,15 +32,14 @@ constexpr uint32_t SZ_K = BN * 128, SZ_V = BN * 128, SZ_B = BN * 64, SZ_POS = BN
 constexpr uint32_t SZ_STAGE = SZ_K + SZ_V + SZ_B + SZ_POS;    // 21504 = 21 KiB
 constexpr uint32_t SZ_P = BM * 128;
 constexpr uint32_t OFF_Q = 0, OFF_C = OFF_Q + SZ_Q, OFF_ST = OFF_C + SZ_C;
-constexpr uint32_t OFF_P = OFF_ST + NSTAGE * SZ_STAGE;
-constexpr uint32_t OFF_BAR = OFF_P + 2 * SZ_P;
+constexpr uint32_t OFF_BAR = OFF_ST + NSTAGE * SZ_STAGE;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
 constexpr uint32_t TMEM_COLS = 256;
-constexpr int COL_S = 0, COL_U = 64, COL_O = 128;
+constexpr int COL_S = 0, COL_U = 64, COL_O = 128, COL_P = 192;   // P: two 32-column bf16x2 buffers
 // barrier indices
 constexpr int B_Q = 0, B_KVF = 1, B_KVE = 3, B_SUF = 5, B_SUE = 6, B_PF = 7, B_PE = 9, B_O = 11;
 
-static_assert(OFF_ST % 1024 == 0 && SZ_STAGE % 1024 == 0 && OFF_P % 1024 == 0, "swizzle alignment");
+static_assert(OFF_ST % 1024 == 0 && SZ_STAGE % 1024 == 0, "swizzle alignment");
 
 template <bool kHalf>
 __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant__ FwdParams p) {
@@ -109,11 +111,11 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         const int buf = m & 1, s = m % NSTAGE;
         if (!mbar_wait(BAR(B_PF + buf), (m >> 1) & 1, p.status)) return false;
         tc_fence_after();
-        const uint32_t sP = sbase + OFF_P + (uint32_t)buf * SZ_P;
+        const uint32_t tP = tbase + COL_P + (uint32_t)buf * 32;
         const uint32_t sV = stage_addr(s) + SZ_K;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          umma_ss(tO, desc_k128(sP + k * 32), desc_mn128(sV + k * 2048), id_pv, (m > 0 || k > 0) ? 1u : 0u);
+          umma_ts(tO, tP + k * 8, desc_mn128(sV + k * 2048), id_pv, (m > 0 || k > 0) ? 1u : 0u);
         umma_commit(BAR(B_PE + buf));
         umma_commit(BAR(B_KVE + s));
         return true;
@@ -151,7 +153,10 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     const uint32_t tS = tmem_addr(tbase, warp, COL_S);
     const uint32_t tU = tmem_addr(tbase, warp, COL_U);
     const uint32_t tO = tmem_addr(tbase, warp, COL_O);
-    float m_ref = -INFINITY, l = 0.f, lb = 0.f;
+    const float2 c1v = bcast2(c1), l2e = bcast2(kLOG2E), fi2 = bcast2(fi), neg1 = bcast2(-1.f);
+    float m_ref = -INFINITY;
+    float2 lacc[4] = {bcast2(0.f), bcast2(0.f), bcast2(0.f), bcast2(0.f)};   // l = sum of fp32 p
+    float2 lbacc[2] = {bcast2(0.f), bcast2(0.f)};                              // sum of DT(p)
     bool ok = true;
     for (int n = 0; n < ntiles; ++n) {
       const int s = n % NSTAGE;
@@ -159,53 +164,57 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
       if (!warp_wait(BAR(B_SUF), n & 1, p.status)) { ok = false; break; }
       tc_fence_after();
       const float4* cpos = reinterpret_cast<const float4*>(gbase + OFF_ST + s * SZ_STAGE + SZ_K + SZ_V + SZ_B);
-      float x[64];
+      float sv[64], uv[64];
+      tmem_ld32(tS, sv);
+      tmem_ld32(tS + 32, sv + 32);
+      tmem_ld32(tU, uv);
+      tmem_ld32(tU + 32, uv + 32);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(BAR(B_SUE));            // S and U are in registers: the next tile's GEMMs may start
+      float2* x2 = reinterpret_cast<float2*>(sv);     // x overwrites S in place, two columns per float2
       if (n < ndiag) {
-        // diagonal tile: pairwise decay, causal mask and sequence end
+        // diagonal tile: pairwise decay exp(min(g_i - g_j, 0)), causal mask and sequence end
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          float sv[32], uv[32];
-          tmem_ld32(tS + half * 32, sv);
-          tmem_ld32(tU + half * 32, uv);
-          tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const int cc = half * 32 + c;
-            const float4 pj = cpos[cc];
-            const float dec = exp2f(fminf((gi - pj.x) * kLOG2E, 0.f));
-            const float xv = fmaf(sv[c], c1, fmaf(fi - pj.y, kLOG2E, lam2 * (dec * uv[c])));
-            const int j = j0 + cc;
-            x[cc] = (j <= row && j < L) ? xv : -INFINITY;
-          }
+        for (int c = 0; c < 32; ++c) {
+          const float4 pa = cpos[2 * c], pb = cpos[2 * c + 1];
+          const float da = exp2f(fminf((gi - pa.x) * kLOG2E, 0.f));
+          const float db = exp2f(fminf((gi - pb.x) * kLOG2E, 0.f));
+          const float2 u = mul2(make_float2(da, db), make_float2(uv[2 * c], uv[2 * c + 1]));
+          const float2 t = fma2(make_float2(pa.y, pb.y), neg1, fi2);                  // F_i - F_j
+          const float2 y = fma2(u, bcast2(lam2), mul2(t, l2e));
+          float2 x = fma2(x2[c], c1v, y);
+          const int j = j0 + 2 * c;
+          if (!(j <= row && j < L)) x.x = -INFINITY;
+          if (!(j + 1 <= row && j + 1 < L)) x.y = -INFINITY;
+          x2[c] = x;
         }
       } else {
         const float ge = cpos[BN - 1].x;
-        const float rsm = rs * exp2f(fminf((ga - ge) * kLOG2E, 0.f)) * kLOG2E;   // lam rowf mid log2e
+        const float2 rsm = bcast2(rs * exp2f(fminf((ga - ge) * kLOG2E, 0.f)) * kLOG2E);   // lam rowf mid log2e
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          float sv[32], uv[32];
-          tmem_ld32(tS + half * 32, sv);
-          tmem_ld32(tU + half * 32, uv);
-          tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const int cc = half * 32 + c;
-            const float4 pj = cpos[cc];
-            x[cc] = fmaf(sv[c], c1, fmaf(fi - pj.y, kLOG2E, (uv[c] * pj.w) * rsm));
-          }
+        for (int c = 0; c < 32; ++c) {
+          const float4 pa = cpos[2 * c], pb = cpos[2 * c + 1];
+          const float2 w = mul2(make_float2(uv[2 * c], uv[2 * c + 1]), make_float2(pa.w, pb.w));   // U colf
+          const float2 t = fma2(make_float2(pa.y, pb.y), neg1, fi2);
+          const float2 y = fma2(w, rsm, mul2(t, l2e));
+          x2[c] = fma2(x2[c], c1v, y);
         }
       }
-      tc_fence_before();
-      mbar_arrive(BAR(B_SUE));            // S and U are in registers: the next tile's GEMMs may start
-
-      float mt = x[0];
+      // tile maximum: 8 independent partial maxima
+      float mx[8];
 #pragma unroll
-      for (int c = 1; c < 64; ++c) mt = fmaxf(mt, x[c]);
+      for (int i = 0; i < 8; ++i) mx[i] = fmaxf(sv[i], sv[i + 8]);
+#pragma unroll
+      for (int c = 16; c < 64; c += 8)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], sv[c + i]);
+      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       const bool need = mt > m_ref + 8.f;
       const float m_new = need ? mt : m_ref;
       const float corr = need ? ex2_approx(m_ref - m_new) : 1.f;
       if (__any_sync(0xffffffffu, need) && n > 0) {
-        // lazy correction of O: wait until O += P V of the previous tile has landed
+        // lazy correction of O and of the DT(p) row sum: wait until the previous tile's UMMAs have landed
         if (!warp_wait(BAR(B_PE + ((n - 1) & 1)), ((n - 1) >> 1) & 1, p.status)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
@@ -219,31 +228,32 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         }
         tmem_wait_st();
       }
-      l *= corr;
-      lb *= corr;
+      const float2 corr2 = bcast2(corr);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) lacc[i] = mul2(lacc[i], corr2);
+      lbacc[0] = mul2(lbacc[0], corr2);
+      lbacc[1] = mul2(lbacc[1], corr2);
       m_ref = m_new;
-      const float mu = (m_ref == -INFINITY) ? 0.f : m_ref;
+      const float2 mu2 = bcast2((m_ref == -INFINITY) ? 0.f : -m_ref);
       if (n >= 2 && !warp_wait(BAR(B_PE + (n & 1)), ((n >> 1) - 1) & 1, p.status)) { ok = false; break; }
-      const uint32_t sP = sbase + OFF_P + (uint32_t)(n & 1) * SZ_P;
+      uint32_t w[32];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        uint32_t w[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float p0 = ex2_approx(x[q * 8 + 2 * i] - mu);
-          const float p1 = ex2_approx(x[q * 8 + 2 * i + 1] - mu);
-          l += p0;
-          l += p1;
-          w[i] = pack2<kHalf>(p0, p1);
-          lb += unpack_lo<kHalf>(w[i]);
-          lb += unpack_hi<kHalf>(w[i]);
-        }
-        st_shared_v4(sP + sw128_off(r, q), w[0], w[1], w[2], w[3]);
+      for (int c = 0; c < 32; ++c) {
+        const float2 d = add2(x2[c], mu2);
+        const float2 pe = make_float2(ex2_approx(d.x), ex2_approx(d.y));
+        lacc[c & 3] = add2(lacc[c & 3], pe);
+        w[c] = pack2<kHalf>(pe.x, pe.y);
+        lbacc[c & 1] = add2(lbacc[c & 1], make_float2(unpack_lo<kHalf>(w[c]), unpack_hi<kHalf>(w[c])));
       }
-      fence_proxy_async_smem();
+      tmem_st32u(tmem_addr(tbase, warp, COL_P + (n & 1) * 32), w);
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(BAR(B_PF + (n & 1)));
     }
+    const float2 lsum = add2(add2(lacc[0], lacc[1]), add2(lacc[2], lacc[3]));
+    const float l = lsum.x + lsum.y;
+    const float2 lbsum = add2(lbacc[0], lbacc[1]);
+    const float lb = lbsum.x + lbsum.y;
     if (ok && !warp_wait(BAR(B_O), 0, p.status)) ok = false;
     if (ok) {
       tc_fence_after();

@@ -6,7 +6,8 @@
 //
 // HBM-bound: per cached key and head it reads k (128 B), v (128 B), b~ (64 B), g and F (8 B).
 // Split-K over the key axis: grid (splits, B*H); each CTA (256 threads) walks its key range in chunks
-// of 256 keys - phase 1 one thread per key computes the score from its k / b~ rows, phase 2 the chunk
+// of 256 keys - phase 1 scores four keys per warp step with eight lanes per key (each step reads whole
+// 128-byte k rows and 64-byte b~ rows, a 3-step shuffle finishes the dot products), phase 2 the chunk
 // maximum, phase 3 p = 2^(x - m), phase 4 every warp accumulates p v over its keys with one lane per pair
 // of head dimensions (coalesced 128-byte v rows). A second kernel merges the splits' (m, l, acc).
 #include <cuda_runtime.h>
@@ -51,10 +52,23 @@ __global__ void __launch_bounds__(NT) decode_split_kernel(DecodeParams p) {
   __shared__ float s_acc[NW][64];
   __shared__ float s_l[NW];
 
-  // query row and its side values (fp32)
-  float q[64], c[32];
-  load_row<kHalf>(p.q + 2 * ((int64_t)b * p.q_sb + (int64_t)h * p.q_sh), 8, q);
-  load_row<kHalf>(p.c + 2 * ((int64_t)b * p.c_sb + (int64_t)h * p.c_sh), 4, c);
+  // this lane's slices of the query row: lanes are grouped 8 per key, lane part p holds head dims
+  // [8p, 8p + 8) of q and, for p < 4, state dims [8p, 8p + 8) of c
+  const int sub = lane >> 3, part = lane & 7;
+  float q8[8], c8[8];
+  {
+    const uint4 v = reinterpret_cast<const uint4*>(p.q + 2 * ((int64_t)b * p.q_sb + (int64_t)h * p.q_sh))[part];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) { q8[2 * e] = unpack_lo<kHalf>(w[e]); q8[2 * e + 1] = unpack_hi<kHalf>(w[e]); }
+  }
+  {
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (part < 4) v = reinterpret_cast<const uint4*>(p.c + 2 * ((int64_t)b * p.c_sb + (int64_t)h * p.c_sh))[part];
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) { c8[2 * e] = unpack_lo<kHalf>(w[e]); c8[2 * e + 1] = unpack_hi<kHalf>(w[e]); }
+  }
   const float gq = p.g_q[bh];
   const float fq = p.f_q ? p.f_q[bh] : 0.f;
   const float lam = p.lam[h];
@@ -70,40 +84,37 @@ __global__ void __launch_bounds__(NT) decode_split_kernel(DecodeParams p) {
   float acc0 = 0.f, acc1 = 0.f;  // this lane's two head dims of the warp's partial p.v
   float lsum = 0.f;              // warp's partial sum of p (kept by every lane)
   for (int base = j_begin; base < j_end; base += NT) {
-    // ---- phase 1: one key per thread
-    const int j = base + tid;
-    float x = -INFINITY;
-    if (j < j_end) {
-      // stream the k and b~ rows 16 bytes at a time (8 values)
+    // ---- phase 1: warp w scores keys [base + 32w, base + 32w + 32), 4 keys per step, 8 lanes per key;
+    //      each step reads four whole 128-byte k rows and 64-byte b~ rows (coalesced)
+#pragma unroll 2
+    for (int it = 0; it < 8; ++it) {
+      const int kk = warp * 32 + it * 4 + sub;
+      const int j = base + kk;
+      const bool ok = j < j_end;
+      const int jj = ok ? j : j_begin;
+      const uint4 kv = reinterpret_cast<const uint4*>(kbase + 2 * (int64_t)jj * p.k_sl)[part];
+      uint4 bv = make_uint4(0, 0, 0, 0);
+      if (part < 4) bv = reinterpret_cast<const uint4*>(bbase + 2 * (int64_t)jj * p.b_sl)[part];
+      const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
       float qk = 0.f, cb = 0.f;
-      const uint4* kr = reinterpret_cast<const uint4*>(kbase + 2 * (int64_t)j * p.k_sl);
-      const uint4* br = reinterpret_cast<const uint4*>(bbase + 2 * (int64_t)j * p.b_sl);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint4 v = kr[i];
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          qk = fmaf(q[i * 8 + 2 * e], unpack_lo<kHalf>(w[e]), qk);
-          qk = fmaf(q[i * 8 + 2 * e + 1], unpack_hi<kHalf>(w[e]), qk);
-        }
+      for (int e = 0; e < 4; ++e) {
+        qk = fmaf(q8[2 * e], unpack_lo<kHalf>(kw[e]), qk);
+        qk = fmaf(q8[2 * e + 1], unpack_hi<kHalf>(kw[e]), qk);
+        cb = fmaf(c8[2 * e], unpack_lo<kHalf>(bw[e]), cb);
+        cb = fmaf(c8[2 * e + 1], unpack_hi<kHalf>(bw[e]), cb);
       }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint4 v = br[i];
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          cb = fmaf(c[i * 8 + 2 * e], unpack_lo<kHalf>(w[e]), cb);
-          cb = fmaf(c[i * 8 + 2 * e + 1], unpack_hi<kHalf>(w[e]), cb);
-        }
-      }
-      const float gj = gbase[j];
-      const float fj = fbase ? fbase[j] : 0.f;
+      const float gj = gbase[jj];
+      const float fj = fbase ? fbase[jj] : 0.f;
       const float dec = exp2f(fminf((gq - gj) * kLog2e, 0.f));
-      x = fmaf(qk, c1, fmaf(fq - fj, kLog2e, lam2 * (dec * cb)));
+      float part_x = fmaf(qk, c1, lam2 * (dec * cb));
+      part_x += __shfl_xor_sync(0xffffffffu, part_x, 1);
+      part_x += __shfl_xor_sync(0xffffffffu, part_x, 2);
+      part_x += __shfl_xor_sync(0xffffffffu, part_x, 4);
+      if (part == 0) s_x[kk] = ok ? fmaf(fq - fj, kLog2e, part_x) : -INFINITY;
     }
-    s_x[tid] = x;
+    __syncthreads();
+    const float x = s_x[tid];
     // ---- phase 2: chunk maximum
     float mx = x;
 #pragma unroll
@@ -121,6 +132,7 @@ __global__ void __launch_bounds__(NT) decode_split_kernel(DecodeParams p) {
     acc1 *= corr;
     lsum *= corr;
     const int nk = min(NT, j_end - base);
+#pragma unroll 8
     for (int t = warp; t < nk; t += NW) {
       const float pj = exp2f(s_x[t] - m_new);
       const uint32_t vv = *reinterpret_cast<const uint32_t*>(vbase + 2 * ((int64_t)(base + t) * p.v_sl + 2 * lane));
