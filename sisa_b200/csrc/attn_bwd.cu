@@ -17,8 +17,8 @@
 // Both kernels: 16 compute warps (four warpgroups splitting each tile's 64 columns 16/16/16/16; thread =
 // TMEM lane = owned row, four compute warps per SM sub-partition), one TMA producer warp and one UMMA warp. Per tile the compute warps pull
 // S, U, dP into registers and release TMEM at once, so the next tile's GEMMs overlap their math;
-// the gradient GEMMs read bf16 operands the compute warps wrote to double-buffered, 128B-swizzled
-// shared memory.
+// the gradient GEMMs read the bf16 operands (dS, P^T, ...) the compute warps stored into tensor
+// memory (A from TMEM), so the tensor core fetches only the B tiles from shared memory.
 #include <cuda_runtime.h>
 
 #include "attn_common.cuh"
@@ -40,15 +40,15 @@ namespace dqk {
 constexpr uint32_t SZ_Q = 128 * 128, SZ_DO = 128 * 128, SZ_C = 128 * 64;
 constexpr uint32_t SZ_K = 64 * 128, SZ_V = 64 * 128, SZ_B = 64 * 64, SZ_POS = 64 * 16;
 constexpr uint32_t SZ_STAGE = SZ_K + SZ_V + SZ_B + SZ_POS;   // 21504
-constexpr uint32_t SZ_OP = 128 * 128;                          // one 128 x 64 bf16 operand tile
 constexpr uint32_t OFF_Q = 0, OFF_DO = OFF_Q + SZ_Q, OFF_C = OFF_DO + SZ_DO, OFF_ST = OFF_C + SZ_C;
-constexpr uint32_t OFF_OP = OFF_ST + NST * SZ_STAGE;           // [buf][dS, dSC]
-constexpr uint32_t OFF_RED = OFF_OP + 4 * SZ_OP;               // 128 rows x NWG x 8 floats
+constexpr uint32_t OFF_RED = OFF_ST + NST * SZ_STAGE;          // 128 rows x NWG x 8 floats
 constexpr uint32_t OFF_BAR = OFF_RED + 128 * NWG * 8 * 4;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
-constexpr int COL_S = 0, COL_U = 64, COL_DP = 128, COL_DQ = 192, COL_DCO = 256, COL_DCD = 288;
+// TMEM: S, U, dP per tile; dQ, dC_off, dC_diag accumulators; the bf16 operands dS and dS*cf of the
+// gradient UMMAs (two buffers of 2 x 32 columns, written by the compute warps, read as A from TMEM)
+constexpr int COL_S = 0, COL_U = 64, COL_DP = 128, COL_DQ = 192, COL_DCO = 256, COL_DCD = 288, COL_OPS = 320;
 constexpr int B_KVF = 0, B_KVE = 3, B_Q = 6, B_SUF = 7, B_SUE = 8, B_OPF = 9, B_OPE = 11, B_ACC = 13;
-static_assert(OFF_ST % 1024 == 0 && OFF_OP % 1024 == 0, "alignment");
+static_assert(OFF_ST % 1024 == 0, "alignment");
 }  // namespace dqk
 
 // ----------------------------------------------------------------------------- dkv kernel layout
@@ -56,24 +56,25 @@ namespace dkv {
 constexpr uint32_t SZ_K = 128 * 128, SZ_V = 128 * 128, SZ_B = 128 * 64;
 constexpr uint32_t SZ_Q = 64 * 128, SZ_DO = 64 * 128, SZ_C = 64 * 64, SZ_POS = 64 * 16, SZ_RST = 64 * 16;
 constexpr uint32_t SZ_STAGE = SZ_Q + SZ_DO + SZ_C + SZ_POS + SZ_RST;   // 22528
-constexpr uint32_t SZ_OP = 128 * 128;
 constexpr uint32_t OFF_K = 0, OFF_V = OFF_K + SZ_K, OFF_B = OFF_V + SZ_V, OFF_ST = OFF_B + SZ_B;
-constexpr uint32_t OFF_OP = OFF_ST + NST * SZ_STAGE;                   // [buf][P, dS, dSb]
-constexpr uint32_t OFF_RED = OFF_OP + 6 * SZ_OP;                       // 128 rows x NWG x 2 floats
+constexpr uint32_t OFF_RED = OFF_ST + NST * SZ_STAGE;                  // 128 rows x NWG x 2 floats
 constexpr uint32_t OFF_BAR = OFF_RED + 128 * NWG * 2 * 4;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
-constexpr int COL_S = 0, COL_U = 64, COL_DP = 128, COL_DV = 192, COL_DK = 256, COL_DBD = 320, COL_DBO = 352;
+// TMEM: S^T, U^T, dP^T per tile; dV, dK, dB_diag, dB_off accumulators; the bf16 operands P^T, dS^T,
+// (dS^' rq)^T (one buffer of 3 x 32 columns, A operands read from TMEM)
+constexpr int COL_S = 0, COL_U = 64, COL_DP = 128, COL_DV = 192, COL_DK = 256, COL_DBD = 320, COL_DBO = 352,
+              COL_OPS = 384;
 constexpr int B_KVF = 0, B_KVE = 3, B_K = 6, B_SUF = 7, B_SUE = 8, B_OPF = 9, B_OPE = 11, B_ACC = 13;
-static_assert(OFF_ST % 1024 == 0 && SZ_STAGE % 1024 == 0 && OFF_OP % 1024 == 0, "alignment");
+static_assert(OFF_ST % 1024 == 0 && SZ_STAGE % 1024 == 0, "alignment");
 }  // namespace dkv
 
 constexpr uint32_t TMEM_COLS = 512;
 
-// Write this thread's NCOL low-precision values of a 64-column operand row as NCOL/8 swizzled chunks.
-__device__ __forceinline__ void st_op_part(uint32_t tile, int row, int wg, const uint32_t* w) {
-#pragma unroll
-  for (int q = 0; q < NCOL / 8; ++q)
-    st_shared_v4(tile + sw128_off(row, wg * (NCOL / 8) + q), w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+// Store this thread's NCOL low-precision operand values (NCOL/2 packed pairs) into its lane of a
+// 32-column TMEM operand tile: warpgroup wg owns columns [wg * NCOL/2, (wg + 1) * NCOL/2).
+__device__ __forceinline__ void st_op_tmem(uint32_t tbase, int quarter, int col, int wg, const uint32_t* w) {
+  static_assert(NCOL == 16, "one x8 store per operand");
+  tmem_st8(tmem_addr(tbase, quarter, col + wg * (NCOL / 2)), w);
 }
 
 template <bool kHalf>
@@ -151,17 +152,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
         const int buf = m & 1, s = m % NST;
         if (!mbar_wait(BAR(B_OPF + buf), (m >> 1) & 1, p.status)) return false;
         tc_fence_after();
-        const uint32_t sDS = sbase + OFF_OP + (uint32_t)buf * 2 * SZ_OP, sDSC = sDS + SZ_OP;
+        const uint32_t tDS = tbase + COL_OPS + (uint32_t)buf * 64, tDSC = tDS + 32;
         const uint32_t st = stage_addr(s);
         const bool dg = m < ndiag;
         const uint32_t tdc = tbase + (dg ? COL_DCD : COL_DCO);
         int& cnt = dg ? ndcd : ndco;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          umma_ss(tbase + COL_DQ, desc_k128(sDS + k * 32), desc_mn128(st + k * 2048), id_dq, (m > 0 || k > 0));
+          umma_ts(tbase + COL_DQ, tDS + k * 8, desc_mn128(st + k * 2048), id_dq, (m > 0 || k > 0));
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          umma_ss(tdc, desc_k128(sDSC + k * 32), desc_mn64(st + SZ_K + SZ_V + k * 1024), id_dc, (cnt > 0 || k > 0));
+          umma_ts(tdc, tDSC + k * 8, desc_mn64(st + SZ_K + SZ_V + k * 1024), id_dc, (cnt > 0 || k > 0));
         ++cnt;
         umma_commit(BAR(B_OPE + buf));
         umma_commit(BAR(B_KVE + s));
@@ -321,10 +322,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
         }
       }
       if (n >= 2 && !warp_wait(BAR(B_OPE + (n & 1)), ((n >> 1) - 1) & 1, p.status)) { ok = false; break; }
-      const uint32_t sDS = sbase + OFF_OP + (uint32_t)(n & 1) * 2 * SZ_OP;
-      st_op_part(sDS, r, wg, wds);
-      st_op_part(sDS + SZ_OP, r, wg, wdc);
-      fence_proxy_async_smem();
+      st_op_tmem(tbase, quarter, COL_OPS + (n & 1) * 64, wg, wds);
+      st_op_tmem(tbase, quarter, COL_OPS + (n & 1) * 64 + 32, wg, wdc);
+      tmem_wait_st();
+      tc_fence_before();
       mbar_arrive(BAR(B_OPF + (n & 1)));
     }
     za += za2.x + za2.y;
@@ -495,20 +496,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
         const int buf = m & 1, s = m % NST;
         if (!mbar_wait(BAR(B_OPF + buf), (m >> 1) & 1, p.status)) return false;
         tc_fence_after();
-        const uint32_t sPT = sbase + OFF_OP + (uint32_t)buf * 3 * SZ_OP, sDST = sPT + SZ_OP, sDSB = sDST + SZ_OP;
+        const uint32_t tPT = tbase + COL_OPS, tDST = tPT + 32, tDSB = tPT + 64;
         const uint32_t st = stage_addr(s);
         const bool dg = m < ndiag;
         int& cnt = dg ? nbd : nbo;
         const uint32_t tdb = tbase + (dg ? COL_DBD : COL_DBO);
 #pragma unroll
         for (int k = 0; k < 4; ++k)   // dV += P^T dO
-          umma_ss(tbase + COL_DV, desc_k128(sPT + k * 32), desc_mn128(st + SZ_Q + k * 2048), id_mn64, (m > 0 || k > 0));
+          umma_ts(tbase + COL_DV, tPT + k * 8, desc_mn128(st + SZ_Q + k * 2048), id_mn64, (m > 0 || k > 0));
 #pragma unroll
         for (int k = 0; k < 4; ++k)   // dK += dS^T Q
-          umma_ss(tbase + COL_DK, desc_k128(sDST + k * 32), desc_mn128(st + k * 2048), id_mn64, (m > 0 || k > 0));
+          umma_ts(tbase + COL_DK, tDST + k * 8, desc_mn128(st + k * 2048), id_mn64, (m > 0 || k > 0));
 #pragma unroll
         for (int k = 0; k < 4; ++k)   // dB += dSb^T C
-          umma_ss(tdb, desc_k128(sDSB + k * 32), desc_mn64(st + SZ_Q + SZ_DO + k * 1024), id_mn32, (cnt > 0 || k > 0));
+          umma_ts(tdb, tDSB + k * 8, desc_mn64(st + SZ_Q + SZ_DO + k * 1024), id_mn32, (cnt > 0 || k > 0));
         ++cnt;
         umma_commit(BAR(B_OPE + buf));
         umma_commit(BAR(B_KVE + s));
@@ -632,12 +633,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
           wb[c / 2] = pack2<kHalf>(dsb.x, dsb.y);
         }
       }
-      if (n >= 2 && !warp_wait(BAR(B_OPE + (n & 1)), ((n >> 1) - 1) & 1, p.status)) { ok = false; break; }
-      const uint32_t sPT = sbase + OFF_OP + (uint32_t)(n & 1) * 3 * SZ_OP;
-      st_op_part(sPT, r, wg, wp);
-      st_op_part(sPT + SZ_OP, r, wg, wk);
-      st_op_part(sPT + 2 * SZ_OP, r, wg, wb);
-      fence_proxy_async_smem();
+      // one operand buffer: the previous tile's gradient UMMAs must have read it
+      if (n >= 1 && !warp_wait(BAR(B_OPE + ((n - 1) & 1)), ((n - 1) >> 1) & 1, p.status)) { ok = false; break; }
+      st_op_tmem(tbase, quarter, COL_OPS, wg, wp);
+      st_op_tmem(tbase, quarter, COL_OPS + 32, wg, wk);
+      st_op_tmem(tbase, quarter, COL_OPS + 64, wg, wb);
+      tmem_wait_st();
+      tc_fence_before();
       mbar_arrive(BAR(B_OPF + (n & 1)));
     }
     dfs += dfs2.x + dfs2.y;
