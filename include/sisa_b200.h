@@ -152,6 +152,18 @@ int sisa_decode_attn(const sisa_view4* q, const sisa_view4* c, const float* g_q,
                      int64_t B, int64_t H, int64_t N, int dtype, const sisa_view4* y, void* workspace,
                      int32_t* status, void* stream);
 
+/* Allocation-free variant of sisa_decode_attn (no counterpart in the reference): identical arguments
+ * except that there is no workspace. For callers that cannot allocate device memory when they decode
+ * (inside CUDA-graph capture, hosts without a device allocator, fixed memory budgets). The split-K
+ * partials live in a fixed 4.3 MB array owned by the library on every GPU that loads it; B*H may not
+ * exceed 16384 (SISA_ERR_VALUE otherwise). The first call on a device resolves the array's address and
+ * must precede any stream capture. Calls that overlap on the GPU share the array and race. */
+int sisa_decode_attn_noalloc(const sisa_view4* q, const sisa_view4* c, const float* g_q, const float* f_q,
+                             const sisa_view4* k_cache, const sisa_view4* v_cache, const sisa_view4* b_cache,
+                             const float* g_cache, const float* f_cache, int64_t gf_stride, const float* lam,
+                             int64_t B, int64_t H, int64_t N, int dtype, const sisa_view4* y,
+                             int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -55,6 +55,8 @@ SIGNATURES = {
     "sisa_decode_attn": (_I, [_VP, _VP, _P, _P, _VP, _VP, _VP, _P, _P, _I64, _P, _I64, _I64, _I64, _I, _VP, _P,
                               _P, _P]),
     "sisa_decode_workspace": (_I64, [_I64, _I64, _I64]),
+    "sisa_decode_attn_noalloc": (_I, [_VP, _VP, _P, _P, _VP, _VP, _VP, _P, _P, _I64, _P, _I64, _I64, _I64, _I, _VP,
+                                      _P, _P]),
 }
 
 

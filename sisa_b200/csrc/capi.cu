@@ -142,6 +142,11 @@ int64_t nch64(int64_t L) { return (L + 63) / 64; }
 
 }  // namespace
 
+namespace sisa {
+// Records an error for sisa_last_error() from entry points defined outside this file.
+int capi_fail(int code, const char* msg) { return fail(code, "%s", msg); }
+}  // namespace sisa
+
 extern "C" {
 
 const char* sisa_version(void) { return "sisa_b200 0.1.0 (sm_100a)"; }

@@ -12,6 +12,7 @@
 // of head dimensions (coalesced 128-byte v rows). A second kernel merges the splits' (m, l, acc).
 #include <cuda_runtime.h>
 #include <cstdint>
+#include <mutex>
 
 #include "sm100.cuh"
 #include "decode.h"
@@ -215,3 +216,92 @@ cudaError_t launch_decode(const DecodeParams& p, int dtype, cudaStream_t st) {
 }
 
 }  // namespace sisa
+
+// =============================================================================================
+// Allocation-free decode entry point.
+//
+// Some callers cannot allocate device memory at the moment they decode: code running inside a
+// CUDA-graph capture (allocations cannot be captured, and cudaFree would synchronise the device),
+// hosts that bind only this C ABI and have no device allocator of their own, and serving loops that
+// run under a fixed, pre-reserved memory budget. sisa_decode_attn needs a caller-provided workspace
+// for its split-K partials; this variant keeps those partials in a fixed array that the library
+// owns instead, so the caller passes only inputs and outputs.
+//
+// The array below lives in every GPU that loads this library, from module load until process exit.
+// Its device address is resolved once per device, on the first call made on that device (that
+// first call must therefore come before any stream capture that includes the entry point). All
+// calls on a device share the one array and it keeps the last call's contents: every call rewrites
+// each partial record it reads before reading it, so nothing needs clearing, but two calls that
+// overlap on the GPU (different streams, no ordering between them) race on the array and corrupt
+// each other's results.
+// =============================================================================================
+namespace sisa {
+namespace dec {
+constexpr int64_t kStaticRecords = 16384;        // (split, batch, head) partial records of 66 floats: 4.3 MB
+static __device__ __align__(256) float g_static_partials[kStaticRecords * 66];
+}  // namespace dec
+int capi_fail(int code, const char* msg);
+}  // namespace sisa
+
+extern "C" int sisa_decode_attn_noalloc(const sisa_view4* q, const sisa_view4* c, const float* g_q, const float* f_q,
+                                        const sisa_view4* k_cache, const sisa_view4* v_cache,
+                                        const sisa_view4* b_cache, const float* g_cache, const float* f_cache,
+                                        int64_t gf_stride, const float* lam, int64_t B, int64_t H, int64_t N,
+                                        int dtype, const sisa_view4* y, int32_t* status, void* stream) {
+  using sisa::capi_fail;
+  static std::mutex mu;
+  static void* scratch_by_device[256] = {};
+  if (B < 1 || H < 1 || N < 1) return capi_fail(SISA_ERR_VALUE, "sisa_decode_attn_noalloc: B, H and N must be >= 1");
+  if (B * H > sisa::dec::kStaticRecords)
+    return capi_fail(SISA_ERR_VALUE,
+                     "sisa_decode_attn_noalloc: B*H exceeds the 16384 (batch, head) rows of the library's fixed "
+                     "scratch; use sisa_decode_attn with a caller workspace");
+  if (dtype != SISA_BF16 && dtype != SISA_F16) return capi_fail(SISA_ERR_TYPE, "dtype must be SISA_BF16 or SISA_F16");
+  const sisa_view4* views[6] = {q, c, k_cache, v_cache, b_cache, y};
+  for (const sisa_view4* v : views) {
+    if (!v || !v->data) return capi_fail(SISA_ERR_VALUE, "sisa_decode_attn_noalloc: null view");
+    if ((reinterpret_cast<uintptr_t>(v->data) & 15u) || v->stride_l % 8 || v->stride_h % 8 || v->stride_b % 8)
+      return capi_fail(SISA_ERR_ALIGN, "sisa_decode_attn_noalloc: views need 16-byte rows and strides");
+  }
+  if (!g_q || !g_cache || !lam) return capi_fail(SISA_ERR_VALUE, "sisa_decode_attn_noalloc: null pointer");
+  if ((f_q == nullptr) != (f_cache == nullptr))
+    return capi_fail(SISA_ERR_VALUE, "sisa_decode_attn_noalloc: f_q and f_cache must both be given or both be null");
+  if (gf_stride < N) return capi_fail(SISA_ERR_VALUE, "sisa_decode_attn_noalloc: g/F cache row stride < N");
+  // The scratch is resolved on the device that owns the data, with that device current.
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, q->data) != cudaSuccess || attr.type != cudaMemoryTypeDevice)
+    return capi_fail(SISA_ERR_VALUE, "sisa_decode_attn_noalloc: q is not device memory");
+  if (attr.device < 0 || attr.device >= 256) return capi_fail(SISA_ERR_VALUE, "sisa_decode_attn_noalloc: bad device");
+  if (cudaSetDevice(attr.device) != cudaSuccess) return capi_fail(SISA_ERR_CUDA, "sisa_decode_attn_noalloc: cudaSetDevice failed");
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    scratch = scratch_by_device[attr.device];
+    if (!scratch) {
+      const cudaError_t e = cudaGetSymbolAddress(&scratch, sisa::dec::g_static_partials);
+      if (e != cudaSuccess || !scratch)
+        return capi_fail(SISA_ERR_CUDA, "sisa_decode_attn_noalloc: cudaGetSymbolAddress of the fixed scratch failed");
+      scratch_by_device[attr.device] = scratch;
+    }
+  }
+  sisa::DecodeParams p{};
+  p.q = static_cast<const char*>(q->data); p.q_sb = q->stride_b; p.q_sh = q->stride_h;
+  p.c = static_cast<const char*>(c->data); p.c_sb = c->stride_b; p.c_sh = c->stride_h;
+  p.g_q = g_q; p.f_q = f_q;
+  p.k = static_cast<const char*>(k_cache->data); p.k_sb = k_cache->stride_b; p.k_sh = k_cache->stride_h;
+  p.k_sl = k_cache->stride_l;
+  p.v = static_cast<const char*>(v_cache->data); p.v_sb = v_cache->stride_b; p.v_sh = v_cache->stride_h;
+  p.v_sl = v_cache->stride_l;
+  p.bm = static_cast<const char*>(b_cache->data); p.b_sb = b_cache->stride_b; p.b_sh = b_cache->stride_h;
+  p.b_sl = b_cache->stride_l;
+  p.g = g_cache; p.f = f_cache; p.gf_stride = gf_stride; p.lam = lam;
+  p.y = static_cast<char*>(y->data); p.y_sb = y->stride_b; p.y_sh = y->stride_h;
+  p.ws = static_cast<float*>(scratch);
+  p.B = (int)B; p.H = (int)H; p.N = (int)N;
+  int64_t splits = sisa::decode_splits(B, H, N);
+  const int64_t cap = sisa::dec::kStaticRecords / (B * H);     // >= 1 by the check above
+  p.splits = (int)(splits < cap ? splits : cap);
+  p.status = status;
+  const cudaError_t e = sisa::launch_decode(p, dtype, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : capi_fail(SISA_ERR_CUDA, "sisa_decode_attn_noalloc launch failed");
+}
