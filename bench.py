@@ -137,7 +137,7 @@ class Step:
         self.dy = torch.randn((b, t, h * 64), generator=g, device=dev).to(torch.bfloat16)
         self.c_rot = torch.empty((b, h, t, 32), **bf)
         self.b_rot = torch.empty((b, h, t, 32), **bf)
-        self.pos = torch.empty((b, h, t, 4), **f32)
+        self.pos = _lib.pos_planes(b, h, t, dev)
         self.tot = torch.empty(self.lib.sisa_prep_fwd_workspace(b, h, t), dtype=torch.uint8, device=dev)
         self.o = torch.empty_strided((b, h, t, 64), (t * h * 64, 64, h * 64, 1), **bf)
         self.lse = torch.empty((b, h, t), **f32)

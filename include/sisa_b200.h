@@ -57,6 +57,10 @@ int sisa_device_check(int device);
  * Replaces sisa.kernels.fused_prep.fused_layout (src/sisa/kernels/fused_prep.py:71-96). */
 int sisa_fused_layout(int64_t n_head, int64_t* out9);
 
+/* Row length Lp of the position planes: L rounded up to a multiple of 4, so that every plane starts
+ * on a 16-byte boundary (the tensor-memory-access loads need 16-byte strides). */
+int64_t sisa_pos_len(int64_t L);
+
 /* Workspace sizes in bytes for the entry points below (caller allocates; 256-byte aligned). */
 int64_t sisa_prep_fwd_workspace(int64_t B, int64_t H, int64_t L);   /* block totals, fp32 */
 int64_t sisa_prep_bwd_workspace(int64_t B, int64_t H, int64_t L);   /* block totals, fp64 */
@@ -68,8 +72,10 @@ int64_t sisa_attn_bwd_workspace(int64_t B, int64_t H, int64_t L);   /* per-row s
  * proj: (B, L, NPAD) in `dtype` with element strides proj_sb, proj_sl (column stride 1).
  * z: (B, L, H) fp32 with strides z_sb, z_sl (head stride 1), or NULL for no forget gate.
  * c_rot, b_rot: (B, H, L, 32) contiguous, `dtype`.
- * pos: (B, H, L, 4) fp32 contiguous, per position {g, F, rowf, colf} where rowf/colf are the
- *   decay factors relative to the start/end of the position's 64-row block.
+ * pos: (B, H, 4, Lp) fp32 contiguous planes, Lp = sisa_pos_len(L): plane 0 g, plane 1 F, plane 2 rowf,
+ *   plane 3 colf, where rowf/colf are the decay factors relative to the start/end of the position's
+ *   64-row block. Entries [L, Lp) of each plane are not written. (The reference keeps g and F as
+ *   separate (B, H, L) tensors; one planar record lets one bulk copy fetch all four per key tile.)
  * workspace: sisa_prep_fwd_workspace(B, H, L) bytes. */
 int sisa_prep_fwd(const void* proj, int64_t B, int64_t L, int64_t H, int64_t proj_sb, int64_t proj_sl,
                   int dtype, const float* z, int64_t z_sb, int64_t z_sl,
@@ -77,8 +83,9 @@ int sisa_prep_fwd(const void* proj, int64_t B, int64_t L, int64_t H, int64_t pro
                   int32_t* status, void* stream);
 
 /* Position records for the unfused entry point (src/sisa/kernels/attention.py:129-153):
- * pos = {g, fgate (0 if NULL), rowf, colf} from g (B, H, L) and fgate (B, H, L) fp32 with the
- * given element strides; sets SISA_ST_NONMONOTONE when g rises by more than 1e-3. */
+ * pos planes {g, fgate (0 if NULL), rowf, colf}, (B, H, 4, Lp) as above, from g (B, H, L) and
+ * fgate (B, H, L) fp32 with the given element strides; sets SISA_ST_NONMONOTONE when g rises by
+ * more than 1e-3. */
 int sisa_pack_positions(const float* g, int64_t g_sb, int64_t g_sh, int64_t g_sl,
                         const float* fgate, int64_t f_sb, int64_t f_sh, int64_t f_sl,
                         int64_t B, int64_t H, int64_t L, float* pos, int32_t* status, void* stream);
@@ -86,7 +93,7 @@ int sisa_pack_positions(const float* g, int64_t g_sb, int64_t g_sh, int64_t g_sl
 /* Exact SISA attention forward on tcgen05 (src/sisa/kernels/attention.py:177-296, host 686-727):
  *   s_ij = q_i.k_j/8 + lam_h exp(g_i-g_j) (c_i.b_j) + (F_i - F_j), j <= i;  o = softmax(s) v.
  * q, k, v: (B, H, L, 64) views in `dtype`; c, b: (B, H, L, 32) views in `dtype`.
- * pos: (B, H, L, 4) from sisa_prep_fwd / sisa_pack_positions. lam: (H,) fp32.
+ * pos: (B, H, 4, Lp) planes from sisa_prep_fwd / sisa_pack_positions. lam: (H,) fp32.
  * o: (B, H, L, 64) view in `dtype`. lse: (B, H, L) fp32 contiguous, log2 units.
  * o32: (B, H, L, 64) fp32 contiguous self-normalised output for the exact-delta backward,
  *   or NULL when no backward follows. All views: 16-byte aligned rows, strides multiple of 8. */

@@ -42,6 +42,7 @@ SIGNATURES = {
     "sisa_prep_fwd_workspace": (_I64, [_I64, _I64, _I64]),
     "sisa_prep_bwd_workspace": (_I64, [_I64, _I64, _I64]),
     "sisa_attn_bwd_workspace": (_I64, [_I64, _I64, _I64]),
+    "sisa_pos_len": (_I64, [_I64]),
     "sisa_prep_fwd": (_I, [_P, _I64, _I64, _I64, _I64, _I64, _I, _P, _I64, _I64, _P, _P, _P, _P, _P, _P]),
     "sisa_pack_positions": (_I, [_P, _I64, _I64, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64, _P, _P, _P]),
     "sisa_attn_fwd": (_I, [_VP, _VP, _VP, _VP, _VP, _P, _P, _I64, _I64, _I64, _I, _VP, _P, _P, _P, _P]),
@@ -88,6 +89,19 @@ def load():
 def exported_symbols() -> list[str]:
     lib = load()
     return [n for n in SIGNATURES if hasattr(lib, n)]
+
+
+def pos_planes(B: int, H: int, L: int, device) -> "torch.Tensor":
+    """Allocate the planar position records (B, H, 4, Lp) fp32 that sisa_prep_fwd / sisa_pack_positions
+    fill (planes g, F, rowf, colf; Lp = sisa_pos_len(L))."""
+    import torch
+
+    return torch.empty((B, H, 4, load().sisa_pos_len(L)), device=device, dtype=torch.float32)
+
+
+def pos_records(pos, L: int):
+    """(B, H, L, 4) view {g, F, rowf, colf} of planar position records."""
+    return pos[..., :L].transpose(-1, -2)
 
 
 def last_error() -> str:

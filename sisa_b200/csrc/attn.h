@@ -12,14 +12,14 @@ struct FwdParams {
   CUtensorMap tm_v;    // box (64, 64)
   CUtensorMap tm_c;    // (32, L, H, B), box (32, 128), 64B swizzle
   CUtensorMap tm_b;    // box (32, 64)
-  CUtensorMap tm_pos;  // (4, L, B*H) fp32, box (4, 64, 1)
-  const float4* pos;
+  CUtensorMap tm_pos;  // (L, 4, B*H) fp32 planes, box (64, 4, 1)
+  const float* pos;    // (B*H, 4, Lp) planes {g, F, rowf, colf}
   const float* lam;
   char* o;
   int64_t o_sb, o_sh, o_sl;
   float* lse;
   float* o32;
-  int B, H, L, ntq;
+  int B, H, L, Lp, ntq;
   int32_t* status;
 };
 
@@ -28,9 +28,9 @@ struct BwdParams {
   CUtensorMap tm_q128, tm_do128, tm_c128, tm_k64, tm_v64, tm_b64;
   // dkv kernel (key-tile owner): K, V, B resident (box rows 128); Q, dO, C streamed (box rows 64)
   CUtensorMap tm_k128, tm_v128, tm_b128, tm_q64, tm_do64, tm_c64;
-  CUtensorMap tm_pos;    // (4, L, B*H) fp32, box (4, 64, 1)
-  CUtensorMap tm_rstat;  // (4, L, B*H) fp32, box (4, 64, 1): {lse, delta, T-delta, dS_tt}
-  const float4* pos;
+  CUtensorMap tm_pos;    // (L, 4, B*H) fp32 planes, box (64, 4, 1)
+  CUtensorMap tm_rstat;  // (L, 4, B*H) fp32 planes, box (64, 4, 1)
+  const float* pos;      // (B*H, 4, Lp) planes {g, F, rowf, colf}
   const float* lam;
   const char* q;  int64_t q_sb, q_sh, q_sl;
   const char* k;  int64_t k_sb, k_sh, k_sl;
@@ -46,12 +46,12 @@ struct BwdParams {
   float* db; int64_t db_sb, db_sh, db_sl;
   float* dg;
   float* dF;
-  float4* rstat;   // (B*H, L)
+  float* rstat;    // (B*H, 4, Lp) planes {F log2e - lse, -delta, -(T^ - delta), dS_tt} per query row
   float* rg;       // (B*H, L) row part of dg (times lambda)
   float* rf;       // row part of dF
   float* rl;       // per-row dlambda
   float* dlam;
-  int B, H, L, ntq128, ntq64;
+  int B, H, L, Lp, ntq128, ntq64;
   int has_f;
   int32_t* status;
 };

@@ -15,10 +15,20 @@
 //    dC, so the Phi_i - Phi_j cancellation of d theta holds), and the dq kernel's dS_tt on the diagonal.
 //
 // Both kernels: 16 compute warps (four warpgroups splitting each tile's 64 columns 16/16/16/16; thread =
-// TMEM lane = owned row, four compute warps per SM sub-partition), one TMA producer warp and one UMMA warp. Per tile the compute warps pull
-// S, U, dP into registers and release TMEM at once, so the next tile's GEMMs overlap their math;
-// the gradient GEMMs read the bf16 operands (dS, P^T, ...) the compute warps stored into tensor
-// memory (A from TMEM), so the tensor core fetches only the B tiles from shared memory.
+// TMEM lane = owned row, four compute warps per SM sub-partition), one TMA producer warp and two UMMA
+// warps. Per tile the compute warps pull S, U, dP into registers and release TMEM at once, so the next
+// tile's GEMMs overlap their math; the gradient GEMMs read the bf16 operands (dS, P^T, ...) the compute
+// warps stored into tensor memory (A from TMEM), so the tensor core fetches only the B tiles from
+// shared memory.
+//
+// UMMA issue is split over two single-thread issuers on different SM sub-partitions: one issues the
+// score GEMMs (S, U, dP) and waits only on the stage-full and scores-consumed barriers, the other
+// issues the gradient GEMMs and waits only on the operands-full barrier. An mbarrier wait costs the
+// issuing thread some 150 cycles even when the phase has already completed, and a compute warp that can
+// issue every cycle starves a same-sub-partition issuer several-fold, so one issuer doing both chains
+// serialises ~6 waits per tile; two issuers keep the tensor pipe fed while either one waits. A tile's
+// score GEMMs have completed before its operands exist, so the gradient issuer's commit alone releases
+// the stage.
 #include <cuda_runtime.h>
 
 #include "attn_common.cuh"
@@ -31,8 +41,8 @@ constexpr int NST = 3;
 constexpr int NWG = 4;           // compute warpgroups; each owns 64 / NWG columns of every tile
 constexpr int NCOL = 64 / NWG;   // 16
 constexpr int NCW = 4 * NWG;     // compute warps
-constexpr int NTHREADS = 32 * NCW + 64;    // + one TMA warp + one UMMA warp
-constexpr int WARP_TMA = NCW, WARP_MMA = NCW + 1;
+constexpr int NTHREADS = 32 * NCW + 96;    // + one TMA warp + two UMMA issuer warps
+constexpr int WARP_TMA = NCW, WARP_MMA = NCW + 1, WARP_GRAD = NCW + 2;   // sub-partitions 0, 1, 2
 constexpr int NCT = 32 * NCW;    // compute threads
 
 // ----------------------------------------------------------------------------- dq kernel layout
@@ -58,12 +68,17 @@ constexpr uint32_t SZ_Q = 64 * 128, SZ_DO = 64 * 128, SZ_C = 64 * 64, SZ_POS = 6
 constexpr uint32_t SZ_STAGE = SZ_Q + SZ_DO + SZ_C + SZ_POS + SZ_RST;   // 22528
 constexpr uint32_t OFF_K = 0, OFF_V = OFF_K + SZ_K, OFF_B = OFF_V + SZ_V, OFF_ST = OFF_B + SZ_B;
 constexpr uint32_t OFF_RED = OFF_ST + NST * SZ_STAGE;                  // 128 rows x NWG x 2 floats
-constexpr uint32_t OFF_BAR = OFF_RED + 128 * NWG * 2 * 4;
+constexpr uint32_t SZ_DSB = 128 * 128;                                 // (dS^' rq)^T operand: 128 keys x 64 queries
+constexpr uint32_t OFF_DSB = OFF_RED + 128 * NWG * 2 * 4;              // two buffers, K-major, 128-byte swizzle
+constexpr uint32_t OFF_BAR = OFF_DSB + 2 * SZ_DSB;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
-// TMEM: S^T, U^T, dP^T per tile; dV, dK, dB_diag, dB_off accumulators; the bf16 operands P^T, dS^T,
-// (dS^' rq)^T (one buffer of 3 x 32 columns, A operands read from TMEM)
+// TMEM: S^T, U^T, dP^T per tile; dV, dK, dB_diag, dB_off accumulators; the bf16 operands P^T and dS^T
+// (two buffers of 2 x 32 columns, A operands read from TMEM). The third operand, (dS^' rq)^T, goes
+// through shared memory (two buffers), so the compute warps store tile n while the gradient UMMAs of
+// tile n-1 still read theirs.
 constexpr int COL_S = 0, COL_U = 64, COL_DP = 128, COL_DV = 192, COL_DK = 256, COL_DBD = 320, COL_DBO = 352,
               COL_OPS = 384;
+static_assert(OFF_DSB % 1024 == 0, "swizzled operand tiles need 1024-byte alignment");
 constexpr int B_KVF = 0, B_KVE = 3, B_K = 6, B_SUF = 7, B_SUE = 8, B_OPF = 9, B_OPE = 11, B_ACC = 13;
 static_assert(OFF_ST % 1024 == 0 && SZ_STAGE % 1024 == 0, "alignment");
 }  // namespace dkv
@@ -136,38 +151,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
         tma_load_4d(st, &p.tm_k64, BAR(B_KVF + s), 0, j0, h, b);
         tma_load_4d(st + SZ_K, &p.tm_v64, BAR(B_KVF + s), 0, j0, h, b);
         tma_load_4d(st + SZ_K + SZ_V, &p.tm_b64, BAR(B_KVF + s), 0, j0, h, b);
-        tma_load_3d(st + SZ_K + SZ_V + SZ_B, &p.tm_pos, BAR(B_KVF + s), 0, j0, bh);
+        tma_load_3d(st + SZ_K + SZ_V + SZ_B, &p.tm_pos, BAR(B_KVF + s), j0, 0, bh);
       }
     }
   } else if (warp == WARP_MMA) {
+    // score GEMMs S = Q K^T, U = C B~^T, dP = dO V^T of every key tile
     if (lane == 0) {
       constexpr uint32_t fmt = kHalf ? 0 : 1;
       constexpr uint32_t id_s = make_idesc(128, 64, fmt, 0, 0);
-      constexpr uint32_t id_dq = make_idesc(128, 64, fmt, 0, 1);
-      constexpr uint32_t id_dc = make_idesc(128, 32, fmt, 0, 1);
       const uint32_t sQ = sbase + OFF_Q, sDO = sbase + OFF_DO, sC = sbase + OFF_C;
       bool ok = mbar_wait(BAR(B_Q), 0, p.status);
-      int ndco = 0, ndcd = 0;   // GEMMs issued into dC_off / dC_diag so far
-      auto issue_grads = [&](int m) -> bool {
-        const int buf = m & 1, s = m % NST;
-        if (!mbar_wait(BAR(B_OPF + buf), (m >> 1) & 1, p.status)) return false;
-        tc_fence_after();
-        const uint32_t tDS = tbase + COL_OPS + (uint32_t)buf * 64, tDSC = tDS + 32;
-        const uint32_t st = stage_addr(s);
-        const bool dg = m < ndiag;
-        const uint32_t tdc = tbase + (dg ? COL_DCD : COL_DCO);
-        int& cnt = dg ? ndcd : ndco;
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          umma_ts(tbase + COL_DQ, tDS + k * 8, desc_mn128(st + k * 2048), id_dq, (m > 0 || k > 0));
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          umma_ts(tdc, tDSC + k * 8, desc_mn64(st + SZ_K + SZ_V + k * 1024), id_dc, (cnt > 0 || k > 0));
-        ++cnt;
-        umma_commit(BAR(B_OPE + buf));
-        umma_commit(BAR(B_KVE + s));
-        return true;
-      };
       for (int n = 0; ok && n < ntiles; ++n) {
         const int s = n % NST;
         if (!mbar_wait(BAR(B_KVF + s), (n / NST) & 1, p.status)) { ok = false; break; }
@@ -183,9 +176,34 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
         for (int k = 0; k < 4; ++k)
           umma_ss(tbase + COL_DP, desc_k128(sDO + k * 32), desc_k128(st + SZ_K + k * 32), id_s, k > 0);
         umma_commit(BAR(B_SUF));
-        if (n > 0 && !issue_grads(n - 1)) { ok = false; break; }
       }
-      if (ok) issue_grads(ntiles - 1);
+    }
+  } else if (warp == WARP_GRAD) {
+    // gradient GEMMs dQ += dS^ K, dC += (dS^ colf mid) B~ from the operands in TMEM; releases the stage
+    if (lane == 0) {
+      constexpr uint32_t fmt = kHalf ? 0 : 1;
+      constexpr uint32_t id_dq = make_idesc(128, 64, fmt, 0, 1);
+      constexpr uint32_t id_dc = make_idesc(128, 32, fmt, 0, 1);
+      int ndco = 0, ndcd = 0;   // GEMMs issued into dC_off / dC_diag so far
+      for (int m = 0; m < ntiles; ++m) {
+        const int buf = m & 1, s = m % NST;
+        if (!mbar_wait(BAR(B_OPF + buf), (m >> 1) & 1, p.status)) break;
+        tc_fence_after();
+        const uint32_t tDS = tbase + COL_OPS + (uint32_t)buf * 64, tDSC = tDS + 32;
+        const uint32_t st = stage_addr(s);
+        const bool dg = m < ndiag;
+        const uint32_t tdc = tbase + (dg ? COL_DCD : COL_DCO);
+        int& cnt = dg ? ndcd : ndco;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_ts(tbase + COL_DQ, tDS + k * 8, desc_mn128(st + k * 2048), id_dq, (m > 0 || k > 0));
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          umma_ts(tdc, tDSC + k * 8, desc_mn64(st + SZ_K + SZ_V + k * 1024), id_dc, (cnt > 0 || k > 0));
+        ++cnt;
+        umma_commit(BAR(B_OPE + buf));
+        umma_commit(BAR(B_KVE + s));
+      }
       // The accumulator of a region that received no GEMM is never read (see the epilogue).
       umma_commit(BAR(B_ACC));
     }
@@ -196,9 +214,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
     const int row = m0 + r;
     const bool vrow = row < L;
     const int64_t rb = (int64_t)bh * L;
-    const float4 pi = p.pos[rb + (vrow ? row : L - 1)];
-    const float gi = pi.x, fi = pi.y;
-    const float ga = p.pos[rb + m0].x;
+    const float* posbh = p.pos + (int64_t)bh * 4 * p.Lp;   // planes g, F, rowf, colf
+    const int rr = vrow ? row : L - 1;
+    const float gi = posbh[rr], fi = posbh[p.Lp + rr];
+    const float ga = posbh[m0];
     const float lam = p.lam[h];
     const float rowf = exp2f(fminf((gi - ga) * kLOG2E, 0.f));
     const float rs = lam * rowf;
@@ -253,8 +272,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
     const uint32_t tU = tmem_addr(tbase, quarter, COL_U + wg * NCOL);
     const uint32_t tP = tmem_addr(tbase, quarter, COL_DP + wg * NCOL);
     float za = 0.f, ya = 0.f, wa = 0.f, xa = 0.f, ptt = 0.f, dptt = 0.f, xd = 0.f;
-    const float2 c1v = bcast2(c1), l2e = bcast2(kLOG2E), fi2 = bcast2(fi), neg1 = bcast2(-1.f);
-    const float2 nlse2 = bcast2(-lse), ndl2 = bcast2(-dl), rs2v = bcast2(rs2);
+    // (F_i - F_j) log2e - lse = fma(F_j, -log2e, F_i log2e - lse): one packed FMA per column pair
+    const float filse = fi * kLOG2E - lse;
+    const float2 c1v = bcast2(c1), nl2e = bcast2(-kLOG2E), filse2 = bcast2(filse);
+    const float2 ndl2 = bcast2(-dl), rs2v = bcast2(rs2);
     float2 xo2 = bcast2(0.f), yo2 = bcast2(0.f), za2 = bcast2(0.f), wa2 = bcast2(0.f);
     for (int n = 0; ok && n < ntiles; ++n) {
       const int s = n % NST;
@@ -268,22 +289,28 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(BAR(B_SUE));
-      const float4* cpos = reinterpret_cast<const float4*>(gbase + OFF_ST + s * SZ_STAGE + SZ_K + SZ_V + SZ_B) + wg * NCOL;
+      // key position planes of this tile ([4][64] floats {g, F, rowf, colf}), this warpgroup's columns
+      const float* kpos = reinterpret_cast<const float*>(gbase + OFF_ST + s * SZ_STAGE + SZ_K + SZ_V + SZ_B);
+      const float4* kg4 = reinterpret_cast<const float4*>(kpos + wg * NCOL);
+      const float4* kf4 = reinterpret_cast<const float4*>(kpos + 64 + wg * NCOL);
+      const float4* kc4 = reinterpret_cast<const float4*>(kpos + 192 + wg * NCOL);
       uint32_t wds[NCOL / 2], wdc[NCOL / 2];
       if (n < ndiag) {
 #pragma unroll
         for (int c = 0; c < NCOL; c += 2) {
+          const float4 g4 = kg4[c / 4], f4 = kf4[c / 4];
           float dsv[2], dcv[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const int cc = c + e;
-            const float4 pj = cpos[cc];
+            const float gj = (c & 2) ? (e ? g4.w : g4.z) : (e ? g4.y : g4.x);
+            const float fj = (c & 2) ? (e ? f4.w : f4.z) : (e ? f4.y : f4.x);
             const int j = j0 + cc;
             const bool valid = (j <= row) && (j < L);
-            const float dec = valid ? exp2f(fminf((gi - pj.x) * kLOG2E, 0.f)) : 0.f;
+            const float dec = valid ? exp2f(fminf((gi - gj) * kLOG2E, 0.f)) : 0.f;
             const float u = dec * uv[cc];
-            const float x = fmaf(sv[cc], c1, fmaf(fi - pj.y, kLOG2E, lam2 * u));
-            const float pr = valid ? ex2_approx(x - lse) : 0.f;
+            const float x = fmaf(sv[cc], c1, fmaf(fj, -kLOG2E, fmaf(lam2, u, filse)));   // x - lse (log2)
+            const float pr = valid ? ex2_approx(x) : 0.f;
             const float ds = pr * (pv[cc] - dl);
             const bool eye = (j == row);
             const float dso = eye ? 0.f : ds;
@@ -300,15 +327,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
           wdc[c / 2] = pack2<kHalf>(dcv[0], dcv[1]);
         }
       } else {
-        const float ge = reinterpret_cast<const float4*>(gbase + OFF_ST + s * SZ_STAGE + SZ_K + SZ_V + SZ_B)[63].x;
+        const float ge = kpos[63];
         const float2 mid2 = bcast2(exp2f(fminf((ga - ge) * kLOG2E, 0.f)));
 #pragma unroll
         for (int c = 0; c < NCOL; c += 2) {
-          const float4 pa = cpos[c], pb = cpos[c + 1];
-          const float2 cf = mul2(make_float2(pa.w, pb.w), mid2);                  // colf mid
+          const float4 f4 = kf4[c / 4], c4 = kc4[c / 4];
+          const float2 fj = (c & 2) ? make_float2(f4.z, f4.w) : make_float2(f4.x, f4.y);
+          const float2 cj = (c & 2) ? make_float2(c4.z, c4.w) : make_float2(c4.x, c4.y);
+          const float2 cf = mul2(cj, mid2);                                         // colf mid
           const float2 uc = mul2(make_float2(uv[c], uv[c + 1]), cf);
-          const float2 t = fma2(make_float2(pa.y, pb.y), neg1, fi2);              // F_i - F_j
-          const float2 y = fma2(uc, rs2v, fma2(t, l2e, nlse2));
+          const float2 y = fma2(uc, rs2v, fma2(fj, nl2e, filse2));
           const float2 x = fma2(make_float2(sv[c], sv[c + 1]), c1v, y);          // x - lse (log2)
           const float2 pr = make_float2(ex2_approx(x.x), ex2_approx(x.y));
           const float2 ds = mul2(pr, add2(make_float2(pv[c], pv[c + 1]), ndl2));  // P (dP - delta'')
@@ -356,7 +384,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
       if (ok) {
         tc_fence_after();
         if (vrow) {
-          p.rstat[rb + row] = make_float4(-lse, -dl, -dd, dstt);   // negated: the dkv kernel adds them
+          // the dkv kernel's per-query records: F log2e - lse, and the negated delta terms it adds
+          float* rst = p.rstat + (int64_t)bh * 4 * p.Lp + row;
+          rst[0] = filse;
+          rst[p.Lp] = -dl;
+          rst[2 * p.Lp] = -dd;
+          rst[3 * p.Lp] = dstt;
           p.rl[rb + row] = dl_row + dstt * xd;
           p.rg[rb + row] = lam * dl_row;
           p.rf[rb + row] = wa - za * dd;
@@ -479,42 +512,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
         tma_load_4d(st, &p.tm_q64, BAR(B_KVF + s), 0, m0, h, b);
         tma_load_4d(st + SZ_Q, &p.tm_do64, BAR(B_KVF + s), 0, m0, h, b);
         tma_load_4d(st + SZ_Q + SZ_DO, &p.tm_c64, BAR(B_KVF + s), 0, m0, h, b);
-        tma_load_3d(st + SZ_Q + SZ_DO + SZ_C, &p.tm_pos, BAR(B_KVF + s), 0, m0, bh);
-        tma_load_3d(st + SZ_Q + SZ_DO + SZ_C + SZ_POS, &p.tm_rstat, BAR(B_KVF + s), 0, m0, bh);
+        tma_load_3d(st + SZ_Q + SZ_DO + SZ_C, &p.tm_pos, BAR(B_KVF + s), m0, 0, bh);
+        tma_load_3d(st + SZ_Q + SZ_DO + SZ_C + SZ_POS, &p.tm_rstat, BAR(B_KVF + s), m0, 0, bh);
       }
     }
   } else if (warp == WARP_MMA) {
+    // score GEMMs S^T = K Q^T, U^T = B~ C^T, dP^T = V dO^T of every query tile
     if (lane == 0) {
       constexpr uint32_t fmt = kHalf ? 0 : 1;
       constexpr uint32_t id_s = make_idesc(128, 64, fmt, 0, 0);
-      constexpr uint32_t id_mn64 = make_idesc(128, 64, fmt, 0, 1);
-      constexpr uint32_t id_mn32 = make_idesc(128, 32, fmt, 0, 1);
       const uint32_t sK = sbase + OFF_K, sV = sbase + OFF_V, sB = sbase + OFF_B;
       bool ok = mbar_wait(BAR(B_K), 0, p.status);
-      int nbo = 0, nbd = 0;
-      auto issue_grads = [&](int m) -> bool {
-        const int buf = m & 1, s = m % NST;
-        if (!mbar_wait(BAR(B_OPF + buf), (m >> 1) & 1, p.status)) return false;
-        tc_fence_after();
-        const uint32_t tPT = tbase + COL_OPS, tDST = tPT + 32, tDSB = tPT + 64;
-        const uint32_t st = stage_addr(s);
-        const bool dg = m < ndiag;
-        int& cnt = dg ? nbd : nbo;
-        const uint32_t tdb = tbase + (dg ? COL_DBD : COL_DBO);
-#pragma unroll
-        for (int k = 0; k < 4; ++k)   // dV += P^T dO
-          umma_ts(tbase + COL_DV, tPT + k * 8, desc_mn128(st + SZ_Q + k * 2048), id_mn64, (m > 0 || k > 0));
-#pragma unroll
-        for (int k = 0; k < 4; ++k)   // dK += dS^T Q
-          umma_ts(tbase + COL_DK, tDST + k * 8, desc_mn128(st + k * 2048), id_mn64, (m > 0 || k > 0));
-#pragma unroll
-        for (int k = 0; k < 4; ++k)   // dB += dSb^T C
-          umma_ts(tdb, tDSB + k * 8, desc_mn64(st + SZ_Q + SZ_DO + k * 1024), id_mn32, (cnt > 0 || k > 0));
-        ++cnt;
-        umma_commit(BAR(B_OPE + buf));
-        umma_commit(BAR(B_KVE + s));
-        return true;
-      };
       for (int n = 0; ok && n < ntiles; ++n) {
         const int s = n % NST;
         if (!mbar_wait(BAR(B_KVF + s), (n / NST) & 1, p.status)) { ok = false; break; }
@@ -530,9 +538,38 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
         for (int k = 0; k < 4; ++k)
           umma_ss(tbase + COL_DP, desc_k128(sV + k * 32), desc_k128(st + SZ_Q + k * 32), id_s, k > 0);
         umma_commit(BAR(B_SUF));
-        if (n > 0 && !issue_grads(n - 1)) { ok = false; break; }
       }
-      if (ok) issue_grads(ntiles - 1);
+    }
+  } else if (warp == WARP_GRAD) {
+    // gradient GEMMs dV += P^T dO, dK += dS^T Q, dB += dSb^T C from the operands in TMEM; releases the stage
+    if (lane == 0) {
+      constexpr uint32_t fmt = kHalf ? 0 : 1;
+      constexpr uint32_t id_mn64 = make_idesc(128, 64, fmt, 0, 1);
+      constexpr uint32_t id_mn32 = make_idesc(128, 32, fmt, 0, 1);
+      int nbo = 0, nbd = 0;
+      for (int m = 0; m < ntiles; ++m) {
+        const int buf = m & 1, s = m % NST;
+        if (!mbar_wait(BAR(B_OPF + buf), (m >> 1) & 1, p.status)) break;
+        tc_fence_after();
+        const uint32_t tPT = tbase + COL_OPS + (uint32_t)buf * 64, tDST = tPT + 32;
+        const uint32_t sDSB = sbase + OFF_DSB + (uint32_t)buf * SZ_DSB;
+        const uint32_t st = stage_addr(s);
+        const bool dg = m < ndiag;
+        int& cnt = dg ? nbd : nbo;
+        const uint32_t tdb = tbase + (dg ? COL_DBD : COL_DBO);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)   // dV += P^T dO
+          umma_ts(tbase + COL_DV, tPT + k * 8, desc_mn128(st + SZ_Q + k * 2048), id_mn64, (m > 0 || k > 0));
+#pragma unroll
+        for (int k = 0; k < 4; ++k)   // dK += dS^T Q
+          umma_ts(tbase + COL_DK, tDST + k * 8, desc_mn128(st + k * 2048), id_mn64, (m > 0 || k > 0));
+#pragma unroll
+        for (int k = 0; k < 4; ++k)   // dB += dSb^T C
+          umma_ss(tdb, desc_k128(sDSB + k * 32), desc_mn64(st + SZ_Q + SZ_DO + k * 1024), id_mn32, (cnt > 0 || k > 0));
+        ++cnt;
+        umma_commit(BAR(B_OPE + buf));
+        umma_commit(BAR(B_KVE + s));
+      }
       umma_commit(BAR(B_ACC));
     }
   } else {
@@ -541,22 +578,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
     const int j = n0 + r;                                // owned key row
     const bool vcol = j < L;
     const int64_t rb = (int64_t)bh * L;
-    const float4 pjv = p.pos[rb + (vcol ? j : L - 1)];
-    const float gj = pjv.x, fj = pjv.y;
-    const float ge = p.pos[rb + min(n0 + 127, L - 1)].x;
+    const float* posbh = p.pos + (int64_t)bh * 4 * p.Lp;   // planes g, F, rowf, colf
+    const int jj = vcol ? j : L - 1;
+    const float gj = posbh[jj], fj = posbh[p.Lp + jj];
+    const float ge = posbh[min(n0 + 127, L - 1)];
     const float lam = p.lam[h];
     const float colf = exp2f(fminf((ge - gj) * kLOG2E, 0.f));     // 128-row key-tile anchor
     const float rk = lam * colf;
     const float rk2 = rk * kLOG2E;
     const float lam2 = lam * kLOG2E;
     const float c1 = kScale * kLOG2E;
-    const float dstt_j = vcol ? p.rstat[rb + j].w : 0.f;
+    const float dstt_j = vcol ? p.rstat[(int64_t)bh * 4 * p.Lp + 3 * p.Lp + j] : 0.f;
     float* red = reinterpret_cast<float*>(gbase + OFF_RED);
     const uint32_t tS = tmem_addr(tbase, quarter, COL_S + wg * NCOL);
     const uint32_t tU = tmem_addr(tbase, quarter, COL_U + wg * NCOL);
     const uint32_t tP = tmem_addr(tbase, quarter, COL_DP + wg * NCOL);
     float dgu = 0.f, dfs = 0.f;
-    const float2 c1v = bcast2(c1), l2e = bcast2(kLOG2E), nfj2 = bcast2(-fj), rk2v = bcast2(rk2);
+    const float nfjl = -fj * kLOG2E;                              // x - lse_i = ... + (F_i log2e - lse_i) - F_j log2e
+    const float2 c1v = bcast2(c1), nfjl2 = bcast2(nfjl), rk2v = bcast2(rk2);
     float2 dgo2 = bcast2(0.f), dfs2 = bcast2(0.f);
     bool ok = true;
     for (int n = 0; ok && n < ntiles; ++n) {
@@ -572,28 +611,39 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
       tc_fence_before();
       mbar_arrive(BAR(B_SUE));
       const uint8_t* st = gbase + OFF_ST + s * SZ_STAGE;
-      const float4* cpos = reinterpret_cast<const float4*>(st + SZ_Q + SZ_DO + SZ_C) + wg * NCOL;
-      const float4* crst = reinterpret_cast<const float4*>(st + SZ_Q + SZ_DO + SZ_C + SZ_POS) + wg * NCOL;
+      // query position planes {g, F, rowf, colf} and row-statistic planes {F log2e - lse, -delta,
+      // -(T^ - delta), dS_tt} of this tile ([4][64] floats each), this warpgroup's columns
+      const float* qpos = reinterpret_cast<const float*>(st + SZ_Q + SZ_DO + SZ_C);
+      const float* qrst = reinterpret_cast<const float*>(st + SZ_Q + SZ_DO + SZ_C + SZ_POS);
+      const float4* qg4 = reinterpret_cast<const float4*>(qpos + wg * NCOL);
+      const float4* qr4 = reinterpret_cast<const float4*>(qpos + 128 + wg * NCOL);
+      const float4* qG4 = reinterpret_cast<const float4*>(qrst + wg * NCOL);
+      const float4* qD4 = reinterpret_cast<const float4*>(qrst + 64 + wg * NCOL);
+      const float4* qT4 = reinterpret_cast<const float4*>(qrst + 128 + wg * NCOL);
       uint32_t wp[NCOL / 2], wk[NCOL / 2], wb[NCOL / 2];
       if (n < ndiag) {
 #pragma unroll
         for (int c = 0; c < NCOL; c += 2) {
+          const float4 g4 = qg4[c / 4], G4 = qG4[c / 4], D4 = qD4[c / 4], T4 = qT4[c / 4];
           float pe[2], ke[2], be[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const int cc = c + e;
             const int i = i0 + cc;
-            const float4 pi = cpos[cc];
-            const float4 ri = crst[cc];
+            const int sel = (c & 2) + e;
+            const float gi = sel == 0 ? g4.x : sel == 1 ? g4.y : sel == 2 ? g4.z : g4.w;
+            const float Gi = sel == 0 ? G4.x : sel == 1 ? G4.y : sel == 2 ? G4.z : G4.w;
+            const float nDi = sel == 0 ? D4.x : sel == 1 ? D4.y : sel == 2 ? D4.z : D4.w;
+            const float nTi = sel == 0 ? T4.x : sel == 1 ? T4.y : sel == 2 ? T4.z : T4.w;
             const bool valid = (i >= j) && (i < L);
             const bool strict = valid && (i > j);
             const bool eye = valid && (i == j);
-            const float dec = valid ? exp2f(fminf((pi.x - gj) * kLOG2E, 0.f)) : 0.f;
+            const float dec = valid ? exp2f(fminf((gi - gj) * kLOG2E, 0.f)) : 0.f;
             const float u = dec * uv[cc];
-            const float x = fmaf(sv[cc], c1, fmaf(pi.y - fj, kLOG2E, lam2 * u));
-            const float pr = valid ? ex2_approx(x + ri.x) : 0.f;   // ri = {-lse, -delta, -(T^-delta), dS_tt}
-            const float dsh = pr * (pv[cc] + ri.y);
-            const float dsx = fmaf(pr, ri.z, dsh);
+            const float x = fmaf(sv[cc], c1, fmaf(lam2, u, Gi + nfjl));   // x - lse_i (log2)
+            const float pr = valid ? ex2_approx(x) : 0.f;
+            const float dsh = pr * (pv[cc] + nDi);
+            const float dsx = fmaf(pr, nTi, dsh);
             const float dso = strict ? dsx : 0.f;
             dgu = fmaf(dso, u, dgu);
             dfs += dso;
@@ -606,25 +656,28 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
           wb[c / 2] = pack2<kHalf>(be[0], be[1]);
         }
       } else {
-        const float gs = reinterpret_cast<const float4*>(st + SZ_Q + SZ_DO + SZ_C)[0].x;   // query block start
+        const float gs = qpos[0];                                  // query block start
         const float2 mid2 = bcast2(exp2f(fminf((gs - ge) * kLOG2E, 0.f)));
         const bool tail = (n0 + 64 * n + 64 > L);
 #pragma unroll
         for (int c = 0; c < NCOL; c += 2) {
-          const float4 pa = cpos[c], pb = cpos[c + 1];
-          const float4 ra = crst[c], rb4 = crst[c + 1];
-          const float2 rq = mul2(make_float2(pa.z, pb.z), mid2);                    // rowf mid
+          const float4 r4 = qr4[c / 4], G4 = qG4[c / 4], D4 = qD4[c / 4], T4 = qT4[c / 4];
+          const bool hi = (c & 2) != 0;
+          const float2 rowf2 = hi ? make_float2(r4.z, r4.w) : make_float2(r4.x, r4.y);
+          const float2 G2 = hi ? make_float2(G4.z, G4.w) : make_float2(G4.x, G4.y);
+          const float2 nD2 = hi ? make_float2(D4.z, D4.w) : make_float2(D4.x, D4.y);
+          const float2 nT2 = hi ? make_float2(T4.z, T4.w) : make_float2(T4.x, T4.y);
+          const float2 rq = mul2(rowf2, mid2);                                      // rowf mid
           const float2 uc = mul2(make_float2(uv[c], uv[c + 1]), rq);
-          const float2 t = add2(make_float2(pa.y, pb.y), nfj2);                     // F_i - F_j
-          const float2 y = fma2(uc, rk2v, fma2(t, l2e, make_float2(ra.x, rb4.x))); // ... - lse_i
+          const float2 y = fma2(uc, rk2v, add2(G2, nfjl2));                         // ... - lse_i
           const float2 x = fma2(make_float2(sv[c], sv[c + 1]), c1v, y);
           float2 pr = make_float2(ex2_approx(x.x), ex2_approx(x.y));
           if (tail) {
             if (i0 + c >= L) pr.x = 0.f;
             if (i0 + c + 1 >= L) pr.y = 0.f;
           }
-          const float2 dsh = mul2(pr, add2(make_float2(pv[c], pv[c + 1]), make_float2(ra.y, rb4.y)));
-          const float2 dsx = fma2(pr, make_float2(ra.z, rb4.z), dsh);              // exact dS
+          const float2 dsh = mul2(pr, add2(make_float2(pv[c], pv[c + 1]), nD2));
+          const float2 dsx = fma2(pr, nT2, dsh);                                    // exact dS
           dgo2 = fma2(dsx, uc, dgo2);
           dfs2 = add2(dfs2, dsx);
           const float2 dsb = mul2(dsh, rq);
@@ -633,14 +686,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
           wb[c / 2] = pack2<kHalf>(dsb.x, dsb.y);
         }
       }
-      // one operand buffer: the previous tile's gradient UMMAs must have read it
-      if (n >= 1 && !warp_wait(BAR(B_OPE + ((n - 1) & 1)), ((n - 1) >> 1) & 1, p.status)) { ok = false; break; }
-      st_op_tmem(tbase, quarter, COL_OPS, wg, wp);
-      st_op_tmem(tbase, quarter, COL_OPS + 32, wg, wk);
-      st_op_tmem(tbase, quarter, COL_OPS + 64, wg, wb);
+      // two operand buffers: the gradient UMMAs of tile n-2 must have read this one
+      const int ob = n & 1;
+      if (n >= 2 && !warp_wait(BAR(B_OPE + ob), ((n >> 1) - 1) & 1, p.status)) { ok = false; break; }
+      st_op_tmem(tbase, quarter, COL_OPS + ob * 64, wg, wp);
+      st_op_tmem(tbase, quarter, COL_OPS + ob * 64 + 32, wg, wk);
+      {
+        const uint32_t dsb = sbase + OFF_DSB + (uint32_t)ob * SZ_DSB;   // this thread's key row, 16 query columns
+        st_shared_v4(dsb + sw128_off(r, 2 * wg), wb[0], wb[1], wb[2], wb[3]);
+        st_shared_v4(dsb + sw128_off(r, 2 * wg + 1), wb[4], wb[5], wb[6], wb[7]);
+      }
       tmem_wait_st();
+      fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(BAR(B_OPF + (n & 1)));
+      mbar_arrive(BAR(B_OPF + ob));
     }
     dfs += dfs2.x + dfs2.y;
     dgu = fmaf(colf, dgo2.x + dgo2.y, dgu);

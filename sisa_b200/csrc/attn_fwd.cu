@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         tma_load_4d(st, &p.tm_k, BAR(B_KVF + s), 0, j0, h, b);
         tma_load_4d(st + SZ_K, &p.tm_v, BAR(B_KVF + s), 0, j0, h, b);
         tma_load_4d(st + SZ_K + SZ_V, &p.tm_b, BAR(B_KVF + s), 0, j0, h, b);
-        tma_load_3d(st + SZ_K + SZ_V + SZ_B, &p.tm_pos, BAR(B_KVF + s), 0, j0, bh);
+        tma_load_3d(st + SZ_K + SZ_V + SZ_B, &p.tm_pos, BAR(B_KVF + s), j0, 0, bh);
       }
     }
   } else if (warp == 5) {
@@ -142,10 +142,10 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     const int r = tid;
     const int row = m0 + r;
     const bool vrow = row < L;
-    const float4* posbh = p.pos + (int64_t)bh * L;
-    const float4 pi = posbh[vrow ? row : L - 1];
-    const float gi = pi.x, fi = pi.y;
-    const float ga = posbh[m0].x;
+    const float* posbh = p.pos + (int64_t)bh * 4 * p.Lp;        // planes g, F, rowf, colf
+    const int rr = vrow ? row : L - 1;
+    const float gi = posbh[rr], fi = posbh[p.Lp + rr];
+    const float ga = posbh[m0];
     const float lam = p.lam[h];
     const float rs = lam * exp2f(fminf((gi - ga) * kLOG2E, 0.f));   // lam * rowf (128-row anchor)
     const float lam2 = lam * kLOG2E;
@@ -153,7 +153,8 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     const uint32_t tS = tmem_addr(tbase, warp, COL_S);
     const uint32_t tU = tmem_addr(tbase, warp, COL_U);
     const uint32_t tO = tmem_addr(tbase, warp, COL_O);
-    const float2 c1v = bcast2(c1), l2e = bcast2(kLOG2E), fi2 = bcast2(fi), neg1 = bcast2(-1.f);
+    // (F_i - F_j) log2e = fma(F_j, -log2e, F_i log2e): one packed FMA per column pair
+    const float2 c1v = bcast2(c1), nl2e = bcast2(-kLOG2E), fil2 = bcast2(fi * kLOG2E), lam2v = bcast2(lam2);
     float m_ref = -INFINITY;
     float2 lacc[4] = {bcast2(0.f), bcast2(0.f), bcast2(0.f), bcast2(0.f)};   // l = sum of fp32 p
     float2 lbacc[2] = {bcast2(0.f), bcast2(0.f)};                              // sum of DT(p)
@@ -163,7 +164,11 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
       const int j0 = key0(n);
       if (!warp_wait(BAR(B_SUF), n & 1, p.status)) { ok = false; break; }
       tc_fence_after();
-      const float4* cpos = reinterpret_cast<const float4*>(gbase + OFF_ST + s * SZ_STAGE + SZ_K + SZ_V + SZ_B);
+      // key position planes of this tile: [4][64] floats {g, F, rowf, colf}
+      const float* kpos = reinterpret_cast<const float*>(gbase + OFF_ST + s * SZ_STAGE + SZ_K + SZ_V + SZ_B);
+      const float4* kg4 = reinterpret_cast<const float4*>(kpos);
+      const float4* kf4 = reinterpret_cast<const float4*>(kpos + BN);
+      const float4* kc4 = reinterpret_cast<const float4*>(kpos + 3 * BN);
       float sv[64], uv[64];
       tmem_ld32(tS, sv);
       tmem_ld32(tS + 32, sv + 32);
@@ -173,32 +178,43 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
       tc_fence_before();
       mbar_arrive(BAR(B_SUE));            // S and U are in registers: the next tile's GEMMs may start
       float2* x2 = reinterpret_cast<float2*>(sv);     // x overwrites S in place, two columns per float2
+      const float2* u2 = reinterpret_cast<const float2*>(uv);
       if (n < ndiag) {
         // diagonal tile: pairwise decay exp(min(g_i - g_j, 0)), causal mask and sequence end
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float4 pa = cpos[2 * c], pb = cpos[2 * c + 1];
-          const float da = exp2f(fminf((gi - pa.x) * kLOG2E, 0.f));
-          const float db = exp2f(fminf((gi - pb.x) * kLOG2E, 0.f));
-          const float2 u = mul2(make_float2(da, db), make_float2(uv[2 * c], uv[2 * c + 1]));
-          const float2 t = fma2(make_float2(pa.y, pb.y), neg1, fi2);                  // F_i - F_j
-          const float2 y = fma2(u, bcast2(lam2), mul2(t, l2e));
-          float2 x = fma2(x2[c], c1v, y);
-          const int j = j0 + 2 * c;
-          if (!(j <= row && j < L)) x.x = -INFINITY;
-          if (!(j + 1 <= row && j + 1 < L)) x.y = -INFINITY;
-          x2[c] = x;
+        for (int q = 0; q < 16; ++q) {
+          const float4 g4 = kg4[q], f4 = kf4[q];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int c = 2 * q + e;
+            const float gja = e ? g4.z : g4.x, gjb = e ? g4.w : g4.y;
+            const float2 fj = e ? make_float2(f4.z, f4.w) : make_float2(f4.x, f4.y);
+            const float da = exp2f(fminf((gi - gja) * kLOG2E, 0.f));
+            const float db = exp2f(fminf((gi - gjb) * kLOG2E, 0.f));
+            const float2 u = mul2(make_float2(da, db), u2[c]);
+            const float2 y = fma2(u, lam2v, fma2(fj, nl2e, fil2));
+            float2 x = fma2(x2[c], c1v, y);
+            const int j = j0 + 2 * c;
+            if (!(j <= row && j < L)) x.x = -INFINITY;
+            if (!(j + 1 <= row && j + 1 < L)) x.y = -INFINITY;
+            x2[c] = x;
+          }
         }
       } else {
-        const float ge = cpos[BN - 1].x;
+        const float ge = kpos[BN - 1];
         const float2 rsm = bcast2(rs * exp2f(fminf((ga - ge) * kLOG2E, 0.f)) * kLOG2E);   // lam rowf mid log2e
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float4 pa = cpos[2 * c], pb = cpos[2 * c + 1];
-          const float2 w = mul2(make_float2(uv[2 * c], uv[2 * c + 1]), make_float2(pa.w, pb.w));   // U colf
-          const float2 t = fma2(make_float2(pa.y, pb.y), neg1, fi2);
-          const float2 y = fma2(w, rsm, mul2(t, l2e));
-          x2[c] = fma2(x2[c], c1v, y);
+        for (int q = 0; q < 16; ++q) {
+          const float4 f4 = kf4[q], c4 = kc4[q];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int c = 2 * q + e;
+            const float2 fj = e ? make_float2(f4.z, f4.w) : make_float2(f4.x, f4.y);
+            const float2 cf = e ? make_float2(c4.z, c4.w) : make_float2(c4.x, c4.y);
+            const float2 w = mul2(u2[c], cf);                        // U colf
+            const float2 y = fma2(w, rsm, fma2(fj, nl2e, fil2));
+            x2[c] = fma2(x2[c], c1v, y);
+          }
         }
       }
       // tile maximum: 8 independent partial maxima

@@ -71,12 +71,14 @@ int map_view4(CUtensorMap* m, const sisa_view4* v, int64_t B, int64_t H, int64_t
 }
 
 // (4, L, B*H) fp32 records, box (4, 64, 1).
-int map_records(CUtensorMap* m, const void* ptr, int64_t BH, int64_t L, const char* name) {
+// Planar per-position records (B*H, 4, Lp) fp32: dims (L, 4, B*H), box (64, 4, 1), so one copy
+// brings the four planes of a 64-row block as [4][64] floats.
+int map_records(CUtensorMap* m, const void* ptr, int64_t BH, int64_t L, int64_t Lp, const char* name) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(SISA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  cuuint64_t dims[3] = {4, (cuuint64_t)L, (cuuint64_t)BH};
-  cuuint64_t strides[2] = {16, (cuuint64_t)(L * 16)};
-  cuuint32_t box[3] = {4, 64, 1};
+  cuuint64_t dims[3] = {(cuuint64_t)L, 4, (cuuint64_t)BH};
+  cuuint64_t strides[2] = {(cuuint64_t)(Lp * 4), (cuuint64_t)(Lp * 16)};
+  cuuint32_t box[3] = {64, 4, 1};
   cuuint32_t es[3] = {1, 1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(ptr), dims, strides, box, es,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
@@ -171,7 +173,9 @@ int sisa_fused_layout(int64_t n_head, int64_t* out9) {
 
 int64_t sisa_prep_fwd_workspace(int64_t B, int64_t H, int64_t L) { return B * H * nch64(L) * 18 * 4; }
 int64_t sisa_prep_bwd_workspace(int64_t B, int64_t H, int64_t L) { return B * H * nch64(L) * 18 * 8; }
-int64_t sisa_attn_bwd_workspace(int64_t B, int64_t H, int64_t L) { return B * H * L * (16 + 3 * 4); }
+int64_t sisa_pos_len(int64_t L) { return (L + 3) & ~int64_t(3); }
+// rstat planes (B*H, 4, Lp) fp32, then rg, rf, rl (B*H, L) fp32 each
+int64_t sisa_attn_bwd_workspace(int64_t B, int64_t H, int64_t L) { return B * H * (sisa_pos_len(L) * 16 + L * 12); }
 
 int sisa_prep_fwd(const void* proj, int64_t B, int64_t L, int64_t H, int64_t proj_sb, int64_t proj_sl, int dtype,
                   const float* z, int64_t z_sb, int64_t z_sl, void* c_rot, void* b_rot, float* pos, void* workspace,
@@ -192,7 +196,8 @@ int sisa_prep_fwd(const void* proj, int64_t B, int64_t L, int64_t H, int64_t pro
   p.z = z; p.z_sb = z_sb; p.z_sl = z_sl;
   p.B = B; p.L = L; p.H = H;
   p.col_b = off[3]; p.col_c = off[4]; p.col_th = off[5]; p.col_a = off[6];
-  p.c_rot = c_rot; p.b_rot = b_rot; p.pos = pos; p.tot = static_cast<float*>(workspace); p.status = status;
+  p.c_rot = c_rot; p.b_rot = b_rot; p.pos = pos; p.Lp = sisa_pos_len(L);
+  p.tot = static_cast<float*>(workspace); p.status = status;
   cudaError_t e = sisa::launch_prep_fwd(p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_prep_fwd launch");
 }
@@ -207,7 +212,7 @@ int sisa_pack_positions(const float* g, int64_t g_sb, int64_t g_sh, int64_t g_sl
   sisa::PackLaunch p{};
   p.g = g; p.g_sb = g_sb; p.g_sh = g_sh; p.g_sl = g_sl;
   p.f = fgate; p.f_sb = f_sb; p.f_sh = f_sh; p.f_sl = f_sl;
-  p.B = B; p.H = H; p.L = L; p.pos = pos; p.status = status;
+  p.B = B; p.H = H; p.L = L; p.Lp = sisa_pos_len(L); p.pos = pos; p.status = status;
   cudaError_t e = sisa::launch_pack_positions(p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_pack_positions launch");
 }
@@ -231,13 +236,13 @@ int sisa_attn_fwd(const sisa_view4* q, const sisa_view4* k, const sisa_view4* v,
       (rc = map_view4(&p.tm_v, v, B, H, L, 64, 2, dt, 64, CU_TENSOR_MAP_SWIZZLE_128B, "v")) ||
       (rc = map_view4(&p.tm_c, c, B, H, L, 32, 2, dt, 128, CU_TENSOR_MAP_SWIZZLE_64B, "c")) ||
       (rc = map_view4(&p.tm_b, b, B, H, L, 32, 2, dt, 64, CU_TENSOR_MAP_SWIZZLE_64B, "b")) ||
-      (rc = map_records(&p.tm_pos, pos, B * H, L, "pos")))
+      (rc = map_records(&p.tm_pos, pos, B * H, L, sisa_pos_len(L), "pos")))
     return rc;
-  p.pos = reinterpret_cast<const float4*>(pos);
+  p.pos = pos;
   p.lam = lam;
   p.o = static_cast<char*>(o->data); p.o_sb = o->stride_b; p.o_sh = o->stride_h; p.o_sl = o->stride_l;
   p.lse = lse; p.o32 = o32;
-  p.B = (int)B; p.H = (int)H; p.L = (int)L; p.ntq = (int)((L + 127) / 128);
+  p.B = (int)B; p.H = (int)H; p.L = (int)L; p.Lp = (int)sisa_pos_len(L); p.ntq = (int)((L + 127) / 128);
   p.status = status;
   cudaError_t e = sisa::launch_attn_fwd(p, dtype, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_attn_fwd launch");
@@ -266,8 +271,8 @@ int sisa_attn_bwd(const sisa_view4* q, const sisa_view4* k, const sisa_view4* v,
   const CUtensorMapSwizzle s128 = CU_TENSOR_MAP_SWIZZLE_128B, s64 = CU_TENSOR_MAP_SWIZZLE_64B;
   char* ws = static_cast<char*>(workspace);
   const int64_t n = B * H * L;
-  p.rstat = reinterpret_cast<float4*>(ws);
-  p.rg = reinterpret_cast<float*>(ws + n * 16);
+  p.rstat = reinterpret_cast<float*>(ws);
+  p.rg = reinterpret_cast<float*>(ws + B * H * sisa_pos_len(L) * 16);
   p.rf = p.rg + n;
   p.rl = p.rf + n;
   if ((rc = map_view4(&p.tm_q128, q, B, H, L, 64, 2, dt, 128, s128, "q")) ||
@@ -282,10 +287,10 @@ int sisa_attn_bwd(const sisa_view4* q, const sisa_view4* k, const sisa_view4* v,
       (rc = map_view4(&p.tm_q64, q, B, H, L, 64, 2, dt, 64, s128, "q")) ||
       (rc = map_view4(&p.tm_do64, dout, B, H, L, 64, 2, dt, 64, s128, "dout")) ||
       (rc = map_view4(&p.tm_c64, c, B, H, L, 32, 2, dt, 64, s64, "c")) ||
-      (rc = map_records(&p.tm_pos, pos, B * H, L, "pos")) ||
-      (rc = map_records(&p.tm_rstat, p.rstat, B * H, L, "rstat")))
+      (rc = map_records(&p.tm_pos, pos, B * H, L, sisa_pos_len(L), "pos")) ||
+      (rc = map_records(&p.tm_rstat, p.rstat, B * H, L, sisa_pos_len(L), "rstat")))
     return rc;
-  p.pos = reinterpret_cast<const float4*>(pos);
+  p.pos = pos;
   p.lam = lam;
   p.q = static_cast<const char*>(q->data); p.q_sb = q->stride_b; p.q_sh = q->stride_h; p.q_sl = q->stride_l;
   p.k = static_cast<const char*>(k->data); p.k_sb = k->stride_b; p.k_sh = k->stride_h; p.k_sl = k->stride_l;
@@ -300,7 +305,7 @@ int sisa_attn_bwd(const sisa_view4* q, const sisa_view4* k, const sisa_view4* v,
   p.dc = static_cast<float*>(dc->data); p.dc_sb = dc->stride_b; p.dc_sh = dc->stride_h; p.dc_sl = dc->stride_l;
   p.db = static_cast<float*>(db->data); p.db_sb = db->stride_b; p.db_sh = db->stride_h; p.db_sl = db->stride_l;
   p.dg = dg; p.dF = dF; p.dlam = dlam;
-  p.B = (int)B; p.H = (int)H; p.L = (int)L;
+  p.B = (int)B; p.H = (int)H; p.L = (int)L; p.Lp = (int)sisa_pos_len(L);
   p.ntq128 = (int)((L + 127) / 128); p.ntq64 = (int)((L + 63) / 64);
   p.has_f = dF != nullptr;
   p.status = status;

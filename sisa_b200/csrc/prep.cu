@@ -96,7 +96,8 @@ struct PrepArgs {
   int col_b, col_c, col_th, col_a;
   void* c_rot;
   void* b_rot;
-  float4* pos;
+  float* pos;      // (B*H, 4, Lp) planes {g, F, rowf, colf}
+  int Lp;
   float* tot;      // (B*H, nch, kTot)
   int32_t* status;
 };
@@ -157,6 +158,20 @@ __global__ void __launch_bounds__(256) prep_sums_kernel(PrepArgs a) {
   }
 }
 
+// Store the records of positions t0, t0 + 1 (t0 even) into the four planes {g, F, rowf, colf} of one
+// (batch, head): one 8-byte store per plane when both positions exist (Lp is a multiple of 4).
+__device__ __forceinline__ void store_planes(float* pl, int Lp, int t0, int L, const float g[2], const float f[2],
+                                             const float rf[2], const float cf[2]) {
+  if (t0 + 1 < L) {
+    *reinterpret_cast<float2*>(pl + t0) = make_float2(g[0], g[1]);
+    *reinterpret_cast<float2*>(pl + Lp + t0) = make_float2(f[0], f[1]);
+    *reinterpret_cast<float2*>(pl + 2 * Lp + t0) = make_float2(rf[0], rf[1]);
+    *reinterpret_cast<float2*>(pl + 3 * Lp + t0) = make_float2(cf[0], cf[1]);
+  } else if (t0 < L) {
+    pl[t0] = g[0]; pl[Lp + t0] = f[0]; pl[2 * Lp + t0] = rf[0]; pl[3 * Lp + t0] = cf[0];
+  }
+}
+
 // Sequential sum of the totals of blocks [0, c) (component k, computed by lane k, fixed order).
 __device__ __forceinline__ float prefix_total(const float* tot, int64_t bh, int nch, int c, int k) {
   float acc = 0.f;
@@ -188,14 +203,14 @@ __global__ void __launch_bounds__(256) prep_fwd_kernel(PrepArgs a) {
     const float pre_f = __shfl_sync(0xffffffffu, mypre, 1);
     const float f0 = pre_f + s0, f1 = pre_f + s1;
     const float gg[2] = {g0, g1}, ff[2] = {f0, f1};
+    {
+      float rf[2], cf[2];
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const int t = t0 + r;
-      if (t < a.L) {
-        const float rowf = exp2f(fminf((gg[r] - gs) * kLog2e, 0.f));
-        const float colf = exp2f(fminf((ge - gg[r]) * kLog2e, 0.f));
-        a.pos[bh * a.L + t] = make_float4(gg[r], ff[r], rowf, colf);
+      for (int r = 0; r < 2; ++r) {
+        rf[r] = exp2f(fminf((gg[r] - gs) * kLog2e, 0.f));
+        cf[r] = exp2f(fminf((ge - gg[r]) * kLog2e, 0.f));
       }
+      store_planes(a.pos + bh * 4 * a.Lp, a.Lp, t0, a.L, gg, ff, rf, cf);
     }
     // Phi and the rotation of C and B
     float phi[2][kS2];
@@ -244,8 +259,8 @@ struct PackArgs {
   int64_t g_sb, g_sh, g_sl;
   const float* f;
   int64_t f_sb, f_sh, f_sl;
-  int H, L;
-  float4* pos;
+  int H, L, Lp;
+  float* pos;      // (B*H, 4, Lp) planes
   int32_t* status;
 };
 
@@ -264,21 +279,23 @@ __global__ void __launch_bounds__(256) pack_positions_kernel(PackArgs a, int nch
   const float gs = gp[(int64_t)base * a.g_sl];
   const float ge = gp[(int64_t)last * a.g_sl];
   bool bad = false;
+  float gg[2] = {0.f, 0.f}, ff[2] = {0.f, 0.f}, rf[2] = {0.f, 0.f}, cf[2] = {0.f, 0.f};
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     const int t = base + 2 * lane + r;
     if (t >= a.L) continue;
     const float g = gp[(int64_t)t * a.g_sl];
-    const float f = fp ? fp[(int64_t)t * a.f_sl] : 0.f;
-    const float rowf = exp2f(fminf((g - gs) * kLog2e, 0.f));
-    const float colf = exp2f(fminf((ge - g) * kLog2e, 0.f));
+    gg[r] = g;
+    ff[r] = fp ? fp[(int64_t)t * a.f_sl] : 0.f;
     // NaN-propagating clamps, as the reference: a NaN g gives NaN factors.
-    a.pos[bh * a.L + t] = make_float4(g, f, (g != g) ? g : rowf, (g != g) ? g : colf);
+    rf[r] = (g != g) ? g : exp2f(fminf((g - gs) * kLog2e, 0.f));
+    cf[r] = (g != g) ? g : exp2f(fminf((ge - g) * kLog2e, 0.f));
     if (t > 0) {
       const float inc = g - gp[(int64_t)(t - 1) * a.g_sl];
       bad |= !(inc <= 1e-3f);
     }
   }
+  store_planes(a.pos + bh * 4 * a.Lp, a.Lp, base + 2 * lane, a.L, gg, ff, rf, cf);
   if (__any_sync(0xffffffffu, bad) && lane == 0 && a.status) atomicOr(a.status, SISA_ST_NONMONOTONE);
 }
 
@@ -513,7 +530,7 @@ cudaError_t launch_prep_fwd(const PrepFwdLaunch& p, cudaStream_t st) {
   a.z = p.z; a.z_sb = p.z_sb; a.z_sl = p.z_sl;
   a.B = (int)p.B; a.L = (int)p.L; a.H = (int)p.H; a.nch = (int)((p.L + kBlk - 1) / kBlk);
   a.col_b = (int)p.col_b; a.col_c = (int)p.col_c; a.col_th = (int)p.col_th; a.col_a = (int)p.col_a;
-  a.c_rot = p.c_rot; a.b_rot = p.b_rot; a.pos = reinterpret_cast<float4*>(p.pos);
+  a.c_rot = p.c_rot; a.b_rot = p.b_rot; a.pos = p.pos; a.Lp = (int)p.Lp;
   a.tot = p.tot; a.status = p.status;
   dim3 grid(a.nch, a.B);
   if (p.dtype == 1) {
@@ -530,7 +547,7 @@ cudaError_t launch_pack_positions(const PackLaunch& p, cudaStream_t st) {
   PackArgs a;
   a.g = p.g; a.g_sb = p.g_sb; a.g_sh = p.g_sh; a.g_sl = p.g_sl;
   a.f = p.f; a.f_sb = p.f_sb; a.f_sh = p.f_sh; a.f_sl = p.f_sl;
-  a.H = (int)p.H; a.L = (int)p.L; a.pos = reinterpret_cast<float4*>(p.pos); a.status = p.status;
+  a.H = (int)p.H; a.L = (int)p.L; a.Lp = (int)p.Lp; a.pos = p.pos; a.status = p.status;
   const int nch = (int)((p.L + kBlk - 1) / kBlk);
   const int64_t nwork = p.B * p.H * nch;
   pack_positions_kernel<<<(unsigned)((nwork + 7) / 8), 256, 0, st>>>(a, nch, nwork);

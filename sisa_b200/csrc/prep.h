@@ -15,7 +15,8 @@ struct PrepFwdLaunch {
   int64_t col_b, col_c, col_th, col_a;
   void* c_rot;
   void* b_rot;
-  float* pos;
+  float* pos;      // (B*H, 4, Lp) planes
+  int64_t Lp;
   float* tot;
   int32_t* status;
 };
@@ -25,7 +26,7 @@ struct PackLaunch {
   int64_t g_sb, g_sh, g_sl;
   const float* f;
   int64_t f_sb, f_sh, f_sl;
-  int64_t B, H, L;
+  int64_t B, H, L, Lp;
   float* pos;
   int32_t* status;
 };

@@ -28,7 +28,7 @@ def _aligned(t: torch.Tensor) -> torch.Tensor:
 def pack_positions(g: torch.Tensor, fgate: torch.Tensor | None) -> torch.Tensor:
     lib = _lib.load()
     B, H, L = g.shape
-    pos = torch.empty((B, H, L, 4), device=g.device, dtype=torch.float32)
+    pos = _lib.pos_planes(B, H, L, g.device)
     st = backends.status_word(g.device)
     fs = fgate.stride() if fgate is not None else (0, 0, 0)
     rc = lib.sisa_pack_positions(g.data_ptr(), *g.stride(), _lib.ptr(fgate), *fs, B, H, L, pos.data_ptr(),

@@ -65,7 +65,7 @@ def prep_forward(proj: torch.Tensor, z: torch.Tensor | None, H: int):
     dev = proj.device
     c_rot = torch.empty((B, H, L, D_STATE), device=dev, dtype=proj.dtype)
     b_rot = torch.empty_like(c_rot)
-    pos = torch.empty((B, H, L, 4), device=dev, dtype=torch.float32)
+    pos = _lib.pos_planes(B, H, L, dev)
     tot = _ws(lib.sisa_prep_fwd_workspace(B, H, L), dev)
     st = backends.status_word(dev)
     rc = lib.sisa_prep_fwd(proj.data_ptr(), B, L, H, proj.stride(0), proj.stride(1), _lib.dtype_code(proj.dtype),

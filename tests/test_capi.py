@@ -53,7 +53,13 @@ def test_workspace_sizes():
     lib = _lib.load()
     assert lib.sisa_prep_fwd_workspace(2, 3, 130) == 2 * 3 * 3 * 18 * 4
     assert lib.sisa_prep_bwd_workspace(2, 3, 130) == 2 * 3 * 3 * 18 * 8
-    assert lib.sisa_attn_bwd_workspace(2, 3, 130) == 2 * 3 * 130 * 28
+    # row-statistic planes (4 x Lp fp32) + three (L,) fp32 row parts per (batch, head)
+    assert lib.sisa_attn_bwd_workspace(2, 3, 130) == 2 * 3 * (132 * 16 + 130 * 12)
+
+
+def test_position_plane_length():
+    lib = _lib.load()
+    assert [lib.sisa_pos_len(L) for L in (1, 4, 5, 130, 4096)] == [4, 4, 8, 132, 4096]
 
 
 def test_host_side_argument_errors_need_no_gpu():

@@ -5,6 +5,7 @@ import pytest
 import torch
 
 from oracle import sisa_oracle as O
+from sisa_b200 import _lib
 from tests.helpers import PREP_SCAN_REL, rel_err
 
 pytestmark = pytest.mark.gpu
@@ -19,7 +20,7 @@ def _run(B, L, H, seed, with_z=True, dtype=torch.bfloat16):
     c_rot, b_rot, pos, tot = prep_forward(proj.to(dev), z.to(dev) if with_z else None, H)
     torch.cuda.synchronize()
     ref = O.prep(proj.double(), z.double() if with_z else None, H)
-    return c_rot.cpu(), b_rot.cpu(), pos.cpu(), ref
+    return c_rot.cpu(), b_rot.cpu(), _lib.pos_records(pos, L).cpu(), ref
 
 
 @pytest.mark.parametrize("L", [1, 2, 63, 64, 65, 130, 1000, 4096])
