@@ -277,6 +277,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
     const float2 c1v = bcast2(c1), nl2e = bcast2(-kLOG2E), filse2 = bcast2(filse);
     const float2 ndl2 = bcast2(-dl), rs2v = bcast2(rs2);
     float2 xo2 = bcast2(0.f), yo2 = bcast2(0.f), za2 = bcast2(0.f), wa2 = bcast2(0.f);
+    float2 xd2 = bcast2(0.f), yd2 = bcast2(0.f);   // u-weighted sums of diagonal tiles (u fully decayed)
     for (int n = 0; ok && n < ntiles; ++n) {
       const int s = n % NST;
       const int j0 = key0(n) + wg * NCOL;
@@ -296,35 +297,70 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
       const float4* kc4 = reinterpret_cast<const float4*>(kpos + 192 + wg * NCOL);
       uint32_t wds[NCOL / 2], wdc[NCOL / 2];
       if (n < ndiag) {
+        // Diagonal tile (keys jt .. jt+63). The class of this warp's 32 rows is uniform:
+        //  after  - every row lies past the key tile: exp(g_i - g_j) = exp(g_i - ge) colf_j with both
+        //           factors <= 1 (ge = g at the key tile's end), packed like the off-diagonal path;
+        //  before - every row precedes the key tile: nothing is valid;
+        //  across - the diagonal crosses these rows: pairwise exp(min(g_i - g_j, 0)), causal mask, and
+        //           the diagonal element itself kept apart (the exact-delta terms).
+        const int jt = key0(n), r0 = m0 + quarter * 32;
+        if (r0 > jt + 63) {
+          const float rowe = ex2_approx(fminf((gi - kpos[63]) * kLOG2E, 0.f));
+          const float2 rowe2 = bcast2(rowe), lamv = bcast2(lam), lam2v = bcast2(lam2);
 #pragma unroll
-        for (int c = 0; c < NCOL; c += 2) {
-          const float4 g4 = kg4[c / 4], f4 = kf4[c / 4];
-          float dsv[2], dcv[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int cc = c + e;
-            const float gj = (c & 2) ? (e ? g4.w : g4.z) : (e ? g4.y : g4.x);
-            const float fj = (c & 2) ? (e ? f4.w : f4.z) : (e ? f4.y : f4.x);
-            const int j = j0 + cc;
-            const bool valid = (j <= row) && (j < L);
-            const float dec = valid ? exp2f(fminf((gi - gj) * kLOG2E, 0.f)) : 0.f;
-            const float u = dec * uv[cc];
-            const float x = fmaf(sv[cc], c1, fmaf(fj, -kLOG2E, fmaf(lam2, u, filse)));   // x - lse (log2)
-            const float pr = valid ? ex2_approx(x) : 0.f;
-            const float ds = pr * (pv[cc] - dl);
-            const bool eye = (j == row);
-            const float dso = eye ? 0.f : ds;
-            if (eye) { ptt += pr; dptt += pv[cc]; xd += uv[cc]; }
-            const float po = eye ? 0.f : pr;
-            za += po;
-            ya = fmaf(po, u, ya);
-            wa += dso;
-            xa = fmaf(dso, u, xa);
-            dsv[e] = dso;
-            dcv[e] = dso * (lam * dec);
+          for (int c = 0; c < NCOL; c += 2) {
+            const float4 f4 = kf4[c / 4], c4 = kc4[c / 4];
+            const float2 fj = (c & 2) ? make_float2(f4.z, f4.w) : make_float2(f4.x, f4.y);
+            const float2 cj = (c & 2) ? make_float2(c4.z, c4.w) : make_float2(c4.x, c4.y);
+            const float2 dec = mul2(cj, rowe2);
+            const float2 u = mul2(make_float2(uv[c], uv[c + 1]), dec);
+            const float2 y = fma2(u, lam2v, fma2(fj, nl2e, filse2));
+            const float2 x = fma2(make_float2(sv[c], sv[c + 1]), c1v, y);
+            const float2 pr = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            const float2 ds = mul2(pr, add2(make_float2(pv[c], pv[c + 1]), ndl2));
+            xd2 = fma2(ds, u, xd2);
+            yd2 = fma2(pr, u, yd2);
+            za2 = add2(za2, pr);
+            wa2 = add2(wa2, ds);
+            const float2 dsc = mul2(ds, mul2(dec, lamv));
+            wds[c / 2] = pack2<kHalf>(ds.x, ds.y);
+            wdc[c / 2] = pack2<kHalf>(dsc.x, dsc.y);
           }
-          wds[c / 2] = pack2<kHalf>(dsv[0], dsv[1]);
-          wdc[c / 2] = pack2<kHalf>(dcv[0], dcv[1]);
+        } else if (r0 + 31 < jt) {
+#pragma unroll
+          for (int c = 0; c < NCOL / 2; ++c) { wds[c] = 0u; wdc[c] = 0u; }
+        } else {
+          const float gil = gi * kLOG2E;
+#pragma unroll
+          for (int c = 0; c < NCOL; c += 2) {
+            const float4 g4 = kg4[c / 4], f4 = kf4[c / 4];
+            float dsv[2], dcv[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int cc = c + e;
+              const float gj = (c & 2) ? (e ? g4.w : g4.z) : (e ? g4.y : g4.x);
+              const float fj = (c & 2) ? (e ? f4.w : f4.z) : (e ? f4.y : f4.x);
+              const int j = j0 + cc;
+              const bool valid = (j <= row) && (j < L);
+              const float dec = valid ? ex2_approx(fminf(fmaf(gj, -kLOG2E, gil), 0.f)) : 0.f;
+              const float u = dec * uv[cc];
+              const float x = fmaf(sv[cc], c1, fmaf(fj, -kLOG2E, fmaf(lam2, u, filse)));   // x - lse (log2)
+              const float pr = valid ? ex2_approx(x) : 0.f;
+              const float ds = pr * (pv[cc] - dl);
+              const bool eye = (j == row);
+              const float dso = eye ? 0.f : ds;
+              if (eye) { ptt += pr; dptt += pv[cc]; xd += uv[cc]; }
+              const float po = eye ? 0.f : pr;
+              za += po;
+              ya = fmaf(po, u, ya);
+              wa += dso;
+              xa = fmaf(dso, u, xa);
+              dsv[e] = dso;
+              dcv[e] = dso * (lam * dec);
+            }
+            wds[c / 2] = pack2<kHalf>(dsv[0], dsv[1]);
+            wdc[c / 2] = pack2<kHalf>(dcv[0], dcv[1]);
+          }
         }
       } else {
         const float ge = kpos[63];
@@ -358,8 +394,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
     }
     za += za2.x + za2.y;
     wa += wa2.x + wa2.y;
-    xa = fmaf(rowf, xo2.x + xo2.y, xa);
-    ya = fmaf(rowf, yo2.x + yo2.y, ya);
+    xa = fmaf(rowf, xo2.x + xo2.y, xa) + (xd2.x + xd2.y);
+    ya = fmaf(rowf, yo2.x + yo2.y, ya) + (yd2.x + yd2.y);
     // ---- combine the warpgroups' row sums (wg > 0 -> smem -> wg 0, fixed order)
     if (wg > 0) {
       redr[wg * 8 + 0] = za; redr[wg * 8 + 1] = ya; redr[wg * 8 + 2] = wa; redr[wg * 8 + 3] = xa;
@@ -597,6 +633,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
     const float nfjl = -fj * kLOG2E;                              // x - lse_i = ... + (F_i log2e - lse_i) - F_j log2e
     const float2 c1v = bcast2(c1), nfjl2 = bcast2(nfjl), rk2v = bcast2(rk2);
     float2 dgo2 = bcast2(0.f), dfs2 = bcast2(0.f);
+    float2 dgd2 = bcast2(0.f);   // u-weighted dS sum of diagonal tiles (u fully decayed)
     bool ok = true;
     for (int n = 0; ok && n < ntiles; ++n) {
       const int s = n % NST;
@@ -622,6 +659,48 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
       const float4* qT4 = reinterpret_cast<const float4*>(qrst + 128 + wg * NCOL);
       uint32_t wp[NCOL / 2], wk[NCOL / 2], wb[NCOL / 2];
       if (n < ndiag) {
+        // Diagonal query tile (queries mt .. mt+63). The class of this warp's 32 keys is uniform:
+        //  before - every key precedes the query tile: exp(g_i - g_j) = rowf_i exp(g_mt - g_j) with both
+        //           factors <= 1 (rowf relative to the query block start mt), packed like the
+        //           off-diagonal path; every pair is strictly causal;
+        //  after  - every key follows the query tile: nothing is valid;
+        //  across - the diagonal crosses these keys: pairwise decay, causal mask, diagonal element.
+        const int mt = n0 + 64 * n, k0 = n0 + quarter * 32;
+        if (k0 + 31 < mt) {
+          const float ek = ex2_approx(fminf((qpos[0] - gj) * kLOG2E, 0.f));   // exp(g_mt - g_j)
+          const float2 ek2 = bcast2(ek), lamv = bcast2(lam), lam2v = bcast2(lam2);
+          const bool tail = (mt + 64 > L);
+#pragma unroll
+          for (int c = 0; c < NCOL; c += 2) {
+            const float4 r4 = qr4[c / 4], G4 = qG4[c / 4], D4 = qD4[c / 4], T4 = qT4[c / 4];
+            const bool hi = (c & 2) != 0;
+            const float2 rowf2 = hi ? make_float2(r4.z, r4.w) : make_float2(r4.x, r4.y);
+            const float2 G2 = hi ? make_float2(G4.z, G4.w) : make_float2(G4.x, G4.y);
+            const float2 nD2 = hi ? make_float2(D4.z, D4.w) : make_float2(D4.x, D4.y);
+            const float2 nT2 = hi ? make_float2(T4.z, T4.w) : make_float2(T4.x, T4.y);
+            const float2 dec = mul2(rowf2, ek2);
+            const float2 u = mul2(make_float2(uv[c], uv[c + 1]), dec);
+            const float2 y = fma2(u, lam2v, add2(G2, nfjl2));
+            const float2 x = fma2(make_float2(sv[c], sv[c + 1]), c1v, y);
+            float2 pr = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            if (tail) {
+              if (i0 + c >= L) pr.x = 0.f;
+              if (i0 + c + 1 >= L) pr.y = 0.f;
+            }
+            const float2 dsh = mul2(pr, add2(make_float2(pv[c], pv[c + 1]), nD2));
+            const float2 dsx = fma2(pr, nT2, dsh);
+            dgd2 = fma2(dsx, u, dgd2);
+            dfs2 = add2(dfs2, dsx);
+            const float2 dsb = mul2(dsh, mul2(dec, lamv));
+            wp[c / 2] = pack2<kHalf>(pr.x, pr.y);
+            wk[c / 2] = pack2<kHalf>(dsx.x, dsx.y);
+            wb[c / 2] = pack2<kHalf>(dsb.x, dsb.y);
+          }
+        } else if (k0 > mt + 63) {
+#pragma unroll
+          for (int c = 0; c < NCOL / 2; ++c) { wp[c] = 0u; wk[c] = 0u; wb[c] = 0u; }
+        } else {
+          const float gjl = gj * kLOG2E;
 #pragma unroll
         for (int c = 0; c < NCOL; c += 2) {
           const float4 g4 = qg4[c / 4], G4 = qG4[c / 4], D4 = qD4[c / 4], T4 = qT4[c / 4];
@@ -638,7 +717,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
             const bool valid = (i >= j) && (i < L);
             const bool strict = valid && (i > j);
             const bool eye = valid && (i == j);
-            const float dec = valid ? exp2f(fminf((gi - gj) * kLOG2E, 0.f)) : 0.f;
+            const float dec = valid ? ex2_approx(fminf(fmaf(gi, kLOG2E, -gjl), 0.f)) : 0.f;
             const float u = dec * uv[cc];
             const float x = fmaf(sv[cc], c1, fmaf(lam2, u, Gi + nfjl));   // x - lse_i (log2)
             const float pr = valid ? ex2_approx(x) : 0.f;
@@ -654,6 +733,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
           wp[c / 2] = pack2<kHalf>(pe[0], pe[1]);
           wk[c / 2] = pack2<kHalf>(ke[0], ke[1]);
           wb[c / 2] = pack2<kHalf>(be[0], be[1]);
+        }
         }
       } else {
         const float gs = qpos[0];                                  // query block start
@@ -702,7 +782,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
       mbar_arrive(BAR(B_OPF + ob));
     }
     dfs += dfs2.x + dfs2.y;
-    dgu = fmaf(colf, dgo2.x + dgo2.y, dgu);
+    dgu = fmaf(colf, dgo2.x + dgo2.y, dgu) + (dgd2.x + dgd2.y);
     float* redr = red + r * (NWG * 2);
     if (wg > 0) { redr[wg * 2 + 0] = dgu; redr[wg * 2 + 1] = dfs; }
     named_bar_sync(1, NCT);

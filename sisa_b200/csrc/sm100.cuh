@@ -289,6 +289,17 @@ __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Named barrier that also returns the AND of `v` over the participating threads, so that a group of
+// warps can leave a loop together when any of them has failed a bounded wait.
+__device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r) : "r"((uint32_t)v), "r"(id), "r"(nthreads) : "memory");
+  return r != 0;
+}
+
 __device__ __forceinline__ uint32_t elect_lane0() { return (threadIdx.x & 31u) == 0u; }
 
 }  // namespace sisa
