@@ -38,6 +38,10 @@ sys.path.insert(0, str(ROOT))
 B, T, H = 8, 4096, 16
 FLOP_PER_PAIR = 1152
 FWD_FLOP_PER_PAIR = 320
+# DRAM bytes (read + write) of attn_fwd + attn_bwd_dq + attn_bwd_dkv for one cfg1 step: ncu
+# dram__bytes_read.sum + dram__bytes_write.sum at B=1, H=8, T=4096 (profiles/attn_kernels_B1T4096H8_ncu.md),
+# scaled by the number of (batch, head, position) units; the traffic per unit does not depend on B or H.
+ATTN_TRAFFIC_PER_UNIT = 1.2158e9 / (8 * 16 * 4096)
 METRIC = "SISA attn fwd+bwd TFLOP/s (T=4096 bf16)"
 
 
@@ -267,7 +271,9 @@ def run_cuda(args):
                        "flop_per_pair": FLOP_PER_PAIR},
             "roofline": {"kernel": "sisa_attn_fwd + sisa_attn_bwd (tcgen05)", "bound": "tensor",
                          "achieved": round(ach, 3), "peak": burst, "unit": "TFLOP/s", "frac": round(ach / burst, 4),
-                         "peak_source": f"{src} bf16 burst", "traffic": None,
+                         "peak_source": f"{src} bf16 burst",
+                         "traffic": round(ATTN_TRAFFIC_PER_UNIT * b_ * h_ * t_),
+                         "traffic_note": "ncu DRAM bytes of the three attention kernels per step, scaled from B=1 H=8",
                          "per_call_ms": {k: round(v, 4) for k, v in per.items()},
                          "attn_fwd_tflops": round(FWD_FLOP_PER_PAIR * pairs(b_, h_, t_) / (per["attn_fwd"] * 1e-3) / 1e12, 3),
                          "attn_bwd_tflops": round((FLOP_PER_PAIR - FWD_FLOP_PER_PAIR) * pairs(b_, h_, t_) /
