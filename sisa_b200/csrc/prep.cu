@@ -29,10 +29,14 @@ constexpr int kS2 = 16;           // rotation pairs per head (d_state / 2)
 constexpr int kTot = 2 + kS2;     // totals per (b, h, block): log alpha, log f, theta[16]
 constexpr float kLog2e = 1.4426950408889634f;
 
+// Read-only global loads go through the non-coherent path (ld.global.nc): the inputs are never written
+// by these kernels, and the compiler may then hoist the loads above the outputs' stores instead of
+// serialising every load round trip behind them.
 template <bool kHalf>
 __device__ __forceinline__ float ld_lp(const void* p, int64_t i) {
-  if constexpr (kHalf) return __half2float(reinterpret_cast<const __half*>(p)[i]);
-  else return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  const unsigned short bits = __ldg(reinterpret_cast<const unsigned short*>(p) + i);
+  if constexpr (kHalf) return __half2float(__ushort_as_half(bits));
+  else return __bfloat162float(__ushort_as_bfloat16(bits));
 }
 
 __device__ __forceinline__ float neg_softplus(float a) {       // torch softplus, threshold 20
@@ -112,11 +116,11 @@ __device__ __forceinline__ void load_elems(const PrepArgs& a, int b, int h, int 
     const bool ok = t < a.L;
     const int64_t row = (int64_t)b * a.proj_sb + (int64_t)(ok ? t : 0) * a.proj_sl;
     la[r] = ok ? neg_softplus(ld_lp<kHalf>(a.proj, row + a.col_a + h)) : 0.f;
-    lf[r] = (ok && a.z) ? logsigmoid(a.z[(int64_t)b * a.z_sb + (int64_t)t * a.z_sl + h]) : 0.f;
+    lf[r] = (ok && a.z) ? logsigmoid(__ldg(a.z + (int64_t)b * a.z_sb + (int64_t)t * a.z_sl + h)) : 0.f;
     const uint4* tp = reinterpret_cast<const uint4*>(
         reinterpret_cast<const char*>(a.proj) + (row + a.col_th + h * kS2) * 2);
     uint4 v0 = make_uint4(0, 0, 0, 0), v1 = make_uint4(0, 0, 0, 0);
-    if (ok) { v0 = tp[0]; v1 = tp[1]; }
+    if (ok) { v0 = __ldg(tp); v1 = __ldg(tp + 1); }
     const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -172,12 +176,20 @@ __device__ __forceinline__ void store_planes(float* pl, int Lp, int t0, int L, c
   }
 }
 
-// Sequential sum of the totals of blocks [0, c) (component k, computed by lane k, fixed order).
+// Sequential sum of the totals of blocks [0, c) (component k, computed by lane k, fixed order). The
+// order of the additions is what makes g non-increasing across block boundaries (the next block's
+// prefix is exactly this block's prefix plus its total), so it stays sequential; the loads are issued
+// 16 at a time so the sum costs ceil(c / 16) round trips instead of one per block.
 __device__ __forceinline__ float prefix_total(const float* tot, int64_t bh, int nch, int c, int k) {
   float acc = 0.f;
   const float* p = tot + bh * nch * kTot + k;
-#pragma unroll 4
-  for (int cc = 0; cc < c; ++cc) acc += p[(int64_t)cc * kTot];
+  for (int c0 = 0; c0 < c; c0 += 16) {
+    float v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = (c0 + i < c) ? __ldg(p + (int64_t)(c0 + i) * kTot) : 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) if (c0 + i < c) acc += v[i];
+  }
   return acc;
 }
 
@@ -235,9 +247,12 @@ __global__ void __launch_bounds__(256) prep_fwd_kernel(PrepArgs a) {
         const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.proj) + (row + col) * 2);
         uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(which == 0 ? a.c_rot : a.b_rot) +
                                               ((bh * a.L + t) * 32) * 2);
+        uint4 vq[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) vq[q] = __ldg(src + q);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const uint4 v = src[q];
+          const uint4 v = vq[q];
           const uint32_t w[4] = {v.x, v.y, v.z, v.w};
           uint32_t o[4];
 #pragma unroll
@@ -276,22 +291,22 @@ __global__ void __launch_bounds__(256) pack_positions_kernel(PackArgs a, int nch
   const float* fp = a.f ? a.f + (int64_t)b * a.f_sb + (int64_t)h * a.f_sh : nullptr;
   const int base = c * kBlk;
   const int last = min(base + kBlk - 1, a.L - 1);
-  const float gs = gp[(int64_t)base * a.g_sl];
-  const float ge = gp[(int64_t)last * a.g_sl];
+  const float gs = __ldg(gp + (int64_t)base * a.g_sl);
+  const float ge = __ldg(gp + (int64_t)last * a.g_sl);
   bool bad = false;
   float gg[2] = {0.f, 0.f}, ff[2] = {0.f, 0.f}, rf[2] = {0.f, 0.f}, cf[2] = {0.f, 0.f};
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     const int t = base + 2 * lane + r;
     if (t >= a.L) continue;
-    const float g = gp[(int64_t)t * a.g_sl];
+    const float g = __ldg(gp + (int64_t)t * a.g_sl);
     gg[r] = g;
-    ff[r] = fp ? fp[(int64_t)t * a.f_sl] : 0.f;
+    ff[r] = fp ? __ldg(fp + (int64_t)t * a.f_sl) : 0.f;
     // NaN-propagating clamps, as the reference: a NaN g gives NaN factors.
     rf[r] = (g != g) ? g : exp2f(fminf((g - gs) * kLog2e, 0.f));
     cf[r] = (g != g) ? g : exp2f(fminf((ge - g) * kLog2e, 0.f));
     if (t > 0) {
-      const float inc = g - gp[(int64_t)(t - 1) * a.g_sl];
+      const float inc = g - __ldg(gp + (int64_t)(t - 1) * a.g_sl);
       bad |= !(inc <= 1e-3f);
     }
   }
@@ -333,7 +348,7 @@ __device__ __forceinline__ void recompute_phi(const PrepBwdArgs& a, int b, int h
     const uint4* tp = reinterpret_cast<const uint4*>(
         reinterpret_cast<const char*>(a.proj) + (row + a.col_th + h * kS2) * 2);
     uint4 v0 = make_uint4(0, 0, 0, 0), v1 = make_uint4(0, 0, 0, 0);
-    if (ok) { v0 = tp[0]; v1 = tp[1]; }
+    if (ok) { v0 = __ldg(tp); v1 = __ldg(tp + 1); }
     const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
@@ -374,10 +389,16 @@ __device__ __forceinline__ void rotation_grads(const PrepBwdArgs& a, int b, int 
       const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.proj) + (row + col) * 2);
       const float4* gsrc = reinterpret_cast<const float4*>((which == 0 ? a.dc : a.db) + (bh * a.L + t) * 32);
       uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.dproj) + (drow + col) * 2);
+      uint4 vq[4];
+      float4 gq[8];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) vq[q] = __ldg(src + q);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) gq[q] = __ldg(gsrc + q);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const uint4 v = src[q];
-        const float4 g0 = gsrc[2 * q], g1 = gsrc[2 * q + 1];
+        const uint4 v = vq[q];
+        const float4 g0 = gq[2 * q], g1 = gq[2 * q + 1];
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
         const float gd[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
         uint32_t o[4];
@@ -405,12 +426,12 @@ __global__ void __launch_bounds__(256) prep_bsums_kernel(PrepBwdArgs a) {
   for (int h = warp; h < a.H; h += 8) {
     const int64_t bh = (int64_t)b * a.H + h;
     double x0, x1, r0, r1, tv[kTot];
-    x0 = t0 < a.L ? (double)a.dg[bh * a.L + t0] : 0.0;
-    x1 = t0 + 1 < a.L ? (double)a.dg[bh * a.L + t0 + 1] : 0.0;
+    x0 = t0 < a.L ? (double)__ldg(a.dg + bh * a.L + t0) : 0.0;
+    x1 = t0 + 1 < a.L ? (double)__ldg(a.dg + bh * a.L + t0 + 1) : 0.0;
     rscan64(x0, x1, r0, r1);
     tv[0] = __shfl_sync(0xffffffffu, r0, 0);
-    x0 = (a.dF && t0 < a.L) ? (double)a.dF[bh * a.L + t0] : 0.0;
-    x1 = (a.dF && t0 + 1 < a.L) ? (double)a.dF[bh * a.L + t0 + 1] : 0.0;
+    x0 = (a.dF && t0 < a.L) ? (double)__ldg(a.dF + bh * a.L + t0) : 0.0;
+    x1 = (a.dF && t0 + 1 < a.L) ? (double)__ldg(a.dF + bh * a.L + t0 + 1) : 0.0;
     rscan64(x0, x1, r0, r1);
     tv[1] = __shfl_sync(0xffffffffu, r0, 0);
     float phi[2][kS2], dphi[2][kS2];
@@ -431,11 +452,17 @@ __global__ void __launch_bounds__(256) prep_bsums_kernel(PrepBwdArgs a) {
   }
 }
 
+// Sum of the totals of blocks (c, nch) in the order c+1, c+2, ... (fp64), loads batched like prefix_total.
 __device__ __forceinline__ double suffix_total(const double* bt, int64_t bh, int nch, int c, int k) {
   double acc = 0.0;
   const double* p = bt + bh * nch * kTot + k;
-#pragma unroll 4
-  for (int cc = c + 1; cc < nch; ++cc) acc += p[(int64_t)cc * kTot];
+  for (int c0 = c + 1; c0 < nch; c0 += 16) {
+    double v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = (c0 + i < nch) ? __ldg(p + (int64_t)(c0 + i) * kTot) : 0.0;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) if (c0 + i < nch) acc += v[i];
+  }
   return acc;
 }
 
@@ -455,8 +482,8 @@ __global__ void __launch_bounds__(256) prep_bwd_kernel(PrepBwdArgs a) {
     const double mysuf = lane < kTot ? suffix_total(a.bt, bh, a.nch, c, lane) : 0.0;
     double x0, x1, r0, r1;
     // d alpha = -(sum_{s>=t} dg_s) * softplus'(alpha)
-    x0 = t0 < a.L ? (double)a.dg[bh * a.L + t0] : 0.0;
-    x1 = t0 + 1 < a.L ? (double)a.dg[bh * a.L + t0 + 1] : 0.0;
+    x0 = t0 < a.L ? (double)__ldg(a.dg + bh * a.L + t0) : 0.0;
+    x1 = t0 + 1 < a.L ? (double)__ldg(a.dg + bh * a.L + t0 + 1) : 0.0;
     rscan64(x0, x1, r0, r1);
     {
       const double suf = __shfl_sync(0xffffffffu, mysuf, 0);
@@ -474,8 +501,8 @@ __global__ void __launch_bounds__(256) prep_bwd_kernel(PrepBwdArgs a) {
     }
     // dz = (sum_{s>=t} dF_s) * logsigmoid'(z)
     if (a.z) {
-      x0 = (a.dF && t0 < a.L) ? (double)a.dF[bh * a.L + t0] : 0.0;
-      x1 = (a.dF && t0 + 1 < a.L) ? (double)a.dF[bh * a.L + t0 + 1] : 0.0;
+      x0 = (a.dF && t0 < a.L) ? (double)__ldg(a.dF + bh * a.L + t0) : 0.0;
+      x1 = (a.dF && t0 + 1 < a.L) ? (double)__ldg(a.dF + bh * a.L + t0 + 1) : 0.0;
       rscan64(x0, x1, r0, r1);
       const double suf = __shfl_sync(0xffffffffu, mysuf, 1);
       const double rr[2] = {r0, r1};
@@ -484,7 +511,7 @@ __global__ void __launch_bounds__(256) prep_bwd_kernel(PrepBwdArgs a) {
         const int t = t0 + r;
         if (t >= a.L) continue;
         const float dlf = (float)(suf + rr[r]);
-        const float zv = a.z[(int64_t)b * a.z_sb + (int64_t)t * a.z_sl + h];
+        const float zv = __ldg(a.z + (int64_t)b * a.z_sb + (int64_t)t * a.z_sl + h);
         a.dz[((int64_t)b * a.L + t) * a.H + h] = dlf * logsigmoid_grad(zv);
       }
     }

@@ -73,3 +73,6 @@ def test_host_side_argument_errors_need_no_gpu():
     assert rc == _lib.ERR_TYPE
     with pytest.raises(TypeError):
         _lib.check(rc, "sisa_prep_fwd")
+    # (batch, head) rows are a launch-grid dimension: at most 65535 of them
+    rc = lib.sisa_prep_fwd(None, 65536, 10, 1, 0, 0, 0, None, 0, 0, None, None, None, None, None, None)
+    assert rc == _lib.ERR_VALUE and "too large" in _lib.last_error()
