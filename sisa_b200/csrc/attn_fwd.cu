@@ -12,11 +12,14 @@
 // x = s log2e and write P = 2^(x - m) as packed bf16 straight into tensor memory (one tcgen05.st
 // per thread), from where the MMA warp accumulates O += P V with A read from TMEM - the tensor core
 // reads only V from shared memory, which keeps these small-N UMMAs off the shared-memory bandwidth
-// limit. The running maximum is rescaled lazily: O (in TMEM), l and sum DT(p) are corrected only
-// when a row's tile maximum exceeds the reference maximum by more than 2^8, so most tiles need no
-// correction pass. The per-element arithmetic runs on packed fp32 pairs (FFMA2/FADD2/FMUL2) with
-// tree reductions. Key tiles are visited diagonal first, then from the start of the sequence.
-// TMEM: 256 columns (S 64 | U 64 | O 64 | P 2 x 32), so two CTAs share an SM and one CTA's MMAs
+// limit. The P V UMMA runs with N = 80 against V followed by a constant tile that is 1 in its first
+// column, so O's column 64 accumulates sum_j DT(p_ij) (the denominator of the self-normalised output)
+// on the tensor core instead of two unpacks and an add per column pair. The running maximum is
+// rescaled lazily: O (in TMEM, its sum column included) and l are corrected only when a row's tile
+// maximum exceeds the reference maximum by more than 2^8, so most tiles need no correction pass. The
+// per-element arithmetic runs on packed fp32 pairs (FFMA2/FADD2/FMUL2) with tree reductions. Key
+// tiles are visited diagonal first, then from the start of the sequence.
+// TMEM: 240 of 256 columns (S 64 | U 64 | O 80 | P 32), so two CTAs share an SM and one CTA's MMAs
 // overlap the other's softmax.
 #include <cuda_runtime.h>
 
@@ -28,16 +31,22 @@ namespace fwd {
 
 constexpr int BM = 128, BN = 64, NSTAGE = 2;
 constexpr uint32_t SZ_Q = BM * 128, SZ_C = BM * 64;
-constexpr uint32_t SZ_K = BN * 128, SZ_V = BN * 128, SZ_B = BN * 64, SZ_POS = BN * 16;
-constexpr uint32_t SZ_STAGE = SZ_K + SZ_V + SZ_B + SZ_POS;    // 21504 = 21 KiB
+constexpr uint32_t SZ_K = BN * 128, SZ_V = BN * 128, SZ_ONE = BN * 128, SZ_B = BN * 64, SZ_POS = BN * 16;
+// Stage: K | V | ONE | B~ | pos. ONE is a constant tile (1 in the first column of every key row) that
+// sits where the P V UMMA with N = 80 reads the second 64-wide slice of its V operand, so O's column 64
+// accumulates sum_j DT(p_ij) on the tensor core.
+constexpr uint32_t OFFS_V = SZ_K, OFFS_ONE = OFFS_V + SZ_V, OFFS_B = OFFS_ONE + SZ_ONE, OFFS_POS = OFFS_B + SZ_B;
+constexpr uint32_t SZ_STAGE = OFFS_POS + SZ_POS;              // 29696 = 29 KiB
 constexpr uint32_t SZ_P = BM * 128;
 constexpr uint32_t OFF_Q = 0, OFF_C = OFF_Q + SZ_Q, OFF_ST = OFF_C + SZ_C;
 constexpr uint32_t OFF_BAR = OFF_ST + NSTAGE * SZ_STAGE;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
 constexpr uint32_t TMEM_COLS = 256;
-constexpr int COL_S = 0, COL_U = 64, COL_O = 128, COL_P = 192;   // P: two 32-column bf16x2 buffers
+constexpr int NO = 80;                                           // O columns: 64 head dims | sum DT(p) | 15 zero
+constexpr int COL_S = 0, COL_U = 64, COL_O = 128, COL_P = COL_O + NO;   // P: one 32-column bf16x2 buffer
+static_assert(COL_P + 32 <= (int)TMEM_COLS, "TMEM budget");
 // barrier indices
-constexpr int B_Q = 0, B_KVF = 1, B_KVE = 3, B_SUF = 5, B_SUE = 6, B_PF = 7, B_PE = 9, B_O = 11;
+constexpr int B_Q = 0, B_KVF = 1, B_KVE = 3, B_SUF = 5, B_SUE = 6, B_PF = 7, B_PE = 8, B_O = 9;
 
 static_assert(OFF_ST % 1024 == 0 && SZ_STAGE % 1024 == 0, "swizzle alignment");
 
@@ -65,11 +74,21 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     for (int s = 0; s < NSTAGE; ++s) { mbar_init(BAR(B_KVF + s), 1); mbar_init(BAR(B_KVE + s), 1); }
     mbar_init(BAR(B_SUF), 1);
     mbar_init(BAR(B_SUE), 128);
-    for (int i = 0; i < 2; ++i) { mbar_init(BAR(B_PF + i), 128); mbar_init(BAR(B_PE + i), 1); }
+    mbar_init(BAR(B_PF), 128);
+    mbar_init(BAR(B_PE), 1);
     mbar_init(BAR(B_O), 1);
     fence_barrier_init();
   }
   if (warp == 5) { tmem_alloc(smem_u32(tmem_slot), TMEM_COLS); tmem_relinquish(); }
+  if (tid < NSTAGE * BN) {
+    // ONE tile row (128-byte swizzle, as TMA lays out V): element 0 of key row k lives in 16-byte chunk k % 8
+    const int s = tid / BN, k = tid % BN;
+    const uint32_t row = sbase + OFF_ST + (uint32_t)s * SZ_STAGE + OFFS_ONE + (uint32_t)k * 128;
+    const uint32_t one = kHalf ? 0x3C00u : 0x3F80u;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) st_shared_v4(row + (uint32_t)c * 16, c == (k & 7) ? one : 0u, 0u, 0u, 0u);
+    fence_proxy_async_smem();
+  }
   if (warp == 4 && lane == 0) {
     tma_prefetch_desc(&p.tm_q); tma_prefetch_desc(&p.tm_k); tma_prefetch_desc(&p.tm_v);
     tma_prefetch_desc(&p.tm_c); tma_prefetch_desc(&p.tm_b); tma_prefetch_desc(&p.tm_pos);
@@ -93,30 +112,30 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         if (n >= NSTAGE && !mbar_wait(BAR(B_KVE + s), ((n / NSTAGE) - 1) & 1, p.status)) break;
         const int j0 = key0(n);
         const uint32_t st = stage_addr(s);
-        mbar_expect_tx(BAR(B_KVF + s), SZ_STAGE);
+        mbar_expect_tx(BAR(B_KVF + s), SZ_K + SZ_V + SZ_B + SZ_POS);
         tma_load_4d(st, &p.tm_k, BAR(B_KVF + s), 0, j0, h, b);
-        tma_load_4d(st + SZ_K, &p.tm_v, BAR(B_KVF + s), 0, j0, h, b);
-        tma_load_4d(st + SZ_K + SZ_V, &p.tm_b, BAR(B_KVF + s), 0, j0, h, b);
-        tma_load_3d(st + SZ_K + SZ_V + SZ_B, &p.tm_pos, BAR(B_KVF + s), j0, 0, bh);
+        tma_load_4d(st + OFFS_V, &p.tm_v, BAR(B_KVF + s), 0, j0, h, b);
+        tma_load_4d(st + OFFS_B, &p.tm_b, BAR(B_KVF + s), 0, j0, h, b);
+        tma_load_3d(st + OFFS_POS, &p.tm_pos, BAR(B_KVF + s), j0, 0, bh);
       }
     }
   } else if (warp == 5) {
     // ------------------------------------------------------------------ UMMA issuer
     if (lane == 0) {
       constexpr uint32_t id_qk = make_idesc(128, 64, kHalf ? 0 : 1, 0, 0);
-      constexpr uint32_t id_pv = make_idesc(128, 64, kHalf ? 0 : 1, 0, 1);
+      constexpr uint32_t id_pv = make_idesc(128, NO, kHalf ? 0 : 1, 0, 1);
       const uint32_t tS = tbase + COL_S, tU = tbase + COL_U, tO = tbase + COL_O;
       bool ok = mbar_wait(BAR(B_Q), 0, p.status);
       auto issue_pv = [&](int m) -> bool {
-        const int buf = m & 1, s = m % NSTAGE;
-        if (!mbar_wait(BAR(B_PF + buf), (m >> 1) & 1, p.status)) return false;
+        const int s = m % NSTAGE;
+        if (!mbar_wait(BAR(B_PF), m & 1, p.status)) return false;
         tc_fence_after();
-        const uint32_t tP = tbase + COL_P + (uint32_t)buf * 32;
-        const uint32_t sV = stage_addr(s) + SZ_K;
+        const uint32_t tP = tbase + COL_P;
+        const uint32_t sV = stage_addr(s) + OFFS_V;     // N = 80: V, then the ONE tile 8192 bytes (LBO) on
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           umma_ts(tO, tP + k * 8, desc_mn128(sV + k * 2048), id_pv, (m > 0 || k > 0) ? 1u : 0u);
-        umma_commit(BAR(B_PE + buf));
+        umma_commit(BAR(B_PE));
         umma_commit(BAR(B_KVE + s));
         return true;
       };
@@ -130,7 +149,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         for (int k = 0; k < 4; ++k) umma_ss(tS, desc_k128(sQ + k * 32), desc_k128(st + k * 32), id_qk, k > 0);
 #pragma unroll
         for (int k = 0; k < 2; ++k)
-          umma_ss(tU, desc_k64(sC + k * 32), desc_k64(st + SZ_K + SZ_V + k * 32), id_qk, k > 0);
+          umma_ss(tU, desc_k64(sC + k * 32), desc_k64(st + OFFS_B + k * 32), id_qk, k > 0);
         umma_commit(BAR(B_SUF));
         if (n > 0 && !issue_pv(n - 1)) { ok = false; break; }
       }
@@ -157,7 +176,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     const float2 c1v = bcast2(c1), nl2e = bcast2(-kLOG2E), fil2 = bcast2(fi * kLOG2E), lam2v = bcast2(lam2);
     float m_ref = -INFINITY;
     float2 lacc[4] = {bcast2(0.f), bcast2(0.f), bcast2(0.f), bcast2(0.f)};   // l = sum of fp32 p
-    float2 lbacc[2] = {bcast2(0.f), bcast2(0.f)};                              // sum of DT(p)
+    // (sum of DT(p) is O's column 64, accumulated by the P V UMMA)
     bool ok = true;
     for (int n = 0; n < ntiles; ++n) {
       const int s = n % NSTAGE;
@@ -165,7 +184,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
       if (!warp_wait(BAR(B_SUF), n & 1, p.status)) { ok = false; break; }
       tc_fence_after();
       // key position planes of this tile: [4][64] floats {g, F, rowf, colf}
-      const float* kpos = reinterpret_cast<const float*>(gbase + OFF_ST + s * SZ_STAGE + SZ_K + SZ_V + SZ_B);
+      const float* kpos = reinterpret_cast<const float*>(gbase + OFF_ST + s * SZ_STAGE + OFFS_POS);
       const float4* kg4 = reinterpret_cast<const float4*>(kpos);
       const float4* kf4 = reinterpret_cast<const float4*>(kpos + BN);
       const float4* kc4 = reinterpret_cast<const float4*>(kpos + 3 * BN);
@@ -217,24 +236,26 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
           }
         }
       }
-      // tile maximum: 8 independent partial maxima
+      // tile maximum: 8 independent partial maxima over 8 columns each, three-input max
       float mx[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = fmaxf(sv[i], sv[i + 8]);
-#pragma unroll
-      for (int c = 16; c < 64; c += 8)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], sv[c + i]);
-      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      for (int i = 0; i < 8; ++i) {
+        mx[i] = fmax3(sv[i], sv[i + 8], sv[i + 16]);
+        mx[i] = fmax3(mx[i], sv[i + 24], sv[i + 32]);
+        mx[i] = fmax3(mx[i], sv[i + 40], sv[i + 48]);
+        mx[i] = fmaxf(mx[i], sv[i + 56]);
+      }
+      const float mt = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
       const bool need = mt > m_ref + 8.f;
       const float m_new = need ? mt : m_ref;
       const float corr = need ? ex2_approx(m_ref - m_new) : 1.f;
       if (__any_sync(0xffffffffu, need) && n > 0) {
-        // lazy correction of O and of the DT(p) row sum: wait until the previous tile's UMMAs have landed
-        if (!warp_wait(BAR(B_PE + ((n - 1) & 1)), ((n - 1) >> 1) & 1, p.status)) { ok = false; break; }
+        // lazy correction of O (including its DT(p) sum column): wait until the previous tile's UMMAs
+        // have landed
+        if (!warp_wait(BAR(B_PE), (n - 1) & 1, p.status)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < 5; ++q) {
           float ov[16];
           tmem_ld16(tO + q * 16, ov);
           tmem_wait_ld();
@@ -247,11 +268,8 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
       const float2 corr2 = bcast2(corr);
 #pragma unroll
       for (int i = 0; i < 4; ++i) lacc[i] = mul2(lacc[i], corr2);
-      lbacc[0] = mul2(lbacc[0], corr2);
-      lbacc[1] = mul2(lbacc[1], corr2);
       m_ref = m_new;
       const float2 mu2 = bcast2((m_ref == -INFINITY) ? 0.f : -m_ref);
-      if (n >= 2 && !warp_wait(BAR(B_PE + (n & 1)), ((n >> 1) - 1) & 1, p.status)) { ok = false; break; }
       uint32_t w[32];
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
@@ -259,23 +277,23 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         const float2 pe = make_float2(ex2_approx(d.x), ex2_approx(d.y));
         lacc[c & 3] = add2(lacc[c & 3], pe);
         w[c] = pack2<kHalf>(pe.x, pe.y);
-        lbacc[c & 1] = add2(lbacc[c & 1], make_float2(unpack_lo<kHalf>(w[c]), unpack_hi<kHalf>(w[c])));
       }
-      tmem_st32u(tmem_addr(tbase, warp, COL_P + (n & 1) * 32), w);
+      // one P buffer: the previous tile's P V UMMAs must have read it
+      if (n >= 1 && !warp_wait(BAR(B_PE), (n - 1) & 1, p.status)) { ok = false; break; }
+      tmem_st32u(tmem_addr(tbase, warp, COL_P), w);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(BAR(B_PF + (n & 1)));
+      mbar_arrive(BAR(B_PF));
     }
     const float2 lsum = add2(add2(lacc[0], lacc[1]), add2(lacc[2], lacc[3]));
     const float l = lsum.x + lsum.y;
-    const float2 lbsum = add2(lbacc[0], lbacc[1]);
-    const float lb = lbsum.x + lbsum.y;
     if (ok && !warp_wait(BAR(B_O), 0, p.status)) ok = false;
     if (ok) {
       tc_fence_after();
-      float ov[64];
+      float ov[64], lb;
       tmem_ld32(tO, ov);
       tmem_ld32(tO + 32, ov + 32);
+      tmem_ld1(tO + 64, lb);
       tmem_wait_ld();
       if (vrow) {
         const float ls = (l == 0.f) ? 1.f : l;

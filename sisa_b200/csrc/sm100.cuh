@@ -237,6 +237,13 @@ __host__ __device__ constexpr uint32_t make_idesc(int M, int N, int ab_fmt, int 
 }
 
 // ------------------------------------------------------------------------------------ math helpers
+// Three-input maximum (one instruction on sm_100; NaN inputs are ignored like fmaxf's).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
