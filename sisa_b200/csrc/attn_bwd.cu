@@ -226,28 +226,41 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
     const float c1 = kScale * kLOG2E;
     const float lse = vrow ? p.lse[rb + row] : INFINITY;
     float* red = reinterpret_cast<float*>(gbase + OFF_RED);
-    bool ok = warp_wait(BAR(B_Q), 0, p.status);
     // delta'' = do . o'' over this warpgroup's NCOL head dims (o'' snaps to the DT output where they agree
-    // to 2^-15, attention.py:341-350), combined across the two warpgroups.
+    // to 2^-15, attention.py:341-350), combined across the warpgroups. The o and o'' row slices are
+    // loaded (16-byte, non-coherent) before waiting for the dO tile, so both latencies overlap.
+    static_assert(NCOL == 16, "two 16-byte chunks of o, four of o''");
+    uint4 ov[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+    float4 o3v[4] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f),
+                     make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+    if (vrow) {
+      const uint4* orow = reinterpret_cast<const uint4*>(
+          p.o + 2 * ((int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)row * p.o_sl));
+      ov[0] = __ldg(orow + 2 * wg);
+      ov[1] = __ldg(orow + 2 * wg + 1);
+      if (p.o32) {
+        const float4* o32row = reinterpret_cast<const float4*>(p.o32 + (rb + row) * kD) + 4 * wg;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) o3v[j] = __ldg(o32row + j);
+      }
+    }
+    bool ok = warp_wait(BAR(B_Q), 0, p.status);
     float dh = 0.f;
     if (ok && vrow) {
-      const char* orow = p.o + 2 * ((int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)row * p.o_sl);
-      const float* o32row = p.o32 ? p.o32 + (rb + row) * kD : nullptr;
+      const float* o3 = reinterpret_cast<const float*>(o3v);
 #pragma unroll
-      for (int q = 0; q < NCOL / 8; ++q) {
-        const int chunk = wg * (NCOL / 8) + q;
+      for (int q = 0; q < 2; ++q) {
+        const int chunk = wg * 2 + q;
         const uint4 dv = *reinterpret_cast<const uint4*>(gbase + OFF_DO + sw128_off(r, chunk));
-        const uint4 ov = *reinterpret_cast<const uint4*>(orow + chunk * 16);
-        const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w}, ow[4] = {ov.x, ov.y, ov.z, ov.w};
+        const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w}, ow[4] = {ov[q].x, ov[q].y, ov[q].z, ov[q].w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int d = chunk * 8 + 2 * i + e;
             float o = e ? unpack_hi<kHalf>(ow[i]) : unpack_lo<kHalf>(ow[i]);
-            if (o32row) {
-              const float o3 = o32row[d];
-              o = (fabsf(o3 - o) <= 3.0517578125e-05f * fabsf(o)) ? o : o3;
+            if (p.o32) {
+              const float o32 = o3[q * 8 + 2 * i + e];
+              o = (fabsf(o32 - o) <= 3.0517578125e-05f * fabsf(o)) ? o : o32;
             }
             const float dd = e ? unpack_hi<kHalf>(dw[i]) : unpack_lo<kHalf>(dw[i]);
             dh = fmaf(o, dd, dh);
