@@ -106,8 +106,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
   using namespace dqk;
   extern __shared__ uint8_t smem_raw[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int qt = p.ntq128 - 1 - (int)blockIdx.x;
-  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  int bh, rank;
+  tile_order(p.ntq128, p.B * p.H, bh, rank);
+  const int qt = p.ntq128 - 1 - rank;                // heaviest query tiles first
+  const int b = bh / p.H, h = bh % p.H;
   const int L = p.L;
   const int m0 = qt * 128;
   const int ndiag = (m0 + 64 < L) ? 2 : 1;
@@ -517,8 +519,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
   using namespace dkv;
   extern __shared__ uint8_t smem_raw[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int kt = (int)blockIdx.x;                    // early key tiles carry the most work
-  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  int bh, kt;
+  tile_order(p.ntq128, p.B * p.H, bh, kt);           // early key tiles carry the most work
+  const int b = bh / p.H, h = bh % p.H;
   const int L = p.L;
   const int n0 = kt * 128;
   const int ntiles = (L - n0 + 63) / 64;             // query tiles m0 = n0 + 64 n < L

@@ -39,6 +39,26 @@ __device__ __forceinline__ uint32_t tmem_addr(uint32_t base, int warp_quarter, i
   return base + ((uint32_t)(warp_quarter * 32) << 16) + (uint32_t)col;
 }
 
+// Work order of the attention grids (launched as (ntile, B*H) blocks, dispatched in linear order):
+// heads are taken in groups of 16, and within a group every head's heaviest tile goes out before any
+// lighter one. Light tiles then finish the grid (a short last wave), while at any time only about one
+// group's K/V/B~ tiles (16 heads, ~22 MB at L = 4096) are live in L2. rank 0 is the heaviest tile.
+__device__ __forceinline__ void tile_order(int ntile, int BH, int& bh, int& rank) {
+  constexpr int GH = 16;
+  const int lin = (int)blockIdx.x + (int)gridDim.x * (int)blockIdx.y;
+  const int full = BH / GH, per = GH * ntile;
+  const int g = lin / per;
+  if (g < full) {
+    const int k = lin - g * per;
+    rank = k / GH;
+    bh = g * GH + k % GH;
+  } else {
+    const int rem = BH - full * GH, k = lin - full * per;
+    rank = k / rem;
+    bh = full * GH + k % rem;
+  }
+}
+
 // Warp-uniform bounded wait used by the compute warps.
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int32_t* status) {
   const bool ok = mbar_wait(bar, parity, status);

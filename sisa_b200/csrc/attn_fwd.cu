@@ -54,8 +54,10 @@ template <bool kHalf>
 __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant__ FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int qt = p.ntq - 1 - (int)blockIdx.x;      // heaviest query tiles first
-  const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
+  int bh, rank;
+  tile_order(p.ntq, p.B * p.H, bh, rank);
+  const int qt = p.ntq - 1 - rank;                 // heaviest query tiles first
+  const int b = bh / p.H, h = bh % p.H;
   const int L = p.L;
   const int m0 = qt * BM;
   const int ndiag = (m0 + BN < L) ? 2 : 1;
