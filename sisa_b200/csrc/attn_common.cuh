@@ -39,13 +39,12 @@ __device__ __forceinline__ uint32_t tmem_addr(uint32_t base, int warp_quarter, i
   return base + ((uint32_t)(warp_quarter * 32) << 16) + (uint32_t)col;
 }
 
-// Work order of the attention grids (launched as (ntile, B*H) blocks, dispatched in linear order):
-// heads are taken in groups of 16, and within a group every head's heaviest tile goes out before any
-// lighter one. Light tiles then finish the grid (a short last wave), while at any time only about one
-// group's K/V/B~ tiles (16 heads, ~22 MB at L = 4096) are live in L2. rank 0 is the heaviest tile.
-__device__ __forceinline__ void tile_order(int ntile, int BH, int& bh, int& rank) {
+// Work order of the attention kernels: heads are taken in groups of 16, and within a group every
+// head's heaviest tile goes out before any lighter one. Light tiles then finish the kernel (a short
+// last wave), while at any time only about one group's K/V/B~ tiles (16 heads, ~22 MB at L = 4096) are
+// live in L2. Maps the linear work index to (bh, rank); rank 0 is the heaviest tile.
+__device__ __forceinline__ void tile_order_lin(int lin, int ntile, int BH, int& bh, int& rank) {
   constexpr int GH = 16;
-  const int lin = (int)blockIdx.x + (int)gridDim.x * (int)blockIdx.y;
   const int full = BH / GH, per = GH * ntile;
   const int g = lin / per;
   if (g < full) {
@@ -57,6 +56,11 @@ __device__ __forceinline__ void tile_order(int ntile, int BH, int& bh, int& rank
     rank = k / rem;
     bh = full * GH + k % rem;
   }
+}
+
+// The same order for a grid of (ntile, B*H) blocks, dispatched in linear order.
+__device__ __forceinline__ void tile_order(int ntile, int BH, int& bh, int& rank) {
+  tile_order_lin((int)blockIdx.x + (int)gridDim.x * (int)blockIdx.y, ntile, BH, bh, rank);
 }
 
 // Warp-uniform bounded wait used by the compute warps.
