@@ -5,11 +5,13 @@
 //   s_j = q.k_j / 8 + lam_h exp(min(g_q - g_j, 0)) (c.b~_j) + (F_q - F_j),   y = sum_j softmax(s)_j v_j.
 //
 // HBM-bound: per cached key and head it reads k (128 B), v (128 B), b~ (64 B), g and F (8 B).
-// Split-K over the key axis: grid (splits, B*H); each CTA (256 threads) walks its key range in chunks
-// of 256 keys - phase 1 scores four keys per warp step with eight lanes per key (each step reads whole
-// 128-byte k rows and 64-byte b~ rows, a 3-step shuffle finishes the dot products), phase 2 the chunk
-// maximum, phase 3 p = 2^(x - m), phase 4 every warp accumulates p v over its keys with one lane per pair
-// of head dimensions (coalesced 128-byte v rows). A second kernel merges the splits' (m, l, acc).
+// Split-K over the key axis: grid (splits, B*H) of 256-thread CTAs. Every warp runs its own online
+// softmax over groups of four keys: eight lanes per key, each lane holding one 16-byte slice (8 head
+// dims) of the key's k, v and b~ rows, so one warp step reads four whole k and v rows (512 bytes each,
+// coalesced) and the v loads of a step travel with its k loads. A 3-step shuffle finishes each dot
+// product, the running maximum is rescaled lazily (only when a key exceeds it by more than 2^8), and
+// each lane accumulates p v over its 8 head dims. There is no block-wide barrier in the key loop; the
+// eight warps' (m, l, acc) are merged once at the end, and a second kernel merges the splits.
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <mutex>
@@ -20,7 +22,7 @@
 namespace sisa {
 namespace dec {
 
-constexpr int NT = 256;          // threads per CTA = keys per chunk
+constexpr int NT = 256;          // threads per CTA
 constexpr int NW = NT / 32;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -40,7 +42,7 @@ __device__ __forceinline__ void load_row(const char* p, int n16, float* out) {
 }
 
 template <bool kHalf>
-__global__ void __launch_bounds__(NT) decode_split_kernel(DecodeParams p) {
+__global__ void __launch_bounds__(NT, 4) decode_split_kernel(DecodeParams p) {
   const int split = blockIdx.x, bh = blockIdx.y;
   const int b = bh / p.H, h = bh % p.H;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -48,13 +50,11 @@ __global__ void __launch_bounds__(NT) decode_split_kernel(DecodeParams p) {
   const int j_begin = split * per;
   const int j_end = min(p.N, j_begin + per);
 
-  __shared__ float s_x[NT];
-  __shared__ float s_red[NW];
+  __shared__ float s_m[NW], s_l[NW];
   __shared__ float s_acc[NW][64];
-  __shared__ float s_l[NW];
 
-  // this lane's slices of the query row: lanes are grouped 8 per key, lane part p holds head dims
-  // [8p, 8p + 8) of q and, for p < 4, state dims [8p, 8p + 8) of c
+  // lanes are grouped eight per key: sub = which of the step's four keys, part = 16-byte slice, i.e. head
+  // dims [8 part, 8 part + 8) of q, k and v and, for part < 4, state dims [8 part, 8 part + 8) of c and b~
   const int sub = lane >> 3, part = lane & 7;
   float q8[8], c8[8];
   {
@@ -81,85 +81,93 @@ __global__ void __launch_bounds__(NT) decode_split_kernel(DecodeParams p) {
   const float* gbase = p.g + (int64_t)bh * p.gf_stride;
   const float* fbase = p.f ? p.f + (int64_t)bh * p.gf_stride : nullptr;
 
-  float m_run = -INFINITY;       // running maximum (log2 units), identical in every thread
-  float acc0 = 0.f, acc1 = 0.f;  // this lane's two head dims of the warp's partial p.v
-  float lsum = 0.f;              // warp's partial sum of p (kept by every lane)
-  for (int base = j_begin; base < j_end; base += NT) {
-    // ---- phase 1: warp w scores keys [base + 32w, base + 32w + 32), 4 keys per step, 8 lanes per key;
-    //      each step reads four whole 128-byte k rows and 64-byte b~ rows (coalesced)
+  float m_ref = -INFINITY;        // this warp's reference maximum (log2 units)
+  float acc[8];                   // this lane's 8 head dims of the warp's sum of p v (its key sub-group)
+#pragma unroll
+  for (int d = 0; d < 8; ++d) acc[d] = 0.f;
+  float lsum = 0.f;               // sum of p over this lane's sub-group keys
+  // warp w takes the groups of four keys w, w + 8, w + 16, ... of the split
 #pragma unroll 2
-    for (int it = 0; it < 8; ++it) {
-      const int kk = warp * 32 + it * 4 + sub;
-      const int j = base + kk;
-      const bool ok = j < j_end;
-      const int jj = ok ? j : j_begin;
-      const uint4 kv = reinterpret_cast<const uint4*>(kbase + 2 * (int64_t)jj * p.k_sl)[part];
-      uint4 bv = make_uint4(0, 0, 0, 0);
-      if (part < 4) bv = reinterpret_cast<const uint4*>(bbase + 2 * (int64_t)jj * p.b_sl)[part];
-      const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
-      float qk = 0.f, cb = 0.f;
+  for (int j0 = j_begin + 4 * warp; j0 < j_end; j0 += 4 * NW) {
+    const int j = j0 + sub;
+    const bool ok = j < j_end;
+    const int jj = ok ? j : j_begin;
+    const uint4 kv = __ldg(reinterpret_cast<const uint4*>(kbase + 2 * (int64_t)jj * p.k_sl) + part);
+    const uint4 vv = __ldg(reinterpret_cast<const uint4*>(vbase + 2 * (int64_t)jj * p.v_sl) + part);
+    uint4 bv = make_uint4(0, 0, 0, 0);
+    if (part < 4) bv = __ldg(reinterpret_cast<const uint4*>(bbase + 2 * (int64_t)jj * p.b_sl) + part);
+    const float gj = __ldg(gbase + jj);
+    const float fj = fbase ? __ldg(fbase + jj) : 0.f;
+    const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+    float qk = 0.f, cb = 0.f;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        qk = fmaf(q8[2 * e], unpack_lo<kHalf>(kw[e]), qk);
-        qk = fmaf(q8[2 * e + 1], unpack_hi<kHalf>(kw[e]), qk);
-        cb = fmaf(c8[2 * e], unpack_lo<kHalf>(bw[e]), cb);
-        cb = fmaf(c8[2 * e + 1], unpack_hi<kHalf>(bw[e]), cb);
-      }
-      const float gj = gbase[jj];
-      const float fj = fbase ? fbase[jj] : 0.f;
-      const float dec = exp2f(fminf((gq - gj) * kLog2e, 0.f));
-      float part_x = fmaf(qk, c1, lam2 * (dec * cb));
-      part_x += __shfl_xor_sync(0xffffffffu, part_x, 1);
-      part_x += __shfl_xor_sync(0xffffffffu, part_x, 2);
-      part_x += __shfl_xor_sync(0xffffffffu, part_x, 4);
-      if (part == 0) s_x[kk] = ok ? fmaf(fq - fj, kLog2e, part_x) : -INFINITY;
+    for (int e = 0; e < 4; ++e) {
+      qk = fmaf(q8[2 * e], unpack_lo<kHalf>(kw[e]), qk);
+      qk = fmaf(q8[2 * e + 1], unpack_hi<kHalf>(kw[e]), qk);
+      cb = fmaf(c8[2 * e], unpack_lo<kHalf>(bw[e]), cb);
+      cb = fmaf(c8[2 * e + 1], unpack_hi<kHalf>(bw[e]), cb);
     }
-    __syncthreads();
-    const float x = s_x[tid];
-    // ---- phase 2: chunk maximum
-    float mx = x;
+    const float dec = exp2f(fminf((gq - gj) * kLog2e, 0.f));
+    float x = fmaf(qk, c1, lam2 * (dec * cb));
+    x += __shfl_xor_sync(0xffffffffu, x, 1);
+    x += __shfl_xor_sync(0xffffffffu, x, 2);
+    x += __shfl_xor_sync(0xffffffffu, x, 4);
+    x = ok ? fmaf(fq - fj, kLog2e, x) : -INFINITY;
+    // step maximum over the four keys; rescale only when it exceeds the reference by more than 2^8
+    float mx = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 8));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    if (mx > m_ref + 8.f) {
+      const float corr = (m_ref == -INFINITY) ? 0.f : exp2f(m_ref - mx);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if (lane == 0) s_red[warp] = mx;
-    __syncthreads();
-    mx = s_red[0];
-#pragma unroll
-    for (int w = 1; w < NW; ++w) mx = fmaxf(mx, s_red[w]);
-    const float m_new = fmaxf(m_run, mx);
-    const float corr = (m_run == -INFINITY) ? 0.f : exp2f(m_run - m_new);
-    m_run = m_new;
-    // ---- phase 3/4: p and p v (warp w takes keys w, w+8, ... of the chunk)
-    acc0 *= corr;
-    acc1 *= corr;
-    lsum *= corr;
-    const int nk = min(NT, j_end - base);
-#pragma unroll 8
-    for (int t = warp; t < nk; t += NW) {
-      const float pj = exp2f(s_x[t] - m_new);
-      const uint32_t vv = *reinterpret_cast<const uint32_t*>(vbase + 2 * ((int64_t)(base + t) * p.v_sl + 2 * lane));
-      acc0 = fmaf(pj, unpack_lo<kHalf>(vv), acc0);
-      acc1 = fmaf(pj, unpack_hi<kHalf>(vv), acc1);
-      lsum += pj;
+      for (int d = 0; d < 8; ++d) acc[d] *= corr;
+      lsum *= corr;
+      m_ref = mx;
     }
-    __syncthreads();    // s_x / s_red are rewritten by the next chunk
+    const float pj = ok ? exp2f(x - m_ref) : 0.f;
+    const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      acc[2 * e] = fmaf(pj, unpack_lo<kHalf>(vw[e]), acc[2 * e]);
+      acc[2 * e + 1] = fmaf(pj, unpack_hi<kHalf>(vw[e]), acc[2 * e + 1]);
+    }
+    lsum += pj;
   }
-  // ---- merge the warps' partials and write this split's (m, l, acc[64])
-  s_acc[warp][2 * lane] = acc0;
-  s_acc[warp][2 * lane + 1] = acc1;
-  if (lane == 0) s_l[warp] = lsum;
+  // ---- the warp's sums over its four key sub-groups (all lanes of a sub-group hold the same lsum)
+#pragma unroll
+  for (int d = 0; d < 8; ++d) {
+    acc[d] += __shfl_xor_sync(0xffffffffu, acc[d], 8);
+    acc[d] += __shfl_xor_sync(0xffffffffu, acc[d], 16);
+  }
+  lsum += __shfl_xor_sync(0xffffffffu, lsum, 8);
+  lsum += __shfl_xor_sync(0xffffffffu, lsum, 16);
+  if (sub == 0) {
+#pragma unroll
+    for (int d = 0; d < 8; ++d) s_acc[warp][8 * part + d] = acc[d];
+  }
+  if (lane == 0) { s_m[warp] = m_ref; s_l[warp] = lsum; }
   __syncthreads();
+  // ---- merge the warps (rescaled to their common maximum) and write this split's (m, l, acc[64])
+  float m = s_m[0];
+#pragma unroll
+  for (int w = 1; w < NW; ++w) m = fmaxf(m, s_m[w]);
   float* out = p.ws + ((int64_t)split * p.B * p.H + bh) * 66;
   if (tid < 64) {
     float a = 0.f;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) a += s_acc[w][tid];
+    for (int w = 0; w < NW; ++w) {
+      const float sc = (s_m[w] == -INFINITY) ? 0.f : exp2f(s_m[w] - m);
+      a = fmaf(s_acc[w][tid], sc, a);
+    }
     out[2 + tid] = a;
   }
   if (tid == 0) {
     float l = 0.f;
 #pragma unroll
-    for (int w = 0; w < NW; ++w) l += s_l[w];
-    out[0] = m_run;
+    for (int w = 0; w < NW; ++w) {
+      const float sc = (s_m[w] == -INFINITY) ? 0.f : exp2f(s_m[w] - m);
+      l = fmaf(s_l[w], sc, l);
+    }
+    out[0] = m;
     out[1] = l;
   }
 }
@@ -191,8 +199,10 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(DecodeParams p) {
 
 }  // namespace dec
 
+// Splits of the key axis: about eight waves of the split kernel at four 256-thread CTAs per SM (so the
+// last, partial wave is a small share), at least 256 keys per split, at most 64 splits.
 int decode_splits(int64_t B, int64_t H, int64_t N) {
-  const int64_t target = 148 * 8;
+  const int64_t target = 148 * 4 * 8;
   const int64_t bh = B * H;
   int64_t s = (target + bh - 1) / bh;
   const int64_t maxs = (N + dec::NT - 1) / dec::NT;
