@@ -434,16 +434,18 @@ def run_lce(args):
     torch.cuda.reset_peak_memory_stats()
     s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     k = max(3, min(args.steps, 30))
-    s_.record()
-    for _ in range(k):
-        step()
-    e_.record()
-    torch.cuda.synchronize()
+    with Clocks(0) as clk:
+        s_.record()
+        for _ in range(k):
+            step()
+        e_.record()
+        torch.cuda.synchronize()
     ms = s_.elapsed_time(e_) / k
     peak = torch.cuda.max_memory_allocated() - base
     print(json.dumps({"metric": "linear-CE fwd+bwd tokens/s (cfg2)", "value": round(N / (ms * 1e-3), 1),
                       "unit": "tokens/s", "ms_per_step": round(ms, 3), "tflops": round(6 * N * V * D / (ms * 1e9), 1),
-                      "peak_mem_mb": round(peak / 2**20, 1), "steps": k, "config": {"N": N, "D": D, "V": V}}))
+                      "peak_mem_mb": round(peak / 2**20, 1), "steps": k, "config": {"N": N, "D": D, "V": V},
+                      "clocks": clk.summary()}))
 
 
 def run_decode(args):
@@ -476,12 +478,13 @@ def run_decode(args):
             nxt = logits.float().argmax(-1)
         torch.cuda.synchronize()
         n = S - 3
-        s_.record()
-        for _ in range(n):
-            logits = model(nxt.unsqueeze(1), cache=cache, logits_to_keep=1).logits[:, -1]
-            nxt = logits.float().argmax(-1)
-        e_.record()
-        torch.cuda.synchronize()
+        with Clocks(0) as clk:
+            s_.record()
+            for _ in range(n):
+                logits = model(nxt.unsqueeze(1), cache=cache, logits_to_keep=1).logits[:, -1]
+                nxt = logits.float().argmax(-1)
+            e_.record()
+            torch.cuda.synchronize()
         step_ms = s_.elapsed_time(e_) / n
     L_avg = P + 3 + n / 2
     per_tok = cfg.n_layer * cfg.n_head * (64 * 2 * 2 + 32 * 2 + 8)   # k, v, b~ (bf16) + g, F (fp32)
@@ -491,7 +494,8 @@ def run_decode(args):
                       "prefill_tokens_s": round(Bd * P / (prefill_ms * 1e-3), 1), "prefill_ms": round(prefill_ms, 1),
                       "decode_steps_timed": n, "cache_bytes_per_step": int(cache_bytes),
                       "hbm_gbs": round((cache_bytes + weight_bytes) / (step_ms * 1e-3) / 1e9, 1),
-                      "config": {"batch": Bd, "prompt": P, "new_tokens": S, "model": "sisa-152m"}}))
+                      "config": {"batch": Bd, "prompt": P, "new_tokens": S, "model": "sisa-152m"},
+                      "clocks": clk.summary()}))
 
 
 def run_reference(args):
