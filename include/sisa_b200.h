@@ -95,8 +95,8 @@ int sisa_pack_positions(const float* g, int64_t g_sb, int64_t g_sh, int64_t g_sl
  * q, k, v: (B, H, L, 64) views in `dtype`; c, b: (B, H, L, 32) views in `dtype`.
  * pos: (B, H, 4, Lp) planes from sisa_prep_fwd / sisa_pack_positions. lam: (H,) fp32.
  * o: (B, H, L, 64) view in `dtype`. lse: (B, H, L) fp32 contiguous, log2 units.
- * o32: (B, H, L, 64) fp32 contiguous self-normalised output for the exact-delta backward,
- *   or NULL when no backward follows. All views: 16-byte aligned rows, strides multiple of 8. */
+ * o32: (B, H, L, 64) fp32 contiguous o'' for the exact-delta backward (the self-normalised output,
+ *   already snapped to o where the two agree to 2^-15), or NULL when no backward follows. All views: 16-byte aligned rows, strides multiple of 8. */
 int sisa_attn_fwd(const sisa_view4* q, const sisa_view4* k, const sisa_view4* v,
                   const sisa_view4* c, const sisa_view4* b, const float* pos, const float* lam,
                   int64_t B, int64_t H, int64_t L, int dtype,

@@ -228,22 +228,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
     const float c1 = kScale * kLOG2E;
     const float lse = vrow ? p.lse[rb + row] : INFINITY;
     float* red = reinterpret_cast<float*>(gbase + OFF_RED);
-    // delta'' = do . o'' over this warpgroup's NCOL head dims (o'' snaps to the DT output where they agree
-    // to 2^-15, attention.py:341-350), combined across the warpgroups. The o and o'' row slices are
-    // loaded (16-byte, non-coherent) before waiting for the dO tile, so both latencies overlap.
+    // delta'' = do . o'' over this warpgroup's NCOL head dims, combined across the warpgroups. o'' comes
+    // from the forward already snapped to the rounded output (attention.py:341-350); without it, o'' = o.
+    // The row slices are loaded (16-byte, non-coherent) before waiting for the dO tile, so both
+    // latencies overlap.
     static_assert(NCOL == 16, "two 16-byte chunks of o, four of o''");
     uint4 ov[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
     float4 o3v[4] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f),
                      make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
     if (vrow) {
-      const uint4* orow = reinterpret_cast<const uint4*>(
-          p.o + 2 * ((int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)row * p.o_sl));
-      ov[0] = __ldg(orow + 2 * wg);
-      ov[1] = __ldg(orow + 2 * wg + 1);
       if (p.o32) {
         const float4* o32row = reinterpret_cast<const float4*>(p.o32 + (rb + row) * kD) + 4 * wg;
 #pragma unroll
         for (int j = 0; j < 4; ++j) o3v[j] = __ldg(o32row + j);
+      } else {
+        const uint4* orow = reinterpret_cast<const uint4*>(
+            p.o + 2 * ((int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)row * p.o_sl));
+        ov[0] = __ldg(orow + 2 * wg);
+        ov[1] = __ldg(orow + 2 * wg + 1);
       }
     }
     bool ok = warp_wait(BAR(B_Q), 0, p.status);
@@ -259,11 +261,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
         for (int i = 0; i < 4; ++i) {
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            float o = e ? unpack_hi<kHalf>(ow[i]) : unpack_lo<kHalf>(ow[i]);
-            if (p.o32) {
-              const float o32 = o3[q * 8 + 2 * i + e];
-              o = (fabsf(o32 - o) <= 3.0517578125e-05f * fabsf(o)) ? o : o32;
-            }
+            const float o = p.o32 ? o3[q * 8 + 2 * i + e] : (e ? unpack_hi<kHalf>(ow[i]) : unpack_lo<kHalf>(ow[i]));
             const float dd = e ? unpack_hi<kHalf>(dw[i]) : unpack_lo<kHalf>(dw[i]);
             dh = fmaf(o, dd, dh);
           }
@@ -431,73 +429,72 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
       const float dstt = ptt * (za * x0 - wa) / ssum;
       const float dl_row = xa + (dl - tt) * ya;
       const float dd = tt - dl;
-      if (ok && !warp_wait(BAR(B_ACC), 0, p.status)) ok = false;
-      if (ok) {
-        tc_fence_after();
+      if (vrow) {
+        // the dkv kernel's per-query records: F log2e - lse, and the negated delta terms it adds
+        float* rst = p.rstat + (int64_t)bh * 4 * p.Lp + row;
+        rst[0] = filse;
+        rst[p.Lp] = -dl;
+        rst[2 * p.Lp] = -dd;
+        rst[3 * p.Lp] = dstt;
+        p.rl[rb + row] = dl_row + dstt * xd;
+        p.rg[rb + row] = lam * dl_row;
+        p.rf[rb + row] = wa - za * dd;
+      }
+      redr[5] = dstt;                         // handed to the other warpgroups for their column slices
+    }
+    named_bar_sync(1, NCT);
+    const float dstt = redr[5];
+    if (ok && !warp_wait(BAR(B_ACC), 0, p.status)) ok = false;
+    if (ok) {
+      tc_fence_after();
+      // every warpgroup drains its slice of the accumulators:
+      // dq = scale * (sum_{j<t} dS^ k_j + DT(dS_tt) k_t), columns [16 wg, 16 wg + 16)
+      {
+        float acc[16];
+        tmem_ld16(tmem_addr(tbase, quarter, COL_DQ + 16 * wg), acc);
+        tmem_wait_ld();
         if (vrow) {
-          // the dkv kernel's per-query records: F log2e - lse, and the negated delta terms it adds
-          float* rst = p.rstat + (int64_t)bh * 4 * p.Lp + row;
-          rst[0] = filse;
-          rst[p.Lp] = -dl;
-          rst[2 * p.Lp] = -dd;
-          rst[3 * p.Lp] = dstt;
-          p.rl[rb + row] = dl_row + dstt * xd;
-          p.rg[rb + row] = lam * dl_row;
-          p.rf[rb + row] = wa - za * dd;
-        }
-        // dq = scale * (sum_{j<t} dS^ k_j + DT(dS_tt) k_t), 32 columns at a time (TMEM loads are warp-wide)
-        const float dsr = round_lp<kHalf>(dstt);
-        const char* krow = p.k + 2 * ((int64_t)b * p.k_sb + (int64_t)h * p.k_sh + (int64_t)(vrow ? row : 0) * p.k_sl);
-        uint4* dqrow = reinterpret_cast<uint4*>(p.dq + 2 * ((int64_t)b * p.dq_sb + (int64_t)h * p.dq_sh + (int64_t)(vrow ? row : 0) * p.dq_sl));
-#pragma unroll 1
-        for (int half = 0; half < 2; ++half) {
-          float acc[32];
-          tmem_ld32(tmem_addr(tbase, quarter, COL_DQ + half * 32), acc);
-          tmem_wait_ld();
-          if (vrow) {
+          const float dsr = round_lp<kHalf>(dstt);
+          const uint4* krow = reinterpret_cast<const uint4*>(
+              p.k + 2 * ((int64_t)b * p.k_sb + (int64_t)h * p.k_sh + (int64_t)row * p.k_sl));
+          uint4* dqrow = reinterpret_cast<uint4*>(p.dq + 2 * ((int64_t)b * p.dq_sb + (int64_t)h * p.dq_sh + (int64_t)row * p.dq_sl));
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const uint4 kv = reinterpret_cast<const uint4*>(krow)[half * 4 + q];
-              const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
-              uint32_t w[4];
+          for (int q = 0; q < 2; ++q) {
+            const uint4 kv = krow[2 * wg + q];
+            const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
+            uint32_t w[4];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const float a0 = fmaf(dsr, unpack_lo<kHalf>(kw[i]), acc[q * 8 + 2 * i]) * kScale;
-                const float a1 = fmaf(dsr, unpack_hi<kHalf>(kw[i]), acc[q * 8 + 2 * i + 1]) * kScale;
-                w[i] = pack2<kHalf>(a0, a1);
-              }
-              dqrow[half * 4 + q] = make_uint4(w[0], w[1], w[2], w[3]);
+            for (int i = 0; i < 4; ++i) {
+              const float a0 = fmaf(dsr, unpack_lo<kHalf>(kw[i]), acc[q * 8 + 2 * i]) * kScale;
+              const float a1 = fmaf(dsr, unpack_hi<kHalf>(kw[i]), acc[q * 8 + 2 * i + 1]) * kScale;
+              w[i] = pack2<kHalf>(a0, a1);
             }
+            dqrow[2 * wg + q] = make_uint4(w[0], w[1], w[2], w[3]);
           }
         }
-        // dc = dC_diag + lam rowf dC_off + DT(lam dS_tt) b_t   (fp32), 16 columns at a time
-        const float dsl = round_lp<kHalf>(dstt * lam);
-        const char* brow = p.bm + 2 * ((int64_t)b * p.b_sb + (int64_t)h * p.b_sh + (int64_t)(vrow ? row : 0) * p.b_sl);
-        float* dcrow = p.dc + ((int64_t)b * p.dc_sb + (int64_t)h * p.dc_sh + (int64_t)(vrow ? row : 0) * p.dc_sl);
-#pragma unroll 1
-        for (int half = 0; half < 2; ++half) {
-          float dco[16], dcd[16];
-          tmem_ld16(tmem_addr(tbase, quarter, COL_DCO + half * 16), dco);
-          tmem_ld16(tmem_addr(tbase, quarter, COL_DCD + half * 16), dcd);
-          tmem_wait_ld();
-          if (vrow) {
+      }
+      // dc = dC_diag + lam rowf dC_off + DT(lam dS_tt) b_t (fp32), columns [8 wg, 8 wg + 8)
+      {
+        float dco[8], dcd[8];
+        tmem_ld8(tmem_addr(tbase, quarter, COL_DCO + 8 * wg), dco);
+        tmem_ld8(tmem_addr(tbase, quarter, COL_DCD + 8 * wg), dcd);
+        tmem_wait_ld();
+        if (vrow) {
+          const float dsl = round_lp<kHalf>(dstt * lam);
+          const uint4 bv = reinterpret_cast<const uint4*>(
+              p.bm + 2 * ((int64_t)b * p.b_sb + (int64_t)h * p.b_sh + (int64_t)row * p.b_sl))[wg];
+          const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+          float4* dcrow = reinterpret_cast<float4*>(p.dc + ((int64_t)b * p.dc_sb + (int64_t)h * p.dc_sh + (int64_t)row * p.dc_sl));
+          float o[8];
 #pragma unroll
-            for (int q = 0; q < 2; ++q) {
-              const uint4 bv = reinterpret_cast<const uint4*>(brow)[half * 2 + q];
-              const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
-              float o[8];
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const int d = q * 8 + 2 * i;
-                const float d0 = (ndiag > 0 ? dcd[d] : 0.f) + (ntiles > ndiag ? rs * dco[d] : 0.f);
-                const float d1 = (ndiag > 0 ? dcd[d + 1] : 0.f) + (ntiles > ndiag ? rs * dco[d + 1] : 0.f);
-                o[2 * i] = fmaf(dsl, unpack_lo<kHalf>(bw[i]), d0);
-                o[2 * i + 1] = fmaf(dsl, unpack_hi<kHalf>(bw[i]), d1);
-              }
-              reinterpret_cast<float4*>(dcrow)[half * 4 + 2 * q] = make_float4(o[0], o[1], o[2], o[3]);
-              reinterpret_cast<float4*>(dcrow)[half * 4 + 2 * q + 1] = make_float4(o[4], o[5], o[6], o[7]);
-            }
+          for (int i = 0; i < 4; ++i) {
+            const float d0 = (ndiag > 0 ? dcd[2 * i] : 0.f) + (ntiles > ndiag ? rs * dco[2 * i] : 0.f);
+            const float d1 = (ndiag > 0 ? dcd[2 * i + 1] : 0.f) + (ntiles > ndiag ? rs * dco[2 * i + 1] : 0.f);
+            o[2 * i] = fmaf(dsl, unpack_lo<kHalf>(bw[i]), d0);
+            o[2 * i + 1] = fmaf(dsl, unpack_hi<kHalf>(bw[i]), d1);
           }
+          dcrow[2 * wg] = make_float4(o[0], o[1], o[2], o[3]);
+          dcrow[2 * wg + 1] = make_float4(o[4], o[5], o[6], o[7]);
         }
       }
     }
@@ -802,52 +799,50 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
     float* redr = red + r * (NWG * 2);
     if (wg > 0) { redr[wg * 2 + 0] = dgu; redr[wg * 2 + 1] = dfs; }
     named_bar_sync(1, NCT);
-    if (wg == 0) {
-#pragma unroll
-      for (int w = 1; w < NWG; ++w) { dgu += redr[w * 2 + 0]; dfs += redr[w * 2 + 1]; }
-      if (ok && !warp_wait(BAR(B_ACC), 0, p.status)) ok = false;
-      if (ok) {
-        tc_fence_after();
-        uint4* dkrow = reinterpret_cast<uint4*>(p.dk + 2 * ((int64_t)b * p.dk_sb + (int64_t)h * p.dk_sh + (int64_t)j * p.dk_sl));
-        uint4* dvrow = reinterpret_cast<uint4*>(p.dv + 2 * ((int64_t)b * p.dv_sb + (int64_t)h * p.dv_sh + (int64_t)j * p.dv_sl));
-        // dK and dV, 32 columns at a time (TMEM loads are warp-collective: every lane takes part)
+    if (ok && !warp_wait(BAR(B_ACC), 0, p.status)) ok = false;
+    if (ok) {
+      tc_fence_after();
+      // every warpgroup drains its slice of the accumulators: dK and dV columns [16 wg, 16 wg + 16),
+      // dB columns [8 wg, 8 wg + 8)
 #pragma unroll 1
-        for (int part = 0; part < 4; ++part) {
-          const int col = (part < 2 ? COL_DK : COL_DV) + (part & 1) * 32;
-          float acc[32];
-          tmem_ld32(tmem_addr(tbase, quarter, col), acc);
-          tmem_wait_ld();
-          const float sc = part < 2 ? kScale : 1.f;
-          uint4* dst = (part < 2 ? dkrow : dvrow) + (part & 1) * 4;
-          if (vcol) {
+      for (int part = 0; part < 2; ++part) {
+        float acc[16];
+        tmem_ld16(tmem_addr(tbase, quarter, (part == 0 ? COL_DK : COL_DV) + 16 * wg), acc);
+        tmem_wait_ld();
+        if (vcol) {
+          const float sc = part == 0 ? kScale : 1.f;
+          uint4* dst = part == 0
+              ? reinterpret_cast<uint4*>(p.dk + 2 * ((int64_t)b * p.dk_sb + (int64_t)h * p.dk_sh + (int64_t)j * p.dk_sl))
+              : reinterpret_cast<uint4*>(p.dv + 2 * ((int64_t)b * p.dv_sb + (int64_t)h * p.dv_sh + (int64_t)j * p.dv_sl));
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint32_t w4[4];
+          for (int q = 0; q < 2; ++q) {
+            uint32_t w4[4];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) w4[i] = pack2<kHalf>(acc[q * 8 + 2 * i] * sc, acc[q * 8 + 2 * i + 1] * sc);
-              dst[q] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-            }
+            for (int i = 0; i < 4; ++i) w4[i] = pack2<kHalf>(acc[q * 8 + 2 * i] * sc, acc[q * 8 + 2 * i + 1] * sc);
+            dst[2 * wg + q] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
           }
         }
-        {
-          float dbo[32], dbd[32];
-          tmem_ld32(tmem_addr(tbase, quarter, COL_DBO), dbo);
-          tmem_ld32(tmem_addr(tbase, quarter, COL_DBD), dbd);
-          tmem_wait_ld();
-          if (vcol) {
-            const bool has_off = ntiles > ndiag;
-            float* dbrow = p.db + ((int64_t)b * p.db_sb + (int64_t)h * p.db_sh + (int64_t)j * p.db_sl);
+      }
+      {
+        float dbo[8], dbd[8];
+        tmem_ld8(tmem_addr(tbase, quarter, COL_DBO + 8 * wg), dbo);
+        tmem_ld8(tmem_addr(tbase, quarter, COL_DBD + 8 * wg), dbd);
+        tmem_wait_ld();
+        if (vcol) {
+          const bool has_off = ntiles > ndiag;
+          float4* dbrow = reinterpret_cast<float4*>(p.db + ((int64_t)b * p.db_sb + (int64_t)h * p.db_sh + (int64_t)j * p.db_sl));
+          float o[8];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              float o[4];
-#pragma unroll
-              for (int i = 0; i < 4; ++i) o[i] = dbd[q * 4 + i] + (has_off ? rk * dbo[q * 4 + i] : 0.f);
-              reinterpret_cast<float4*>(dbrow)[q] = make_float4(o[0], o[1], o[2], o[3]);
-            }
-            p.dg[rb + j] = p.rg[rb + j] - lam * dgu;
-            if (p.dF) p.dF[rb + j] = p.rf[rb + j] - dfs;
-          }
+          for (int i = 0; i < 8; ++i) o[i] = dbd[i] + (has_off ? rk * dbo[i] : 0.f);
+          dbrow[2 * wg] = make_float4(o[0], o[1], o[2], o[3]);
+          dbrow[2 * wg + 1] = make_float4(o[4], o[5], o[6], o[7]);
         }
+      }
+      if (wg == 0 && vcol) {
+#pragma unroll
+        for (int w = 1; w < NWG; ++w) { dgu += redr[w * 2 + 0]; dfs += redr[w * 2 + 1]; }
+        p.dg[rb + j] = p.rg[rb + j] - lam * dgu;
+        if (p.dF) p.dF[rb + j] = p.rf[rb + j] - dfs;
       }
     }
   }

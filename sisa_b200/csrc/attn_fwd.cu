@@ -309,10 +309,19 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
           orow[q] = make_uint4(w[0], w[1], w[2], w[3]);
         }
         if (p.o32) {
+          // o'' for the exact-delta backward: the self-normalised fp32 output, snapped to the rounded
+          // output where the two agree to 2^-15 (attention.py:341-350 does this in the backward)
           float4* o32row = reinterpret_cast<float4*>(p.o32 + ((int64_t)bh * L + row) * kD);
 #pragma unroll
-          for (int q = 0; q < 16; ++q)
-            o32row[q] = make_float4(ov[4 * q] / lbs, ov[4 * q + 1] / lbs, ov[4 * q + 2] / lbs, ov[4 * q + 3] / lbs);
+          for (int q = 0; q < 16; ++q) {
+            float o3[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float o32 = ov[4 * q + i] / lbs, olp = round_lp<kHalf>(ov[4 * q + i] / ls);
+              o3[i] = (fabsf(o32 - olp) <= 3.0517578125e-05f * fabsf(olp)) ? olp : o32;
+            }
+            o32row[q] = make_float4(o3[0], o3[1], o3[2], o3[3]);
+          }
         }
         const float lse = ((m_ref == -INFINITY) ? 0.f : m_ref) + log2f(ls);
         p.lse[(int64_t)bh * L + row] = lse;
