@@ -30,6 +30,12 @@ struct BwdParams {
   CUtensorMap tm_k128, tm_v128, tm_b128, tm_q64, tm_do64, tm_c64;
   CUtensorMap tm_pos;    // (L, 4, B*H) fp32 planes, box (64, 4, 1)
   CUtensorMap tm_rstat;  // (L, 4, B*H) fp32 planes, box (64, 4, 1)
+  // dq kernel: o'' as (64, L, B*H) fp32, box (32, 128, 1), 128B swizzle; or, without o'', o as a
+  // (64, L, H, B) view, box (64, 128). dq (64, L, H, B) and dc (32, L, H, B) fp32, box rows 128,
+  // 128B swizzle, for the epilogue's bulk-tensor stores.
+  CUtensorMap tm_o, tm_dq, tm_dc;
+  // dkv kernel: dk, dv (64, L, H, B) and db (32, L, H, B) fp32, box rows 128, 128B swizzle (stores)
+  CUtensorMap tm_dk, tm_dv, tm_db;
   const float* pos;      // (B*H, 4, Lp) planes {g, F, rowf, colf}
   const float* lam;
   const char* q;  int64_t q_sb, q_sh, q_sl;
@@ -55,6 +61,8 @@ struct BwdParams {
   int has_f;
   int32_t* status;
 };
+
+static_assert(sizeof(BwdParams) <= 4096, "kernel parameter block");
 
 cudaError_t launch_attn_fwd(const FwdParams& p, int dtype, cudaStream_t st);
 cudaError_t launch_attn_bwd(const BwdParams& p, int dtype, cudaStream_t st);

@@ -52,13 +52,24 @@ constexpr uint32_t SZ_K = 64 * 128, SZ_V = 64 * 128, SZ_B = 64 * 64, SZ_POS = 64
 constexpr uint32_t SZ_STAGE = SZ_K + SZ_V + SZ_B + SZ_POS;   // 21504
 constexpr uint32_t OFF_Q = 0, OFF_DO = OFF_Q + SZ_Q, OFF_C = OFF_DO + SZ_DO, OFF_ST = OFF_C + SZ_C;
 constexpr uint32_t OFF_RED = OFF_ST + NST * SZ_STAGE;          // 128 rows x NWG x 8 floats
-constexpr uint32_t OFF_BAR = OFF_RED + 128 * NWG * 8 * 4;
+// o'' of the tile for delta'' (two 128-byte-swizzled boxes of 32 fp32 columns; o itself, when the
+// forward kept no o'', is one 64-column low-precision box)
+constexpr uint32_t SZ_OB = 128 * 128, OFF_O = OFF_RED + 128 * NWG * 8 * 4;
+// the tile's own key and B~ rows (k_t, b_t) for the diagonal terms of the epilogue
+constexpr uint32_t OFF_KR = OFF_O + 2 * SZ_OB, OFF_BR = OFF_KR + 128 * 128;
+constexpr uint32_t OFF_BAR = OFF_BR + 128 * 64;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
+// The epilogue stages dq (low precision, 128-byte rows) in the Q region and dc (fp32, 128-byte rows)
+// in the dO region for bulk-tensor stores; both are free once the last gradient UMMA has completed.
 // TMEM: S, U, dP per tile; dQ, dC_off, dC_diag accumulators; the bf16 operands dS and dS*cf of the
 // gradient UMMAs (two buffers of 2 x 32 columns, written by the compute warps, read as A from TMEM)
 constexpr int COL_S = 0, COL_U = 64, COL_DP = 128, COL_DQ = 192, COL_DCO = 256, COL_DCD = 288, COL_OPS = 320;
-constexpr int B_KVF = 0, B_KVE = 3, B_Q = 6, B_SUF = 7, B_SUE = 8, B_OPF = 9, B_OPE = 11, B_ACC = 13;
-static_assert(OFF_ST % 1024 == 0, "alignment");
+constexpr int B_KVF = 0, B_KVE = 3, B_Q = 6, B_SUF = 7, B_SUE = 8, B_OPF = 9, B_OPE = 11, B_ACC = 13, B_O = 14,
+              B_KR = 15;
+static_assert(OFF_ST % 1024 == 0 && OFF_O % 1024 == 0 && OFF_KR % 1024 == 0 && OFF_BR % 1024 == 0 &&
+                  SZ_STAGE % 1024 == 0, "swizzled tiles need 1024-byte alignment");
+static_assert(SMEM_BYTES <= 232448, "shared memory per block");
+static_assert(B_KR * 8 < 128, "barriers end below the TMEM slot");
 }  // namespace dqk
 
 // ----------------------------------------------------------------------------- dkv kernel layout
@@ -128,6 +139,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
     mbar_init(BAR(B_SUE), NCT);
     for (int i = 0; i < 2; ++i) { mbar_init(BAR(B_OPF + i), NCT); mbar_init(BAR(B_OPE + i), 1); }
     mbar_init(BAR(B_ACC), 1);
+    mbar_init(BAR(B_O), 1);
+    mbar_init(BAR(B_KR), 1);
     fence_barrier_init();
   }
   if (warp == WARP_MMA) { tmem_alloc(smem_u32(tmem_slot), TMEM_COLS); tmem_relinquish(); }
@@ -154,7 +167,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
         tma_load_4d(st + SZ_K, &p.tm_v64, BAR(B_KVF + s), 0, j0, h, b);
         tma_load_4d(st + SZ_K + SZ_V, &p.tm_b64, BAR(B_KVF + s), 0, j0, h, b);
         tma_load_3d(st + SZ_K + SZ_V + SZ_B, &p.tm_pos, BAR(B_KVF + s), j0, 0, bh);
+        if (n == 0) {
+          // o'' for delta'', behind the first key tile (the score GEMMs need that first)
+          if (p.o32) {
+            mbar_expect_tx(BAR(B_O), 2 * SZ_OB);
+            tma_load_3d(sbase + OFF_O, &p.tm_o, BAR(B_O), 0, m0, bh);
+            tma_load_3d(sbase + OFF_O + SZ_OB, &p.tm_o, BAR(B_O), 32, m0, bh);
+          } else {
+            mbar_expect_tx(BAR(B_O), SZ_OB);
+            tma_load_4d(sbase + OFF_O, &p.tm_o, BAR(B_O), 0, m0, h, b);
+          }
+        }
       }
+      // the tile's own key and B~ rows, needed only by the epilogue
+      mbar_expect_tx(BAR(B_KR), 128 * 128 + 128 * 64);
+      tma_load_4d(sbase + OFF_KR, &p.tm_k128, BAR(B_KR), 0, m0, h, b);
+      tma_load_4d(sbase + OFF_BR, &p.tm_b128, BAR(B_KR), 0, m0, h, b);
     }
   } else if (warp == WARP_MMA) {
     // score GEMMs S = Q K^T, U = C B~^T, dP = dO V^T of every key tile
@@ -230,41 +258,35 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
     float* red = reinterpret_cast<float*>(gbase + OFF_RED);
     // delta'' = do . o'' over this warpgroup's NCOL head dims, combined across the warpgroups. o'' comes
     // from the forward already snapped to the rounded output (attention.py:341-350); without it, o'' = o.
-    // The row slices are loaded (16-byte, non-coherent) before waiting for the dO tile, so both
-    // latencies overlap.
-    static_assert(NCOL == 16, "two 16-byte chunks of o, four of o''");
-    uint4 ov[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-    float4 o3v[4] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f),
-                     make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
-    if (vrow) {
-      if (p.o32) {
-        const float4* o32row = reinterpret_cast<const float4*>(p.o32 + (rb + row) * kD) + 4 * wg;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) o3v[j] = __ldg(o32row + j);
-      } else {
-        const uint4* orow = reinterpret_cast<const uint4*>(
-            p.o + 2 * ((int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)row * p.o_sl));
-        ov[0] = __ldg(orow + 2 * wg);
-        ov[1] = __ldg(orow + 2 * wg + 1);
-      }
-    }
+    // Both arrive by TMA (o'' as two 128-byte-swizzled boxes of 32 fp32 columns), so the compute warps
+    // hold no registers on global loads while they wait.
+    static_assert(NCOL == 16, "two 16-byte chunks of dO / o, four of o''");
     bool ok = warp_wait(BAR(B_Q), 0, p.status);
+    ok = ok && warp_wait(BAR(B_O), 0, p.status);
     float dh = 0.f;
-    if (ok && vrow) {
-      const float* o3 = reinterpret_cast<const float*>(o3v);
+    if (ok) {
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
         const int chunk = wg * 2 + q;
         const uint4 dv = *reinterpret_cast<const uint4*>(gbase + OFF_DO + sw128_off(r, chunk));
-        const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w}, ow[4] = {ov[q].x, ov[q].y, ov[q].z, ov[q].w};
+        const uint32_t dw[4] = {dv.x, dv.y, dv.z, dv.w};
+        float o[8];
+        if (p.o32) {
+          // fp32 columns 8 chunk .. 8 chunk + 7: box chunk / 4, 16-byte chunks 2 (chunk % 4) and + 1
+          const uint8_t* ob = gbase + OFF_O + (chunk >> 2) * SZ_OB;
+          const float4 o0 = *reinterpret_cast<const float4*>(ob + sw128_off(r, 2 * (chunk & 3)));
+          const float4 o1 = *reinterpret_cast<const float4*>(ob + sw128_off(r, 2 * (chunk & 3) + 1));
+          o[0] = o0.x; o[1] = o0.y; o[2] = o0.z; o[3] = o0.w; o[4] = o1.x; o[5] = o1.y; o[6] = o1.z; o[7] = o1.w;
+        } else {
+          const uint4 ov = *reinterpret_cast<const uint4*>(gbase + OFF_O + sw128_off(r, chunk));
+          const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) { o[2 * i] = unpack_lo<kHalf>(ow[i]); o[2 * i + 1] = unpack_hi<kHalf>(ow[i]); }
+        }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const float o = p.o32 ? o3[q * 8 + 2 * i + e] : (e ? unpack_hi<kHalf>(ow[i]) : unpack_lo<kHalf>(ow[i]));
-            const float dd = e ? unpack_hi<kHalf>(dw[i]) : unpack_lo<kHalf>(dw[i]);
-            dh = fmaf(o, dd, dh);
-          }
+          dh = fmaf(o[2 * i], unpack_lo<kHalf>(dw[i]), dh);
+          dh = fmaf(o[2 * i + 1], unpack_hi<kHalf>(dw[i]), dh);
         }
       }
     }
@@ -445,32 +467,28 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
     named_bar_sync(1, NCT);
     const float dstt = redr[5];
     if (ok && !warp_wait(BAR(B_ACC), 0, p.status)) ok = false;
+    if (ok && !warp_wait(BAR(B_KR), 0, p.status)) ok = false;
     if (ok) {
       tc_fence_after();
-      // every warpgroup drains its slice of the accumulators:
+      // every warpgroup drains its slice of the accumulators into the staging tiles:
       // dq = scale * (sum_{j<t} dS^ k_j + DT(dS_tt) k_t), columns [16 wg, 16 wg + 16)
       {
         float acc[16];
         tmem_ld16(tmem_addr(tbase, quarter, COL_DQ + 16 * wg), acc);
         tmem_wait_ld();
-        if (vrow) {
-          const float dsr = round_lp<kHalf>(dstt);
-          const uint4* krow = reinterpret_cast<const uint4*>(
-              p.k + 2 * ((int64_t)b * p.k_sb + (int64_t)h * p.k_sh + (int64_t)row * p.k_sl));
-          uint4* dqrow = reinterpret_cast<uint4*>(p.dq + 2 * ((int64_t)b * p.dq_sb + (int64_t)h * p.dq_sh + (int64_t)row * p.dq_sl));
+        const float dsr = round_lp<kHalf>(dstt);
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const uint4 kv = krow[2 * wg + q];
-            const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
-            uint32_t w[4];
+        for (int q = 0; q < 2; ++q) {
+          const uint4 kv = *reinterpret_cast<const uint4*>(gbase + OFF_KR + sw128_off(r, 2 * wg + q));
+          const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w};
+          uint32_t w[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float a0 = fmaf(dsr, unpack_lo<kHalf>(kw[i]), acc[q * 8 + 2 * i]) * kScale;
-              const float a1 = fmaf(dsr, unpack_hi<kHalf>(kw[i]), acc[q * 8 + 2 * i + 1]) * kScale;
-              w[i] = pack2<kHalf>(a0, a1);
-            }
-            dqrow[2 * wg + q] = make_uint4(w[0], w[1], w[2], w[3]);
+          for (int i = 0; i < 4; ++i) {
+            const float a0 = fmaf(dsr, unpack_lo<kHalf>(kw[i]), acc[q * 8 + 2 * i]) * kScale;
+            const float a1 = fmaf(dsr, unpack_hi<kHalf>(kw[i]), acc[q * 8 + 2 * i + 1]) * kScale;
+            w[i] = pack2<kHalf>(a0, a1);
           }
+          st_shared_v4(sbase + OFF_Q + sw128_off(r, 2 * wg + q), w[0], w[1], w[2], w[3]);
         }
       }
       // dc = dC_diag + lam rowf dC_off + DT(lam dS_tt) b_t (fp32), columns [8 wg, 8 wg + 8)
@@ -479,24 +497,29 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
         tmem_ld8(tmem_addr(tbase, quarter, COL_DCO + 8 * wg), dco);
         tmem_ld8(tmem_addr(tbase, quarter, COL_DCD + 8 * wg), dcd);
         tmem_wait_ld();
-        if (vrow) {
-          const float dsl = round_lp<kHalf>(dstt * lam);
-          const uint4 bv = reinterpret_cast<const uint4*>(
-              p.bm + 2 * ((int64_t)b * p.b_sb + (int64_t)h * p.b_sh + (int64_t)row * p.b_sl))[wg];
-          const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
-          float4* dcrow = reinterpret_cast<float4*>(p.dc + ((int64_t)b * p.dc_sb + (int64_t)h * p.dc_sh + (int64_t)row * p.dc_sl));
-          float o[8];
+        const float dsl = round_lp<kHalf>(dstt * lam);
+        const uint4 bv = *reinterpret_cast<const uint4*>(gbase + OFF_BR + sw64_off(r, wg));
+        const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+        uint32_t o[8];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float d0 = (ndiag > 0 ? dcd[2 * i] : 0.f) + (ntiles > ndiag ? rs * dco[2 * i] : 0.f);
-            const float d1 = (ndiag > 0 ? dcd[2 * i + 1] : 0.f) + (ntiles > ndiag ? rs * dco[2 * i + 1] : 0.f);
-            o[2 * i] = fmaf(dsl, unpack_lo<kHalf>(bw[i]), d0);
-            o[2 * i + 1] = fmaf(dsl, unpack_hi<kHalf>(bw[i]), d1);
-          }
-          dcrow[2 * wg] = make_float4(o[0], o[1], o[2], o[3]);
-          dcrow[2 * wg + 1] = make_float4(o[4], o[5], o[6], o[7]);
+        for (int i = 0; i < 4; ++i) {
+          const float d0 = (ndiag > 0 ? dcd[2 * i] : 0.f) + (ntiles > ndiag ? rs * dco[2 * i] : 0.f);
+          const float d1 = (ndiag > 0 ? dcd[2 * i + 1] : 0.f) + (ntiles > ndiag ? rs * dco[2 * i + 1] : 0.f);
+          o[2 * i] = __float_as_uint(fmaf(dsl, unpack_lo<kHalf>(bw[i]), d0));
+          o[2 * i + 1] = __float_as_uint(fmaf(dsl, unpack_hi<kHalf>(bw[i]), d1));
         }
+        st_shared_v4(sbase + OFF_DO + sw128_off(r, 2 * wg), o[0], o[1], o[2], o[3]);
+        st_shared_v4(sbase + OFF_DO + sw128_off(r, 2 * wg + 1), o[4], o[5], o[6], o[7]);
       }
+      fence_proxy_async_smem();
+    }
+    // one thread stores both tiles (rows past L are clipped) and waits until they have been read
+    named_bar_sync(1, NCT);
+    if (tid == 0 && ok) {
+      tma_store_4d(&p.tm_dq, sbase + OFF_Q, 0, m0, h, b);
+      tma_store_4d(&p.tm_dc, sbase + OFF_DO, 0, m0, h, b);
+      bulk_commit();
+      bulk_wait_read0();
     }
   }
   tc_fence_before();
@@ -802,25 +825,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
     if (ok && !warp_wait(BAR(B_ACC), 0, p.status)) ok = false;
     if (ok) {
       tc_fence_after();
-      // every warpgroup drains its slice of the accumulators: dK and dV columns [16 wg, 16 wg + 16),
-      // dB columns [8 wg, 8 wg + 8)
+      // every warpgroup drains its slice of the accumulators into the staging tiles (the resident K and
+      // V tiles and the dSb buffers, all free once the last gradient UMMA has completed):
+      // dK and dV columns [16 wg, 16 wg + 16), dB columns [8 wg, 8 wg + 8)
 #pragma unroll 1
       for (int part = 0; part < 2; ++part) {
         float acc[16];
         tmem_ld16(tmem_addr(tbase, quarter, (part == 0 ? COL_DK : COL_DV) + 16 * wg), acc);
         tmem_wait_ld();
-        if (vcol) {
-          const float sc = part == 0 ? kScale : 1.f;
-          uint4* dst = part == 0
-              ? reinterpret_cast<uint4*>(p.dk + 2 * ((int64_t)b * p.dk_sb + (int64_t)h * p.dk_sh + (int64_t)j * p.dk_sl))
-              : reinterpret_cast<uint4*>(p.dv + 2 * ((int64_t)b * p.dv_sb + (int64_t)h * p.dv_sh + (int64_t)j * p.dv_sl));
+        const float sc = part == 0 ? kScale : 1.f;
+        const uint32_t dst = sbase + (part == 0 ? OFF_K : OFF_V);
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            uint32_t w4[4];
+        for (int q = 0; q < 2; ++q) {
+          uint32_t w4[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) w4[i] = pack2<kHalf>(acc[q * 8 + 2 * i] * sc, acc[q * 8 + 2 * i + 1] * sc);
-            dst[2 * wg + q] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-          }
+          for (int i = 0; i < 4; ++i) w4[i] = pack2<kHalf>(acc[q * 8 + 2 * i] * sc, acc[q * 8 + 2 * i + 1] * sc);
+          st_shared_v4(dst + sw128_off(r, 2 * wg + q), w4[0], w4[1], w4[2], w4[3]);
         }
       }
       {
@@ -828,22 +848,29 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
         tmem_ld8(tmem_addr(tbase, quarter, COL_DBO + 8 * wg), dbo);
         tmem_ld8(tmem_addr(tbase, quarter, COL_DBD + 8 * wg), dbd);
         tmem_wait_ld();
-        if (vcol) {
-          const bool has_off = ntiles > ndiag;
-          float4* dbrow = reinterpret_cast<float4*>(p.db + ((int64_t)b * p.db_sb + (int64_t)h * p.db_sh + (int64_t)j * p.db_sl));
-          float o[8];
+        const bool has_off = ntiles > ndiag;
+        uint32_t o[8];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) o[i] = dbd[i] + (has_off ? rk * dbo[i] : 0.f);
-          dbrow[2 * wg] = make_float4(o[0], o[1], o[2], o[3]);
-          dbrow[2 * wg + 1] = make_float4(o[4], o[5], o[6], o[7]);
-        }
+        for (int i = 0; i < 8; ++i) o[i] = __float_as_uint(dbd[i] + (has_off ? rk * dbo[i] : 0.f));
+        st_shared_v4(sbase + OFF_DSB + sw128_off(r, 2 * wg), o[0], o[1], o[2], o[3]);
+        st_shared_v4(sbase + OFF_DSB + sw128_off(r, 2 * wg + 1), o[4], o[5], o[6], o[7]);
       }
+      fence_proxy_async_smem();
       if (wg == 0 && vcol) {
 #pragma unroll
         for (int w = 1; w < NWG; ++w) { dgu += redr[w * 2 + 0]; dfs += redr[w * 2 + 1]; }
         p.dg[rb + j] = p.rg[rb + j] - lam * dgu;
         if (p.dF) p.dF[rb + j] = p.rf[rb + j] - dfs;
       }
+    }
+    // one thread stores the three tiles (rows past L are clipped) and waits until they have been read
+    named_bar_sync(1, NCT);
+    if (tid == 0 && ok) {
+      tma_store_4d(&p.tm_dk, sbase + OFF_K, 0, n0, h, b);
+      tma_store_4d(&p.tm_dv, sbase + OFF_V, 0, n0, h, b);
+      tma_store_4d(&p.tm_db, sbase + OFF_DSB, 0, n0, h, b);
+      bulk_commit();
+      bulk_wait_read0();
     }
   }
   tc_fence_before();

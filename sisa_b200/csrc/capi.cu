@@ -87,6 +87,21 @@ int map_records(CUtensorMap* m, const void* ptr, int64_t BH, int64_t L, int64_t 
   return SISA_OK;
 }
 
+// Dense (B*H, L, X) rows as a (X, L, B*H) map, box (box_x, rows, 1).
+int map_rows3(CUtensorMap* m, const void* ptr, int64_t BH, int64_t L, int64_t X, int elem_bytes,
+              CUtensorMapDataType dt, int box_x, int rows, CUtensorMapSwizzle sw, const char* name) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(SISA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[3] = {(cuuint64_t)X, (cuuint64_t)L, (cuuint64_t)BH};
+  cuuint64_t strides[2] = {(cuuint64_t)(X * elem_bytes), (cuuint64_t)(X * elem_bytes * L)};
+  cuuint32_t box[3] = {(cuuint32_t)box_x, (cuuint32_t)rows, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = enc(m, dt, 3, const_cast<void*>(ptr), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SISA_ERR_ALIGN, "%s: cuTensorMapEncodeTiled failed (%d)", name, (int)r);
+  return SISA_OK;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Tensor-map encoding is a driver call that needs a current context on the calling thread. A thread
@@ -289,7 +304,14 @@ int sisa_attn_bwd(const sisa_view4* q, const sisa_view4* k, const sisa_view4* v,
       (rc = map_view4(&p.tm_do64, dout, B, H, L, 64, 2, dt, 64, s128, "dout")) ||
       (rc = map_view4(&p.tm_c64, c, B, H, L, 32, 2, dt, 64, s64, "c")) ||
       (rc = map_records(&p.tm_pos, pos, B * H, L, sisa_pos_len(L), "pos")) ||
-      (rc = map_records(&p.tm_rstat, p.rstat, B * H, L, sisa_pos_len(L), "rstat")))
+      (rc = map_records(&p.tm_rstat, p.rstat, B * H, L, sisa_pos_len(L), "rstat")) ||
+      (rc = o32 ? map_rows3(&p.tm_o, o32, B * H, L, 64, 4, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 32, 128, s128, "o32")
+                : map_view4(&p.tm_o, o, B, H, L, 64, 2, dt, 128, s128, "o")) ||
+      (rc = map_view4(&p.tm_dq, dq, B, H, L, 64, 2, dt, 128, s128, "dq")) ||
+      (rc = map_view4(&p.tm_dc, dc, B, H, L, 32, 4, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 128, s128, "dc")) ||
+      (rc = map_view4(&p.tm_dk, dk, B, H, L, 64, 2, dt, 128, s128, "dk")) ||
+      (rc = map_view4(&p.tm_dv, dv, B, H, L, 64, 2, dt, 128, s128, "dv")) ||
+      (rc = map_view4(&p.tm_db, db, B, H, L, 32, 4, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 128, s128, "db")))
     return rc;
   p.pos = pos;
   p.lam = lam;
