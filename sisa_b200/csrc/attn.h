@@ -13,6 +13,8 @@ struct FwdParams {
   CUtensorMap tm_c;    // (32, L, H, B), box (32, 128), 64B swizzle
   CUtensorMap tm_b;    // box (32, 64)
   CUtensorMap tm_pos;  // (L, 4, B*H) fp32 planes, box (64, 4, 1)
+  CUtensorMap tm_ost;  // o, (64, L, H, B) view, box (64, 128), 128B swizzle (bulk-tensor store)
+  CUtensorMap tm_o32;  // o'', (64, L, B*H) fp32, box (32, 128, 1), 128B swizzle (bulk-tensor store)
   const float* pos;    // (B*H, 4, Lp) planes {g, F, rowf, colf}
   const float* lam;
   char* o;

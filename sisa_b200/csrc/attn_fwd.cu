@@ -41,6 +41,7 @@ constexpr uint32_t SZ_P = BM * 128;
 constexpr uint32_t OFF_Q = 0, OFF_C = OFF_Q + SZ_Q, OFF_ST = OFF_C + SZ_C;
 constexpr uint32_t OFF_BAR = OFF_ST + NSTAGE * SZ_STAGE;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
+static_assert(NSTAGE * SZ_STAGE >= 2 * BM * 128 && SZ_Q >= BM * 128, "epilogue staging fits");
 constexpr uint32_t TMEM_COLS = 256;
 constexpr int NO = 80;                                           // O columns: 64 head dims | sum DT(p) | 15 zero
 constexpr int COL_S = 0, COL_U = 64, COL_O = 128, COL_P = COL_O + NO;   // P: one 32-column bf16x2 buffer
@@ -297,36 +298,49 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
       tmem_ld32(tO + 32, ov + 32);
       tmem_ld1(tO + 64, lb);
       tmem_wait_ld();
-      if (vrow) {
-        const float ls = (l == 0.f) ? 1.f : l;
-        const float lbs = (lb == 0.f) ? 1.f : lb;
-        uint4* orow = reinterpret_cast<uint4*>(p.o + 2 * ((int64_t)b * p.o_sb + (int64_t)h * p.o_sh + (int64_t)row * p.o_sl));
+      const float ls = (l == 0.f) ? 1.f : l;
+      const float lbs = (lb == 0.f) ? 1.f : lb;
+      const float rls = 1.f / ls, rlbs = 1.f / lbs;
+      // The row is staged in shared memory that the finished GEMMs no longer read: o (low precision,
+      // 128-byte rows) in the Q tile, o'' (fp32, two 32-column boxes) over the stages.
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          uint32_t w[4];
+      for (int q = 0; q < 8; ++q) {
+        uint32_t w[4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) w[i] = pack2<kHalf>(ov[q * 8 + 2 * i] / ls, ov[q * 8 + 2 * i + 1] / ls);
-          orow[q] = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-        if (p.o32) {
-          // o'' for the exact-delta backward: the self-normalised fp32 output, snapped to the rounded
-          // output where the two agree to 2^-15 (attention.py:341-350 does this in the backward)
-          float4* o32row = reinterpret_cast<float4*>(p.o32 + ((int64_t)bh * L + row) * kD);
+        for (int i = 0; i < 4; ++i) w[i] = pack2<kHalf>(ov[q * 8 + 2 * i] * rls, ov[q * 8 + 2 * i + 1] * rls);
+        st_shared_v4(sbase + OFF_Q + sw128_off(r, q), w[0], w[1], w[2], w[3]);
+      }
+      if (p.o32) {
+        // o'' for the exact-delta backward: the self-normalised fp32 output, snapped to the rounded
+        // output where the two agree to 2^-15 (attention.py:341-350 does this in the backward)
 #pragma unroll
-          for (int q = 0; q < 16; ++q) {
-            float o3[4];
+        for (int q = 0; q < 16; ++q) {
+          uint32_t o3[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float o32 = ov[4 * q + i] / lbs, olp = round_lp<kHalf>(ov[4 * q + i] / ls);
-              o3[i] = (fabsf(o32 - olp) <= 3.0517578125e-05f * fabsf(olp)) ? olp : o32;
-            }
-            o32row[q] = make_float4(o3[0], o3[1], o3[2], o3[3]);
+          for (int i = 0; i < 4; ++i) {
+            const float o32 = ov[4 * q + i] * rlbs, olp = round_lp<kHalf>(ov[4 * q + i] * rls);
+            o3[i] = __float_as_uint((fabsf(o32 - olp) <= 3.0517578125e-05f * fabsf(olp)) ? olp : o32);
           }
+          st_shared_v4(sbase + OFF_ST + (q >> 3) * (BM * 128) + sw128_off(r, q & 7), o3[0], o3[1], o3[2], o3[3]);
         }
+      }
+      fence_proxy_async_smem();
+      if (vrow) {
         const float lse = ((m_ref == -INFINITY) ? 0.f : m_ref) + log2f(ls);
         p.lse[(int64_t)bh * L + row] = lse;
         if (!isfinite(lse) && p.status) atomicOr(p.status, SISA_ST_NONFINITE);
       }
+    }
+    // one thread stores the tiles (rows past L are clipped) and waits until they have been read
+    named_bar_sync(1, 128);
+    if (tid == 0 && ok) {
+      tma_store_4d(&p.tm_ost, sbase + OFF_Q, 0, m0, h, b);
+      if (p.o32) {
+        tma_store_3d(&p.tm_o32, sbase + OFF_ST, 0, m0, bh);
+        tma_store_3d(&p.tm_o32, sbase + OFF_ST + BM * 128, 32, m0, bh);
+      }
+      bulk_commit();
+      bulk_wait_read0();
     }
   }
   tc_fence_before();

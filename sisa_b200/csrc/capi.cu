@@ -252,7 +252,10 @@ int sisa_attn_fwd(const sisa_view4* q, const sisa_view4* k, const sisa_view4* v,
       (rc = map_view4(&p.tm_v, v, B, H, L, 64, 2, dt, 64, CU_TENSOR_MAP_SWIZZLE_128B, "v")) ||
       (rc = map_view4(&p.tm_c, c, B, H, L, 32, 2, dt, 128, CU_TENSOR_MAP_SWIZZLE_64B, "c")) ||
       (rc = map_view4(&p.tm_b, b, B, H, L, 32, 2, dt, 64, CU_TENSOR_MAP_SWIZZLE_64B, "b")) ||
-      (rc = map_records(&p.tm_pos, pos, B * H, L, sisa_pos_len(L), "pos")))
+      (rc = map_records(&p.tm_pos, pos, B * H, L, sisa_pos_len(L), "pos")) ||
+      (rc = map_view4(&p.tm_ost, o, B, H, L, 64, 2, dt, 128, CU_TENSOR_MAP_SWIZZLE_128B, "o")) ||
+      (o32 && (rc = map_rows3(&p.tm_o32, o32, B * H, L, 64, 4, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 32, 128,
+                              CU_TENSOR_MAP_SWIZZLE_128B, "o32"))))
     return rc;
   p.pos = pos;
   p.lam = lam;
