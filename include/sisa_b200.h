@@ -63,7 +63,7 @@ int64_t sisa_pos_len(int64_t L);
 
 /* Workspace sizes in bytes for the entry points below (caller allocates; 256-byte aligned). */
 int64_t sisa_prep_fwd_workspace(int64_t B, int64_t H, int64_t L);   /* block totals, fp32 */
-int64_t sisa_prep_bwd_workspace(int64_t B, int64_t H, int64_t L);   /* block totals, fp64 */
+int64_t sisa_prep_bwd_workspace(int64_t B, int64_t H, int64_t L);   /* fp64 block totals + fp32 per-token d Phi */
 int64_t sisa_attn_bwd_workspace(int64_t B, int64_t H, int64_t L);   /* per-row statistics */
 
 /* Fused preparation, forward (src/sisa/kernels/fused_prep.py:247-352, launched at :527-564):

@@ -188,7 +188,8 @@ int sisa_fused_layout(int64_t n_head, int64_t* out9) {
 }
 
 int64_t sisa_prep_fwd_workspace(int64_t B, int64_t H, int64_t L) { return B * H * nch64(L) * 18 * 4; }
-int64_t sisa_prep_bwd_workspace(int64_t B, int64_t H, int64_t L) { return B * H * nch64(L) * 18 * 8; }
+// fp64 block totals (B*H, nch, 18), then the per-token d Phi (B*H, L, 16) fp32
+int64_t sisa_prep_bwd_workspace(int64_t B, int64_t H, int64_t L) { return B * H * (nch64(L) * 18 * 8 + L * 16 * 4); }
 int64_t sisa_pos_len(int64_t L) { return (L + 3) & ~int64_t(3); }
 // rstat planes (B*H, 4, Lp) fp32, then rg, rf, rl (B*H, L) fp32 each
 int64_t sisa_attn_bwd_workspace(int64_t B, int64_t H, int64_t L) { return B * H * (sisa_pos_len(L) * 16 + L * 12); }
@@ -353,7 +354,8 @@ int sisa_prep_bwd(const void* proj, int64_t B, int64_t L, int64_t H, int64_t pro
   if (proj_sl < off[8] || dproj_sl < off[8]) return fail(SISA_ERR_VALUE, "proj/dproj row stride < NPAD");
   if (!aligned16(proj) || !aligned16(dproj) || proj_sl % 8 || proj_sb % 8 || dproj_sl % 8 || dproj_sb % 8)
     return fail(SISA_ERR_ALIGN, "proj/dproj must be 16-byte aligned with strides that are multiples of 8");
-  if (!aligned16(dc) || !aligned16(db)) return fail(SISA_ERR_ALIGN, "dc/db must be 16-byte aligned");
+  if (!aligned16(dc) || !aligned16(db) || !aligned16(workspace))
+    return fail(SISA_ERR_ALIGN, "dc, db and workspace must be 16-byte aligned");
   sisa::PrepBwdLaunch p{};
   p.proj = proj; p.proj_sb = proj_sb; p.proj_sl = proj_sl; p.dtype = dtype;
   p.z = z; p.z_sb = z_sb; p.z_sl = z_sl;

@@ -12,7 +12,9 @@
 //
 // Backward (reference: src/sisa/kernels/fused_prep.py:385-494): reverse cumulative sums in fp64
 // (block totals + in-block warp scans), rounded to fp32 once; inverse rotation of dc~/db~; d theta
-// from both rotations; zero padding columns.
+// from both rotations; zero padding columns. Two passes: the first recomputes Phi, writes dC and dB
+// (final), the per-token d Phi (fp32 workspace) and the fp64 block totals; the second reads only dg,
+// dF, alpha, z and d Phi, so the rotation inputs are read once.
 //
 // Layout: one CTA = one batch row b and one 64-token block; warp w handles heads w, w+8, ...;
 // lane l handles tokens 2l and 2l+1 of the block.
@@ -331,6 +333,7 @@ struct PrepBwdArgs {
   int64_t dproj_sb, dproj_sl;
   float* dz;               // (B,L,H)
   double* bt;              // (B*H, nch, kTot) fp64
+  float* dphi;             // (B*H, L, kS2) fp32: per-token d Phi of both rotations
   int32_t* status;
 };
 
@@ -436,7 +439,15 @@ __global__ void __launch_bounds__(256) prep_bsums_kernel(PrepBwdArgs a) {
     tv[1] = __shfl_sync(0xffffffffu, r0, 0);
     float phi[2][kS2], dphi[2][kS2];
     recompute_phi<kHalf>(a, b, h, c, t0, phi);
-    rotation_grads<kHalf, false>(a, b, h, t0, phi, dphi);
+    rotation_grads<kHalf, true>(a, b, h, t0, phi, dphi);
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      if (t0 + r >= a.L) continue;
+      float4* dst = reinterpret_cast<float4*>(a.dphi + (bh * a.L + t0 + r) * kS2);
+#pragma unroll
+      for (int q = 0; q < kS2 / 4; ++q)
+        dst[q] = make_float4(dphi[r][4 * q], dphi[r][4 * q + 1], dphi[r][4 * q + 2], dphi[r][4 * q + 3]);
+    }
 #pragma unroll
     for (int p = 0; p < kS2; ++p) {
       rscan64((double)dphi[0][p], (double)dphi[1][p], r0, r1);
@@ -517,10 +528,18 @@ __global__ void __launch_bounds__(256, 2) prep_bwd_kernel(PrepBwdArgs a) {
         a.dz[((int64_t)b * a.L + t) * a.H + h] = dlf * logsigmoid_grad(zv);
       }
     }
-    // inverse rotation of C/B, d theta = sum_{s>=t} dPhi_s
-    float phi[2][kS2], dphi[2][kS2];
-    recompute_phi<kHalf>(a, b, h, c, t0, phi);
-    rotation_grads<kHalf, true>(a, b, h, t0, phi, dphi);
+    // d theta = sum_{s>=t} dPhi_s (dC and dB were written by the first pass)
+    float dphi[2][kS2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const bool ok = t0 + r < a.L;
+      const float4* src = reinterpret_cast<const float4*>(a.dphi + (bh * a.L + (ok ? t0 + r : 0)) * kS2);
+#pragma unroll
+      for (int q = 0; q < kS2 / 4; ++q) {
+        const float4 v = ok ? __ldg(src + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+        dphi[r][4 * q] = v.x; dphi[r][4 * q + 1] = v.y; dphi[r][4 * q + 2] = v.z; dphi[r][4 * q + 3] = v.w;
+      }
+    }
     float dth[2][kS2];
 #pragma unroll
     for (int p = 0; p < kS2; ++p) {
@@ -592,6 +611,7 @@ cudaError_t launch_prep_bwd(const PrepBwdLaunch& p, cudaStream_t st) {
   a.ntot = (int)p.ntot; a.npad = (int)p.npad;
   a.tot = p.tot; a.dc = p.dc; a.db = p.db; a.dg = p.dg; a.dF = p.dF;
   a.dproj = p.dproj; a.dproj_sb = p.dproj_sb; a.dproj_sl = p.dproj_sl; a.dz = p.dz; a.bt = p.bt;
+  a.dphi = reinterpret_cast<float*>(p.bt + (int64_t)a.B * a.H * a.nch * kTot);
   a.status = p.status;
   dim3 grid(a.nch, a.B);
   if (p.dtype == 1) {

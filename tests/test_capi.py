@@ -52,7 +52,8 @@ def test_layout_agrees_with_python_and_oracle(golden):
 def test_workspace_sizes():
     lib = _lib.load()
     assert lib.sisa_prep_fwd_workspace(2, 3, 130) == 2 * 3 * 3 * 18 * 4
-    assert lib.sisa_prep_bwd_workspace(2, 3, 130) == 2 * 3 * 3 * 18 * 8
+    # fp64 block totals (B*H, nch, 18) + per-token d Phi (B*H, L, 16) fp32
+    assert lib.sisa_prep_bwd_workspace(2, 3, 130) == 2 * 3 * (3 * 18 * 8 + 130 * 16 * 4)
     # row-statistic planes (4 x Lp fp32) + three (L,) fp32 row parts per (batch, head)
     assert lib.sisa_attn_bwd_workspace(2, 3, 130) == 2 * 3 * (132 * 16 + 130 * 12)
 
