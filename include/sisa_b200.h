@@ -62,7 +62,7 @@ int sisa_fused_layout(int64_t n_head, int64_t* out9);
 int64_t sisa_pos_len(int64_t L);
 
 /* Workspace sizes in bytes for the entry points below (caller allocates; 256-byte aligned). */
-int64_t sisa_prep_fwd_workspace(int64_t B, int64_t H, int64_t L);   /* block totals, fp32 */
+int64_t sisa_prep_fwd_workspace(int64_t B, int64_t H, int64_t L);   /* per-block scan prefixes, fp32 */
 int64_t sisa_prep_bwd_workspace(int64_t B, int64_t H, int64_t L);   /* fp64 block totals + fp32 per-token d Phi */
 int64_t sisa_attn_bwd_workspace(int64_t B, int64_t H, int64_t L);   /* per-row statistics */
 
@@ -120,7 +120,7 @@ int sisa_attn_bwd(const sisa_view4* q, const sisa_view4* k, const sisa_view4* v,
  * dproj: (B, L, NPAD) `dtype` with strides dproj_sb, dproj_sl; only the B, C, TH, A and padding
  * columns are written here (the Q, K, V columns come from sisa_attn_bwd).
  * dc, db: (B, H, L, 32) fp32 contiguous; dg, dF: (B, H, L) fp32 (dF NULL without z).
- * dz: (B, L, H) fp32 contiguous (ignored without z). tot: the forward's workspace (block totals).
+ * dz: (B, L, H) fp32 contiguous (ignored without z). tot: the forward's workspace (per-block scan prefixes).
  * workspace: sisa_prep_bwd_workspace(B, H, L) bytes. */
 int sisa_prep_bwd(const void* proj, int64_t B, int64_t L, int64_t H, int64_t proj_sb, int64_t proj_sl,
                   int dtype, const float* z, int64_t z_sb, int64_t z_sl, const void* tot,

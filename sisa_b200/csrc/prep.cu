@@ -17,7 +17,8 @@
 // dF, alpha, z and d Phi, so the rotation inputs are read once.
 //
 // Layout: one CTA = one batch row b and one 64-token block; warp w handles heads w, w+8, ...;
-// lane l handles tokens 2l and 2l+1 of the block.
+// lane l handles tokens 2l and 2l+1 of the block. The backward's rotation pass stages its rows in
+// shared memory instead (prep_brot_kernel).
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -178,21 +179,30 @@ __device__ __forceinline__ void store_planes(float* pl, int Lp, int t0, int L, c
   }
 }
 
-// Sequential sum of the totals of blocks [0, c) (component k, computed by lane k, fixed order). The
-// order of the additions is what makes g non-increasing across block boundaries (the next block's
-// prefix is exactly this block's prefix plus its total), so it stays sequential; the loads are issued
-// 16 at a time so the sum costs ceil(c / 16) round trips instead of one per block.
-__device__ __forceinline__ float prefix_total(const float* tot, int64_t bh, int nch, int c, int k) {
-  float acc = 0.f;
-  const float* p = tot + bh * nch * kTot + k;
-  for (int c0 = 0; c0 < c; c0 += 16) {
-    float v[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = (c0 + i < c) ? __ldg(p + (int64_t)(c0 + i) * kTot) : 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) if (c0 + i < c) acc += v[i];
+// In-place exclusive scans of the per-block totals along the block axis, one warp per (row, component)
+// chain; lane j of a round of 32 blocks takes the running sum before block j is added, so the additions
+// stay in block order. Forward (fp32, increasing blocks): pre[c] = ((t_0 + t_1) + ...) + t_{c-1}, the
+// order of prefix_total, which keeps g non-increasing across blocks. Backward (fp64, decreasing blocks):
+// suf[c] = sum of the totals of the blocks after c.
+template <typename T, bool kReverse>
+__global__ void __launch_bounds__(256) block_scan_kernel(T* tot, int64_t nchains, int nch) {
+  const int64_t w = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (w >= nchains) return;
+  const int lane = threadIdx.x & 31;
+  T* base = tot + (w / kTot) * (int64_t)nch * kTot + w % kTot;
+  T acc = T(0);
+  for (int c0 = 0; c0 < nch; c0 += 32) {
+    const bool ok = c0 + lane < nch;
+    const int64_t c = kReverse ? nch - 1 - (c0 + lane) : c0 + lane;
+    const T v = ok ? base[c * kTot] : T(0);
+    T mine = acc;
+    const int n = min(32, nch - c0);
+    for (int j = 0; j < n; ++j) {
+      if (lane == j) mine = acc;
+      acc += __shfl_sync(0xffffffffu, v, j);
+    }
+    if (ok) base[c * kTot] = mine;
   }
-  return acc;
 }
 
 template <bool kHalf>
@@ -204,7 +214,7 @@ __global__ void __launch_bounds__(256) prep_fwd_kernel(PrepArgs a) {
     const int64_t bh = (int64_t)b * a.H + h;
     float la[2], lf[2], th[2][kS2];
     load_elems<kHalf>(a, b, h, t0, la, lf, th);
-    const float mypre = lane < kTot ? prefix_total(a.tot, bh, a.nch, c, lane) : 0.f;
+    const float mypre = lane < kTot ? __ldg(a.tot + (bh * a.nch + c) * kTot + lane) : 0.f;   // prefix of the blocks before c
     float s0, s1;
     // g, rowf, colf
     scan64(la[0], la[1], s0, s1);
@@ -324,7 +334,7 @@ struct PrepBwdArgs {
   int64_t z_sb, z_sl;
   int B, L, H, nch;
   int col_b, col_c, col_th, col_a, ntot, npad;
-  const float* tot;        // forward block totals (fp32)
+  const float* tot;        // forward block prefixes (fp32, exclusive)
   const float* dc;         // (B,H,L,32) fp32
   const float* db;
   const float* dg;         // (B,H,L)
@@ -332,149 +342,170 @@ struct PrepBwdArgs {
   void* dproj;
   int64_t dproj_sb, dproj_sl;
   float* dz;               // (B,L,H)
-  double* bt;              // (B*H, nch, kTot) fp64
+  double* bt;              // (B*H, nch, kTot) fp64 block totals, then their exclusive suffixes
   float* dphi;             // (B*H, L, kS2) fp32: per-token d Phi of both rotations
   int32_t* status;
 };
 
-// Recompute Phi for the two tokens of this lane with the forward's exact code path.
-template <bool kHalf>
-__device__ __forceinline__ void recompute_phi(const PrepBwdArgs& a, int b, int h, int c, int t0, float phi[2][kS2]) {
-  const int lane = threadIdx.x & 31;
-  const int64_t bh = (int64_t)b * a.H + h;
-  float th[2][kS2];
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const int t = t0 + r;
-    const bool ok = t < a.L;
-    const int64_t row = (int64_t)b * a.proj_sb + (int64_t)(ok ? t : 0) * a.proj_sl;
-    const uint4* tp = reinterpret_cast<const uint4*>(
-        reinterpret_cast<const char*>(a.proj) + (row + a.col_th + h * kS2) * 2);
-    uint4 v0 = make_uint4(0, 0, 0, 0), v1 = make_uint4(0, 0, 0, 0);
-    if (ok) { v0 = __ldg(tp); v1 = __ldg(tp + 1); }
-    const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      th[r][2 * i] = unpack_lo<kHalf>(w[i]);
-      th[r][2 * i + 1] = unpack_hi<kHalf>(w[i]);
-    }
-  }
-  const float mypre = lane < kTot ? prefix_total(a.tot, bh, a.nch, c, lane) : 0.f;
-#pragma unroll
-  for (int p = 0; p < kS2; ++p) {
-    float s0, s1;
-    scan64(th[0][p], th[1][p], s0, s1);
-    const float pre = __shfl_sync(0xffffffffu, mypre, 2 + p);
-    phi[0][p] = pre + s0;
-    phi[1][p] = pre + s1;
-  }
-}
-
-// d Phi (both rotations) and, when kWrite, the inverse-rotated input gradients of C and B.
-template <bool kHalf, bool kWrite>
-__device__ __forceinline__ void rotation_grads(const PrepBwdArgs& a, int b, int h, int t0, const float phi[2][kS2],
-                                               float dphi[2][kS2]) {
-  const int64_t bh = (int64_t)b * a.H + h;
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-#pragma unroll
-    for (int p = 0; p < kS2; ++p) dphi[r][p] = 0.f;
-    const int t = t0 + r;
-    if (t >= a.L) continue;
-    const int64_t row = (int64_t)b * a.proj_sb + (int64_t)t * a.proj_sl;
-    const int64_t drow = (int64_t)b * a.dproj_sb + (int64_t)t * a.dproj_sl;
-    float cs[kS2], sn[kS2];
-#pragma unroll
-    for (int p = 0; p < kS2; ++p) sincosf(phi[r][p], &sn[p], &cs[p]);
-#pragma unroll
-    for (int which = 0; which < 2; ++which) {
-      const int col = (which == 0 ? a.col_c : a.col_b) + h * 32;
-      const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.proj) + (row + col) * 2);
-      const float4* gsrc = reinterpret_cast<const float4*>((which == 0 ? a.dc : a.db) + (bh * a.L + t) * 32);
-      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.dproj) + (drow + col) * 2);
-      uint4 vq[4];
-      float4 gq[8];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) vq[q] = __ldg(src + q);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) gq[q] = __ldg(gsrc + q);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint4 v = vq[q];
-        const float4 g0 = gq[2 * q], g1 = gq[2 * q + 1];
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-        const float gd[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-        uint32_t o[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int p = q * 4 + i;
-          const float ze = unpack_lo<kHalf>(w[i]), zo = unpack_hi<kHalf>(w[i]);
-          const float oe = ze * cs[p] - zo * sn[p];
-          const float oo = ze * sn[p] + zo * cs[p];
-          const float de = gd[2 * i], dd = gd[2 * i + 1];
-          dphi[r][p] += dd * oe - de * oo;
-          if constexpr (kWrite) o[i] = pack2<kHalf>(de * cs[p] + dd * sn[p], dd * cs[p] - de * sn[p]);
-        }
-        if constexpr (kWrite) dst[q] = make_uint4(o[0], o[1], o[2], o[3]);
-      }
-    }
-  }
+// First backward pass, one CTA per (batch, 64-token block, kHG heads). The rows' C, B and theta
+// columns of those heads and their dc~, db~ rows are copied into shared memory with coalesced 16-byte
+// copies (16 threads per 256-byte row segment) instead of one scattered row segment per lane; warp
+// (head, pair half) then computes, per lane, tokens 2l and 2l+1 with the forward's scan for Phi:
+// dC and dB (final, written back into the staged rows and stored coalesced), the per-token d Phi and
+// the fp64 block totals of dg, dF and d Phi.
+constexpr int kHG = 4;
+constexpr uint32_t kRotRow = kHG * 64;   // bytes of one token's C (or B) columns of kHG heads
+constexpr uint32_t kThRow = kHG * 32;    // theta bytes of one token
+constexpr uint32_t kSmC = 0, kSmB = kSmC + kBlk * kRotRow, kSmTh = kSmB + kBlk * kRotRow;
+constexpr uint32_t kSmDc = kSmTh + kBlk * kThRow, kSmDb = kSmDc + kHG * kBlk * 128;
+constexpr uint32_t kSmBrot = kSmDb + kHG * kBlk * 128;   // 106496 bytes
+// 16-byte chunk ch of token row t sits at chunk (ch & ~7) | ((ch ^ (t >> 1)) & 7): the 32 lanes of a
+// warp, owning tokens 2l and 2l+1, read one logical chunk from eight different bank groups.
+__device__ __forceinline__ uint32_t swz_chunk(int t, int ch) {
+  return ((uint32_t)ch & ~7u) | (((uint32_t)ch ^ ((uint32_t)t >> 1)) & 7u);
 }
 
 template <bool kHalf>
-__global__ void __launch_bounds__(256) prep_bsums_kernel(PrepBwdArgs a) {
-  const int c = blockIdx.x, b = blockIdx.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t0 = c * kBlk + 2 * lane;
-  for (int h = warp; h < a.H; h += 8) {
+__global__ void __launch_bounds__(256, 2) prep_brot_kernel(PrepBwdArgs a) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  const int c = blockIdx.x, b = blockIdx.y, h0 = blockIdx.z * kHG;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t sb = smem_u32(sm);
+  const int tb = c * kBlk;
+  const char* proj = static_cast<const char*>(a.proj);
+  // ---- coalesced copies; rows past L and heads past H become zeros
+  for (int k = tid; k < kBlk * 16; k += 256) {
+    const int t = k >> 4, ch = k & 15;
+    const bool ok = tb + t < a.L && h0 + (ch >> 2) < a.H;
+    const int64_t row = (int64_t)b * a.proj_sb + (int64_t)(ok ? tb + t : 0) * a.proj_sl;
+    const uint32_t so = (uint32_t)t * kRotRow + swz_chunk(t, ch) * 16;
+    cp_async16(sb + kSmC + so, proj + (row + a.col_c + h0 * 32) * 2 + (ok ? ch * 16 : 0), ok ? 16 : 0);
+    cp_async16(sb + kSmB + so, proj + (row + a.col_b + h0 * 32) * 2 + (ok ? ch * 16 : 0), ok ? 16 : 0);
+  }
+  for (int k = tid; k < kBlk * 8; k += 256) {
+    const int t = k >> 3, ch = k & 7;
+    const bool ok = tb + t < a.L && h0 + (ch >> 1) < a.H;
+    const int64_t row = (int64_t)b * a.proj_sb + (int64_t)(ok ? tb + t : 0) * a.proj_sl;
+    cp_async16(sb + kSmTh + (uint32_t)t * kThRow + swz_chunk(t, ch) * 16,
+               proj + (row + a.col_th + h0 * kS2) * 2 + (ok ? ch * 16 : 0), ok ? 16 : 0);
+  }
+  for (int k = tid; k < kHG * kBlk * 8; k += 256) {
+    const int hl = k >> 9, t = (k >> 3) & (kBlk - 1), ch = k & 7;
+    const bool ok = tb + t < a.L && h0 + hl < a.H;
+    const int64_t e = (((int64_t)b * a.H + (ok ? h0 + hl : 0)) * a.L + (ok ? tb + t : 0)) * 32 + ch * 4;
+    const uint32_t so = (uint32_t)hl * (kBlk * 128) + (uint32_t)t * 128 + swz_chunk(t, ch) * 16;
+    cp_async16(sb + kSmDc + so, a.dc + e, ok ? 16 : 0);
+    cp_async16(sb + kSmDb + so, a.db + e, ok ? 16 : 0);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+
+  const int hl = warp >> 1, ph = warp & 1;   // head in the group; pairs 8 ph .. 8 ph + 7
+  const int h = h0 + hl;
+  if (h < a.H) {
     const int64_t bh = (int64_t)b * a.H + h;
-    double x0, x1, r0, r1, tv[kTot];
-    x0 = t0 < a.L ? (double)__ldg(a.dg + bh * a.L + t0) : 0.0;
-    x1 = t0 + 1 < a.L ? (double)__ldg(a.dg + bh * a.L + t0 + 1) : 0.0;
-    rscan64(x0, x1, r0, r1);
-    tv[0] = __shfl_sync(0xffffffffu, r0, 0);
-    x0 = (a.dF && t0 < a.L) ? (double)__ldg(a.dF + bh * a.L + t0) : 0.0;
-    x1 = (a.dF && t0 + 1 < a.L) ? (double)__ldg(a.dF + bh * a.L + t0 + 1) : 0.0;
-    rscan64(x0, x1, r0, r1);
-    tv[1] = __shfl_sync(0xffffffffu, r0, 0);
-    float phi[2][kS2], dphi[2][kS2];
-    recompute_phi<kHalf>(a, b, h, c, t0, phi);
-    rotation_grads<kHalf, true>(a, b, h, t0, phi, dphi);
+    const int tl = 2 * lane;
+    double* dst = a.bt + (bh * a.nch + c) * kTot;
+    if (ph == 0) {
+      // block totals of dg and dF
+      double x0, x1, r0, r1, tg, tf;
+      x0 = tb + tl < a.L ? (double)__ldg(a.dg + bh * a.L + tb + tl) : 0.0;
+      x1 = tb + tl + 1 < a.L ? (double)__ldg(a.dg + bh * a.L + tb + tl + 1) : 0.0;
+      rscan64(x0, x1, r0, r1);
+      tg = __shfl_sync(0xffffffffu, r0, 0);
+      x0 = (a.dF && tb + tl < a.L) ? (double)__ldg(a.dF + bh * a.L + tb + tl) : 0.0;
+      x1 = (a.dF && tb + tl + 1 < a.L) ? (double)__ldg(a.dF + bh * a.L + tb + tl + 1) : 0.0;
+      rscan64(x0, x1, r0, r1);
+      tf = __shfl_sync(0xffffffffu, r0, 0);
+      if (lane == 0) { dst[0] = tg; dst[1] = tf; }
+    }
+    // Phi of pairs 8 ph .. 8 ph + 7: the forward's in-block scan plus the fp32 prefix of its totals
+    constexpr int kP = kS2 / 2;
+    float th[2][kP];
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
-      if (t0 + r >= a.L) continue;
-      float4* dst = reinterpret_cast<float4*>(a.dphi + (bh * a.L + t0 + r) * kS2);
+      const uint4 v = ld_shared_v4(sb + kSmTh + (uint32_t)(tl + r) * kThRow + swz_chunk(tl + r, 2 * hl + ph) * 16);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int q = 0; q < kS2 / 4; ++q)
-        dst[q] = make_float4(dphi[r][4 * q], dphi[r][4 * q + 1], dphi[r][4 * q + 2], dphi[r][4 * q + 3]);
+      for (int i = 0; i < 4; ++i) { th[r][2 * i] = unpack_lo<kHalf>(w[i]); th[r][2 * i + 1] = unpack_hi<kHalf>(w[i]); }
     }
+    const float mypre = lane < kP ? __ldg(a.tot + (bh * a.nch + c) * kTot + 2 + kP * ph + lane) : 0.f;
+    float phi[2][kP];
 #pragma unroll
-    for (int p = 0; p < kS2; ++p) {
+    for (int p = 0; p < kP; ++p) {
+      float s0, s1;
+      scan64(th[0][p], th[1][p], s0, s1);
+      const float pre = __shfl_sync(0xffffffffu, mypre, p);
+      phi[0][p] = pre + s0;
+      phi[1][p] = pre + s1;
+    }
+    // d Phi from both rotations; dC = R(Phi)^T dc~, dB = R(Phi)^T db~ written over the staged C, B
+    float dphi[2][kP];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int t = tl + r;
+#pragma unroll
+      for (int p = 0; p < kP; ++p) dphi[r][p] = 0.f;
+      if (tb + t >= a.L) continue;
+      float cs[kP], sn[kP];
+#pragma unroll
+      for (int p = 0; p < kP; ++p) sincosf(phi[r][p], &sn[p], &cs[p]);
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const uint32_t zrow = sb + (which == 0 ? kSmC : kSmB) + (uint32_t)t * kRotRow;
+        const uint32_t grow = sb + (which == 0 ? kSmDc : kSmDb) + (uint32_t)hl * (kBlk * 128) + (uint32_t)t * 128;
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const uint32_t za = zrow + swz_chunk(t, 4 * hl + 2 * ph + q) * 16;
+          const uint4 v = ld_shared_v4(za);
+          const uint4 g0 = ld_shared_v4(grow + swz_chunk(t, 4 * ph + 2 * q) * 16);
+          const uint4 g1 = ld_shared_v4(grow + swz_chunk(t, 4 * ph + 2 * q + 1) * 16);
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+          const float gd[8] = {__uint_as_float(g0.x), __uint_as_float(g0.y), __uint_as_float(g0.z), __uint_as_float(g0.w),
+                               __uint_as_float(g1.x), __uint_as_float(g1.y), __uint_as_float(g1.z), __uint_as_float(g1.w)};
+          uint32_t o[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int p = q * 4 + i;
+            const float ze = unpack_lo<kHalf>(w[i]), zo = unpack_hi<kHalf>(w[i]);
+            const float oe = ze * cs[p] - zo * sn[p];
+            const float oo = ze * sn[p] + zo * cs[p];
+            const float de = gd[2 * i], dd = gd[2 * i + 1];
+            dphi[r][p] += dd * oe - de * oo;
+            o[i] = pack2<kHalf>(de * cs[p] + dd * sn[p], dd * cs[p] - de * sn[p]);
+          }
+          st_shared_v4(za, o[0], o[1], o[2], o[3]);
+        }
+      }
+      float4* dp = reinterpret_cast<float4*>(a.dphi + (bh * a.L + tb + t) * kS2 + kP * ph);
+      dp[0] = make_float4(dphi[r][0], dphi[r][1], dphi[r][2], dphi[r][3]);
+      dp[1] = make_float4(dphi[r][4], dphi[r][5], dphi[r][6], dphi[r][7]);
+    }
+    double tv[kP];
+#pragma unroll
+    for (int p = 0; p < kP; ++p) {
+      double r0, r1;
       rscan64((double)dphi[0][p], (double)dphi[1][p], r0, r1);
-      tv[2 + p] = __shfl_sync(0xffffffffu, r0, 0);
+      tv[p] = __shfl_sync(0xffffffffu, r0, 0);
     }
-    double* dst = a.bt + (bh * a.nch + c) * kTot;
-    if (lane < kTot) {
+    if (lane < kP) {
       double mine = tv[0];
 #pragma unroll
-      for (int k = 1; k < kTot; ++k) if (lane == k) mine = tv[k];
-      dst[lane] = mine;
+      for (int k = 1; k < kP; ++k) if (lane == k) mine = tv[k];
+      dst[2 + kP * ph + lane] = mine;
     }
   }
-}
-
-// Sum of the totals of blocks (c, nch) in the order c+1, c+2, ... (fp64), loads batched like prefix_total.
-__device__ __forceinline__ double suffix_total(const double* bt, int64_t bh, int nch, int c, int k) {
-  double acc = 0.0;
-  const double* p = bt + bh * nch * kTot + k;
-  for (int c0 = c + 1; c0 < nch; c0 += 16) {
-    double v[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = (c0 + i < nch) ? __ldg(p + (int64_t)(c0 + i) * kTot) : 0.0;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) if (c0 + i < nch) acc += v[i];
+  __syncthreads();
+  // ---- coalesced stores of dC and dB
+  char* dproj = static_cast<char*>(a.dproj);
+  for (int k = tid; k < kBlk * 16; k += 256) {
+    const int t = k >> 4, ch = k & 15;
+    if (tb + t >= a.L || h0 + (ch >> 2) >= a.H) continue;
+    const int64_t drow = (int64_t)b * a.dproj_sb + (int64_t)(tb + t) * a.dproj_sl;
+    const uint32_t so = (uint32_t)t * kRotRow + swz_chunk(t, ch) * 16;
+    *reinterpret_cast<uint4*>(dproj + (drow + a.col_c + h0 * 32) * 2 + ch * 16) = ld_shared_v4(sb + kSmC + so);
+    *reinterpret_cast<uint4*>(dproj + (drow + a.col_b + h0 * 32) * 2 + ch * 16) = ld_shared_v4(sb + kSmB + so);
   }
-  return acc;
 }
 
 template <bool kHalf>
@@ -492,7 +523,7 @@ __global__ void __launch_bounds__(256, 2) prep_bwd_kernel(PrepBwdArgs a) {
   const int t0 = c * kBlk + 2 * lane;
   for (int h = warp; h < a.H; h += 8) {
     const int64_t bh = (int64_t)b * a.H + h;
-    const double mysuf = lane < kTot ? suffix_total(a.bt, bh, a.nch, c, lane) : 0.0;
+    const double mysuf = lane < kTot ? __ldg(a.bt + (bh * a.nch + c) * kTot + lane) : 0.0;   // sum of the blocks after c
     double x0, x1, r0, r1;
     // d alpha = -(sum_{s>=t} dg_s) * softplus'(alpha)
     x0 = t0 < a.L ? (double)__ldg(a.dg + bh * a.L + t0) : 0.0;
@@ -583,11 +614,13 @@ cudaError_t launch_prep_fwd(const PrepFwdLaunch& p, cudaStream_t st) {
   dim3 grid(a.nch, a.B);
   if (p.dtype == 1) {
     prep_sums_kernel<true><<<grid, 256, 0, st>>>(a);
-    prep_fwd_kernel<true><<<grid, 256, 0, st>>>(a);
   } else {
     prep_sums_kernel<false><<<grid, 256, 0, st>>>(a);
-    prep_fwd_kernel<false><<<grid, 256, 0, st>>>(a);
   }
+  const int64_t nchains = (int64_t)a.B * a.H * kTot;
+  block_scan_kernel<float, false><<<(unsigned)((nchains + 7) / 8), 256, 0, st>>>(a.tot, nchains, a.nch);
+  if (p.dtype == 1) prep_fwd_kernel<true><<<grid, 256, 0, st>>>(a);
+  else prep_fwd_kernel<false><<<grid, 256, 0, st>>>(a);
   return cudaGetLastError();
 }
 
@@ -614,13 +647,18 @@ cudaError_t launch_prep_bwd(const PrepBwdLaunch& p, cudaStream_t st) {
   a.dphi = reinterpret_cast<float*>(p.bt + (int64_t)a.B * a.H * a.nch * kTot);
   a.status = p.status;
   dim3 grid(a.nch, a.B);
+  dim3 grid_rot(a.nch, a.B, (a.H + kHG - 1) / kHG);
   if (p.dtype == 1) {
-    prep_bsums_kernel<true><<<grid, 256, 0, st>>>(a);
-    prep_bwd_kernel<true><<<grid, 256, 0, st>>>(a);
+    cudaFuncSetAttribute(prep_brot_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmBrot);
+    prep_brot_kernel<true><<<grid_rot, 256, kSmBrot, st>>>(a);
   } else {
-    prep_bsums_kernel<false><<<grid, 256, 0, st>>>(a);
-    prep_bwd_kernel<false><<<grid, 256, 0, st>>>(a);
+    cudaFuncSetAttribute(prep_brot_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmBrot);
+    prep_brot_kernel<false><<<grid_rot, 256, kSmBrot, st>>>(a);
   }
+  const int64_t nchains = (int64_t)a.B * a.H * kTot;
+  block_scan_kernel<double, true><<<(unsigned)((nchains + 7) / 8), 256, 0, st>>>(a.bt, nchains, a.nch);
+  if (p.dtype == 1) prep_bwd_kernel<true><<<grid, 256, 0, st>>>(a);
+  else prep_bwd_kernel<false><<<grid, 256, 0, st>>>(a);
   return cudaGetLastError();
 }
 
