@@ -205,66 +205,144 @@ __global__ void __launch_bounds__(256) block_scan_kernel(T* tot, int64_t nchains
   }
 }
 
+// Shared-memory layout of the rotation passes (prep_fwd_kernel, prep_brot_kernel): one CTA per
+// (batch, 64-token block, kHG heads); the rows' C, B and theta columns of those heads (and, backward,
+// their dc~ and db~ rows) are staged with coalesced 16-byte copies (16 threads per 256-byte row
+// segment) instead of one scattered row segment per lane.
+constexpr int kHG = 4;
+constexpr uint32_t kRotRow = kHG * 64;   // bytes of one token's C (or B) columns of kHG heads
+constexpr uint32_t kThRow = kHG * 32;    // theta bytes of one token
+constexpr uint32_t kSmC = 0, kSmB = kSmC + kBlk * kRotRow, kSmTh = kSmB + kBlk * kRotRow;
+constexpr uint32_t kSmFrot = kSmTh + kBlk * kThRow;     // 40960 bytes
+constexpr uint32_t kSmDc = kSmFrot, kSmDb = kSmDc + kHG * kBlk * 128;
+constexpr uint32_t kSmBrot = kSmDb + kHG * kBlk * 128;  // 106496 bytes
+// 16-byte chunk ch of token row t sits at chunk (ch & ~7) | ((ch ^ (t >> 1)) & 7): the 32 lanes of a
+// warp, owning tokens 2l and 2l+1, read one logical chunk from eight different bank groups.
+__device__ __forceinline__ uint32_t swz_chunk(int t, int ch) {
+  return ((uint32_t)ch & ~7u) | (((uint32_t)ch ^ ((uint32_t)t >> 1)) & 7u);
+}
+
+// Coalesced copies of the C, B (which = 0, 1 at byte offsets kSmC, kSmB) and theta columns of heads
+// [h0, h0 + kHG) for tokens [tb, tb + 64); rows past L and heads past H become zeros.
+__device__ __forceinline__ void stage_rot_rows(const void* projv, int64_t proj_sb, int64_t proj_sl, int b, int tb,
+                                               int h0, int L, int H, int col_c, int col_b, int col_th, uint32_t sb) {
+  const char* proj = static_cast<const char*>(projv);
+  for (int k = threadIdx.x; k < kBlk * 16; k += blockDim.x) {
+    const int t = k >> 4, ch = k & 15;
+    const bool ok = tb + t < L && h0 + (ch >> 2) < H;
+    const int64_t row = (int64_t)b * proj_sb + (int64_t)(ok ? tb + t : 0) * proj_sl;
+    const uint32_t so = (uint32_t)t * kRotRow + swz_chunk(t, ch) * 16;
+    cp_async16(sb + kSmC + so, proj + (row + col_c + h0 * 32) * 2 + (ok ? ch * 16 : 0), ok ? 16 : 0);
+    cp_async16(sb + kSmB + so, proj + (row + col_b + h0 * 32) * 2 + (ok ? ch * 16 : 0), ok ? 16 : 0);
+  }
+  for (int k = threadIdx.x; k < kBlk * 8; k += blockDim.x) {
+    const int t = k >> 3, ch = k & 7;
+    const bool ok = tb + t < L && h0 + (ch >> 1) < H;
+    const int64_t row = (int64_t)b * proj_sb + (int64_t)(ok ? tb + t : 0) * proj_sl;
+    cp_async16(sb + kSmTh + (uint32_t)t * kThRow + swz_chunk(t, ch) * 16,
+               proj + (row + col_th + h0 * kS2) * 2 + (ok ? ch * 16 : 0), ok ? 16 : 0);
+  }
+}
+
+// Phi of pairs [8 ph, 8 ph + 8) of head hl for tokens tl, tl + 1 (tl = 2 lane): the staged theta,
+// the in-block warp scan and the block's prefix (the forward's exact arithmetic).
+template <bool kHalf>
+__device__ __forceinline__ void stage_phi(uint32_t sb, const float* pre_row, int hl, int ph, float phi[2][kS2 / 2]) {
+  constexpr int kP = kS2 / 2;
+  const int lane = threadIdx.x & 31, tl = 2 * lane;
+  float th[2][kP];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const uint4 v = ld_shared_v4(sb + kSmTh + (uint32_t)(tl + r) * kThRow + swz_chunk(tl + r, 2 * hl + ph) * 16);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { th[r][2 * i] = unpack_lo<kHalf>(w[i]); th[r][2 * i + 1] = unpack_hi<kHalf>(w[i]); }
+  }
+  const float mypre = lane < kP ? __ldg(pre_row + 2 + kP * ph + lane) : 0.f;
+#pragma unroll
+  for (int p = 0; p < kP; ++p) {
+    float s0, s1;
+    scan64(th[0][p], th[1][p], s0, s1);
+    const float pre = __shfl_sync(0xffffffffu, mypre, p);
+    phi[0][p] = pre + s0;
+    phi[1][p] = pre + s1;
+  }
+}
+
+// Forward, one CTA per (batch, 64-token block, kHG heads); warp (head hl, pair half ph). While the
+// copies are in flight, the ph = 0 warp of a head scans g and writes the g, rowf and colf planes, the
+// ph = 1 warp scans F; then each warp rotates its eight pairs of C and B in shared memory, and the
+// rotated rows leave as coalesced runs (64 tokens x 64 bytes per head are contiguous in c~, b~).
 template <bool kHalf>
 __global__ void __launch_bounds__(256) prep_fwd_kernel(PrepArgs a) {
-  const int c = blockIdx.x, b = blockIdx.y;
+  extern __shared__ __align__(16) uint8_t sm[];
+  constexpr int kP = kS2 / 2;
+  const int c = blockIdx.x, b = blockIdx.y, h0 = blockIdx.z * kHG;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t0 = c * kBlk + 2 * lane;
-  for (int h = warp; h < a.H; h += 8) {
-    const int64_t bh = (int64_t)b * a.H + h;
-    float la[2], lf[2], th[2][kS2];
-    load_elems<kHalf>(a, b, h, t0, la, lf, th);
-    const float mypre = lane < kTot ? __ldg(a.tot + (bh * a.nch + c) * kTot + lane) : 0.f;   // prefix of the blocks before c
+  const uint32_t sb = smem_u32(sm);
+  const int tb = c * kBlk, tl = 2 * lane;
+  stage_rot_rows(a.proj, a.proj_sb, a.proj_sl, b, tb, h0, a.L, a.H, a.col_c, a.col_b, a.col_th, sb);
+  const int hl = warp >> 1, ph = warp & 1, h = h0 + hl;
+  const int64_t bh = (int64_t)b * a.H + h;
+  const float* pre_row = a.tot + (bh * a.nch + c) * kTot;   // exclusive prefixes of this block
+  if (h < a.H) {
+    float x[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int t = tb + tl + r;
+      const bool ok = t < a.L;
+      if (ph == 0) {
+        const int64_t row = (int64_t)b * a.proj_sb + (int64_t)(ok ? t : 0) * a.proj_sl;
+        x[r] = ok ? neg_softplus(ld_lp<kHalf>(a.proj, row + a.col_a + h)) : 0.f;
+      } else {
+        x[r] = (ok && a.z) ? logsigmoid(__ldg(a.z + (int64_t)b * a.z_sb + (int64_t)t * a.z_sl + h)) : 0.f;
+      }
+    }
     float s0, s1;
-    // g, rowf, colf
-    scan64(la[0], la[1], s0, s1);
-    const float pre_g = __shfl_sync(0xffffffffu, mypre, 0);
-    const float g0 = pre_g + s0, g1 = pre_g + s1;
-    const float gs = __shfl_sync(0xffffffffu, g0, 0);
-    const float ge = __shfl_sync(0xffffffffu, g1, 31);   // masked rows add 0: equals the last valid g
-    // F
-    scan64(lf[0], lf[1], s0, s1);
-    const float pre_f = __shfl_sync(0xffffffffu, mypre, 1);
-    const float f0 = pre_f + s0, f1 = pre_f + s1;
-    const float gg[2] = {g0, g1}, ff[2] = {f0, f1};
-    {
+    scan64(x[0], x[1], s0, s1);
+    const float pre = __ldg(pre_row + ph);
+    const float v[2] = {pre + s0, pre + s1};
+    float* pl = a.pos + bh * 4 * a.Lp;
+    const int t0 = tb + tl;
+    auto store_plane = [&](float* q, float e0, float e1) {
+      if (t0 + 1 < a.L) *reinterpret_cast<float2*>(q + t0) = make_float2(e0, e1);
+      else if (t0 < a.L) q[t0] = e0;
+    };
+    if (ph == 0) {
+      const float gs = __shfl_sync(0xffffffffu, v[0], 0);
+      const float ge = __shfl_sync(0xffffffffu, v[1], 31);   // masked rows add 0: equals the last valid g
       float rf[2], cf[2];
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
-        rf[r] = exp2f(fminf((gg[r] - gs) * kLog2e, 0.f));
-        cf[r] = exp2f(fminf((ge - gg[r]) * kLog2e, 0.f));
+        rf[r] = exp2f(fminf((v[r] - gs) * kLog2e, 0.f));
+        cf[r] = exp2f(fminf((ge - v[r]) * kLog2e, 0.f));
       }
-      store_planes(a.pos + bh * 4 * a.Lp, a.Lp, t0, a.L, gg, ff, rf, cf);
+      store_plane(pl, v[0], v[1]);
+      store_plane(pl + 2 * a.Lp, rf[0], rf[1]);
+      store_plane(pl + 3 * a.Lp, cf[0], cf[1]);
+    } else {
+      store_plane(pl + a.Lp, v[0], v[1]);
     }
-    // Phi and the rotation of C and B
-    float phi[2][kS2];
-#pragma unroll
-    for (int p = 0; p < kS2; ++p) {
-      scan64(th[0][p], th[1][p], s0, s1);
-      const float pre = __shfl_sync(0xffffffffu, mypre, 2 + p);
-      phi[0][p] = pre + s0;
-      phi[1][p] = pre + s1;
-    }
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  if (h < a.H) {
+    float phi[2][kP];
+    stage_phi<kHalf>(sb, pre_row, hl, ph, phi);
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
-      const int t = t0 + r;
-      if (t >= a.L) continue;
-      const int64_t row = (int64_t)b * a.proj_sb + (int64_t)t * a.proj_sl;
-      float cs[kS2], sn[kS2];
+      const int t = tl + r;
+      if (tb + t >= a.L) continue;
+      float cs[kP], sn[kP];
 #pragma unroll
-      for (int p = 0; p < kS2; ++p) sincosf(phi[r][p], &sn[p], &cs[p]);
+      for (int p = 0; p < kP; ++p) sincosf(phi[r][p], &sn[p], &cs[p]);
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
-        const int col = (which == 0 ? a.col_c : a.col_b) + h * 32;
-        const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const char*>(a.proj) + (row + col) * 2);
-        uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(which == 0 ? a.c_rot : a.b_rot) +
-                                              ((bh * a.L + t) * 32) * 2);
-        uint4 vq[4];
+        const uint32_t zrow = sb + (which == 0 ? kSmC : kSmB) + (uint32_t)t * kRotRow;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) vq[q] = __ldg(src + q);
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const uint4 v = vq[q];
+        for (int q = 0; q < 2; ++q) {
+          const uint32_t za = zrow + swz_chunk(t, 4 * hl + 2 * ph + q) * 16;
+          const uint4 v = ld_shared_v4(za);
           const uint32_t w[4] = {v.x, v.y, v.z, v.w};
           uint32_t o[4];
 #pragma unroll
@@ -273,10 +351,19 @@ __global__ void __launch_bounds__(256) prep_fwd_kernel(PrepArgs a) {
             const float ze = unpack_lo<kHalf>(w[i]), zo = unpack_hi<kHalf>(w[i]);
             o[i] = pack2<kHalf>(ze * cs[p] - zo * sn[p], ze * sn[p] + zo * cs[p]);
           }
-          dst[q] = make_uint4(o[0], o[1], o[2], o[3]);
+          st_shared_v4(za, o[0], o[1], o[2], o[3]);
         }
       }
     }
+  }
+  __syncthreads();
+  for (int k = threadIdx.x; k < kHG * kBlk * 4; k += blockDim.x) {
+    const int hk = k >> 8, t = (k >> 2) & (kBlk - 1), q = k & 3;
+    if (tb + t >= a.L || h0 + hk >= a.H) continue;
+    const uint32_t so = (uint32_t)t * kRotRow + swz_chunk(t, 4 * hk + q) * 16;
+    const int64_t e = (((int64_t)b * a.H + h0 + hk) * a.L + tb + t) * 64 + q * 16;   // bytes
+    *reinterpret_cast<uint4*>(static_cast<char*>(a.c_rot) + e) = ld_shared_v4(sb + kSmC + so);
+    *reinterpret_cast<uint4*>(static_cast<char*>(a.b_rot) + e) = ld_shared_v4(sb + kSmB + so);
   }
 }
 
@@ -347,24 +434,10 @@ struct PrepBwdArgs {
   int32_t* status;
 };
 
-// First backward pass, one CTA per (batch, 64-token block, kHG heads). The rows' C, B and theta
-// columns of those heads and their dc~, db~ rows are copied into shared memory with coalesced 16-byte
-// copies (16 threads per 256-byte row segment) instead of one scattered row segment per lane; warp
-// (head, pair half) then computes, per lane, tokens 2l and 2l+1 with the forward's scan for Phi:
-// dC and dB (final, written back into the staged rows and stored coalesced), the per-token d Phi and
-// the fp64 block totals of dg, dF and d Phi.
-constexpr int kHG = 4;
-constexpr uint32_t kRotRow = kHG * 64;   // bytes of one token's C (or B) columns of kHG heads
-constexpr uint32_t kThRow = kHG * 32;    // theta bytes of one token
-constexpr uint32_t kSmC = 0, kSmB = kSmC + kBlk * kRotRow, kSmTh = kSmB + kBlk * kRotRow;
-constexpr uint32_t kSmDc = kSmTh + kBlk * kThRow, kSmDb = kSmDc + kHG * kBlk * 128;
-constexpr uint32_t kSmBrot = kSmDb + kHG * kBlk * 128;   // 106496 bytes
-// 16-byte chunk ch of token row t sits at chunk (ch & ~7) | ((ch ^ (t >> 1)) & 7): the 32 lanes of a
-// warp, owning tokens 2l and 2l+1, read one logical chunk from eight different bank groups.
-__device__ __forceinline__ uint32_t swz_chunk(int t, int ch) {
-  return ((uint32_t)ch & ~7u) | (((uint32_t)ch ^ ((uint32_t)t >> 1)) & 7u);
-}
-
+// First backward pass, one CTA per (batch, 64-token block, kHG heads), laid out like the forward's
+// rotation pass plus the heads' dc~ and db~ rows; warp (head, pair half) computes, per lane, tokens 2l
+// and 2l+1 with the forward's Phi: dC and dB (final, written back into the staged rows and stored
+// coalesced), the per-token d Phi and the fp64 block totals of dg, dF and d Phi.
 template <bool kHalf>
 __global__ void __launch_bounds__(256, 2) prep_brot_kernel(PrepBwdArgs a) {
   extern __shared__ __align__(16) uint8_t sm[];
@@ -374,21 +447,7 @@ __global__ void __launch_bounds__(256, 2) prep_brot_kernel(PrepBwdArgs a) {
   const int tb = c * kBlk;
   const char* proj = static_cast<const char*>(a.proj);
   // ---- coalesced copies; rows past L and heads past H become zeros
-  for (int k = tid; k < kBlk * 16; k += 256) {
-    const int t = k >> 4, ch = k & 15;
-    const bool ok = tb + t < a.L && h0 + (ch >> 2) < a.H;
-    const int64_t row = (int64_t)b * a.proj_sb + (int64_t)(ok ? tb + t : 0) * a.proj_sl;
-    const uint32_t so = (uint32_t)t * kRotRow + swz_chunk(t, ch) * 16;
-    cp_async16(sb + kSmC + so, proj + (row + a.col_c + h0 * 32) * 2 + (ok ? ch * 16 : 0), ok ? 16 : 0);
-    cp_async16(sb + kSmB + so, proj + (row + a.col_b + h0 * 32) * 2 + (ok ? ch * 16 : 0), ok ? 16 : 0);
-  }
-  for (int k = tid; k < kBlk * 8; k += 256) {
-    const int t = k >> 3, ch = k & 7;
-    const bool ok = tb + t < a.L && h0 + (ch >> 1) < a.H;
-    const int64_t row = (int64_t)b * a.proj_sb + (int64_t)(ok ? tb + t : 0) * a.proj_sl;
-    cp_async16(sb + kSmTh + (uint32_t)t * kThRow + swz_chunk(t, ch) * 16,
-               proj + (row + a.col_th + h0 * kS2) * 2 + (ok ? ch * 16 : 0), ok ? 16 : 0);
-  }
+  stage_rot_rows(a.proj, a.proj_sb, a.proj_sl, b, tb, h0, a.L, a.H, a.col_c, a.col_b, a.col_th, sb);
   for (int k = tid; k < kHG * kBlk * 8; k += 256) {
     const int hl = k >> 9, t = (k >> 3) & (kBlk - 1), ch = k & 7;
     const bool ok = tb + t < a.L && h0 + hl < a.H;
@@ -419,26 +478,10 @@ __global__ void __launch_bounds__(256, 2) prep_brot_kernel(PrepBwdArgs a) {
       tf = __shfl_sync(0xffffffffu, r0, 0);
       if (lane == 0) { dst[0] = tg; dst[1] = tf; }
     }
-    // Phi of pairs 8 ph .. 8 ph + 7: the forward's in-block scan plus the fp32 prefix of its totals
+    // Phi of pairs 8 ph .. 8 ph + 7, exactly as the forward computed it
     constexpr int kP = kS2 / 2;
-    float th[2][kP];
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const uint4 v = ld_shared_v4(sb + kSmTh + (uint32_t)(tl + r) * kThRow + swz_chunk(tl + r, 2 * hl + ph) * 16);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) { th[r][2 * i] = unpack_lo<kHalf>(w[i]); th[r][2 * i + 1] = unpack_hi<kHalf>(w[i]); }
-    }
-    const float mypre = lane < kP ? __ldg(a.tot + (bh * a.nch + c) * kTot + 2 + kP * ph + lane) : 0.f;
     float phi[2][kP];
-#pragma unroll
-    for (int p = 0; p < kP; ++p) {
-      float s0, s1;
-      scan64(th[0][p], th[1][p], s0, s1);
-      const float pre = __shfl_sync(0xffffffffu, mypre, p);
-      phi[0][p] = pre + s0;
-      phi[1][p] = pre + s1;
-    }
+    stage_phi<kHalf>(sb, a.tot + (bh * a.nch + c) * kTot, hl, ph, phi);
     // d Phi from both rotations; dC = R(Phi)^T dc~, dB = R(Phi)^T db~ written over the staged C, B
     float dphi[2][kP];
 #pragma unroll
@@ -612,6 +655,7 @@ cudaError_t launch_prep_fwd(const PrepFwdLaunch& p, cudaStream_t st) {
   a.c_rot = p.c_rot; a.b_rot = p.b_rot; a.pos = p.pos; a.Lp = (int)p.Lp;
   a.tot = p.tot; a.status = p.status;
   dim3 grid(a.nch, a.B);
+  dim3 grid_rot(a.nch, a.B, (a.H + kHG - 1) / kHG);
   if (p.dtype == 1) {
     prep_sums_kernel<true><<<grid, 256, 0, st>>>(a);
   } else {
@@ -619,8 +663,8 @@ cudaError_t launch_prep_fwd(const PrepFwdLaunch& p, cudaStream_t st) {
   }
   const int64_t nchains = (int64_t)a.B * a.H * kTot;
   block_scan_kernel<float, false><<<(unsigned)((nchains + 7) / 8), 256, 0, st>>>(a.tot, nchains, a.nch);
-  if (p.dtype == 1) prep_fwd_kernel<true><<<grid, 256, 0, st>>>(a);
-  else prep_fwd_kernel<false><<<grid, 256, 0, st>>>(a);
+  if (p.dtype == 1) prep_fwd_kernel<true><<<grid_rot, 256, kSmFrot, st>>>(a);
+  else prep_fwd_kernel<false><<<grid_rot, 256, kSmFrot, st>>>(a);
   return cudaGetLastError();
 }
 
