@@ -445,7 +445,6 @@ __global__ void __launch_bounds__(256, 2) prep_brot_kernel(PrepBwdArgs a) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t sb = smem_u32(sm);
   const int tb = c * kBlk;
-  const char* proj = static_cast<const char*>(a.proj);
   // ---- coalesced copies; rows past L and heads past H become zeros
   stage_rot_rows(a.proj, a.proj_sb, a.proj_sl, b, tb, h0, a.L, a.H, a.col_c, a.col_b, a.col_th, sb);
   for (int k = tid; k < kHG * kBlk * 8; k += 256) {
@@ -557,89 +556,106 @@ __device__ __forceinline__ void st_lp(void* p, int64_t i, float v) {
   else reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
 }
 
-// Two CTAs per SM (128 registers): the kernel is latency-bound on its loads, and the second CTA's warps
-// keep twice the bytes in flight (measured 0.271 -> 0.237 ms at cfg1 despite a small spill).
+// Second backward pass, one CTA per (batch, 64-token block, kHG heads), laid out like the rotation
+// passes. The heads' per-token d Phi rows (64 bytes, contiguous per head) are staged with coalesced
+// copies, two tokens per 128-byte line, chunk-swizzled by line. Warp (head hl, pair half ph) forms d
+// theta of its eight pairs (fp64 suffix sums, rounded once) into a staged theta tile that leaves as
+// coalesced row segments; while the copies fly, the ph = 0 warp of a head writes d alpha, the ph = 1
+// warp dz.
+constexpr uint32_t kSmDphi = 0;                                   // [kHG][32 lines][128 B] fp32
+constexpr uint32_t kSmDth = kSmDphi + kHG * kBlk * 64;            // [64 tokens][kThRow] low precision
+constexpr uint32_t kSmBwd2 = kSmDth + kBlk * kThRow;              // 24576 bytes
+
 template <bool kHalf>
-__global__ void __launch_bounds__(256, 2) prep_bwd_kernel(PrepBwdArgs a) {
-  const int c = blockIdx.x, b = blockIdx.y;
+__global__ void __launch_bounds__(256) prep_bwd_kernel(PrepBwdArgs a) {
+  extern __shared__ __align__(16) uint8_t sm[];
+  constexpr int kP = kS2 / 2;
+  const int c = blockIdx.x, b = blockIdx.y, h0 = blockIdx.z * kHG;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t0 = c * kBlk + 2 * lane;
-  for (int h = warp; h < a.H; h += 8) {
-    const int64_t bh = (int64_t)b * a.H + h;
-    const double mysuf = lane < kTot ? __ldg(a.bt + (bh * a.nch + c) * kTot + lane) : 0.0;   // sum of the blocks after c
-    double x0, x1, r0, r1;
-    // d alpha = -(sum_{s>=t} dg_s) * softplus'(alpha)
-    x0 = t0 < a.L ? (double)__ldg(a.dg + bh * a.L + t0) : 0.0;
-    x1 = t0 + 1 < a.L ? (double)__ldg(a.dg + bh * a.L + t0 + 1) : 0.0;
+  const uint32_t sb = smem_u32(sm);
+  const int tb = c * kBlk, tl = 2 * lane;
+  for (int k = threadIdx.x; k < kHG * kBlk * 4; k += blockDim.x) {
+    const int hk = k >> 8, t = (k >> 2) & (kBlk - 1), q = k & 3;
+    const bool ok = tb + t < a.L && h0 + hk < a.H;
+    const int64_t e = (((int64_t)b * a.H + (ok ? h0 + hk : 0)) * a.L + (ok ? tb + t : 0)) * kS2 + q * 4;
+    cp_async16(sb + kSmDphi + (uint32_t)hk * (kBlk * 64) + (uint32_t)(t >> 1) * 128 + swz_chunk(t, (t & 1) * 4 + q) * 16,
+               a.dphi + e, ok ? 16 : 0);
+  }
+  const int hl = warp >> 1, ph = warp & 1, h = h0 + hl;
+  const int64_t bh = (int64_t)b * a.H + h;
+  const double* suf_row = a.bt + (bh * a.nch + c) * kTot;   // sums of the totals of the blocks after c
+  if (h < a.H && (ph == 0 || a.z)) {
+    // ph 0: d alpha = -(sum_{s>=t} dg_s) softplus'(alpha); ph 1: dz = (sum_{s>=t} dF_s) logsigmoid'(z)
+    const float* src = ph == 0 ? a.dg : a.dF;
+    double r0, r1;
+    const double x0 = (src && tb + tl < a.L) ? (double)__ldg(src + bh * a.L + tb + tl) : 0.0;
+    const double x1 = (src && tb + tl + 1 < a.L) ? (double)__ldg(src + bh * a.L + tb + tl + 1) : 0.0;
     rscan64(x0, x1, r0, r1);
-    {
-      const double suf = __shfl_sync(0xffffffffu, mysuf, 0);
-      const double rr[2] = {r0, r1};
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int t = t0 + r;
-        if (t >= a.L) continue;
-        const float dla = (float)(suf + rr[r]);
-        const int64_t row = (int64_t)b * a.proj_sb + (int64_t)t * a.proj_sl;
-        const float al = ld_lp<kHalf>(a.proj, row + a.col_a + h);
-        st_lp<kHalf>(a.dproj, (int64_t)b * a.dproj_sb + (int64_t)t * a.dproj_sl + a.col_a + h,
-                     -dla * softplus_grad(al));
-      }
-    }
-    // dz = (sum_{s>=t} dF_s) * logsigmoid'(z)
-    if (a.z) {
-      x0 = (a.dF && t0 < a.L) ? (double)__ldg(a.dF + bh * a.L + t0) : 0.0;
-      x1 = (a.dF && t0 + 1 < a.L) ? (double)__ldg(a.dF + bh * a.L + t0 + 1) : 0.0;
-      rscan64(x0, x1, r0, r1);
-      const double suf = __shfl_sync(0xffffffffu, mysuf, 1);
-      const double rr[2] = {r0, r1};
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int t = t0 + r;
-        if (t >= a.L) continue;
-        const float dlf = (float)(suf + rr[r]);
-        const float zv = __ldg(a.z + (int64_t)b * a.z_sb + (int64_t)t * a.z_sl + h);
-        a.dz[((int64_t)b * a.L + t) * a.H + h] = dlf * logsigmoid_grad(zv);
-      }
-    }
-    // d theta = sum_{s>=t} dPhi_s (dC and dB were written by the first pass)
-    float dphi[2][kS2];
+    const double suf = __ldg(suf_row + ph);
+    const double rr[2] = {r0, r1};
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
-      const bool ok = t0 + r < a.L;
-      const float4* src = reinterpret_cast<const float4*>(a.dphi + (bh * a.L + (ok ? t0 + r : 0)) * kS2);
-#pragma unroll
-      for (int q = 0; q < kS2 / 4; ++q) {
-        const float4 v = ok ? __ldg(src + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-        dphi[r][4 * q] = v.x; dphi[r][4 * q + 1] = v.y; dphi[r][4 * q + 2] = v.z; dphi[r][4 * q + 3] = v.w;
+      const int t = tb + tl + r;
+      if (t >= a.L) continue;
+      const float sum = (float)(suf + rr[r]);
+      if (ph == 0) {
+        const int64_t row = (int64_t)b * a.proj_sb + (int64_t)t * a.proj_sl;
+        const float al = ld_lp<kHalf>(a.proj, row + a.col_a + h);
+        st_lp<kHalf>(a.dproj, (int64_t)b * a.dproj_sb + (int64_t)t * a.dproj_sl + a.col_a + h, -sum * softplus_grad(al));
+      } else {
+        const float zv = __ldg(a.z + (int64_t)b * a.z_sb + (int64_t)t * a.z_sl + h);
+        a.dz[((int64_t)b * a.L + t) * a.H + h] = sum * logsigmoid_grad(zv);
       }
     }
-    float dth[2][kS2];
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  if (h < a.H) {
+    // d theta = sum_{s>=t} dPhi_s (dC and dB were written by the first pass)
+    float dphi[2][kP];
 #pragma unroll
-    for (int p = 0; p < kS2; ++p) {
+    for (int r = 0; r < 2; ++r) {
+      const int t = tl + r;
+      const uint32_t line = sb + kSmDphi + (uint32_t)hl * (kBlk * 64) + (uint32_t)(t >> 1) * 128;
+      const uint4 v0 = ld_shared_v4(line + swz_chunk(t, (t & 1) * 4 + 2 * ph) * 16);
+      const uint4 v1 = ld_shared_v4(line + swz_chunk(t, (t & 1) * 4 + 2 * ph + 1) * 16);
+      const uint32_t w[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+      for (int p = 0; p < kP; ++p) dphi[r][p] = __uint_as_float(w[p]);
+    }
+    const double mysuf = lane < kP ? __ldg(suf_row + 2 + kP * ph + lane) : 0.0;
+    float dth[2][kP];
+#pragma unroll
+    for (int p = 0; p < kP; ++p) {
+      double r0, r1;
       rscan64((double)dphi[0][p], (double)dphi[1][p], r0, r1);
-      const double suf = __shfl_sync(0xffffffffu, mysuf, 2 + p);
+      const double suf = __shfl_sync(0xffffffffu, mysuf, p);
       dth[0][p] = (float)(suf + r0);
       dth[1][p] = (float)(suf + r1);
     }
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
-      const int t = t0 + r;
-      if (t >= a.L) continue;
-      uint32_t o[8];
+      const int t = tl + r;
+      uint32_t o[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = pack2<kHalf>(dth[r][2 * i], dth[r][2 * i + 1]);
-      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<char*>(a.dproj) +
-                                            ((int64_t)b * a.dproj_sb + (int64_t)t * a.dproj_sl + a.col_th + h * kS2) * 2);
-      dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-      dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+      for (int i = 0; i < 4; ++i) o[i] = pack2<kHalf>(dth[r][2 * i], dth[r][2 * i + 1]);
+      st_shared_v4(sb + kSmDth + (uint32_t)t * kThRow + swz_chunk(t, 2 * hl + ph) * 16, o[0], o[1], o[2], o[3]);
     }
   }
-  // zero the padding columns [ntot, npad) of this block's rows
+  __syncthreads();
+  char* dproj = static_cast<char*>(a.dproj);
+  for (int k = threadIdx.x; k < kBlk * 8; k += blockDim.x) {
+    const int t = k >> 3, ch = k & 7;
+    if (tb + t >= a.L || h0 + (ch >> 1) >= a.H) continue;
+    const int64_t drow = (int64_t)b * a.dproj_sb + (int64_t)(tb + t) * a.dproj_sl;
+    *reinterpret_cast<uint4*>(dproj + (drow + a.col_th + h0 * kS2) * 2 + ch * 16) =
+        ld_shared_v4(sb + kSmDth + (uint32_t)t * kThRow + swz_chunk(t, ch) * 16);
+  }
+  // zero the padding columns [ntot, npad) of this block's rows (first head group only)
   const int npadc = a.npad - a.ntot;
-  if (npadc > 0) {
+  if (npadc > 0 && blockIdx.z == 0) {
     for (int i = threadIdx.x; i < kBlk * npadc; i += blockDim.x) {
-      const int t = c * kBlk + i / npadc;
+      const int t = tb + i / npadc;
       if (t < a.L) st_lp<kHalf>(a.dproj, (int64_t)b * a.dproj_sb + (int64_t)t * a.dproj_sl + a.ntot + i % npadc, 0.f);
     }
   }
@@ -690,7 +706,6 @@ cudaError_t launch_prep_bwd(const PrepBwdLaunch& p, cudaStream_t st) {
   a.dproj = p.dproj; a.dproj_sb = p.dproj_sb; a.dproj_sl = p.dproj_sl; a.dz = p.dz; a.bt = p.bt;
   a.dphi = reinterpret_cast<float*>(p.bt + (int64_t)a.B * a.H * a.nch * kTot);
   a.status = p.status;
-  dim3 grid(a.nch, a.B);
   dim3 grid_rot(a.nch, a.B, (a.H + kHG - 1) / kHG);
   if (p.dtype == 1) {
     cudaFuncSetAttribute(prep_brot_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmBrot);
@@ -701,8 +716,8 @@ cudaError_t launch_prep_bwd(const PrepBwdLaunch& p, cudaStream_t st) {
   }
   const int64_t nchains = (int64_t)a.B * a.H * kTot;
   block_scan_kernel<double, true><<<(unsigned)((nchains + 7) / 8), 256, 0, st>>>(a.bt, nchains, a.nch);
-  if (p.dtype == 1) prep_bwd_kernel<true><<<grid, 256, 0, st>>>(a);
-  else prep_bwd_kernel<false><<<grid, 256, 0, st>>>(a);
+  if (p.dtype == 1) prep_bwd_kernel<true><<<grid_rot, 256, kSmBwd2, st>>>(a);
+  else prep_bwd_kernel<false><<<grid_rot, 256, kSmBwd2, st>>>(a);
   return cudaGetLastError();
 }
 
