@@ -37,7 +37,6 @@ constexpr uint32_t SZ_K = BN * 128, SZ_V = BN * 128, SZ_ONE = BN * 128, SZ_B = B
 // accumulates sum_j DT(p_ij) on the tensor core.
 constexpr uint32_t OFFS_V = SZ_K, OFFS_ONE = OFFS_V + SZ_V, OFFS_B = OFFS_ONE + SZ_ONE, OFFS_POS = OFFS_B + SZ_B;
 constexpr uint32_t SZ_STAGE = OFFS_POS + SZ_POS;              // 29696 = 29 KiB
-constexpr uint32_t SZ_P = BM * 128;
 constexpr uint32_t OFF_Q = 0, OFF_C = OFF_Q + SZ_Q, OFF_ST = OFF_C + SZ_C;
 constexpr uint32_t OFF_BAR = OFF_ST + NSTAGE * SZ_STAGE;
 constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;

@@ -244,21 +244,27 @@ __device__ __forceinline__ void stage_rot_rows(const void* projv, int64_t proj_s
   }
 }
 
-// Phi of pairs [8 ph, 8 ph + 8) of head hl for tokens tl, tl + 1 (tl = 2 lane): the staged theta,
+// Phi of pairs [kP pg, kP pg + kP) of head hl for tokens tl, tl + 1 (tl = 2 lane): the staged theta,
 // the in-block warp scan and the block's prefix (the forward's exact arithmetic).
-template <bool kHalf>
-__device__ __forceinline__ void stage_phi(uint32_t sb, const float* pre_row, int hl, int ph, float phi[2][kS2 / 2]) {
-  constexpr int kP = kS2 / 2;
+template <bool kHalf, int kP>
+__device__ __forceinline__ void stage_phi(uint32_t sb, const float* pre_row, int hl, int pg, float phi[2][kP]) {
+  static_assert(kP == 8 || kP == 4, "eight or four pairs per warp");
   const int lane = threadIdx.x & 31, tl = 2 * lane;
   float th[2][kP];
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
-    const uint4 v = ld_shared_v4(sb + kSmTh + (uint32_t)(tl + r) * kThRow + swz_chunk(tl + r, 2 * hl + ph) * 16);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    const uint32_t ca = sb + kSmTh + (uint32_t)(tl + r) * kThRow + swz_chunk(tl + r, 2 * hl + kP * pg / 8) * 16;
+    uint32_t w[kP / 2];
+    if constexpr (kP == 8) {
+      const uint4 v = ld_shared_v4(ca);
+      w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+    } else {
+      asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(w[0]), "=r"(w[1]) : "r"(ca + 8 * (pg & 1)) : "memory");
+    }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) { th[r][2 * i] = unpack_lo<kHalf>(w[i]); th[r][2 * i + 1] = unpack_hi<kHalf>(w[i]); }
+    for (int i = 0; i < kP / 2; ++i) { th[r][2 * i] = unpack_lo<kHalf>(w[i]); th[r][2 * i + 1] = unpack_hi<kHalf>(w[i]); }
   }
-  const float mypre = lane < kP ? __ldg(pre_row + 2 + kP * ph + lane) : 0.f;
+  const float mypre = lane < kP ? __ldg(pre_row + 2 + kP * pg + lane) : 0.f;
 #pragma unroll
   for (int p = 0; p < kP; ++p) {
     float s0, s1;
@@ -328,7 +334,7 @@ __global__ void __launch_bounds__(256) prep_fwd_kernel(PrepArgs a) {
   __syncthreads();
   if (h < a.H) {
     float phi[2][kP];
-    stage_phi<kHalf>(sb, pre_row, hl, ph, phi);
+    stage_phi<kHalf, kP>(sb, pre_row, hl, ph, phi);
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
       const int t = tl + r;
@@ -438,16 +444,19 @@ struct PrepBwdArgs {
 // rotation pass plus the heads' dc~ and db~ rows; warp (head, pair half) computes, per lane, tokens 2l
 // and 2l+1 with the forward's Phi: dC and dB (final, written back into the staged rows and stored
 // coalesced), the per-token d Phi and the fp64 block totals of dg, dF and d Phi.
+constexpr int kBrotP = 4;                                    // pairs per warp
+constexpr int kBrotThreads = kHG * (kS2 / kBrotP) * 32;      // 512
 template <bool kHalf>
-__global__ void __launch_bounds__(256, 2) prep_brot_kernel(PrepBwdArgs a) {
+__global__ void __launch_bounds__(kBrotThreads, 2) prep_brot_kernel(PrepBwdArgs a) {
   extern __shared__ __align__(16) uint8_t sm[];
+  constexpr int kP = kBrotP, kWph = kS2 / kP;
   const int c = blockIdx.x, b = blockIdx.y, h0 = blockIdx.z * kHG;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t sb = smem_u32(sm);
   const int tb = c * kBlk;
   // ---- coalesced copies; rows past L and heads past H become zeros
   stage_rot_rows(a.proj, a.proj_sb, a.proj_sl, b, tb, h0, a.L, a.H, a.col_c, a.col_b, a.col_th, sb);
-  for (int k = tid; k < kHG * kBlk * 8; k += 256) {
+  for (int k = tid; k < kHG * kBlk * 8; k += blockDim.x) {
     const int hl = k >> 9, t = (k >> 3) & (kBlk - 1), ch = k & 7;
     const bool ok = tb + t < a.L && h0 + hl < a.H;
     const int64_t e = (((int64_t)b * a.H + (ok ? h0 + hl : 0)) * a.L + (ok ? tb + t : 0)) * 32 + ch * 4;
@@ -458,13 +467,13 @@ __global__ void __launch_bounds__(256, 2) prep_brot_kernel(PrepBwdArgs a) {
   cp_async_wait_all();
   __syncthreads();
 
-  const int hl = warp >> 1, ph = warp & 1;   // head in the group; pairs 8 ph .. 8 ph + 7
+  const int hl = warp / kWph, pg = warp % kWph;   // head in the group; pairs kP pg .. kP pg + kP - 1
   const int h = h0 + hl;
   if (h < a.H) {
     const int64_t bh = (int64_t)b * a.H + h;
     const int tl = 2 * lane;
     double* dst = a.bt + (bh * a.nch + c) * kTot;
-    if (ph == 0) {
+    if (pg == 0) {
       // block totals of dg and dF
       double x0, x1, r0, r1, tg, tf;
       x0 = tb + tl < a.L ? (double)__ldg(a.dg + bh * a.L + tb + tl) : 0.0;
@@ -477,10 +486,9 @@ __global__ void __launch_bounds__(256, 2) prep_brot_kernel(PrepBwdArgs a) {
       tf = __shfl_sync(0xffffffffu, r0, 0);
       if (lane == 0) { dst[0] = tg; dst[1] = tf; }
     }
-    // Phi of pairs 8 ph .. 8 ph + 7, exactly as the forward computed it
-    constexpr int kP = kS2 / 2;
+    // Phi of this warp's pairs, exactly as the forward computed it
     float phi[2][kP];
-    stage_phi<kHalf>(sb, a.tot + (bh * a.nch + c) * kTot, hl, ph, phi);
+    stage_phi<kHalf, kP>(sb, a.tot + (bh * a.nch + c) * kTot, hl, pg, phi);
     // d Phi from both rotations; dC = R(Phi)^T dc~, dB = R(Phi)^T db~ written over the staged C, B
     float dphi[2][kP];
 #pragma unroll
@@ -497,11 +505,11 @@ __global__ void __launch_bounds__(256, 2) prep_brot_kernel(PrepBwdArgs a) {
         const uint32_t zrow = sb + (which == 0 ? kSmC : kSmB) + (uint32_t)t * kRotRow;
         const uint32_t grow = sb + (which == 0 ? kSmDc : kSmDb) + (uint32_t)hl * (kBlk * 128) + (uint32_t)t * 128;
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const uint32_t za = zrow + swz_chunk(t, 4 * hl + 2 * ph + q) * 16;
+        for (int q = 0; q < kP / 4; ++q) {   // four pairs: one 16-byte chunk of C (B), two of dc~ (db~)
+          const uint32_t za = zrow + swz_chunk(t, 4 * hl + (kP / 4) * pg + q) * 16;
           const uint4 v = ld_shared_v4(za);
-          const uint4 g0 = ld_shared_v4(grow + swz_chunk(t, 4 * ph + 2 * q) * 16);
-          const uint4 g1 = ld_shared_v4(grow + swz_chunk(t, 4 * ph + 2 * q + 1) * 16);
+          const uint4 g0 = ld_shared_v4(grow + swz_chunk(t, (kP / 2) * pg + 2 * q) * 16);
+          const uint4 g1 = ld_shared_v4(grow + swz_chunk(t, (kP / 2) * pg + 2 * q + 1) * 16);
           const uint32_t w[4] = {v.x, v.y, v.z, v.w};
           const float gd[8] = {__uint_as_float(g0.x), __uint_as_float(g0.y), __uint_as_float(g0.z), __uint_as_float(g0.w),
                                __uint_as_float(g1.x), __uint_as_float(g1.y), __uint_as_float(g1.z), __uint_as_float(g1.w)};
@@ -519,9 +527,10 @@ __global__ void __launch_bounds__(256, 2) prep_brot_kernel(PrepBwdArgs a) {
           st_shared_v4(za, o[0], o[1], o[2], o[3]);
         }
       }
-      float4* dp = reinterpret_cast<float4*>(a.dphi + (bh * a.L + tb + t) * kS2 + kP * ph);
-      dp[0] = make_float4(dphi[r][0], dphi[r][1], dphi[r][2], dphi[r][3]);
-      dp[1] = make_float4(dphi[r][4], dphi[r][5], dphi[r][6], dphi[r][7]);
+      float4* dp = reinterpret_cast<float4*>(a.dphi + (bh * a.L + tb + t) * kS2 + kP * pg);
+#pragma unroll
+      for (int q = 0; q < kP / 4; ++q)
+        dp[q] = make_float4(dphi[r][4 * q], dphi[r][4 * q + 1], dphi[r][4 * q + 2], dphi[r][4 * q + 3]);
     }
     double tv[kP];
 #pragma unroll
@@ -534,13 +543,13 @@ __global__ void __launch_bounds__(256, 2) prep_brot_kernel(PrepBwdArgs a) {
       double mine = tv[0];
 #pragma unroll
       for (int k = 1; k < kP; ++k) if (lane == k) mine = tv[k];
-      dst[2 + kP * ph + lane] = mine;
+      dst[2 + kP * pg + lane] = mine;
     }
   }
   __syncthreads();
   // ---- coalesced stores of dC and dB
   char* dproj = static_cast<char*>(a.dproj);
-  for (int k = tid; k < kBlk * 16; k += 256) {
+  for (int k = tid; k < kBlk * 16; k += blockDim.x) {
     const int t = k >> 4, ch = k & 15;
     if (tb + t >= a.L || h0 + (ch >> 2) >= a.H) continue;
     const int64_t drow = (int64_t)b * a.dproj_sb + (int64_t)(tb + t) * a.dproj_sl;
@@ -709,10 +718,10 @@ cudaError_t launch_prep_bwd(const PrepBwdLaunch& p, cudaStream_t st) {
   dim3 grid_rot(a.nch, a.B, (a.H + kHG - 1) / kHG);
   if (p.dtype == 1) {
     cudaFuncSetAttribute(prep_brot_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmBrot);
-    prep_brot_kernel<true><<<grid_rot, 256, kSmBrot, st>>>(a);
+    prep_brot_kernel<true><<<grid_rot, kBrotThreads, kSmBrot, st>>>(a);
   } else {
     cudaFuncSetAttribute(prep_brot_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmBrot);
-    prep_brot_kernel<false><<<grid_rot, 256, kSmBrot, st>>>(a);
+    prep_brot_kernel<false><<<grid_rot, kBrotThreads, kSmBrot, st>>>(a);
   }
   const int64_t nchains = (int64_t)a.B * a.H * kTot;
   block_scan_kernel<double, true><<<(unsigned)((nchains + 7) / 8), 256, 0, st>>>(a.bt, nchains, a.nch);
