@@ -51,7 +51,7 @@ constexpr uint32_t SZ_Q = 128 * 128, SZ_DO = 128 * 128, SZ_C = 128 * 64;
 constexpr uint32_t SZ_K = 64 * 128, SZ_V = 64 * 128, SZ_B = 64 * 64, SZ_POS = 64 * 16;
 constexpr uint32_t SZ_STAGE = SZ_K + SZ_V + SZ_B + SZ_POS;   // 21504
 constexpr uint32_t OFF_Q = 0, OFF_DO = OFF_Q + SZ_Q, OFF_C = OFF_DO + SZ_DO, OFF_ST = OFF_C + SZ_C;
-constexpr uint32_t OFF_RED = OFF_ST + NST * SZ_STAGE;          // 128 rows x NWG x 8 floats
+constexpr uint32_t OFF_RED = OFF_ST + NST * SZ_STAGE;          // [8 values][NWG][128 rows] floats
 // o'' of the tile for delta'' (two 128-byte-swizzled boxes of 32 fp32 columns; o itself, when the
 // forward kept no o'', is one 64-column low-precision box)
 constexpr uint32_t SZ_OB = 128 * 128, OFF_O = OFF_RED + 128 * NWG * 8 * 4;
@@ -78,7 +78,7 @@ constexpr uint32_t SZ_K = 128 * 128, SZ_V = 128 * 128, SZ_B = 128 * 64;
 constexpr uint32_t SZ_Q = 64 * 128, SZ_DO = 64 * 128, SZ_C = 64 * 64, SZ_POS = 64 * 16, SZ_RST = 64 * 16;
 constexpr uint32_t SZ_STAGE = SZ_Q + SZ_DO + SZ_C + SZ_POS + SZ_RST;   // 22528
 constexpr uint32_t OFF_K = 0, OFF_V = OFF_K + SZ_K, OFF_B = OFF_V + SZ_V, OFF_ST = OFF_B + SZ_B;
-constexpr uint32_t OFF_RED = OFF_ST + NST * SZ_STAGE;                  // 128 rows x NWG x 2 floats
+constexpr uint32_t OFF_RED = OFF_ST + NST * SZ_STAGE;                  // [2 values][NWG][128 rows] floats
 constexpr uint32_t SZ_DSB = 128 * 128;                                 // (dS^' rq)^T operand: 128 keys x 64 queries
 constexpr uint32_t OFF_DSB = OFF_RED + 128 * NWG * 2 * 4;              // two buffers, K-major, 128-byte swizzle
 constexpr uint32_t OFF_BAR = OFF_DSB + 2 * SZ_DSB;
@@ -291,18 +291,19 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
       }
     }
     // partial sums of the other warpgroups go to wg 0, which forms delta'' (fixed order) and hands it back
-    float* redr = red + r * (NWG * 8);
-    if (wg > 0) redr[wg * 8 + 7] = dh;
+    // row exchange slots, [value][warpgroup][row]: a warp's 32 rows are one 128-byte line
+    auto rx = [&](int k, int w) -> float& { return red[(k * NWG + w) * 128 + r]; };
+    if (wg > 0) rx(7, wg) = dh;
     named_bar_sync(1, NCT);
     float dl = 0.f;
     if (wg == 0) {
       dl = dh;
 #pragma unroll
-      for (int w = 1; w < NWG; ++w) dl += redr[w * 8 + 7];
-      redr[6] = dl;
+      for (int w = 1; w < NWG; ++w) dl += rx(7, w);
+      rx(6, 0) = dl;
     }
     named_bar_sync(1, NCT);
-    if (wg > 0) dl = redr[6];
+    if (wg > 0) dl = rx(6, 0);
     const uint32_t tS = tmem_addr(tbase, quarter, COL_S + wg * NCOL);
     const uint32_t tU = tmem_addr(tbase, quarter, COL_U + wg * NCOL);
     const uint32_t tP = tmem_addr(tbase, quarter, COL_DP + wg * NCOL);
@@ -433,15 +434,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
     ya = fmaf(rowf, yo2.x + yo2.y, ya) + (yd2.x + yd2.y);
     // ---- combine the warpgroups' row sums (wg > 0 -> smem -> wg 0, fixed order)
     if (wg > 0) {
-      redr[wg * 8 + 0] = za; redr[wg * 8 + 1] = ya; redr[wg * 8 + 2] = wa; redr[wg * 8 + 3] = xa;
-      redr[wg * 8 + 4] = ptt; redr[wg * 8 + 5] = dptt; redr[wg * 8 + 6] = xd;
+      rx(0, wg) = za; rx(1, wg) = ya; rx(2, wg) = wa; rx(3, wg) = xa;
+      rx(4, wg) = ptt; rx(5, wg) = dptt; rx(6, wg) = xd;
     }
     named_bar_sync(1, NCT);
     if (wg == 0) {
 #pragma unroll
       for (int w = 1; w < NWG; ++w) {
-        za += redr[w * 8 + 0]; ya += redr[w * 8 + 1]; wa += redr[w * 8 + 2]; xa += redr[w * 8 + 3];
-        ptt += redr[w * 8 + 4]; dptt += redr[w * 8 + 5]; xd += redr[w * 8 + 6];
+        za += rx(0, w); ya += rx(1, w); wa += rx(2, w); xa += rx(3, w);
+        ptt += rx(4, w); dptt += rx(5, w); xd += rx(6, w);
       }
       // exact delta, delta-free diagonal (attention.py:449-480)
       float ssum = ptt + za;
@@ -462,10 +463,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
         p.rg[rb + row] = lam * dl_row;
         p.rf[rb + row] = wa - za * dd;
       }
-      redr[5] = dstt;                         // handed to the other warpgroups for their column slices
+      rx(5, 0) = dstt;                        // handed to the other warpgroups for their column slices
     }
     named_bar_sync(1, NCT);
-    const float dstt = redr[5];
+    const float dstt = rx(5, 0);
     if (ok && !warp_wait(BAR(B_ACC), 0, p.status)) ok = false;
     if (ok && !warp_wait(BAR(B_KR), 0, p.status)) ok = false;
     if (ok) {
@@ -819,8 +820,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
     }
     dfs += dfs2.x + dfs2.y;
     dgu = fmaf(colf, dgo2.x + dgo2.y, dgu) + (dgd2.x + dgd2.y);
-    float* redr = red + r * (NWG * 2);
-    if (wg > 0) { redr[wg * 2 + 0] = dgu; redr[wg * 2 + 1] = dfs; }
+    // row exchange slots, [value][warpgroup][row]: a warp's 32 rows are one 128-byte line
+    auto rx = [&](int k, int w) -> float& { return red[(k * NWG + w) * 128 + r]; };
+    if (wg > 0) { rx(0, wg) = dgu; rx(1, wg) = dfs; }
     named_bar_sync(1, NCT);
     if (ok && !warp_wait(BAR(B_ACC), 0, p.status)) ok = false;
     if (ok) {
@@ -858,7 +860,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
       fence_proxy_async_smem();
       if (wg == 0 && vcol) {
 #pragma unroll
-        for (int w = 1; w < NWG; ++w) { dgu += redr[w * 2 + 0]; dfs += redr[w * 2 + 1]; }
+        for (int w = 1; w < NWG; ++w) { dgu += rx(0, w); dfs += rx(1, w); }
         p.dg[rb + j] = p.rg[rb + j] - lam * dgu;
         if (p.dF) p.dF[rb + j] = p.rf[rb + j] - dfs;
       }
