@@ -41,7 +41,7 @@ FWD_FLOP_PER_PAIR = 320
 # DRAM bytes (read + write) of attn_fwd + attn_bwd_dq + attn_bwd_dkv for one cfg1 step: ncu
 # dram__bytes_read.sum + dram__bytes_write.sum at B=1, H=8, T=4096 (profiles/attn_kernels_B1T4096H8_ncu.md),
 # scaled by the number of (batch, head, position) units; the traffic per unit does not depend on B or H.
-ATTN_TRAFFIC_PER_UNIT = 1.2158e9 / (8 * 16 * 4096)
+ATTN_TRAFFIC_PER_UNIT = 1.1537e9 / (8 * 16 * 4096)
 METRIC = "SISA attn fwd+bwd TFLOP/s (T=4096 bf16)"
 
 
@@ -286,7 +286,7 @@ def run_cuda(args):
             "clocks": clk.summary(),
         }
         if not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(args.cpu_sample_heads)
+            line["cpu_baseline"] = cpu_baseline(H)
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.barrier()
@@ -392,19 +392,22 @@ def cpu_step(heads, seed=0):
     return FLOP_PER_PAIR * pairs(1, heads, T)
 
 
-def cpu_baseline(heads):
+def cpu_baseline(heads, budget_s=10.0, max_steps=64):
+    """The oracle port on the host cores: B=1 x `heads` units at the full T per sample, new seeds, until
+    about `budget_s` seconds of CPU work have run (at least two samples)."""
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     cpu_step(heads, seed=1)
     t0 = time.perf_counter()
-    n = 2
+    n = 0
     flop = 0
-    for i in range(n):
-        flop += cpu_step(heads, seed=2 + i)
+    while n < 2 or (time.perf_counter() - t0 < budget_s and n < max_steps):
+        flop += cpu_step(heads, seed=2 + n)
+        n += 1
     dt = time.perf_counter() - t0
     return {"value": round(flop / dt / 1e12, 5), "unit": "TFLOP/s", "cores": threads, "kind": "port",
-            "sample": f"{n} steps of B=1 x H={heads} heads at T=4096 (1/{B * H // heads} of a cfg1 step), fp32, "
-                      f"{dt:.1f} s"}
+            "sample": f"{n} samples of B=1 x H={heads} heads at T=4096 ({B * H // heads} samples make a cfg1 step), "
+                      f"fp32, {dt:.1f} s"}
 
 
 def run_lce(args):

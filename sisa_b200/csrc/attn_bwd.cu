@@ -132,7 +132,34 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
   const uint32_t bar0 = sbase + OFF_BAR;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + 128);
 #define BAR(i) (bar0 + 8u * (uint32_t)(i))
-  if (tid == 0) {
+  auto key0 = [&](int n) { return n < ndiag ? m0 + n * 64 : (n - ndiag) * 64; };
+  auto stage_addr = [&](int s) { return sbase + OFF_ST + (uint32_t)s * SZ_STAGE; };
+  // The TMA thread initialises the barriers and issues the resident tiles and the first NST key tiles
+  // before the block-wide sync (which also waits for the TMEM allocation): nothing else touches those
+  // barriers or buffers until after it, and the loads' latency starts that much earlier.
+  const int npre = ntiles < NST ? ntiles : NST;
+  auto issue_stage = [&](int n) {
+    const int s = n % NST;
+    const int j0 = key0(n);
+    const uint32_t st = stage_addr(s);
+    mbar_expect_tx(BAR(B_KVF + s), SZ_STAGE);
+    tma_load_4d(st, &p.tm_k64, BAR(B_KVF + s), 0, j0, h, b);
+    tma_load_4d(st + SZ_K, &p.tm_v64, BAR(B_KVF + s), 0, j0, h, b);
+    tma_load_4d(st + SZ_K + SZ_V, &p.tm_b64, BAR(B_KVF + s), 0, j0, h, b);
+    tma_load_3d(st + SZ_K + SZ_V + SZ_B, &p.tm_pos, BAR(B_KVF + s), j0, 0, bh);
+    if (n == 0) {
+      // o'' for delta'', behind the first key tile (the score GEMMs need that first)
+      if (p.o32) {
+        mbar_expect_tx(BAR(B_O), 2 * SZ_OB);
+        tma_load_3d(sbase + OFF_O, &p.tm_o, BAR(B_O), 0, m0, bh);
+        tma_load_3d(sbase + OFF_O + SZ_OB, &p.tm_o, BAR(B_O), 32, m0, bh);
+      } else {
+        mbar_expect_tx(BAR(B_O), SZ_OB);
+        tma_load_4d(sbase + OFF_O, &p.tm_o, BAR(B_O), 0, m0, h, b);
+      }
+    }
+  };
+  if (warp == WARP_TMA && lane == 0) {
     for (int s = 0; s < NST; ++s) { mbar_init(BAR(B_KVF + s), 1); mbar_init(BAR(B_KVE + s), 1); }
     mbar_init(BAR(B_Q), 1);
     mbar_init(BAR(B_SUF), 1);
@@ -142,42 +169,25 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
     mbar_init(BAR(B_O), 1);
     mbar_init(BAR(B_KR), 1);
     fence_barrier_init();
+    fence_proxy_async_smem();
+    mbar_expect_tx(BAR(B_Q), SZ_Q + SZ_DO + SZ_C);
+    tma_load_4d(sbase + OFF_Q, &p.tm_q128, BAR(B_Q), 0, m0, h, b);
+    tma_load_4d(sbase + OFF_DO, &p.tm_do128, BAR(B_Q), 0, m0, h, b);
+    tma_load_4d(sbase + OFF_C, &p.tm_c128, BAR(B_Q), 0, m0, h, b);
+    for (int n = 0; n < npre; ++n) issue_stage(n);
   }
   if (warp == WARP_MMA) { tmem_alloc(smem_u32(tmem_slot), TMEM_COLS); tmem_relinquish(); }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  auto key0 = [&](int n) { return n < ndiag ? m0 + n * 64 : (n - ndiag) * 64; };
-  auto stage_addr = [&](int s) { return sbase + OFF_ST + (uint32_t)s * SZ_STAGE; };
 
   if (warp == WARP_TMA) {
     if (lane == 0) {
-      mbar_expect_tx(BAR(B_Q), SZ_Q + SZ_DO + SZ_C);
-      tma_load_4d(sbase + OFF_Q, &p.tm_q128, BAR(B_Q), 0, m0, h, b);
-      tma_load_4d(sbase + OFF_DO, &p.tm_do128, BAR(B_Q), 0, m0, h, b);
-      tma_load_4d(sbase + OFF_C, &p.tm_c128, BAR(B_Q), 0, m0, h, b);
-      for (int n = 0; n < ntiles; ++n) {
+      for (int n = npre; n < ntiles; ++n) {
         const int s = n % NST;
-        if (n >= NST && !mbar_wait(BAR(B_KVE + s), ((n / NST) - 1) & 1, p.status)) break;
-        const int j0 = key0(n);
-        const uint32_t st = stage_addr(s);
-        mbar_expect_tx(BAR(B_KVF + s), SZ_STAGE);
-        tma_load_4d(st, &p.tm_k64, BAR(B_KVF + s), 0, j0, h, b);
-        tma_load_4d(st + SZ_K, &p.tm_v64, BAR(B_KVF + s), 0, j0, h, b);
-        tma_load_4d(st + SZ_K + SZ_V, &p.tm_b64, BAR(B_KVF + s), 0, j0, h, b);
-        tma_load_3d(st + SZ_K + SZ_V + SZ_B, &p.tm_pos, BAR(B_KVF + s), j0, 0, bh);
-        if (n == 0) {
-          // o'' for delta'', behind the first key tile (the score GEMMs need that first)
-          if (p.o32) {
-            mbar_expect_tx(BAR(B_O), 2 * SZ_OB);
-            tma_load_3d(sbase + OFF_O, &p.tm_o, BAR(B_O), 0, m0, bh);
-            tma_load_3d(sbase + OFF_O + SZ_OB, &p.tm_o, BAR(B_O), 32, m0, bh);
-          } else {
-            mbar_expect_tx(BAR(B_O), SZ_OB);
-            tma_load_4d(sbase + OFF_O, &p.tm_o, BAR(B_O), 0, m0, h, b);
-          }
-        }
+        if (!mbar_wait(BAR(B_KVE + s), ((n / NST) - 1) & 1, p.status)) break;
+        issue_stage(n);
       }
       // the tile's own key and B~ rows, needed only by the epilogue
       mbar_expect_tx(BAR(B_KR), 128 * 128 + 128 * 64);
@@ -554,7 +564,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
   const uint32_t bar0 = sbase + OFF_BAR;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + 128);
 #define BAR(i) (bar0 + 8u * (uint32_t)(i))
-  if (tid == 0) {
+  auto stage_addr = [&](int s) { return sbase + OFF_ST + (uint32_t)s * SZ_STAGE; };
+  auto issue_stage = [&](int n) {
+    const int s = n % NST;
+    const int m0 = n0 + 64 * n;
+    const uint32_t st = stage_addr(s);
+    mbar_expect_tx(BAR(B_KVF + s), SZ_STAGE);
+    tma_load_4d(st, &p.tm_q64, BAR(B_KVF + s), 0, m0, h, b);
+    tma_load_4d(st + SZ_Q, &p.tm_do64, BAR(B_KVF + s), 0, m0, h, b);
+    tma_load_4d(st + SZ_Q + SZ_DO, &p.tm_c64, BAR(B_KVF + s), 0, m0, h, b);
+    tma_load_3d(st + SZ_Q + SZ_DO + SZ_C, &p.tm_pos, BAR(B_KVF + s), m0, 0, bh);
+    tma_load_3d(st + SZ_Q + SZ_DO + SZ_C + SZ_POS, &p.tm_rstat, BAR(B_KVF + s), m0, 0, bh);
+  };
+  // As in the dq kernel, the TMA thread initialises the barriers and issues the resident tiles and
+  // the first NST query tiles before the block-wide sync.
+  const int npre = ntiles < NST ? ntiles : NST;
+  if (warp == WARP_TMA && lane == 0) {
     for (int s = 0; s < NST; ++s) { mbar_init(BAR(B_KVF + s), 1); mbar_init(BAR(B_KVE + s), 1); }
     mbar_init(BAR(B_K), 1);
     mbar_init(BAR(B_SUF), 1);
@@ -562,31 +587,25 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
     for (int i = 0; i < 2; ++i) { mbar_init(BAR(B_OPF + i), NCT); mbar_init(BAR(B_OPE + i), 1); }
     mbar_init(BAR(B_ACC), 1);
     fence_barrier_init();
+    fence_proxy_async_smem();
+    mbar_expect_tx(BAR(B_K), SZ_K + SZ_V + SZ_B);
+    tma_load_4d(sbase + OFF_K, &p.tm_k128, BAR(B_K), 0, n0, h, b);
+    tma_load_4d(sbase + OFF_V, &p.tm_v128, BAR(B_K), 0, n0, h, b);
+    tma_load_4d(sbase + OFF_B, &p.tm_b128, BAR(B_K), 0, n0, h, b);
+    for (int n = 0; n < npre; ++n) issue_stage(n);
   }
   if (warp == WARP_MMA) { tmem_alloc(smem_u32(tmem_slot), TMEM_COLS); tmem_relinquish(); }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  auto stage_addr = [&](int s) { return sbase + OFF_ST + (uint32_t)s * SZ_STAGE; };
 
   if (warp == WARP_TMA) {
     if (lane == 0) {
-      mbar_expect_tx(BAR(B_K), SZ_K + SZ_V + SZ_B);
-      tma_load_4d(sbase + OFF_K, &p.tm_k128, BAR(B_K), 0, n0, h, b);
-      tma_load_4d(sbase + OFF_V, &p.tm_v128, BAR(B_K), 0, n0, h, b);
-      tma_load_4d(sbase + OFF_B, &p.tm_b128, BAR(B_K), 0, n0, h, b);
-      for (int n = 0; n < ntiles; ++n) {
+      for (int n = npre; n < ntiles; ++n) {
         const int s = n % NST;
-        if (n >= NST && !mbar_wait(BAR(B_KVE + s), ((n / NST) - 1) & 1, p.status)) break;
-        const int m0 = n0 + 64 * n;
-        const uint32_t st = stage_addr(s);
-        mbar_expect_tx(BAR(B_KVF + s), SZ_STAGE);
-        tma_load_4d(st, &p.tm_q64, BAR(B_KVF + s), 0, m0, h, b);
-        tma_load_4d(st + SZ_Q, &p.tm_do64, BAR(B_KVF + s), 0, m0, h, b);
-        tma_load_4d(st + SZ_Q + SZ_DO, &p.tm_c64, BAR(B_KVF + s), 0, m0, h, b);
-        tma_load_3d(st + SZ_Q + SZ_DO + SZ_C, &p.tm_pos, BAR(B_KVF + s), m0, 0, bh);
-        tma_load_3d(st + SZ_Q + SZ_DO + SZ_C + SZ_POS, &p.tm_rstat, BAR(B_KVF + s), m0, 0, bh);
+        if (!mbar_wait(BAR(B_KVE + s), ((n / NST) - 1) & 1, p.status)) break;
+        issue_stage(n);
       }
     }
   } else if (warp == WARP_MMA) {
