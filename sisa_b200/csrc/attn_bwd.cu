@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
     if (lane == 0) {
       for (int n = npre; n < ntiles; ++n) {
         const int s = n % NST;
-        if (!mbar_wait(BAR(B_KVE + s), ((n / NST) - 1) & 1, p.status)) break;
+        if (!mbar_wait<true>(BAR(B_KVE + s), ((n / NST) - 1) & 1, p.status)) break;
         issue_stage(n);
       }
       // the tile's own key and B~ rows, needed only by the epilogue
@@ -604,7 +604,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
     if (lane == 0) {
       for (int n = npre; n < ntiles; ++n) {
         const int s = n % NST;
-        if (!mbar_wait(BAR(B_KVE + s), ((n / NST) - 1) & 1, p.status)) break;
+        if (!mbar_wait<true>(BAR(B_KVE + s), ((n / NST) - 1) & 1, p.status)) break;
         issue_stage(n);
       }
     }

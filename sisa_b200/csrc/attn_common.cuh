@@ -64,8 +64,9 @@ __device__ __forceinline__ void tile_order(int ntile, int BH, int& bh, int& rank
 }
 
 // Warp-uniform bounded wait used by the compute warps.
+template <bool kSleep = false>
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int32_t* status) {
-  const bool ok = mbar_wait(bar, parity, status);
+  const bool ok = mbar_wait<kSleep>(bar, parity, status);
   return __all_sync(0xffffffffu, ok);
 }
 

@@ -111,7 +111,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
       tma_load_4d(sC, &p.tm_c, BAR(B_Q), 0, m0, h, b);
       for (int n = 0; n < ntiles; ++n) {
         const int s = n % NSTAGE;
-        if (n >= NSTAGE && !mbar_wait(BAR(B_KVE + s), ((n / NSTAGE) - 1) & 1, p.status)) break;
+        if (n >= NSTAGE && !mbar_wait<true>(BAR(B_KVE + s), ((n / NSTAGE) - 1) & 1, p.status)) break;
         const int j0 = key0(n);
         const uint32_t st = stage_addr(s);
         mbar_expect_tx(BAR(B_KVF + s), SZ_K + SZ_V + SZ_B + SZ_POS);
@@ -127,10 +127,10 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
       constexpr uint32_t id_qk = make_idesc(128, 64, kHalf ? 0 : 1, 0, 0);
       constexpr uint32_t id_pv = make_idesc(128, NO, kHalf ? 0 : 1, 0, 1);
       const uint32_t tS = tbase + COL_S, tU = tbase + COL_U, tO = tbase + COL_O;
-      bool ok = mbar_wait(BAR(B_Q), 0, p.status);
+      bool ok = mbar_wait<true>(BAR(B_Q), 0, p.status);
       auto issue_pv = [&](int m) -> bool {
         const int s = m % NSTAGE;
-        if (!mbar_wait(BAR(B_PF), m & 1, p.status)) return false;
+        if (!mbar_wait<true>(BAR(B_PF), m & 1, p.status)) return false;
         tc_fence_after();
         const uint32_t tP = tbase + COL_P;
         const uint32_t sV = stage_addr(s) + OFFS_V;     // N = 80: V, then the ONE tile 8192 bytes (LBO) on
@@ -143,8 +143,8 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
       };
       for (int n = 0; ok && n < ntiles; ++n) {
         const int s = n % NSTAGE;
-        if (!mbar_wait(BAR(B_KVF + s), (n / NSTAGE) & 1, p.status)) { ok = false; break; }
-        if (n > 0 && !mbar_wait(BAR(B_SUE), (n - 1) & 1, p.status)) { ok = false; break; }
+        if (!mbar_wait<true>(BAR(B_KVF + s), (n / NSTAGE) & 1, p.status)) { ok = false; break; }
+        if (n > 0 && !mbar_wait<true>(BAR(B_SUE), (n - 1) & 1, p.status)) { ok = false; break; }
         tc_fence_after();
         const uint32_t st = stage_addr(s);
 #pragma unroll
@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     for (int n = 0; n < ntiles; ++n) {
       const int s = n % NSTAGE;
       const int j0 = key0(n);
-      if (!warp_wait(BAR(B_SUF), n & 1, p.status)) { ok = false; break; }
+      if (!warp_wait<true>(BAR(B_SUF), n & 1, p.status)) { ok = false; break; }
       tc_fence_after();
       // key position planes of this tile: [4][64] floats {g, F, rowf, colf}
       const float* kpos = reinterpret_cast<const float*>(gbase + OFF_ST + s * SZ_STAGE + OFFS_POS);
@@ -254,7 +254,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
       if (__any_sync(0xffffffffu, need) && n > 0) {
         // lazy correction of O (including its DT(p) sum column): wait until the previous tile's UMMAs
         // have landed
-        if (!warp_wait(BAR(B_PE), (n - 1) & 1, p.status)) { ok = false; break; }
+        if (!warp_wait<true>(BAR(B_PE), (n - 1) & 1, p.status)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int q = 0; q < 5; ++q) {
@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         w[c] = pack2<kHalf>(pe.x, pe.y);
       }
       // one P buffer: the previous tile's P V UMMAs must have read it
-      if (n >= 1 && !warp_wait(BAR(B_PE), (n - 1) & 1, p.status)) { ok = false; break; }
+      if (n >= 1 && !warp_wait<true>(BAR(B_PE), (n - 1) & 1, p.status)) { ok = false; break; }
       tmem_st32u(tmem_addr(tbase, warp, COL_P), w);
       tmem_wait_st();
       tc_fence_before();
@@ -289,7 +289,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     }
     const float2 lsum = add2(add2(lacc[0], lacc[1]), add2(lacc[2], lacc[3]));
     const float l = lsum.x + lsum.y;
-    if (ok && !warp_wait(BAR(B_O), 0, p.status)) ok = false;
+    if (ok && !warp_wait<true>(BAR(B_O), 0, p.status)) ok = false;
     if (ok) {
       tc_fence_after();
       float ov[64], lb;

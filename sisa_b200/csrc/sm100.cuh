@@ -45,26 +45,42 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
                ::"r"(bar), "r"(bytes) : "memory");
 }
 
+// One test of a phase. Without a hint it returns at once; with kSleep the thread is suspended until
+// the phase completes or the hint (ns) expires, so a waiting warp does not spin through issue slots
+// that the warps doing arithmetic on the same sub-partition need (a suspended warp also resumes a
+// little later than a spinning one, which matters on latency-critical hand-offs).
+constexpr uint32_t kSuspendHintNs = 10000000u;   // 10 ms
+template <bool kSleep = false>
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.b32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  if constexpr (kSleep) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(bar), "r"(parity), "r"(kSuspendHintNs) : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  }
   return ok != 0;
 }
 
 // Wait until the phase with the given parity has completed. Returns false (and records
-// SISA_ST_TIMEOUT) if that does not happen within SISA_WAIT_NS.
+// SISA_ST_TIMEOUT) if that does not happen within SISA_WAIT_NS (plus, when sleeping, at most 64
+// suspend hints before the timer starts).
+template <bool kSleep = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t* status) {
 #pragma unroll 1
   for (int i = 0; i < 64; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait<kSleep>(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
 #pragma unroll 1
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait<kSleep>(bar, parity)) return true;
     if (globaltimer() - t0 > SISA_WAIT_NS) {
       if (status) atomicOr(status, SISA_ST_TIMEOUT);
       return false;
