@@ -175,7 +175,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     const uint32_t tU = tmem_addr(tbase, warp, COL_U);
     const uint32_t tO = tmem_addr(tbase, warp, COL_O);
     // (F_i - F_j) log2e = fma(F_j, -log2e, F_i log2e): one packed FMA per column pair
-    const float2 c1v = bcast2(c1), nl2e = bcast2(-kLOG2E), fil2 = bcast2(fi * kLOG2E), lam2v = bcast2(lam2);
+    const float2 c1v = bcast2(c1), nl2e = bcast2(-kLOG2E), lam2v = bcast2(lam2);
     float m_ref = -INFINITY;
     float2 lacc[4] = {bcast2(0.f), bcast2(0.f), bcast2(0.f), bcast2(0.f)};   // l = sum of fp32 p
     // (sum of DT(p) is O's column 64, accumulated by the P V UMMA)
@@ -200,6 +200,10 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
       mbar_arrive(BAR(B_SUE));            // S and U are in registers: the next tile's GEMMs may start
       float2* x2 = reinterpret_cast<float2*>(sv);     // x overwrites S in place, two columns per float2
       const float2* u2 = reinterpret_cast<const float2*>(uv);
+      // The running reference max is folded into the row constant: the loops below produce
+      // d = x - m_ref directly (m_ref = 0 before the first finite maximum).
+      const float mbase = (m_ref == -INFINITY) ? 0.f : m_ref;
+      const float2 film2 = bcast2(fi * kLOG2E - mbase);
       if (n < ndiag) {
         // diagonal tile: pairwise decay exp(min(g_i - g_j, 0)), causal mask and sequence end
 #pragma unroll
@@ -213,7 +217,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
             const float da = exp2f(fminf((gi - gja) * kLOG2E, 0.f));
             const float db = exp2f(fminf((gi - gjb) * kLOG2E, 0.f));
             const float2 u = mul2(make_float2(da, db), u2[c]);
-            const float2 y = fma2(u, lam2v, fma2(fj, nl2e, fil2));
+            const float2 y = fma2(u, lam2v, fma2(fj, nl2e, film2));
             float2 x = fma2(x2[c], c1v, y);
             const int j = j0 + 2 * c;
             if (!(j <= row && j < L)) x.x = -INFINITY;
@@ -233,7 +237,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
             const float2 fj = e ? make_float2(f4.z, f4.w) : make_float2(f4.x, f4.y);
             const float2 cf = e ? make_float2(c4.z, c4.w) : make_float2(c4.x, c4.y);
             const float2 w = mul2(u2[c], cf);                        // U colf
-            const float2 y = fma2(w, rsm, fma2(fj, nl2e, fil2));
+            const float2 y = fma2(w, rsm, fma2(fj, nl2e, film2));
             x2[c] = fma2(x2[c], c1v, y);
           }
         }
@@ -247,11 +251,15 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         mx[i] = fmax3(mx[i], sv[i + 40], sv[i + 48]);
         mx[i] = fmaxf(mx[i], sv[i + 56]);
       }
+      // mt: this tile's maximum of x - m_ref. The reference moves only when it is exceeded by more
+      // than 2^8 (or on the first finite maximum); then O, l and sum DT(p) are scaled by 2^-(shift).
       const float mt = fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
-      const bool need = mt > m_ref + 8.f;
-      const float m_new = need ? mt : m_ref;
+      const bool need = (m_ref == -INFINITY) ? (mt > -INFINITY) : (mt > 8.f);
+      const float shift = need ? mt : 0.f;
+      const float m_new = need ? mbase + mt : m_ref;
       const float corr = need ? ex2_approx(m_ref - m_new) : 1.f;
-      if (__any_sync(0xffffffffu, need) && n > 0) {
+      const bool any_need = __any_sync(0xffffffffu, need);
+      if (any_need && n > 0) {
         // lazy correction of O (including its DT(p) sum column): wait until the previous tile's UMMAs
         // have landed
         if (!warp_wait<true>(BAR(B_PE), (n - 1) & 1, p.status)) { ok = false; break; }
@@ -271,12 +279,16 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
 #pragma unroll
       for (int i = 0; i < 4; ++i) lacc[i] = mul2(lacc[i], corr2);
       m_ref = m_new;
-      const float2 mu2 = bcast2((m_ref == -INFINITY) ? 0.f : -m_ref);
+      if (any_need) {
+        // rows whose reference moved shift their exponents (warp-uniform branch, rare after the first tile)
+        const float2 ns2 = bcast2(-shift);
+#pragma unroll
+        for (int c = 0; c < 32; ++c) x2[c] = add2(x2[c], ns2);
+      }
       uint32_t w[32];
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
-        const float2 d = add2(x2[c], mu2);
-        const float2 pe = make_float2(ex2_approx(d.x), ex2_approx(d.y));
+        const float2 pe = make_float2(ex2_approx(x2[c].x), ex2_approx(x2[c].y));
         lacc[c & 3] = add2(lacc[c & 3], pe);
         w[c] = pack2<kHalf>(pe.x, pe.y);
       }
