@@ -909,18 +909,30 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
 }
 
 // d lambda_h = sum over (b, t) of the per-row parts, in fp64 with a fixed reduction tree, rounded once
-// (attention.py:781-783).
-__global__ void __launch_bounds__(256) dlam_kernel(const float* rl, float* dlam, int B, int H, int L) {
+// (attention.py:781-783). One CTA of 1024 threads per head; thread i takes the elements i, i + 1024,
+// ... of the head's B x L values (eight loads in flight per round), then a tree over the threads.
+constexpr int kDlamThreads = 1024;
+__global__ void __launch_bounds__(kDlamThreads) dlam_kernel(const float* rl, float* dlam, int B, int H, int L) {
   const int h = blockIdx.x;
-  __shared__ double part[256];
+  __shared__ double part[kDlamThreads];
+  const int64_t n = (int64_t)B * L;
+  auto at = [&](int64_t e) {
+    const int64_t bb = e / L;
+    return __ldg(rl + (bb * H + h) * L + (e - bb * L));
+  };
   double acc = 0.0;
-  for (int bb = 0; bb < B; ++bb) {
-    const float* src = rl + ((int64_t)bb * H + h) * L;
-    for (int t = threadIdx.x; t < L; t += 256) acc += (double)src[t];
+  int64_t e = threadIdx.x;
+  for (; e + 7 * kDlamThreads < n; e += 8 * kDlamThreads) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = at(e + (int64_t)i * kDlamThreads);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc += (double)v[i];
   }
+  for (; e < n; e += kDlamThreads) acc += (double)at(e);
   part[threadIdx.x] = acc;
   __syncthreads();
-  for (int w = 128; w > 0; w >>= 1) {
+  for (int w = kDlamThreads / 2; w > 0; w >>= 1) {
     if ((int)threadIdx.x < w) part[threadIdx.x] += part[threadIdx.x + w];
     __syncthreads();
   }
@@ -944,7 +956,7 @@ cudaError_t launch_attn_bwd(const BwdParams& p, int dtype, cudaStream_t st) {
     attn_bwd_dq_kernel<false><<<gq, NTHREADS, dqk::SMEM_BYTES, st>>>(p);
     attn_bwd_dkv_kernel<false><<<gk, NTHREADS, dkv::SMEM_BYTES, st>>>(p);
   }
-  dlam_kernel<<<p.H, 256, 0, st>>>(p.rl, p.dlam, p.B, p.H, p.L);
+  dlam_kernel<<<p.H, kDlamThreads, 0, st>>>(p.rl, p.dlam, p.B, p.H, p.L);
   return cudaGetLastError();
 }
 
