@@ -42,13 +42,15 @@
 namespace sisa {
 namespace bwd {
 
-constexpr int NST = 3;
+constexpr int NST = 4;           // key (dq) / query (dkv) tile stages
 constexpr int NWG = 4;           // compute warpgroups; each owns 64 / NWG columns of every tile
 constexpr int NCOL = 64 / NWG;   // 16
 constexpr int NCW = 4 * NWG;     // compute warps
 constexpr int NTHREADS = 32 * NCW + 96;    // + one TMA warp + two UMMA issuer warps
 constexpr int WARP_TMA = NCW, WARP_MMA = NCW + 1, WARP_GRAD = NCW + 2;   // sub-partitions 0, 1, 2
 constexpr int NCT = 32 * NCW;    // compute threads
+// barrier area: up to 32 mbarriers, then the TMEM address slot
+constexpr uint32_t kTmemSlot = 256, kBarBytes = 512;
 
 // ----------------------------------------------------------------------------- dq kernel layout
 namespace dqk {
@@ -63,18 +65,18 @@ constexpr uint32_t SZ_OB = 128 * 128, OFF_O = OFF_RED + 128 * NWG * 8 * 4;
 // the tile's own key and B~ rows (k_t, b_t) for the diagonal terms of the epilogue
 constexpr uint32_t OFF_KR = OFF_O + 2 * SZ_OB, OFF_BR = OFF_KR + 128 * 128;
 constexpr uint32_t OFF_BAR = OFF_BR + 128 * 64;
-constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr uint32_t SMEM_BYTES = OFF_BAR + kBarBytes + 1024;
 // The epilogue stages dq (low precision, 128-byte rows) in the Q region and dc (fp32, 128-byte rows)
 // in the dO region for bulk-tensor stores; both are free once the last gradient UMMA has completed.
 // TMEM: S, U, dP per tile; dQ, dC_off, dC_diag accumulators; the bf16 operands dS and dS*cf of the
 // gradient UMMAs (two buffers of 2 x 32 columns, written by the compute warps, read as A from TMEM)
 constexpr int COL_S = 0, COL_U = 64, COL_DP = 128, COL_DQ = 192, COL_DCO = 256, COL_DCD = 288, COL_OPS = 320;
-constexpr int B_KVF = 0, B_KVE = 3, B_Q = 6, B_SUF = 7, B_SUE = 8, B_OPF = 9, B_OPE = 11, B_ACC = 13, B_O = 14,
-              B_KR = 15;
+constexpr int B_KVF = 0, B_KVE = NST, B_Q = 2 * NST, B_SUF = B_Q + 1, B_SUE = B_Q + 2, B_OPF = B_Q + 3,
+              B_OPE = B_Q + 5, B_ACC = B_Q + 7, B_O = B_Q + 8, B_KR = B_Q + 9;
 static_assert(OFF_ST % 1024 == 0 && OFF_O % 1024 == 0 && OFF_KR % 1024 == 0 && OFF_BR % 1024 == 0 &&
                   SZ_STAGE % 1024 == 0, "swizzled tiles need 1024-byte alignment");
 static_assert(SMEM_BYTES <= 232448, "shared memory per block");
-static_assert(B_KR * 8 < 128, "barriers end below the TMEM slot");
+static_assert(B_KR * 8 < kTmemSlot, "barriers end below the TMEM slot");
 }  // namespace dqk
 
 // ----------------------------------------------------------------------------- dkv kernel layout
@@ -87,7 +89,7 @@ constexpr uint32_t OFF_RED = OFF_ST + NST * SZ_STAGE;                  // [2 val
 constexpr uint32_t SZ_DSB = 128 * 128;                                 // (dS^' rq)^T operand: 128 keys x 64 queries
 constexpr uint32_t OFF_DSB = OFF_RED + 128 * NWG * 2 * 4;              // two buffers, K-major, 128-byte swizzle
 constexpr uint32_t OFF_BAR = OFF_DSB + 2 * SZ_DSB;
-constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
+constexpr uint32_t SMEM_BYTES = OFF_BAR + kBarBytes + 1024;
 // TMEM: S^T, U^T, dP^T per tile; dV, dK, dB_diag, dB_off accumulators; the bf16 operands P^T and dS^T
 // (two buffers of 2 x 32 columns, A operands read from TMEM). The third operand, (dS^' rq)^T, goes
 // through shared memory (two buffers), so the compute warps store tile n while the gradient UMMAs of
@@ -95,7 +97,9 @@ constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
 constexpr int COL_S = 0, COL_U = 64, COL_DP = 128, COL_DV = 192, COL_DK = 256, COL_DBD = 320, COL_DBO = 352,
               COL_OPS = 384;
 static_assert(OFF_DSB % 1024 == 0, "swizzled operand tiles need 1024-byte alignment");
-constexpr int B_KVF = 0, B_KVE = 3, B_K = 6, B_SUF = 7, B_SUE = 8, B_OPF = 9, B_OPE = 11, B_ACC = 13;
+constexpr int B_KVF = 0, B_KVE = NST, B_K = 2 * NST, B_SUF = B_K + 1, B_SUE = B_K + 2, B_OPF = B_K + 3,
+              B_OPE = B_K + 5, B_ACC = B_K + 7;
+static_assert(B_ACC * 8 < kTmemSlot, "barriers end below the TMEM slot");
 static_assert(OFF_ST % 1024 == 0 && SZ_STAGE % 1024 == 0, "alignment");
 }  // namespace dkv
 
@@ -135,7 +139,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
   const uint32_t sbase = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (sbase - raw);
   const uint32_t bar0 = sbase + OFF_BAR;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + 128);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + kTmemSlot);
 #define BAR(i) (bar0 + 8u * (uint32_t)(i))
   auto key0 = [&](int n) { return n < ndiag ? m0 + n * 64 : (n - ndiag) * 64; };
   auto stage_addr = [&](int s) { return sbase + OFF_ST + (uint32_t)s * SZ_STAGE; };
@@ -567,7 +571,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
   const uint32_t sbase = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (sbase - raw);
   const uint32_t bar0 = sbase + OFF_BAR;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + 128);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + OFF_BAR + kTmemSlot);
 #define BAR(i) (bar0 + 8u * (uint32_t)(i))
   auto stage_addr = [&](int s) { return sbase + OFF_ST + (uint32_t)s * SZ_STAGE; };
   auto issue_stage = [&](int n) {
