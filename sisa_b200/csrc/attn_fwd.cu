@@ -29,7 +29,7 @@
 namespace sisa {
 namespace fwd {
 
-constexpr int BM = 128, BN = 64, NSTAGE = 2;
+constexpr int BM = 128, BN = 64, NSTAGE = 3;
 constexpr uint32_t SZ_Q = BM * 128, SZ_C = BM * 64;
 constexpr uint32_t SZ_K = BN * 128, SZ_V = BN * 128, SZ_ONE = BN * 128, SZ_B = BN * 64, SZ_POS = BN * 16;
 // Stage: K | V | ONE | B~ | pos. ONE is a constant tile (1 in the first column of every key row) that
@@ -46,7 +46,11 @@ constexpr int NO = 80;                                           // O columns: 6
 constexpr int COL_S = 0, COL_U = 64, COL_O = 128, COL_P = COL_O + NO;   // P: one 32-column bf16x2 buffer
 static_assert(COL_P + 32 <= (int)TMEM_COLS, "TMEM budget");
 // barrier indices
-constexpr int B_Q = 0, B_KVF = 1, B_KVE = 3, B_SUF = 5, B_SUE = 6, B_PF = 7, B_PE = 8, B_O = 9;
+constexpr int B_Q = 0, B_KVF = 1, B_KVE = 1 + NSTAGE, B_SUF = 1 + 2 * NSTAGE, B_SUE = B_SUF + 1, B_PF = B_SUF + 2,
+              B_PE = B_SUF + 3, B_O = B_SUF + 4;
+static_assert(B_O * 8 < 128, "barriers end below the TMEM slot");
+// two CTAs per SM: 2 x (SMEM_BYTES + 1 KB reserved per block) within the SM's 228 KB
+static_assert(2 * (OFF_ST + NSTAGE * SZ_STAGE + 256 + 1024 + 1024) <= 228 * 1024, "two CTAs per SM");
 
 static_assert(OFF_ST % 1024 == 0 && SZ_STAGE % 1024 == 0, "swizzle alignment");
 
