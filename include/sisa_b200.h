@@ -36,6 +36,7 @@ extern "C" {
 /* ---- element types of low-precision operands ---- */
 #define SISA_BF16 0
 #define SISA_F16  1
+#define SISA_F32  2   /* only where an entry point says so */
 
 /* A (B, H, L, X) view: element strides of the first three axes; the last axis is contiguous. */
 typedef struct sisa_view4 {
@@ -144,6 +145,27 @@ int sisa_lce_logits(const void* x, int64_t R, int64_t D, int64_t x_ld, const voi
 int sisa_lce_grad(void* logits, int64_t logits_ld, int64_t R, int64_t V, int64_t Vp, int dtype,
                   const int64_t* labels, int64_t ignore_index, const float* inv_n, float grad_scale,
                   int compute_grad, const void* workspace, float* loss_rows, int32_t* status, void* stream);
+
+/* Fused RMSNorm and SwiGLU activation of the model's blocks (src/sisa/modeling.py:26-49). Element
+ * types SISA_BF16, SISA_F16 or SISA_F32; row strides (x_ld ...) in elements, unit inner stride.
+ * sisa_rmsnorm_fwd: rstd[r] = rsqrt(mean_c x[r,c]^2 + eps), y = (x * rstd) * w, fp32 arithmetic,
+ *   one rounding to y's type. w (d,) fp32.
+ * sisa_rmsnorm_bwd: dx = rstd (g - xh mean(g xh)) with xh = x rstd, g = dy w; when dw is not null also
+ *   dw = sum over rows of dy xh (fp32, fixed reduction order; needs sisa_rmsnorm_bwd_workspace bytes).
+ * sisa_swiglu_fwd: a = silu(g) u; sisa_swiglu_bwd: dg = da u silu'(g), du = da silu(g) (fp32
+ *   arithmetic, one rounding). rows * ceil(f / 8) < 2^31.
+ * These wait on nothing; status may be null. */
+int64_t sisa_rmsnorm_bwd_workspace(int64_t rows, int64_t d);
+int sisa_rmsnorm_fwd(const void* x, int64_t x_ld, int x_dtype, const float* w, int64_t rows, int64_t d, float eps,
+                     void* y, int64_t y_ld, int y_dtype, float* rstd, int32_t* status, void* stream);
+int sisa_rmsnorm_bwd(const void* dy, int64_t dy_ld, int dy_dtype, const void* x, int64_t x_ld, int x_dtype,
+                     const float* w, const float* rstd, int64_t rows, int64_t d, void* dx, int64_t dx_ld, int dx_dtype,
+                     float* dw, void* workspace, int32_t* status, void* stream);
+int sisa_swiglu_fwd(const void* g, int64_t g_ld, const void* u, int64_t u_ld, int64_t rows, int64_t f, int dtype,
+                    void* a, int64_t a_ld, int32_t* status, void* stream);
+int sisa_swiglu_bwd(const void* da, int64_t da_ld, const void* g, int64_t g_ld, const void* u, int64_t u_ld,
+                    int64_t rows, int64_t f, int dtype, void* dg, int64_t dg_ld, void* du, int64_t du_ld,
+                    int32_t* status, void* stream);
 
 /* Incremental decode: one new query row per (batch, head) against N cached keys
  * (src/sisa/modeling.py:224-238 via src/sisa/functional.py:69-103, src/sisa/generation.py:58-95):

@@ -15,6 +15,7 @@
 #include "prep.h"
 #include "decode.h"
 #include "lce.h"
+#include "norm.h"
 
 namespace {
 
@@ -480,6 +481,77 @@ int sisa_lce_grad(void* logits, int64_t logits_ld, int64_t R, int64_t V, int64_t
   p.compute_grad = compute_grad; p.status = status;
   cudaError_t e = sisa::launch_lce_grad(p, dtype, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_lce_grad launch");
+}
+
+// ------------------------------------------------------------------------------------ norm, SwiGLU
+static int check_edtype(int dt, const char* what) {
+  if (dt != SISA_BF16 && dt != SISA_F16 && dt != SISA_F32)
+    return fail(SISA_ERR_TYPE, "%s: dtype must be SISA_BF16, SISA_F16 or SISA_F32", what);
+  return SISA_OK;
+}
+
+int64_t sisa_rmsnorm_bwd_workspace(int64_t rows, int64_t d) { return sisa::rmsnorm_splits(rows) * d * 4; }
+
+int sisa_rmsnorm_fwd(const void* x, int64_t x_ld, int x_dtype, const float* w, int64_t rows, int64_t d, float eps,
+                     void* y, int64_t y_ld, int y_dtype, float* rstd, int32_t* status, void* stream) {
+  (void)status;
+  int rc;
+  if ((rc = check_edtype(x_dtype, "sisa_rmsnorm_fwd x")) || (rc = check_edtype(y_dtype, "sisa_rmsnorm_fwd y"))) return rc;
+  if (!x || !w || !y || !rstd) return fail(SISA_ERR_VALUE, "sisa_rmsnorm_fwd: null pointer");
+  if (rows < 1 || d < 1 || d > (1 << 20) || x_ld < d || y_ld < d || rows > ((int64_t)1 << 34))
+    return fail(SISA_ERR_VALUE, "sisa_rmsnorm_fwd: bad shape (rows %lld, d %lld)", (long long)rows, (long long)d);
+  sisa::RmsNormFwd p{x, x_ld, x_dtype, w, rows, d, eps, y, y_ld, y_dtype, rstd};
+  cudaError_t e = sisa::launch_rmsnorm_fwd(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_rmsnorm_fwd launch");
+}
+
+int sisa_rmsnorm_bwd(const void* dy, int64_t dy_ld, int dy_dtype, const void* x, int64_t x_ld, int x_dtype,
+                     const float* w, const float* rstd, int64_t rows, int64_t d, void* dx, int64_t dx_ld, int dx_dtype,
+                     float* dw, void* workspace, int32_t* status, void* stream) {
+  (void)status;
+  int rc;
+  if ((rc = check_edtype(dy_dtype, "sisa_rmsnorm_bwd dy")) || (rc = check_edtype(x_dtype, "sisa_rmsnorm_bwd x")) ||
+      (rc = check_edtype(dx_dtype, "sisa_rmsnorm_bwd dx")))
+    return rc;
+  if (!dy || !x || !w || !rstd || !dx || (dw && !workspace)) return fail(SISA_ERR_VALUE, "sisa_rmsnorm_bwd: null pointer");
+  if (rows < 1 || d < 1 || d > (1 << 20) || dy_ld < d || x_ld < d || dx_ld < d || rows > ((int64_t)1 << 34))
+    return fail(SISA_ERR_VALUE, "sisa_rmsnorm_bwd: bad shape (rows %lld, d %lld)", (long long)rows, (long long)d);
+  sisa::RmsNormBwd p{dy, dy_ld, dy_dtype, x, x_ld, x_dtype, w, rstd, rows, d, dx, dx_ld, dx_dtype, dw,
+                     static_cast<float*>(workspace)};
+  cudaError_t e = sisa::launch_rmsnorm_bwd(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_rmsnorm_bwd launch");
+}
+
+static int check_swiglu(int64_t rows, int64_t f, int dtype, const char* what) {
+  int rc;
+  if ((rc = check_edtype(dtype, what))) return rc;
+  if (rows < 1 || f < 1 || rows * ((f + 7) / 8) >= ((int64_t)1 << 31))
+    return fail(SISA_ERR_VALUE, "%s: bad shape (rows %lld, f %lld)", what, (long long)rows, (long long)f);
+  return SISA_OK;
+}
+
+int sisa_swiglu_fwd(const void* g, int64_t g_ld, const void* u, int64_t u_ld, int64_t rows, int64_t f, int dtype,
+                    void* a, int64_t a_ld, int32_t* status, void* stream) {
+  (void)status;
+  int rc;
+  if ((rc = check_swiglu(rows, f, dtype, "sisa_swiglu_fwd"))) return rc;
+  if (!g || !u || !a || g_ld < f || u_ld < f || a_ld < f) return fail(SISA_ERR_VALUE, "sisa_swiglu_fwd: null pointer or stride");
+  sisa::SwiGluFwd p{g, g_ld, u, u_ld, rows, f, a, a_ld, dtype};
+  cudaError_t e = sisa::launch_swiglu_fwd(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_swiglu_fwd launch");
+}
+
+int sisa_swiglu_bwd(const void* da, int64_t da_ld, const void* g, int64_t g_ld, const void* u, int64_t u_ld,
+                    int64_t rows, int64_t f, int dtype, void* dg, int64_t dg_ld, void* du, int64_t du_ld,
+                    int32_t* status, void* stream) {
+  (void)status;
+  int rc;
+  if ((rc = check_swiglu(rows, f, dtype, "sisa_swiglu_bwd"))) return rc;
+  if (!da || !g || !u || !dg || !du || da_ld < f || g_ld < f || u_ld < f || dg_ld < f || du_ld < f)
+    return fail(SISA_ERR_VALUE, "sisa_swiglu_bwd: null pointer or stride");
+  sisa::SwiGluBwd p{da, da_ld, g, g_ld, u, u_ld, rows, f, dg, dg_ld, du, du_ld, dtype};
+  cudaError_t e = sisa::launch_swiglu_bwd(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_swiglu_bwd launch");
 }
 
 }  // extern "C"

@@ -28,30 +28,53 @@ __all__ = ["RMSNorm", "SwiGLU", "SISAAttention", "SISABlock", "SISAModel", "SISA
 IGNORE_INDEX = -100
 
 
-class RMSNorm(nn.Module):
-    """RMSNorm computed in fp32; output in the input's dtype (modeling.py:26-36)."""
+def _fused_kernels(x: Tensor, config: SISAConfig | None) -> bool:
+    """The sm_100a RMSNorm/SwiGLU kernels serve a block when its attention path is not ``"torch"`` and
+    ``x`` is on a device those kernels run on; everything else takes the eager reference code."""
+    if config is None or config.attn_impl == "torch" or not x.is_cuda:
+        return False
+    from . import backends
 
-    def __init__(self, dim: int, eps: float = 1e-6):
+    return backends.cuda_status(x.device)[0]
+
+
+class RMSNorm(nn.Module):
+    """RMSNorm computed in fp32; output in the input's dtype (modeling.py:26-36). With a ``config`` whose
+    attention path is not ``"torch"``, CUDA inputs take the fused kernel (kernels/norm.py)."""
+
+    def __init__(self, dim: int, eps: float = 1e-6, config: SISAConfig | None = None):
         super().__init__()
         self.weight = nn.Parameter(torch.ones(dim))
         self.eps = eps
+        self._config = config
 
     def forward(self, x: Tensor) -> Tensor:
+        if _fused_kernels(x, self._config):
+            from .kernels.norm import rms_norm
+
+            return rms_norm(x, self.weight, self.eps)
         norm = torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + self.eps)
         return ((x.float() * norm) * self.weight.float()).to(x.dtype)
 
 
 class SwiGLU(nn.Module):
-    """``w_down(silu(w_gate x) * w_up x)`` without biases (modeling.py:39-49)."""
+    """``w_down(silu(w_gate x) * w_up x)`` without biases (modeling.py:39-49); the activation takes the
+    fused kernel under the same rule as RMSNorm."""
 
-    def __init__(self, d_model: int, d_ff: int):
+    def __init__(self, d_model: int, d_ff: int, config: SISAConfig | None = None):
         super().__init__()
         self.w_gate = nn.Linear(d_model, d_ff, bias=False)
         self.w_up = nn.Linear(d_model, d_ff, bias=False)
         self.w_down = nn.Linear(d_ff, d_model, bias=False)
+        self._config = config
 
     def forward(self, x: Tensor) -> Tensor:
-        return self.w_down(F.silu(self.w_gate(x)) * self.w_up(x))
+        g, u = self.w_gate(x), self.w_up(x)
+        if _fused_kernels(x, self._config) and g.dtype == u.dtype:
+            from .kernels.norm import swiglu
+
+            return self.w_down(swiglu(g, u))
+        return self.w_down(F.silu(g) * u)
 
 
 def _compute_dtype(x: Tensor) -> torch.dtype:
@@ -230,10 +253,10 @@ class SISABlock(nn.Module):
     def __init__(self, config: SISAConfig, layer_idx: int = 0):
         super().__init__()
         self.config = config
-        self.attn_norm = RMSNorm(config.d_model, config.norm_eps)
+        self.attn_norm = RMSNorm(config.d_model, config.norm_eps, config)
         self.attn = SISAAttention(config, layer_idx)
-        self.ffn_norm = RMSNorm(config.d_model, config.norm_eps)
-        self.ffn = SwiGLU(config.d_model, config.d_ff)
+        self.ffn_norm = RMSNorm(config.d_model, config.norm_eps, config)
+        self.ffn = SwiGLU(config.d_model, config.d_ff, config)
         self._reset_ffn_and_norms()
 
     @torch.no_grad()
@@ -273,7 +296,7 @@ class SISAModel(nn.Module):
         cfg = self.config
         self.embed = nn.Embedding(cfg.vocab_size, cfg.d_model)
         self.layers = nn.ModuleList([SISABlock(cfg, i) for i in range(cfg.n_layer)])
-        self.final_norm = RMSNorm(cfg.d_model, cfg.norm_eps)
+        self.final_norm = RMSNorm(cfg.d_model, cfg.norm_eps, cfg)
         self._reset_embedding_and_norm()
 
     @torch.no_grad()
