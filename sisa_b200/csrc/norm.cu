@@ -96,17 +96,36 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_dw_kernel(const TD* __restric
   const int64_t r0 = (int64_t)blockIdx.y * rows_per_split;
   const int64_t r1 = r0 + rows_per_split < rows ? r0 + rows_per_split : rows;
   float acc = 0.f;
-  for (int64_t r = r0; r < r1; ++r) acc = fmaf(ld(dy + r * dys, c), ld(x + r * xs, c) * __ldg(rstd + r), acc);
+  int64_t r = r0;
+  for (; r + 8 <= r1; r += 8) {   // eight rows' loads in flight, added in row order
+    float a[8], b[8], q[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) { a[k] = ld(dy + (r + k) * dys, c); b[k] = ld(x + (r + k) * xs, c); q[k] = __ldg(rstd + r + k); }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc = fmaf(a[k], b[k] * q[k], acc);
+  }
+  for (; r < r1; ++r) acc = fmaf(ld(dy + r * dys, c), ld(x + r * xs, c) * __ldg(rstd + r), acc);
   part[(int64_t)blockIdx.y * d + c] = acc;
 }
 
+// dw[c] = sum of the partials: a warp per column, lane j adds splits j, j + 32, ... in order, then a
+// fixed xor tree over the lanes (deterministic).
 __global__ void __launch_bounds__(256) rmsnorm_dw_reduce_kernel(const float* __restrict__ part, int nsplit, int d,
                                                                 float* __restrict__ dw) {
-  const int c = blockIdx.x * 256 + threadIdx.x;
+  const int c = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (c >= d) return;
   float acc = 0.f;
-  for (int s = 0; s < nsplit; ++s) acc += part[(int64_t)s * d + c];
-  dw[c] = acc;
+  int s = lane;
+  for (; s + 7 * 32 < nsplit; s += 8 * 32) {
+    float v[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = part[(int64_t)(s + 32 * k) * d + c];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc += v[k];
+  }
+  for (; s < nsplit; s += 32) acc += part[(int64_t)s * d + c];
+  acc = warp_sum(acc);
+  if (lane == 0) dw[c] = acc;
 }
 
 __device__ __forceinline__ float sigmoidf_(float v) { return 1.f / (1.f + __expf(-v)); }
@@ -205,7 +224,8 @@ cudaError_t launch_rmsnorm_fwd(const RmsNormFwd& p, cudaStream_t st) {
   });
 }
 
-int64_t rmsnorm_splits(int64_t rows) { return rows < 64 ? 1 : 64; }
+// dw partials: one per 16 rows (at most 4096), so that enough threads are in flight
+int64_t rmsnorm_splits(int64_t rows) { const int64_t s = (rows + 15) / 16; return s < 4096 ? s : 4096; }
 
 cudaError_t launch_rmsnorm_bwd(const RmsNormBwd& p, cudaStream_t st) {
   using namespace norm;
@@ -226,7 +246,7 @@ cudaError_t launch_rmsnorm_bwd(const RmsNormBwd& p, cudaStream_t st) {
         if (e != cudaSuccess || !p.dw) return e;
         rmsnorm_bwd_dw_kernel<TX, TD><<<gdw, 256, 0, st>>>(static_cast<const TD*>(p.dy), p.dys, static_cast<const TX*>(p.x),
                                                            p.xs, p.rstd, p.rows, (int)p.d, rps, p.part);
-        rmsnorm_dw_reduce_kernel<<<(unsigned)((p.d + 255) / 256), 256, 0, st>>>(p.part, (int)nsplit, (int)p.d, p.dw);
+        rmsnorm_dw_reduce_kernel<<<(unsigned)((p.d + 7) / 8), 256, 0, st>>>(p.part, (int)nsplit, (int)p.d, p.dw);
         return cudaGetLastError();
       });
     });
