@@ -146,7 +146,7 @@ int sisa_lce_grad(void* logits, int64_t logits_ld, int64_t R, int64_t V, int64_t
                   const int64_t* labels, int64_t ignore_index, const float* inv_n, float grad_scale,
                   int compute_grad, const void* workspace, float* loss_rows, int32_t* status, void* stream);
 
-/* Fused RMSNorm and SwiGLU activation of the model's blocks (src/sisa/modeling.py:26-49). Element
+/* Fused RMSNorm and SwiGLU activation of the model's blocks (src/sisa/modeling.py:25-49). Element
  * types SISA_BF16, SISA_F16 or SISA_F32; row strides (x_ld ...) in elements, unit inner stride.
  * sisa_rmsnorm_fwd: rstd[r] = rsqrt(mean_c x[r,c]^2 + eps), y = (x * rstd) * w, fp32 arithmetic,
  *   one rounding to y's type. w (d,) fp32.
@@ -161,6 +161,49 @@ int sisa_rmsnorm_fwd(const void* x, int64_t x_ld, int x_dtype, const float* w, i
 int sisa_rmsnorm_bwd(const void* dy, int64_t dy_ld, int dy_dtype, const void* x, int64_t x_ld, int x_dtype,
                      const float* w, const float* rstd, int64_t rows, int64_t d, void* dx, int64_t dx_ld, int dx_dtype,
                      float* dw, void* workspace, int32_t* status, void* stream);
+
+/* RMSNorm at a block boundary with the work eager PyTorch runs around it as separate kernels
+ * (src/sisa/modeling.py:275-276 with :25-36, :167-168 and the autocast casts before the linears):
+ *   v = x + res (res optional; rounded to x's type, as the reference's residual add; written to xsum),
+ *   rstd = rsqrt(mean(v^2) + eps), h = (v rstd) w rounded to x's type (the reference's RMSNorm output),
+ *   y[k] = h in y_dtype[k] for k < n_out (n_out 1 or 2: one copy per consumer, so that each consumer's
+ *   gradient arrives separately and is summed in fp32 as the reference sums them),
+ *   proj_out = h proj_w^T + proj_b in fp32 when n_proj > 0 (the attention's forget projection;
+ *   proj_w (n_proj, d) and proj_b (n_proj,) fp32, n_proj <= 32, n_proj * d * 4 <= 200 KB).
+ * Backward: G = sum_k dy[k] (null entries skipped) + dproj_out proj_w; dv = rstd (G w - xh mean(G w xh))
+ *   + dv_in (the gradient v gets from its other consumers; may be null), with xh = v rstd; dv is
+ *   stored as dx and, when dres is not null, also in dres's type (the residual's gradient); and, each
+ *   when not null, dweight = sum_r G xh, dproj_w = sum_r dproj_out^T h, dproj_b = sum_r dproj_out, from
+ *   per-row-split partial sums in a fixed order (deterministic; sisa_norm_bwd_workspace bytes). */
+typedef struct sisa_norm_fwd_args {
+  const void* x; int64_t x_ld; int x_dtype;
+  const void* res; int64_t res_ld; int res_dtype;
+  void* xsum; int64_t xsum_ld;
+  const float* weight;
+  int64_t rows, d;
+  float eps;
+  int n_out;
+  void* y[2]; int64_t y_ld[2]; int y_dtype[2];
+  float* rstd;
+  const float* proj_w; const float* proj_b; int64_t n_proj; float* proj_out;
+} sisa_norm_fwd_args;
+
+typedef struct sisa_norm_bwd_args {
+  const void* v; int64_t v_ld; int v_dtype;     /* the normalised rows: x, or xsum with a residual add */
+  const float* weight; const float* rstd;
+  int64_t rows, d;
+  const void* dy[2]; int64_t dy_ld[2]; int dy_dtype[2];
+  const void* dv_in; int64_t dv_in_ld; int dv_in_dtype;
+  const float* proj_w; int64_t n_proj; const float* dproj_out;
+  void* dx; int64_t dx_ld; int dx_dtype;
+  void* dres; int64_t dres_ld; int dres_dtype;
+  float* dweight; float* dproj_w; float* dproj_b;
+  void* workspace;
+} sisa_norm_bwd_args;
+
+int64_t sisa_norm_bwd_workspace(int64_t rows, int64_t d, int64_t n_proj);
+int sisa_norm_fwd(const sisa_norm_fwd_args* args, int32_t* status, void* stream);
+int sisa_norm_bwd(const sisa_norm_bwd_args* args, int32_t* status, void* stream);
 int sisa_swiglu_fwd(const void* g, int64_t g_ld, const void* u, int64_t u_ld, int64_t rows, int64_t f, int dtype,
                     void* a, int64_t a_ld, int32_t* status, void* stream);
 int sisa_swiglu_bwd(const void* da, int64_t da_ld, const void* g, int64_t g_ld, const void* u, int64_t u_ld,

@@ -33,6 +33,37 @@ _I64 = ctypes.c_int64
 _I = ctypes.c_int
 _VP = ctypes.POINTER(View4)
 
+
+class NormFwdArgs(ctypes.Structure):
+    """``sisa_norm_fwd_args``: one RMSNorm at a block boundary (residual add, up to two output copies, an
+    optional fp32 projection of the output)."""
+
+    _fields_ = [("x", _P), ("x_ld", _I64), ("x_dtype", _I),
+                ("res", _P), ("res_ld", _I64), ("res_dtype", _I),
+                ("xsum", _P), ("xsum_ld", _I64),
+                ("weight", _P),
+                ("rows", _I64), ("d", _I64),
+                ("eps", ctypes.c_float),
+                ("n_out", _I),
+                ("y", _P * 2), ("y_ld", _I64 * 2), ("y_dtype", _I * 2),
+                ("rstd", _P),
+                ("proj_w", _P), ("proj_b", _P), ("n_proj", _I64), ("proj_out", _P)]
+
+
+class NormBwdArgs(ctypes.Structure):
+    """``sisa_norm_bwd_args``: the backward of :class:`NormFwdArgs`."""
+
+    _fields_ = [("v", _P), ("v_ld", _I64), ("v_dtype", _I),
+                ("weight", _P), ("rstd", _P),
+                ("rows", _I64), ("d", _I64),
+                ("dy", _P * 2), ("dy_ld", _I64 * 2), ("dy_dtype", _I * 2),
+                ("dv_in", _P), ("dv_in_ld", _I64), ("dv_in_dtype", _I),
+                ("proj_w", _P), ("n_proj", _I64), ("dproj_out", _P),
+                ("dx", _P), ("dx_ld", _I64), ("dx_dtype", _I),
+                ("dres", _P), ("dres_ld", _I64), ("dres_dtype", _I),
+                ("dweight", _P), ("dproj_w", _P), ("dproj_b", _P),
+                ("workspace", _P)]
+
 # name -> (restype, argtypes); every symbol declared in include/sisa_b200.h
 SIGNATURES = {
     "sisa_version": (ctypes.c_char_p, []),
@@ -61,6 +92,9 @@ SIGNATURES = {
     "sisa_rmsnorm_bwd_workspace": (_I64, [_I64, _I64]),
     "sisa_rmsnorm_fwd": (_I, [_P, _I64, _I, _P, _I64, _I64, ctypes.c_float, _P, _I64, _I, _P, _P, _P]),
     "sisa_rmsnorm_bwd": (_I, [_P, _I64, _I, _P, _I64, _I, _P, _P, _I64, _I64, _P, _I64, _I, _P, _P, _P, _P]),
+    "sisa_norm_bwd_workspace": (_I64, [_I64, _I64, _I64]),
+    "sisa_norm_fwd": (_I, [ctypes.POINTER(NormFwdArgs), _P, _P]),
+    "sisa_norm_bwd": (_I, [ctypes.POINTER(NormBwdArgs), _P, _P]),
     "sisa_swiglu_fwd": (_I, [_P, _I64, _P, _I64, _I64, _I64, _I, _P, _I64, _P, _P]),
     "sisa_swiglu_bwd": (_I, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I, _P, _I64, _P, _I64, _P, _P]),
 }

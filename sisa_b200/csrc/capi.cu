@@ -490,36 +490,117 @@ static int check_edtype(int dt, const char* what) {
   return SISA_OK;
 }
 
-int64_t sisa_rmsnorm_bwd_workspace(int64_t rows, int64_t d) { return sisa::rmsnorm_splits(rows) * d * 4; }
+int64_t sisa_rmsnorm_bwd_workspace(int64_t rows, int64_t d) {
+  return rows < 1 || d < 1 ? 0 : sisa::norm_bwd_partials(rows, 0) * sisa::norm_part_cols(d, 0) * 4;
+}
+int64_t sisa_norm_bwd_workspace(int64_t rows, int64_t d, int64_t n_proj) {
+  return rows < 1 || d < 1 || n_proj < 0 ? 0 : sisa::norm_bwd_partials(rows, n_proj) * sisa::norm_part_cols(d, n_proj) * 4;
+}
+
+static bool norm_shape_ok(int64_t rows, int64_t d) { return rows >= 1 && d >= 1 && d <= (1 << 20) && rows <= ((int64_t)1 << 34); }
+
+// A row operand: null is allowed when `optional`; else its type and stride are checked.
+static int check_rows_arg(const void* ptr, int64_t ld, int dt, int64_t d, bool optional, const char* what) {
+  if (!ptr) return optional ? SISA_OK : fail(SISA_ERR_VALUE, "%s: null pointer", what);
+  int rc;
+  if ((rc = check_edtype(dt, what))) return rc;
+  if (ld < d) return fail(SISA_ERR_VALUE, "%s: row stride %lld < d %lld", what, (long long)ld, (long long)d);
+  return SISA_OK;
+}
+
+static int check_proj(int64_t n_proj, int64_t d, const char* what) {
+  if (n_proj < 0 || n_proj > 32 || n_proj * d * 4 > 200 * 1024)
+    return fail(SISA_ERR_VALUE, "%s: n_proj %lld with d %lld (at most 32 columns and 200 KB of weights)", what,
+                (long long)n_proj, (long long)d);
+  return SISA_OK;
+}
+
+int sisa_norm_fwd(const sisa_norm_fwd_args* a, int32_t* status, void* stream) {
+  if (!a) return fail(SISA_ERR_VALUE, "sisa_norm_fwd: null args");
+  if (!norm_shape_ok(a->rows, a->d))
+    return fail(SISA_ERR_VALUE, "sisa_norm_fwd: bad shape (rows %lld, d %lld)", (long long)a->rows, (long long)a->d);
+  if (a->n_out < 1 || a->n_out > 2) return fail(SISA_ERR_VALUE, "sisa_norm_fwd: n_out must be 1 or 2");
+  int rc;
+  if ((rc = check_rows_arg(a->x, a->x_ld, a->x_dtype, a->d, false, "sisa_norm_fwd x")) ||
+      (rc = check_rows_arg(a->res, a->res_ld, a->res_dtype, a->d, true, "sisa_norm_fwd res")) ||
+      (rc = check_rows_arg(a->xsum, a->xsum_ld, a->x_dtype, a->d, true, "sisa_norm_fwd xsum")) ||
+      (rc = check_rows_arg(a->y[0], a->y_ld[0], a->y_dtype[0], a->d, false, "sisa_norm_fwd y[0]")) ||
+      (a->n_out > 1 && (rc = check_rows_arg(a->y[1], a->y_ld[1], a->y_dtype[1], a->d, false, "sisa_norm_fwd y[1]"))) ||
+      (rc = check_proj(a->n_proj, a->d, "sisa_norm_fwd")))
+    return rc;
+  if (!a->weight || !a->rstd) return fail(SISA_ERR_VALUE, "sisa_norm_fwd: null weight or rstd");
+  if (a->xsum && !a->res) return fail(SISA_ERR_VALUE, "sisa_norm_fwd: xsum without res");
+  if (a->n_proj > 0 && (!a->proj_w || !a->proj_b || !a->proj_out))
+    return fail(SISA_ERR_VALUE, "sisa_norm_fwd: n_proj > 0 needs proj_w, proj_b and proj_out");
+  sisa::NormFwd p{};
+  p.x = a->x; p.xs = a->x_ld; p.xdt = a->x_dtype;
+  p.res = a->res; p.ress = a->res_ld; p.resdt = a->res ? a->res_dtype : 2;
+  p.xsum = a->xsum; p.xsums = a->xsum_ld;
+  p.w = a->weight; p.rows = a->rows; p.d = a->d; p.eps = a->eps;
+  p.nout = a->n_out;
+  for (int k = 0; k < 2; ++k) {
+    const bool on = k < a->n_out;
+    p.y[k] = on ? a->y[k] : nullptr; p.ys[k] = on ? a->y_ld[k] : 0; p.ydt[k] = on ? a->y_dtype[k] : 2;
+  }
+  p.rstd = a->rstd;
+  p.pw = a->proj_w; p.pb = a->proj_b; p.np = (int)a->n_proj; p.pz = a->proj_out;
+  p.status = status;
+  cudaError_t e = sisa::launch_norm_fwd(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_norm_fwd launch");
+}
+
+int sisa_norm_bwd(const sisa_norm_bwd_args* a, int32_t* status, void* stream) {
+  if (!a) return fail(SISA_ERR_VALUE, "sisa_norm_bwd: null args");
+  if (!norm_shape_ok(a->rows, a->d))
+    return fail(SISA_ERR_VALUE, "sisa_norm_bwd: bad shape (rows %lld, d %lld)", (long long)a->rows, (long long)a->d);
+  int rc;
+  if ((rc = check_rows_arg(a->v, a->v_ld, a->v_dtype, a->d, false, "sisa_norm_bwd v")) ||
+      (rc = check_rows_arg(a->dy[0], a->dy_ld[0], a->dy_dtype[0], a->d, true, "sisa_norm_bwd dy[0]")) ||
+      (rc = check_rows_arg(a->dy[1], a->dy_ld[1], a->dy_dtype[1], a->d, true, "sisa_norm_bwd dy[1]")) ||
+      (rc = check_rows_arg(a->dv_in, a->dv_in_ld, a->dv_in_dtype, a->d, true, "sisa_norm_bwd dv_in")) ||
+      (rc = check_rows_arg(a->dx, a->dx_ld, a->dx_dtype, a->d, false, "sisa_norm_bwd dx")) ||
+      (rc = check_rows_arg(a->dres, a->dres_ld, a->dres_dtype, a->d, true, "sisa_norm_bwd dres")) ||
+      (rc = check_proj(a->n_proj, a->d, "sisa_norm_bwd")))
+    return rc;
+  if (!a->weight || !a->rstd) return fail(SISA_ERR_VALUE, "sisa_norm_bwd: null weight or rstd");
+  if (a->n_proj > 0 && (!a->proj_w || !a->dproj_out))
+    return fail(SISA_ERR_VALUE, "sisa_norm_bwd: n_proj > 0 needs proj_w and dproj_out");
+  if ((a->dweight || a->dproj_w || a->dproj_b) && !a->workspace)
+    return fail(SISA_ERR_VALUE, "sisa_norm_bwd: weight gradients need the workspace");
+  if (a->n_proj == 0 && (a->dproj_w || a->dproj_b))
+    return fail(SISA_ERR_VALUE, "sisa_norm_bwd: dproj_w / dproj_b without a projection");
+  sisa::NormBwd p{};
+  p.v = a->v; p.vs = a->v_ld; p.vdt = a->v_dtype;
+  p.w = a->weight; p.rstd = a->rstd; p.rows = a->rows; p.d = a->d;
+  for (int k = 0; k < 2; ++k) { p.dy[k] = a->dy[k]; p.dys[k] = a->dy_ld[k]; p.dydt[k] = a->dy[k] ? a->dy_dtype[k] : 2; }
+  p.dvin = a->dv_in; p.dvins = a->dv_in_ld; p.dvindt = a->dv_in ? a->dv_in_dtype : 2;
+  p.pw = a->proj_w; p.np = (int)a->n_proj; p.dz = a->dproj_out;
+  p.dx = a->dx; p.dxs = a->dx_ld; p.dxdt = a->dx_dtype;
+  p.dres = a->dres; p.dress = a->dres_ld; p.dresdt = a->dres ? a->dres_dtype : 2;
+  p.dw = a->dweight; p.dpw = a->dproj_w; p.dpb = a->dproj_b;
+  p.part = static_cast<float*>(a->workspace);
+  p.status = status;
+  cudaError_t e = sisa::launch_norm_bwd(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_norm_bwd launch");
+}
 
 int sisa_rmsnorm_fwd(const void* x, int64_t x_ld, int x_dtype, const float* w, int64_t rows, int64_t d, float eps,
                      void* y, int64_t y_ld, int y_dtype, float* rstd, int32_t* status, void* stream) {
-  (void)status;
-  int rc;
-  if ((rc = check_edtype(x_dtype, "sisa_rmsnorm_fwd x")) || (rc = check_edtype(y_dtype, "sisa_rmsnorm_fwd y"))) return rc;
-  if (!x || !w || !y || !rstd) return fail(SISA_ERR_VALUE, "sisa_rmsnorm_fwd: null pointer");
-  if (rows < 1 || d < 1 || d > (1 << 20) || x_ld < d || y_ld < d || rows > ((int64_t)1 << 34))
-    return fail(SISA_ERR_VALUE, "sisa_rmsnorm_fwd: bad shape (rows %lld, d %lld)", (long long)rows, (long long)d);
-  sisa::RmsNormFwd p{x, x_ld, x_dtype, w, rows, d, eps, y, y_ld, y_dtype, rstd};
-  cudaError_t e = sisa::launch_rmsnorm_fwd(p, static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_rmsnorm_fwd launch");
+  sisa_norm_fwd_args a{};
+  a.x = x; a.x_ld = x_ld; a.x_dtype = x_dtype; a.weight = w; a.rows = rows; a.d = d; a.eps = eps;
+  a.n_out = 1; a.y[0] = y; a.y_ld[0] = y_ld; a.y_dtype[0] = y_dtype; a.rstd = rstd;
+  return sisa_norm_fwd(&a, status, stream);
 }
 
 int sisa_rmsnorm_bwd(const void* dy, int64_t dy_ld, int dy_dtype, const void* x, int64_t x_ld, int x_dtype,
                      const float* w, const float* rstd, int64_t rows, int64_t d, void* dx, int64_t dx_ld, int dx_dtype,
                      float* dw, void* workspace, int32_t* status, void* stream) {
-  (void)status;
-  int rc;
-  if ((rc = check_edtype(dy_dtype, "sisa_rmsnorm_bwd dy")) || (rc = check_edtype(x_dtype, "sisa_rmsnorm_bwd x")) ||
-      (rc = check_edtype(dx_dtype, "sisa_rmsnorm_bwd dx")))
-    return rc;
-  if (!dy || !x || !w || !rstd || !dx || (dw && !workspace)) return fail(SISA_ERR_VALUE, "sisa_rmsnorm_bwd: null pointer");
-  if (rows < 1 || d < 1 || d > (1 << 20) || dy_ld < d || x_ld < d || dx_ld < d || rows > ((int64_t)1 << 34))
-    return fail(SISA_ERR_VALUE, "sisa_rmsnorm_bwd: bad shape (rows %lld, d %lld)", (long long)rows, (long long)d);
-  sisa::RmsNormBwd p{dy, dy_ld, dy_dtype, x, x_ld, x_dtype, w, rstd, rows, d, dx, dx_ld, dx_dtype, dw,
-                     static_cast<float*>(workspace)};
-  cudaError_t e = sisa::launch_rmsnorm_bwd(p, static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_rmsnorm_bwd launch");
+  if (!dy) return fail(SISA_ERR_VALUE, "sisa_rmsnorm_bwd: null pointer");
+  sisa_norm_bwd_args a{};
+  a.v = x; a.v_ld = x_ld; a.v_dtype = x_dtype; a.weight = w; a.rstd = rstd; a.rows = rows; a.d = d;
+  a.dy[0] = dy; a.dy_ld[0] = dy_ld; a.dy_dtype[0] = dy_dtype;
+  a.dx = dx; a.dx_ld = dx_ld; a.dx_dtype = dx_dtype; a.dweight = dw; a.workspace = workspace;
+  return sisa_norm_bwd(&a, status, stream);
 }
 
 static int check_swiglu(int64_t rows, int64_t f, int dtype, const char* what) {

@@ -69,8 +69,13 @@ class SwiGLU(nn.Module):
         self._config = config
 
     def forward(self, x: Tensor) -> Tensor:
-        g, u = self.w_gate(x), self.w_up(x)
-        if _fused_kernels(x, self._config) and g.dtype == u.dtype:
+        return self.forward_split(x, x)
+
+    def forward_split(self, x_gate: Tensor, x_up: Tensor) -> Tensor:
+        """The forward with the gate and up projections fed from separate copies of the input (the fused
+        block path hands each its own copy, so that their gradients are summed in fp32)."""
+        g, u = self.w_gate(x_gate), self.w_up(x_up)
+        if _fused_kernels(x_gate, self._config) and g.dtype == u.dtype:
             from .kernels.norm import swiglu
 
             return self.w_down(swiglu(g, u))
@@ -204,13 +209,15 @@ class SISAAttention(nn.Module):
         bsz, h, seq_len, dh = y.shape
         return self.W_O(y.transpose(1, 2).reshape(bsz, seq_len, h * dh))
 
-    def _forward_fused(self, x: Tensor) -> Tensor:
+    def _forward_fused(self, x: Tensor, z: Tensor | None = None) -> Tensor:
+        """Projection, layer core and output projection (modeling.py:213-222); ``z`` is the forget
+        projection of ``x`` when the caller computed it already (the fused block norm does)."""
         from .kernels.fused import sisa_fused
 
         bsz, seq_len, d = x.shape
         weight, bias = self.fused_weights()
         proj = F.linear(x, weight, bias)
-        y = sisa_fused(proj, self._forget_logits(x), self.lam(), self.config.n_head)
+        y = sisa_fused(proj, self._forget_logits(x) if z is None else z, self.lam(), self.config.n_head)
         return self.W_O(y.reshape(bsz, seq_len, d))
 
     def _forward_cached(self, x: Tensor, cache: "SISACache", requested: str) -> Tensor:
@@ -272,8 +279,36 @@ class SISABlock(nn.Module):
         self.attn.reset_parameters()
 
     def forward(self, x: Tensor, cache: "SISACache | None" = None) -> Tensor:
+        if cache is None and self.fused_path(x):
+            xs, m = self.forward_pair(x, None)
+            return xs + m
         x = x + self.attn(self.attn_norm(x), cache=cache)
         return x + self.ffn(self.ffn_norm(x))
+
+    def fused_path(self, x: Tensor) -> bool:
+        """Whether :meth:`forward_pair` serves input ``x``: the norm kernels run and the attention takes
+        the fused CUDA layer core."""
+        return _fused_kernels(x, self.config) and _resolve_impl(self.config.attn_impl, x, self.config) == "cuda"
+
+    def forward_pair(self, x: Tensor, m: Tensor | None) -> tuple[Tensor, Tensor]:
+        """The block on the fused path, with the previous block's last residual add ``x + m`` folded into
+        this block's first norm. Returns ``(x + m + attn, ffn)``: the caller (the next block, or the
+        final norm) adds the second term. Each norm also writes its output in the dtype of the linears
+        that read it, and the attention norm computes the fp32 forget projection, so neither the casts
+        nor the separate gradient sums of eager PyTorch run (kernels/norm.py ``block_norm``)."""
+        from .kernels.norm import block_norm
+
+        cd = _compute_dtype(x)
+        attn = self.attn
+        fp = (attn.forget_proj.weight, attn.forget_proj.bias)
+        if m is None:
+            h, z = block_norm(x, self.attn_norm.weight, self.attn_norm.eps, out_dtypes=(cd,), proj=fp)
+            xs = x
+        else:
+            xs, h, z = block_norm(x, self.attn_norm.weight, self.attn_norm.eps, res=m, out_dtypes=(cd,), proj=fp)
+        a = attn._forward_fused(h, z)
+        xs, f_gate, f_up = block_norm(xs, self.ffn_norm.weight, self.ffn_norm.eps, res=a, out_dtypes=(cd, cd))
+        return xs, self.ffn.forward_split(f_gate, f_up)
 
 
 @dataclass
@@ -313,6 +348,14 @@ class SISAModel(nn.Module):
     def forward(self, input_ids: Tensor, *, cache: "SISACache | None" = None) -> Tensor:
         x = self.embed(input_ids)
         use_ckpt = self.config.gradient_checkpointing and self.training and cache is None and torch.is_grad_enabled()
+        if cache is None and len(self.layers) and self.layers[0].fused_path(x):
+            m = None
+            for layer in self.layers:
+                x, m = (checkpoint(layer.forward_pair, x, m, use_reentrant=False) if use_ckpt
+                        else layer.forward_pair(x, m))
+            from .kernels.norm import block_norm
+
+            return block_norm(x, self.final_norm.weight, self.final_norm.eps, res=m, keep_sum=False)[0]
         for layer in self.layers:
             x = checkpoint(layer, x, use_reentrant=False) if use_ckpt else layer(x, cache=cache)
         return self.final_norm(x)

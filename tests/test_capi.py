@@ -77,3 +77,33 @@ def test_host_side_argument_errors_need_no_gpu():
     # (batch, head) rows are a launch-grid dimension: at most 65535 of them
     rc = lib.sisa_prep_fwd(None, 65536, 10, 1, 0, 0, 0, None, 0, 0, None, None, None, None, None, None)
     assert rc == _lib.ERR_VALUE and "too large" in _lib.last_error()
+
+
+def test_norm_args_structs_match_the_c_header(tmp_path):
+    """The ctypes mirrors of sisa_norm_fwd_args / sisa_norm_bwd_args have the C layout (gcc, no GPU)."""
+    import ctypes
+    import shutil
+    import subprocess
+
+    from sisa_b200 import _lib
+
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not found")
+    root = Path(__file__).resolve().parents[1]
+    src = tmp_path / "layout.c"
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "sisa_b200.h"', 'int main(void) {']
+    for cname, cls in (("sisa_norm_fwd_args", _lib.NormFwdArgs), ("sisa_norm_bwd_args", _lib.NormBwdArgs)):
+        lines.append(f'printf("{cname} size %zu\\n", sizeof({cname}));')
+        for fname, _ in cls._fields_:
+            lines.append(f'printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines += ["return 0;", "}"]
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run([gcc, "-I", str(root / "include"), str(src), "-o", str(exe)], check=True)
+    got = dict(line.rsplit(" ", 1) for line in subprocess.run([str(exe)], check=True, capture_output=True,
+                                                              text=True).stdout.splitlines())
+    for cname, cls in (("sisa_norm_fwd_args", _lib.NormFwdArgs), ("sisa_norm_bwd_args", _lib.NormBwdArgs)):
+        assert int(got[f"{cname} size"]) == ctypes.sizeof(cls)
+        for fname, _ in cls._fields_:
+            assert int(got[f"{cname} {fname}"]) == getattr(cls, fname).offset, (cname, fname)

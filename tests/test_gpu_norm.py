@@ -90,3 +90,91 @@ def test_model_blocks_use_the_fused_kernels_on_the_cuda_path():
     cfg_t = sisa.SISAConfig.preset("sisa-152m", attn_impl="torch")
     assert not modeling._fused_kernels(x, cfg_t)
     assert not modeling._fused_kernels(x.cpu(), cfg)
+
+
+def _ref_block(x, res, w, pw, pb, eps, out_dtypes):
+    """Eager reference of the block boundary: residual add, RMSNorm (modeling.py:25-36), the casts of
+    the consumers and the fp32 forget projection (modeling.py:167-168)."""
+    v = x + res if res is not None else x
+    vf = v.float()
+    h = ((vf * torch.rsqrt(vf.pow(2).mean(-1, keepdim=True) + eps)) * w.float()).to(v.dtype)
+    ys = [h.to(dt) for dt in out_dtypes]
+    z = torch.nn.functional.linear(h.float(), pw.float(), pb.float()) if pw is not None else None
+    return v, ys, z
+
+
+@pytest.mark.parametrize("rows,d,xdt,with_res,n_out,n_proj", [
+    (300, 768, torch.float32, True, 1, 12),     # the attention norm of a cfg3 block
+    (300, 768, torch.float32, True, 2, 0),      # the SwiGLU norm
+    (129, 768, torch.float32, False, 1, 12),    # the first block (no residual add)
+    (77, 100, torch.float32, True, 2, 3),       # d not a multiple of 4: scalar path
+    (64, 256, torch.bfloat16, True, 1, 16),     # bf16 residual stream
+    (33, 1280, torch.float32, True, 1, 20),     # row not cached in registers, 32 projection slots
+])
+def test_block_norm_matches_eager(rows, d, xdt, with_res, n_out, n_proj):
+    from sisa_b200.kernels.norm import block_norm
+
+    dev = _dev()
+    gen = torch.Generator(device=dev).manual_seed(rows * 3 + d)
+    rnd = lambda *s, sc=1.0: torch.randn(s, generator=gen, device=dev) * sc
+    x = rnd(2, rows, d, sc=2.0).to(xdt)
+    res = rnd(2, rows, d).to(torch.bfloat16) if with_res else None
+    w = torch.rand((d,), generator=gen, device=dev) + 0.5
+    pw = rnd(n_proj, d, sc=0.05) if n_proj else None
+    pb = rnd(n_proj) if n_proj else None
+    out_dtypes = (torch.bfloat16,) * n_out
+    leaves = [t for t in (x, res, w, pw, pb) if t is not None]
+    ref_in = [t.detach().clone().requires_grad_(True) for t in leaves]
+    ker_in = [t.detach().clone().requires_grad_(True) for t in leaves]
+
+    def unpack(ins):
+        it = iter(ins)
+        xx = next(it)
+        rr = next(it) if with_res else None
+        ww = next(it)
+        pp = (next(it), next(it)) if n_proj else (None, None)
+        return xx, rr, ww, pp
+
+    xr, rr, wr, (pwr, pbr) = unpack(ref_in)
+    v_ref, ys_ref, z_ref = _ref_block(xr, rr, wr, pwr, pbr, 1e-6, out_dtypes)
+    xk, rk, wk, (pwk, pbk) = unpack(ker_in)
+    outs = block_norm(xk, wk, 1e-6, res=rk, out_dtypes=out_dtypes, proj=(pwk, pbk) if n_proj else None)
+    ref_outs = ([v_ref] if with_res else []) + ys_ref + ([z_ref] if n_proj else [])
+    assert len(outs) == len(ref_outs)
+    for o, r in zip(outs, ref_outs):
+        assert o.dtype == r.dtype and o.shape == r.shape
+        tol = 1e-5 if o.dtype == torch.float32 else 1e-2
+        assert torch.allclose(o.float(), r.float(), rtol=tol, atol=tol)
+    # independent upstream gradients for every output
+    gouts = [rnd(*o.shape).to(o.dtype) for o in outs]
+    torch.autograd.backward(ref_outs, gouts)
+    torch.autograd.backward(list(outs), gouts)
+    for a, b in zip(ker_in, ref_in):
+        assert a.grad is not None and a.grad.dtype == b.grad.dtype
+        lowp = a.grad.dtype != torch.float32 or xdt != torch.float32
+        tol = 3e-2 if lowp else 2e-4
+        err = (a.grad.float() - b.grad.float()).abs().max().item()
+        assert err <= tol * (1 + b.grad.float().abs().max().item()), (tuple(a.shape), err)
+
+
+def test_block_norm_weight_gradients_repeatable():
+    from sisa_b200.kernels.norm import block_norm
+
+    dev = _dev()
+    gen = torch.Generator(device=dev).manual_seed(11)
+    x = torch.randn((4096, 768), generator=gen, device=dev)
+    res = torch.randn((4096, 768), generator=gen, device=dev).to(torch.bfloat16)
+    w = torch.rand((768,), generator=gen, device=dev)
+    pw = torch.randn((12, 768), generator=gen, device=dev) * 0.05
+    pb = torch.randn((12,), generator=gen, device=dev)
+    gs = None
+    grads = []
+    for _ in range(2):
+        ins = [t.detach().clone().requires_grad_(True) for t in (w, pw, pb)]
+        outs = block_norm(x, ins[0], 1e-6, res=res, out_dtypes=(torch.bfloat16,), proj=(ins[1], ins[2]))
+        if gs is None:
+            gs = [torch.randn(o.shape, generator=gen, device=dev).to(o.dtype) for o in outs]
+        torch.autograd.backward(list(outs), gs)
+        grads.append([t.grad for t in ins])
+    for a, b in zip(*grads):
+        assert torch.equal(a, b)
