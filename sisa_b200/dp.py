@@ -47,18 +47,28 @@ def build_model(config: SISAConfig, device: torch.device, seed: int = 0) -> SISA
     return SISAForCausalLM(config).to(device)
 
 
-def make_optimizer(model: SISAForCausalLM, lr: float = 6e-4, weight_decay: float = 0.1) -> torch.optim.Optimizer:
-    """AdamW over the model's parameter groups (train_minimal.py:253-260)."""
+def make_optimizer(model: SISAForCausalLM, lr: float = 6e-4, weight_decay: float = 0.1,
+                   capturable: bool = False) -> torch.optim.Optimizer:
+    """AdamW over the model's parameter groups (train_minimal.py:253-260). ``capturable`` keeps the step
+    counters on the device so that the step can be captured in a CUDA graph."""
+    cuda = next(model.parameters()).is_cuda
     return torch.optim.AdamW(model.param_groups(lr, weight_decay=weight_decay), lr=lr, betas=(0.9, 0.95),
-                             weight_decay=weight_decay, fused=next(model.parameters()).is_cuda)
+                             weight_decay=weight_decay, fused=cuda, capturable=capturable and cuda)
 
 
 class Trainer:
     """One optimizer step per call: forward (bf16 autocast on CUDA), loss, backward with overlapped
-    gradient allreduce, clipping, AdamW."""
+    gradient allreduce, clipping, AdamW.
+
+    With ``cuda_graph=True`` (one process, CUDA) the whole step (forward, backward, clipping and the
+    optimizer) is captured once as a CUDA graph and replayed from a static input buffer, which removes
+    the launch gaps of its several hundred kernels and the host's dispatch work. The first call runs
+    eagerly (it also creates the optimizer state, which a capture must not allocate); the second
+    captures and replays; every call is exactly one optimizer step. A new input shape captures again.
+    """
 
     def __init__(self, model: SISAForCausalLM, optimizer: torch.optim.Optimizer | None = None, *,
-                 fused_ce: bool = True, clip: float = 1.0, bucket_cap_mb: float = 64.0):
+                 fused_ce: bool = True, clip: float = 1.0, bucket_cap_mb: float = 64.0, cuda_graph: bool = False):
         self.module = model
         dev = next(model.parameters()).device
         self.device = dev
@@ -69,12 +79,49 @@ class Trainer:
                 bucket_cap_mb=bucket_cap_mb, broadcast_buffers=False)
         else:
             self.model = model
-        self.opt = optimizer or make_optimizer(model)
+        self.cuda_graph = cuda_graph and dev.type == "cuda" and not self.distributed
+        self.opt = optimizer or make_optimizer(model, capturable=self.cuda_graph)
         self.fused_ce = fused_ce and dev.type == "cuda"
         self.clip = clip
+        self._graph = None
+        self._static_ids = None
+        self._static_loss = None
 
     def step(self, ids: torch.Tensor) -> torch.Tensor:
         """Train on ``ids`` (B, T) (labels = ids, shifted inside the model). Returns the loss (device)."""
+        if self.cuda_graph:
+            return self._graphed_step(ids)
+        return self._eager_step(ids)
+
+    def _graphed_step(self, ids: torch.Tensor) -> torch.Tensor:
+        if self._static_ids is None or self._static_ids.shape != ids.shape:
+            self._graph = None                       # first call for this shape: eager, capture on the next
+            self._static_ids = ids.detach().clone()
+            return self._eager_step(ids)
+        if self._graph is None:
+            self._capture()
+        self._static_ids.copy_(ids, non_blocking=True)
+        self._graph.replay()
+        return self._static_loss.clone()
+
+    def _capture(self) -> None:
+        self.opt.zero_grad(set_to_none=True)         # the captured backward allocates the gradients
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            self._static_loss = self._forward_backward(self._static_ids)
+            if self.clip:
+                torch.nn.utils.clip_grad_norm_(self.module.parameters(), self.clip)
+            self.opt.step()
+        self._graph = graph
+
+    def _forward_backward(self, ids: torch.Tensor) -> torch.Tensor:
+        self.model.train()
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            loss = self.model(ids, labels=ids, fused_ce=self.fused_ce).loss
+        loss.backward()
+        return loss.detach()
+
+    def _eager_step(self, ids: torch.Tensor) -> torch.Tensor:
         self.model.train()
         if self.device.type == "cuda":
             with torch.autocast("cuda", dtype=torch.bfloat16):

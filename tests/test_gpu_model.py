@@ -89,3 +89,25 @@ def test_cuda_model_deterministic(cuda_dev):
     assert torch.equal(l1, l2)
     for n in g1:
         assert torch.equal(g1[n], g2[n]), n
+
+
+def test_trainer_cuda_graph_matches_eager(cuda_dev):
+    """The captured whole-step graph (forward, backward, clipping, AdamW) trains like the eager step."""
+    from sisa_b200 import dp
+
+    cfg = sisa.SISAConfig(vocab_size=97, d_model=128, n_layer=2, n_head=2, d_ff=96, attn_impl="cuda")
+    ids = [torch.randint(0, 97, (2, 256), generator=torch.Generator().manual_seed(7 + i)).to(cuda_dev)
+           for i in range(4)]
+    losses = {}
+    params = {}
+    for mode in (False, True):
+        model = dp.build_model(cfg, cuda_dev, seed=3)
+        tr = dp.Trainer(model, cuda_graph=mode)
+        losses[mode] = [float(tr.step(ids[i % 4])) for i in range(6)]
+        torch.cuda.synchronize()
+        params[mode] = {n: p.detach().clone() for n, p in model.named_parameters()}
+    assert losses[True][0] == losses[False][0]
+    for a, b in zip(losses[True], losses[False]):
+        assert abs(a - b) <= 1e-4 * max(1.0, abs(b)), (losses[True], losses[False])
+    for n in params[False]:
+        assert torch.allclose(params[True][n], params[False][n], rtol=1e-4, atol=1e-5), n
