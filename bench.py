@@ -480,6 +480,63 @@ def run_lce(args):
                       "clocks": clk.summary()}))
 
 
+def run_norm(args):
+    """The block-boundary norms of one cfg3 block (8 x 2048 tokens, d_model 768, 12 heads) through
+    ``block_norm``: the attention norm (residual add, bf16 output, fp32 forget projection) and the
+    SwiGLU norm (residual add, two bf16 outputs), forward and backward with every gradient. fp32
+    residual stream ~ N(0, 4), bf16 residual ~ N(0, 1). Metric: bytes moved per second (algorithmic)."""
+    from sisa_b200.kernels.norm import block_norm
+
+    dev = torch.device("cuda", 0)
+    rows, d, nproj = args.norm_rows, 768, 12
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = (torch.randn((rows, d), generator=g, device=dev) * 2).requires_grad_(True)
+    res = torch.randn((rows, d), generator=g, device=dev).to(torch.bfloat16).requires_grad_(True)
+    w = (torch.rand((d,), generator=g, device=dev) + 0.5).requires_grad_(True)
+    pw = (torch.randn((nproj, d), generator=g, device=dev) * 0.05).requires_grad_(True)
+    pb = torch.randn((nproj,), generator=g, device=dev).requires_grad_(True)
+    bf = torch.bfloat16
+    g_attn = [torch.randn((rows, d), generator=g, device=dev), torch.randn((rows, d), generator=g, device=dev).to(bf),
+              torch.randn((rows, nproj), generator=g, device=dev)]
+    g_ffn = [torch.randn((rows, d), generator=g, device=dev)] + \
+        [torch.randn((rows, d), generator=g, device=dev).to(bf) for _ in range(2)]
+
+    def step():
+        a = block_norm(x, w, 1e-6, res=res, out_dtypes=(bf,), proj=(pw, pb))
+        torch.autograd.backward(list(a), g_attn)
+        f = block_norm(x, w, 1e-6, res=res, out_dtypes=(bf, bf))
+        torch.autograd.backward(list(f), g_ffn)
+        for t in (x, res, w, pw, pb):
+            t.grad = None
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()      # replayed, so that the time is the kernels' and not the host's
+    with torch.cuda.graph(graph):
+        step()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    k = max(3, min(args.steps, 50))
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(k)]
+    with Clocks(0) as clk:
+        for i in range(k):
+            flush.zero_()   # inputs are 75 MB per norm: flush L2 between steps
+            ev[i][0].record()
+            graph.replay()
+            ev[i][1].record()
+        torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in ev) / k
+    # algorithmic bytes per row: attention norm fwd 9268 + bwd 12340, SwiGLU norm fwd 10756 + bwd 13828
+    per_row = (3072 + 1536 + 3072 + 1536 + 48 + 4) + (3072 + 1536 + 3072 + 48 + 4 + 3072 + 1536) + \
+        (3072 + 1536 + 3072 + 2 * 1536 + 4) + (3072 + 2 * 1536 + 3072 + 4 + 3072 + 1536)
+    print(json.dumps({"metric": "block-boundary RMSNorm fwd+bwd (attention and SwiGLU norms of one cfg3 block)",
+                      "value": round(rows * per_row / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                      "ms_per_step": round(ms, 4), "steps": k, "dtype": "fp32 stream, bf16 outputs",
+                      "config": {"rows": rows, "d": d, "n_proj": nproj, "bytes_per_row": per_row,
+                                 "l2": "flushed between steps", "timing": "CUDA graph replay of the step"},
+                      "clocks": clk.summary()}))
+
+
 def run_decode(args):
     """cfg4: 12-layer sisa-152m, random init, bf16 weights; batch 64, prompt 8192 ids (id 0 first), greedy decode.
     Reports prefill tokens/s and per-step decode latency with the cache bytes read per step."""
@@ -566,8 +623,10 @@ def main(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-train", action="store_true")
-    ap.add_argument("--workload", choices=["attn", "lce", "decode"], default="attn",
-                    help="attn (default: config 1 + the config 3 training leg), lce (config 2), decode (config 4)")
+    ap.add_argument("--workload", choices=["attn", "lce", "decode", "norm"], default="attn",
+                    help="attn (default: config 1 + the config 3 training leg), lce (config 2), decode (config 4), "
+                         "norm (the fused block-boundary norms of config 3)")
+    ap.add_argument("--norm-rows", type=int, default=16384)
     ap.add_argument("--decode-batch", type=int, default=64)
     ap.add_argument("--decode-prompt", type=int, default=8192)
     ap.add_argument("--decode-steps", type=int, default=256)
@@ -583,6 +642,8 @@ def main(argv=None):
         run_lce(args)
     elif args.workload == "decode":
         run_decode(args)
+    elif args.workload == "norm":
+        run_norm(args)
     else:
         run_cuda(args)
 
