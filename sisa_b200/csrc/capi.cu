@@ -134,8 +134,9 @@ int check_view(const sisa_view4* v, int elem_bytes, const char* name) {
 int check_dims(int64_t B, int64_t H, int64_t L) {
   if (B < 1 || H < 1 || L < 1) return fail(SISA_ERR_VALUE, "B, H and L must be >= 1 (got %lld, %lld, %lld)",
                                            (long long)B, (long long)H, (long long)L);
-  // The attention grids are (L/128, B*H): the second grid dimension is limited to 65535 blocks.
-  if (L > (1ll << 24) || B * H > 65535)
+  // The attention grids are (L/128, B*H) and the preparation grids (H/4, L/64, B): their second and
+  // third grid dimensions are limited to 65535 blocks.
+  if (L > 65535ll * 64 || B * H > 65535)
     return fail(SISA_ERR_VALUE, "problem too large (B*H=%lld, L=%lld)", (long long)(B * H), (long long)L);
   return SISA_OK;
 }

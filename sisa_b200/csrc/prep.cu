@@ -283,7 +283,7 @@ template <bool kHalf>
 __global__ void __launch_bounds__(256) prep_fwd_kernel(PrepArgs a) {
   extern __shared__ __align__(16) uint8_t sm[];
   constexpr int kP = kS2 / 2;
-  const int c = blockIdx.x, b = blockIdx.y, h0 = blockIdx.z * kHG;
+  const int h0 = blockIdx.x * kHG, c = blockIdx.y, b = blockIdx.z;   // head groups of one row block adjacent
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t sb = smem_u32(sm);
   const int tb = c * kBlk, tl = 2 * lane;
@@ -450,7 +450,7 @@ template <bool kHalf>
 __global__ void __launch_bounds__(kBrotThreads, 2) prep_brot_kernel(PrepBwdArgs a) {
   extern __shared__ __align__(16) uint8_t sm[];
   constexpr int kP = kBrotP, kWph = kS2 / kP;
-  const int c = blockIdx.x, b = blockIdx.y, h0 = blockIdx.z * kHG;
+  const int h0 = blockIdx.x * kHG, c = blockIdx.y, b = blockIdx.z;   // head groups of one row block adjacent
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t sb = smem_u32(sm);
   const int tb = c * kBlk;
@@ -579,7 +579,7 @@ template <bool kHalf>
 __global__ void __launch_bounds__(256) prep_bwd_kernel(PrepBwdArgs a) {
   extern __shared__ __align__(16) uint8_t sm[];
   constexpr int kP = kS2 / 2;
-  const int c = blockIdx.x, b = blockIdx.y, h0 = blockIdx.z * kHG;
+  const int h0 = blockIdx.x * kHG, c = blockIdx.y, b = blockIdx.z;   // head groups of one row block adjacent
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t sb = smem_u32(sm);
   const int tb = c * kBlk, tl = 2 * lane;
@@ -662,7 +662,7 @@ __global__ void __launch_bounds__(256) prep_bwd_kernel(PrepBwdArgs a) {
   }
   // zero the padding columns [ntot, npad) of this block's rows (first head group only)
   const int npadc = a.npad - a.ntot;
-  if (npadc > 0 && blockIdx.z == 0) {
+  if (npadc > 0 && blockIdx.x == 0) {
     for (int i = threadIdx.x; i < kBlk * npadc; i += blockDim.x) {
       const int t = tb + i / npadc;
       if (t < a.L) st_lp<kHalf>(a.dproj, (int64_t)b * a.dproj_sb + (int64_t)t * a.dproj_sl + a.ntot + i % npadc, 0.f);
@@ -680,7 +680,7 @@ cudaError_t launch_prep_fwd(const PrepFwdLaunch& p, cudaStream_t st) {
   a.c_rot = p.c_rot; a.b_rot = p.b_rot; a.pos = p.pos; a.Lp = (int)p.Lp;
   a.tot = p.tot; a.status = p.status;
   dim3 grid(a.nch, a.B);
-  dim3 grid_rot(a.nch, a.B, (a.H + kHG - 1) / kHG);
+  dim3 grid_rot((a.H + kHG - 1) / kHG, a.nch, a.B);
   if (p.dtype == 1) {
     prep_sums_kernel<true><<<grid, 256, 0, st>>>(a);
   } else {
@@ -715,7 +715,7 @@ cudaError_t launch_prep_bwd(const PrepBwdLaunch& p, cudaStream_t st) {
   a.dproj = p.dproj; a.dproj_sb = p.dproj_sb; a.dproj_sl = p.dproj_sl; a.dz = p.dz; a.bt = p.bt;
   a.dphi = reinterpret_cast<float*>(p.bt + (int64_t)a.B * a.H * a.nch * kTot);
   a.status = p.status;
-  dim3 grid_rot(a.nch, a.B, (a.H + kHG - 1) / kHG);
+  dim3 grid_rot((a.H + kHG - 1) / kHG, a.nch, a.B);
   if (p.dtype == 1) {
     cudaFuncSetAttribute(prep_brot_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmBrot);
     prep_brot_kernel<true><<<grid_rot, kBrotThreads, kSmBrot, st>>>(a);
