@@ -35,6 +35,7 @@
 // score GEMMs have completed before its operands exist, so the gradient issuer's commit alone releases
 // the stage.
 #include <cuda_runtime.h>
+#include <cooperative_groups.h>
 
 #include "attn_common.cuh"
 #include "attn.h"
@@ -913,34 +914,45 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
 }
 
 // d lambda_h = sum over (b, t) of the per-row parts, in fp64 with a fixed reduction tree, rounded once
-// (attention.py:781-783). One CTA of 1024 threads per head; thread i takes the elements i, i + 1024,
-// ... of the head's B x L values (eight loads in flight per round), then a tree over the threads.
-constexpr int kDlamThreads = 1024;
-__global__ void __launch_bounds__(kDlamThreads) dlam_kernel(const float* rl, float* dlam, int B, int H, int L) {
-  const int h = blockIdx.x;
+// (attention.py:781-783). One cluster of kDlamCluster CTAs per head: CTA rank q, thread i takes the
+// elements (q kDlamThreads + i) + k kDlamThreads kDlamCluster of the head's B x L values (eight loads in
+// flight per round), a tree over the CTA's threads, then rank 0 adds the CTAs' sums in rank order
+// through distributed shared memory (deterministic, no atomics, no workspace).
+constexpr int kDlamThreads = 512, kDlamCluster = 8;
+__global__ void __cluster_dims__(kDlamCluster, 1, 1) __launch_bounds__(kDlamThreads)
+    dlam_kernel(const float* rl, float* dlam, int B, int H, int L) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int h = blockIdx.y, rank = (int)cluster.block_rank();
   __shared__ double part[kDlamThreads];
-  const int64_t n = (int64_t)B * L;
+  const int64_t n = (int64_t)B * L, stride = (int64_t)kDlamThreads * kDlamCluster;
   auto at = [&](int64_t e) {
     const int64_t bb = e / L;
     return __ldg(rl + (bb * H + h) * L + (e - bb * L));
   };
   double acc = 0.0;
-  int64_t e = threadIdx.x;
-  for (; e + 7 * kDlamThreads < n; e += 8 * kDlamThreads) {
+  int64_t e = (int64_t)rank * kDlamThreads + threadIdx.x;
+  for (; e + 7 * stride < n; e += 8 * stride) {
     float v[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = at(e + (int64_t)i * kDlamThreads);
+    for (int i = 0; i < 8; ++i) v[i] = at(e + (int64_t)i * stride);
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc += (double)v[i];
   }
-  for (; e < n; e += kDlamThreads) acc += (double)at(e);
+  for (; e < n; e += stride) acc += (double)at(e);
   part[threadIdx.x] = acc;
   __syncthreads();
   for (int w = kDlamThreads / 2; w > 0; w >>= 1) {
     if ((int)threadIdx.x < w) part[threadIdx.x] += part[threadIdx.x + w];
     __syncthreads();
   }
-  if (threadIdx.x == 0) dlam[h] = (float)part[0];
+  cluster.sync();                        // every CTA's part[0] is final
+  if (rank == 0 && threadIdx.x == 0) {
+    double t = 0.0;
+    for (int q = 0; q < kDlamCluster; ++q) t += *cluster.map_shared_rank(&part[0], q);
+    dlam[h] = (float)t;
+  }
+  cluster.sync();                        // the other CTAs' shared memory stays until rank 0 has read it
 }
 
 }  // namespace bwd
@@ -960,7 +972,7 @@ cudaError_t launch_attn_bwd(const BwdParams& p, int dtype, cudaStream_t st) {
     attn_bwd_dq_kernel<false><<<gq, NTHREADS, dqk::SMEM_BYTES, st>>>(p);
     attn_bwd_dkv_kernel<false><<<gk, NTHREADS, dkv::SMEM_BYTES, st>>>(p);
   }
-  dlam_kernel<<<p.H, kDlamThreads, 0, st>>>(p.rl, p.dlam, p.B, p.H, p.L);
+  dlam_kernel<<<dim3(kDlamCluster, p.H), kDlamThreads, 0, st>>>(p.rl, p.dlam, p.B, p.H, p.L);
   return cudaGetLastError();
 }
 
