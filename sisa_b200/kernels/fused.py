@@ -11,7 +11,7 @@ import torch
 
 from .. import _lib, backends
 
-__all__ = ["sisa_fused", "fused_layout", "concat_fused_weights"]
+__all__ = ["sisa_fused", "fused_layout", "concat_fused_weights", "fused_projection"]
 
 D_HEAD = 64
 D_STATE = 32
@@ -47,6 +47,47 @@ def concat_fused_weights(W_Q, W_K, W_V, W_B, W_C, W_theta, W_alpha, b_alpha):
     if W.shape[0] != off["NPAD"]:
         raise ValueError(f"concatenated weight has {W.shape[0]} rows, expected {off['NPAD']} for n_head={H}")
     return W, torch.cat(bs, 0)
+
+
+class _FusedProjFn(torch.autograd.Function):
+    """``proj = x W_cat^T + b_cat`` in the compute dtype, where ``b_cat`` is zero except the alpha
+    columns. The forward is the call ``F.linear`` makes under autocast (inputs cast to the compute dtype,
+    bias added in the GEMM epilogue before the one rounding); the backward runs the same two GEMMs as
+    autograd's linear backward, but forms the bias gradient from the H alpha columns only, where
+    autograd reduces all NPAD columns of the output gradient."""
+
+    @staticmethod
+    def forward(ctx, x, weight, b_alpha, col_a, dtype):
+        H = b_alpha.shape[0]
+        xc, wc = x.to(dtype), weight.to(dtype)
+        bias = torch.zeros((weight.shape[0],), dtype=dtype, device=x.device)
+        bias[col_a:col_a + H] = b_alpha.to(dtype)
+        with torch.autocast(x.device.type, enabled=False):
+            out = torch.nn.functional.linear(xc, wc, bias)
+        ctx.save_for_backward(xc, wc)
+        ctx.col_a, ctx.H = col_a, H
+        ctx.dtypes = (x.dtype, weight.dtype, b_alpha.dtype)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        xc, wc = ctx.saved_tensors
+        g2 = g.reshape(-1, g.shape[-1])
+        dx = dw = db = None
+        if ctx.needs_input_grad[0]:
+            dx = (g2 @ wc).view(xc.shape).to(ctx.dtypes[0])
+        if ctx.needs_input_grad[1]:
+            dw = (g2.t() @ xc.reshape(-1, xc.shape[-1])).to(ctx.dtypes[1])
+        if ctx.needs_input_grad[2]:
+            db = g2[:, ctx.col_a:ctx.col_a + ctx.H].sum(0).to(ctx.dtypes[2])
+        return dx, dw, db, None, None
+
+
+def fused_projection(x: torch.Tensor, weight: torch.Tensor, b_alpha: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """``F.linear(x, W_cat, b_cat)`` under autocast to ``dtype`` (fused_prep.py:99-122) with ``b_cat`` built
+    from ``b_alpha``; the same values, and a backward that reduces only the alpha columns for the bias."""
+    col_a = fused_layout(b_alpha.shape[0])["A"]
+    return _FusedProjFn.apply(x, weight, b_alpha, col_a, dtype)
 
 
 def _heads(t: torch.Tensor, col: int, H: int, w: int) -> torch.Tensor:

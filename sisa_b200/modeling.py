@@ -216,7 +216,13 @@ class SISAAttention(nn.Module):
 
         bsz, seq_len, d = x.shape
         weight, bias = self.fused_weights()
-        proj = F.linear(x, weight, bias)
+        cd = _compute_dtype(x)
+        if x.is_cuda and (cd != x.dtype or cd != weight.dtype):
+            from .kernels.fused import fused_projection
+
+            proj = fused_projection(x, weight, self.alpha_proj.bias, cd)   # autocast's linear, lean bias gradient
+        else:
+            proj = F.linear(x, weight, bias)
         y = sisa_fused(proj, self._forget_logits(x) if z is None else z, self.lam(), self.config.n_head)
         return self.W_O(y.reshape(bsz, seq_len, d))
 

@@ -111,3 +111,32 @@ def test_trainer_cuda_graph_matches_eager(cuda_dev):
         assert abs(a - b) <= 1e-4 * max(1.0, abs(b)), (losses[True], losses[False])
     for n in params[False]:
         assert torch.allclose(params[True][n], params[False][n], rtol=1e-4, atol=1e-5), n
+
+
+def test_fused_projection_matches_autocast_linear(cuda_dev):
+    """fused_projection = F.linear(x, W_cat, b_cat) under bf16 autocast: identical output and gradients
+    (the bias gradient from the alpha columns only)."""
+    from sisa_b200.kernels.fused import concat_fused_weights, fused_projection, fused_layout
+
+    H, d = 4, 256
+    gen = torch.Generator(device=cuda_dev).manual_seed(5)
+    rnd = lambda *s: torch.randn(s, generator=gen, device=cuda_dev) * 0.05  # noqa: E731
+    ws = [rnd(H * 64, d), rnd(H * 64, d), rnd(H * 64, d), rnd(H * 32, d), rnd(H * 32, d), rnd(H * 16, d), rnd(H, d)]
+    ba = rnd(H)
+    x = torch.randn((2, 96, d), generator=gen, device=cuda_dev).to(torch.bfloat16)
+    ref = [t.detach().clone().requires_grad_(True) for t in ws + [ba]]
+    ker = [t.detach().clone().requires_grad_(True) for t in ws + [ba]]
+    xr, xk = x.detach().clone().requires_grad_(True), x.detach().clone().requires_grad_(True)
+    go = torch.randn((2, 96, fused_layout(H)["NPAD"]), generator=gen, device=cuda_dev).to(torch.bfloat16)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        W, b = concat_fused_weights(*ref)
+        yr = torch.nn.functional.linear(xr, W, b)
+        Wk, _ = concat_fused_weights(*ker)
+        yk = fused_projection(xk, Wk, ker[-1], torch.bfloat16)
+    assert yk.dtype == yr.dtype and torch.equal(yk, yr)
+    yr.backward(go)
+    yk.backward(go)
+    assert torch.equal(xk.grad, xr.grad)
+    for a, r in zip(ker[:-1], ref[:-1]):
+        assert torch.equal(a.grad, r.grad)
+    assert torch.allclose(ker[-1].grad, ref[-1].grad, rtol=1e-2, atol=1e-3)
