@@ -236,6 +236,21 @@ int sisa_decode_attn_noalloc(const sisa_view4* q, const sisa_view4* c, const flo
                              int64_t B, int64_t H, int64_t N, int dtype, const sisa_view4* y,
                              int32_t* status, void* stream);
 
+/* One decode step's layer input from the fused projection row of the new token (the single-token case
+ * of src/sisa/modeling.py:171-199 with the recurrences continued from the cache, generation.py:58-95):
+ * per (batch b, head h), with proj the (B, NPAD) row in `dtype` (columns as sisa_fused_layout) and z the
+ * (B, H) fp32 forget logits (z_sb row stride; may be null together with f_cache and f_out):
+ *   g = g_cache[pos-1] - softplus(alpha), F = f_cache[pos-1] + logsigmoid(z), Phi = phi + theta (16 pairs),
+ *   c~ = R(Phi) c, b~ = R(Phi) b (fp32, torch's separate products, one rounding).
+ * Writes k, v, b~ into the caches at position pos, g and F into g_cache/f_cache[pos] and g_out/f_out
+ * (B, H), c~ into c_out (B, H, 32) contiguous, and advances phi (B, H, 16) fp32 contiguous in place.
+ * 1 <= pos < gf_stride; the caches are (B, H, >pos, 64 or 32) views with even element strides. q is the
+ * Q columns of proj, passed to sisa_decode_attn as a view. */
+int sisa_decode_prep(const void* proj, int64_t proj_sb, const float* z, int64_t z_sb, int64_t B, int64_t H,
+                     int dtype, const sisa_view4* k_cache, const sisa_view4* v_cache, const sisa_view4* b_cache,
+                     float* g_cache, float* f_cache, int64_t gf_stride, int64_t pos, float* phi, void* c_out,
+                     float* g_out, float* f_out, int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -89,6 +89,8 @@ SIGNATURES = {
     "sisa_decode_workspace": (_I64, [_I64, _I64, _I64]),
     "sisa_decode_attn_noalloc": (_I, [_VP, _VP, _P, _P, _VP, _VP, _VP, _P, _P, _I64, _P, _I64, _I64, _I64, _I, _VP,
                                       _P, _P]),
+    "sisa_decode_prep": (_I, [_P, _I64, _P, _I64, _I64, _I64, _I, _VP, _VP, _VP, _P, _P, _I64, _I64, _P, _P, _P, _P,
+                              _P, _P]),
     "sisa_rmsnorm_bwd_workspace": (_I64, [_I64, _I64]),
     "sisa_rmsnorm_fwd": (_I, [_P, _I64, _I, _P, _I64, _I64, ctypes.c_float, _P, _I64, _I, _P, _P, _P]),
     "sisa_rmsnorm_bwd": (_I, [_P, _I64, _I, _P, _I64, _I, _P, _P, _I64, _I64, _P, _I64, _I, _P, _P, _P, _P]),

@@ -409,6 +409,47 @@ int sisa_decode_attn(const sisa_view4* q, const sisa_view4* c, const float* g_q,
   return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_decode_attn launch");
 }
 
+int sisa_decode_prep(const void* proj, int64_t proj_sb, const float* z, int64_t z_sb, int64_t B, int64_t H,
+                     int dtype, const sisa_view4* k_cache, const sisa_view4* v_cache, const sisa_view4* b_cache,
+                     float* g_cache, float* f_cache, int64_t gf_stride, int64_t pos, float* phi, void* c_out,
+                     float* g_out, float* f_out, int32_t* status, void* stream) {
+  (void)status;
+  int rc;
+  if ((rc = check_dims(B, H, pos + 1)) || (rc = check_dtype(dtype))) return rc;
+  if ((rc = check_view(k_cache, 2, "k_cache")) || (rc = check_view(v_cache, 2, "v_cache")) ||
+      (rc = check_view(b_cache, 2, "b_cache")))
+    return rc;
+  if (!proj || !g_cache || !phi || !c_out || !g_out) return fail(SISA_ERR_VALUE, "sisa_decode_prep: null pointer");
+  if ((z == nullptr) != (f_cache == nullptr) || (z == nullptr) != (f_out == nullptr))
+    return fail(SISA_ERR_VALUE, "sisa_decode_prep: z, f_cache and f_out must all be given or all be null");
+  if (pos < 1 || pos >= gf_stride)
+    return fail(SISA_ERR_VALUE, "sisa_decode_prep: position %lld outside [1, %lld)", (long long)pos, (long long)gf_stride);
+  int64_t off[9];
+  if ((rc = sisa_fused_layout(H, off))) return rc;
+  const auto al4 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 3u) == 0; };
+  if (!al4(proj) || proj_sb < off[7] || proj_sb % 2 || !al4(c_out) || !al4(k_cache->data) || !al4(v_cache->data) ||
+      !al4(b_cache->data) || (k_cache->stride_b | k_cache->stride_h | k_cache->stride_l) % 2 ||
+      (v_cache->stride_b | v_cache->stride_h | v_cache->stride_l) % 2 ||
+      (b_cache->stride_b | b_cache->stride_h | b_cache->stride_l) % 2)
+    return fail(SISA_ERR_ALIGN, "sisa_decode_prep: operands need 4-byte alignment and even element strides");
+  sisa::DecodePrepParams p{};
+  p.proj = static_cast<const uint16_t*>(proj); p.proj_sb = proj_sb;
+  p.z = z; p.z_sb = z_sb;
+  p.col_k = (int)off[1]; p.col_v = (int)off[2]; p.col_b = (int)off[3]; p.col_c = (int)off[4];
+  p.col_th = (int)off[5]; p.col_a = (int)off[6];
+  p.k = static_cast<uint16_t*>(k_cache->data); p.k_sb = k_cache->stride_b; p.k_sh = k_cache->stride_h;
+  p.k_sl = k_cache->stride_l;
+  p.v = static_cast<uint16_t*>(v_cache->data); p.v_sb = v_cache->stride_b; p.v_sh = v_cache->stride_h;
+  p.v_sl = v_cache->stride_l;
+  p.bm = static_cast<uint16_t*>(b_cache->data); p.b_sb = b_cache->stride_b; p.b_sh = b_cache->stride_h;
+  p.b_sl = b_cache->stride_l;
+  p.g = g_cache; p.f = f_cache; p.gf_stride = gf_stride; p.phi = phi;
+  p.c_out = static_cast<uint16_t*>(c_out); p.g_out = g_out; p.f_out = f_out;
+  p.B = (int)B; p.H = (int)H; p.pos = pos;
+  cudaError_t e = sisa::launch_decode_prep(p, dtype, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_decode_prep launch");
+}
+
 int64_t sisa_lce_workspace(int64_t R, int64_t Vp) {
   const int64_t nblk = (Vp + 255) / 256;
   return R * nblk * 8 + ((R * 4 + 255) / 256) * 256;

@@ -17,6 +17,7 @@
 #include <mutex>
 
 #include "sm100.cuh"
+#include "gate_math.cuh"
 #include "decode.h"
 
 namespace sisa {
@@ -210,6 +211,65 @@ int decode_splits(int64_t B, int64_t H, int64_t N) {
   if (s < 1) s = 1;
   if (s > 64) s = 64;
   return (int)s;
+}
+
+// One decode step's layer input (the single-token case of modeling.py:171-199 / fused_prep.py:247-352),
+// one warp per (batch, head): g_t = g_{t-1} - softplus(alpha_t), F_t = F_{t-1} + logsigmoid(z_t),
+// Phi_t = Phi_{t-1} + theta_t (16 pairs), c~ = R(Phi_t) c and b~ = R(Phi_t) b in fp32 with torch's
+// separate products (no contraction), rounded once; k, v, b~, g, F go into the caches at pos, c~, g_t,
+// F_t to the query-side outputs, and Phi advances in place.
+template <bool kHalf>
+__global__ void __launch_bounds__(256) decode_prep_kernel(DecodePrepParams p) {
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (w >= p.B * p.H) return;
+  const int b = w / p.H, h = w - b * p.H;
+  const uint16_t* row = p.proj + (int64_t)b * p.proj_sb;
+  auto to_f = [](uint16_t x) {
+    if constexpr (kHalf) return __half2float(__ushort_as_half(x));
+    else return __uint_as_float((uint32_t)x << 16);
+  };
+  auto to_lp = [](float x) -> uint16_t {
+    if constexpr (kHalf) return __half_as_ushort(__float2half_rn(x));
+    else return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+  };
+  // k and v rows: 64 elements, two per lane
+  {
+    const uint32_t kk = reinterpret_cast<const uint32_t*>(row + p.col_k + h * 64)[lane];
+    const uint32_t vv = reinterpret_cast<const uint32_t*>(row + p.col_v + h * 64)[lane];
+    reinterpret_cast<uint32_t*>(p.k + (int64_t)b * p.k_sb + (int64_t)h * p.k_sh + p.pos * p.k_sl)[lane] = kk;
+    reinterpret_cast<uint32_t*>(p.v + (int64_t)b * p.v_sb + (int64_t)h * p.v_sh + p.pos * p.v_sl)[lane] = vv;
+  }
+  const int64_t bh = (int64_t)b * p.H + h;
+  if (lane < 16) {
+    float* ph = p.phi + bh * 16 + lane;
+    const float phin = to_f(row[p.col_th + h * 16 + lane]) + *ph;
+    *ph = phin;
+    const float cs = cosf(phin), sn = sinf(phin);
+    const int e = 2 * lane;
+    const float ce = to_f(row[p.col_c + h * 32 + e]), co = to_f(row[p.col_c + h * 32 + e + 1]);
+    const float be = to_f(row[p.col_b + h * 32 + e]), bo = to_f(row[p.col_b + h * 32 + e + 1]);
+    const uint32_t cr = (uint32_t)to_lp(__fsub_rn(__fmul_rn(ce, cs), __fmul_rn(co, sn))) |
+                        ((uint32_t)to_lp(__fadd_rn(__fmul_rn(ce, sn), __fmul_rn(co, cs))) << 16);
+    const uint32_t br = (uint32_t)to_lp(__fsub_rn(__fmul_rn(be, cs), __fmul_rn(bo, sn))) |
+                        ((uint32_t)to_lp(__fadd_rn(__fmul_rn(be, sn), __fmul_rn(bo, cs))) << 16);
+    reinterpret_cast<uint32_t*>(p.c_out + bh * 32)[lane] = cr;
+    reinterpret_cast<uint32_t*>(p.bm + (int64_t)b * p.b_sb + (int64_t)h * p.b_sh + p.pos * p.b_sl)[lane] = br;
+  } else if (lane == 16) {
+    const float gq = neg_softplus(to_f(row[p.col_a + h])) + p.g[bh * p.gf_stride + p.pos - 1];
+    p.g[bh * p.gf_stride + p.pos] = gq;
+    p.g_out[bh] = gq;
+  } else if (lane == 17 && p.f) {
+    const float fq = logsigmoid(p.z[(int64_t)b * p.z_sb + h]) + p.f[bh * p.gf_stride + p.pos - 1];
+    p.f[bh * p.gf_stride + p.pos] = fq;
+    p.f_out[bh] = fq;
+  }
+}
+
+cudaError_t launch_decode_prep(const DecodePrepParams& p, int dtype, cudaStream_t st) {
+  const unsigned grid = (unsigned)((p.B * p.H + 7) / 8);
+  if (dtype == 1) decode_prep_kernel<true><<<grid, 256, 0, st>>>(p);
+  else decode_prep_kernel<false><<<grid, 256, 0, st>>>(p);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_decode(const DecodeParams& p, int dtype, cudaStream_t st) {

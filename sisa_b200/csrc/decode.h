@@ -23,7 +23,24 @@ struct DecodeParams {
   int32_t* status;
 };
 
+// One decode step's layer input from the fused projection row (decode_prep_kernel).
+struct DecodePrepParams {
+  const uint16_t* proj; int64_t proj_sb;        // (B, NPAD) low precision, row stride in elements
+  const float* z; int64_t z_sb;                 // (B, H) forget logits or null
+  int col_k, col_v, col_b, col_c, col_th, col_a;
+  uint16_t* k; int64_t k_sb, k_sh, k_sl;        // caches, element strides; the new row goes to pos
+  uint16_t* v; int64_t v_sb, v_sh, v_sl;
+  uint16_t* bm; int64_t b_sb, b_sh, b_sl;
+  float* g; float* f; int64_t gf_stride;        // (B*H, gf_stride); f null without forget logits
+  float* phi;                                   // (B, H, 16) contiguous, advanced in place
+  uint16_t* c_out;                              // (B, H, 32) contiguous
+  float* g_out; float* f_out;                   // (B, H)
+  int B, H;
+  int64_t pos;
+};
+
 int decode_splits(int64_t B, int64_t H, int64_t N);
 cudaError_t launch_decode(const DecodeParams& p, int dtype, cudaStream_t st);
+cudaError_t launch_decode_prep(const DecodePrepParams& p, int dtype, cudaStream_t st);
 
 }  // namespace sisa

@@ -24,6 +24,7 @@
 
 #include "sm100.cuh"
 #include "prep.h"
+#include "gate_math.cuh"
 
 namespace sisa {
 
@@ -40,24 +41,6 @@ __device__ __forceinline__ float ld_lp(const void* p, int64_t i) {
   const unsigned short bits = __ldg(reinterpret_cast<const unsigned short*>(p) + i);
   if constexpr (kHalf) return __half2float(__ushort_as_half(bits));
   else return __bfloat162float(__ushort_as_bfloat16(bits));
-}
-
-__device__ __forceinline__ float neg_softplus(float a) {       // torch softplus, threshold 20
-  return -(a > 20.f ? a : log1pf(expf(a)));
-}
-__device__ __forceinline__ float softplus_grad(float a) {      // torch softplus_backward
-  if (a > 20.f) return 1.f;
-  const float e = expf(a);
-  return e / (e + 1.f);
-}
-__device__ __forceinline__ float logsigmoid(float z) {         // torch log_sigmoid_forward; NaN propagates
-  const float m = (z != z) ? z : fminf(z, 0.f);
-  return m - log1pf(expf(-fabsf(z)));
-}
-__device__ __forceinline__ float logsigmoid_grad(float z) {    // torch log_sigmoid_backward
-  const float e = expf(-fabsf(z));
-  const float r = e / (1.f + e);
-  return z < 0.f ? 1.f - r : r;
 }
 
 // Inclusive scan of a 64-element sequence held two per lane (x0 = element 2l, x1 = element 2l+1).

@@ -50,8 +50,8 @@ class LayerState:
     def capacity(self) -> int:
         return self.k_buf.shape[2]
 
-    def append(self, k: Tensor, v: Tensor, b: Tensor, g: Tensor, fgate: Tensor, phi: Tensor) -> None:
-        n = k.shape[2]
+    def reserve(self, n: int) -> None:
+        """Make room for ``n`` more positions (the buffers grow by doubling)."""
         if self.length + n > self.capacity:
             old = (self.k_buf, self.v_buf, self.b_buf, self.g_buf, self.f_buf)
             B, H, _, D = self.k_buf.shape
@@ -59,6 +59,17 @@ class LayerState:
             self._alloc(B, H, cap, D, self.b_buf.shape[-1], self.k_buf.dtype, self.k_buf.device)
             for dst, src in zip((self.k_buf, self.v_buf, self.b_buf, self.g_buf, self.f_buf), old):
                 dst[:, :, :self.length].copy_(src[:, :, :self.length])
+
+    def phi_buffer(self) -> Tensor:
+        """``phi`` as an fp32 contiguous tensor this state owns (the fused decode step advances it in place)."""
+        if not (self.phi.dtype == torch.float32 and self.phi.is_contiguous() and getattr(self, "_phi_owned", False)):
+            self.phi = self.phi.float().contiguous().clone()
+            self._phi_owned = True
+        return self.phi
+
+    def append(self, k: Tensor, v: Tensor, b: Tensor, g: Tensor, fgate: Tensor, phi: Tensor) -> None:
+        n = k.shape[2]
+        self.reserve(n)
         t0, t1 = self.length, self.length + n
         self.k_buf[:, :, t0:t1].copy_(k)
         self.v_buf[:, :, t0:t1].copy_(v)
@@ -66,6 +77,7 @@ class LayerState:
         self.g_buf[:, :, t0:t1].copy_(g)
         self.f_buf[:, :, t0:t1].copy_(fgate)
         self.phi = phi
+        self._phi_owned = False
         self.length = t1
 
     @property

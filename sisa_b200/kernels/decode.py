@@ -10,7 +10,7 @@ import torch
 
 from .. import _lib, backends
 
-__all__ = ["decode_attention"]
+__all__ = ["decode_attention", "decode_prep"]
 
 
 def decode_attention(q: torch.Tensor, c: torch.Tensor, g: torch.Tensor, fgate: torch.Tensor | None, state,
@@ -40,3 +40,41 @@ def decode_attention(q: torch.Tensor, c: torch.Tensor, g: torch.Tensor, fgate: t
     _lib.check(rc, "sisa_decode_attn")
     backends.after_call(dev)
     return y
+
+
+def decode_prep(proj: torch.Tensor, z: torch.Tensor | None, state, n_head: int):
+    """One decode step's layer input on the sm_100a kernel: from the new token's fused projection row
+    ``proj`` (B, 1, NPAD) and forget logits ``z`` (B, 1, H) fp32, continue the g / F / Phi recurrences
+    from ``state`` (generation.py:58-95), rotate c and b, and append k, v, b~, g, F to the cache.
+    Returns q (a view of proj's Q columns), c~ (B, H, 1, 32), g and F (B, H, 1) fp32, as
+    :func:`decode_attention` takes them; the state then holds the new position."""
+    lib = _lib.load()
+    B, H = proj.shape[0], n_head
+    proj2 = proj.reshape(B, proj.shape[-1])
+    if proj2.stride(-1) != 1 or proj2.stride(0) % 2:
+        proj2 = proj2.contiguous()
+    if proj2.dtype != state.k_buf.dtype:
+        raise TypeError(f"decode_prep: projection dtype {proj2.dtype} differs from the cache's {state.k_buf.dtype}")
+    dev = proj.device
+    state.reserve(1)
+    phi = state.phi_buffer()
+    pos = state.length
+    c = torch.empty((B, H, 1, 32), dtype=proj2.dtype, device=dev)
+    g = torch.empty((B, H, 1), dtype=torch.float32, device=dev)
+    f = None
+    z2 = None
+    if z is not None:
+        z2 = z.reshape(B, H).float().contiguous()
+        f = torch.empty((B, H, 1), dtype=torch.float32, device=dev)
+    vk, vv, vb = (_lib.view4(t) for t in (state.k_buf, state.v_buf, state.b_buf))
+    st = backends.status_word(dev)
+    rc = lib.sisa_decode_prep(proj2.data_ptr(), proj2.stride(0), _lib.ptr(z2), 0 if z2 is None else z2.stride(0), B, H,
+                              _lib.dtype_code(proj2.dtype), _lib.vref(vk), _lib.vref(vv), _lib.vref(vb),
+                              state.g_buf.data_ptr(), None if z2 is None else state.f_buf.data_ptr(),
+                              state.g_buf.shape[2], pos, phi.data_ptr(), c.data_ptr(), g.data_ptr(), _lib.ptr(f),
+                              st.data_ptr(), _lib.stream_ptr(dev))
+    _lib.check(rc, "sisa_decode_prep")
+    backends.after_call(dev)
+    state.length = pos + 1
+    q = proj2[:, :H * 64].view(B, H, 64).unsqueeze(2)
+    return q, c, g, f

@@ -226,8 +226,39 @@ class SISAAttention(nn.Module):
         y = sisa_fused(proj, self._forget_logits(x) if z is None else z, self.lam(), self.config.n_head)
         return self.W_O(y.reshape(bsz, seq_len, d))
 
+    def _fused_weights_static(self) -> tuple[Tensor, Tensor]:
+        """``fused_weights()``, kept between calls while no gradient is recorded and no weight changed
+        (decode reuses it every step)."""
+        if torch.is_grad_enabled():
+            return self.fused_weights()
+        parts = (self.W_Q.weight, self.W_K.weight, self.W_V.weight, self.W_B.weight, self.W_C.weight,
+                 self.theta_proj.weight, self.alpha_proj.weight, self.alpha_proj.bias)
+        key = tuple((t.data_ptr(), t._version, t.dtype) for t in parts)
+        hit = getattr(self, "_wcat_static", None)
+        if hit is None or hit[0] != key:
+            hit = (key, self.fused_weights())
+            self._wcat_static = hit
+        return hit[1]
+
+    def _decode_fused(self, x: Tensor, state) -> Tensor:
+        """One decode step on the CUDA path: one projection GEMM, one kernel for the recurrences, the
+        rotation and the cache append (kernels/decode.py ``decode_prep``), then the decode attention."""
+        from .kernels.decode import decode_attention, decode_prep
+
+        weight, bias = self._fused_weights_static()
+        proj = F.linear(x, weight, bias)
+        q, c, g, fgate = decode_prep(proj, self._forget_logits(x), state, self.config.n_head)
+        return self._output(decode_attention(q, c, g, fgate, state, self.lam()))
+
+    def _use_fused_decode(self, x: Tensor, state, requested: str) -> bool:
+        """One new token on the CUDA path without autograd, into a cache of the compute dtype."""
+        return (state is not None and x.shape[1] == 1 and x.is_cuda and not torch.is_grad_enabled()
+                and _resolve_impl(requested, x, self.config) == "cuda" and _compute_dtype(x) == state.k_buf.dtype)
+
     def _forward_cached(self, x: Tensor, cache: "SISACache", requested: str) -> Tensor:
         state = cache.get(self.layer_idx)
+        if self._use_fused_decode(x, state, requested):
+            return self._decode_fused(x, state)
         q, k, v, c, b, g, fgate, phi = self._prepare(x, state)
         if state is None:
             impl = _resolve_impl(requested, x, self.config)

@@ -75,3 +75,39 @@ def test_generate_cuda_runs_and_is_deterministic(cuda_dev):
     a = model.generate(ids, max_new_tokens=12)
     b = model.generate(ids, max_new_tokens=12)
     assert a.shape == (4, 77) and torch.equal(a, b)
+
+
+def test_fused_decode_step_matches_unfused_glue(cuda_dev, monkeypatch):
+    """The fused decode step (one projection GEMM + sisa_decode_prep) against the unfused glue of the same
+    step (separate projections, torch recurrences and rotation, cache append), logits and caches; the
+    cache starts with one free slot, so the fused step also grows it."""
+    from sisa_b200 import modeling
+    from sisa_b200.generation import SISACache
+
+    model = _tiny(cuda_dev, "cuda").to(cuda_dev).to(torch.bfloat16)
+    ids = torch.randint(0, 97, (3, 40), generator=torch.Generator().manual_seed(3)).to(cuda_dev)
+
+    def run(fused):
+        if not fused:
+            monkeypatch.setattr(modeling.SISAAttention, "_use_fused_decode", lambda self, x, state, requested: False)
+        cache = SISACache(capacity=34)
+        out = []
+        with torch.no_grad():
+            out.append(model(ids[:, :33], cache=cache, logits_to_keep=1).logits[:, -1].float())
+            for t in range(33, 40):
+                out.append(model(ids[:, t:t + 1], cache=cache, logits_to_keep=1).logits[:, -1].float())
+        monkeypatch.undo()
+        return out, cache
+
+    got, cg = run(True)
+    want, cw = run(False)
+    for a, b in zip(got, want):
+        assert max_abs(a.cpu(), b.cpu()) <= 2e-2
+    for i in range(2):
+        sg, sw = cg.get(i), cw.get(i)
+        assert sg.length == sw.length == 40
+        for name in ("k", "v", "b"):
+            assert max_abs(getattr(sg, name).float().cpu(), getattr(sw, name).float().cpu()) <= 2e-2, name
+        for name in ("g", "fgate"):
+            assert max_abs(getattr(sg, name).cpu(), getattr(sw, name).cpu()) <= 1e-3, name
+        assert max_abs(sg.phi.reshape(sw.phi.shape).cpu(), sw.phi.float().cpu()) <= 1e-3
