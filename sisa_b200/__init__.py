@@ -17,13 +17,14 @@ from .config import PRESETS, SISAConfig
 __version__ = "0.1.0"
 
 __all__ = ["SISAConfig", "PRESETS", "SISAAttention", "SISABlock", "SISAModel", "SISAForCausalLM", "SISAOutput",
-           "sisa_attention", "set_check_mode", "__version__"]
+           "sisa_attention", "load_paper_checkpoint", "convert_state_dict", "set_check_mode", "__version__"]
 
 _LAZY_ATTRS = {
     "SISAAttention": "modeling", "SISABlock": "modeling", "SISAModel": "modeling",
     "SISAForCausalLM": "modeling", "SISAOutput": "modeling", "sisa_attention": "functional",
+    "load_paper_checkpoint": "checkpoint", "convert_state_dict": "checkpoint",
 }
-_LAZY_SUBMODULES = ("backends", "kernels", "generation", "functional", "modeling")
+_LAZY_SUBMODULES = ("backends", "kernels", "generation", "functional", "modeling", "checkpoint")
 
 
 def set_check_mode(mode: str) -> None:

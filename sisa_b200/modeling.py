@@ -471,3 +471,17 @@ class SISAForCausalLM(SISAModel):
 
         return generate(self, input_ids, max_new_tokens, temperature=temperature, top_k=top_k,
                         eos_token_id=eos_token_id, do_sample=do_sample, **kwargs)
+
+    def save_pretrained(self, path: str, *, safe_serialization: bool = True) -> None:
+        """Write ``config.json`` and the weights to directory ``path`` (modeling.py:484-488)."""
+        from .checkpoint import save_pretrained
+
+        save_pretrained(self, path, safe_serialization=safe_serialization)
+
+    @classmethod
+    def from_pretrained(cls, path: str, *, dtype: torch.dtype | None = None,
+                        **config_overrides: Any) -> "SISAForCausalLM":
+        """Load a directory written by :meth:`save_pretrained` here or in the reference."""
+        from .checkpoint import from_pretrained
+
+        return from_pretrained(path, dtype=dtype, **config_overrides)

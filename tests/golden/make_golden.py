@@ -13,6 +13,8 @@ Cases (all seeded):
   model_case.pt  tiny SISAForCausalLM (torch backend, fp64): state dict, loss, logits, a few grads,
                  greedy generate() tokens and the cached-decode logits
   known.pt       preset parameter counts, fused layouts for H = 8, 12, 16
+  ckpt_case.pt   a tiny model saved by the reference's save_pretrained (safetensors and .bin bytes), its
+                 logits, and its convert_state_dict of paper-layout and wrapper-prefixed keys
 """
 from __future__ import annotations
 
@@ -152,14 +154,71 @@ def known(ref):
                     vocab_size=97, d_model=128, n_layer=2, n_head=2, d_ff=96)).state_dict().keys()))
 
 
+def paper_layout(state_dict, prefix=""):
+    """A state dict renamed to the paper training code's layout: attention parameters directly under
+    ``layers.{i}``, norms and SwiGLU as compiled submodules (``._orig_mod.``), an optional wrapper prefix."""
+    out = {}
+    for key, value in state_dict.items():
+        parts = key.split(".")
+        if len(parts) > 3 and parts[0] == "layers" and parts[2] == "attn":
+            del parts[2]
+        elif len(parts) > 3 and parts[0] == "layers" and parts[2] in ("attn_norm", "ffn_norm", "ffn"):
+            parts.insert(3, "_orig_mod")
+        elif parts[0] == "final_norm":
+            parts.insert(1, "_orig_mod")
+        out[prefix + ".".join(parts)] = value
+    return out
+
+
+def ckpt_case(ref):
+    """Files written by the reference's save_pretrained (both formats), its logits, and its key
+    conversion of paper-layout and wrapper-prefixed keys."""
+    import tempfile
+
+    cfg = ref.SISAConfig(vocab_size=61, d_model=32, n_layer=2, n_head=2, d_ff=40, d_state=8, attn_impl="torch")
+    torch.manual_seed(21)
+    model = ref.SISAForCausalLM(cfg)
+    gen = torch.Generator().manual_seed(22)
+    with torch.no_grad():
+        for layer in model.layers:
+            layer.attn.W_C.weight.copy_(torch.randn(layer.attn.W_C.weight.shape, generator=gen) * 0.1)
+    model.eval()
+    ids = torch.randint(0, 61, (2, 24), generator=gen)
+    with torch.no_grad():
+        logits = model(ids).logits
+    files = {}
+    for safe, name in ((True, "model.safetensors"), (False, "pytorch_model.bin")):
+        with tempfile.TemporaryDirectory() as tmp:
+            model.save_pretrained(tmp, safe_serialization=safe)
+            files[name] = (Path(tmp) / name).read_bytes()
+            files["config.json"] = (Path(tmp) / "config.json").read_bytes()
+    keys = list(model.state_dict().keys())
+    odd = ["module.layers.0.W_Q.weight", "_orig_mod.module.layers.1.lambda_raw", "module._orig_mod.embed.weight",
+           "layers.3.ffn._orig_mod.w_up.weight", "layers.10.W_Obias", "layers.2.alpha_proj", "layers.x.W_Q.weight",
+           "module", "_orig_mod.", "final_norm._orig_mod.weight", "layers.0.attn.W_B.weight", "layers.0.W_Z.weight"]
+    key_map = {}
+    for prefix in ("", "module.", "_orig_mod.", "module._orig_mod."):
+        src = [prefix + k for k in paper_layout(dict.fromkeys(keys, torch.zeros(1)))]
+        conv = ref.convert_state_dict(dict.fromkeys(src, torch.zeros(1)))
+        key_map.update(zip(src, conv))
+    for k in odd:
+        key_map[k] = next(iter(ref.convert_state_dict({k: torch.zeros(1)})))
+    inferred = ref.checkpoint.infer_config_from_state_dict(paper_layout(model.state_dict(), "module."))
+    return dict(files=files, ids=ids, logits=logits, key_map=key_map, inferred=inferred.to_dict(),
+                state_dict_keys=keys)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of the reference checkout (read-only)")
+    ap.add_argument("--only", nargs="*", help="write only these cases")
     args = ap.parse_args(argv)
     ref = import_reference(Path(args.ref))
     torch.set_num_threads(4)
     for name, fn in (("attn_case", attn_case), ("prep_case", prep_case), ("lce_case", lce_case),
-                     ("model_case", model_case), ("known", known)):
+                     ("model_case", model_case), ("known", known), ("ckpt_case", ckpt_case)):
+        if args.only and name not in args.only:
+            continue
         torch.save(fn(ref), HERE / f"{name}.pt")
         print("wrote", name)
 
