@@ -445,7 +445,7 @@ def run_lce(args):
     from sisa_b200.kernels.linear_ce import linear_cross_entropy
 
     dev = torch.device("cuda", 0)
-    N, D, V = 16384, 1024, 50277
+    N, D, V = args.lce_tokens, 1024, 50277
     g = torch.Generator(device=dev).manual_seed(0)
     h = torch.randn((N, D), generator=g, device=dev).to(torch.bfloat16).requires_grad_(True)
     w = (torch.randn((V, D), generator=g, device=dev) * 0.02).requires_grad_(True)
@@ -541,10 +541,12 @@ def run_decode(args):
     """cfg4: 12-layer sisa-152m, random init, bf16 weights; batch 64, prompt 8192 ids (id 0 first), greedy decode.
     Reports prefill tokens/s and per-step decode latency with the cache bytes read per step."""
     import sisa_b200 as sisa
-    from sisa_b200.generation import SISACache
+    from sisa_b200.generation import DecodeGraph, SISACache
 
     dev = torch.device("cuda", 0)
     Bd, P, S = args.decode_batch, args.decode_prompt, args.decode_steps
+    if S < 10:
+        raise ValueError("--decode-steps must be >= 10 (1 + 4 eager, 2 warm-up graph steps, then timed steps)")
     cfg = sisa.SISAConfig.preset("sisa-152m", attn_impl="cuda")
     torch.manual_seed(0)
     model = sisa.SISAForCausalLM(cfg).to(dev).to(torch.bfloat16).eval()
@@ -562,26 +564,44 @@ def run_decode(args):
         torch.cuda.synchronize()
         prefill_ms = s_.elapsed_time(e_)
         nxt = logits.float().argmax(-1)
-        for _ in range(3):      # warm-up decode steps
+        # eager steps (every kernel dispatched from Python), the first on the graph's capture stream
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
             logits = model(nxt.unsqueeze(1), cache=cache, logits_to_keep=1).logits[:, -1]
             nxt = logits.float().argmax(-1)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        n_eager = 4
+        s_.record()
+        for _ in range(n_eager):
+            logits = model(nxt.unsqueeze(1), cache=cache, logits_to_keep=1).logits[:, -1]
+            nxt = logits.float().argmax(-1)
+        e_.record()
         torch.cuda.synchronize()
-        n = S - 3
+        eager_ms = s_.elapsed_time(e_) / n_eager
+        # the same step captured once as a CUDA graph (generate's default) and replayed per token
+        graph = DecodeGraph(model, cache, Bd, stream=side)
+        for _ in range(2):
+            nxt = graph.step(nxt).float().argmax(-1)
+        torch.cuda.synchronize()
+        n = S - 3 - n_eager
         with Clocks(0) as clk:
             s_.record()
             for _ in range(n):
-                logits = model(nxt.unsqueeze(1), cache=cache, logits_to_keep=1).logits[:, -1]
-                nxt = logits.float().argmax(-1)
+                nxt = graph.step(nxt).float().argmax(-1)
             e_.record()
             torch.cuda.synchronize()
         step_ms = s_.elapsed_time(e_) / n
-    L_avg = P + 3 + n / 2
+        graph.close()
+    L_avg = P + 3 + n_eager + n / 2
     per_tok = cfg.n_layer * cfg.n_head * (64 * 2 * 2 + 32 * 2 + 8)   # k, v, b~ (bf16) + g, F (fp32)
     cache_bytes = Bd * L_avg * per_tok
     weight_bytes = 2 * (cfg.num_parameters())
     print(json.dumps({"metric": "decode step latency (cfg4)", "value": round(step_ms, 3), "unit": "ms/step",
                       "prefill_tokens_s": round(Bd * P / (prefill_ms * 1e-3), 1), "prefill_ms": round(prefill_ms, 1),
-                      "decode_steps_timed": n, "cache_bytes_per_step": int(cache_bytes),
+                      "decode_steps_timed": n, "eager_ms_per_step": round(eager_ms, 3),
+                      "timing": "CUDA graph replay of the whole decode step (DecodeGraph)",
+                      "cache_bytes_per_step": int(cache_bytes),
                       "hbm_gbs": round((cache_bytes + weight_bytes) / (step_ms * 1e-3) / 1e9, 1),
                       "config": {"batch": Bd, "prompt": P, "new_tokens": S, "model": "sisa-152m"},
                       "clocks": clk.summary()}))
@@ -627,6 +647,7 @@ def main(argv=None):
                     help="attn (default: config 1 + the config 3 training leg), lce (config 2), decode (config 4), "
                          "norm (the fused block-boundary norms of config 3)")
     ap.add_argument("--norm-rows", type=int, default=16384)
+    ap.add_argument("--lce-tokens", type=int, default=16384, help="hidden rows of the lce workload (cfg2: 16384)")
     ap.add_argument("--decode-batch", type=int, default=64)
     ap.add_argument("--decode-prompt", type=int, default=8192)
     ap.add_argument("--decode-steps", type=int, default=256)

@@ -24,6 +24,7 @@ extern "C" {
 #define SISA_ST_NONMONOTONE 2  /* g rose by more than 1e-3 between neighbours (attention.py:123-125,675-683) */
 #define SISA_ST_TIMEOUT     4  /* a bounded device wait gave up; results are invalid */
 #define SISA_ST_BAD_SEED    8  /* linear-CE backward seed differs from the promised grad_scale (linear_ce.py:202-206) */
+#define SISA_ST_BAD_POS    16  /* a decode position read on the device lay outside the cache; nothing was written */
 
 /* ---- return codes ---- */
 #define SISA_OK              0
@@ -250,6 +251,27 @@ int sisa_decode_prep(const void* proj, int64_t proj_sb, const float* z, int64_t 
                      int dtype, const sisa_view4* k_cache, const sisa_view4* v_cache, const sisa_view4* b_cache,
                      float* g_cache, float* f_cache, int64_t gf_stride, int64_t pos, float* phi, void* c_out,
                      float* g_out, float* f_out, int32_t* status, void* stream);
+
+/* Device-position forms of sisa_decode_prep and sisa_decode_attn, for a decode step that is captured
+ * once as a CUDA graph and replayed for every new token. The reference runs the same step eagerly from
+ * its generate() loop (src/sisa/generation.py:177-189 calling modeling.py:224-238); its per-token host
+ * work is what the graph removes. The arguments are those of the host-position forms, except:
+ *   sisa_decode_prep_dpos: the position is *d_pos (int32 in device memory, read when the kernel runs);
+ *     max_pos (2 <= max_pos <= gf_stride, at most the caches' position count) bounds it: a position
+ *     outside [1, max_pos) sets SISA_ST_BAD_POS and writes nothing.
+ *   sisa_decode_attn_dpos: attends over N = *d_pos + 1 cached keys; max_n bounds N (a position outside
+ *     [1, max_n) sets SISA_ST_BAD_POS and y is zero) and sizes the split count and the workspace,
+ *     sisa_decode_workspace(B, H, max_n) bytes.
+ * The caller advances *d_pos between steps (inside the graph). */
+int sisa_decode_prep_dpos(const void* proj, int64_t proj_sb, const float* z, int64_t z_sb, int64_t B, int64_t H,
+                          int dtype, const sisa_view4* k_cache, const sisa_view4* v_cache, const sisa_view4* b_cache,
+                          float* g_cache, float* f_cache, int64_t gf_stride, const int32_t* d_pos, int64_t max_pos,
+                          float* phi, void* c_out, float* g_out, float* f_out, int32_t* status, void* stream);
+int sisa_decode_attn_dpos(const sisa_view4* q, const sisa_view4* c, const float* g_q, const float* f_q,
+                          const sisa_view4* k_cache, const sisa_view4* v_cache, const sisa_view4* b_cache,
+                          const float* g_cache, const float* f_cache, int64_t gf_stride, const float* lam,
+                          int64_t B, int64_t H, const int32_t* d_pos, int64_t max_n, int dtype, const sisa_view4* y,
+                          void* workspace, int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }

@@ -17,7 +17,7 @@ _LIB = None
 
 # return codes / status bits (sisa_b200.h)
 OK, ERR_VALUE, ERR_TYPE, ERR_ALIGN, ERR_CUDA, ERR_UNSUPPORTED = 0, 1, 2, 3, 4, 5
-ST_NONFINITE, ST_NONMONOTONE, ST_TIMEOUT, ST_BAD_SEED = 1, 2, 4, 8
+ST_NONFINITE, ST_NONMONOTONE, ST_TIMEOUT, ST_BAD_SEED, ST_BAD_POS = 1, 2, 4, 8, 16
 BF16, F16 = 0, 1
 
 
@@ -91,6 +91,10 @@ SIGNATURES = {
                                       _P, _P]),
     "sisa_decode_prep": (_I, [_P, _I64, _P, _I64, _I64, _I64, _I, _VP, _VP, _VP, _P, _P, _I64, _I64, _P, _P, _P, _P,
                               _P, _P]),
+    "sisa_decode_prep_dpos": (_I, [_P, _I64, _P, _I64, _I64, _I64, _I, _VP, _VP, _VP, _P, _P, _I64, _P, _I64, _P, _P,
+                                   _P, _P, _P, _P]),
+    "sisa_decode_attn_dpos": (_I, [_VP, _VP, _P, _P, _VP, _VP, _VP, _P, _P, _I64, _P, _I64, _I64, _P, _I64, _I, _VP,
+                                   _P, _P, _P]),
     "sisa_rmsnorm_bwd_workspace": (_I64, [_I64, _I64]),
     "sisa_rmsnorm_fwd": (_I, [_P, _I64, _I, _P, _I64, _I64, ctypes.c_float, _P, _I64, _I, _P, _P, _P]),
     "sisa_rmsnorm_bwd": (_I, [_P, _I64, _I, _P, _I64, _I, _P, _P, _I64, _I64, _P, _I64, _I, _P, _P, _P, _P]),

@@ -80,6 +80,8 @@ def _raise_for(bits: int) -> None:
         raise FloatingPointError(_GUARD_MSG)
     if bits & _lib.ST_BAD_SEED:
         raise RuntimeError("linear_cross_entropy: backward seed differs from the promised grad_scale")
+    if bits & _lib.ST_BAD_POS:
+        raise ValueError("decode: the device position lay outside the cache; the step wrote nothing")
 
 
 def check_status(device: torch.device | int | None = None) -> None:

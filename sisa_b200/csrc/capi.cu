@@ -374,11 +374,12 @@ int64_t sisa_decode_workspace(int64_t B, int64_t H, int64_t N) {
   return (int64_t)sisa::decode_splits(B, H, N) * B * H * 66 * 4;
 }
 
-int sisa_decode_attn(const sisa_view4* q, const sisa_view4* c, const float* g_q, const float* f_q,
-                     const sisa_view4* k_cache, const sisa_view4* v_cache, const sisa_view4* b_cache,
-                     const float* g_cache, const float* f_cache, int64_t gf_stride, const float* lam, int64_t B,
-                     int64_t H, int64_t N, int dtype, const sisa_view4* y, void* workspace, int32_t* status,
-                     void* stream) {
+// Shared by sisa_decode_attn (d_pos null, N keys) and sisa_decode_attn_dpos (N = *d_pos + 1 <= max_n keys).
+static int decode_attn_impl(const sisa_view4* q, const sisa_view4* c, const float* g_q, const float* f_q,
+                            const sisa_view4* k_cache, const sisa_view4* v_cache, const sisa_view4* b_cache,
+                            const float* g_cache, const float* f_cache, int64_t gf_stride, const float* lam,
+                            int64_t B, int64_t H, int64_t N, const int32_t* d_pos, int dtype, const sisa_view4* y,
+                            void* workspace, int32_t* status, void* stream) {
   int rc;
   if ((rc = check_dims(B, H, N)) || (rc = check_dtype(dtype))) return rc;
   if ((rc = check_view(q, 2, "q")) || (rc = check_view(c, 2, "c")) || (rc = check_view(k_cache, 2, "k_cache")) ||
@@ -405,15 +406,38 @@ int sisa_decode_attn(const sisa_view4* q, const sisa_view4* c, const float* g_q,
   p.ws = static_cast<float*>(workspace);
   p.B = (int)B; p.H = (int)H; p.N = (int)N; p.splits = sisa::decode_splits(B, H, N);
   p.status = status;
+  p.d_pos = d_pos;
   cudaError_t e = sisa::launch_decode(p, dtype, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_decode_attn launch");
 }
 
-int sisa_decode_prep(const void* proj, int64_t proj_sb, const float* z, int64_t z_sb, int64_t B, int64_t H,
-                     int dtype, const sisa_view4* k_cache, const sisa_view4* v_cache, const sisa_view4* b_cache,
-                     float* g_cache, float* f_cache, int64_t gf_stride, int64_t pos, float* phi, void* c_out,
-                     float* g_out, float* f_out, int32_t* status, void* stream) {
-  (void)status;
+int sisa_decode_attn(const sisa_view4* q, const sisa_view4* c, const float* g_q, const float* f_q,
+                     const sisa_view4* k_cache, const sisa_view4* v_cache, const sisa_view4* b_cache,
+                     const float* g_cache, const float* f_cache, int64_t gf_stride, const float* lam, int64_t B,
+                     int64_t H, int64_t N, int dtype, const sisa_view4* y, void* workspace, int32_t* status,
+                     void* stream) {
+  return decode_attn_impl(q, c, g_q, f_q, k_cache, v_cache, b_cache, g_cache, f_cache, gf_stride, lam, B, H, N,
+                          nullptr, dtype, y, workspace, status, stream);
+}
+
+int sisa_decode_attn_dpos(const sisa_view4* q, const sisa_view4* c, const float* g_q, const float* f_q,
+                          const sisa_view4* k_cache, const sisa_view4* v_cache, const sisa_view4* b_cache,
+                          const float* g_cache, const float* f_cache, int64_t gf_stride, const float* lam,
+                          int64_t B, int64_t H, const int32_t* d_pos, int64_t max_n, int dtype, const sisa_view4* y,
+                          void* workspace, int32_t* status, void* stream) {
+  if (!d_pos || (reinterpret_cast<uintptr_t>(d_pos) & 3u))
+    return fail(SISA_ERR_VALUE, "sisa_decode_attn_dpos: d_pos must be a 4-byte aligned device pointer");
+  return decode_attn_impl(q, c, g_q, f_q, k_cache, v_cache, b_cache, g_cache, f_cache, gf_stride, lam, B, H, max_n,
+                          d_pos, dtype, y, workspace, status, stream);
+}
+
+// Shared by sisa_decode_prep (host position pos) and sisa_decode_prep_dpos (position *d_pos, checked on the
+// device against [1, pos), where pos then carries max_pos).
+static int decode_prep_impl(const void* proj, int64_t proj_sb, const float* z, int64_t z_sb, int64_t B, int64_t H,
+                            int dtype, const sisa_view4* k_cache, const sisa_view4* v_cache,
+                            const sisa_view4* b_cache, float* g_cache, float* f_cache, int64_t gf_stride,
+                            int64_t pos, const int32_t* d_pos, float* phi, void* c_out, float* g_out, float* f_out,
+                            int32_t* status, void* stream) {
   int rc;
   if ((rc = check_dims(B, H, pos + 1)) || (rc = check_dtype(dtype))) return rc;
   if ((rc = check_view(k_cache, 2, "k_cache")) || (rc = check_view(v_cache, 2, "v_cache")) ||
@@ -422,7 +446,10 @@ int sisa_decode_prep(const void* proj, int64_t proj_sb, const float* z, int64_t 
   if (!proj || !g_cache || !phi || !c_out || !g_out) return fail(SISA_ERR_VALUE, "sisa_decode_prep: null pointer");
   if ((z == nullptr) != (f_cache == nullptr) || (z == nullptr) != (f_out == nullptr))
     return fail(SISA_ERR_VALUE, "sisa_decode_prep: z, f_cache and f_out must all be given or all be null");
-  if (pos < 1 || pos >= gf_stride)
+  if (d_pos && (pos < 2 || pos > gf_stride))
+    return fail(SISA_ERR_VALUE, "sisa_decode_prep_dpos: max_pos %lld outside [2, %lld]", (long long)pos,
+                (long long)gf_stride);
+  if (!d_pos && (pos < 1 || pos >= gf_stride))
     return fail(SISA_ERR_VALUE, "sisa_decode_prep: position %lld outside [1, %lld)", (long long)pos, (long long)gf_stride);
   int64_t off[9];
   if ((rc = sisa_fused_layout(H, off))) return rc;
@@ -445,9 +472,29 @@ int sisa_decode_prep(const void* proj, int64_t proj_sb, const float* z, int64_t 
   p.b_sl = b_cache->stride_l;
   p.g = g_cache; p.f = f_cache; p.gf_stride = gf_stride; p.phi = phi;
   p.c_out = static_cast<uint16_t*>(c_out); p.g_out = g_out; p.f_out = f_out;
-  p.B = (int)B; p.H = (int)H; p.pos = pos;
+  p.B = (int)B; p.H = (int)H;
+  p.pos = d_pos ? 0 : pos;
+  p.d_pos = d_pos; p.max_pos = d_pos ? pos : 0; p.status = status;
   cudaError_t e = sisa::launch_decode_prep(p, dtype, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_decode_prep launch");
+}
+
+int sisa_decode_prep(const void* proj, int64_t proj_sb, const float* z, int64_t z_sb, int64_t B, int64_t H,
+                     int dtype, const sisa_view4* k_cache, const sisa_view4* v_cache, const sisa_view4* b_cache,
+                     float* g_cache, float* f_cache, int64_t gf_stride, int64_t pos, float* phi, void* c_out,
+                     float* g_out, float* f_out, int32_t* status, void* stream) {
+  return decode_prep_impl(proj, proj_sb, z, z_sb, B, H, dtype, k_cache, v_cache, b_cache, g_cache, f_cache, gf_stride,
+                          pos, nullptr, phi, c_out, g_out, f_out, status, stream);
+}
+
+int sisa_decode_prep_dpos(const void* proj, int64_t proj_sb, const float* z, int64_t z_sb, int64_t B, int64_t H,
+                          int dtype, const sisa_view4* k_cache, const sisa_view4* v_cache, const sisa_view4* b_cache,
+                          float* g_cache, float* f_cache, int64_t gf_stride, const int32_t* d_pos, int64_t max_pos,
+                          float* phi, void* c_out, float* g_out, float* f_out, int32_t* status, void* stream) {
+  if (!d_pos || (reinterpret_cast<uintptr_t>(d_pos) & 3u))
+    return fail(SISA_ERR_VALUE, "sisa_decode_prep_dpos: d_pos must be a 4-byte aligned device pointer");
+  return decode_prep_impl(proj, proj_sb, z, z_sb, B, H, dtype, k_cache, v_cache, b_cache, g_cache, f_cache, gf_stride,
+                          max_pos, d_pos, phi, c_out, g_out, f_out, status, stream);
 }
 
 int64_t sisa_lce_workspace(int64_t R, int64_t Vp) {

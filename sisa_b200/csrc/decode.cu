@@ -42,14 +42,27 @@ __device__ __forceinline__ void load_row(const char* p, int n16, float* out) {
   }
 }
 
+// One group of four keys as the warp's lanes load it (eight lanes per key, 16 bytes of k, v and b~ each).
+struct KeyGroup {
+  uint4 k, v, b;
+  float g, f;
+};
+
 template <bool kHalf>
 __global__ void __launch_bounds__(NT, 4) decode_split_kernel(DecodeParams p) {
   const int split = blockIdx.x, bh = blockIdx.y;
   const int b = bh / p.H, h = bh % p.H;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int per = (p.N + p.splits - 1) / p.splits;
+  // key count: the host's N, or the device position + 1 (a position outside [0, N) attends to nothing)
+  int N = p.N;
+  if (p.d_pos) {
+    const int pos = *p.d_pos;
+    N = (pos >= 1 && pos < p.N) ? pos + 1 : 0;
+    if (N == 0 && split == 0 && tid == 0 && p.status) atomicOr(p.status, SISA_ST_BAD_POS);
+  }
+  const int per = (N + p.splits - 1) / p.splits;
   const int j_begin = split * per;
-  const int j_end = min(p.N, j_begin + per);
+  const int j_end = min(N, j_begin + per);
 
   __shared__ float s_m[NW], s_l[NW];
   __shared__ float s_acc[NW][64];
@@ -81,25 +94,35 @@ __global__ void __launch_bounds__(NT, 4) decode_split_kernel(DecodeParams p) {
   const char* bbase = p.bm + 2 * ((int64_t)b * p.b_sb + (int64_t)h * p.b_sh);
   const float* gbase = p.g + (int64_t)bh * p.gf_stride;
   const float* fbase = p.f ? p.f + (int64_t)bh * p.gf_stride : nullptr;
+  // this lane's slices of key j (j clamped into the split so that every load stays in bounds)
+  auto load_group = [&](int j0, KeyGroup& d) {
+    const int j = j0 + sub;
+    const int jj = j < j_end ? j : j_begin;
+    d.k = __ldg(reinterpret_cast<const uint4*>(kbase + 2 * (int64_t)jj * p.k_sl) + part);
+    d.v = __ldg(reinterpret_cast<const uint4*>(vbase + 2 * (int64_t)jj * p.v_sl) + part);
+    d.b = make_uint4(0, 0, 0, 0);
+    if (part < 4) d.b = __ldg(reinterpret_cast<const uint4*>(bbase + 2 * (int64_t)jj * p.b_sl) + part);
+    d.g = __ldg(gbase + jj);
+    d.f = fbase ? __ldg(fbase + jj) : 0.f;
+  };
 
   float m_ref = -INFINITY;        // this warp's reference maximum (log2 units)
   float acc[8];                   // this lane's 8 head dims of the warp's sum of p v (its key sub-group)
 #pragma unroll
   for (int d = 0; d < 8; ++d) acc[d] = 0.f;
   float lsum = 0.f;               // sum of p over this lane's sub-group keys
-  // warp w takes the groups of four keys w, w + 8, w + 16, ... of the split
-#pragma unroll 2
-  for (int j0 = j_begin + 4 * warp; j0 < j_end; j0 += 4 * NW) {
-    const int j = j0 + sub;
-    const bool ok = j < j_end;
-    const int jj = ok ? j : j_begin;
-    const uint4 kv = __ldg(reinterpret_cast<const uint4*>(kbase + 2 * (int64_t)jj * p.k_sl) + part);
-    const uint4 vv = __ldg(reinterpret_cast<const uint4*>(vbase + 2 * (int64_t)jj * p.v_sl) + part);
-    uint4 bv = make_uint4(0, 0, 0, 0);
-    if (part < 4) bv = __ldg(reinterpret_cast<const uint4*>(bbase + 2 * (int64_t)jj * p.b_sl) + part);
-    const float gj = __ldg(gbase + jj);
-    const float fj = fbase ? __ldg(fbase + jj) : 0.f;
-    const uint32_t kw[4] = {kv.x, kv.y, kv.z, kv.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+  // Warp w takes the groups of four keys w, w + 8, w + 16, ... of the split. The next group's loads are
+  // issued before the current group is processed, so two groups are in flight per warp whatever the
+  // compiler does around the data-dependent rescale branch.
+  int j0 = j_begin + 4 * warp;
+  KeyGroup cur{};
+  if (j0 < j_end) load_group(j0, cur);
+#pragma unroll 1
+  for (; j0 < j_end; j0 += 4 * NW) {
+    KeyGroup nxt = cur;
+    if (j0 + 4 * NW < j_end) load_group(j0 + 4 * NW, nxt);
+    const bool ok = j0 + sub < j_end;
+    const uint32_t kw[4] = {cur.k.x, cur.k.y, cur.k.z, cur.k.w}, bw[4] = {cur.b.x, cur.b.y, cur.b.z, cur.b.w};
     float qk = 0.f, cb = 0.f;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -108,12 +131,12 @@ __global__ void __launch_bounds__(NT, 4) decode_split_kernel(DecodeParams p) {
       cb = fmaf(c8[2 * e], unpack_lo<kHalf>(bw[e]), cb);
       cb = fmaf(c8[2 * e + 1], unpack_hi<kHalf>(bw[e]), cb);
     }
-    const float dec = exp2f(fminf((gq - gj) * kLog2e, 0.f));
+    const float dec = exp2f(fminf((gq - cur.g) * kLog2e, 0.f));
     float x = fmaf(qk, c1, lam2 * (dec * cb));
     x += __shfl_xor_sync(0xffffffffu, x, 1);
     x += __shfl_xor_sync(0xffffffffu, x, 2);
     x += __shfl_xor_sync(0xffffffffu, x, 4);
-    x = ok ? fmaf(fq - fj, kLog2e, x) : -INFINITY;
+    x = ok ? fmaf(fq - cur.f, kLog2e, x) : -INFINITY;
     // step maximum over the four keys; rescale only when it exceeds the reference by more than 2^8
     float mx = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, 8));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
@@ -125,13 +148,14 @@ __global__ void __launch_bounds__(NT, 4) decode_split_kernel(DecodeParams p) {
       m_ref = mx;
     }
     const float pj = ok ? exp2f(x - m_ref) : 0.f;
-    const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
+    const uint32_t vw[4] = {cur.v.x, cur.v.y, cur.v.z, cur.v.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       acc[2 * e] = fmaf(pj, unpack_lo<kHalf>(vw[e]), acc[2 * e]);
       acc[2 * e + 1] = fmaf(pj, unpack_hi<kHalf>(vw[e]), acc[2 * e + 1]);
     }
     lsum += pj;
+    cur = nxt;
   }
   // ---- the warp's sums over its four key sub-groups (all lanes of a sub-group hold the same lsum)
 #pragma unroll
@@ -173,7 +197,10 @@ __global__ void __launch_bounds__(NT, 4) decode_split_kernel(DecodeParams p) {
   }
 }
 
-// One warp per (batch, head): merge the splits, normalise, write y in the low-precision dtype.
+// One warp per (batch, head): merge the splits, normalise, write y in the low-precision dtype. The
+// splits' (m, l) records are read by the lanes in parallel (lane s takes splits s, s + 32, ...) and
+// reduced across the warp; then each lane owns two head dims and walks the splits with independent
+// 8-byte loads, the split weights arriving by shuffle from the lane that computed them.
 template <bool kHalf>
 __global__ void __launch_bounds__(256) decode_combine_kernel(DecodeParams p) {
   const int bh = blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -181,16 +208,33 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(DecodeParams p) {
   const int lane = threadIdx.x & 31;
   const int b = bh / p.H, h = bh % p.H;
   const int64_t stride = (int64_t)p.B * p.H * 66;
+  const float* rec = p.ws + (int64_t)bh * 66;
   float m = -INFINITY;
-  for (int s = 0; s < p.splits; ++s) m = fmaxf(m, p.ws[s * stride + (int64_t)bh * 66]);
-  float l = 0.f, a0 = 0.f, a1 = 0.f;
-  for (int s = 0; s < p.splits; ++s) {
-    const float* part = p.ws + s * stride + (int64_t)bh * 66;
-    const float ms = part[0];
-    const float w = (ms == -INFINITY) ? 0.f : exp2f(ms - m);
-    l = fmaf(part[1], w, l);
-    a0 = fmaf(part[2 + 2 * lane], w, a0);
-    a1 = fmaf(part[3 + 2 * lane], w, a1);
+  for (int s = lane; s < p.splits; s += 32) m = fmaxf(m, rec[s * stride]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float l = 0.f;
+  for (int s = lane; s < p.splits; s += 32) {
+    const float ms = rec[s * stride];
+    l = fmaf(rec[s * stride + 1], (ms == -INFINITY) ? 0.f : exp2f(ms - m), l);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+  float a0 = 0.f, a1 = 0.f;
+  for (int s0 = 0; s0 < p.splits; s0 += 32) {
+    float wl = 0.f;
+    if (s0 + lane < p.splits) {
+      const float ms = rec[(s0 + lane) * stride];
+      wl = (ms == -INFINITY) ? 0.f : exp2f(ms - m);
+    }
+    const int cnt = min(32, p.splits - s0);
+#pragma unroll 4
+    for (int i = 0; i < cnt; ++i) {
+      const float w = __shfl_sync(0xffffffffu, wl, i);
+      const float2 v = *reinterpret_cast<const float2*>(rec + (s0 + i) * stride + 2 + 2 * lane);
+      a0 = fmaf(v.x, w, a0);
+      a1 = fmaf(v.y, w, a1);
+    }
   }
   const float ls = (l == 0.f) ? 1.f : l;
   uint32_t* y = reinterpret_cast<uint32_t*>(p.y + 2 * ((int64_t)b * p.y_sb + (int64_t)h * p.y_sh));
@@ -222,6 +266,14 @@ template <bool kHalf>
 __global__ void __launch_bounds__(256) decode_prep_kernel(DecodePrepParams p) {
   const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (w >= p.B * p.H) return;
+  int64_t pos = p.pos;
+  if (p.d_pos) {                  // position read on the device: out of range writes nothing
+    pos = *p.d_pos;
+    if (pos < 1 || pos >= p.max_pos) {
+      if (w == 0 && lane == 0 && p.status) atomicOr(p.status, SISA_ST_BAD_POS);
+      return;
+    }
+  }
   const int b = w / p.H, h = w - b * p.H;
   const uint16_t* row = p.proj + (int64_t)b * p.proj_sb;
   auto to_f = [](uint16_t x) {
@@ -236,8 +288,8 @@ __global__ void __launch_bounds__(256) decode_prep_kernel(DecodePrepParams p) {
   {
     const uint32_t kk = reinterpret_cast<const uint32_t*>(row + p.col_k + h * 64)[lane];
     const uint32_t vv = reinterpret_cast<const uint32_t*>(row + p.col_v + h * 64)[lane];
-    reinterpret_cast<uint32_t*>(p.k + (int64_t)b * p.k_sb + (int64_t)h * p.k_sh + p.pos * p.k_sl)[lane] = kk;
-    reinterpret_cast<uint32_t*>(p.v + (int64_t)b * p.v_sb + (int64_t)h * p.v_sh + p.pos * p.v_sl)[lane] = vv;
+    reinterpret_cast<uint32_t*>(p.k + (int64_t)b * p.k_sb + (int64_t)h * p.k_sh + pos * p.k_sl)[lane] = kk;
+    reinterpret_cast<uint32_t*>(p.v + (int64_t)b * p.v_sb + (int64_t)h * p.v_sh + pos * p.v_sl)[lane] = vv;
   }
   const int64_t bh = (int64_t)b * p.H + h;
   if (lane < 16) {
@@ -253,14 +305,14 @@ __global__ void __launch_bounds__(256) decode_prep_kernel(DecodePrepParams p) {
     const uint32_t br = (uint32_t)to_lp(__fsub_rn(__fmul_rn(be, cs), __fmul_rn(bo, sn))) |
                         ((uint32_t)to_lp(__fadd_rn(__fmul_rn(be, sn), __fmul_rn(bo, cs))) << 16);
     reinterpret_cast<uint32_t*>(p.c_out + bh * 32)[lane] = cr;
-    reinterpret_cast<uint32_t*>(p.bm + (int64_t)b * p.b_sb + (int64_t)h * p.b_sh + p.pos * p.b_sl)[lane] = br;
+    reinterpret_cast<uint32_t*>(p.bm + (int64_t)b * p.b_sb + (int64_t)h * p.b_sh + pos * p.b_sl)[lane] = br;
   } else if (lane == 16) {
-    const float gq = neg_softplus(to_f(row[p.col_a + h])) + p.g[bh * p.gf_stride + p.pos - 1];
-    p.g[bh * p.gf_stride + p.pos] = gq;
+    const float gq = neg_softplus(to_f(row[p.col_a + h])) + p.g[bh * p.gf_stride + pos - 1];
+    p.g[bh * p.gf_stride + pos] = gq;
     p.g_out[bh] = gq;
   } else if (lane == 17 && p.f) {
-    const float fq = logsigmoid(p.z[(int64_t)b * p.z_sb + h]) + p.f[bh * p.gf_stride + p.pos - 1];
-    p.f[bh * p.gf_stride + p.pos] = fq;
+    const float fq = logsigmoid(p.z[(int64_t)b * p.z_sb + h]) + p.f[bh * p.gf_stride + pos - 1];
+    p.f[bh * p.gf_stride + pos] = fq;
     p.f_out[bh] = fq;
   }
 }

@@ -19,8 +19,9 @@ struct DecodeParams {
   const float* lam;
   char* y; int64_t y_sb, y_sh;             // (B, H, 1, 64) low precision
   float* ws;                               // (splits, B*H, 66) fp32
-  int B, H, N, splits;
+  int B, H, N, splits;                     // with d_pos: N is the largest key count the caches hold
   int32_t* status;
+  const int32_t* d_pos;                    // null, or the new position on the device: N = *d_pos + 1 keys
 };
 
 // One decode step's layer input from the fused projection row (decode_prep_kernel).
@@ -37,6 +38,9 @@ struct DecodePrepParams {
   float* g_out; float* f_out;                   // (B, H)
   int B, H;
   int64_t pos;
+  const int32_t* d_pos;                         // null, or the position on the device (replaces pos)
+  int64_t max_pos;                              // with d_pos: positions must lie in [1, max_pos)
+  int32_t* status;                              // with d_pos: SISA_ST_BAD_POS for a position out of range
 };
 
 int decode_splits(int64_t B, int64_t H, int64_t N);

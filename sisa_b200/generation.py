@@ -19,7 +19,7 @@ from torch import Tensor
 if TYPE_CHECKING:  # pragma: no cover
     from .modeling import SISAForCausalLM
 
-__all__ = ["LayerState", "SISACache", "generate"]
+__all__ = ["LayerState", "SISACache", "DecodeGraph", "generate"]
 
 _ROUND = 256
 
@@ -37,6 +37,7 @@ class LayerState:
         self._alloc(B, H, cap, D, b.shape[-1], k.dtype, k.device)
         self.length = 0
         self.phi = phi
+        self.pos_dev: Tensor | None = None   # device position counter while a DecodeGraph drives this cache
         self.append(k, v, b, g, fgate, phi)
 
     def _alloc(self, B, H, cap, D, S, dtype, device):
@@ -139,6 +140,89 @@ class SISACache:
         return len(self._layers)
 
 
+class DecodeGraph:
+    """One decode step of ``model`` captured once as a CUDA graph and replayed for every new token.
+
+    The step is every layer's projection, recurrences, cache append, decode attention and MLP, then the
+    final norm and the LM head of the new position. The reference's ``generate`` dispatches each of its
+    kernels from Python for every token (generation.py:177-189); at decode batch sizes that host work,
+    not the GPU, sets the step time. Here the kernels that depend on the position read it from an int32
+    counter on the device (``pos_dev``, given to every layer state), and the graph advances the counter
+    at its end, so one capture serves every position. :meth:`step` advances the host-side lengths of the
+    layer states to match.
+
+    Build it after at least one eager decode step into ``cache`` (that step creates the concatenated
+    projection weights and the libraries' per-stream state), with room in the cache for every further
+    step: the buffers must not move once captured. :meth:`close` detaches the counter from the cache.
+    """
+
+    def __init__(self, model: "SISAForCausalLM", cache: "SISACache", batch: int,
+                 stream: "torch.cuda.Stream | None" = None):
+        if not DecodeGraph.supported(model, cache):
+            raise ValueError("DecodeGraph needs a CUDA model on the cuda attention path with a filled cache, no "
+                             "autograd or autocast, and a check mode other than 'sync'")
+        first = next(model.parameters())
+        dev = first.device
+        self.cache = cache
+        self.states = [cache.get(i) for i in range(len(model.layers))]
+        self.stream = stream if stream is not None else torch.cuda.Stream(dev)   # capture (and replay) stream
+        self.ids = torch.zeros((batch, 1), dtype=torch.long, device=dev)
+        self.pos_dev = torch.full((1,), cache.seq_len, dtype=torch.int32, device=dev)
+        lengths = [st.length for st in self.states]
+        for st in self.states:
+            st.phi_buffer()
+            st.pos_dev = self.pos_dev
+        self.graph = torch.cuda.CUDAGraph()
+        self.stream.wait_stream(torch.cuda.current_stream(dev))
+        try:
+            with torch.cuda.graph(self.graph, stream=self.stream):
+                self.logits = model(self.ids, cache=cache, logits_to_keep=1).logits[:, -1]
+                self.pos_dev.add_(1)
+        except BaseException:
+            self.close()
+            raise
+        finally:
+            for st, n in zip(self.states, lengths):   # capture ran the host code once but no kernel
+                st.length = n
+
+    @staticmethod
+    def supported(model: "SISAForCausalLM", cache: "SISACache") -> bool:
+        from . import backends
+        from .modeling import _resolve_impl
+
+        first = next(model.parameters(), None)
+        if first is None or not first.is_cuda or torch.is_grad_enabled() or torch.is_autocast_enabled("cuda"):
+            return False
+        if backends.get_check_mode() == "sync" or len(cache) != len(model.layers) or cache.seq_len < 1:
+            return False
+        dt = model.embed.weight.dtype
+        if dt not in (torch.bfloat16, torch.float16):
+            return False
+        probe = torch.empty((1, 1, model.config.d_model), dtype=dt, device=first.device)
+        return _resolve_impl(model.config.attn_impl, probe, model.config) == "cuda" and all(
+            cache.get(i) is not None and cache.get(i).k_buf.dtype == dt for i in range(len(model.layers)))
+
+    def room(self) -> int:
+        """Steps left before the cache is full."""
+        return min(st.capacity - st.length for st in self.states)
+
+    def step(self, ids: Tensor) -> Tensor:
+        """Feed one token per row (``ids``: (B,) or (B, 1)); returns the (B, vocab) logits of the new position
+        (a buffer that the next step overwrites)."""
+        if self.room() < 1:
+            raise ValueError("DecodeGraph: the cache is full")
+        self.ids.copy_(ids.reshape(-1, 1))
+        self.graph.replay()
+        for st in self.states:
+            st.length += 1
+        return self.logits
+
+    def close(self) -> None:
+        for st in self.states:
+            if getattr(st, "pos_dev", None) is self.pos_dev:
+                st.pos_dev = None
+
+
 def _eos_ids(eos_token_id) -> list[int]:
     """Normalise ``eos_token_id`` to a list of ints (generation.py:98-122)."""
     if eos_token_id is None:
@@ -183,12 +267,14 @@ def _next_token(logits: Tensor, *, do_sample: bool, temperature: float, top_k: i
 def generate(model: "SISAForCausalLM", input_ids: Tensor, max_new_tokens: int, temperature: float = 1.0,
              top_k: int | None = None, eos_token_id: int | Iterable[int] | Tensor | None = None,
              do_sample: bool = False, *, generator: torch.Generator | None = None,
-             eos_check_every: int = 16) -> Tensor:
+             eos_check_every: int = 16, cuda_graph: bool = True) -> Tensor:
     """Generate continuations of ``input_ids`` (generation.py:139-191).
 
     Same results as the reference. The all-finished check reads the device only every
     ``eos_check_every`` steps; the tokens generated past the step where every row had finished are
-    cut off afterwards, so the returned length is the reference's.
+    cut off afterwards, so the returned length is the reference's. With ``cuda_graph`` (default) and a
+    model that :meth:`DecodeGraph.supported` accepts, the first decode step runs eagerly and the rest
+    replay it as one CUDA graph.
     """
     if max_new_tokens < 0:
         raise ValueError("max_new_tokens must be >= 0")
@@ -210,6 +296,35 @@ def generate(model: "SISAForCausalLM", input_ids: Tensor, max_new_tokens: int, t
     pieces = [input_ids]
     done = torch.zeros(input_ids.shape[0], dtype=torch.bool, device=input_ids.device)
     all_done_at = []       # device flags: every row finished after step s
+    use_graph = cuda_graph and max_new_tokens > 2 and DecodeGraph.supported(model, cache)
+    out = _decode_loop(model, input_ids, max_new_tokens, logits, cache, pieces, done, all_done_at, eos_t,
+                       do_sample, temperature, top_k, generator, eos_check_every, use_graph)
+    if all_done_at:
+        flags = torch.stack(all_done_at).cpu()
+        hit = torch.nonzero(flags).flatten()
+        if hit.numel():
+            out = out[:, :input_ids.shape[1] + int(hit[0]) + 1]
+    return out.squeeze(0) if squeeze else out
+
+
+def _decode_loop(model, input_ids, max_new_tokens, logits, cache, pieces, done, all_done_at, eos_t, do_sample,
+                 temperature, top_k, generator, eos_check_every, use_graph) -> Tensor:
+    """The token loop of :func:`generate`; with ``use_graph`` the second and later steps replay a
+    :class:`DecodeGraph` captured after the first, which runs eagerly on the graph's stream."""
+    side = torch.cuda.Stream(input_ids.device) if use_graph else None
+    graphs: list[DecodeGraph] = []
+    try:
+        _token_steps(model, input_ids, max_new_tokens, logits, cache, pieces, done, all_done_at, eos_t, do_sample,
+                     temperature, top_k, generator, eos_check_every, side, graphs)
+    finally:
+        for graph in graphs:
+            graph.close()
+    return torch.cat(pieces, dim=1)
+
+
+def _token_steps(model, input_ids, max_new_tokens, logits, cache, pieces, done, all_done_at, eos_t, do_sample,
+                 temperature, top_k, generator, eos_check_every, side, graphs) -> None:
+    graph = None
     for step in range(max_new_tokens):
         nxt = _next_token(logits, do_sample=do_sample, temperature=temperature, top_k=top_k,
                           generator=generator).to(input_ids.dtype)
@@ -222,11 +337,19 @@ def generate(model: "SISAForCausalLM", input_ids: Tensor, max_new_tokens: int, t
             break
         if eos_t is not None and (step + 1) % eos_check_every == 0 and bool(all_done_at[-1]):
             break
-        logits = model(nxt.unsqueeze(1), cache=cache, logits_to_keep=1).logits[:, -1]
-    out = torch.cat(pieces, dim=1)
-    if all_done_at:
-        flags = torch.stack(all_done_at).cpu()
-        hit = torch.nonzero(flags).flatten()
-        if hit.numel():
-            out = out[:, :input_ids.shape[1] + int(hit[0]) + 1]
-    return out.squeeze(0) if squeeze else out
+        if graph is not None:
+            logits = graph.step(nxt)
+        elif side is not None:
+            # eager step on the capture stream (libraries set up their per-stream state), then capture
+            cur = torch.cuda.current_stream(input_ids.device)
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                logits = model(nxt.unsqueeze(1), cache=cache, logits_to_keep=1).logits[:, -1]
+            cur.wait_stream(side)
+            logits.record_stream(cur)
+            if max_new_tokens - step > 2:
+                graph = DecodeGraph(model, cache, input_ids.shape[0], stream=side)
+                graphs.append(graph)
+            side = None
+        else:
+            logits = model(nxt.unsqueeze(1), cache=cache, logits_to_keep=1).logits[:, -1]

@@ -111,3 +111,94 @@ def test_fused_decode_step_matches_unfused_glue(cuda_dev, monkeypatch):
         for name in ("g", "fgate"):
             assert max_abs(getattr(sg, name).cpu(), getattr(sw, name).cpu()) <= 1e-3, name
         assert max_abs(sg.phi.reshape(sw.phi.shape).cpu(), sw.phi.float().cpu()) <= 1e-3
+
+
+def _prefilled(model, ids, n_prompt, capacity):
+    from sisa_b200.generation import SISACache
+
+    cache = SISACache(capacity=capacity)
+    with torch.no_grad():
+        logits = model(ids[:, :n_prompt], cache=cache, logits_to_keep=1).logits[:, -1]
+    return cache, logits
+
+
+def test_decode_graph_matches_eager_steps(cuda_dev):
+    """A DecodeGraph replay (device position counter, capacity-sized split-K) against eager decode steps of
+    the same model from the same prefill: logits of every step and the caches afterwards."""
+    from sisa_b200.generation import DecodeGraph
+
+    model = _tiny(cuda_dev, "cuda").to(cuda_dev).to(torch.bfloat16).eval()
+    ids = torch.randint(0, 97, (3, 60), generator=torch.Generator().manual_seed(4)).to(cuda_dev)
+    ce, _ = _prefilled(model, ids, 41, 300)
+    cg, _ = _prefilled(model, ids, 41, 300)
+    with torch.no_grad():
+        want = [model(ids[:, t:t + 1], cache=ce, logits_to_keep=1).logits[:, -1].float() for t in range(41, 60)]
+        got = [model(ids[:, 41:42], cache=cg, logits_to_keep=1).logits[:, -1].float()]
+        assert DecodeGraph.supported(model, cg)
+        graph = DecodeGraph(model, cg, 3)
+        assert all(cg.get(i).length == 42 for i in range(2))
+        for t in range(42, 60):
+            got.append(graph.step(ids[:, t]).float().clone())
+        assert int(graph.pos_dev.item()) == 60 and graph.room() == cg.get(0).capacity - 60
+        graph.close()
+    assert all(cg.get(i).pos_dev is None for i in range(2))
+    for a, b in zip(got, want):
+        assert max_abs(a.cpu(), b.cpu()) <= 2e-2
+    for i in range(2):
+        sg, se = cg.get(i), ce.get(i)
+        assert sg.length == se.length == 60
+        for name in ("k", "v", "b"):
+            assert max_abs(getattr(sg, name).float().cpu(), getattr(se, name).float().cpu()) <= 2e-2, name
+        for name in ("g", "fgate"):
+            assert max_abs(getattr(sg, name).cpu(), getattr(se, name).cpu()) <= 1e-3, name
+    # the cache stays usable eagerly after the graph is closed
+    with torch.no_grad():
+        more = model(ids[:, 59:60], cache=cg, logits_to_keep=1).logits[:, -1]
+    assert torch.isfinite(more.float()).all() and cg.get(0).length == 61
+
+
+def test_generate_graph_equals_eager(cuda_dev):
+    model = _tiny(cuda_dev, "cuda").to(cuda_dev).to(torch.bfloat16)
+    ids = torch.randint(0, 97, (4, 70), generator=torch.Generator().manual_seed(5)).to(cuda_dev)
+    a = model.generate(ids, max_new_tokens=20, cuda_graph=True)
+    b = model.generate(ids, max_new_tokens=20, cuda_graph=False)
+    assert a.shape == (4, 90) and torch.equal(a, b)
+    c = model.generate(ids, max_new_tokens=20, eos_token_id=int(a[0, 75]))   # early stop with the graph
+    assert c.shape[1] <= 90 and torch.equal(c[:, :71], a[:, :71])
+
+
+def test_device_position_out_of_range_sets_status(cuda_dev):
+    """A device position outside the cache: sisa_decode_prep_dpos writes nothing and sisa_decode_attn_dpos
+    attends to nothing; both set SISA_ST_BAD_POS in the status word (no device fault)."""
+    from sisa_b200 import _lib, backends
+    from sisa_b200.kernels.decode import decode_attention, decode_prep
+
+    model = _tiny(cuda_dev, "cuda").to(cuda_dev).to(torch.bfloat16).eval()
+    ids = torch.randint(0, 97, (2, 30), generator=torch.Generator().manual_seed(6)).to(cuda_dev)
+    cache, _ = _prefilled(model, ids, 20, 64)
+    st = cache.get(0)
+    att = model.layers[0].attn
+    x = model.layers[0].attn_norm(model.embed(ids[:, 20:21]))
+    word = backends.status_word(cuda_dev)
+    with torch.no_grad():
+        weight, bias = att._fused_weights_static()
+        proj = torch.nn.functional.linear(x, weight, bias)
+        before = [t.clone() for t in (st.k_buf, st.v_buf, st.b_buf, st.g_buf, st.f_buf, st.phi_buffer())]
+        torch.cuda.synchronize()
+        word.zero_()
+        st.pos_dev = torch.full((1,), st.capacity, dtype=torch.int32, device=cuda_dev)
+        try:
+            q, c, g, f = decode_prep(proj, att._forget_logits(x), st, 2)
+            torch.cuda.synchronize()
+            assert int(word.item()) & _lib.ST_BAD_POS
+            after = (st.k_buf, st.v_buf, st.b_buf, st.g_buf, st.f_buf, st.phi)
+            for a, b in zip(before, after):   # bitwise: the buffers' unused tails hold arbitrary bits
+                assert torch.equal(a.contiguous().view(torch.uint8), b.contiguous().view(torch.uint8))
+            word.zero_()
+            y = decode_attention(q, c, g, f, st, att.lam())
+            torch.cuda.synchronize()
+            assert int(word.item()) & _lib.ST_BAD_POS
+            assert torch.count_nonzero(y) == 0
+        finally:
+            st.pos_dev = None
+            word.zero_()
