@@ -137,10 +137,28 @@ __global__ void __launch_bounds__(256) norm_fwd_kernel(const __grid_constant__ N
   float* s_w = smem;
   float* s_pb = smem + (kCache ? d : 0);
   float* s_pw = s_pb + (NP > 0 ? pad : 0);
-  if constexpr (kCache)
-    for (int i = threadIdx.x; i < d; i += blockDim.x) s_w[i] = __ldg(p.w + i);
+  if constexpr (kCache) {
+    if ((d & 3) == 0 && (reinterpret_cast<uintptr_t>(p.w) & 15u) == 0) {
+#pragma unroll 4
+      for (int i = threadIdx.x; i < d / 4; i += blockDim.x)
+        reinterpret_cast<float4*>(s_w)[i] = __ldg(reinterpret_cast<const float4*>(p.w) + i);
+    } else {
+      for (int i = threadIdx.x; i < d; i += blockDim.x) s_w[i] = __ldg(p.w + i);
+    }
+  }
   if constexpr (NP > 0) {
-    for (int i = threadIdx.x; i < p.np * d; i += blockDim.x) s_pw[i] = __ldg(p.pw + i);
+    // The projection (np x d fp32, 36 KB at d = 768) is staged by every CTA; with few rows per launch
+    // (a decode step's 64) this copy is the kernel's critical path, so it moves as 16-byte loads issued
+    // four at a time rather than as a chain of dependent scalar loads.
+    const int n = p.np * d;
+    if ((n & 3) == 0 && ((reinterpret_cast<uintptr_t>(p.pw) | reinterpret_cast<uintptr_t>(s_pw)) & 15u) == 0) {
+      const float4* src = reinterpret_cast<const float4*>(p.pw);
+      float4* dst = reinterpret_cast<float4*>(s_pw);
+#pragma unroll 4
+      for (int i = threadIdx.x; i < n / 4; i += blockDim.x) dst[i] = __ldg(src + i);
+    } else {
+      for (int i = threadIdx.x; i < n; i += blockDim.x) s_pw[i] = __ldg(p.pw + i);
+    }
     for (int i = threadIdx.x; i < p.np; i += blockDim.x) s_pb[i] = __ldg(p.pb + i);
   }
   if constexpr (kCache || NP > 0) __syncthreads();

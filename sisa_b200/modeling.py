@@ -82,6 +82,23 @@ class SwiGLU(nn.Module):
         return self.w_down(F.silu(g) * u)
 
 
+def _static(owner: nn.Module, name: str, make, *tensors: Tensor):
+    """``make(*tensors)``, kept on ``owner`` under ``name`` while none of ``tensors`` changed (same storage,
+    version and dtype). For the decode step, which runs without autograd and would otherwise recompute
+    these weight-only values (fp32 copies, concatenations) every token; a captured decode graph reads
+    the kept tensors, which stay valid while the weights are unchanged."""
+    key = tuple((t.data_ptr(), t._version, t.dtype) for t in tensors)
+    hit = owner.__dict__.get(name)
+    if hit is None or hit[0] != key:
+        hit = (key, make(*tensors))
+        owner.__dict__[name] = hit
+    return hit[1]
+
+
+def _fp32(*tensors: Tensor) -> tuple[Tensor, ...]:
+    return tuple(t.float().contiguous() for t in tensors)
+
+
 def _compute_dtype(x: Tensor) -> torch.dtype:
     dt = x.device.type
     try:
@@ -240,15 +257,17 @@ class SISAAttention(nn.Module):
             self._wcat_static = hit
         return hit[1]
 
-    def _decode_fused(self, x: Tensor, state) -> Tensor:
+    def _decode_fused(self, x: Tensor, state, z: Tensor | None = None) -> Tensor:
         """One decode step on the CUDA path: one projection GEMM, one kernel for the recurrences, the
-        rotation and the cache append (kernels/decode.py ``decode_prep``), then the decode attention."""
+        rotation and the cache append (kernels/decode.py ``decode_prep``), then the decode attention.
+        ``z`` is the forget projection of ``x`` when the caller computed it already (the block norm does)."""
         from .kernels.decode import decode_attention, decode_prep
 
         weight, bias = self._fused_weights_static()
         proj = F.linear(x, weight, bias)
-        q, c, g, fgate = decode_prep(proj, self._forget_logits(x), state, self.config.n_head)
-        return self._output(decode_attention(q, c, g, fgate, state, self.lam()))
+        q, c, g, fgate = decode_prep(proj, self._forget_logits(x) if z is None else z, state, self.config.n_head)
+        lam = _static(self, "_lam_static", lambda t: F.softplus(t).float(), self.lambda_raw)
+        return self._output(decode_attention(q, c, g, fgate, state, lam))
 
     def _use_fused_decode(self, x: Tensor, state, requested: str) -> bool:
         """One new token on the CUDA path without autograd, into a cache of the compute dtype."""
@@ -327,6 +346,34 @@ class SISABlock(nn.Module):
         the fused CUDA layer core."""
         return _fused_kernels(x, self.config) and _resolve_impl(self.config.attn_impl, x, self.config) == "cuda"
 
+    def decode_pair_path(self, x: Tensor, cache: "SISACache") -> bool:
+        """Whether :meth:`decode_pair` serves the one-token input ``x``: the norm kernels run and the
+        attention takes the fused decode step."""
+        return (x.shape[1] == 1 and _fused_kernels(x, self.config)
+                and self.attn._use_fused_decode(x, cache.get(self.attn.layer_idx), self.config.attn_impl))
+
+    def decode_pair(self, x: Tensor, m: Tensor | None, cache: "SISACache") -> tuple[Tensor, Tensor]:
+        """One decode step of the block in :meth:`forward_pair`'s form: the previous block's residual add
+        is folded into the attention norm, which also computes the forget projection in fp32 from its
+        rounded output (the value the eager step's ``F.linear(h.float(), ...)`` reads)."""
+        from .kernels.norm import block_norm, swiglu
+
+        attn, ffn = self.attn, self.ffn
+        wa, pw, pb, wf = _static(self, "_decode_fp32", _fp32, self.attn_norm.weight, attn.forget_proj.weight,
+                                 attn.forget_proj.bias, self.ffn_norm.weight)
+        if m is None:
+            h, z = block_norm(x, wa, self.attn_norm.eps, proj=(pw, pb))
+            xs = x
+        else:
+            xs, h, z = block_norm(x, wa, self.attn_norm.eps, res=m, proj=(pw, pb))
+        a = attn._decode_fused(h, cache.get(attn.layer_idx), z)
+        xs, f_in = block_norm(xs, wf, self.ffn_norm.eps, res=a)
+        # gate and up projections as one GEMM over the concatenated weights, the activation on its halves
+        w_gu = _static(ffn, "_gate_up_static", lambda g, u: torch.cat([g, u]), ffn.w_gate.weight, ffn.w_up.weight)
+        gu = F.linear(f_in, w_gu)
+        d_ff = ffn.w_gate.weight.shape[0]
+        return xs, ffn.w_down(swiglu(gu[..., :d_ff], gu[..., d_ff:]))
+
     def forward_pair(self, x: Tensor, m: Tensor | None) -> tuple[Tensor, Tensor]:
         """The block on the fused path, with the previous block's last residual add ``x + m`` folded into
         this block's first norm. Returns ``(x + m + attn, ffn)``: the caller (the next block, or the
@@ -393,6 +440,14 @@ class SISAModel(nn.Module):
             from .kernels.norm import block_norm
 
             return block_norm(x, self.final_norm.weight, self.final_norm.eps, res=m, keep_sum=False)[0]
+        if cache is not None and len(self.layers) and all(layer.decode_pair_path(x, cache) for layer in self.layers):
+            from .kernels.norm import block_norm
+
+            m = None
+            for layer in self.layers:
+                x, m = layer.decode_pair(x, m, cache)
+            (wn,) = _static(self, "_final_fp32", _fp32, self.final_norm.weight)
+            return block_norm(x, wn, self.final_norm.eps, res=m, keep_sum=False)[0]
         for layer in self.layers:
             x = checkpoint(layer, x, use_reentrant=False) if use_ckpt else layer(x, cache=cache)
         return self.final_norm(x)
