@@ -304,7 +304,7 @@ def run_train(args, rank, world, dev):
 
     cfg = sisa.SISAConfig.preset("sisa-152m", attn_impl="cuda")
     model = dp.build_model(cfg, dev, seed=0)
-    trainer = dp.Trainer(model, cuda_graph=world == 1)
+    trainer = dp.Trainer(model, cuda_graph=True)
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     bt, tt = args.train_batch, 2048
     batches = [torch.randint(0, cfg.vocab_size, (bt, tt), device=dev, generator=g) for _ in range(4)]
@@ -332,7 +332,8 @@ def run_train(args, rank, world, dev):
             "ms_per_step": round(ms, 3), "steps": k_steps, "per_rank_batch": [bt, tt], "model": "sisa-152m",
             "params": cfg.num_parameters(), "loss_last": round(float(loss), 4),
             "mfu_vs_sustained": round(tok_s * TRAIN_FLOP_PER_TOKEN / (world * sustained * 1e12), 4),
-            "parallelism": (f"dp{world} (DDP, NCCL allreduce overlapped with backward)" if world > 1
+            "parallelism": (f"dp{world} (whole step as one CUDA graph per rank: flat fp32 gradients, one "
+                            "NCCL allreduce inside the graph)" if world > 1
                             else "dp1 (whole step as one CUDA graph)")}
 
 

@@ -3,14 +3,22 @@
 The reference has no distributed code (its README calls DDP untested); its training loop is
 examples/train_minimal.py:253-301: fp32 master weights, bf16 autocast, fused AdamW with the model's
 parameter groups (betas 0.9/0.95), gradient clipping at 1.0, chunked linear-CE loss. This module runs
-that step data-parallel: every rank holds a replica, processes its own batch, and DDP averages the
-gradients with bucketed NCCL allreduces that overlap the backward pass (buckets are views of the
-gradients, so no extra copy). The optimizer stays replicated.
+that step data-parallel: every rank holds a replica, processes its own batch, and the gradients are
+averaged across ranks; the optimizer stays replicated. Two forms:
+
+* DDP (eager): bucketed NCCL allreduces overlap the backward pass (buckets are views of the
+  gradients, so no extra copy).
+* Flat gradients (``Trainer(cuda_graph=True)`` on several GPUs, or ``flat_grads=True``): every
+  parameter's gradient is a view of one fp32 buffer, the loss is scaled by 1/world (exact for world
+  sizes that are powers of two), and one SUM allreduce of the buffer follows the backward. On CUDA the
+  whole step, allreduce included, is captured as one CUDA graph and replayed, as on one GPU; the
+  allreduce then runs after the backward instead of overlapping it.
 """
 from __future__ import annotations
 
 import datetime
 import os
+import warnings
 
 import torch
 import torch.distributed as dist
@@ -57,10 +65,11 @@ def make_optimizer(model: SISAForCausalLM, lr: float = 6e-4, weight_decay: float
 
 
 class Trainer:
-    """One optimizer step per call: forward (bf16 autocast on CUDA), loss, backward with overlapped
-    gradient allreduce, clipping, AdamW.
+    """One optimizer step per call: forward (bf16 autocast on CUDA), loss, backward, gradient allreduce,
+    clipping, AdamW.
 
-    With ``cuda_graph=True`` (one process, CUDA) the whole step (forward, backward, clipping and the
+    With ``cuda_graph=True`` (CUDA; on several GPUs with flat gradients and the allreduce inside) the
+    whole step (forward, backward, clipping and the
     optimizer) is captured once as a CUDA graph and replayed from a static input buffer, which removes
     the launch gaps of its several hundred kernels and the host's dispatch work. The first call runs
     eagerly (it also creates the optimizer state, which a capture must not allocate); the second
@@ -68,24 +77,46 @@ class Trainer:
     """
 
     def __init__(self, model: SISAForCausalLM, optimizer: torch.optim.Optimizer | None = None, *,
-                 fused_ce: bool = True, clip: float = 1.0, bucket_cap_mb: float = 64.0, cuda_graph: bool = False):
+                 fused_ce: bool = True, clip: float = 1.0, bucket_cap_mb: float = 64.0, cuda_graph: bool = False,
+                 flat_grads: bool = False):
         self.module = model
         dev = next(model.parameters()).device
         self.device = dev
         self.distributed = dist.is_initialized() and dist.get_world_size() > 1
-        if self.distributed:
+        self.world = dist.get_world_size() if self.distributed else 1
+        self.cuda_graph = cuda_graph and dev.type == "cuda"
+        self.flat = self.distributed and (self.cuda_graph or flat_grads)
+        self._grads = None
+        if self.flat:
+            self.model = model
+            self._make_flat_grads()
+        elif self.distributed:
             self.model = torch.nn.parallel.DistributedDataParallel(
                 model, device_ids=[dev.index] if dev.type == "cuda" else None, gradient_as_bucket_view=True,
                 bucket_cap_mb=bucket_cap_mb, broadcast_buffers=False)
         else:
             self.model = model
-        self.cuda_graph = cuda_graph and dev.type == "cuda" and not self.distributed
         self.opt = optimizer or make_optimizer(model, capturable=self.cuda_graph)
         self.fused_ce = fused_ce and dev.type == "cuda"
         self.clip = clip
         self._graph = None
         self._static_ids = None
         self._static_loss = None
+
+    def _make_flat_grads(self) -> None:
+        """Rank 0's parameters on every rank, and every gradient a view of one fp32 buffer (autograd
+        accumulates into existing gradients in place, so the views persist across steps)."""
+        params = [p for p in self.module.parameters() if p.requires_grad]
+        if any(p.dtype != torch.float32 for p in params):
+            raise TypeError("flat gradients need fp32 parameters (the master weights)")
+        with torch.no_grad():
+            for p in params:
+                dist.broadcast(p.data, 0)
+        self._grads = torch.zeros(sum(p.numel() for p in params), dtype=torch.float32, device=self.device)
+        off = 0
+        for p in params:
+            p.grad = self._grads[off:off + p.numel()].view_as(p)
+            off += p.numel()
 
     def step(self, ids: torch.Tensor) -> torch.Tensor:
         """Train on ``ids`` (B, T) (labels = ids, shifted inside the model). Returns the loss (device)."""
@@ -100,37 +131,64 @@ class Trainer:
             return self._eager_step(ids)
         if self._graph is None:
             self._capture()
+            if self._graph is None:                  # a rank could not capture: eager steps from here on
+                return self._eager_step(ids)
         self._static_ids.copy_(ids, non_blocking=True)
         self._graph.replay()
         return self._static_loss.clone()
 
     def _capture(self) -> None:
-        self.opt.zero_grad(set_to_none=True)         # the captured backward allocates the gradients
+        if not self.flat:
+            self.opt.zero_grad(set_to_none=True)     # the captured backward allocates the gradients
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            self._static_loss = self._forward_backward(self._static_ids)
-            if self.clip:
-                torch.nn.utils.clip_grad_norm_(self.module.parameters(), self.clip)
-            self.opt.step()
+        ok = True
+        try:
+            # thread_local with NCCL: its watchdog thread may query events while this thread captures
+            with torch.cuda.graph(graph, capture_error_mode="thread_local" if self.distributed else "global"):
+                self._static_loss = self._forward_backward(self._static_ids)
+                self._update()
+        except Exception:
+            ok = False
+            if not self.distributed:
+                raise
+        if self.distributed:
+            # every rank replays only if every rank captured (a lone replay would wait in its allreduce);
+            # otherwise all ranks continue with eager steps of the same form
+            flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=self.device)
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+            if int(flag.item()) == 0:
+                warnings.warn("Trainer: CUDA graph capture of the data-parallel step failed on a rank; "
+                              "continuing with eager steps", RuntimeWarning)
+                self.cuda_graph = False
+                self._graph = None
+                return
         self._graph = graph
 
-    def _forward_backward(self, ids: torch.Tensor) -> torch.Tensor:
-        self.model.train()
-        with torch.autocast("cuda", dtype=torch.bfloat16):
-            loss = self.model(ids, labels=ids, fused_ce=self.fused_ce).loss
-        loss.backward()
-        return loss.detach()
-
-    def _eager_step(self, ids: torch.Tensor) -> torch.Tensor:
-        self.model.train()
-        if self.device.type == "cuda":
-            with torch.autocast("cuda", dtype=torch.bfloat16):
-                loss = self.model(ids, labels=ids, fused_ce=self.fused_ce).loss
-        else:
-            loss = self.model(ids, labels=ids).loss
-        loss.backward()
+    def _update(self) -> None:
+        """Gradient allreduce (flat form), clipping and the optimizer step."""
+        if self.flat:
+            dist.all_reduce(self._grads, op=dist.ReduceOp.SUM)
         if self.clip:
             torch.nn.utils.clip_grad_norm_(self.module.parameters(), self.clip)
         self.opt.step()
-        self.opt.zero_grad(set_to_none=True)
+
+    def _loss(self, ids: torch.Tensor) -> torch.Tensor:
+        if self.device.type == "cuda":
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                return self.model(ids, labels=ids, fused_ce=self.fused_ce).loss
+        return self.model(ids, labels=ids).loss
+
+    def _forward_backward(self, ids: torch.Tensor) -> torch.Tensor:
+        self.model.train()
+        if self.flat:
+            self._grads.zero_()
+        loss = self._loss(ids)
+        (loss * (1.0 / self.world) if self.flat else loss).backward()
         return loss.detach()
+
+    def _eager_step(self, ids: torch.Tensor) -> torch.Tensor:
+        loss = self._forward_backward(ids)
+        self._update()
+        if not self.flat:
+            self.opt.zero_grad(set_to_none=True)
+        return loss

@@ -8,6 +8,7 @@ import sys
 import time
 from pathlib import Path
 
+import pytest
 import torch
 import torch.multiprocessing as mp
 
@@ -42,7 +43,8 @@ def _worker(rank, world, port, mode, q):
         _, _, dev = dp.init_distributed("gloo", timeout_s=15.0)
         model = dp.build_model(_cfg(), dev, seed=0)
         # SGD: the update is linear in the averaged gradient, so it can be compared with one process
-        trainer = dp.Trainer(model, torch.optim.SGD(model.parameters(), lr=0.5), fused_ce=False)
+        trainer = dp.Trainer(model, torch.optim.SGD(model.parameters(), lr=0.5), fused_ce=False,
+                             flat_grads=mode == "flat")
         if mode == "exit" and rank == 1:
             os._exit(3)                       # leaves between steps, no collective in flight
         t0 = time.time()
@@ -67,7 +69,7 @@ def _run(mode, world=2, timeout=120):
     for p in procs:
         p.start()
     out = {}
-    expect = world if mode == "ok" else 1
+    expect = 1 if mode == "exit" else world
     t0 = time.time()
     while len(out) < expect and time.time() - t0 < timeout:
         try:
@@ -82,8 +84,11 @@ def _run(mode, world=2, timeout=120):
     return out
 
 
-def test_dp_gloo_gradients_are_averaged_and_replicas_agree():
-    out = _run("ok")
+@pytest.mark.parametrize("mode", ["ok", "flat"])
+def test_dp_gloo_gradients_are_averaged_and_replicas_agree(mode):
+    """DDP ("ok") and the flat-gradient form ("flat": one buffer, loss scaled by 1/world, one SUM
+    allreduce; the form the multi-GPU CUDA graph captures)."""
+    out = _run(mode)
     assert set(out) == {0, 1} and all(v[1] == "ok" for v in out.values()), out
     p0 = {n: torch.from_numpy(a) for n, a in out[0][3].items()}
     p1 = {n: torch.from_numpy(a) for n, a in out[1][3].items()}
