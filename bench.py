@@ -326,6 +326,7 @@ def run_train(args, rank, world, dev):
     ms = float(ms.item()) / k_steps
     tok_s = world * bt * tt / (ms * 1e-3)
     burst, sustained, _, _ = measured_peaks()
+    trainer.close()                     # the graph holds NCCL work: release it before the group goes
     del trainer, model
     torch.cuda.empty_cache()
     return {"metric": "12L train tokens/s", "value": round(tok_s, 1), "unit": "tokens/s", "n_gpus": world,

@@ -118,6 +118,15 @@ class Trainer:
             p.grad = self._grads[off:off + p.numel()].view_as(p)
             off += p.numel()
 
+    def close(self) -> None:
+        """Release the captured step. A graph that holds NCCL work must be released before
+        ``destroy_process_group``; later calls to :meth:`step` capture again."""
+        if self._graph is not None:
+            torch.cuda.synchronize(self.device)
+            self._graph.reset()
+            self._graph = None
+            self._static_ids = None
+
     def step(self, ids: torch.Tensor) -> torch.Tensor:
         """Train on ``ids`` (B, T) (labels = ids, shifted inside the model). Returns the loss (device)."""
         if self.cuda_graph:
