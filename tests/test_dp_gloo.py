@@ -44,11 +44,17 @@ def _worker(rank, world, port, mode, q):
         model = dp.build_model(_cfg(), dev, seed=0)
         # SGD: the update is linear in the averaged gradient, so it can be compared with one process
         trainer = dp.Trainer(model, torch.optim.SGD(model.parameters(), lr=0.5), fused_ce=False,
-                             flat_grads=mode == "flat")
+                             flat_grads=mode in ("flat", "capfail"))
         if mode == "exit" and rank == 1:
             os._exit(3)                       # leaves between steps, no collective in flight
+        if mode == "capfail":
+            _fake_capture(trainer, fail=rank == 1)
         t0 = time.time()
         loss = trainer.step(_batch(rank))
+        if mode == "capfail":
+            for _ in range(2):                # eager capture attempt and replay steps; all must end eager
+                loss = trainer.step(_batch(rank))
+            assert not trainer.cuda_graph and trainer._graph is None
         # numpy copies travel by value (tensors would be shared through handles that die with this process)
         q.put((rank, "ok", float(loss), {n: p.detach().numpy().copy() for n, p in model.named_parameters()},
                time.time() - t0))
@@ -59,6 +65,38 @@ def _worker(rank, world, port, mode, q):
 
         if dist.is_initialized() and mode != "exit":
             dist.destroy_process_group()
+
+
+def _fake_capture(trainer, fail):
+    """Stand-ins for CUDA-graph capture on CPU: on the failing rank the capture raises; on the other it
+    succeeds without running anything (a real capture records kernels but executes none, so it issues
+    no collective)."""
+    import contextlib
+    import warnings
+
+    class _Graph:
+        def replay(self):
+            raise AssertionError("a graph must not be replayed after a rank failed to capture")
+
+        def reset(self):
+            pass
+
+    @contextlib.contextmanager
+    def _graph(graph, **kw):
+        if fail:
+            raise RuntimeError("capture failed (test)")
+        real = trainer._forward_backward, trainer._update
+        trainer._forward_backward = lambda ids: torch.zeros(())
+        trainer._update = lambda: None
+        try:
+            yield
+        finally:
+            trainer._forward_backward, trainer._update = real
+
+    warnings.simplefilter("ignore", RuntimeWarning)
+    trainer.cuda_graph = True
+    torch.cuda.CUDAGraph = _Graph
+    torch.cuda.graph = _graph
 
 
 def _run(mode, world=2, timeout=120):
@@ -103,6 +141,16 @@ def test_dp_gloo_gradients_are_averaged_and_replicas_agree(mode):
     trainer.step(torch.cat([_batch(0), _batch(1)]))
     for n, p in model.named_parameters():
         assert torch.allclose(p.detach(), p0[n], rtol=1e-5, atol=1e-6), n
+
+
+def test_dp_gloo_capture_failure_on_one_rank_falls_back_everywhere():
+    """The graphed data-parallel step captures on every rank, then the ranks agree (MIN of a flag) before
+    any replay: if one rank failed to capture, all continue with eager steps of the same form instead
+    of one replaying a graph whose allreduce no peer would join."""
+    out = _run("capfail")
+    assert set(out) == {0, 1} and all(v[1] == "ok" for v in out.values()), out
+    for n, a in out[0][3].items():
+        assert (a == out[1][3][n]).all(), n
 
 
 def test_dp_gloo_peer_exit_is_detected():
