@@ -104,3 +104,19 @@ def test_auto_on_cpu_is_torch_and_cuda_forced_on_cpu_raises():
     assert backends.select_impl("auto", x, None) == "torch"
     with pytest.raises(ValueError):
         backends.select_impl("cuda", x, None)
+
+
+def test_decode_graph_is_not_used_on_cpu(golden):
+    """DecodeGraph needs the cuda attention path; on a CPU model generate() runs the eager loop whatever
+    ``cuda_graph`` says, and the tokens are the reference's."""
+    from sisa_b200.generation import DecodeGraph
+
+    case, model = load_ref_model(golden)
+    m64 = model.double()
+    with torch.no_grad():
+        cache = SISACache()
+        m64(case["prompt"], cache=cache, logits_to_keep=1)
+        assert not DecodeGraph.supported(m64, cache)
+        a = m64.generate(case["prompt"], max_new_tokens=8)
+        b = m64.generate(case["prompt"], max_new_tokens=8, cuda_graph=False)
+    assert torch.equal(a, b) and torch.equal(a, case["generated"])
