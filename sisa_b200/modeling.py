@@ -18,7 +18,7 @@ from torch import Tensor
 from torch.utils.checkpoint import checkpoint
 
 from .config import ATTN_IMPLS, SISAConfig
-from .functional import _autocast_off, _work_dtype, attend_rows, rotate_pairs, sisa_attention
+from .functional import attention_rows, compute_dtype, no_autocast, rotate_pairs, sisa_attention
 
 if TYPE_CHECKING:  # pragma: no cover
     from .generation import SISACache
@@ -80,6 +80,14 @@ class SwiGLU(nn.Module):
 
             return self.w_down(swiglu(g, u))
         return self.w_down(F.silu(g) * u)
+
+
+def _cast_keep_fp32(fn: Any, t: Tensor) -> Tensor:
+    """``fn(t)``, except that a result in fp16/bf16 is replaced by ``t`` in fp32 on the result's device."""
+    out = fn(t)
+    if out.dtype in (torch.float16, torch.bfloat16):
+        out = t.to(device=out.device, dtype=torch.float32)
+    return out
 
 
 def _static(owner: nn.Module, name: str, make, *tensors: Tensor):
@@ -153,40 +161,49 @@ class SISAAttention(nn.Module):
 
     @torch.no_grad()
     def reset_parameters(self) -> None:
-        """Every weight ~ N(0, init_std) except W_C = 0 (zero_init_c) and theta_proj ~ N(0, theta_init_std);
-        alpha bias = decay_bias_init, forget bias = forget_bias_init, lambda_raw = lambda_raw_init."""
+        """The SISA initialisation: weights ~ N(0, std) with std from the table below (W_C zero when
+        zero_init_c), the decay and forget biases and lambda_raw at their configured constants."""
         cfg = self.config
-        for lin in (self.W_Q, self.W_K, self.W_V, self.W_O, self.W_B, self.alpha_proj, self.forget_proj):
-            nn.init.normal_(lin.weight, std=cfg.init_std)
-        if cfg.zero_init_c:
-            nn.init.zeros_(self.W_C.weight)
-        else:
-            nn.init.normal_(self.W_C.weight, std=cfg.init_std)
-        nn.init.normal_(self.theta_proj.weight, std=cfg.theta_init_std)
-        nn.init.constant_(self.alpha_proj.bias, cfg.decay_bias_init)
-        nn.init.constant_(self.forget_proj.bias, cfg.forget_bias_init)
+        stds = {"W_Q": cfg.init_std, "W_K": cfg.init_std, "W_V": cfg.init_std, "W_O": cfg.init_std,
+                "W_B": cfg.init_std, "W_C": 0.0 if cfg.zero_init_c else cfg.init_std,
+                "alpha_proj": cfg.init_std, "theta_proj": cfg.theta_init_std, "forget_proj": cfg.init_std}
+        for name, std in stds.items():
+            w = getattr(self, name).weight
+            if std > 0:
+                w.normal_(0.0, std)
+            else:
+                w.zero_()
+        self.alpha_proj.bias.fill_(cfg.decay_bias_init)
+        self.forget_proj.bias.fill_(cfg.forget_bias_init)
         self.lambda_raw.fill_(cfg.lambda_raw_init)
 
     def _apply(self, fn: Any, recurse: bool = True) -> "SISAAttention":
-        low = (torch.float16, torch.bfloat16)
-        old = self.lambda_raw
-        old_data = old.data
-        old_grad = None if old.grad is None else old.grad.data
-        super()._apply(fn, recurse)
-        p = self.lambda_raw
-        if p.dtype in low:
-            src = old_data if old_data.dtype not in low else p.data
-            p.data = src.to(device=p.device, dtype=torch.float32)
-            if p.grad is not None:
-                gsrc = old_grad if old_grad is not None and old_grad.dtype not in low else p.grad
-                p.grad = gsrc.to(device=p.device, dtype=torch.float32)
+        """Module-wide casts and moves (``.to``, ``.cuda``, ``.bfloat16`` ...) reach every tensor, but
+        lambda_raw (and its gradient) never drops below fp32: a cast to fp16/bf16 only moves it to the
+        target device with its fp32 value intact; other casts (fp64) apply as usual. The parameter stays
+        the same object, so optimizers that hold it keep working."""
+        lam = self._parameters.pop("lambda_raw")
+        try:
+            super()._apply(fn, recurse)
+        finally:
+            self._parameters["lambda_raw"] = lam
+        with torch.no_grad():
+            data = _cast_keep_fp32(fn, lam.data)
+            grad = None if lam.grad is None else _cast_keep_fp32(fn, lam.grad)
+            if torch._has_compatible_shallow_copy_type(lam, data):
+                lam.data = data
+                lam.grad = grad
+            else:                                   # e.g. to_empty() from the meta device: a new parameter
+                new = nn.Parameter(data, requires_grad=lam.requires_grad)
+                new.grad = grad
+                self._parameters["lambda_raw"] = new
         return self
 
     def lam(self) -> Tensor:
         return F.softplus(self.lambda_raw).float()
 
     def _forget_logits(self, x: Tensor) -> Tensor:
-        with _autocast_off(x.device.type):
+        with no_autocast(x.device.type):
             return F.linear(x.float(), self.forget_proj.weight.float(), self.forget_proj.bias.float())
 
     def fused_weights(self) -> tuple[Tensor, Tensor]:
@@ -197,28 +214,34 @@ class SISAAttention(nn.Module):
                                     self.alpha_proj.bias)
 
     def _prepare(self, x: Tensor, state: Any = None):
-        """Torch glue of the unfused path (modeling.py:171-199); with a decode ``state`` the recurrences
-        continue from its last position. Returns q, k, v, c~, b~ (compute dtype) and g, F, Phi (fp32)."""
-        bsz, seq_len, _ = x.shape
-        h, dh, s = self.config.n_head, self.config.d_head, self.config.d_state
-        q = self.W_Q(x).view(bsz, seq_len, h, dh).transpose(1, 2)
-        k = self.W_K(x).view(bsz, seq_len, h, dh).transpose(1, 2)
-        v = self.W_V(x).view(bsz, seq_len, h, dh).transpose(1, 2)
-        b = self.W_B(x).view(bsz, seq_len, h, s).transpose(1, 2)
-        c = self.W_C(x).view(bsz, seq_len, h, s).transpose(1, 2)
-        a = self.alpha_proj(x).transpose(1, 2)
-        theta = self.theta_proj(x).view(bsz, seq_len, h, s // 2).transpose(1, 2)
-        g = torch.cumsum(-F.softplus(a.float()), dim=2)
-        phi = torch.cumsum(theta.float(), dim=2)
+        """Inputs of the unfused attention (the glue of src/sisa/modeling.py:171-199), computed from one
+        projection GEMM over the concatenated weights (columns Q | K | V | B | C | theta | alpha, the
+        alpha bias the only bias), then the recurrences in fp32: g = cumsum(-softplus(alpha)),
+        Phi = cumsum(theta), F = cumsum(log sigmoid(z)), continued from the last cached position when a
+        decode ``state`` is given, and the rotation of c and b by Phi. Returns q, k, v, c~, b~ in the
+        compute dtype and g, F, Phi in fp32, all (B, H, L, .)."""
+        B, L, _ = x.shape
+        H, dh, ds = self.config.n_head, self.config.d_head, self.config.d_state
+        widths = (dh, dh, dh, ds, ds, ds // 2, 1)
+        lins = (self.W_Q, self.W_K, self.W_V, self.W_B, self.W_C, self.theta_proj, self.alpha_proj)
+        weight = torch.cat([lin.weight for lin in lins])
+        bias = torch.cat([torch.zeros(weight.shape[0] - H, dtype=self.alpha_proj.bias.dtype,
+                                      device=self.alpha_proj.bias.device), self.alpha_proj.bias])
+        proj = F.linear(x, weight, bias)
+        heads = [part.view(B, L, H, w).transpose(1, 2)
+                 for part, w in zip(proj.split([H * w for w in widths], dim=-1), widths)]
+        q, k, v, b, c, theta, alpha = heads
         z = self._forget_logits(x)
-        with _autocast_off(x.device.type):
+        with no_autocast(x.device.type):
+            g = torch.cumsum(-F.softplus(alpha[..., 0].float()), dim=2)
+            phi = torch.cumsum(theta.float(), dim=2)
             fgate = torch.cumsum(F.logsigmoid(z).transpose(1, 2), dim=2)
-        if state is not None:
-            g = g + state.g_last()
-            phi = phi + state.phi.unsqueeze(2)
-            fgate = fgate + state.f_last()
-        c = rotate_pairs(c.float(), phi)
-        b = rotate_pairs(b.float(), phi)
+            if state is not None:
+                g = g + state.g_last()
+                phi = phi + state.phi.unsqueeze(2)
+                fgate = fgate + state.f_last()
+            c = rotate_pairs(c.float(), phi)
+            b = rotate_pairs(b.float(), phi)
         cd = _compute_dtype(x)
         return q.to(cd), k.to(cd), v.to(cd), c.to(cd), b.to(cd), g, fgate, phi
 
@@ -293,9 +316,10 @@ class SISAAttention(nn.Module):
 
             y = decode_attention(q, c, g, fgate, state, self.lam())
             return self._output(y)
-        wd = _work_dtype(q.dtype)
-        y = attend_rows(q.to(wd), state.k.to(wd), state.v.to(wd), c.to(wd), state.b.to(wd), g.to(wd),
-                        state.g.to(wd), self.lam().to(wd), fgate.to(wd), state.fgate.to(wd), start)
+        wd = compute_dtype(q.dtype)
+        y, _ = attention_rows(q.to(wd), state.k.to(wd), state.v.to(wd), c.to(wd), state.b.to(wd), g.to(wd),
+                              state.g.to(wd), self.lam().to(wd), fgate.to(wd), state.fgate.to(wd), start,
+                              block=self.config.torch_block_q)
         return self._output(y.to(q.dtype))
 
     def forward(self, x: Tensor, *, cache: "SISACache | None" = None, impl: str | None = None) -> Tensor:
@@ -462,25 +486,26 @@ class SISAModel(nn.Module):
 
     def param_groups(self, lr: float, weight_decay: float = 0.1, lambda_lr: float | None = None,
                      no_decay_timescale_biases: bool = True) -> list[dict[str, Any]]:
-        """Optimizer groups "default", "timescale_biases" (alpha/forget biases, no decay) and "lambda"
-        (modeling.py:366-394)."""
-        default, timescale, lam = [], [], []
-        for name, p in self.named_parameters():
-            if not p.requires_grad:
-                continue
+        """Optimizer groups (the reference's groups, src/sisa/modeling.py:366-394): "default" (every other
+        parameter, with weight decay), "timescale_biases" (the alpha and forget biases, no decay; only
+        with ``no_decay_timescale_biases``) and "lambda" (lambda_raw, no decay, at ``lambda_lr``, which
+        defaults to ``lr``). Empty groups are left out."""
+        def group_of(name: str) -> str:
             if name.endswith("lambda_raw"):
-                lam.append(p)
-            elif no_decay_timescale_biases and name.endswith(("alpha_proj.bias", "forget_proj.bias")):
-                timescale.append(p)
-            else:
-                default.append(p)
-        groups = [{"params": default, "lr": lr, "weight_decay": weight_decay, "name": "default"}]
-        if timescale:
-            groups.append({"params": timescale, "lr": lr, "weight_decay": 0.0, "name": "timescale_biases"})
-        if lam:
-            groups.append({"params": lam, "lr": lr if lambda_lr is None else lambda_lr, "weight_decay": 0.0,
-                           "name": "lambda"})
-        return groups
+                return "lambda"
+            if no_decay_timescale_biases and name.rsplit(".", 2)[-2:] in (["alpha_proj", "bias"],
+                                                                          ["forget_proj", "bias"]):
+                return "timescale_biases"
+            return "default"
+
+        members: dict[str, list[nn.Parameter]] = {"default": [], "timescale_biases": [], "lambda": []}
+        for name, p in self.named_parameters():
+            if p.requires_grad:
+                members[group_of(name)].append(p)
+        settings = {"default": (lr, weight_decay), "timescale_biases": (lr, 0.0),
+                    "lambda": (lr if lambda_lr is None else lambda_lr, 0.0)}
+        return [{"params": ps, "lr": settings[g][0], "weight_decay": settings[g][1], "name": g}
+                for g, ps in members.items() if ps or g == "default"]
 
 
 class SISAForCausalLM(SISAModel):
@@ -499,24 +524,25 @@ class SISAForCausalLM(SISAModel):
             raise ValueError("logits_to_keep cannot be combined with labels")
         hidden = super().forward(input_ids, cache=cache)
         weight = self.embed.weight
-        loss = logits = None
-        fused_ce = fused_ce and labels is not None
+        if labels is None:
+            logits = None
+            if return_logits:
+                logits = F.linear(hidden[:, -logits_to_keep:] if logits_to_keep else hidden, weight)
+            return SISAOutput(logits=logits)
+        # position t predicts token t + 1: the last position has no target, the first token no prediction
+        inputs, targets = hidden[:, :-1], labels[:, 1:]
         if fused_ce:
             if not hidden.is_cuda:
                 raise ValueError("fused_ce=True needs CUDA tensors")
             from .kernels.linear_ce import linear_cross_entropy
 
-            d = hidden.shape[-1]
-            loss = linear_cross_entropy(hidden[:, :-1].reshape(-1, d), weight, labels[:, 1:].reshape(-1),
+            loss = linear_cross_entropy(inputs.reshape(-1, inputs.shape[-1]), weight, targets.reshape(-1),
                                         ignore_index=IGNORE_INDEX)
-        elif labels is not None and not return_logits:
-            loss = self._loss_fn(hidden[:, :-1], weight, labels[:, 1:])
-        if return_logits and not fused_ce:
-            logits = F.linear(hidden[:, -logits_to_keep:] if logits_to_keep else hidden, weight)
-            if labels is not None:
-                vocab = logits.shape[-1]
-                loss = F.cross_entropy(logits[:, :-1].reshape(-1, vocab).float(), labels[:, 1:].reshape(-1),
-                                       ignore_index=IGNORE_INDEX)
+            return SISAOutput(loss=loss)
+        if not return_logits:
+            return SISAOutput(loss=self._loss_fn(inputs, weight, targets))
+        logits = F.linear(hidden, weight)
+        loss = F.cross_entropy(logits[:, :-1].flatten(0, 1).float(), targets.flatten(), ignore_index=IGNORE_INDEX)
         return SISAOutput(loss=loss, logits=logits)
 
     def generate(self, input_ids: Tensor, max_new_tokens: int, temperature: float = 1.0, top_k: int | None = None,
