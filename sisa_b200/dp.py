@@ -9,10 +9,12 @@ averaged across ranks; the optimizer stays replicated. Two forms:
 * DDP (eager): bucketed NCCL allreduces overlap the backward pass (buckets are views of the
   gradients, so no extra copy).
 * Flat gradients (``Trainer(cuda_graph=True)`` on several GPUs, or ``flat_grads=True``): every
-  parameter's gradient is a view of one fp32 buffer, the loss is scaled by 1/world (exact for world
-  sizes that are powers of two), and one SUM allreduce of the buffer follows the backward. On CUDA the
-  whole step, allreduce included, is captured as one CUDA graph and replayed, as on one GPU; the
-  allreduce then runs after the backward instead of overlapping it.
+  parameter's gradient is a view of one fp32 buffer, laid out in the order the backward produces
+  them and cut into buckets, and the loss is scaled by 1/world (exact for world sizes that are powers
+  of two). As the backward finishes a bucket, a SUM allreduce of it starts on a side stream, so the
+  allreduces overlap the rest of the backward; buckets start strictly in bucket order, which keeps the
+  collective order identical on every rank. On CUDA the whole step, allreduces included, is captured
+  as one CUDA graph and replayed, as on one GPU.
 """
 from __future__ import annotations
 
@@ -64,6 +66,90 @@ def make_optimizer(model: SISAForCausalLM, lr: float = 6e-4, weight_decay: float
                              weight_decay=weight_decay, fused=cuda, capturable=capturable and cuda)
 
 
+class GradBuckets:
+    """Flat fp32 gradients, allreduced bucket by bucket as the backward finishes them.
+
+    Every trainable parameter's gradient is a view of one fp32 buffer. The buffer holds the
+    parameters in reverse registration order, which is about the order the backward finishes them
+    (last block first), and is cut at parameter boundaries into buckets of about ``cap_mb``. A
+    post-accumulate-grad hook counts the finished parameters of each bucket. A bucket starts once it
+    and every bucket before it are complete, so all ranks issue the same allreduces in the same order
+    whatever order the hooks fire in. On CUDA each allreduce runs on a side stream that first waits for
+    the stream the backward ran on; :meth:`finish` starts any bucket still pending (parameters that
+    received no gradient this step) and makes the caller's stream wait for the side stream. Under CUDA
+    graph capture the waits become graph dependencies, so a replay overlaps the allreduces with the
+    backward in the same way.
+    """
+
+    def __init__(self, params: list[torch.nn.Parameter], device: torch.device, cap_mb: float = 40.0):
+        self.device = device
+        order = list(reversed(params))
+        self.buffer = torch.zeros(sum(p.numel() for p in order), dtype=torch.float32, device=device)
+        cap = max(1, int(cap_mb * 2**20 / 4))
+        self.bounds: list[tuple[int, int]] = []       # [start, end) of each bucket in the buffer
+        self._bucket_of: dict[int, int] = {}
+        off, start = 0, 0
+        for p in order:
+            p.grad = self.buffer[off:off + p.numel()].view_as(p)
+            if off > start and off + p.numel() - start > cap:
+                self.bounds.append((start, off))
+                start = off
+            self._bucket_of[id(p)] = len(self.bounds)
+            off += p.numel()
+        self.bounds.append((start, off))
+        self._size = [0] * len(self.bounds)
+        for p in order:
+            self._size[self._bucket_of[id(p)]] += 1
+        self._left: list[int] = []
+        self._next = 0
+        self.side = torch.cuda.Stream(device) if device.type == "cuda" else None
+        self._hooks = [p.register_post_accumulate_grad_hook(self._on_grad) for p in order]
+
+    def __len__(self) -> int:
+        return len(self.bounds)
+
+    def start_step(self) -> None:
+        """Zero the gradients and rearm the bucket counters (call before the backward)."""
+        self.buffer.zero_()
+        self._left = list(self._size)
+        self._next = 0
+
+    def _on_grad(self, p: torch.Tensor) -> None:
+        if not self._left:
+            return                                   # a backward outside a step (no allreduce wanted)
+        k = self._bucket_of[id(p)]
+        self._left[k] -= 1
+        while self._next < len(self.bounds) and self._left[self._next] == 0:
+            self._launch(self._next)
+            self._next += 1
+
+    def _launch(self, k: int) -> None:
+        a, b = self.bounds[k]
+        view = self.buffer[a:b]
+        if self.side is None:
+            dist.all_reduce(view, op=dist.ReduceOp.SUM)
+            return
+        ready = torch.cuda.Event()
+        ready.record(torch.cuda.current_stream(self.device))
+        self.side.wait_event(ready)
+        with torch.cuda.stream(self.side):
+            dist.all_reduce(view, op=dist.ReduceOp.SUM)
+
+    def finish(self) -> None:
+        """Start the buckets still pending and order the caller's stream after every allreduce."""
+        while self._next < len(self.bounds):
+            self._launch(self._next)
+            self._next += 1
+        self._left = []
+        if self.side is not None:
+            torch.cuda.current_stream(self.device).wait_stream(self.side)
+
+    def remove(self) -> None:
+        for h in self._hooks:
+            h.remove()
+        self._hooks = []
+
+
 class Trainer:
     """One optimizer step per call: forward (bf16 autocast on CUDA), loss, backward, gradient allreduce,
     clipping, AdamW.
@@ -77,7 +163,7 @@ class Trainer:
     """
 
     def __init__(self, model: SISAForCausalLM, optimizer: torch.optim.Optimizer | None = None, *,
-                 fused_ce: bool = True, clip: float = 1.0, bucket_cap_mb: float = 64.0, cuda_graph: bool = False,
+                 fused_ce: bool = True, clip: float = 1.0, bucket_cap_mb: float = 40.0, cuda_graph: bool = False,
                  flat_grads: bool = False):
         self.module = model
         dev = next(model.parameters()).device
@@ -86,10 +172,10 @@ class Trainer:
         self.world = dist.get_world_size() if self.distributed else 1
         self.cuda_graph = cuda_graph and dev.type == "cuda"
         self.flat = self.distributed and (self.cuda_graph or flat_grads)
-        self._grads = None
+        self._buckets: GradBuckets | None = None
         if self.flat:
             self.model = model
-            self._make_flat_grads()
+            self._make_flat_grads(bucket_cap_mb)
         elif self.distributed:
             self.model = torch.nn.parallel.DistributedDataParallel(
                 model, device_ids=[dev.index] if dev.type == "cuda" else None, gradient_as_bucket_view=True,
@@ -103,20 +189,16 @@ class Trainer:
         self._static_ids = None
         self._static_loss = None
 
-    def _make_flat_grads(self) -> None:
-        """Rank 0's parameters on every rank, and every gradient a view of one fp32 buffer (autograd
-        accumulates into existing gradients in place, so the views persist across steps)."""
+    def _make_flat_grads(self, cap_mb: float) -> None:
+        """Rank 0's parameters on every rank, and every gradient a view of one bucketed fp32 buffer
+        (autograd accumulates into existing gradients in place, so the views persist across steps)."""
         params = [p for p in self.module.parameters() if p.requires_grad]
         if any(p.dtype != torch.float32 for p in params):
             raise TypeError("flat gradients need fp32 parameters (the master weights)")
         with torch.no_grad():
             for p in params:
                 dist.broadcast(p.data, 0)
-        self._grads = torch.zeros(sum(p.numel() for p in params), dtype=torch.float32, device=self.device)
-        off = 0
-        for p in params:
-            p.grad = self._grads[off:off + p.numel()].view_as(p)
-            off += p.numel()
+        self._buckets = GradBuckets(params, self.device, cap_mb)
 
     def close(self) -> None:
         """Release the captured step. A graph that holds NCCL work must be released before
@@ -174,9 +256,7 @@ class Trainer:
         self._graph = graph
 
     def _update(self) -> None:
-        """Gradient allreduce (flat form), clipping and the optimizer step."""
-        if self.flat:
-            dist.all_reduce(self._grads, op=dist.ReduceOp.SUM)
+        """Clipping and the optimizer step (in the flat form the allreduces have run during the backward)."""
         if self.clip:
             torch.nn.utils.clip_grad_norm_(self.module.parameters(), self.clip)
         self.opt.step()
@@ -190,9 +270,11 @@ class Trainer:
     def _forward_backward(self, ids: torch.Tensor) -> torch.Tensor:
         self.model.train()
         if self.flat:
-            self._grads.zero_()
+            self._buckets.start_step()
         loss = self._loss(ids)
         (loss * (1.0 / self.world) if self.flat else loss).backward()
+        if self.flat:
+            self._buckets.finish()
         return loss.detach()
 
     def _eager_step(self, ids: torch.Tensor) -> torch.Tensor:

@@ -43,8 +43,12 @@ def _worker(rank, world, port, mode, q):
         _, _, dev = dp.init_distributed("gloo", timeout_s=15.0)
         model = dp.build_model(_cfg(), dev, seed=0)
         # SGD: the update is linear in the averaged gradient, so it can be compared with one process
+        # the flat form with small buckets (a few parameters each), so several allreduces start during
+        # the backward
         trainer = dp.Trainer(model, torch.optim.SGD(model.parameters(), lr=0.5), fused_ce=False,
-                             flat_grads=mode in ("flat", "capfail"))
+                             flat_grads=mode in ("flat", "capfail"), bucket_cap_mb=0.05)
+        if mode == "flat":
+            assert len(trainer._buckets) >= 4, len(trainer._buckets)
         if mode == "exit" and rank == 1:
             os._exit(3)                       # leaves between steps, no collective in flight
         if mode == "capfail":
@@ -158,3 +162,36 @@ def test_dp_gloo_peer_exit_is_detected():
     assert 0 in out, out
     rank, status, kind, msg, _ = out[0]
     assert status == "error", out[0]
+
+
+def test_grad_buckets_start_in_order_once_complete(monkeypatch):
+    """Bucket bookkeeping in one process, with the allreduce replaced by a recorder: every bucket starts
+    exactly once, in bucket order, and only after each of its parameters has its final gradient."""
+    sys.path.insert(0, ROOT)
+    from sisa_b200 import dp
+
+    model = dp.build_model(_cfg(), torch.device("cpu"), seed=0)
+    params = [p for p in model.parameters() if p.requires_grad]
+    starts = []
+
+    def record(view, op=None):
+        starts.append((view.data_ptr(), view.numel(), view.clone()))
+
+    monkeypatch.setattr(dp.dist, "all_reduce", record)
+    buckets = dp.GradBuckets(params, torch.device("cpu"), cap_mb=0.05)
+    assert len(buckets) >= 4
+    buckets.start_step()
+    loss = model(_batch(0), labels=_batch(0)).loss
+    loss.backward()
+    buckets.finish()
+    assert len(starts) == len(buckets)
+    base = buckets.buffer.data_ptr()
+    for k, ((ptr, n, snap), (a, b)) in enumerate(zip(starts, buckets.bounds)):
+        assert (ptr - base) // 4 == a and n == b - a, k
+        assert torch.equal(snap, buckets.buffer[a:b]), f"bucket {k} started before its gradients were final"
+    # the gradients are views of the buffer and equal autograd's own
+    ref = dp.build_model(_cfg(), torch.device("cpu"), seed=0)
+    ref(_batch(0), labels=_batch(0)).loss.backward()
+    for (n_, p), q in zip(model.named_parameters(), ref.parameters()):
+        assert torch.allclose(p.grad, q.grad, rtol=1e-6, atol=1e-7), n_
+    buckets.remove()
