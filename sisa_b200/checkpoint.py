@@ -126,17 +126,17 @@ def _model_without_init(config: SISAConfig) -> "SISAForCausalLM":
 
 
 def _load_exact(model: torch.nn.Module, state_dict: Mapping[str, Tensor]) -> None:
-    """Strict load with the reference's error messages (checkpoint.py:118-129)."""
-    want = model.state_dict()
-    missing = sorted(want.keys() - state_dict.keys())
-    unexpected = sorted(state_dict.keys() - want.keys())
+    """Strict load: every model key present with its shape and nothing else, else ValueError listing the
+    first few offending keys (missing / unexpected / shape mismatch)."""
+    want = {k: tuple(t.shape) for k, t in model.state_dict().items()}
+    have = {k: tuple(t.shape) for k, t in state_dict.items()}
+    missing, unexpected = sorted(want.keys() - have.keys()), sorted(have.keys() - want.keys())
     if missing or unexpected:
-        raise ValueError(f"state dict does not match the model: {len(missing)} missing {missing[:8]}, "
-                         f"{len(unexpected)} unexpected {unexpected[:8]}")
-    wrong = [(k, tuple(state_dict[k].shape), tuple(t.shape)) for k, t in want.items()
-             if tuple(state_dict[k].shape) != tuple(t.shape)]
+        raise ValueError(f"the state dict does not fit the model: {len(missing)} missing keys {missing[:8]}, "
+                         f"{len(unexpected)} unexpected keys {unexpected[:8]}")
+    wrong = [(k, have[k], shape) for k, shape in want.items() if have[k] != shape]
     if wrong:
-        raise ValueError(f"shape mismatch (key, checkpoint, model): {wrong[:8]}")
+        raise ValueError(f"shape mismatch, as (key, checkpoint shape, model shape): {wrong[:8]}")
     model.load_state_dict(state_dict, strict=True)
 
 
@@ -153,17 +153,17 @@ def _weights_of(obj: Any) -> dict[str, Tensor]:
 
 
 def _read_torch_file(path: Path, weights_only: bool) -> Any:
-    """``torch.load`` to the CPU, memory-mapped where the file format allows it."""
+    """``torch.load`` to the CPU. Files in torch's zip format are memory-mapped (tensors are read on first
+    use); older pickle-only files cannot be mapped and are read whole. With ``weights_only`` a file that
+    needs arbitrary Python objects raises UnpicklingError naming the ``trust_pickle`` flag."""
+    with open(path, "rb") as f:
+        zip_format = f.read(4) == b"PK\x03\x04"
     try:
-        return torch.load(path, map_location="cpu", mmap=True, weights_only=weights_only)
+        return torch.load(path, map_location="cpu", mmap=zip_format, weights_only=weights_only)
     except pickle.UnpicklingError as err:
         raise pickle.UnpicklingError(
-            f"{err}\nThe checkpoint holds objects that torch.load(weights_only=True) refuses. If you trust "
-            "the file, pass trust_pickle=True.") from None
-    except RuntimeError as err:
-        if "mmap" not in str(err):
-            raise
-    return torch.load(path, map_location="cpu", weights_only=weights_only)   # legacy (non-zip) files
+            f"{err}\n{path} stores Python objects beyond tensors, which the safe loader refuses; load it with "
+            "trust_pickle=True only if you trust where the file came from.") from None
 
 
 def load_paper_checkpoint(path: str | Path, *, trust_pickle: bool = False, dtype: torch.dtype | None = None,

@@ -224,43 +224,59 @@ class DecodeGraph:
 
 
 def _eos_ids(eos_token_id) -> list[int]:
-    """Normalise ``eos_token_id`` to a list of ints (generation.py:98-122)."""
+    """The end-of-sequence ids as a list (the accepted forms of src/sisa/generation.py:98-122): None gives
+    none; an integer, a 0-d or 1-d integer tensor or array, or an iterable of integers gives its values.
+    Booleans, strings, bytes, floating-point or 2-d arrays raise TypeError."""
     if eos_token_id is None:
         return []
-    bad = TypeError(f"eos_token_id must be an integer or an iterable of integers, "
-                    f"got {eos_token_id!r} ({type(eos_token_id).__name__})")
-    if isinstance(eos_token_id, (bool, str, bytes)):
-        raise bad
-    if isinstance(eos_token_id, numbers.Integral):
-        return [int(eos_token_id)]
-    dtype = getattr(eos_token_id, "dtype", None)
-    if dtype is not None:
-        is_float = dtype.is_floating_point if torch.is_tensor(eos_token_id) else dtype.kind not in "iu"
-        if is_float or getattr(eos_token_id, "ndim", 1) > 1:
-            raise bad
-        if getattr(eos_token_id, "ndim", None) == 0:
-            return [int(eos_token_id)]
-        return [int(t) for t in eos_token_id.tolist()]
-    try:
-        ids = list(eos_token_id)
-    except TypeError:
-        raise bad from None
-    if not all(isinstance(t, numbers.Integral) and not isinstance(t, bool) for t in ids):
-        raise bad
+    x = eos_token_id
+    err = TypeError(f"eos_token_id must be an integer or an iterable of integers, got {x!r} ({type(x).__name__})")
+    if isinstance(x, (bool, str, bytes)):
+        raise err
+    if isinstance(x, numbers.Integral):
+        return [int(x)]
+    dtype = getattr(x, "dtype", None)
+    if dtype is not None:                               # a torch tensor or a numpy array
+        floating = dtype.is_floating_point if torch.is_tensor(x) else dtype.kind not in "iu"
+        if floating or x.ndim > 1:
+            raise err
+        return [int(v) for v in x.reshape(-1).tolist()]
+    if not isinstance(x, Iterable):
+        raise err
+    ids = list(x)
+    if any(isinstance(t, bool) or not isinstance(t, numbers.Integral) for t in ids):
+        raise err
     return [int(t) for t in ids]
 
 
 def _next_token(logits: Tensor, *, do_sample: bool, temperature: float, top_k: int | None,
                 generator: torch.Generator | None) -> Tensor:
-    logits = logits.float()
+    """Greedy argmax, or a sample from softmax(logits / temperature) restricted to the ``top_k`` largest
+    logits. The sample is drawn among the k candidates only (a softmax over k values instead of the
+    vocabulary), so it follows the reference's distribution but not its random stream."""
+    scores = logits.float()
     if not do_sample:
-        return logits.argmax(dim=-1)
-    logits = logits / temperature
-    if top_k is not None and top_k < logits.shape[-1]:
-        kth = torch.topk(logits, top_k, dim=-1).values[..., -1:]
-        logits = logits.masked_fill(logits < kth, float("-inf"))
-    probs = torch.softmax(logits, dim=-1)
-    return torch.multinomial(probs, num_samples=1, generator=generator).squeeze(-1)
+        return scores.argmax(dim=-1)
+    scores = scores / temperature
+    if top_k is not None and top_k < scores.shape[-1]:
+        vals, idx = torch.topk(scores, top_k, dim=-1)
+        pick = torch.multinomial(torch.softmax(vals, dim=-1), num_samples=1, generator=generator)
+        return idx.gather(-1, pick).squeeze(-1)
+    return torch.multinomial(torch.softmax(scores, dim=-1), num_samples=1, generator=generator).squeeze(-1)
+
+
+def _check_generate_args(input_ids: Tensor, max_new_tokens: int, do_sample: bool, temperature: float,
+                         top_k: int | None) -> None:
+    """The argument errors of the reference's generate (ValueError, same messages)."""
+    problems = [
+        (max_new_tokens < 0, "max_new_tokens must be >= 0"),
+        (do_sample and temperature <= 0, "temperature must be positive when do_sample=True"),
+        (top_k is not None and top_k <= 0, "top_k must be a positive integer"),
+        (input_ids.dim() not in (1, 2) or input_ids.shape[-1] == 0, "input_ids must be a non-empty (B, L) tensor"),
+    ]
+    for bad, msg in problems:
+        if bad:
+            raise ValueError(msg)
 
 
 @torch.no_grad()
@@ -276,17 +292,10 @@ def generate(model: "SISAForCausalLM", input_ids: Tensor, max_new_tokens: int, t
     model that :meth:`DecodeGraph.supported` accepts, the first decode step runs eagerly and the rest
     replay it as one CUDA graph.
     """
-    if max_new_tokens < 0:
-        raise ValueError("max_new_tokens must be >= 0")
-    if do_sample and temperature <= 0:
-        raise ValueError("temperature must be positive when do_sample=True")
-    if top_k is not None and top_k <= 0:
-        raise ValueError("top_k must be a positive integer")
+    _check_generate_args(input_ids, max_new_tokens, do_sample, temperature, top_k)
     squeeze = input_ids.dim() == 1
     if squeeze:
         input_ids = input_ids.unsqueeze(0)
-    if input_ids.dim() != 2 or input_ids.shape[1] == 0:
-        raise ValueError("input_ids must be a non-empty (B, L) tensor")
     if max_new_tokens == 0:
         return input_ids.squeeze(0) if squeeze else input_ids
     eos = _eos_ids(eos_token_id)
