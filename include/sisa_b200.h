@@ -5,7 +5,9 @@
  * Nothing in this library allocates device memory, synchronises the host or throws across the
  * ABI: the caller owns every output and workspace buffer, and the work is ordered only by the
  * stream that is passed in. Kernels never trap; run-time conditions are OR-ed into *status
- * (SISA_ST_* bits) and left for the caller to read.
+ * (SISA_ST_* bits) and left for the caller to read. Entry points that need a current context (to
+ * encode TMA tensor maps) make the device that owns their data current for the length of the call
+ * and give the calling thread back its previous context before they return.
  *
  * Reference interfaces (tlstngud/sisa, paths inside that project) that each entry point
  * replaces are cited beside it.
@@ -226,11 +228,13 @@ int sisa_decode_attn(const sisa_view4* q, const sisa_view4* c, const float* g_q,
                      int32_t* status, void* stream);
 
 /* Allocation-free variant of sisa_decode_attn (no counterpart in the reference): identical arguments
- * except that there is no workspace. For callers that cannot allocate device memory when they decode
- * (inside CUDA-graph capture, hosts without a device allocator, fixed memory budgets). The split-K
- * partials live in a fixed 4.3 MB array owned by the library on every GPU that loads it; B*H may not
- * exceed 16384 (SISA_ERR_VALUE otherwise). The first call on a device resolves the array's address and
- * must precede any stream capture. Calls that overlap on the GPU share the array and race. */
+ * except that there is no workspace. For callers that cannot allocate device memory when they decode:
+ * host programs that bind only this C ABI and have no device allocator, and serving loops held to a
+ * fixed, pre-reserved memory budget. The split-K partials live in a fixed 4.3 MB array owned by the
+ * library on every GPU that loads it; B*H may not exceed 16384 (SISA_ERR_VALUE otherwise). The first
+ * call on a device resolves the array's address with that device current, so it should come before
+ * any stream capture; a cudaDeviceReset makes that address stale. Calls that overlap on the GPU share
+ * the array and race. The caller's current device is unchanged on return. */
 int sisa_decode_attn_noalloc(const sisa_view4* q, const sisa_view4* c, const float* g_q, const float* f_q,
                              const sisa_view4* k_cache, const sisa_view4* v_cache, const sisa_view4* b_cache,
                              const float* g_cache, const float* f_cache, int64_t gf_stride, const float* lam,
@@ -272,6 +276,15 @@ int sisa_decode_attn_dpos(const sisa_view4* q, const sisa_view4* c, const float*
                           const float* g_cache, const float* f_cache, int64_t gf_stride, const float* lam,
                           int64_t B, int64_t H, const int32_t* d_pos, int64_t max_n, int dtype, const sisa_view4* y,
                           void* workspace, int32_t* status, void* stream);
+
+/* Diagnostic: one block runs the library's bounded-wait handshake (a producer warp, consumer warps
+ * waiting on an mbarrier, a tensor-memory allocation freed at the end) with the wait limit limit_ns
+ * (1e3..1e9 ns) in place of the library's 2 s. With producer_arrives = 0 nothing ever arrives, so the
+ * consumers' waits run out: SISA_ST_TIMEOUT is OR-ed into *status, *result (device int32) receives the
+ * number of consumer warps that gave up (2), and the kernel returns with the context usable. With
+ * producer_arrives = 1, *result is 0. The reference asserts on the device instead
+ * (src/sisa/kernels/fused_prep.py:502-523 via torch._assert_async), which ends the CUDA context. */
+int sisa_selftest_wait(int producer_arrives, int64_t limit_ns, int32_t* status, int32_t* result, void* stream);
 
 #ifdef __cplusplus
 }

@@ -103,6 +103,7 @@ SIGNATURES = {
     "sisa_norm_bwd": (_I, [ctypes.POINTER(NormBwdArgs), _P, _P]),
     "sisa_swiglu_fwd": (_I, [_P, _I64, _P, _I64, _I64, _I64, _I, _P, _I64, _P, _P]),
     "sisa_swiglu_bwd": (_I, [_P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I, _P, _I64, _P, _I64, _P, _P]),
+    "sisa_selftest_wait": (_I, [_I, _I64, _P, _P, _P]),
 }
 
 

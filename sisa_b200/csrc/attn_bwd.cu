@@ -269,7 +269,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
     const float gi = posbh[rr], fi = posbh[p.Lp + rr];
     const float ga = posbh[m0];
     const float lam = p.lam[h];
-    const float rowf = exp2f(fminf((gi - ga) * kLOG2E, 0.f));
+    const float rowf = exp2f(fmin_nan((gi - ga) * kLOG2E, 0.f));
     const float rs = lam * rowf;
     const float rs2 = rs * kLOG2E;
     const float lam2 = lam * kLOG2E;
@@ -361,7 +361,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
         //           the diagonal element itself kept apart (the exact-delta terms).
         const int jt = key0(n), r0 = m0 + quarter * 32;
         if (r0 > jt + 63) {
-          const float rowe = ex2_approx(fminf((gi - kpos[63]) * kLOG2E, 0.f));
+          const float rowe = ex2_approx(fmin_nan((gi - kpos[63]) * kLOG2E, 0.f));
           const float2 rowe2 = bcast2(rowe), lamv = bcast2(lam), lam2v = bcast2(lam2);
 #pragma unroll
           for (int c = 0; c < NCOL; c += 2) {
@@ -398,7 +398,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
               const float fj = (c & 2) ? (e ? f4.w : f4.z) : (e ? f4.y : f4.x);
               const int j = j0 + cc;
               const bool valid = (j <= row) && (j < L);
-              const float dec = valid ? ex2_approx(fminf(fmaf(gj, -kLOG2E, gil), 0.f)) : 0.f;
+              const float dec = valid ? ex2_approx(fmin_nan(fmaf(gj, -kLOG2E, gil), 0.f)) : 0.f;
               const float u = dec * uv[cc];
               const float x = fmaf(sv[cc], c1, fmaf(fj, -kLOG2E, fmaf(lam2, u, filse)));   // x - lse (log2)
               const float pr = valid ? ex2_approx(x) : 0.f;
@@ -420,7 +420,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dq_kernel(const __grid_c
         }
       } else {
         const float ge = kpos[63];
-        const float2 mid2 = bcast2(exp2f(fminf((ga - ge) * kLOG2E, 0.f)));
+        const float2 mid2 = bcast2(exp2f(fmin_nan((ga - ge) * kLOG2E, 0.f)));
 #pragma unroll
         for (int c = 0; c < NCOL; c += 2) {
           const float4 f4 = kf4[c / 4], c4 = kc4[c / 4];
@@ -685,7 +685,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
     const float gj = posbh[jj], fj = posbh[p.Lp + jj];
     const float ge = posbh[min(n0 + 127, L - 1)];
     const float lam = p.lam[h];
-    const float colf = exp2f(fminf((ge - gj) * kLOG2E, 0.f));     // 128-row key-tile anchor
+    const float colf = exp2f(fmin_nan((ge - gj) * kLOG2E, 0.f));     // 128-row key-tile anchor
     const float rk = lam * colf;
     const float rk2 = rk * kLOG2E;
     const float lam2 = lam * kLOG2E;
@@ -733,7 +733,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
         //  across - the diagonal crosses these keys: pairwise decay, causal mask, diagonal element.
         const int mt = n0 + 64 * n, k0 = n0 + quarter * 32;
         if (k0 + 31 < mt) {
-          const float ek = ex2_approx(fminf((qpos[0] - gj) * kLOG2E, 0.f));   // exp(g_mt - g_j)
+          const float ek = ex2_approx(fmin_nan((qpos[0] - gj) * kLOG2E, 0.f));   // exp(g_mt - g_j)
           const float2 ek2 = bcast2(ek), lamv = bcast2(lam), lam2v = bcast2(lam2);
           const bool tail = (mt + 64 > L);
 #pragma unroll
@@ -783,7 +783,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
             const bool valid = (i >= j) && (i < L);
             const bool strict = valid && (i > j);
             const bool eye = valid && (i == j);
-            const float dec = valid ? ex2_approx(fminf(fmaf(gi, kLOG2E, -gjl), 0.f)) : 0.f;
+            const float dec = valid ? ex2_approx(fmin_nan(fmaf(gi, kLOG2E, -gjl), 0.f)) : 0.f;
             const float u = dec * uv[cc];
             const float x = fmaf(sv[cc], c1, fmaf(lam2, u, Gi + nfjl));   // x - lse_i (log2)
             const float pr = valid ? ex2_approx(x) : 0.f;
@@ -803,7 +803,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
         }
       } else {
         const float gs = qpos[0];                                  // query block start
-        const float2 mid2 = bcast2(exp2f(fminf((gs - ge) * kLOG2E, 0.f)));
+        const float2 mid2 = bcast2(exp2f(fmin_nan((gs - ge) * kLOG2E, 0.f)));
         const bool tail = (n0 + 64 * n + 64 > L);
 #pragma unroll
         for (int c = 0; c < NCOL; c += 2) {

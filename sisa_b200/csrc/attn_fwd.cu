@@ -172,7 +172,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     const float gi = posbh[rr], fi = posbh[p.Lp + rr];
     const float ga = posbh[m0];
     const float lam = p.lam[h];
-    const float rs = lam * exp2f(fminf((gi - ga) * kLOG2E, 0.f));   // lam * rowf (128-row anchor)
+    const float rs = lam * exp2f(fmin_nan((gi - ga) * kLOG2E, 0.f));   // lam * rowf (128-row anchor)
     const float lam2 = lam * kLOG2E;
     const float c1 = kScale * kLOG2E;
     const uint32_t tS = tmem_addr(tbase, warp, COL_S);
@@ -218,8 +218,8 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
             const int c = 2 * q + e;
             const float gja = e ? g4.z : g4.x, gjb = e ? g4.w : g4.y;
             const float2 fj = e ? make_float2(f4.z, f4.w) : make_float2(f4.x, f4.y);
-            const float da = exp2f(fminf((gi - gja) * kLOG2E, 0.f));
-            const float db = exp2f(fminf((gi - gjb) * kLOG2E, 0.f));
+            const float da = exp2f(fmin_nan((gi - gja) * kLOG2E, 0.f));
+            const float db = exp2f(fmin_nan((gi - gjb) * kLOG2E, 0.f));
             const float2 u = mul2(make_float2(da, db), u2[c]);
             const float2 y = fma2(u, lam2v, fma2(fj, nl2e, film2));
             float2 x = fma2(x2[c], c1v, y);
@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         }
       } else {
         const float ge = kpos[BN - 1];
-        const float2 rsm = bcast2(rs * exp2f(fminf((ga - ge) * kLOG2E, 0.f)) * kLOG2E);   // lam rowf mid log2e
+        const float2 rsm = bcast2(rs * exp2f(fmin_nan((ga - ge) * kLOG2E, 0.f)) * kLOG2E);   // lam rowf mid log2e
 #pragma unroll
         for (int q = 0; q < 16; ++q) {
           const float4 f4 = kf4[q], c4 = kc4[q];

@@ -16,6 +16,7 @@
 #include "decode.h"
 #include "lce.h"
 #include "norm.h"
+#include "capi_util.h"
 
 namespace {
 
@@ -105,18 +106,29 @@ int map_rows3(CUtensorMap* m, const void* ptr, int64_t BH, int64_t L, int64_t X,
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Tensor-map encoding is a driver call that needs a current context on the calling thread. A thread
-// that has not touched CUDA yet (e.g. an autograd worker) has none, so bind the device that owns the
-// data before encoding. cudaSetDevice initialises that device's primary context if needed.
-int bind_device_of(const void* ptr) {
-  cudaPointerAttributes a;
-  cudaError_t e = cudaPointerGetAttributes(&a, ptr);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaPointerGetAttributes");
-  if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged)
-    return fail(SISA_ERR_VALUE, "tensor data is not device memory");
-  e = cudaSetDevice(a.device);   // makes the primary context current on this thread
-  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
-  return SISA_OK;
+using CtxGetFn = CUresult (*)(CUcontext*);
+using CtxSetFn = CUresult (*)(CUcontext);
+
+// cuCtxGetCurrent / cuCtxSetCurrent through the runtime's driver entry-point query (no link against
+// libcuda), resolved once; null if the driver does not offer them.
+struct CtxFns {
+  CtxGetFn get = nullptr;
+  CtxSetFn set = nullptr;
+};
+const CtxFns& ctx_fns() {
+  static CtxFns f;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      f.get = reinterpret_cast<CtxGetFn>(p);
+    if (cudaGetDriverEntryPoint("cuCtxSetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      f.set = reinterpret_cast<CtxSetFn>(p);
+  });
+  return f;
 }
 
 int check_view(const sisa_view4* v, int elem_bytes, const char* name) {
@@ -136,7 +148,7 @@ int check_dims(int64_t B, int64_t H, int64_t L) {
                                            (long long)B, (long long)H, (long long)L);
   // The attention grids are (L/128, B*H) and the preparation grids (H/4, L/64, B): their second and
   // third grid dimensions are limited to 65535 blocks.
-  if (L > 65535ll * 64 || B * H > 65535)
+  if (L > 65535ll * 64 || B > 65535 || H > 65535 || B * H > 65535)
     return fail(SISA_ERR_VALUE, "problem too large (B*H=%lld, L=%lld)", (long long)(B * H), (long long)L);
   return SISA_OK;
 }
@@ -165,6 +177,34 @@ int64_t nch64(int64_t L) { return (L + 63) / 64; }
 namespace sisa {
 // Records an error for sisa_last_error() from entry points defined outside this file.
 int capi_fail(int code, const char* msg) { return fail(code, "%s", msg); }
+int capi_check_dims(int64_t B, int64_t H, int64_t L) { return check_dims(B, H, L); }
+int capi_check_view(const sisa_view4* v, int elem_bytes, const char* name) { return check_view(v, elem_bytes, name); }
+int capi_check_dtype(int dtype) { return check_dtype(dtype); }
+
+int DeviceScope::bind(const void* ptr) {
+  cudaPointerAttributes a;
+  cudaError_t e = cudaPointerGetAttributes(&a, ptr);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaPointerGetAttributes");
+  if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged)
+    return fail(SISA_ERR_VALUE, "tensor data is not device memory");
+  const CtxFns& f = ctx_fns();
+  CUcontext cur = nullptr;
+  if (f.get && f.set && f.get(&cur) == CUDA_SUCCESS) {
+    prev_ = cur;
+    bound_ = true;
+  }
+  e = cudaSetDevice(a.device);   // makes the device's primary context current on this thread
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  device_ = a.device;
+  return SISA_OK;
+}
+
+DeviceScope::~DeviceScope() {
+  if (!bound_) return;
+  const CtxFns& f = ctx_fns();
+  CUcontext now = nullptr;
+  if (f.get(&now) == CUDA_SUCCESS && now != static_cast<CUcontext>(prev_)) f.set(static_cast<CUcontext>(prev_));
+}
 }  // namespace sisa
 
 extern "C" {
@@ -246,7 +286,8 @@ int sisa_attn_fwd(const sisa_view4* q, const sisa_view4* k, const sisa_view4* v,
     return rc;
   if (!pos || !lam || !lse) return fail(SISA_ERR_VALUE, "sisa_attn_fwd: null pos, lam or lse");
   if (!aligned16(pos) || (o32 && !aligned16(o32))) return fail(SISA_ERR_ALIGN, "pos/o32 must be 16-byte aligned");
-  if ((rc = bind_device_of(q->data))) return rc;
+  sisa::DeviceScope scope;
+  if ((rc = scope.bind(q->data))) return rc;
   const CUtensorMapDataType dt = dtype == SISA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   sisa::FwdParams p;
   memset(&p, 0, sizeof(p));
@@ -286,7 +327,8 @@ int sisa_attn_bwd(const sisa_view4* q, const sisa_view4* k, const sisa_view4* v,
     return fail(SISA_ERR_VALUE, "sisa_attn_bwd: null pos, lam, lse, dg, dlam or workspace");
   if (!aligned16(pos) || !aligned16(workspace) || (o32 && !aligned16(o32)))
     return fail(SISA_ERR_ALIGN, "pos, o32 and workspace must be 16-byte aligned");
-  if ((rc = bind_device_of(q->data))) return rc;
+  sisa::DeviceScope scope;
+  if ((rc = scope.bind(q->data))) return rc;
   const CUtensorMapDataType dt = dtype == SISA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   sisa::BwdParams p;
   memset(&p, 0, sizeof(p));
@@ -514,7 +556,8 @@ int sisa_lce_logits(const void* x, int64_t R, int64_t D, int64_t x_ld, const voi
   if (!aligned16(x) || !aligned16(w) || !aligned16(logits) || x_ld % 8 || w_ld % 8 || logits_ld % 8 ||
       x_ld < D || w_ld < D || logits_ld < Vp)
     return fail(SISA_ERR_ALIGN, "sisa_lce_logits: rows must be 16-byte aligned (ld multiple of 8 and >= width)");
-  if ((rc = bind_device_of(x))) return rc;
+  sisa::DeviceScope scope;
+  if ((rc = scope.bind(x))) return rc;
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(SISA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   const CUtensorMapDataType dt = dtype == SISA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;

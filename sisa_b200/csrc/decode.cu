@@ -19,6 +19,7 @@
 #include "sm100.cuh"
 #include "gate_math.cuh"
 #include "decode.h"
+#include "capi_util.h"
 
 namespace sisa {
 namespace dec {
@@ -131,7 +132,7 @@ __global__ void __launch_bounds__(NT, 4) decode_split_kernel(DecodeParams p) {
       cb = fmaf(c8[2 * e], unpack_lo<kHalf>(bw[e]), cb);
       cb = fmaf(c8[2 * e + 1], unpack_hi<kHalf>(bw[e]), cb);
     }
-    const float dec = exp2f(fminf((gq - cur.g) * kLog2e, 0.f));
+    const float dec = exp2f(fmin_nan((gq - cur.g) * kLog2e, 0.f));
     float x = fmaf(qk, c1, lam2 * (dec * cb));
     x += __shfl_xor_sync(0xffffffffu, x, 1);
     x += __shfl_xor_sync(0xffffffffu, x, 2);
@@ -342,27 +343,28 @@ cudaError_t launch_decode(const DecodeParams& p, int dtype, cudaStream_t st) {
 // =============================================================================================
 // Allocation-free decode entry point.
 //
-// Some callers cannot allocate device memory at the moment they decode: code running inside a
-// CUDA-graph capture (allocations cannot be captured, and cudaFree would synchronise the device),
-// hosts that bind only this C ABI and have no device allocator of their own, and serving loops that
-// run under a fixed, pre-reserved memory budget. sisa_decode_attn needs a caller-provided workspace
+// Some callers of this library cannot allocate device memory when they decode: a host program that
+// binds only this C ABI (from another language, through an FFI) and has no device allocator of its
+// own, and a serving loop that runs under a fixed, pre-reserved memory budget, where an allocation
+// at decode time could fail or fragment the pool. sisa_decode_attn needs a caller-provided workspace
 // for its split-K partials; this variant keeps those partials in a fixed array that the library
 // owns instead, so the caller passes only inputs and outputs.
 //
 // The array below lives in every GPU that loads this library, from module load until process exit.
-// Its device address is resolved once per device, on the first call made on that device (that
-// first call must therefore come before any stream capture that includes the entry point). All
-// calls on a device share the one array and it keeps the last call's contents: every call rewrites
-// each partial record it reads before reading it, so nothing needs clearing, but two calls that
-// overlap on the GPU (different streams, no ordering between them) race on the array and corrupt
-// each other's results.
+// Its device address is resolved once per device, on the first call made on that device, with that
+// device current; that first call should therefore come before any stream capture. A
+// cudaDeviceReset of a device unloads the module, so the address recorded for that device is stale
+// afterwards: do not call this entry point on a device that has been reset in the same process.
+// All calls on a device share the one array and it keeps the last call's contents: every call
+// rewrites each partial record it reads before reading it, so nothing needs clearing, but two calls
+// that overlap on the GPU (different streams, no ordering between them) race on the array and
+// corrupt each other's results.
 // =============================================================================================
 namespace sisa {
 namespace dec {
 constexpr int64_t kStaticRecords = 16384;        // (split, batch, head) partial records of 66 floats: 4.3 MB
 static __device__ __align__(256) float g_static_partials[kStaticRecords * 66];
 }  // namespace dec
-int capi_fail(int code, const char* msg);
 }  // namespace sisa
 
 extern "C" int sisa_decode_attn_noalloc(const sisa_view4* q, const sisa_view4* c, const float* g_q, const float* f_q,
@@ -373,37 +375,36 @@ extern "C" int sisa_decode_attn_noalloc(const sisa_view4* q, const sisa_view4* c
   using sisa::capi_fail;
   static std::mutex mu;
   static void* scratch_by_device[256] = {};
-  if (B < 1 || H < 1 || N < 1) return capi_fail(SISA_ERR_VALUE, "sisa_decode_attn_noalloc: B, H and N must be >= 1");
+  int rc;
+  // the same argument checks as sisa_decode_attn
+  if ((rc = sisa::capi_check_dims(B, H, N)) || (rc = sisa::capi_check_dtype(dtype))) return rc;
+  if ((rc = sisa::capi_check_view(q, 2, "q")) || (rc = sisa::capi_check_view(c, 2, "c")) ||
+      (rc = sisa::capi_check_view(k_cache, 2, "k_cache")) || (rc = sisa::capi_check_view(v_cache, 2, "v_cache")) ||
+      (rc = sisa::capi_check_view(b_cache, 2, "b_cache")) || (rc = sisa::capi_check_view(y, 2, "y")))
+    return rc;
   if (B * H > sisa::dec::kStaticRecords)
     return capi_fail(SISA_ERR_VALUE,
                      "sisa_decode_attn_noalloc: B*H exceeds the 16384 (batch, head) rows of the library's fixed "
                      "scratch; use sisa_decode_attn with a caller workspace");
-  if (dtype != SISA_BF16 && dtype != SISA_F16) return capi_fail(SISA_ERR_TYPE, "dtype must be SISA_BF16 or SISA_F16");
-  const sisa_view4* views[6] = {q, c, k_cache, v_cache, b_cache, y};
-  for (const sisa_view4* v : views) {
-    if (!v || !v->data) return capi_fail(SISA_ERR_VALUE, "sisa_decode_attn_noalloc: null view");
-    if ((reinterpret_cast<uintptr_t>(v->data) & 15u) || v->stride_l % 8 || v->stride_h % 8 || v->stride_b % 8)
-      return capi_fail(SISA_ERR_ALIGN, "sisa_decode_attn_noalloc: views need 16-byte rows and strides");
-  }
   if (!g_q || !g_cache || !lam) return capi_fail(SISA_ERR_VALUE, "sisa_decode_attn_noalloc: null pointer");
   if ((f_q == nullptr) != (f_cache == nullptr))
     return capi_fail(SISA_ERR_VALUE, "sisa_decode_attn_noalloc: f_q and f_cache must both be given or both be null");
   if (gf_stride < N) return capi_fail(SISA_ERR_VALUE, "sisa_decode_attn_noalloc: g/F cache row stride < N");
-  // The scratch is resolved on the device that owns the data, with that device current.
-  cudaPointerAttributes attr;
-  if (cudaPointerGetAttributes(&attr, q->data) != cudaSuccess || attr.type != cudaMemoryTypeDevice)
-    return capi_fail(SISA_ERR_VALUE, "sisa_decode_attn_noalloc: q is not device memory");
-  if (attr.device < 0 || attr.device >= 256) return capi_fail(SISA_ERR_VALUE, "sisa_decode_attn_noalloc: bad device");
-  if (cudaSetDevice(attr.device) != cudaSuccess) return capi_fail(SISA_ERR_CUDA, "sisa_decode_attn_noalloc: cudaSetDevice failed");
+  // The scratch address is resolved on the device that owns the data, with that device current; the
+  // caller's current device is restored when this call returns.
+  sisa::DeviceScope scope;
+  if ((rc = scope.bind(q->data))) return rc;
+  const int dev = scope.device();
+  if (dev < 0 || dev >= 256) return capi_fail(SISA_ERR_VALUE, "sisa_decode_attn_noalloc: bad device");
   void* scratch = nullptr;
   {
     std::lock_guard<std::mutex> lock(mu);
-    scratch = scratch_by_device[attr.device];
+    scratch = scratch_by_device[dev];
     if (!scratch) {
       const cudaError_t e = cudaGetSymbolAddress(&scratch, sisa::dec::g_static_partials);
       if (e != cudaSuccess || !scratch)
         return capi_fail(SISA_ERR_CUDA, "sisa_decode_attn_noalloc: cudaGetSymbolAddress of the fixed scratch failed");
-      scratch_by_device[attr.device] = scratch;
+      scratch_by_device[dev] = scratch;
     }
   }
   sisa::DecodeParams p{};

@@ -303,8 +303,8 @@ __global__ void __launch_bounds__(256) prep_fwd_kernel(PrepArgs a) {
       float rf[2], cf[2];
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
-        rf[r] = exp2f(fminf((v[r] - gs) * kLog2e, 0.f));
-        cf[r] = exp2f(fminf((ge - v[r]) * kLog2e, 0.f));
+        rf[r] = exp2f(fmin_nan((v[r] - gs) * kLog2e, 0.f));
+        cf[r] = exp2f(fmin_nan((ge - v[r]) * kLog2e, 0.f));
       }
       store_plane(pl, v[0], v[1]);
       store_plane(pl + 2 * a.Lp, rf[0], rf[1]);
@@ -391,8 +391,8 @@ __global__ void __launch_bounds__(256) pack_positions_kernel(PackArgs a, int nch
     gg[r] = g;
     ff[r] = fp ? __ldg(fp + (int64_t)t * a.f_sl) : 0.f;
     // NaN-propagating clamps, as the reference: a NaN g gives NaN factors.
-    rf[r] = (g != g) ? g : exp2f(fminf((g - gs) * kLog2e, 0.f));
-    cf[r] = (g != g) ? g : exp2f(fminf((ge - g) * kLog2e, 0.f));
+    rf[r] = exp2f(fmin_nan((g - gs) * kLog2e, 0.f));
+    cf[r] = exp2f(fmin_nan((ge - g) * kLog2e, 0.f));
     if (t > 0) {
       const float inc = g - __ldg(gp + (int64_t)(t - 1) * a.g_sl);
       bad |= !(inc <= 1e-3f);

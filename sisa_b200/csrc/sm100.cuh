@@ -70,10 +70,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Wait until the phase with the given parity has completed. Returns false (and records
-// SISA_ST_TIMEOUT) if that does not happen within SISA_WAIT_NS (plus, when sleeping, at most 64
-// suspend hints before the timer starts).
+// SISA_ST_TIMEOUT) if that does not happen within limit_ns of device time (plus, when sleeping, at
+// most 64 suspend hints before the timer starts).
 template <bool kSleep = false>
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t* status) {
+__device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, int32_t* status, uint64_t limit_ns) {
 #pragma unroll 1
   for (int i = 0; i < 64; ++i)
     if (mbar_try_wait<kSleep>(bar, parity)) return true;
@@ -81,11 +81,17 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t
 #pragma unroll 1
   while (true) {
     if (mbar_try_wait<kSleep>(bar, parity)) return true;
-    if (globaltimer() - t0 > SISA_WAIT_NS) {
+    if (globaltimer() - t0 > limit_ns) {
       if (status) atomicOr(status, SISA_ST_TIMEOUT);
       return false;
     }
   }
+}
+
+// The library's wait: mbar_wait_for with the SISA_WAIT_NS limit.
+template <bool kSleep = false>
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t* status) {
+  return mbar_wait_for<kSleep>(bar, parity, status, SISA_WAIT_NS);
 }
 
 // ------------------------------------------------------------------------------------ TMA
@@ -301,6 +307,15 @@ __host__ __device__ constexpr uint32_t make_idesc(int M, int N, int ab_fmt, int 
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Minimum that returns NaN when either input is NaN (fminf returns the other input). The decay clamps
+// exp(min(g_i - g_j, 0)) use it, so that a NaN in g reaches the output as the reference's clamps do
+// instead of turning into a decay factor of 1.
+__device__ __forceinline__ float fmin_nan(float a, float b) {
+  float r;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
   return r;
 }
 

@@ -224,12 +224,14 @@ class SISAAttention(nn.Module):
         H, dh, ds = self.config.n_head, self.config.d_head, self.config.d_state
         widths = (dh, dh, dh, ds, ds, ds // 2, 1)
         lins = (self.W_Q, self.W_K, self.W_V, self.W_B, self.W_C, self.theta_proj, self.alpha_proj)
-        weight = torch.cat([lin.weight for lin in lins])
-        bias = torch.cat([torch.zeros(weight.shape[0] - H, dtype=self.alpha_proj.bias.dtype,
-                                      device=self.alpha_proj.bias.device), self.alpha_proj.bias])
+        n = H * sum(widths)
+        pad = -n % 16                     # zero rows: every row of proj starts 16-byte aligned (kernel views)
+        ab = self.alpha_proj.bias
+        weight = torch.cat([lin.weight for lin in lins] + [self.W_Q.weight.new_zeros(pad, x.shape[-1])])
+        bias = torch.cat([ab.new_zeros(n - H), ab, ab.new_zeros(pad)])
         proj = F.linear(x, weight, bias)
         heads = [part.view(B, L, H, w).transpose(1, 2)
-                 for part, w in zip(proj.split([H * w for w in widths], dim=-1), widths)]
+                 for part, w in zip(proj.split([H * w for w in widths] + [pad], dim=-1), widths)]
         q, k, v, b, c, theta, alpha = heads
         z = self._forget_logits(x)
         with no_autocast(x.device.type):

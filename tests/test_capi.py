@@ -107,3 +107,11 @@ def test_norm_args_structs_match_the_c_header(tmp_path):
         assert int(got[f"{cname} size"]) == ctypes.sizeof(cls)
         for fname, _ in cls._fields_:
             assert int(got[f"{cname} {fname}"]) == getattr(cls, fname).offset, (cname, fname)
+
+
+def test_selftest_wait_rejects_bad_limits():
+    """Host-side argument checks of the diagnostic wait entry point (no kernel is launched)."""
+    lib = _lib.load()
+    assert lib.sisa_selftest_wait(0, 10, None, None, None) == _lib.ERR_VALUE
+    assert "limit_ns" in _lib.last_error()
+    assert lib.sisa_selftest_wait(0, 2_000_000_000, None, None, None) == _lib.ERR_VALUE

@@ -1,12 +1,11 @@
 """The allocation-free decode entry point, sisa_decode_attn_noalloc, against sisa_decode_attn.
 
-Some callers cannot allocate device memory at the moment they decode: code inside a CUDA-graph
-capture (allocations cannot be captured and cudaFree synchronises the device), hosts that bind
-only the C ABI and have no device allocator, and serving loops held to a fixed memory budget. For
-them the library keeps the decode kernel's split-K scratch in a fixed array of its own, and the
-caller passes only inputs and outputs. These tests call both entry points through the C ABI and
-require the same output within the decode tests' tolerance, on consecutive calls (the array keeps
-the previous call's contents), and a clear error for sizes beyond the array.
+Some callers cannot allocate device memory at the moment they decode: host programs that bind only
+the C ABI and have no device allocator of their own, and serving loops held to a fixed, pre-reserved
+memory budget. For them the library keeps the decode kernel's split-K scratch in a fixed array of
+its own, and the caller passes only inputs and outputs. These tests call both entry points through
+the C ABI and require the same output within the decode tests' tolerance, on consecutive calls (the
+array keeps the previous call's contents), and a clear error for sizes beyond the array.
 
 This file is collected last so that a stop-at-first-failure run has already run every other test.
 """
