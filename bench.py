@@ -14,8 +14,15 @@ buffer sets, separate copy streams).
 
 ``train``: the second half of the metric, 12-layer sisa-152m training (d=768, H=12, d_ff=2744, vocab
 50277, reference initialisation) with per-rank batch 8 x 2048 uniform random ids, bf16 autocast, fused
-AdamW, clipping, fused linear-CE, data-parallel over the N ranks (DDP, NCCL allreduce overlapped with the
-backward). tokens/s = all ranks' input tokens / max-over-ranks step time.
+AdamW, clipping, fused linear-CE, data-parallel over the N ranks: the whole step is one CUDA graph per
+rank, and the fp32 gradients are averaged by NCCL allreduces of buckets issued on a second captured
+stream as the backward finishes each bucket (sisa_b200/dp.py). tokens/s = all ranks' input tokens /
+max-over-ranks step time.
+
+On one GPU the default run also reports BASELINE config 2 (``lce``: chunked linear-CE fwd+bwd) and
+config 4 (``decode``: prefill and graphed decode steps of the 12-layer model), and ``incumbent``: the
+reference's own Triton ``sisa_fused`` (installed under baseline/_ref) on the same cfg1 inputs, each with
+the reference's GPU number beside it where the reference has that path.
 
 ``--impl reference``: the reference's pure-PyTorch CPU algorithm (the oracle port) on the host cores,
 on a bounded sample of the same workload (a subset of (batch, head) units at the full T).
@@ -40,8 +47,8 @@ B, T, H = 8, 4096, 16
 FLOP_PER_PAIR = 1152
 FWD_FLOP_PER_PAIR = 320
 # DRAM bytes (read + write) of attn_fwd + attn_bwd_dq + attn_bwd_dkv for one cfg1 step: ncu
-# dram__bytes_read.sum + dram__bytes_write.sum at B=1, H=8, T=4096 (profiles/attn_kernels_B1T4096H8_ncu.md),
-# scaled by the number of (batch, head, position) units; the traffic per unit does not depend on B or H.
+# dram__bytes_read.sum + dram__bytes_write.sum of one capture at B=1, H=8, T=4096, scaled by the number
+# of (batch, head, position) units; the traffic per unit does not depend on B or H.
 ATTN_TRAFFIC_PER_UNIT = 1.1537e9 / (8 * 16 * 4096)
 METRIC = "SISA attn fwd+bwd TFLOP/s (T=4096 bf16)"
 
@@ -59,49 +66,96 @@ def measured_peaks():
 
 
 class Clocks:
-    """Samples nvidia-smi clocks / throttle reasons during the timed region."""
+    """Samples the SM clock and the clock-event (throttle) reasons of one GPU through NVML every
+    ``period`` seconds on a background thread, from ``start()`` to ``stop()``. ``window(name)`` marks a
+    region (the timed steps); ``summary(name)`` reports the samples inside it."""
 
-    def __init__(self, index):
-        self.index = index
-        self.proc = None
-        self.path = Path(f"/tmp/sisa_clocks_{os.getpid()}.csv")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("hw_power_brake_slowdown", "nvmlClocksEventReasonHwPowerBrakeSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
-    def __enter__(self):
+    def __init__(self, device_index, period=0.004):
+        self.period = period
+        self.samples = []          # (host time, sm MHz, reason bits)
+        self.windows = {}
+        self.max_mhz = None
+        self._stop = None
+        self._thread = None
+        self._nvml = None
+        self._handle = None
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}",
-                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
-                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            handle = None
+            try:
+                uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+                handle = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:  # noqa: BLE001
+                handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self._nvml, self._handle = pynvml, handle
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM))
+        except Exception:  # noqa: BLE001
+            self._nvml = None
+
+    def _run(self):
+        nv, h = self._nvml, self._handle
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((time.perf_counter(), float(mhz), int(bits)))
+            except Exception:  # noqa: BLE001
+                pass
+            self._stop.wait(self.period)
+
+    def start(self):
+        if self._nvml is not None and self._thread is None:
+            import threading
+
+            self._stop = threading.Event()
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
         return self
 
-    def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+    def stop(self):
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+            self._thread = None
 
-    def summary(self):
-        if self.proc is None or not self.path.exists():
+    def __enter__(self):
+        return self.start()
+
+    def __exit__(self, *a):
+        self.stop()
+
+    def window(self, name):
+        clk = self
+
+        class _W:
+            def __enter__(self):
+                clk.windows[name] = [time.perf_counter(), None]
+
+            def __exit__(self, *a):
+                clk.windows[name][1] = time.perf_counter()
+        return _W()
+
+    def summary(self, name=None):
+        if self._nvml is None:
             return None
-        rows = []
-        for line in self.path.read_text().splitlines():
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) == 7:
-                rows.append(parts)
+        rows = self.samples
+        if name is not None and name in self.windows and self.windows[name][1] is not None:
+            t0, t1 = self.windows[name]
+            rows = [r for r in rows if t0 <= r[0] <= t1]
         if not rows:
             return None
-        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i].lower() == "active"})
-        mx = float(rows[0][1]) if rows[0][1].replace(".", "").isdigit() else None
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": reasons,
-                "samples": len(rows)}
+        reasons = sorted({label for _, _, bits in rows for label, const in self.REASONS
+                          if bits & getattr(self._nvml, const, 0)})
+        return {"sm_mhz": statistics.median(r[1] for r in rows), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(rows), "window": name or "whole run", "source": f"NVML every {self.period * 1e3:.0f} ms"}
 
 
 def dist_setup(n):
@@ -220,6 +274,7 @@ def run_cuda(args):
     step = Step(dev, b=args.B, t=args.T, h=args.H, seed=1234 + rank)
     stream = torch.cuda.current_stream(dev)
     st = stream.cuda_stream
+    clk = Clocks(local).start()          # sampled through the whole run; the timed steps are a window
     for _ in range(args.warmup):
         step.run(st)
     torch.cuda.synchronize(dev)
@@ -230,7 +285,7 @@ def run_cuda(args):
         torch.distributed.barrier()
     torch.cuda.synchronize(dev)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(local) as clk:
+    with clk.window("timed"):
         start.record()
         for k in range(args.steps):
             step.run(st, evs[k])
@@ -253,9 +308,26 @@ def run_cuda(args):
     # ---- e2e: host buffers in and out through the same C-ABI calls
     e2e = None if args.no_e2e else run_e2e(step, dev, args, world)
     proj_mb = step.proj.numel() * 2 / 1e6
+    inputs = (step.proj, step.z, step.lam, step.dy)
     del step
     torch.cuda.empty_cache()
-    train = None if args.no_train else run_train(args, rank, world, dev)
+    # BASELINE configs 2 and 4 and the reference's own GPU path, on one GPU only (replicas add nothing)
+    extra = {}
+    if world == 1 and not args.no_extra:
+        extra["incumbent"] = incumbent_leg(inputs, args)
+        del inputs
+        torch.cuda.empty_cache()
+        extra["lce"] = lce_leg(args, dev)
+        torch.cuda.empty_cache()
+        extra["decode"] = decode_leg(args, dev, steps=args.extra_decode_steps)
+        torch.cuda.empty_cache()
+    else:
+        del inputs
+    with clk.window("train"):
+        train = None if args.no_train else run_train(args, rank, world, dev)
+    clk.stop()
+    if train is not None:
+        train["clocks"] = clk.summary("train")
 
     if rank == 0:
         burst, sustained, hbm, src = measured_peaks()
@@ -283,8 +355,9 @@ def run_cuda(args):
                          "hbm_peak_gbs": hbm},
             "e2e": e2e,
             "train": train,
+            **extra,
             "gpu_launches": 8 * args.steps,
-            "clocks": clk.summary(),
+            "clocks": clk.summary("timed"),
         }
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(H)
@@ -326,6 +399,7 @@ def run_train(args, rank, world, dev):
     ms = float(ms.item()) / k_steps
     tok_s = world * bt * tt / (ms * 1e-3)
     burst, sustained, _, _ = measured_peaks()
+    trainer_buckets = trainer._buckets.bounds if trainer._buckets is not None else []
     trainer.close()                     # the graph holds NCCL work: release it before the group goes
     del trainer, model
     torch.cuda.empty_cache()
@@ -333,9 +407,9 @@ def run_train(args, rank, world, dev):
             "ms_per_step": round(ms, 3), "steps": k_steps, "per_rank_batch": [bt, tt], "model": "sisa-152m",
             "params": cfg.num_parameters(), "loss_last": round(float(loss), 4),
             "mfu_vs_sustained": round(tok_s * TRAIN_FLOP_PER_TOKEN / (world * sustained * 1e12), 4),
-            "parallelism": (f"dp{world} (whole step as one CUDA graph per rank: flat fp32 gradients, one "
-                            "NCCL allreduce inside the graph)" if world > 1
-                            else "dp1 (whole step as one CUDA graph)")}
+            "parallelism": (f"dp{world} (whole step as one CUDA graph per rank: flat fp32 gradients in "
+                            f"{len(trainer_buckets)} buckets, each allreduced by NCCL on a side stream as the "
+                            "backward finishes it)" if world > 1 else "dp1 (whole step as one CUDA graph)")}
 
 
 def run_e2e(step, dev, args, world):
@@ -441,45 +515,119 @@ def cpu_baseline(heads, budget_s=10.0, max_steps=64):
                       f"fp32, {dt:.1f} s"}
 
 
-def run_lce(args):
-    """cfg2: chunked linear-CE fwd+bwd, hidden [16384 x 1024] bf16 ~ N(0,1), weight [50277 x 1024] fp32 ~ N(0, 0.02^2)
-    under bf16 autocast, labels uniform. Metric: tokens/s (and TFLOP/s on 6 N V D)."""
+def _ref_import():
+    """The reference package (tlstngud/sisa, Triton kernels) from baseline/_ref, or an import error."""
+    ref = ROOT / "baseline" / "_ref"
+    if not (ref / "sisa").is_dir():
+        raise ImportError("baseline/_ref is not installed")
+    if str(ref) not in sys.path:
+        sys.path.insert(0, str(ref))
+    import sisa as sisa_ref   # noqa: F401
+
+    return sisa_ref
+
+
+def _time_cuda(fn, steps, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s_.record()
+    for _ in range(steps):
+        fn()
+    e_.record()
+    torch.cuda.synchronize()
+    return s_.elapsed_time(e_) / steps
+
+
+def incumbent_leg(inputs, args):
+    """The reference's own GPU path on the same cfg1 inputs: its Triton ``sisa_fused`` forward + backward
+    (src/sisa/kernels/fused_prep.py:637) through its autograd function, CUDA-event timed on this GPU."""
+    try:
+        sisa_ref = _ref_import()
+        from sisa.kernels.fused_prep import sisa_fused as ref_fused
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"reference package: {type(e).__name__}: {e}"[:200]}
+    proj, z, lam, dy = inputs
+    H = lam.shape[0]
+    P = proj.detach().clone().requires_grad_(True)
+    Z = z.detach().clone().requires_grad_(True)
+    LAM = lam.detach().clone().requires_grad_(True)
+
+    def step():
+        y = ref_fused(P, Z, LAM, H)
+        y.backward(dy)
+        P.grad = Z.grad = LAM.grad = None
+
+    try:
+        ms = _time_cuda(step, steps=max(3, min(args.steps, 10)), warmup=2)
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"reference Triton path failed: {type(e).__name__}: {e}"[:200]}
+    b_, t_ = proj.shape[0], proj.shape[1]
+    return {"impl": f"reference sisa_fused (Triton, sisa {getattr(sisa_ref, '__version__', '?')}) from baseline/_ref",
+            "value": round(FLOP_PER_PAIR * pairs(b_, H, t_) / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+            "ms_per_step": round(ms, 4), "note": "same inputs as the timed cfg1 step, autograd forward + backward"}
+
+
+def lce_leg(args, dev, steps=None):
+    """cfg2: chunked linear-CE fwd+bwd, hidden [16384 x 1024] bf16 ~ N(0,1), weight [50277 x 1024] fp32
+    ~ N(0, 0.02^2) under bf16 autocast, labels uniform. tokens/s and TFLOP/s on 6 N V D, peak memory,
+    and the reference's Triton linear-CE on the same inputs."""
     from sisa_b200.kernels.linear_ce import linear_cross_entropy
 
-    dev = torch.device("cuda", 0)
     N, D, V = args.lce_tokens, 1024, 50277
     g = torch.Generator(device=dev).manual_seed(0)
     h = torch.randn((N, D), generator=g, device=dev).to(torch.bfloat16).requires_grad_(True)
     w = (torch.randn((V, D), generator=g, device=dev) * 0.02).requires_grad_(True)
     lab = torch.randint(0, V, (N,), generator=g, device=dev)
 
-    def step():
-        with torch.autocast("cuda", dtype=torch.bfloat16):
-            loss = linear_cross_entropy(h, w, lab)
-        loss.backward()
-        h.grad = None
-        w.grad = None
-        return loss
+    def make_step(fn):
+        def step():
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                loss = fn(h, w, lab)
+            loss.backward()
+            h.grad = None
+            w.grad = None
+        return step
 
-    for _ in range(args.warmup):
+    k = steps or max(3, min(args.steps, 30))
+    step = make_step(linear_cross_entropy)
+    for _ in range(max(args.warmup, 2)):
         step()
     torch.cuda.synchronize()
     base = torch.cuda.memory_allocated()
     torch.cuda.reset_peak_memory_stats()
-    s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    k = max(3, min(args.steps, 30))
-    with Clocks(0) as clk:
-        s_.record()
-        for _ in range(k):
-            step()
-        e_.record()
-        torch.cuda.synchronize()
-    ms = s_.elapsed_time(e_) / k
+    ms = _time_cuda(step, steps=k, warmup=0)
     peak = torch.cuda.max_memory_allocated() - base
-    print(json.dumps({"metric": "linear-CE fwd+bwd tokens/s (cfg2)", "value": round(N / (ms * 1e-3), 1),
-                      "unit": "tokens/s", "ms_per_step": round(ms, 3), "tflops": round(6 * N * V * D / (ms * 1e9), 1),
-                      "peak_mem_mb": round(peak / 2**20, 1), "steps": k, "config": {"N": N, "D": D, "V": V},
-                      "clocks": clk.summary()}))
+    out = {"metric": "linear-CE fwd+bwd tokens/s (cfg2)", "value": round(N / (ms * 1e-3), 1), "unit": "tokens/s",
+           "ms_per_step": round(ms, 3), "tflops": round(6 * N * V * D / (ms * 1e9), 1),
+           "peak_mem_mb": round(peak / 2**20, 1), "steps": k, "config": {"N": N, "D": D, "V": V}}
+    try:
+        _ref_import()
+        from sisa.kernels.linear_ce import linear_cross_entropy as ref_lce
+
+        ref_step = make_step(ref_lce)
+        for _ in range(2):
+            ref_step()
+        torch.cuda.synchronize()
+        base = torch.cuda.memory_allocated()
+        torch.cuda.reset_peak_memory_stats()
+        rms = _time_cuda(ref_step, steps=k, warmup=0)
+        rpeak = torch.cuda.max_memory_allocated() - base
+        out["incumbent"] = {"impl": "reference linear_cross_entropy (Triton) from baseline/_ref",
+                            "ms_per_step": round(rms, 3), "value": round(N / (rms * 1e-3), 1), "unit": "tokens/s",
+                            "peak_mem_mb": round(rpeak / 2**20, 1)}
+    except Exception as e:  # noqa: BLE001
+        out["incumbent"] = {"unavailable": f"{type(e).__name__}: {e}"[:200]}
+    return out
+
+
+def run_lce(args):
+    dev = torch.device("cuda", 0)
+    with Clocks(0) as clk:
+        out = lce_leg(args, dev)
+    out["clocks"] = clk.summary()
+    print(json.dumps(out))
 
 
 def run_norm(args):
@@ -539,16 +687,17 @@ def run_norm(args):
                       "clocks": clk.summary()}))
 
 
-def run_decode(args):
-    """cfg4: 12-layer sisa-152m, random init, bf16 weights; batch 64, prompt 8192 ids (id 0 first), greedy decode.
-    Reports prefill tokens/s and per-step decode latency with the cache bytes read per step."""
+def decode_leg(args, dev, steps=None):
+    """cfg4: 12-layer sisa-152m, random init, bf16 weights; batch 64, prompt 8192 ids (id 0 first), then
+    greedy decode steps. Prefill tokens/s and per-step decode latency (CUDA-graph replay of the whole step)
+    with the cache and weight bytes read per step."""
     import sisa_b200 as sisa
     from sisa_b200.generation import DecodeGraph, SISACache
 
-    dev = torch.device("cuda", 0)
-    Bd, P, S = args.decode_batch, args.decode_prompt, args.decode_steps
+    Bd, P = args.decode_batch, args.decode_prompt
+    S = steps or args.decode_steps
     if S < 10:
-        raise ValueError("--decode-steps must be >= 10 (1 + 4 eager, 2 warm-up graph steps, then timed steps)")
+        raise ValueError("decode steps must be >= 10 (1 + 4 eager, 2 warm-up graph steps, then timed steps)")
     cfg = sisa.SISAConfig.preset("sisa-152m", attn_impl="cuda")
     torch.manual_seed(0)
     model = sisa.SISAForCausalLM(cfg).to(dev).to(torch.bfloat16).eval()
@@ -587,26 +736,33 @@ def run_decode(args):
             nxt = graph.step(nxt).float().argmax(-1)
         torch.cuda.synchronize()
         n = S - 3 - n_eager
-        with Clocks(0) as clk:
-            s_.record()
-            for _ in range(n):
-                nxt = graph.step(nxt).float().argmax(-1)
-            e_.record()
-            torch.cuda.synchronize()
+        s_.record()
+        for _ in range(n):
+            nxt = graph.step(nxt).float().argmax(-1)
+        e_.record()
+        torch.cuda.synchronize()
         step_ms = s_.elapsed_time(e_) / n
         graph.close()
+    del cache, model
     L_avg = P + 3 + n_eager + n / 2
     per_tok = cfg.n_layer * cfg.n_head * (64 * 2 * 2 + 32 * 2 + 8)   # k, v, b~ (bf16) + g, F (fp32)
     cache_bytes = Bd * L_avg * per_tok
     weight_bytes = 2 * (cfg.num_parameters())
-    print(json.dumps({"metric": "decode step latency (cfg4)", "value": round(step_ms, 3), "unit": "ms/step",
-                      "prefill_tokens_s": round(Bd * P / (prefill_ms * 1e-3), 1), "prefill_ms": round(prefill_ms, 1),
-                      "decode_steps_timed": n, "eager_ms_per_step": round(eager_ms, 3),
-                      "timing": "CUDA graph replay of the whole decode step (DecodeGraph)",
-                      "cache_bytes_per_step": int(cache_bytes),
-                      "hbm_gbs": round((cache_bytes + weight_bytes) / (step_ms * 1e-3) / 1e9, 1),
-                      "config": {"batch": Bd, "prompt": P, "new_tokens": S, "model": "sisa-152m"},
-                      "clocks": clk.summary()}))
+    return {"metric": "decode step latency (cfg4)", "value": round(step_ms, 3), "unit": "ms/step",
+            "prefill_tokens_s": round(Bd * P / (prefill_ms * 1e-3), 1), "prefill_ms": round(prefill_ms, 1),
+            "decode_steps_timed": n, "eager_ms_per_step": round(eager_ms, 3),
+            "timing": "CUDA graph replay of the whole decode step (DecodeGraph)",
+            "cache_bytes_per_step": int(cache_bytes),
+            "hbm_gbs": round((cache_bytes + weight_bytes) / (step_ms * 1e-3) / 1e9, 1),
+            "config": {"batch": Bd, "prompt": P, "new_tokens": S, "model": "sisa-152m"}}
+
+
+def run_decode(args):
+    dev = torch.device("cuda", 0)
+    with Clocks(0) as clk:
+        out = decode_leg(args, dev)
+    out["clocks"] = clk.summary()
+    print(json.dumps(out))
 
 
 def run_reference(args):
@@ -645,6 +801,9 @@ def main(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-train", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the config 2 / config 4 legs and the reference Triton incumbent of the default run")
+    ap.add_argument("--extra-decode-steps", type=int, default=48, help="decode steps of the default run's cfg4 leg")
     ap.add_argument("--workload", choices=["attn", "lce", "decode", "norm"], default="attn",
                     help="attn (default: config 1 + the config 3 training leg), lce (config 2), decode (config 4), "
                          "norm (the fused block-boundary norms of config 3)")
