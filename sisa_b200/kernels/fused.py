@@ -11,7 +11,7 @@ import torch
 
 from .. import _lib, backends
 
-__all__ = ["sisa_fused", "fused_layout", "concat_fused_weights", "fused_projection"]
+__all__ = ["sisa_fused", "fused_layout", "concat_fused_weights", "fused_projection", "prefill_layer"]
 
 D_HEAD = 64
 D_STATE = 32
@@ -182,6 +182,37 @@ class _SISAFusedFn(torch.autograd.Function):
         _lib.check(rc, "sisa_prep_bwd")
         backends.after_call(dev)
         return dproj, dz, dlam, None
+
+
+def prefill_layer(proj: torch.Tensor, z: torch.Tensor, lam: torch.Tensor, n_head: int):
+    """The layer core over a whole prompt without autograd, keeping what a decode cache needs: the
+    preparation kernel and the tcgen05 forward (no o'' - nothing will run a backward), on the fused
+    projection ``proj`` (B, L, NPAD) and forget logits ``z`` (B, L, H) fp32.
+
+    The reference fills its cache through the unfused path instead (src/sisa/modeling.py:226-232: seven
+    projections, torch recurrences and rotations). Returns ``y`` (B, L, H*64) and the cache entries:
+    k, v (views of proj's K/V columns), b~ (B, H, L, 32) as the kernels rotated it, g and F (views of the
+    position planes) and Phi at the last position (B, H, 16) fp32."""
+    lib = _lib.load()
+    H = int(n_head)
+    B, L, _ = proj.shape
+    dev = proj.device
+    off = fused_layout(H)
+    c_rot, b_rot, pos, _ = prep_forward(proj, z, H)
+    q, k, v = _heads(proj, off["Q"], H, 64), _heads(proj, off["K"], H, 64), _heads(proj, off["V"], H, 64)
+    o = torch.empty_strided((B, H, L, D_HEAD), (L * H * D_HEAD, D_HEAD, H * D_HEAD, 1), device=dev, dtype=proj.dtype)
+    lse = torch.empty((B, H, L), device=dev, dtype=torch.float32)
+    st = backends.status_word(dev)
+    vq, vk, vv, vc, vb, vo = (_lib.view4(t) for t in (q, k, v, c_rot, b_rot, o))
+    rc = lib.sisa_attn_fwd(_lib.vref(vq), _lib.vref(vk), _lib.vref(vv), _lib.vref(vc), _lib.vref(vb),
+                           pos.data_ptr(), lam.data_ptr(), B, H, L, _lib.dtype_code(proj.dtype), _lib.vref(vo),
+                           lse.data_ptr(), None, st.data_ptr(), _lib.stream_ptr(dev))
+    _lib.check(rc, "sisa_attn_fwd")
+    backends.after_call(dev)
+    theta = proj[..., off["TH"]:off["TH"] + H * (D_STATE // 2)]
+    phi_last = theta.float().sum(dim=1).view(B, H, D_STATE // 2)
+    y = o.transpose(1, 2).reshape(B, L, H * D_HEAD)
+    return y, (k, v, b_rot, pos[:, :, 0, :L], pos[:, :, 1, :L], phi_last)
 
 
 def sisa_fused(proj: torch.Tensor, z: torch.Tensor | None, lam: torch.Tensor, n_head: int) -> torch.Tensor:

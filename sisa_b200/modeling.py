@@ -294,6 +294,28 @@ class SISAAttention(nn.Module):
         lam = _static(self, "_lam_static", lambda t: F.softplus(t).float(), self.lambda_raw)
         return self._output(decode_attention(q, c, g, fgate, state, lam))
 
+    def _prefill_fused(self, x: Tensor, cache: "SISACache", z: Tensor | None = None) -> Tensor:
+        """A prompt into an empty cache on the CUDA path: one projection GEMM over the concatenated
+        weights, the preparation kernel and the tcgen05 forward (kernels/fused.py ``prefill_layer``), with
+        the cache filled from their outputs. ``z`` is the forget projection of ``x`` when the caller
+        computed it already (the block norm does)."""
+        from .kernels.fused import prefill_layer
+
+        weight, bias = self._fused_weights_static()
+        proj = F.linear(x, weight, bias)
+        lam = _static(self, "_lam_static", lambda t: F.softplus(t).float(), self.lambda_raw)
+        y, (k, v, b, g, fgate, phi) = prefill_layer(proj, self._forget_logits(x) if z is None else z, lam,
+                                                     self.config.n_head)
+        cache.update(self.layer_idx, k=k, v=v, b=b, g=g, fgate=fgate, phi=phi)
+        return self.W_O(y)
+
+    def _use_fused_prefill(self, x: Tensor, state, requested: str) -> bool:
+        """A prompt into an empty cache on the CUDA path without autograd, in a low-precision compute
+        dtype (the cache takes the projection's dtype)."""
+        return (state is None and x.is_cuda and not torch.is_grad_enabled()
+                and _compute_dtype(x) in (torch.bfloat16, torch.float16)
+                and _resolve_impl(requested, x, self.config) == "cuda")
+
     def _use_fused_decode(self, x: Tensor, state, requested: str) -> bool:
         """One new token on the CUDA path without autograd, into a cache of the compute dtype."""
         return (state is not None and x.shape[1] == 1 and x.is_cuda and not torch.is_grad_enabled()
@@ -303,6 +325,8 @@ class SISAAttention(nn.Module):
         state = cache.get(self.layer_idx)
         if self._use_fused_decode(x, state, requested):
             return self._decode_fused(x, state)
+        if self._use_fused_prefill(x, state, requested):
+            return self._prefill_fused(x, cache)
         q, k, v, c, b, g, fgate, phi = self._prepare(x, state)
         if state is None:
             impl = _resolve_impl(requested, x, self.config)
@@ -378,10 +402,23 @@ class SISABlock(nn.Module):
         return (x.shape[1] == 1 and _fused_kernels(x, self.config)
                 and self.attn._use_fused_decode(x, cache.get(self.attn.layer_idx), self.config.attn_impl))
 
-    def decode_pair(self, x: Tensor, m: Tensor | None, cache: "SISACache") -> tuple[Tensor, Tensor]:
+    def prefill_pair_path(self, x: Tensor, cache: "SISACache") -> bool:
+        """Whether :meth:`prefill_pair` serves the prompt ``x``: the norm kernels run and the attention
+        fills an empty cache through the fused layer core."""
+        return (_fused_kernels(x, self.config)
+                and self.attn._use_fused_prefill(x, cache.get(self.attn.layer_idx), self.config.attn_impl))
+
+    def prefill_pair(self, x: Tensor, m: Tensor | None, cache: "SISACache") -> tuple[Tensor, Tensor]:
+        """The prompt pass of the block in :meth:`decode_pair`'s form, the attention through the fused
+        layer core into an empty cache."""
+        return self.decode_pair(x, m, cache, prefill=True)
+
+    def decode_pair(self, x: Tensor, m: Tensor | None, cache: "SISACache",
+                    prefill: bool = False) -> tuple[Tensor, Tensor]:
         """One decode step of the block in :meth:`forward_pair`'s form: the previous block's residual add
         is folded into the attention norm, which also computes the forget projection in fp32 from its
-        rounded output (the value the eager step's ``F.linear(h.float(), ...)`` reads)."""
+        rounded output (the value the eager step's ``F.linear(h.float(), ...)`` reads). With ``prefill``
+        the rows are a prompt and the attention fills the empty cache instead of decoding one token."""
         from .kernels.norm import block_norm, swiglu
 
         attn, ffn = self.attn, self.ffn
@@ -392,7 +429,7 @@ class SISABlock(nn.Module):
             xs = x
         else:
             xs, h, z = block_norm(x, wa, self.attn_norm.eps, res=m, proj=(pw, pb))
-        a = attn._decode_fused(h, cache.get(attn.layer_idx), z)
+        a = attn._prefill_fused(h, cache, z) if prefill else attn._decode_fused(h, cache.get(attn.layer_idx), z)
         xs, f_in = block_norm(xs, wf, self.ffn_norm.eps, res=a)
         # gate and up projections as one GEMM over the concatenated weights, the activation on its halves
         w_gu = _static(ffn, "_gate_up_static", lambda g, u: torch.cat([g, u]), ffn.w_gate.weight, ffn.w_up.weight)
@@ -466,6 +503,15 @@ class SISAModel(nn.Module):
             from .kernels.norm import block_norm
 
             return block_norm(x, self.final_norm.weight, self.final_norm.eps, res=m, keep_sum=False)[0]
+        if (cache is not None and len(self.layers) and x.shape[1] > 1
+                and all(layer.prefill_pair_path(x, cache) for layer in self.layers)):
+            from .kernels.norm import block_norm
+
+            m = None
+            for layer in self.layers:
+                x, m = layer.prefill_pair(x, m, cache)
+            (wn,) = _static(self, "_final_fp32", _fp32, self.final_norm.weight)
+            return block_norm(x, wn, self.final_norm.eps, res=m, keep_sum=False)[0]
         if cache is not None and len(self.layers) and all(layer.decode_pair_path(x, cache) for layer in self.layers):
             from .kernels.norm import block_norm
 

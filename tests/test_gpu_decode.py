@@ -113,6 +113,48 @@ def test_fused_decode_step_matches_unfused_glue(cuda_dev, monkeypatch):
         assert max_abs(sg.phi.reshape(sw.phi.shape).cpu(), sw.phi.float().cpu()) <= 1e-3
 
 
+def test_fused_prefill_matches_unfused_glue(cuda_dev, monkeypatch):
+    """The prompt pass through the fused layer core (one projection GEMM, sisa_prep_fwd, sisa_attn_fwd, the
+    cache filled from their outputs, block norms on the norm kernels) against the unfused glue of the
+    reference's prefill (separate projections, torch recurrences and rotations, the unfused attention):
+    the last position's logits, every cache entry, and three decode steps from each cache."""
+    from sisa_b200 import modeling
+    from sisa_b200.generation import SISACache
+
+    model = _tiny(cuda_dev, "cuda").to(cuda_dev).to(torch.bfloat16)
+    ids = torch.randint(0, 97, (3, 203), generator=torch.Generator().manual_seed(5)).to(cuda_dev)
+
+    def run(fused):
+        if not fused:
+            monkeypatch.setattr(modeling.SISAAttention, "_use_fused_prefill", lambda self, x, state, requested: False)
+        cache = SISACache(capacity=210)
+        out = []
+        with torch.no_grad():
+            out.append(model(ids[:, :200], cache=cache, logits_to_keep=1).logits[:, -1].float())
+            for t in range(200, 203):
+                out.append(model(ids[:, t:t + 1], cache=cache, logits_to_keep=1).logits[:, -1].float())
+        monkeypatch.undo()
+        return out, cache
+
+    got, cg = run(True)
+    want, cw = run(False)
+    for a, b in zip(got, want):
+        assert max_abs(a.cpu(), b.cpu()) <= 2e-2
+    for i in range(2):
+        sg, sw = cg.get(i), cw.get(i)
+        assert sg.length == sw.length == 203
+        for name in ("k", "v", "b"):
+            assert max_abs(getattr(sg, name).float().cpu(), getattr(sw, name).float().cpu()) <= 2e-2, name
+        for name in ("g", "fgate"):
+            # cumulative sums over 200 positions of gate values that the two paths round through different
+            # GEMMs: compare relative to the sums' size
+            a, b = getattr(sg, name).cpu(), getattr(sw, name).cpu()
+            assert max_abs(a, b) <= 1e-4 * float(b.abs().max()) + 1e-3, name
+        # Phi at the last position sums theta (|theta| up to ~4 in this model) over the prompt; one element
+        # rounded one bf16 step apart by the two GEMMs moves it by 2^-5, a missing token by ~|theta|
+        assert max_abs(sg.phi.reshape(sw.phi.shape).float().cpu(), sw.phi.float().cpu()) <= 0.1
+
+
 def _prefilled(model, ids, n_prompt, capacity):
     from sisa_b200.generation import SISACache
 
