@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import torch
 
-from .. import _lib, backends
+from .. import ops
 
 __all__ = ["sisa_attention_cuda"]
 
@@ -26,65 +26,26 @@ def _aligned(t: torch.Tensor) -> torch.Tensor:
 
 
 def pack_positions(g: torch.Tensor, fgate: torch.Tensor | None) -> torch.Tensor:
-    lib = _lib.load()
-    B, H, L = g.shape
-    pos = _lib.pos_planes(B, H, L, g.device)
-    st = backends.status_word(g.device)
-    fs = fgate.stride() if fgate is not None else (0, 0, 0)
-    rc = lib.sisa_pack_positions(g.data_ptr(), *g.stride(), _lib.ptr(fgate), *fs, B, H, L, pos.data_ptr(),
-                                 st.data_ptr(), _lib.stream_ptr(g.device))
-    _lib.check(rc, "sisa_pack_positions")
-    return pos
+    return ops.pack_positions(g, fgate)
 
 
 class _SISAAttentionFn(torch.autograd.Function):
+    """Unfused attention on the ``sisa_b200`` operators: pack_positions + attn_fwd, backward attn_bwd."""
+
     @staticmethod
     def forward(ctx, q, k, v, c, b, g, lam, fgate):
-        lib = _lib.load()
-        B, H, L, _ = q.shape
-        dev = q.device
-        pos = pack_positions(g, fgate)
-        o = torch.empty_strided((B, H, L, D_HEAD), (L * H * D_HEAD, D_HEAD, H * D_HEAD, 1), device=dev, dtype=q.dtype)
-        lse = torch.empty((B, H, L), device=dev, dtype=torch.float32)
-        need = any(ctx.needs_input_grad)
-        o32 = torch.empty((B, H, L, D_HEAD), device=dev, dtype=torch.float32) if need else None
-        st = backends.status_word(dev)
-        vs = [_lib.view4(t) for t in (q, k, v, c, b, o)]
-        r = [_lib.vref(x) for x in vs]
-        rc = lib.sisa_attn_fwd(r[0], r[1], r[2], r[3], r[4], pos.data_ptr(), lam.data_ptr(), B, H, L,
-                               _lib.dtype_code(q.dtype), r[5], lse.data_ptr(), _lib.ptr(o32), st.data_ptr(),
-                               _lib.stream_ptr(dev))
-        _lib.check(rc, "sisa_attn_fwd")
-        backends.after_call(dev)
+        pos = ops.pack_positions(g, fgate)
+        o, lse, o32 = ops.attn_fwd(q, k, v, c, b, pos, lam, any(ctx.needs_input_grad))
         ctx.save_for_backward(q, k, v, c, b, pos, lam, o, lse, o32)
         ctx.has_f = fgate is not None
         return o
 
     @staticmethod
     def backward(ctx, do):
-        lib = _lib.load()
         q, k, v, c, b, pos, lam, o, lse, o32 = ctx.saved_tensors
-        B, H, L, _ = q.shape
-        dev = q.device
         do = _aligned(do.to(q.dtype))
-        dq, dk, dv = (torch.empty((B, H, L, D_HEAD), device=dev, dtype=q.dtype) for _ in range(3))
-        f32 = dict(device=dev, dtype=torch.float32)
-        dc = torch.empty((B, H, L, D_STATE), **f32)
-        db = torch.empty((B, H, L, D_STATE), **f32)
-        dg = torch.empty((B, H, L), **f32)
-        dF = torch.empty((B, H, L), **f32) if ctx.has_f else None
-        dlam = torch.empty((H,), **f32)
-        ws = torch.empty(max(lib.sisa_attn_bwd_workspace(B, H, L), 16), dtype=torch.uint8, device=dev)
-        st = backends.status_word(dev)
-        vs = [_lib.view4(t) for t in (q, k, v, c, b, o, do, dq, dk, dv, dc, db)]
-        r = [_lib.vref(x) for x in vs]
-        rc = lib.sisa_attn_bwd(r[0], r[1], r[2], r[3], r[4], pos.data_ptr(), lam.data_ptr(), r[5], r[6],
-                               lse.data_ptr(), _lib.ptr(o32), B, H, L, _lib.dtype_code(q.dtype),
-                               r[7], r[8], r[9], r[10], r[11], dg.data_ptr(), _lib.ptr(dF), dlam.data_ptr(),
-                               ws.data_ptr(), st.data_ptr(), _lib.stream_ptr(dev))
-        _lib.check(rc, "sisa_attn_bwd")
-        backends.after_call(dev)
-        return dq, dk, dv, dc, db, dg, dlam, dF
+        dq, dk, dv, dc, db, dg, dlam, dF = ops.attn_bwd(q, k, v, c, b, pos, lam, o, do, lse, o32, ctx.has_f)
+        return dq, dk, dv, dc, db, dg, dlam, (dF if ctx.has_f else None)
 
 
 def _prepare_inputs(q, k, v, c, b, g, lam, fgate):

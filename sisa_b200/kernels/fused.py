@@ -9,7 +9,7 @@ from __future__ import annotations
 
 import torch
 
-from .. import _lib, backends
+from .. import ops
 
 __all__ = ["sisa_fused", "fused_layout", "concat_fused_weights", "fused_projection", "prefill_layer"]
 
@@ -22,13 +22,7 @@ def fused_layout(n_head: int, d_head: int = D_HEAD, d_state: int = D_STATE) -> d
     ``[Q H*64 | K H*64 | V H*64 | B H*32 | C H*32 | TH H*16 | A H | zero padding to a multiple of 16]``."""
     if d_head != D_HEAD or d_state != D_STATE:
         raise ValueError(f"the fused kernels support d_head={D_HEAD} and d_state={D_STATE} only")
-    H = int(n_head)
-    o = {"Q": 0, "K": H * 64, "V": 2 * H * 64, "B": 3 * H * 64, "C": 3 * H * 64 + H * 32,
-         "TH": 3 * H * 64 + 2 * H * 32}
-    o["A"] = o["TH"] + H * 16
-    o["NTOT"] = o["A"] + H
-    o["NPAD"] = (o["NTOT"] + 15) // 16 * 16
-    return o
+    return ops.fused_layout(n_head)
 
 
 def concat_fused_weights(W_Q, W_K, W_V, W_B, W_C, W_theta, W_alpha, b_alpha):
@@ -49,139 +43,104 @@ def concat_fused_weights(W_Q, W_K, W_V, W_B, W_C, W_theta, W_alpha, b_alpha):
     return W, torch.cat(bs, 0)
 
 
+def _cached_wcat(owner, weights, dtype) -> torch.Tensor:
+    """The concatenation of ``weights`` (plus zero padding rows to NPAD) in ``dtype``, kept on ``owner``
+    while every weight keeps its storage, version and dtype. Under training each optimizer step changes the
+    weights, so it is rebuilt once per step and reused by every micro-batch of that step; it never enters
+    the autograd graph."""
+    key = (dtype,) + tuple((w.data_ptr(), w._version, w.dtype) for w in weights)
+    hit = owner.__dict__.get("_wcat_train")
+    if hit is not None and hit[0] == key:
+        return hit[1]
+    H = weights[-1].shape[0]
+    off = fused_layout(H)
+    d = weights[0].shape[1]
+    wc = torch.empty((off["NPAD"], d), dtype=dtype, device=weights[0].device)
+    row = 0
+    with torch.no_grad():
+        for w in weights:
+            wc[row:row + w.shape[0]].copy_(w)
+            row += w.shape[0]
+        wc[row:].zero_()
+    owner.__dict__["_wcat_train"] = (key, wc)
+    return wc
+
+
 class _FusedProjFn(torch.autograd.Function):
-    """``proj = x W_cat^T + b_cat`` in the compute dtype, where ``b_cat`` is zero except the alpha
-    columns. The forward is the call ``F.linear`` makes under autocast (inputs cast to the compute dtype,
-    bias added in the GEMM epilogue before the one rounding); the backward runs the same two GEMMs as
-    autograd's linear backward, but forms the bias gradient from the H alpha columns only, where
-    autograd reduces all NPAD columns of the output gradient."""
+    """``proj = x W_cat^T + b_cat`` in the compute dtype from the seven projection weights, ``b_cat`` zero
+    except the alpha columns: the call ``F.linear`` makes under autocast (inputs in the compute dtype, bias
+    added in the GEMM epilogue before the one rounding). ``W_cat`` comes from :func:`_cached_wcat` instead of
+    a differentiable ``torch.cat``; the backward runs autograd's two linear-backward GEMMs once for the
+    concatenation, hands each weight its rows of dW as a view, and reduces only the H alpha columns for
+    the bias gradient."""
 
     @staticmethod
-    def forward(ctx, x, weight, b_alpha, col_a, dtype):
+    def forward(ctx, x, b_alpha, owner, dtype, *weights):
         H = b_alpha.shape[0]
-        xc, wc = x.to(dtype), weight.to(dtype)
-        bias = torch.zeros((weight.shape[0],), dtype=dtype, device=x.device)
+        col_a = fused_layout(H)["A"]
+        xc = x.to(dtype)
+        wc = _cached_wcat(owner, weights, dtype)
+        bias = torch.zeros((wc.shape[0],), dtype=dtype, device=x.device)
         bias[col_a:col_a + H] = b_alpha.to(dtype)
         with torch.autocast(x.device.type, enabled=False):
             out = torch.nn.functional.linear(xc, wc, bias)
         ctx.save_for_backward(xc, wc)
         ctx.col_a, ctx.H = col_a, H
-        ctx.dtypes = (x.dtype, weight.dtype, b_alpha.dtype)
+        ctx.rows = [w.shape[0] for w in weights]
+        ctx.dtypes = (x.dtype, b_alpha.dtype, [w.dtype for w in weights])
         return out
 
     @staticmethod
     def backward(ctx, g):
         xc, wc = ctx.saved_tensors
         g2 = g.reshape(-1, g.shape[-1])
-        dx = dw = db = None
+        dx = db = None
         if ctx.needs_input_grad[0]:
             dx = (g2 @ wc).view(xc.shape).to(ctx.dtypes[0])
         if ctx.needs_input_grad[1]:
-            dw = (g2.t() @ xc.reshape(-1, xc.shape[-1])).to(ctx.dtypes[1])
-        if ctx.needs_input_grad[2]:
-            db = g2[:, ctx.col_a:ctx.col_a + ctx.H].sum(0).to(ctx.dtypes[2])
-        return dx, dw, db, None, None
+            db = g2[:, ctx.col_a:ctx.col_a + ctx.H].sum(0).to(ctx.dtypes[1])
+        dws = [None] * len(ctx.rows)
+        if any(ctx.needs_input_grad[4:]):
+            dw = g2.t() @ xc.reshape(-1, xc.shape[-1])
+            row = 0
+            for i, (n, dt) in enumerate(zip(ctx.rows, ctx.dtypes[2])):
+                if ctx.needs_input_grad[4 + i]:
+                    dws[i] = dw[row:row + n].to(dt)
+                row += n
+        return (dx, db, None, None, *dws)
 
 
-def fused_projection(x: torch.Tensor, weight: torch.Tensor, b_alpha: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
-    """``F.linear(x, W_cat, b_cat)`` under autocast to ``dtype`` (fused_prep.py:99-122) with ``b_cat`` built
-    from ``b_alpha``; the same values, and a backward that reduces only the alpha columns for the bias."""
-    col_a = fused_layout(b_alpha.shape[0])["A"]
-    return _FusedProjFn.apply(x, weight, b_alpha, col_a, dtype)
-
-
-def _heads(t: torch.Tensor, col: int, H: int, w: int) -> torch.Tensor:
-    B, L, _ = t.shape
-    return t[..., col:col + H * w].view(B, L, H, w).transpose(1, 2)
-
-
-def _ws(nbytes: int, device) -> torch.Tensor:
-    return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device)
+def fused_projection(x: torch.Tensor, weights, b_alpha: torch.Tensor, dtype: torch.dtype, owner) -> torch.Tensor:
+    """``F.linear(x, W_cat, b_cat)`` under autocast to ``dtype`` (fused_prep.py:99-122) from the projection
+    weights ``[W_Q, W_K, W_V, W_B, W_C, W_theta, W_alpha]`` and the alpha bias. The compute-dtype
+    concatenation is cached on ``owner`` while the weights are unchanged."""
+    return _FusedProjFn.apply(x, b_alpha, owner, dtype, *weights)
 
 
 def prep_forward(proj: torch.Tensor, z: torch.Tensor | None, H: int):
     """Run the preparation kernels: returns (c_rot, b_rot, pos, tot)."""
-    lib = _lib.load()
-    B, L, _ = proj.shape
-    dev = proj.device
-    c_rot = torch.empty((B, H, L, D_STATE), device=dev, dtype=proj.dtype)
-    b_rot = torch.empty_like(c_rot)
-    pos = _lib.pos_planes(B, H, L, dev)
-    tot = _ws(lib.sisa_prep_fwd_workspace(B, H, L), dev)
-    st = backends.status_word(dev)
-    rc = lib.sisa_prep_fwd(proj.data_ptr(), B, L, H, proj.stride(0), proj.stride(1), _lib.dtype_code(proj.dtype),
-                           _lib.ptr(z), z.stride(0) if z is not None else 0, z.stride(1) if z is not None else 0,
-                           c_rot.data_ptr(), b_rot.data_ptr(), pos.data_ptr(), tot.data_ptr(), st.data_ptr(),
-                           _lib.stream_ptr(dev))
-    _lib.check(rc, "sisa_prep_fwd")
-    return c_rot, b_rot, pos, tot
+    return ops.prep_fwd(proj, z, H)
 
 
 class _SISAFusedFn(torch.autograd.Function):
+    """The layer core on the ``sisa_b200`` operators: forward = prep_fwd + attn_fwd, backward = fused_bwd."""
+
     @staticmethod
     def forward(ctx, proj, z, lam, H):
-        lib = _lib.load()
         B, L, _ = proj.shape
-        dev = proj.device
         off = fused_layout(H)
-        c_rot, b_rot, pos, tot = prep_forward(proj, z, H)
-        q, k, v = _heads(proj, off["Q"], H, 64), _heads(proj, off["K"], H, 64), _heads(proj, off["V"], H, 64)
-        o = torch.empty_strided((B, H, L, D_HEAD), (L * H * D_HEAD, D_HEAD, H * D_HEAD, 1), device=dev,
-                                dtype=proj.dtype)
-        lse = torch.empty((B, H, L), device=dev, dtype=torch.float32)
-        need = any(ctx.needs_input_grad)
-        o32 = torch.empty((B, H, L, D_HEAD), device=dev, dtype=torch.float32) if need else None
-        st = backends.status_word(dev)
-        vq, vk, vv, vc, vb, vo = (_lib.view4(t) for t in (q, k, v, c_rot, b_rot, o))
-        rc = lib.sisa_attn_fwd(_lib.vref(vq), _lib.vref(vk), _lib.vref(vv), _lib.vref(vc), _lib.vref(vb),
-                               pos.data_ptr(), lam.data_ptr(), B, H, L, _lib.dtype_code(proj.dtype), _lib.vref(vo),
-                               lse.data_ptr(), _lib.ptr(o32), st.data_ptr(), _lib.stream_ptr(dev))
-        _lib.check(rc, "sisa_attn_fwd")
-        backends.after_call(dev)
+        c_rot, b_rot, pos, tot = ops.prep_fwd(proj, z, H)
+        q, k, v = ops.heads(proj, off["Q"], H, 64), ops.heads(proj, off["K"], H, 64), ops.heads(proj, off["V"], H, 64)
+        o, lse, o32 = ops.attn_fwd(q, k, v, c_rot, b_rot, pos, lam, any(ctx.needs_input_grad))
         ctx.save_for_backward(proj, z, lam, c_rot, b_rot, pos, tot, o, lse, o32)
         ctx.H = H
         return o.transpose(1, 2).reshape(B, L, H * D_HEAD)
 
     @staticmethod
     def backward(ctx, dy):
-        lib = _lib.load()
         proj, z, lam, c_rot, b_rot, pos, tot, o, lse, o32 = ctx.saved_tensors
-        H = ctx.H
-        B, L, NP = proj.shape
-        dev = proj.device
-        off = fused_layout(H)
-        dy = dy.contiguous()
-        if dy.dtype != proj.dtype:
-            dy = dy.to(proj.dtype)
-        do = dy.view(B, L, H, D_HEAD).transpose(1, 2)
-        dproj = torch.empty_like(proj)
-        q, k, v = _heads(proj, off["Q"], H, 64), _heads(proj, off["K"], H, 64), _heads(proj, off["V"], H, 64)
-        dq, dk, dv = _heads(dproj, off["Q"], H, 64), _heads(dproj, off["K"], H, 64), _heads(dproj, off["V"], H, 64)
-        f32 = dict(device=dev, dtype=torch.float32)
-        dc = torch.empty((B, H, L, D_STATE), **f32)
-        db = torch.empty((B, H, L, D_STATE), **f32)
-        dg = torch.empty((B, H, L), **f32)
-        dF = torch.empty((B, H, L), **f32) if z is not None else None
-        dlam = torch.empty((H,), **f32)
-        ws = _ws(lib.sisa_attn_bwd_workspace(B, H, L), dev)
-        st = backends.status_word(dev)
-        views = [_lib.view4(t) for t in (q, k, v, c_rot, b_rot, o, do, dq, dk, dv, dc, db)]
-        r = [_lib.vref(x) for x in views]
-        rc = lib.sisa_attn_bwd(r[0], r[1], r[2], r[3], r[4], pos.data_ptr(), lam.data_ptr(), r[5], r[6],
-                               lse.data_ptr(), _lib.ptr(o32), B, H, L, _lib.dtype_code(proj.dtype),
-                               r[7], r[8], r[9], r[10], r[11], dg.data_ptr(), _lib.ptr(dF), dlam.data_ptr(),
-                               ws.data_ptr(), st.data_ptr(), _lib.stream_ptr(dev))
-        _lib.check(rc, "sisa_attn_bwd")
-        dz = torch.empty((B, L, H), **f32) if z is not None else None
-        bt = _ws(lib.sisa_prep_bwd_workspace(B, H, L), dev)
-        rc = lib.sisa_prep_bwd(proj.data_ptr(), B, L, H, proj.stride(0), proj.stride(1),
-                               _lib.dtype_code(proj.dtype), _lib.ptr(z), z.stride(0) if z is not None else 0,
-                               z.stride(1) if z is not None else 0, tot.data_ptr(), dc.data_ptr(), db.data_ptr(),
-                               dg.data_ptr(), _lib.ptr(dF), dproj.data_ptr(), dproj.stride(0), dproj.stride(1),
-                               _lib.ptr(dz), bt.data_ptr(), st.data_ptr(), _lib.stream_ptr(dev))
-        _lib.check(rc, "sisa_prep_bwd")
-        backends.after_call(dev)
-        return dproj, dz, dlam, None
+        dproj, dz, dlam = ops.fused_bwd(proj, z, lam, c_rot, b_rot, pos, tot, o, lse, o32, dy, ctx.H)
+        return dproj, (dz if z is not None else None), dlam, None
 
 
 def prefill_layer(proj: torch.Tensor, z: torch.Tensor, lam: torch.Tensor, n_head: int):
@@ -193,22 +152,12 @@ def prefill_layer(proj: torch.Tensor, z: torch.Tensor, lam: torch.Tensor, n_head
     projections, torch recurrences and rotations). Returns ``y`` (B, L, H*64) and the cache entries:
     k, v (views of proj's K/V columns), b~ (B, H, L, 32) as the kernels rotated it, g and F (views of the
     position planes) and Phi at the last position (B, H, 16) fp32."""
-    lib = _lib.load()
     H = int(n_head)
     B, L, _ = proj.shape
-    dev = proj.device
     off = fused_layout(H)
-    c_rot, b_rot, pos, _ = prep_forward(proj, z, H)
-    q, k, v = _heads(proj, off["Q"], H, 64), _heads(proj, off["K"], H, 64), _heads(proj, off["V"], H, 64)
-    o = torch.empty_strided((B, H, L, D_HEAD), (L * H * D_HEAD, D_HEAD, H * D_HEAD, 1), device=dev, dtype=proj.dtype)
-    lse = torch.empty((B, H, L), device=dev, dtype=torch.float32)
-    st = backends.status_word(dev)
-    vq, vk, vv, vc, vb, vo = (_lib.view4(t) for t in (q, k, v, c_rot, b_rot, o))
-    rc = lib.sisa_attn_fwd(_lib.vref(vq), _lib.vref(vk), _lib.vref(vv), _lib.vref(vc), _lib.vref(vb),
-                           pos.data_ptr(), lam.data_ptr(), B, H, L, _lib.dtype_code(proj.dtype), _lib.vref(vo),
-                           lse.data_ptr(), None, st.data_ptr(), _lib.stream_ptr(dev))
-    _lib.check(rc, "sisa_attn_fwd")
-    backends.after_call(dev)
+    c_rot, b_rot, pos, _ = ops.prep_fwd(proj, z, H)
+    q, k, v = ops.heads(proj, off["Q"], H, 64), ops.heads(proj, off["K"], H, 64), ops.heads(proj, off["V"], H, 64)
+    o, _, _ = ops.attn_fwd(q, k, v, c_rot, b_rot, pos, lam, False)
     theta = proj[..., off["TH"]:off["TH"] + H * (D_STATE // 2)]
     phi_last = theta.float().sum(dim=1).view(B, H, D_STATE // 2)
     y = o.transpose(1, 2).reshape(B, L, H * D_HEAD)

@@ -1,168 +1,178 @@
-"""Chunked linear + cross-entropy for a tied LM head on the sm_100a kernels
-(mirrors src/sisa/kernels/linear_ce.py).
+"""Chunked linear + cross-entropy over a tied LM head on the sm_100a kernels (the interface of
+src/sisa/kernels/linear_ce.py).
 
-``linear_cross_entropy(hidden, weight, labels)`` returns the loss of
-``F.cross_entropy(F.linear(hidden, weight).float(), labels, ignore_index=-100)`` (mean over non-ignored
-rows) and computes the gradients for ``hidden`` and ``weight`` during the forward pass, chunk by chunk:
-the tcgen05 logits kernel (``sisa_lce_logits``) writes a chunk of compute-dtype logits together with
-per-tile online max/sum-exp partials, ``sisa_lce_grad`` turns them into the loss rows and overwrites the
-chunk with G = (softmax - onehot) / N_valid, and two plain cuBLAS GEMMs give dX = G W and dW += G^T X
-(fp32 outputs). Only one chunk of logits exists at a time (by default balanced chunks under 1 GiB).
+``linear_cross_entropy(hidden, weight, labels)`` is the mean over non-ignored rows of
+``cross_entropy(hidden @ weight.T, labels)`` with the logits rounded to the compute dtype, and it never
+holds more than one chunk of logits. Everything happens in one operator, ``sisa_b200::lce``, during the
+forward: per chunk of token rows the tcgen05 logits kernel (``sisa_lce_logits``) writes the chunk's
+logits with per-tile online max / sum-exp partials, ``sisa_lce_grad`` turns them into the per-row loss
+and overwrites the chunk with G = (softmax - onehot) * scale, and two GEMMs take dX = G W and
+dW += G^T X in fp32. The backward only scales the stored gradients by its seed, unless the caller
+promised the seed (``grad_scale``), in which case G was already scaled and the backward checks the
+promise on the device.
 
-CPU tensors or an fp32 compute dtype use the eager formula, as the reference does.
+The operator needs CUDA tensors and a bf16/fp16 compute dtype (autocast's, else the input's). CPU
+tensors take the plain formula :func:`reference_linear_cross_entropy`; an fp32 compute dtype on CUDA is
+rejected rather than silently computed another way.
 """
 from __future__ import annotations
 
 import torch
 import torch.nn.functional as F
+from torch import Tensor
 
 from .. import _lib, backends
 
-__all__ = ["linear_cross_entropy", "reference_linear_cross_entropy"]
+__all__ = ["linear_cross_entropy", "reference_linear_cross_entropy", "chunk_rows"]
 
-_CHUNK_MB = 1024
-_VPAD = 256
-
-
-def _compute_dtype(x):
-    try:
-        if torch.is_autocast_enabled(x.device.type):
-            return torch.get_autocast_dtype(x.device.type)
-    except (TypeError, RuntimeError):
-        pass
-    return x.dtype
+VOCAB_ALIGN = 256          # vocabulary rows of the padded weight copy: the logits kernel's N tile
+LOGITS_BUDGET = 1 << 30    # bytes one chunk of logits may take
+ROW_ALIGN = 128            # chunk rows are whole M tiles of the logits kernel
 
 
-def _pick_chunk(N, Vp, chunk_tokens, elt):
-    """Rows per chunk: explicit, or balanced chunks under the 1 GiB logits budget rounded to 128 rows
-    (linear_ce.py:116-124)."""
-    if chunk_tokens:
-        return max(1, min(N, int(chunk_tokens)))
-    tmax = max(128, (_CHUNK_MB << 20) // (Vp * elt))
-    n_chunks = -(-N // tmax)
-    t = -(-N // n_chunks)
-    return min(N, -(-t // 128) * 128)
+def chunk_rows(n_rows: int, vocab_padded: int, elem_bytes: int, requested: int | None = None) -> int:
+    """Rows per chunk. ``requested`` wins; otherwise the fewest chunks whose logits fit the budget, made
+    equal in size and rounded up to whole 128-row tiles (the reference's rule, linear_ce.py:116-124, which
+    sets the peak memory)."""
+    if requested:
+        return max(1, min(n_rows, int(requested)))
+    fit = max(ROW_ALIGN, LOGITS_BUDGET // (vocab_padded * elem_bytes))
+    chunks = -(-n_rows // fit)
+    even = -(-n_rows // chunks)
+    return min(n_rows, -(-even // ROW_ALIGN) * ROW_ALIGN)
 
 
-def _padded_weight(w, dtype):
-    V, D = w.shape
-    Vp = -(-V // _VPAD) * _VPAD
-    out = torch.empty((Vp, D), dtype=dtype, device=w.device)
-    out[:V].copy_(w.detach())
-    if Vp > V:
-        out[V:].zero_()
-    return out
+def reference_linear_cross_entropy(hidden: Tensor, weight: Tensor, labels: Tensor, ignore_index: int = -100) -> Tensor:
+    """The plain formula ``F.cross_entropy(F.linear(hidden, weight).float(), labels, ignore_index)``
+    (src/sisa/kernels/linear_ce.py:220-224)."""
+    logits = F.linear(hidden, weight)
+    return F.cross_entropy(logits.reshape(-1, logits.shape[-1]).float(), labels.reshape(-1), ignore_index=ignore_index)
 
 
-class _LinearCrossEntropyFn(torch.autograd.Function):
+@torch.library.custom_op("sisa_b200::lce", mutates_args=())
+def _lce(x: Tensor, w_pad: Tensor, labels: Tensor, vocab: int, ignore_index: int, rows: int, need_dx: bool,
+         need_dw: bool, grad_scale: float) -> tuple[Tensor, Tensor, Tensor]:
+    """Loss and gradients of one call. ``x`` (N, D) and ``w_pad`` (Vp, D) in the compute dtype, ``w_pad``
+    zero beyond row ``vocab``; ``labels`` (N,) int64. Returns the fp32 loss, dX (N, D) fp32 and dW (Vp, D)
+    fp32 (each empty when not asked for), both scaled by ``grad_scale``."""
+    lib = _lib.load()
+    N, D = x.shape
+    Vp = w_pad.shape[0]
+    dev = x.device
+    code = _lib.dtype_code(x.dtype)
+    st = backends.status_word(dev)
+    sp = _lib.stream_ptr(dev)
+    valid = (labels != ignore_index).sum()
+    inv_valid = valid.to(torch.float32).reciprocal().reshape(1)
+    per_row = torch.empty(N, dtype=torch.float32, device=dev)
+    chunk = torch.empty((rows, Vp), dtype=x.dtype, device=dev)
+    ws = torch.empty(lib.sisa_lce_workspace(rows, Vp), dtype=torch.uint8, device=dev)
+    dx = torch.empty((N, D) if need_dx else (0,), dtype=torch.float32, device=dev)
+    dw = torch.empty((Vp, D) if need_dw else (0,), dtype=torch.float32, device=dev)
+    for start in range(0, N, rows):
+        stop = min(N, start + rows)
+        g = chunk[:stop - start]
+        xs, ls = x[start:stop], labels[start:stop]
+        _lib.check(lib.sisa_lce_logits(xs.data_ptr(), stop - start, D, xs.stride(0), w_pad.data_ptr(), vocab, Vp,
+                                       w_pad.stride(0), code, ls.data_ptr(), g.data_ptr(), g.stride(0), ws.data_ptr(),
+                                       st.data_ptr(), sp), "sisa_lce_logits")
+        _lib.check(lib.sisa_lce_grad(g.data_ptr(), g.stride(0), stop - start, vocab, Vp, code, ls.data_ptr(),
+                                     ignore_index, inv_valid.data_ptr(), grad_scale, int(need_dx or need_dw),
+                                     ws.data_ptr(), per_row[start:stop].data_ptr(), st.data_ptr(), sp),
+                   "sisa_lce_grad")
+        if need_dx:
+            torch.mm(g, w_pad, out_dtype=torch.float32, out=dx[start:stop])
+        if need_dw:
+            if start == 0:
+                torch.mm(g.t(), xs, out_dtype=torch.float32, out=dw)
+            else:
+                torch.addmm(dw, g.t(), xs, out_dtype=torch.float32, out=dw)
+    backends.after_call(dev)
+    return per_row.sum() / valid, dx, dw
+
+
+@_lce.register_fake
+def _(x, w_pad, labels, vocab, ignore_index, rows, need_dx, need_dw, grad_scale):
+    N, D = x.shape
+    f32 = dict(dtype=torch.float32)
+    return (x.new_empty((), **f32), x.new_empty((N, D) if need_dx else (0,), **f32),
+            x.new_empty((w_pad.shape[0], D) if need_dw else (0,), **f32))
+
+
+class _LinearCE(torch.autograd.Function):
+    """Loss in the forward together with the unscaled (or promised-scale) gradients; the backward scales."""
+
     @staticmethod
-    def forward(ctx, h, w, labels, opts):
-        ignore_index, chunk_tokens, cdtype, need_dh, need_dw, grad_scale = opts
-        lib = _lib.load()
-        need_grad = need_dh or need_dw
-        D = h.shape[-1]
-        V = w.shape[0]
-        dev = h.device
-        x = h.reshape(-1, D)
-        N = x.shape[0]
-        lab = labels.reshape(-1)
-        if lab.dtype != torch.int64:
-            lab = lab.long()
-        lab = lab.contiguous()
-        xb = (x if x.dtype == cdtype else x.to(cdtype)).contiguous()
-        wp = _padded_weight(w, cdtype)
-        Vp = wp.shape[0]
-        n_valid = (lab != ignore_index).sum()
-        inv_n = torch.reciprocal(n_valid.to(torch.float32)).reshape(1)
-        loss_rows = torch.empty(N, dtype=torch.float32, device=dev)
-        T = _pick_chunk(N, Vp, chunk_tokens, wp.element_size())
-        buf = torch.empty((T, Vp), dtype=cdtype, device=dev)
-        ws = torch.empty(lib.sisa_lce_workspace(T, Vp), dtype=torch.uint8, device=dev)
-        dx = torch.empty((N, D), dtype=torch.float32, device=dev) if need_dh else None
-        dw = torch.empty((Vp, D), dtype=torch.float32, device=dev) if need_dw else None
-        gs = 1.0 if grad_scale is None else float(grad_scale)
-        st = backends.status_word(dev)
-        sp = _lib.stream_ptr(dev)
-        code = _lib.dtype_code(cdtype)
-        first = True
-        for s in range(0, N, T):
-            e = min(N, s + T)
-            R = e - s
-            lg = buf[:R]
-            xc = xb[s:e]
-            rc = lib.sisa_lce_logits(xc.data_ptr(), R, D, xc.stride(0), wp.data_ptr(), V, Vp, wp.stride(0), code,
-                                     lab[s:e].data_ptr(), lg.data_ptr(), lg.stride(0), ws.data_ptr(), st.data_ptr(), sp)
-            _lib.check(rc, "sisa_lce_logits")
-            rc = lib.sisa_lce_grad(lg.data_ptr(), lg.stride(0), R, V, Vp, code, lab[s:e].data_ptr(), ignore_index,
-                                   inv_n.data_ptr(), gs, int(need_grad), ws.data_ptr(), loss_rows[s:e].data_ptr(),
-                                   st.data_ptr(), sp)
-            _lib.check(rc, "sisa_lce_grad")
-            if need_dh:
-                torch.mm(lg, wp, out_dtype=torch.float32, out=dx[s:e])
-            if need_dw:
-                if first:
-                    torch.mm(lg.t(), xc, out_dtype=torch.float32, out=dw)
-                else:
-                    torch.addmm(dw, lg.t(), xc, out_dtype=torch.float32, out=dw)
-            first = False
-        backends.after_call(dev)
-        loss = loss_rows.sum() / n_valid
-        ctx.h_shape, ctx.h_dtype, ctx.w_dtype, ctx.grad_scale, ctx.V = h.shape, h.dtype, w.dtype, grad_scale, V
+    def forward(ctx, hidden, weight, labels, ignore_index, rows, cdtype, grad_scale):
+        D = hidden.shape[-1]
+        V = weight.shape[0]
+        x = hidden.reshape(-1, D).to(cdtype).contiguous()
+        Vp = -(-V // VOCAB_ALIGN) * VOCAB_ALIGN
+        w_pad = torch.empty((Vp, D), dtype=cdtype, device=weight.device)
+        w_pad[:V].copy_(weight.detach())            # the autocast rounding of the weight
+        w_pad[V:].zero_()
+        need_dx, need_dw = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        loss, dx, dw = _lce(x, w_pad, labels.reshape(-1).to(torch.int64).contiguous(), V, int(ignore_index),
+                            chunk_rows(x.shape[0], Vp, x.element_size(), rows), need_dx, need_dw,
+                            1.0 if grad_scale is None else float(grad_scale))
         ctx.save_for_backward(dx, dw)
+        ctx.meta = (hidden.shape, hidden.dtype, weight.dtype, V, grad_scale)
         return loss
 
     @staticmethod
     @torch.autograd.function.once_differentiable
-    def backward(ctx, g):
+    def backward(ctx, seed):
         dx, dw = ctx.saved_tensors
-        if ctx.grad_scale is not None:
-            # G was pre-scaled by the promised seed; a different seed sets the status bit
-            bad = (g.to(torch.float32) != float(ctx.grad_scale)).to(torch.int32) * _lib.ST_BAD_SEED
-            st = backends.status_word(g.device)
-            st.bitwise_or_(bad.reshape(1))
-            backends.after_call(g.device)
-            dh = dx.view(ctx.h_shape) if dx is not None else None
-            dW = dw[:ctx.V] if dw is not None else None
+        h_shape, h_dtype, w_dtype, V, grad_scale = ctx.meta
+        dh = dW = None
+        if grad_scale is not None:
+            # the gradients already carry the promised seed; a different one sets a status bit
+            mismatch = (seed.float() != float(grad_scale)).to(torch.int32) * _lib.ST_BAD_SEED
+            backends.status_word(seed.device).bitwise_or_(mismatch.reshape(1))
+            backends.after_call(seed.device)
+            scale = None
         else:
-            g = g.to(torch.float32)
-            dh = torch.mul(dx, g).view(ctx.h_shape) if dx is not None else None
-            dW = torch.mul(dw[:ctx.V], g) if dw is not None else None
-        if dh is not None and dh.dtype != ctx.h_dtype:
-            dh = dh.to(ctx.h_dtype)
-        if dW is not None and dW.dtype != ctx.w_dtype:
-            dW = dW.to(ctx.w_dtype)
-        return dh, dW, None, None
+            scale = seed.float()
+        if ctx.needs_input_grad[0]:
+            dh = (dx if scale is None else dx * scale).view(h_shape).to(h_dtype)
+        if ctx.needs_input_grad[1]:
+            dW = (dw[:V] if scale is None else dw[:V] * scale).to(w_dtype)
+        return dh, dW, None, None, None, None, None
 
 
-def reference_linear_cross_entropy(hidden, weight, labels, ignore_index: int = -100):
-    """The eager formula: ``F.cross_entropy(F.linear(hidden, weight).float(), labels, ignore_index)``."""
-    logits = F.linear(hidden, weight)
-    return F.cross_entropy(logits.view(-1, logits.size(-1)).float(), labels.reshape(-1), ignore_index=ignore_index)
+def _compute_dtype(x: Tensor) -> torch.dtype:
+    if torch.is_autocast_enabled(x.device.type):
+        return torch.get_autocast_dtype(x.device.type)
+    return x.dtype
 
 
-@torch.compiler.disable
-def linear_cross_entropy(hidden: torch.Tensor, weight: torch.Tensor, labels: torch.Tensor, ignore_index: int = -100,
-                         *, chunk_tokens: int | None = None, grad_scale: float | None = None) -> torch.Tensor:
-    """Mean cross-entropy of ``hidden @ weight.T`` against ``labels`` (src/sisa/kernels/linear_ce.py:228-259).
+def linear_cross_entropy(hidden: Tensor, weight: Tensor, labels: Tensor, ignore_index: int = -100, *,
+                         chunk_tokens: int | None = None, grad_scale: float | None = None) -> Tensor:
+    """Mean cross-entropy of ``hidden @ weight.T`` against ``labels`` without materialising all logits
+    (src/sisa/kernels/linear_ce.py:228-259).
 
     Args:
-        hidden: ``(..., D)``; weight: ``(V, D)`` (receives dL/dW); labels: ``(...)`` aligned with hidden rows
-            (no shifting here), ``ignore_index`` rows get no loss and no gradient.
-        chunk_tokens: rows per chunk (default: balanced chunks under a 1 GiB logits buffer).
-        grad_scale: promise that backward is seeded with exactly this value; G is then pre-scaled and a
-            different seed sets ``SISA_ST_BAD_SEED`` (raised by the check mode).
+        hidden: ``(..., D)``, D a multiple of 64; weight: ``(V, D)`` (receives dL/dW); labels: ``(...)``
+            aligned with hidden's rows (not shifted here). Rows labelled ``ignore_index`` get no loss and
+            no gradient.
+        chunk_tokens: rows per chunk (default: equal chunks under a 1 GiB logits buffer).
+        grad_scale: a promise that the backward is seeded with exactly this value; the gradients are then
+            scaled once inside the kernels, and a different seed sets ``SISA_ST_BAD_SEED``.
+
+    Returns the fp32 loss (NaN when every row is ignored, as ``F.cross_entropy``).
     """
-    cdtype = _compute_dtype(hidden)
-    if cdtype not in (torch.bfloat16, torch.float16) or not hidden.is_cuda:
+    if not hidden.is_cuda:
         return reference_linear_cross_entropy(hidden, weight, labels, ignore_index)
-    if weight.dim() != 2 or weight.shape[1] != hidden.shape[-1]:
-        raise ValueError(f"weight must be (V, {hidden.shape[-1]}), got {tuple(weight.shape)}")
-    if labels.numel() != hidden.numel() // hidden.shape[-1]:
-        raise ValueError(f"labels have {labels.numel()} elements, expected one per hidden row "
-                         f"({hidden.numel() // hidden.shape[-1]})")
-    if hidden.shape[-1] % 64:
-        raise ValueError(f"the cuda linear-CE kernel needs a hidden size that is a multiple of 64, got {hidden.shape[-1]}")
-    ge = torch.is_grad_enabled()
-    opts = (ignore_index, chunk_tokens, cdtype, bool(ge and hidden.requires_grad), bool(ge and weight.requires_grad),
-            grad_scale)
-    return _LinearCrossEntropyFn.apply(hidden, weight, labels, opts)
+    cdtype = _compute_dtype(hidden)
+    if cdtype not in (torch.bfloat16, torch.float16):
+        raise TypeError(f"the cuda linear-CE kernels take a bf16/fp16 compute dtype (enable autocast or pass "
+                        f"low-precision inputs), got {cdtype}; reference_linear_cross_entropy computes it in fp32")
+    D = hidden.shape[-1]
+    if weight.dim() != 2 or weight.shape[1] != D:
+        raise ValueError(f"weight must be (V, {D}), got {tuple(weight.shape)}")
+    if labels.numel() * D != hidden.numel():
+        raise ValueError(f"labels have {labels.numel()} elements, expected one per hidden row ({hidden.numel() // D})")
+    if D % 64:
+        raise ValueError(f"the cuda linear-CE kernel needs a hidden size that is a multiple of 64, got {D}")
+    with torch.autocast(hidden.device.type, enabled=False):
+        return _LinearCE.apply(hidden, weight, labels, ignore_index, chunk_tokens, cdtype, grad_scale)

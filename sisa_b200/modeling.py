@@ -206,6 +206,11 @@ class SISAAttention(nn.Module):
         with no_autocast(x.device.type):
             return F.linear(x.float(), self.forget_proj.weight.float(), self.forget_proj.bias.float())
 
+    def projection_weights(self) -> list[Tensor]:
+        """The weights of the fused projection in column order: W_Q, W_K, W_V, W_B, W_C, W_theta, W_alpha."""
+        return [self.W_Q.weight, self.W_K.weight, self.W_V.weight, self.W_B.weight, self.W_C.weight,
+                self.theta_proj.weight, self.alpha_proj.weight]
+
     def fused_weights(self) -> tuple[Tensor, Tensor]:
         from .kernels.fused import concat_fused_weights
 
@@ -257,13 +262,14 @@ class SISAAttention(nn.Module):
         from .kernels.fused import sisa_fused
 
         bsz, seq_len, d = x.shape
-        weight, bias = self.fused_weights()
         cd = _compute_dtype(x)
-        if x.is_cuda and (cd != x.dtype or cd != weight.dtype):
+        if x.is_cuda and (cd != x.dtype or cd != self.W_Q.weight.dtype):
             from .kernels.fused import fused_projection
 
-            proj = fused_projection(x, weight, self.alpha_proj.bias, cd)   # autocast's linear, lean bias gradient
+            # autocast's linear over a cached compute-dtype concatenation, lean bias gradient
+            proj = fused_projection(x, self.projection_weights(), self.alpha_proj.bias, cd, self)
         else:
+            weight, bias = self.fused_weights()
             proj = F.linear(x, weight, bias)
         y = sisa_fused(proj, self._forget_logits(x) if z is None else z, self.lam(), self.config.n_head)
         return self.W_O(y.reshape(bsz, seq_len, d))
