@@ -20,7 +20,7 @@ D_STATE = 32
 def _aligned(t: torch.Tensor) -> torch.Tensor:
     """A view the kernels can take: contiguous last axis, 16-byte rows and strides."""
     unit = 16 // t.element_size()
-    if t.stride(-1) != 1 or t.data_ptr() % 16 or any(s % unit for s in t.stride()[:-1]):
+    if t.stride(-1) != 1 or ops.base_misaligned(t) or any(s % unit for s in t.stride()[:-1]):
         return t.contiguous()
     return t
 

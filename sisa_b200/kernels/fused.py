@@ -190,7 +190,7 @@ def sisa_fused(proj: torch.Tensor, z: torch.Tensor | None, lam: torch.Tensor, n_
         raise ValueError("proj must be a CUDA tensor")
     if L < 1:
         raise ValueError("sequence length must be >= 1")
-    if proj.stride(-1) != 1 or proj.stride(1) != NP or proj.stride(0) % 8 or proj.data_ptr() % 16:
+    if proj.stride(-1) != 1 or proj.stride(1) != NP or proj.stride(0) % 8 or ops.base_misaligned(proj):
         proj = proj.contiguous()
     if z is not None:
         if z.shape != (B, L, H):

@@ -17,7 +17,8 @@ from torch import Tensor
 
 from . import _lib, backends
 
-__all__ = ["prep_fwd", "pack_positions", "attn_fwd", "attn_bwd", "fused_bwd", "fused_layout", "heads"]
+__all__ = ["prep_fwd", "pack_positions", "attn_fwd", "attn_bwd", "fused_bwd", "fused_layout", "heads",
+           "base_misaligned"]
 
 D_HEAD = 64
 D_STATE = 32
@@ -48,6 +49,15 @@ def _bytes(n: int, device) -> Tensor:
 def _o_like(B: int, H: int, L: int, dtype, device) -> Tensor:
     """(B, H, L, 64) with (B, L, H, 64) storage, so that the heads-concatenated output is a view."""
     return torch.empty_strided((B, H, L, D_HEAD), (L * H * D_HEAD, D_HEAD, H * D_HEAD, 1), dtype=dtype, device=device)
+
+
+def base_misaligned(t: Tensor) -> bool:
+    """Whether ``t`` starts off a 16-byte boundary (the TMA tensor maps need 16-byte aligned bases).
+    A traced graph has no storage to look at, so under torch.compile this reports False and the C ABI's
+    own check (SISA_ERR_ALIGN, raised as ValueError) stays the guard."""
+    if torch.compiler.is_compiling():
+        return False
+    return t.data_ptr() % 16 != 0
 
 
 def _none_if_empty(t: Tensor | None) -> Tensor | None:

@@ -2,6 +2,8 @@
 fp64, under bf16 autocast (the reference's tests/test_model_cuda.py gates)."""
 from __future__ import annotations
 
+import types
+
 import pytest
 import torch
 
@@ -128,11 +130,11 @@ def test_fused_projection_matches_autocast_linear(cuda_dev):
     ker = [t.detach().clone().requires_grad_(True) for t in ws + [ba]]
     xr, xk = x.detach().clone().requires_grad_(True), x.detach().clone().requires_grad_(True)
     go = torch.randn((2, 96, fused_layout(H)["NPAD"]), generator=gen, device=cuda_dev).to(torch.bfloat16)
+    owner = types.SimpleNamespace()
     with torch.autocast("cuda", dtype=torch.bfloat16):
         W, b = concat_fused_weights(*ref)
         yr = torch.nn.functional.linear(xr, W, b)
-        Wk, _ = concat_fused_weights(*ker)
-        yk = fused_projection(xk, Wk, ker[-1], torch.bfloat16)
+        yk = fused_projection(xk, ker[:-1], ker[-1], torch.bfloat16, owner)
     assert yk.dtype == yr.dtype and torch.equal(yk, yr)
     yr.backward(go)
     yk.backward(go)
@@ -140,3 +142,16 @@ def test_fused_projection_matches_autocast_linear(cuda_dev):
     for a, r in zip(ker[:-1], ref[:-1]):
         assert torch.equal(a.grad, r.grad)
     assert torch.allclose(ker[-1].grad, ref[-1].grad, rtol=1e-2, atol=1e-3)
+    # the compute-dtype concatenation is kept while the weights are unchanged, rebuilt after an update
+    cached = owner.__dict__["_wcat_train"][1]
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        fused_projection(xk, ker[:-1], ker[-1], torch.bfloat16, owner)
+    assert owner.__dict__["_wcat_train"][1] is cached
+    with torch.no_grad():
+        ker[0].add_(1.0)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y2 = fused_projection(xk, ker[:-1], ker[-1], torch.bfloat16, owner)
+        W2, b2 = concat_fused_weights(*[t.detach() for t in ker])
+        y2r = torch.nn.functional.linear(xk.detach(), W2, b2)
+    assert owner.__dict__["_wcat_train"][1] is not cached
+    assert torch.equal(y2.detach(), y2r)
