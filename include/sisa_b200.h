@@ -140,7 +140,7 @@ int sisa_prep_bwd(const void* proj, int64_t B, int64_t L, int64_t H, int64_t pro
  * sisa_lce_grad: per row lse, loss_rows[r] = lse - logit[label] (0 for ignore_index), and, when
  *   compute_grad, G = (softmax - onehot) * (*inv_n) * grad_scale written over the logits in place
  *   (padding columns 0). inv_n is a device scalar (1 / number of non-ignored rows).
- * The gradient GEMMs dx = G . w and dw += G^T . x are plain GEMMs left to the caller (cuBLAS). */
+ * The gradient GEMMs dx = G . w and dw += G^T . x are sisa_gemm calls. */
 int64_t sisa_lce_workspace(int64_t R, int64_t Vp);
 int sisa_lce_logits(const void* x, int64_t R, int64_t D, int64_t x_ld, const void* w, int64_t V, int64_t Vp,
                     int64_t w_ld, int dtype, const int64_t* labels, void* logits, int64_t logits_ld,
@@ -148,6 +148,17 @@ int sisa_lce_logits(const void* x, int64_t R, int64_t D, int64_t x_ld, const voi
 int sisa_lce_grad(void* logits, int64_t logits_ld, int64_t R, int64_t V, int64_t Vp, int dtype,
                   const int64_t* labels, int64_t ignore_index, const float* inv_n, float grad_scale,
                   int compute_grad, const void* workspace, float* loss_rows, int32_t* status, void* stream);
+
+/* C (+)= A . B^T on CTA pairs of tcgen05 tensor cores (the linear-CE gradient GEMMs, replacing the
+ * torch.matmul calls of src/sisa/kernels/linear_ce.py:170-178). A is M x K and B is N x K in `dtype`
+ * (SISA_BF16 / SISA_F16), each K-major (element (r, k) at r * ld + k; a_mn / b_mn = 0) or MN-major
+ * (element (r, k) at k * ld + r; = 1); C is M x N row-major in out_dtype (SISA_F32, SISA_BF16 or
+ * SISA_F16) with fp32 accumulation and one rounding; accumulate = 1 (fp32 C only) adds to C. Pointers
+ * 16-byte aligned, row strides in elements covering a row and whole 16-byte units; 1 <= M, N, K <= 2^30.
+ * Waits are bounded (SISA_ST_TIMEOUT). */
+int sisa_gemm(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn, void* c, int64_t ldc,
+              int64_t M, int64_t N, int64_t K, int dtype, int out_dtype, int accumulate, int32_t* status,
+              void* stream);
 
 /* Fused RMSNorm and SwiGLU activation of the model's blocks (src/sisa/modeling.py:25-49). Element
  * types SISA_BF16, SISA_F16 or SISA_F32; row strides (x_ld ...) in elements, unit inner stride.

@@ -6,6 +6,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -15,6 +16,7 @@
 #include "prep.h"
 #include "decode.h"
 #include "lce.h"
+#include "gemm.h"
 #include "norm.h"
 #include "capi_util.h"
 
@@ -613,6 +615,80 @@ int sisa_lce_grad(void* logits, int64_t logits_ld, int64_t R, int64_t V, int64_t
   p.compute_grad = compute_grad; p.status = status;
   cudaError_t e = sisa::launch_lce_grad(p, dtype, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_lce_grad launch");
+}
+
+// ------------------------------------------------------------------------------------ GEMM
+// Tensor map of one operand: rows x K, K-major (box 64 K x 128 rows) or MN-major (box 64 rows x 64 K).
+static int map_operand(CUtensorMap* m, const void* ptr, int64_t ld, int mn, int64_t rows, int64_t K,
+                       CUtensorMapDataType dt, const char* name) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(SISA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {(cuuint64_t)(mn ? rows : K), (cuuint64_t)(mn ? K : rows)};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {64, mn ? 64u : 128u}, es[2] = {1, 1};
+  if (enc(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
+      CUDA_SUCCESS)
+    return fail(SISA_ERR_ALIGN, "%s: cuTensorMapEncodeTiled failed", name);
+  return SISA_OK;
+}
+
+int sisa_gemm(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn, void* c, int64_t ldc,
+              int64_t M, int64_t N, int64_t K, int dtype, int out_dtype, int accumulate, int32_t* status,
+              void* stream) {
+  int rc;
+  if ((rc = check_dtype(dtype))) return rc;
+  if (!a || !b || !c) return fail(SISA_ERR_VALUE, "sisa_gemm: null pointer");
+  if ((a_mn != 0 && a_mn != 1) || (b_mn != 0 && b_mn != 1))
+    return fail(SISA_ERR_VALUE, "sisa_gemm: a_mn and b_mn are 0 (K-major) or 1 (MN-major)");
+  if (out_dtype != SISA_F32 && out_dtype != SISA_BF16 && out_dtype != SISA_F16)
+    return fail(SISA_ERR_TYPE, "sisa_gemm: out_dtype must be SISA_F32, SISA_BF16 or SISA_F16 (got %d)", out_dtype);
+  if (accumulate && out_dtype != SISA_F32) return fail(SISA_ERR_VALUE, "sisa_gemm: accumulate needs an fp32 output");
+  const int64_t lim = (int64_t)1 << 30;
+  if (M < 1 || N < 1 || K < 1 || M > lim || N > lim || K > lim)
+    return fail(SISA_ERR_VALUE, "sisa_gemm: need 1 <= M, N, K <= 2^30 (M=%lld N=%lld K=%lld)", (long long)M,
+                (long long)N, (long long)K);
+  const int64_t osz = out_dtype == SISA_F32 ? 4 : 2;
+  if (!aligned16(a) || !aligned16(b) || !aligned16(c) || lda % 8 || ldb % 8 || (ldc * osz) % 16 ||
+      lda < (a_mn ? M : K) || ldb < (b_mn ? N : K) || ldc < N)
+    return fail(SISA_ERR_ALIGN, "sisa_gemm: operands and C must be 16-byte aligned with row strides of whole "
+                "16-byte units covering their rows (lda=%lld ldb=%lld ldc=%lld)", (long long)lda, (long long)ldb,
+                (long long)ldc);
+  sisa::DeviceScope scope;
+  if ((rc = scope.bind(a))) return rc;
+  const CUtensorMapDataType dt = dtype == SISA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  sisa::GemmParams p;
+  memset(&p, 0, sizeof(p));
+  if ((rc = map_operand(&p.tm_a, a, lda, a_mn, M, K, dt, "a"))) return rc;
+  if ((rc = map_operand(&p.tm_b, b, ldb, b_mn, N, K, dt, "b"))) return rc;
+  {
+    EncodeTiledFn enc = encode_fn();
+    cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+    cuuint64_t strides[1] = {(cuuint64_t)(ldc * osz)};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / osz), 32}, es[2] = {1, 1};
+    const CUtensorMapDataType cdt = out_dtype == SISA_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                    : out_dtype == SISA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                            : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    if (enc(&p.tm_c, cdt, 2, c, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return fail(SISA_ERR_ALIGN, "c: cuTensorMapEncodeTiled failed");
+  }
+  p.ldc = ldc;
+  p.M = (int)M; p.N = (int)N; p.K = (int)K;
+  p.num_m = (int)((M + 255) / 256);
+  p.accumulate = accumulate ? 1 : 0;
+  p.status = status;
+  const int out = out_dtype == SISA_F32 ? sisa::GEMM_OUT_F32 : out_dtype == SISA_BF16 ? sisa::GEMM_OUT_BF16
+                                                                                        : sisa::GEMM_OUT_F16;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, scope.device());
+  int wide = K >= 2048 && N >= 512;
+  if (const char* tile = getenv("SISA_GEMM_TILE")) {
+    if (!strcmp(tile, "wide")) wide = 1;
+    else if (!strcmp(tile, "narrow")) wide = 0;
+  }
+  cudaError_t e = sisa::launch_gemm(p, dtype, a_mn, b_mn, out, wide, sms, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_gemm launch");
 }
 
 // ------------------------------------------------------------------------------------ norm, SwiGLU

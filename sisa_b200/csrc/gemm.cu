@@ -1,0 +1,395 @@
+// gemm.cu - persistent GEMM C (+)= A B^T on CTA pairs with the 5th-generation tensor cores
+// (tcgen05 with cta_group::2), used for the linear-CE gradients dX = G W and dW += G^T X.
+//
+// A cluster of two CTAs computes 256 x 256 tiles of C: each CTA loads its own 128 rows of A and its
+// own 128 rows of B per 64-wide K stage with plain TMA tile loads (no multicast), and one UMMA of
+// M = 256, N = 256, K = 16 issued by the leader CTA reads both CTAs' shared memory, so every B byte is
+// loaded once per pair instead of once per CTA. Each CTA's tensor memory holds its 128 rows of the
+// fp32 accumulator, double buffered (2 x 256 columns) so that one tile's epilogue overlaps the next
+// tile's main loop.
+//
+// Roles (192 threads per CTA): warps 0-3 epilogue (thread = accumulator row = TMEM lane), warp 4 TMA
+// producer, warp 5 owner of the tensor memory and, in the leader CTA, the UMMA issuer.
+// Barriers (same offsets in both CTAs):
+//   full[s]      leader only: the leader's producer arrives with the stage's byte count of both CTAs,
+//                and both CTAs' TMA loads complete on it;
+//   empty[s]     both: the leader's UMMA commit arrives on both CTAs' copies when the stage is read;
+//   acc_full[b]  both: the leader's commit after a tile's last K stage;
+//   acc_empty[b] leader only: the 4 epilogue warps of each CTA arrive when they have drained buffer b.
+// Launched in clusters of two CTAs (cudaLaunchKernelEx). Every wait is bounded (SISA_ST_TIMEOUT); all
+// warps of both CTAs meet at the final cluster barrier before the tensor memory is freed, so neither
+// CTA leaves while the leader's UMMAs use its memory.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "attn_common.cuh"
+#include "gemm.h"
+
+namespace sisa {
+namespace gemm {
+
+constexpr int BMC = 128;                   // rows of A per CTA (the pair tile has 256)
+constexpr int BK = 64;
+constexpr uint32_t SZ_HALF = 128 * BK * 2;                 // one CTA's 128 x 64 operand block: 16 KB
+constexpr uint32_t TMEM_COLS = 512;
+
+// Two tile shapes. Narrow: 256 x 256 pair tiles, six 32 KB stages, the accumulator double buffered
+// (2 x 256 columns), so that a tile's epilogue runs under the next tile's UMMAs: for short K. Wide:
+// 256 x 512 pair tiles (two N = 256 UMMAs per K step into the two 256-column halves of one
+// accumulator), four 48 KB stages: a quarter fewer operand bytes per flop from L2, for long K, where
+// the epilogue (which the next tile's UMMAs into each half wait for) is a small part of a tile.
+template <bool kWide>
+struct Cfg {
+  static constexpr int BN = kWide ? 512 : 256;             // columns of the pair tile
+  static constexpr int NST = kWide ? 4 : 6;
+  static constexpr int NBUF = kWide ? 1 : 2;               // accumulator buffers
+  static constexpr int NHALF = kWide ? 2 : 1;              // 256-column halves per buffer
+  static constexpr uint32_t SZ_B = NHALF * SZ_HALF;
+  static constexpr uint32_t SZ_STAGE = SZ_HALF + SZ_B;     // A | B
+  static constexpr uint32_t OFF_EPI = NST * SZ_STAGE;      // 192 KB of stages either way
+  static constexpr uint32_t SZ_EPI = 4096;                 // one staging box: 32 rows x 128 bytes
+  static constexpr uint32_t OFF_BAR = OFF_EPI + 4 * 2 * SZ_EPI;   // two staging boxes per epilogue warp
+  static constexpr int B_FULL = 0, B_EMPTY = NST, B_ACCF = 2 * NST, B_ACCE = 2 * NST + 2;
+  static constexpr uint32_t TMEM_SLOT = 192;               // byte offset of the TMEM address in the barrier area
+  static constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
+  static_assert(SMEM_BYTES <= 232448, "fits the 227 KB shared-memory limit");
+  static_assert((B_ACCE + 2) * 8 <= (int)TMEM_SLOT, "barriers end below the TMEM slot");
+  static_assert(NBUF * NHALF * 256 == (int)TMEM_COLS, "the accumulators fill the tensor memory");
+};
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// The shared::cluster address of `saddr` (a shared::cta address of this CTA) in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// Tile load into this CTA's shared memory that completes on an mbarrier of either CTA of the pair.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* map, uint32_t bar_cluster, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(dst), "l"(map), "r"(bar_cluster), "r"(c0), "r"(c1) : "memory");
+}
+__device__ __forceinline__ void umma_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+// Arrive once, when the UMMAs issued so far complete, on the barrier at this offset in both CTAs.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  const uint16_t both = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+      ::"r"(bar), "h"(both) : "memory");
+}
+// Store (or, for the accumulating fp32 output, add with a reduction in L2) one staged box of C.
+__device__ __forceinline__ void tma_store_2d(const void* map, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(map), "r"(src), "r"(c0), "r"(c1) : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_2d(const void* map, uint32_t src, int c0, int c1) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(map), "r"(src), "r"(c0), "r"(c1) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Tile t -> (pair-tile row mb, column nb). Tiles run in groups of GROUP_M tile rows, column by column
+// within a group, so that the pairs resident at one time cover a near-square block of C and the A and
+// B rows they stream stay in L2 together (each operand byte comes from DRAM about once per block).
+constexpr int GROUP_M = 8;
+__device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& mb, int& nb) {
+  const int per_group = GROUP_M * p.num_n;
+  const int g = t / per_group, r = t - g * per_group;
+  const int rows = min(GROUP_M, p.num_m - g * GROUP_M);
+  mb = g * GROUP_M + r % rows;
+  nb = r / rows;
+}
+
+// One epilogue step of a warp: 32 accumulator rows (its TMEM lane quarter) x 128 bytes of C (32 fp32
+// or 64 bf16/fp16 columns) from tensor memory into a 128-byte-swizzled staging box, then one TMA store
+// of the box (rows and columns beyond C are clipped by the tensor map). Two boxes per warp alternate,
+// so a box is rewritten only after the store issued from it two steps earlier has read it.
+template <int OUT, bool kHalf>
+__device__ __forceinline__ void epilogue_box(const GemmParams& p, uint32_t taddr, uint32_t box, int lane, int col,
+                                             int row0, int& nbox) {
+  constexpr int COLS = OUT == GEMM_OUT_F32 ? 32 : 64;
+  uint32_t w[32];
+  if constexpr (OUT == GEMM_OUT_F32) {
+    tmem_ld32(taddr, reinterpret_cast<float*>(w));
+    tmem_wait_ld();
+  } else {
+    float v[32];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      tmem_ld32(taddr + 32u * half, v);
+      tmem_wait_ld();
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[16 * half + i] = pack2<OUT == GEMM_OUT_F16>(v[2 * i], v[2 * i + 1]);
+    }
+  }
+  if (lane == 0 && nbox >= 2) bulk_wait_read1();
+  __syncwarp();
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    st_shared_v4(box + sw128_off((uint32_t)lane, (uint32_t)q), w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (OUT == GEMM_OUT_F32 && p.accumulate) tma_reduce_add_2d(&p.tm_c, box, col, row0);
+    else tma_store_2d(&p.tm_c, box, col, row0);
+    bulk_commit();
+  }
+  ++nbox;
+  (void)COLS;
+}
+
+template <int OUT, bool kHalf, bool A_MN, bool B_MN, bool kWide>
+__global__ void __launch_bounds__(192, 1) gemm_pair_kernel(const __grid_constant__ GemmParams p) {
+  using C = Cfg<kWide>;
+  constexpr int NST = C::NST, BN = C::BN, NBUF = C::NBUF, NHALF = C::NHALF;
+  extern __shared__ uint8_t smem_raw[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t sbase = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (sbase - raw);
+  const uint32_t bar0 = sbase + C::OFF_BAR;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + C::OFF_BAR + C::TMEM_SLOT);
+#define BAR(i) (bar0 + 8u * (uint32_t)(i))
+  if (tid == 0) {
+    for (int s = 0; s < NST; ++s) { mbar_init(BAR(C::B_FULL + s), 1); mbar_init(BAR(C::B_EMPTY + s), 1); }
+    for (int b = 0; b < 2; ++b) { mbar_init(BAR(C::B_ACCF + b), 1); mbar_init(BAR(C::B_ACCE + b), 8); }
+    fence_barrier_init();
+  }
+  if (warp == 5) { tmem_alloc_pair(smem_u32(tmem_slot), TMEM_COLS); tmem_relinquish_pair(); }
+  if (warp == 4 && lane == 0) { tma_prefetch_desc(&p.tm_a); tma_prefetch_desc(&p.tm_b); tma_prefetch_desc(&p.tm_c); }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();          // the leader's barriers exist before the peer's loads and arrivals reach them
+  tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const int ntiles = p.num_m * p.num_n;
+  const int cid = (int)blockIdx.x >> 1, ncl = (int)gridDim.x >> 1;
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (warp == 4) {
+    // ---------------------------------------------------------------- TMA producer (both CTAs)
+    if (lane == 0) {
+      const uint32_t full_leader = map_rank(BAR(C::B_FULL), 0);
+      int it = 0;
+      bool ok = true;
+      for (int t = cid; ok && t < ntiles; t += ncl) {
+        int mb, nb;
+        tile_coords(p, t, mb, nb);
+        // this CTA's rows: A rows m0 .. m0 + 127; B rows n0 + 256 h .. + 127 for each half h
+        const int m0 = mb * 2 * BMC + (int)rank * BMC, n0 = nb * BN + (int)rank * 128;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % NST;
+          if (it >= NST && !mbar_wait<true>(BAR(C::B_EMPTY + s), ((it / NST) - 1) & 1, p.status)) { ok = false; break; }
+          if (leader) mbar_expect_tx(BAR(C::B_FULL + s), 2 * C::SZ_STAGE);
+          const uint32_t st = sbase + (uint32_t)s * C::SZ_STAGE, fb = full_leader + 8u * (uint32_t)s;
+          if constexpr (A_MN) {
+            tma_load_2d_pair(st, &p.tm_a, fb, m0, kb * BK);
+            tma_load_2d_pair(st + SZ_HALF / 2, &p.tm_a, fb, m0 + 64, kb * BK);
+          } else {
+            tma_load_2d_pair(st, &p.tm_a, fb, kb * BK, m0);
+          }
+#pragma unroll
+          for (int h = 0; h < NHALF; ++h) {
+            const uint32_t sb = st + SZ_HALF * (1 + h);
+            if constexpr (B_MN) {
+              tma_load_2d_pair(sb, &p.tm_b, fb, n0 + 256 * h, kb * BK);
+              tma_load_2d_pair(sb + SZ_HALF / 2, &p.tm_b, fb, n0 + 256 * h + 64, kb * BK);
+            } else {
+              tma_load_2d_pair(sb, &p.tm_b, fb, kb * BK, n0 + 256 * h);
+            }
+          }
+        }
+      }
+      // Tail: the leader's last UMMA commits still arrive on this CTA's empty barriers; see them land
+      // before the CTA can leave.
+      for (int i = it - NST < 0 ? 0 : it - NST; ok && i < it; ++i)
+        ok = mbar_wait<true>(BAR(C::B_EMPTY + i % NST), (i / NST) & 1, p.status);
+    }
+  } else if (warp == 5) {
+    // ---------------------------------------------------------------- UMMA issuer (leader CTA)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = make_idesc(2 * BMC, 256, kHalf ? 0 : 1, A_MN ? 1 : 0, B_MN ? 1 : 0);
+      // The four K = 16 UMMAs of one stage into one 256-column part of the accumulator.
+      auto issue = [&](uint32_t acc, int s, int h, bool first) {
+        const uint32_t sa = sbase + (uint32_t)s * C::SZ_STAGE, sb = sa + SZ_HALF * (1 + h);
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+          const uint64_t da = A_MN ? make_sdesc(sa + k * 2048, 8192, 1024, SW_128B) : make_sdesc(sa + k * 32, 16, 1024, SW_128B);
+          const uint64_t db = B_MN ? make_sdesc(sb + k * 2048, 8192, 1024, SW_128B) : make_sdesc(sb + k * 32, 16, 1024, SW_128B);
+          umma_ss_pair(acc, da, db, idesc, (first && k == 0) ? 0u : 1u);
+        }
+      };
+      auto wait_full = [&](int i) {
+        const bool r = mbar_wait<true>(BAR(C::B_FULL + i % NST), (i / NST) & 1, p.status);
+        tc_fence_after();
+        return r;
+      };
+      auto wait_drained = [&](int part, int round) {
+        const bool r = round == 0 || mbar_wait<true>(BAR(C::B_ACCE + part), (round - 1) & 1, p.status);
+        tc_fence_after();
+        return r;
+      };
+      int it = 0, tl = 0;
+      bool ok = true;
+      for (int t = cid; ok && t < ntiles; t += ncl, ++tl) {
+        const int buf = tl % NBUF, round = tl / NBUF;
+        const uint32_t acc = tbase + (uint32_t)(buf * NHALF * 256);
+        int kb = 0;
+        if constexpr (kWide) {
+          // Half 0 runs ahead over the stages already loaded while the epilogue still drains half 1 of
+          // the previous tile; the stages are released once half 1 has read them too.
+          const int S = nk < NST ? nk : NST;
+          ok = wait_drained(0, round);
+          for (int j = 0; ok && j < S; ++j) {
+            if (!(ok = wait_full(it + j))) break;
+            issue(acc, (it + j) % NST, 0, j == 0);
+          }
+          ok = ok && wait_drained(1, round);
+          for (int j = 0; ok && j < S; ++j) {
+            issue(acc + 256, (it + j) % NST, 1, j == 0);
+            umma_commit_pair(BAR(C::B_EMPTY + (it + j) % NST));
+          }
+          it += S;
+          kb = S;
+        } else {
+          ok = wait_drained(buf, round);
+        }
+        for (; ok && kb < nk; ++kb, ++it) {
+          if (!(ok = wait_full(it))) break;
+#pragma unroll
+          for (int h = 0; h < NHALF; ++h) issue(acc + 256 * h, it % NST, h, kb == 0);
+          umma_commit_pair(BAR(C::B_EMPTY + it % NST));
+        }
+        if (!ok) break;
+        umma_commit_pair(BAR(C::B_ACCF + buf));
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue warps 0-3 (both CTAs)
+    constexpr int COLS = OUT == GEMM_OUT_F32 ? 32 : 64;   // columns per 128-byte staging row
+    const uint32_t acce_leader = map_rank(BAR(C::B_ACCE), 0);
+    const uint32_t boxes = sbase + C::OFF_EPI + (uint32_t)warp * 2 * C::SZ_EPI;
+    int tl = 0, nbox = 0;
+    for (int t = cid; t < ntiles; t += ncl, ++tl) {
+      int mb, nb;
+      tile_coords(p, t, mb, nb);
+      const int buf = tl % NBUF;
+      if (!warp_wait(BAR(C::B_ACCF + buf), (tl / NBUF) & 1, p.status)) break;
+      tc_fence_after();
+      const int row0 = mb * 2 * BMC + (int)rank * BMC + warp * 32;
+#pragma unroll 1
+      for (int h = 0; h < NHALF; ++h) {
+        // columns of half h: 256 h + 128 r + j come from CTA r's B rows n0 + 256 h + j
+#pragma unroll 1
+        for (int c0 = 0; c0 < 256; c0 += COLS) {
+          const int col = nb * BN + 256 * h + c0;
+          if (col < p.N && row0 < p.M)
+            epilogue_box<OUT, kHalf>(p, tbase + ((uint32_t)(warp * 32) << 16) + (uint32_t)((buf * NHALF + h) * 256 + c0),
+                                     boxes + (uint32_t)(nbox & 1) * C::SZ_EPI, lane, col, row0, nbox);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(acce_leader + 8u * (uint32_t)(buf * NHALF + h));
+      }
+    }
+    if (lane == 0) bulk_wait_all();          // the stores have landed before the kernel ends
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();          // neither CTA frees its memory while the pair's UMMAs may still use it
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc_pair(tbase, TMEM_COLS);
+  }
+#undef BAR
+}
+
+}  // namespace gemm
+
+// The grid is the number of CTA pairs that can be resident at once (not every GPC holds an even
+// number of SMs), capped by the number of tiles: the tile loop is persistent, so a pair that had to
+// wait for a free SM pair would add a whole tile's time at the end.
+template <int OUT, bool H, bool W>
+static cudaError_t launch_majors(GemmParams p, int a_mn, int b_mn, int num_sms, cudaStream_t st) {
+  using namespace gemm;
+  p.num_n = (p.N + Cfg<W>::BN - 1) / Cfg<W>::BN;
+  auto run = [&](auto kernel) {
+    const uint32_t smem = Cfg<W>::SMEM_BYTES;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(192);
+    cfg.gridDim = dim3(2 * (num_sms / 2));
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int pairs = 0;
+    if (cudaOccupancyMaxActiveClusters(&pairs, kernel, &cfg) != cudaSuccess || pairs < 1) {
+      cudaGetLastError();
+      pairs = num_sms / 2;
+    }
+    const int ntiles = p.num_m * p.num_n;
+    if (pairs > ntiles) pairs = ntiles;
+    cfg.gridDim = dim3(2 * pairs);
+    return cudaLaunchKernelEx(&cfg, kernel, p);
+  };
+  if (a_mn && b_mn) return run(gemm_pair_kernel<OUT, H, true, true, W>);
+  if (a_mn) return run(gemm_pair_kernel<OUT, H, true, false, W>);
+  if (b_mn) return run(gemm_pair_kernel<OUT, H, false, true, W>);
+  return run(gemm_pair_kernel<OUT, H, false, false, W>);
+}
+
+template <int OUT, bool H>
+static cudaError_t launch_shape(const GemmParams& p, int a_mn, int b_mn, int wide, int num_sms, cudaStream_t st) {
+  return wide ? launch_majors<OUT, H, true>(p, a_mn, b_mn, num_sms, st)
+              : launch_majors<OUT, H, false>(p, a_mn, b_mn, num_sms, st);
+}
+
+cudaError_t launch_gemm(const GemmParams& p, int in_dtype, int a_mn, int b_mn, int out, int wide, int num_sms,
+                        cudaStream_t st) {
+  const bool h = in_dtype == 1;
+  if (out == GEMM_OUT_F32) return h ? launch_shape<GEMM_OUT_F32, true>(p, a_mn, b_mn, wide, num_sms, st)
+                                    : launch_shape<GEMM_OUT_F32, false>(p, a_mn, b_mn, wide, num_sms, st);
+  if (out == GEMM_OUT_BF16) return h ? launch_shape<GEMM_OUT_BF16, true>(p, a_mn, b_mn, wide, num_sms, st)
+                                     : launch_shape<GEMM_OUT_BF16, false>(p, a_mn, b_mn, wide, num_sms, st);
+  return h ? launch_shape<GEMM_OUT_F16, true>(p, a_mn, b_mn, wide, num_sms, st)
+           : launch_shape<GEMM_OUT_F16, false>(p, a_mn, b_mn, wide, num_sms, st);
+}
+
+}  // namespace sisa

@@ -95,8 +95,8 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t
 }
 
 // ------------------------------------------------------------------------------------ TMA
-// Tiled bulk-tensor loads into this CTA's shared memory, completing on an mbarrier. No multicast
-// anywhere in this library: every CTA loads its own tiles.
+// Tiled bulk-tensor loads into this CTA's shared memory, completing on an mbarrier. Every CTA loads
+// its own tiles: no load in this library is shared between CTAs.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* map, uint32_t bar, int c0, int c1) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"

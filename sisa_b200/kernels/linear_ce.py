@@ -6,8 +6,8 @@ src/sisa/kernels/linear_ce.py).
 holds more than one chunk of logits. Everything happens in one operator, ``sisa_b200::lce``, during the
 forward: per chunk of token rows the tcgen05 logits kernel (``sisa_lce_logits``) writes the chunk's
 logits with per-tile online max / sum-exp partials, ``sisa_lce_grad`` turns them into the per-row loss
-and overwrites the chunk with G = (softmax - onehot) * scale, and two GEMMs take dX = G W and
-dW += G^T X in fp32. The backward only scales the stored gradients by its seed, unless the caller
+and overwrites the chunk with G = (softmax - onehot) * scale, and the CTA-pair tcgen05 GEMM
+(``sisa_gemm``) takes dX = G W and dW += G^T X in fp32 (later chunks add into dW with TMA reduce-adds). The backward only scales the stored gradients by its seed, unless the caller
 promised the seed (``grad_scale``), in which case G was already scaled and the backward checks the
 promise on the device.
 
@@ -22,6 +22,7 @@ import torch.nn.functional as F
 from torch import Tensor
 
 from .. import _lib, backends
+from .gemm import matmul_t
 
 __all__ = ["linear_cross_entropy", "reference_linear_cross_entropy", "chunk_rows"]
 
@@ -81,12 +82,9 @@ def _lce(x: Tensor, w_pad: Tensor, labels: Tensor, vocab: int, ignore_index: int
                                      ws.data_ptr(), per_row[start:stop].data_ptr(), st.data_ptr(), sp),
                    "sisa_lce_grad")
         if need_dx:
-            torch.mm(g, w_pad, out_dtype=torch.float32, out=dx[start:stop])
+            matmul_t(g, w_pad.t(), dx[start:stop])
         if need_dw:
-            if start == 0:
-                torch.mm(g.t(), xs, out_dtype=torch.float32, out=dw)
-            else:
-                torch.addmm(dw, g.t(), xs, out_dtype=torch.float32, out=dw)
+            matmul_t(g.t(), xs.t(), dw, accumulate=start > 0)
     backends.after_call(dev)
     return per_row.sum() / valid, dx, dw
 

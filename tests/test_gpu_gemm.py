@@ -1,0 +1,136 @@
+"""The CTA-pair tcgen05 GEMM (``sisa_gemm``) against an fp64 product of the same bf16/fp16 operands:
+both tile shapes (256 x 256 and 256 x 512 pair tiles, forced through ``SISA_GEMM_TILE``), every operand
+majorness, ragged M/N/K, the persistent tile loop (more tiles than CTA pairs), long K (the stage ring
+wraps many times), fp32 accumulation into C and the rounded bf16/fp16 outputs."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _operands(M, N, K, a_mn, b_mn, dtype, dev, seed):
+    gen = torch.Generator().manual_seed(seed)
+    a = torch.randn(M, K, generator=gen).to(dtype)
+    b = torch.randn(N, K, generator=gen).to(dtype)
+    # MN-major: store the transpose row-major (row stride padded to whole 16-byte units) and view it back
+    def lay(x, mn):
+        r, k = x.shape
+        if mn:
+            pad = -r % 8
+            buf = torch.zeros(k, r + pad, dtype=dtype)
+            buf[:, :r] = x.t()
+            return buf.to(dev)[:, :r].t()
+        pad = -k % 8
+        buf = torch.zeros(r, k + pad, dtype=dtype)
+        buf[:, :k] = x
+        return buf.to(dev)[:, :k]
+    return a, b, lay(a, a_mn), lay(b, b_mn)
+
+
+def _check_f32(c, a, b, scale=1e-5):
+    ref = a.double() @ b.double().t()
+    bound = (a.double().abs() @ b.double().abs().t()) * scale + 1e-30
+    err = (c.double().cpu() - ref).abs()
+    assert bool((err <= bound).all()), float((err / bound).max())
+
+
+SHAPES = [(256, 256, 64), (300, 520, 200), (1000, 130, 72), (17, 5, 8), (1, 300, 1000), (260, 1100, 136)]
+
+
+@pytest.fixture(params=["narrow", "wide"])
+def tile(request, monkeypatch):
+    monkeypatch.setenv("SISA_GEMM_TILE", request.param)
+    return request.param
+
+
+@pytest.mark.parametrize("a_mn", [0, 1])
+@pytest.mark.parametrize("b_mn", [0, 1])
+@pytest.mark.parametrize("shape", SHAPES)
+def test_gemm_fp32_out_all_majors(cuda_dev, tile, a_mn, b_mn, shape):
+    from sisa_b200.kernels.gemm import matmul_t
+
+    M, N, K = shape
+    a, b, da, db = _operands(M, N, K, a_mn, b_mn, torch.bfloat16, cuda_dev, seed=M + N + K + 2 * a_mn + b_mn)
+    c = matmul_t(da, db)
+    torch.cuda.synchronize()
+    _check_f32(c, a, b)
+    from sisa_b200 import backends
+    assert int(backends.status_word(cuda_dev).item()) == 0
+
+
+def test_gemm_persistent_tiles_and_long_k(cuda_dev, tile):
+    from sisa_b200.kernels.gemm import matmul_t
+
+    # 16 x 8 = 128 pair tiles (more than the resident CTA pairs) and 3000 / 64 K stages (the six-stage
+    # ring wraps ~8 times per tile)
+    for (M, N, K, a_mn, b_mn) in ((4096, 2048, 256, 0, 0), (1024, 512, 3000, 1, 1), (2304, 1280, 1100, 0, 1)):
+        a, b, da, db = _operands(M, N, K, a_mn, b_mn, torch.bfloat16, cuda_dev, seed=K)
+        c = matmul_t(da, db)
+        torch.cuda.synchronize()
+        _check_f32(c, a, b)
+
+
+def test_gemm_accumulate_and_strided_output(cuda_dev, tile):
+    from sisa_b200.kernels.gemm import matmul_t
+
+    M, N, K = 700, 600, 130
+    a, b, da, db = _operands(M, N, K, 1, 1, torch.bfloat16, cuda_dev, seed=5)
+    base = torch.randn(M, N + 12, generator=torch.Generator().manual_seed(6))
+    out = base.clone().to(cuda_dev)
+    view = out[:, 4:4 + N]
+    matmul_t(da, db, view, accumulate=True)
+    torch.cuda.synchronize()
+    got = out.cpu()
+    assert torch.equal(got[:, :4], base[:, :4]) and torch.equal(got[:, 4 + N:], base[:, 4 + N:])
+    ref = base[:, 4:4 + N].double() + a.double() @ b.double().t()
+    bound = (a.double().abs() @ b.double().abs().t() + base[:, 4:4 + N].double().abs()) * 1e-5
+    assert bool(((got[:, 4:4 + N].double() - ref).abs() <= bound).all())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_gemm_low_precision_out_rounds_once(cuda_dev, tile, dtype):
+    from sisa_b200.kernels.gemm import matmul_t
+
+    M, N, K = 520, 300, 264
+    a, b, da, db = _operands(M, N, K, 0, 1, dtype, cuda_dev, seed=11)
+    c32 = matmul_t(da, db)
+    c = matmul_t(da, db, out_dtype=dtype)
+    torch.cuda.synchronize()
+    assert c.dtype == dtype
+    # the low-precision output is the fp32 result rounded once (ties may differ only where the fp32
+    # results themselves differ, which they do not: same kernel, same order)
+    assert torch.equal(c, c32.to(dtype))
+    _check_f32(c32, a, b)
+
+
+def test_gemm_matches_torch_mm_within_fp32_order(cuda_dev):
+    """The same product as torch.mm with an fp32 output (cuBLAS), up to summation order."""
+    from sisa_b200.kernels.gemm import matmul_t
+
+    gen = torch.Generator().manual_seed(8)
+    G = torch.randn(1024, 2560, generator=gen).to(torch.bfloat16).to(cuda_dev)
+    W = torch.randn(2560, 512, generator=gen).to(torch.bfloat16).to(cuda_dev)
+    X = torch.randn(1024, 512, generator=gen).to(torch.bfloat16).to(cuda_dev)
+    dx = matmul_t(G, W.t())                   # A K-major, B MN-major
+    dw = matmul_t(G.t(), X.t())               # both MN-major
+    ref_dx = torch.mm(G, W, out_dtype=torch.float32)
+    ref_dw = torch.mm(G.t(), X, out_dtype=torch.float32)
+    torch.testing.assert_close(dx, ref_dx, rtol=1e-4, atol=1e-3)
+    torch.testing.assert_close(dw, ref_dw, rtol=1e-4, atol=1e-3)
+
+
+def test_gemm_argument_errors(cuda_dev):
+    from sisa_b200.kernels.gemm import matmul_t
+
+    a = torch.randn(64, 70, device=cuda_dev).to(torch.bfloat16)[:, :66]   # row stride 70: not 16-byte units
+    b = torch.randn(64, 66, device=cuda_dev).to(torch.bfloat16)
+    with pytest.raises(ValueError):
+        matmul_t(a, b)
+    with pytest.raises(TypeError):
+        matmul_t(b, b.half())
+    out = torch.empty(64, 64, device=cuda_dev, dtype=torch.bfloat16)
+    bb = torch.randn(64, 64, device=cuda_dev).to(torch.bfloat16)
+    with pytest.raises(ValueError):
+        matmul_t(bb, bb, out, accumulate=True)
