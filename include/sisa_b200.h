@@ -133,10 +133,11 @@ int sisa_prep_bwd(const void* proj, int64_t B, int64_t L, int64_t H, int64_t pro
                   void* workspace, int32_t* status, void* stream);
 
 /* Chunked linear + cross-entropy over a tied LM head (src/sisa/kernels/linear_ce.py:60-196).
- * sisa_lce_logits: logits (R, Vp) = x (R, D) . w (Vp, D)^T on tcgen05, stored in `dtype` (rounded as
- *   under autocast) at logits (row stride logits_ld), plus per (row, 256-column tile) online
- *   max/sum-exp over the first V columns and the label's logit, kept in `workspace`
- *   (sisa_lce_workspace(R, Vp) bytes). D a multiple of 64, Vp >= V a multiple of 256, w rows [V, Vp) zero.
+ * sisa_lce_logits: logits (R, Vp) = x (R, D) . w (Vp, D)^T on tcgen05 CTA pairs (the sisa_gemm kernel with
+ *   a log-sum-exp epilogue), stored in `dtype` (rounded as under autocast) at logits (row stride
+ *   logits_ld), plus per (row, 64-column segment) online max/sum-exp over the first V columns and the
+ *   label's logit, kept in `workspace` (sisa_lce_workspace(R, Vp) bytes, 16-byte aligned). D a multiple
+ *   of 64, Vp >= V a multiple of 256, w rows [V, Vp) zero.
  * sisa_lce_grad: per row lse, loss_rows[r] = lse - logit[label] (0 for ignore_index), and, when
  *   compute_grad, G = (softmax - onehot) * (*inv_n) * grad_scale written over the logits in place
  *   (padding columns 0). inv_n is a device scalar (1 / number of non-ignored rows).
@@ -148,6 +149,11 @@ int sisa_lce_logits(const void* x, int64_t R, int64_t D, int64_t x_ld, const voi
 int sisa_lce_grad(void* logits, int64_t logits_ld, int64_t R, int64_t V, int64_t Vp, int dtype,
                   const int64_t* labels, int64_t ignore_index, const float* inv_n, float grad_scale,
                   int compute_grad, const void* workspace, float* loss_rows, int32_t* status, void* stream);
+/* The backward of the linear-CE (src/sisa/kernels/linear_ce.py:200-217, grad_output * dx / dW):
+ * out[i] = x[i] * (*seed) in out_dtype (SISA_BF16, SISA_F16 or SISA_F32), or x scaled in place when out
+ * is NULL (SISA_F32). In place with a seed of exactly 1 nothing is written. seed is a device scalar. */
+int sisa_lce_seed_scale(float* x, int64_t n, const float* seed, void* out, int out_dtype, int32_t* status,
+                        void* stream);
 
 /* C (+)= A . B^T on CTA pairs of tcgen05 tensor cores (the linear-CE gradient GEMMs, replacing the
  * torch.matmul calls of src/sisa/kernels/linear_ce.py:170-178). A is M x K and B is N x K in `dtype`

@@ -18,7 +18,7 @@ _LIB = None
 # return codes / status bits (sisa_b200.h)
 OK, ERR_VALUE, ERR_TYPE, ERR_ALIGN, ERR_CUDA, ERR_UNSUPPORTED = 0, 1, 2, 3, 4, 5
 ST_NONFINITE, ST_NONMONOTONE, ST_TIMEOUT, ST_BAD_SEED, ST_BAD_POS = 1, 2, 4, 8, 16
-BF16, F16 = 0, 1
+BF16, F16, F32 = 0, 1, 2
 
 
 class View4(ctypes.Structure):
@@ -84,6 +84,7 @@ SIGNATURES = {
     "sisa_lce_workspace": (_I64, [_I64, _I64]),
     "sisa_lce_logits": (_I, [_P, _I64, _I64, _I64, _P, _I64, _I64, _I64, _I, _P, _P, _I64, _P, _P, _P]),
     "sisa_lce_grad": (_I, [_P, _I64, _I64, _I64, _I64, _I, _P, _I64, _P, ctypes.c_float, _I, _P, _P, _P, _P]),
+    "sisa_lce_seed_scale": (_I, [_P, _I64, _P, _P, _I, _P, _P]),
     "sisa_gemm": (_I, [_P, _I64, _I, _P, _I64, _I, _P, _I64, _I64, _I64, _I64, _I, _I, _I, _P, _P]),
     "sisa_decode_attn": (_I, [_VP, _VP, _P, _P, _VP, _VP, _VP, _P, _P, _I64, _P, _I64, _I64, _I64, _I, _VP, _P,
                               _P, _P]),

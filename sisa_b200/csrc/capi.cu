@@ -541,83 +541,7 @@ int sisa_decode_prep_dpos(const void* proj, int64_t proj_sb, const float* z, int
                           max_pos, d_pos, phi, c_out, g_out, f_out, status, stream);
 }
 
-int64_t sisa_lce_workspace(int64_t R, int64_t Vp) {
-  const int64_t nblk = (Vp + 255) / 256;
-  return R * nblk * 8 + ((R * 4 + 255) / 256) * 256;
-}
-
-int sisa_lce_logits(const void* x, int64_t R, int64_t D, int64_t x_ld, const void* w, int64_t V, int64_t Vp,
-                    int64_t w_ld, int dtype, const int64_t* labels, void* logits, int64_t logits_ld,
-                    void* workspace, int32_t* status, void* stream) {
-  int rc;
-  if ((rc = check_dtype(dtype))) return rc;
-  if (!x || !w || !labels || !logits || !workspace) return fail(SISA_ERR_VALUE, "sisa_lce_logits: null pointer");
-  if (R < 1 || D < 64 || D % 64 || V < 1 || Vp % 256 || Vp < V)
-    return fail(SISA_ERR_VALUE, "sisa_lce_logits: need R >= 1, D a multiple of 64, Vp >= V a multiple of 256 "
-                "(R=%lld D=%lld V=%lld Vp=%lld)", (long long)R, (long long)D, (long long)V, (long long)Vp);
-  if (!aligned16(x) || !aligned16(w) || !aligned16(logits) || x_ld % 8 || w_ld % 8 || logits_ld % 8 ||
-      x_ld < D || w_ld < D || logits_ld < Vp)
-    return fail(SISA_ERR_ALIGN, "sisa_lce_logits: rows must be 16-byte aligned (ld multiple of 8 and >= width)");
-  sisa::DeviceScope scope;
-  if ((rc = scope.bind(x))) return rc;
-  EncodeTiledFn enc = encode_fn();
-  if (!enc) return fail(SISA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  const CUtensorMapDataType dt = dtype == SISA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  sisa::LceParams p;
-  memset(&p, 0, sizeof(p));
-  {
-    cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)R};
-    cuuint64_t strides[1] = {(cuuint64_t)(x_ld * 2)};
-    cuuint32_t box[2] = {64, 128}, es[2] = {1, 1};
-    if (enc(&p.tm_x, dt, 2, const_cast<void*>(x), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
-        CUDA_SUCCESS)
-      return fail(SISA_ERR_ALIGN, "x: cuTensorMapEncodeTiled failed");
-  }
-  {
-    cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)Vp};
-    cuuint64_t strides[1] = {(cuuint64_t)(w_ld * 2)};
-    cuuint32_t box[2] = {64, 256}, es[2] = {1, 1};
-    if (enc(&p.tm_w, dt, 2, const_cast<void*>(w), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) !=
-        CUDA_SUCCESS)
-      return fail(SISA_ERR_ALIGN, "w: cuTensorMapEncodeTiled failed");
-  }
-  const int64_t nblk = Vp / 256;
-  p.logits = static_cast<char*>(logits); p.ld = logits_ld;
-  p.part = static_cast<float2*>(workspace);
-  p.tgt = reinterpret_cast<float*>(static_cast<char*>(workspace) + R * nblk * 8);
-  p.labels = labels;
-  p.R = (int)R; p.D = (int)D; p.V = (int)V; p.Vp = (int)Vp; p.n_mblk = (int)((R + 127) / 128); p.n_nblk = (int)nblk;
-  p.status = status;
-  int dev = 0, sms = 148;
-  cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  cudaError_t e = sisa::launch_lce_logits(p, dtype, sms, static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_lce_logits launch");
-}
-
-int sisa_lce_grad(void* logits, int64_t logits_ld, int64_t R, int64_t V, int64_t Vp, int dtype,
-                  const int64_t* labels, int64_t ignore_index, const float* inv_n, float grad_scale,
-                  int compute_grad, const void* workspace, float* loss_rows, int32_t* status, void* stream) {
-  int rc;
-  if ((rc = check_dtype(dtype))) return rc;
-  if (!logits || !labels || !inv_n || !workspace || !loss_rows) return fail(SISA_ERR_VALUE, "sisa_lce_grad: null pointer");
-  if (R < 1 || Vp % 256 || Vp < V || logits_ld < Vp || logits_ld % 8 || !aligned16(logits))
-    return fail(SISA_ERR_VALUE, "sisa_lce_grad: bad shape or alignment");
-  const int64_t nblk = Vp / 256;
-  sisa::LceGradParams p{};
-  p.logits = static_cast<char*>(logits); p.ld = logits_ld;
-  p.part = static_cast<const float2*>(workspace);
-  p.tgt = reinterpret_cast<const float*>(static_cast<const char*>(workspace) + R * nblk * 8);
-  p.labels = labels; p.inv_n = inv_n; p.gscale = grad_scale; p.loss_rows = loss_rows;
-  p.ignore_index = ignore_index; p.R = (int)R; p.V = (int)V; p.Vp = (int)Vp; p.n_nblk = (int)nblk;
-  p.compute_grad = compute_grad; p.status = status;
-  cudaError_t e = sisa::launch_lce_grad(p, dtype, static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_lce_grad launch");
-}
-
-// ------------------------------------------------------------------------------------ GEMM
+// ------------------------------------------------------------------------------------ tensor maps of the GEMM
 // Tensor map of one operand: rows x K, K-major (box 64 K x 128 rows) or MN-major (box 64 rows x 64 K).
 static int map_operand(CUtensorMap* m, const void* ptr, int64_t ld, int mn, int64_t rows, int64_t K,
                        CUtensorMapDataType dt, const char* name) {
@@ -633,6 +557,104 @@ static int map_operand(CUtensorMap* m, const void* ptr, int64_t ld, int mn, int6
   return SISA_OK;
 }
 
+// Tensor map of C: rows x N row-major in out_dtype; box 32 rows x 128 bytes, 128-byte swizzle.
+static int map_output(CUtensorMap* m, void* ptr, int64_t ld, int64_t rows, int64_t N, int out_dtype) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(SISA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const int64_t osz = out_dtype == SISA_F32 ? 4 : 2;
+  cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * osz)};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / osz), 32}, es[2] = {1, 1};
+  const CUtensorMapDataType cdt = out_dtype == SISA_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                  : out_dtype == SISA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                          : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  if (enc(m, cdt, 2, ptr, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return fail(SISA_ERR_ALIGN, "c: cuTensorMapEncodeTiled failed");
+  return SISA_OK;
+}
+
+int64_t sisa_lce_workspace(int64_t R, int64_t Vp) {
+  const int64_t nseg = (Vp + 63) / 64;
+  return R * nseg * 8 + ((R * 4 + 255) / 256) * 256;
+}
+
+int sisa_lce_logits(const void* x, int64_t R, int64_t D, int64_t x_ld, const void* w, int64_t V, int64_t Vp,
+                    int64_t w_ld, int dtype, const int64_t* labels, void* logits, int64_t logits_ld,
+                    void* workspace, int32_t* status, void* stream) {
+  int rc;
+  if ((rc = check_dtype(dtype))) return rc;
+  if (!x || !w || !labels || !logits || !workspace) return fail(SISA_ERR_VALUE, "sisa_lce_logits: null pointer");
+  if (R < 1 || D < 64 || D % 64 || V < 1 || Vp % 256 || Vp < V || R > ((int64_t)1 << 30) || Vp > ((int64_t)1 << 30))
+    return fail(SISA_ERR_VALUE, "sisa_lce_logits: need R >= 1, D a multiple of 64, Vp >= V a multiple of 256 "
+                "(R=%lld D=%lld V=%lld Vp=%lld)", (long long)R, (long long)D, (long long)V, (long long)Vp);
+  if (!aligned16(x) || !aligned16(w) || !aligned16(logits) || !aligned16(workspace) || x_ld % 8 || w_ld % 8 ||
+      logits_ld % 8 || x_ld < D || w_ld < D || logits_ld < Vp)
+    return fail(SISA_ERR_ALIGN, "sisa_lce_logits: rows must be 16-byte aligned (ld multiple of 8 and >= width)");
+  sisa::DeviceScope scope;
+  if ((rc = scope.bind(x))) return rc;
+  const CUtensorMapDataType dt = dtype == SISA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  sisa::GemmParams p;
+  memset(&p, 0, sizeof(p));
+  if ((rc = map_operand(&p.tm_a, x, x_ld, 0, R, D, dt, "x"))) return rc;
+  if ((rc = map_operand(&p.tm_b, w, w_ld, 0, Vp, D, dt, "w"))) return rc;
+  if ((rc = map_output(&p.tm_c, logits, logits_ld, R, Vp, dtype == SISA_F16 ? SISA_F16 : SISA_BF16))) return rc;
+  const int64_t nseg = Vp / 64;
+  p.ldc = logits_ld;
+  p.M = (int)R; p.N = (int)Vp; p.K = (int)D;
+  p.num_m = (int)((R + 255) / 256);
+  p.status = status;
+  p.labels = labels;
+  p.part = static_cast<float2*>(workspace);
+  p.tgt = reinterpret_cast<float*>(static_cast<char*>(workspace) + R * nseg * 8);
+  p.V = (int)V; p.n_part = (int)nseg;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, scope.device());
+  cudaError_t e = sisa::launch_lce_logits_gemm(p, dtype, sms, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_lce_logits launch");
+}
+
+int sisa_lce_grad(void* logits, int64_t logits_ld, int64_t R, int64_t V, int64_t Vp, int dtype,
+                  const int64_t* labels, int64_t ignore_index, const float* inv_n, float grad_scale,
+                  int compute_grad, const void* workspace, float* loss_rows, int32_t* status, void* stream) {
+  int rc;
+  if ((rc = check_dtype(dtype))) return rc;
+  if (!logits || !labels || !inv_n || !workspace || !loss_rows) return fail(SISA_ERR_VALUE, "sisa_lce_grad: null pointer");
+  if (R < 1 || Vp % 256 || Vp < V || logits_ld < Vp || logits_ld % 8 || !aligned16(logits))
+    return fail(SISA_ERR_VALUE, "sisa_lce_grad: bad shape or alignment");
+  const int64_t nseg = Vp / 64;
+  sisa::LceGradParams p{};
+  p.logits = static_cast<char*>(logits); p.ld = logits_ld;
+  p.part = static_cast<const float2*>(workspace);
+  p.tgt = reinterpret_cast<const float*>(static_cast<const char*>(workspace) + R * nseg * 8);
+  p.labels = labels; p.inv_n = inv_n; p.gscale = grad_scale; p.loss_rows = loss_rows;
+  p.ignore_index = ignore_index; p.R = (int)R; p.V = (int)V; p.Vp = (int)Vp; p.n_nblk = (int)nseg;
+  p.compute_grad = compute_grad; p.status = status;
+  cudaError_t e = sisa::launch_lce_grad(p, dtype, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_lce_grad launch");
+}
+
+int sisa_lce_seed_scale(float* x, int64_t n, const float* seed, void* out, int out_dtype, int32_t* status,
+                        void* stream) {
+  (void)status;
+  if (!x || !seed) return fail(SISA_ERR_VALUE, "sisa_lce_seed_scale: null pointer");
+  if (n < 0) return fail(SISA_ERR_VALUE, "sisa_lce_seed_scale: n < 0");
+  if (out_dtype != SISA_BF16 && out_dtype != SISA_F16 && out_dtype != SISA_F32)
+    return fail(SISA_ERR_TYPE, "sisa_lce_seed_scale: out_dtype must be SISA_BF16, SISA_F16 or SISA_F32");
+  if (!out && out_dtype != SISA_F32) return fail(SISA_ERR_VALUE, "sisa_lce_seed_scale: in place needs SISA_F32");
+  if (!aligned16(x) || (out && !aligned16(out)))
+    return fail(SISA_ERR_ALIGN, "sisa_lce_seed_scale: pointers must be 16-byte aligned");
+  int rc;
+  sisa::DeviceScope scope;
+  if ((rc = scope.bind(x))) return rc;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, scope.device());
+  const int code = out_dtype == SISA_F32 ? 2 : out_dtype == SISA_F16 ? 1 : 0;
+  cudaError_t e = sisa::launch_seed_scale(x, n, seed, out, code, sms, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_lce_seed_scale launch");
+}
+
+// ------------------------------------------------------------------------------------ GEMM
 int sisa_gemm(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn, void* c, int64_t ldc,
               int64_t M, int64_t N, int64_t K, int dtype, int out_dtype, int accumulate, int32_t* status,
               void* stream) {
@@ -661,18 +683,7 @@ int sisa_gemm(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, 
   memset(&p, 0, sizeof(p));
   if ((rc = map_operand(&p.tm_a, a, lda, a_mn, M, K, dt, "a"))) return rc;
   if ((rc = map_operand(&p.tm_b, b, ldb, b_mn, N, K, dt, "b"))) return rc;
-  {
-    EncodeTiledFn enc = encode_fn();
-    cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)M};
-    cuuint64_t strides[1] = {(cuuint64_t)(ldc * osz)};
-    cuuint32_t box[2] = {(cuuint32_t)(128 / osz), 32}, es[2] = {1, 1};
-    const CUtensorMapDataType cdt = out_dtype == SISA_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
-                                    : out_dtype == SISA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                                            : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-    if (enc(&p.tm_c, cdt, 2, c, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-      return fail(SISA_ERR_ALIGN, "c: cuTensorMapEncodeTiled failed");
-  }
+  if ((rc = map_output(&p.tm_c, c, ldc, M, N, out_dtype))) return rc;
   p.ldc = ldc;
   p.M = (int)M; p.N = (int)N; p.K = (int)K;
   p.num_m = (int)((M + 255) / 256);

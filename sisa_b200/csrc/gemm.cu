@@ -1,21 +1,24 @@
 // gemm.cu - persistent GEMM C (+)= A B^T on CTA pairs with the 5th-generation tensor cores
-// (tcgen05 with cta_group::2), used for the linear-CE gradients dX = G W and dW += G^T X.
+// (tcgen05 with cta_group::2): the linear-CE logits (with the online log-sum-exp in the epilogue,
+// src/sisa/kernels/linear_ce.py:60-89) and its gradients dX = G W and dW += G^T X, and the plain
+// GEMMs of the model's projections.
 //
-// A cluster of two CTAs computes 256 x 256 tiles of C: each CTA loads its own 128 rows of A and its
-// own 128 rows of B per 64-wide K stage with plain TMA tile loads (no multicast), and one UMMA of
-// M = 256, N = 256, K = 16 issued by the leader CTA reads both CTAs' shared memory, so every B byte is
-// loaded once per pair instead of once per CTA. Each CTA's tensor memory holds its 128 rows of the
-// fp32 accumulator, double buffered (2 x 256 columns) so that one tile's epilogue overlaps the next
-// tile's main loop.
+// A cluster of two CTAs computes 256 x 256 (narrow) or 256 x 512 (wide) tiles of C: each CTA loads
+// its own 128 rows of A and its own half of the tile's B rows per 64-wide K stage with plain TMA tile
+// loads (no multicast), and the UMMAs of M = 256, N = 256, K = 16 issued by the leader CTA read both
+// CTAs' shared memory, so every B byte is loaded once per pair instead of once per CTA. Each CTA's
+// tensor memory holds its 128 rows of the fp32 accumulator (512 columns: two 256-column buffers, or
+// the two halves of one wide tile).
 //
-// Roles (192 threads per CTA): warps 0-3 epilogue (thread = accumulator row = TMEM lane), warp 4 TMA
-// producer, warp 5 owner of the tensor memory and, in the leader CTA, the UMMA issuer.
+// Roles: E = 16 (narrow) or 8 (wide) epilogue warps (warp w reads TMEM lanes 32 (w % 4) .. + 31, the
+// rows of its lane quarter, and 1024 / E columns of each 256-column part from (w / 4) 1024 / E), then
+// the TMA producer warp, then the owner of the tensor memory and, in the leader CTA, the UMMA issuer.
 // Barriers (same offsets in both CTAs):
 //   full[s]      leader only: the leader's producer arrives with the stage's byte count of both CTAs,
 //                and both CTAs' TMA loads complete on it;
 //   empty[s]     both: the leader's UMMA commit arrives on both CTAs' copies when the stage is read;
 //   acc_full[b]  both: the leader's commit after a tile's last K stage;
-//   acc_empty[b] leader only: the 4 epilogue warps of each CTA arrive when they have drained buffer b.
+//   acc_empty[p] leader only: the epilogue warps of each CTA arrive when they have drained part p.
 // Launched in clusters of two CTAs (cudaLaunchKernelEx). Every wait is bounded (SISA_ST_TIMEOUT); all
 // warps of both CTAs meet at the final cluster barrier before the tensor memory is freed, so neither
 // CTA leaves while the leader's UMMAs use its memory.
@@ -34,22 +37,30 @@ constexpr int BK = 64;
 constexpr uint32_t SZ_HALF = 128 * BK * 2;                 // one CTA's 128 x 64 operand block: 16 KB
 constexpr uint32_t TMEM_COLS = 512;
 
-// Two tile shapes. Narrow: 256 x 256 pair tiles, six 32 KB stages, the accumulator double buffered
-// (2 x 256 columns), so that a tile's epilogue runs under the next tile's UMMAs: for short K. Wide:
-// 256 x 512 pair tiles (two N = 256 UMMAs per K step into the two 256-column halves of one
-// accumulator), four 48 KB stages: a quarter fewer operand bytes per flop from L2, for long K, where
-// the epilogue (which the next tile's UMMAs into each half wait for) is a small part of a tile.
+
+// Two tile shapes. Narrow: 256 x 256 pair tiles, five 32 KB stages, the accumulator double buffered
+// (2 x 256 columns), so that a tile's epilogue runs under the next tile's UMMAs, and 16 epilogue warps
+// (64 columns each): for short K, where the epilogue must keep up with the UMMAs. Wide: 256 x 512 pair
+// tiles (two N = 256 UMMAs per K step into the two 256-column halves of one accumulator), four 48 KB
+// stages and 8 epilogue warps (128 columns each): a quarter fewer operand bytes per flop from L2, for
+// long K, where the epilogue (which the next tile's UMMAs into each half wait for) is a small part of a
+// tile.
 template <bool kWide>
 struct Cfg {
   static constexpr int BN = kWide ? 512 : 256;             // columns of the pair tile
-  static constexpr int NST = kWide ? 4 : 6;
+  static constexpr int NST = kWide ? 4 : 5;
   static constexpr int NBUF = kWide ? 1 : 2;               // accumulator buffers
-  static constexpr int NHALF = kWide ? 2 : 1;              // 256-column halves per buffer
+  static constexpr int NHALF = kWide ? 2 : 1;              // 256-column parts per buffer
+  static constexpr int NEPI = kWide ? 8 : 16;              // epilogue warps
+  static constexpr int CW = 256 / (NEPI / 4);              // columns of a part per epilogue warp
+  static constexpr int NTHREADS = 32 * (NEPI + 2);
+  static constexpr int NBOX = 1;                           // staging boxes per epilogue warp
   static constexpr uint32_t SZ_B = NHALF * SZ_HALF;
   static constexpr uint32_t SZ_STAGE = SZ_HALF + SZ_B;     // A | B
-  static constexpr uint32_t OFF_EPI = NST * SZ_STAGE;      // 192 KB of stages either way
+  static constexpr uint32_t OFF_EPI = NST * SZ_STAGE;      // 160 / 192 KB of stages
   static constexpr uint32_t SZ_EPI = 4096;                 // one staging box: 32 rows x 128 bytes
-  static constexpr uint32_t OFF_BAR = OFF_EPI + 4 * 2 * SZ_EPI;   // two staging boxes per epilogue warp
+  static constexpr uint32_t OFF_BAR = OFF_EPI + NEPI * NBOX * SZ_EPI;
+  static_assert(NTHREADS * (kWide ? 168 : 112) <= 65536, "register budget of one CTA per SM");
   static constexpr int B_FULL = 0, B_EMPTY = NST, B_ACCF = 2 * NST, B_ACCE = 2 * NST + 2;
   static constexpr uint32_t TMEM_SLOT = 192;               // byte offset of the TMEM address in the barrier area
   static constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
@@ -105,6 +116,7 @@ __device__ __forceinline__ void tma_reduce_add_2d(const void* map, uint32_t src,
                ::"l"(map), "r"(src), "r"(c0), "r"(c1) : "memory");
 }
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
@@ -130,14 +142,37 @@ __device__ __forceinline__ void tile_coords(const GemmParams& p, int t, int& mb,
   nb = r / rows;
 }
 
-// One epilogue step of a warp: 32 accumulator rows (its TMEM lane quarter) x 128 bytes of C (32 fp32
-// or 64 bf16/fp16 columns) from tensor memory into a 128-byte-swizzled staging box, then one TMA store
-// of the box (rows and columns beyond C are clipped by the tensor map). Two boxes per warp alternate,
-// so a box is rewritten only after the store issued from it two steps earlier has read it.
-template <int OUT, bool kHalf>
-__device__ __forceinline__ void epilogue_box(const GemmParams& p, uint32_t taddr, uint32_t box, int lane, int col,
-                                             int row0, int& nbox) {
-  constexpr int COLS = OUT == GEMM_OUT_F32 ? 32 : 64;
+// Staging: a warp's 32 rows x 128 bytes of C go into a 128-byte-swizzled box (row r's 16-byte chunk q
+// at r * 128 + ((q ^ (r & 7)) << 4): one st.shared.v4 per chunk and thread, no bank conflicts beyond
+// the 4 wavefronts a 512-byte warp store needs), then one TMA store of the box (rows and columns
+// beyond C are clipped by the tensor map). With NBOX boxes per warp, a box is rewritten only after
+// the store issued from it NBOX steps earlier has read it.
+template <int NBOX>
+__device__ __forceinline__ uint32_t stage_and_store(const GemmParams& p, const uint32_t* w, uint32_t boxes, int lane,
+                                                    int col, int row0, int& nbox, bool reduce) {
+  const uint32_t box = boxes + (uint32_t)(nbox % NBOX) * 4096u;
+  if (lane == 0 && nbox >= NBOX) {
+    if constexpr (NBOX == 1) bulk_wait_read0(); else bulk_wait_read1();
+  }
+  __syncwarp();
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    st_shared_v4(box + sw128_off((uint32_t)lane, (uint32_t)q), w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (reduce) tma_reduce_add_2d(&p.tm_c, box, col, row0);
+    else tma_store_2d(&p.tm_c, box, col, row0);
+    bulk_commit();
+  }
+  ++nbox;
+  return box;
+}
+
+// Epilogue EPI_STORE: one 128-byte box (32 fp32 or 64 bf16/fp16 columns) of the warp's 32 rows.
+template <int OUT, int NBOX>
+__device__ __forceinline__ void epilogue_store(const GemmParams& p, uint32_t taddr, uint32_t boxes, int lane, int col,
+                                               int row0, int& nbox) {
   uint32_t w[32];
   if constexpr (OUT == GEMM_OUT_F32) {
     tmem_ld32(taddr, reinterpret_cast<float*>(w));
@@ -152,26 +187,88 @@ __device__ __forceinline__ void epilogue_box(const GemmParams& p, uint32_t taddr
       for (int i = 0; i < 16; ++i) w[16 * half + i] = pack2<OUT == GEMM_OUT_F16>(v[2 * i], v[2 * i + 1]);
     }
   }
-  if (lane == 0 && nbox >= 2) bulk_wait_read1();
-  __syncwarp();
-#pragma unroll
-  for (int q = 0; q < 8; ++q)
-    st_shared_v4(box + sw128_off((uint32_t)lane, (uint32_t)q), w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-  fence_proxy_async_smem();
-  __syncwarp();
-  if (lane == 0) {
-    if (OUT == GEMM_OUT_F32 && p.accumulate) tma_reduce_add_2d(&p.tm_c, box, col, row0);
-    else tma_store_2d(&p.tm_c, box, col, row0);
-    bulk_commit();
-  }
-  ++nbox;
-  (void)COLS;
+  stage_and_store<NBOX>(p, w, boxes, lane, col, row0, nbox, OUT == GEMM_OUT_F32 && p.accumulate);
 }
 
-template <int OUT, bool kHalf, bool A_MN, bool B_MN, bool kWide>
-__global__ void __launch_bounds__(192, 1) gemm_pair_kernel(const __grid_constant__ GemmParams p) {
+// Maximum of two packed pairs of bf16 / fp16 values, lane by lane, NaN if either is NaN.
+template <bool kHalf>
+__device__ __forceinline__ uint32_t max2_nan(uint32_t a, uint32_t b) {
+  uint32_t r;
+  if constexpr (kHalf) asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  else asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// Epilogue EPI_LCE (the linear-CE logits, C = X W^T in the compute dtype): the warp's one 64-column box
+// of its 32 rows, stored like EPI_STORE, and folded into the thread's running maximum m (log2 units) /
+// sum s of 2^(x log2 e - m) over the rounded logits x of the real vocabulary columns (col < V; a NaN
+// logit makes both NaN), and the label's logit when it lies in the box. The maximum is taken on the
+// packed rounded values (exact), and the sum in four independent chains.
+template <bool kHalf, int NBOX>
+__device__ __forceinline__ void epilogue_lce(const GemmParams& p, uint32_t taddr, uint32_t boxes, int lane, int col,
+                                             int row0, int& nbox, int64_t lab, float& m, float& s, float& tgt,
+                                             bool& has_tgt) {
+  constexpr float kLog2e = 1.4426950408889634f;
+  uint32_t w[32];
+  {
+    float v[64];
+    tmem_ld32(taddr, v);
+    tmem_ld32(taddr + 32u, v + 32);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) w[i] = pack2<kHalf>(v[2 * i], v[2 * i + 1]);
+  }
+  const uint32_t box = stage_and_store<NBOX>(p, w, boxes, lane, col, row0, nbox, false);
+  const int64_t d = lab - col;
+  if (d >= 0 && d < 64) {
+    // the label's rounded logit, read back from this thread's row of the staging box
+    uint16_t h;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h)
+                 : "r"(box + sw128_off((uint32_t)lane, (uint32_t)(d >> 3)) + 2u * (uint32_t)(d & 7)));
+    tgt = unpack_lo<kHalf>((uint32_t)h);
+    has_tgt = true;
+  }
+  float mc;
+  const bool full = col + 64 <= p.V;
+  if (full) {
+    uint32_t q[4] = {w[0], w[1], w[2], w[3]};
+#pragma unroll
+    for (int i = 4; i < 32; ++i) q[i & 3] = max2_nan<kHalf>(q[i & 3], w[i]);
+    const uint32_t qq = max2_nan<kHalf>(max2_nan<kHalf>(q[0], q[1]), max2_nan<kHalf>(q[2], q[3]));
+    mc = max_nan(unpack_lo<kHalf>(qq), unpack_hi<kHalf>(qq)) * kLog2e;
+  } else {
+    mc = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const float x = (i & 1) ? unpack_hi<kHalf>(w[i >> 1]) : unpack_lo<kHalf>(w[i >> 1]);
+      if (col + i < p.V) mc = max_nan(mc, x * kLog2e);
+    }
+  }
+  const float mn = max_nan(m, mc);
+  if (mn != -INFINITY) {
+    float a[4] = {(m == -INFINITY) ? 0.f : s * ex2_approx(m - mn), 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float lo = unpack_lo<kHalf>(w[i]), hi = unpack_hi<kHalf>(w[i]);
+      const float elo = ex2_approx(fmaf(lo, kLog2e, -mn)), ehi = ex2_approx(fmaf(hi, kLog2e, -mn));
+      a[i & 3] += (full || col + 2 * i < p.V ? elo : 0.f) + (full || col + 2 * i + 1 < p.V ? ehi : 0.f);
+    }
+    s = (a[0] + a[1]) + (a[2] + a[3]);
+  }
+  m = mn;
+}
+
+template <int EPI, int OUT, bool kHalf, bool A_MN, bool B_MN, bool kWide>
+__global__ void __launch_bounds__(Cfg<kWide>::NTHREADS, 1) gemm_pair_kernel(const __grid_constant__ GemmParams p) {
   using C = Cfg<kWide>;
-  constexpr int NST = C::NST, BN = C::BN, NBUF = C::NBUF, NHALF = C::NHALF;
+  constexpr int NST = C::NST, BN = C::BN, NBUF = C::NBUF, NHALF = C::NHALF, NBOX = C::NBOX, NEPI = C::NEPI;
+  constexpr int CW = C::CW;
+  constexpr int WP = NEPI, WM = NEPI + 1;                  // producer and UMMA warps
   extern __shared__ uint8_t smem_raw[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t rank = cluster_rank();
@@ -184,11 +281,11 @@ __global__ void __launch_bounds__(192, 1) gemm_pair_kernel(const __grid_constant
 #define BAR(i) (bar0 + 8u * (uint32_t)(i))
   if (tid == 0) {
     for (int s = 0; s < NST; ++s) { mbar_init(BAR(C::B_FULL + s), 1); mbar_init(BAR(C::B_EMPTY + s), 1); }
-    for (int b = 0; b < 2; ++b) { mbar_init(BAR(C::B_ACCF + b), 1); mbar_init(BAR(C::B_ACCE + b), 8); }
+    for (int b = 0; b < 2; ++b) { mbar_init(BAR(C::B_ACCF + b), 1); mbar_init(BAR(C::B_ACCE + b), 2 * NEPI); }
     fence_barrier_init();
   }
-  if (warp == 5) { tmem_alloc_pair(smem_u32(tmem_slot), TMEM_COLS); tmem_relinquish_pair(); }
-  if (warp == 4 && lane == 0) { tma_prefetch_desc(&p.tm_a); tma_prefetch_desc(&p.tm_b); tma_prefetch_desc(&p.tm_c); }
+  if (warp == WM) { tmem_alloc_pair(smem_u32(tmem_slot), TMEM_COLS); tmem_relinquish_pair(); }
+  if (warp == WP && lane == 0) { tma_prefetch_desc(&p.tm_a); tma_prefetch_desc(&p.tm_b); tma_prefetch_desc(&p.tm_c); }
   tc_fence_before();
   __syncthreads();
   cluster_sync();          // the leader's barriers exist before the peer's loads and arrivals reach them
@@ -198,7 +295,7 @@ __global__ void __launch_bounds__(192, 1) gemm_pair_kernel(const __grid_constant
   const int cid = (int)blockIdx.x >> 1, ncl = (int)gridDim.x >> 1;
   const int nk = (p.K + BK - 1) / BK;
 
-  if (warp == 4) {
+  if (warp == WP) {
     // ---------------------------------------------------------------- TMA producer (both CTAs)
     if (lane == 0) {
       const uint32_t full_leader = map_rank(BAR(C::B_FULL), 0);
@@ -237,7 +334,7 @@ __global__ void __launch_bounds__(192, 1) gemm_pair_kernel(const __grid_constant
       for (int i = it - NST < 0 ? 0 : it - NST; ok && i < it; ++i)
         ok = mbar_wait<true>(BAR(C::B_EMPTY + i % NST), (i / NST) & 1, p.status);
     }
-  } else if (warp == 5) {
+  } else if (warp == WM) {
     // ---------------------------------------------------------------- UMMA issuer (leader CTA)
     if (leader && lane == 0) {
       constexpr uint32_t idesc = make_idesc(2 * BMC, 256, kHalf ? 0 : 1, A_MN ? 1 : 0, B_MN ? 1 : 0);
@@ -297,27 +394,46 @@ __global__ void __launch_bounds__(192, 1) gemm_pair_kernel(const __grid_constant
       }
     }
   } else {
-    // ---------------------------------------------------------------- epilogue warps 0-3 (both CTAs)
-    constexpr int COLS = OUT == GEMM_OUT_F32 ? 32 : 64;   // columns per 128-byte staging row
+    // ---------------------------------------------------------------- epilogue warps (both CTAs)
+    constexpr int COLS = (EPI == EPI_STORE && OUT == GEMM_OUT_F32) ? 32 : 64;   // columns per 128-byte box row
+    static_assert(EPI == EPI_STORE || CW == 64, "the linear-CE epilogue takes one 64-column box per warp");
+    const int quarter = warp & 3, cgroup = warp >> 2;
     const uint32_t acce_leader = map_rank(BAR(C::B_ACCE), 0);
-    const uint32_t boxes = sbase + C::OFF_EPI + (uint32_t)warp * 2 * C::SZ_EPI;
+    const uint32_t boxes = sbase + C::OFF_EPI + (uint32_t)warp * NBOX * C::SZ_EPI;
     int tl = 0, nbox = 0;
     for (int t = cid; t < ntiles; t += ncl, ++tl) {
       int mb, nb;
       tile_coords(p, t, mb, nb);
       const int buf = tl % NBUF;
+      const int row0 = mb * 2 * BMC + (int)rank * BMC + quarter * 32;
+      int64_t lab = -1;
+      if constexpr (EPI == EPI_LCE) {
+        if (row0 + lane < p.M) lab = p.labels[row0 + lane];   // in flight during the wait below
+      }
       if (!warp_wait(BAR(C::B_ACCF + buf), (tl / NBUF) & 1, p.status)) break;
       tc_fence_after();
-      const int row0 = mb * 2 * BMC + (int)rank * BMC + warp * 32;
+      const uint32_t tlane = tbase + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
       for (int h = 0; h < NHALF; ++h) {
-        // columns of half h: 256 h + 128 r + j come from CTA r's B rows n0 + 256 h + j
+        // columns 256 h + 128 r + j of the tile come from CTA r's B rows n0 + 256 h + j; this warp
+        // takes the CW columns from 256 h + CW cgroup
+        const int cbase = nb * BN + 256 * h + CW * cgroup;
+        const uint32_t tcol = (uint32_t)((buf * NHALF + h) * 256 + CW * cgroup);
+        if constexpr (EPI == EPI_LCE) {
+          const int row = row0 + lane;
+          float m = -INFINITY, sum = 0.f, tgt = 0.f;
+          bool has_tgt = false;
+          if (row0 < p.M && cbase < p.N)
+            epilogue_lce<kHalf, NBOX>(p, tlane + tcol, boxes, lane, cbase, row0, nbox, lab, m, sum, tgt, has_tgt);
+          if (row < p.M && cbase < p.N) {
+            p.part[(int64_t)row * p.n_part + cbase / 64] = make_float2(m, sum);
+            if (has_tgt) p.tgt[row] = tgt;
+          }
+        } else {
 #pragma unroll 1
-        for (int c0 = 0; c0 < 256; c0 += COLS) {
-          const int col = nb * BN + 256 * h + c0;
-          if (col < p.N && row0 < p.M)
-            epilogue_box<OUT, kHalf>(p, tbase + ((uint32_t)(warp * 32) << 16) + (uint32_t)((buf * NHALF + h) * 256 + c0),
-                                     boxes + (uint32_t)(nbox & 1) * C::SZ_EPI, lane, col, row0, nbox);
+          for (int c0 = 0; c0 < CW; c0 += COLS)
+            if (row0 < p.M && cbase + c0 < p.N)
+              epilogue_store<OUT, NBOX>(p, tlane + tcol + (uint32_t)c0, boxes, lane, cbase + c0, row0, nbox);
         }
         tc_fence_before();
         __syncwarp();
@@ -329,7 +445,7 @@ __global__ void __launch_bounds__(192, 1) gemm_pair_kernel(const __grid_constant
   tc_fence_before();
   __syncthreads();
   cluster_sync();          // neither CTA frees its memory while the pair's UMMAs may still use it
-  if (warp == 5) {
+  if (warp == WM) {
     tc_fence_after();
     tmem_dealloc_pair(tbase, TMEM_COLS);
   }
@@ -341,7 +457,7 @@ __global__ void __launch_bounds__(192, 1) gemm_pair_kernel(const __grid_constant
 // The grid is the number of CTA pairs that can be resident at once (not every GPC holds an even
 // number of SMs), capped by the number of tiles: the tile loop is persistent, so a pair that had to
 // wait for a free SM pair would add a whole tile's time at the end.
-template <int OUT, bool H, bool W>
+template <int EPI, int OUT, bool H, bool W>
 static cudaError_t launch_majors(GemmParams p, int a_mn, int b_mn, int num_sms, cudaStream_t st) {
   using namespace gemm;
   p.num_n = (p.N + Cfg<W>::BN - 1) / Cfg<W>::BN;
@@ -353,7 +469,7 @@ static cudaError_t launch_majors(GemmParams p, int a_mn, int b_mn, int num_sms, 
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
-    cfg.blockDim = dim3(192);
+    cfg.blockDim = dim3(Cfg<W>::NTHREADS);
     cfg.gridDim = dim3(2 * (num_sms / 2));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -369,16 +485,20 @@ static cudaError_t launch_majors(GemmParams p, int a_mn, int b_mn, int num_sms, 
     cfg.gridDim = dim3(2 * pairs);
     return cudaLaunchKernelEx(&cfg, kernel, p);
   };
-  if (a_mn && b_mn) return run(gemm_pair_kernel<OUT, H, true, true, W>);
-  if (a_mn) return run(gemm_pair_kernel<OUT, H, true, false, W>);
-  if (b_mn) return run(gemm_pair_kernel<OUT, H, false, true, W>);
-  return run(gemm_pair_kernel<OUT, H, false, false, W>);
+  if constexpr (EPI == EPI_LCE) {
+    return run(gemm_pair_kernel<EPI, OUT, H, false, false, W>);     // X and W rows are K-major
+  } else {
+    if (a_mn && b_mn) return run(gemm_pair_kernel<EPI, OUT, H, true, true, W>);
+    if (a_mn) return run(gemm_pair_kernel<EPI, OUT, H, true, false, W>);
+    if (b_mn) return run(gemm_pair_kernel<EPI, OUT, H, false, true, W>);
+    return run(gemm_pair_kernel<EPI, OUT, H, false, false, W>);
+  }
 }
 
 template <int OUT, bool H>
 static cudaError_t launch_shape(const GemmParams& p, int a_mn, int b_mn, int wide, int num_sms, cudaStream_t st) {
-  return wide ? launch_majors<OUT, H, true>(p, a_mn, b_mn, num_sms, st)
-              : launch_majors<OUT, H, false>(p, a_mn, b_mn, num_sms, st);
+  return wide ? launch_majors<EPI_STORE, OUT, H, true>(p, a_mn, b_mn, num_sms, st)
+              : launch_majors<EPI_STORE, OUT, H, false>(p, a_mn, b_mn, num_sms, st);
 }
 
 cudaError_t launch_gemm(const GemmParams& p, int in_dtype, int a_mn, int b_mn, int out, int wide, int num_sms,
@@ -390,6 +510,11 @@ cudaError_t launch_gemm(const GemmParams& p, int in_dtype, int a_mn, int b_mn, i
                                      : launch_shape<GEMM_OUT_BF16, false>(p, a_mn, b_mn, wide, num_sms, st);
   return h ? launch_shape<GEMM_OUT_F16, true>(p, a_mn, b_mn, wide, num_sms, st)
            : launch_shape<GEMM_OUT_F16, false>(p, a_mn, b_mn, wide, num_sms, st);
+}
+
+cudaError_t launch_lce_logits_gemm(const GemmParams& p, int in_dtype, int num_sms, cudaStream_t st) {
+  return in_dtype == 1 ? launch_majors<EPI_LCE, GEMM_OUT_F16, true, false>(p, 0, 0, num_sms, st)
+                       : launch_majors<EPI_LCE, GEMM_OUT_BF16, false, false>(p, 0, 0, num_sms, st);
 }
 
 }  // namespace sisa

@@ -1,22 +1,10 @@
-// Host-side launch parameters of the linear + cross-entropy kernels (lce.cu).
+// Host-side launch parameters of the linear + cross-entropy kernels of lce.cu (the logits GEMM is in gemm.cu).
 #pragma once
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 
 namespace sisa {
-
-struct LceParams {
-  CUtensorMap tm_x;        // (D, R) rows of the chunk, box (64, 128), 128B swizzle
-  CUtensorMap tm_w;        // (D, Vp) padded weight rows, box (64, 256), 128B swizzle
-  char* logits;            // (R, ld) low precision, row-major
-  int64_t ld;
-  float2* part;            // (R, n_nblk) {max, sum 2^(x log2e - max)} in log2 units
-  float* tgt;              // (R) target logit
-  const int64_t* labels;   // (R)
-  int R, D, V, Vp, n_mblk, n_nblk;
-  int32_t* status;
-};
 
 struct LceGradParams {
   char* logits;
@@ -32,7 +20,9 @@ struct LceGradParams {
   int32_t* status;
 };
 
-cudaError_t launch_lce_logits(const LceParams& p, int dtype, int num_sms, cudaStream_t st);
 cudaError_t launch_lce_grad(const LceGradParams& p, int dtype, cudaStream_t st);
+// out_dtype: 0 bf16, 1 fp16, 2 fp32 (out null: in place).
+cudaError_t launch_seed_scale(float* x, int64_t n, const float* seed, void* out, int out_dtype, int num_sms,
+                              cudaStream_t st);
 
 }  // namespace sisa

@@ -98,7 +98,12 @@ def _(x, w_pad, labels, vocab, ignore_index, rows, need_dx, need_dw, grad_scale)
 
 
 class _LinearCE(torch.autograd.Function):
-    """Loss in the forward together with the unscaled (or promised-scale) gradients; the backward scales."""
+    """Loss in the forward together with the unscaled (or promised-scale) gradients; the backward scales.
+
+    Eagerly the backward hands out the gradient buffers themselves, multiplied by the seed in place (not
+    at all for a seed of 1, decided on the device), rather than fresh products, so a second backward
+    through the same graph (``retain_graph=True``) is refused. Traced by torch.compile it returns the
+    products ``seed * buffer`` as new tensors."""
 
     @staticmethod
     def forward(ctx, hidden, weight, labels, ignore_index, rows, cdtype, grad_scale):
@@ -114,6 +119,7 @@ class _LinearCE(torch.autograd.Function):
                             chunk_rows(x.shape[0], Vp, x.element_size(), rows), need_dx, need_dw,
                             1.0 if grad_scale is None else float(grad_scale))
         ctx.save_for_backward(dx, dw)
+        ctx.handed = False
         ctx.meta = (hidden.shape, hidden.dtype, weight.dtype, V, grad_scale)
         return loss
 
@@ -122,19 +128,48 @@ class _LinearCE(torch.autograd.Function):
     def backward(ctx, seed):
         dx, dw = ctx.saved_tensors
         h_shape, h_dtype, w_dtype, V, grad_scale = ctx.meta
-        dh = dW = None
+        dev = seed.device
         if grad_scale is not None:
             # the gradients already carry the promised seed; a different one sets a status bit
             mismatch = (seed.float() != float(grad_scale)).to(torch.int32) * _lib.ST_BAD_SEED
-            backends.status_word(seed.device).bitwise_or_(mismatch.reshape(1))
-            backends.after_call(seed.device)
-            scale = None
+            backends.status_word(dev).bitwise_or_(mismatch.reshape(1))
+            backends.after_call(dev)
+        if torch.compiler.is_compiling():
+            scale = None if grad_scale is not None else seed.float()
+            dh = dW = None
+            if ctx.needs_input_grad[0]:
+                dh = (dx if scale is None else dx * scale).view(h_shape).to(h_dtype)
+            if ctx.needs_input_grad[1]:
+                dW = (dw[:V] if scale is None else dw[:V] * scale).to(w_dtype)
+            return dh, dW, None, None, None, None, None
+        if ctx.handed:
+            raise RuntimeError("linear_cross_entropy: backward ran twice through one graph; its gradient buffers "
+                               "went to the first call (retain_graph is not supported)")
+        ctx.handed = True
+        if grad_scale is not None:
+            seed32 = torch.ones(1, dtype=torch.float32, device=dev)
         else:
-            scale = seed.float()
+            seed32 = seed.detach().to(torch.float32).reshape(1).contiguous()
+        lib = _lib.load()
+        st, sp = backends.status_word(dev).data_ptr(), _lib.stream_ptr(dev)
+
+        def scaled(buf, n, dtype):
+            if n == 0:
+                return torch.empty(0, dtype=dtype, device=dev)
+            if dtype in (torch.bfloat16, torch.float16):
+                out = torch.empty(n, dtype=dtype, device=dev)
+                _lib.check(lib.sisa_lce_seed_scale(buf.data_ptr(), n, seed32.data_ptr(), out.data_ptr(),
+                                                   _lib.dtype_code(dtype), st, sp), "sisa_lce_seed_scale")
+                return out
+            _lib.check(lib.sisa_lce_seed_scale(buf.data_ptr(), n, seed32.data_ptr(), None, _lib.F32, st, sp),
+                       "sisa_lce_seed_scale")
+            return buf.reshape(-1)[:n].to(dtype)
+
+        dh = dW = None
         if ctx.needs_input_grad[0]:
-            dh = (dx if scale is None else dx * scale).view(h_shape).to(h_dtype)
+            dh = scaled(dx, dx.numel(), h_dtype).view(h_shape)
         if ctx.needs_input_grad[1]:
-            dW = (dw[:V] if scale is None else dw[:V] * scale).to(w_dtype)
+            dW = scaled(dw, V * dw.shape[1], w_dtype).view(V, dw.shape[1])
         return dh, dW, None, None, None, None, None
 
 

@@ -87,3 +87,31 @@ def test_lce_nan_propagates(cuda_dev):
     assert torch.isnan(loss)
     with pytest.raises(FloatingPointError):
         backends.check_status(0)
+
+
+def test_lce_backward_seed_and_dtypes(cuda_dev):
+    """The backward multiplies the stored gradients by its seed on the device (nothing to do for 1), in
+    the dtypes of hidden and weight; a second backward through one graph is refused."""
+    from sisa_b200.kernels.linear_ce import linear_cross_entropy
+
+    h, w, labels = make_case(300, 128, 1003, seed=6)
+    lab = labels.to(cuda_dev)
+    grads = {}
+    for seed in (1.0, 3.0):
+        H = h.to(cuda_dev).requires_grad_(True)
+        W = w.to(cuda_dev).requires_grad_(True)
+        (linear_cross_entropy(H, W, lab) * seed).backward()
+        grads[seed] = (H.grad, W.grad)
+    assert grads[3.0][0].dtype == torch.bfloat16 and grads[3.0][1].dtype == torch.float32
+    assert torch.equal(grads[3.0][1], grads[1.0][1] * 3.0)          # fp32 dW: the same product
+    assert rel_err(grads[3.0][0].float(), grads[1.0][0].float() * 3.0) <= 1e-2
+    # fp32 hidden under autocast: dh comes back fp32
+    H = h.float().to(cuda_dev).requires_grad_(True)
+    W = w.to(cuda_dev).requires_grad_(True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        loss = linear_cross_entropy(H, W, lab)
+    (loss * 2.0).backward(retain_graph=True)
+    assert H.grad.dtype == torch.float32
+    assert rel_err(H.grad, grads[1.0][0].float() * 2.0) <= 1e-2
+    with pytest.raises(RuntimeError, match="retain_graph"):
+        loss.backward()
