@@ -155,16 +155,32 @@ int sisa_lce_grad(void* logits, int64_t logits_ld, int64_t R, int64_t V, int64_t
 int sisa_lce_seed_scale(float* x, int64_t n, const float* seed, void* out, int out_dtype, int32_t* status,
                         void* stream);
 
-/* C (+)= A . B^T on CTA pairs of tcgen05 tensor cores (the linear-CE gradient GEMMs, replacing the
- * torch.matmul calls of src/sisa/kernels/linear_ce.py:170-178). A is M x K and B is N x K in `dtype`
+/* C (+)= A . B^T (+ bias) on CTA pairs of tcgen05 tensor cores: the linear-CE gradient GEMMs (the
+ * torch.matmul calls of src/sisa/kernels/linear_ce.py:170-178) and the model's linears under autocast
+ * (F.linear of src/sisa/modeling.py:39-49, 213-222, 255). A is M x K and B is N x K in `dtype`
  * (SISA_BF16 / SISA_F16), each K-major (element (r, k) at r * ld + k; a_mn / b_mn = 0) or MN-major
  * (element (r, k) at k * ld + r; = 1); C is M x N row-major in out_dtype (SISA_F32, SISA_BF16 or
- * SISA_F16) with fp32 accumulation and one rounding; accumulate = 1 (fp32 C only) adds to C. Pointers
- * 16-byte aligned, row strides in elements covering a row and whole 16-byte units; 1 <= M, N, K <= 2^30.
+ * SISA_F16) with fp32 accumulation and one rounding; accumulate = 1 (fp32 C only) adds to C. bias
+ * (optional, N values of bias_dtype) is added in fp32 before the rounding. workspace (optional,
+ * sisa_gemm_workspace(M, N, K, out_dtype) bytes on the current device, 0 when no split is wanted; used
+ * by one stream at a time) lets a small fp32 problem split K across CTA pairs: each slice writes an
+ * fp32 partial and the last slice of a tile sums them in slice order (deterministic). Pointers 16-byte
+ * aligned, row strides in elements covering a row and whole 16-byte units; 1 <= M, N, K <= 2^30.
  * Waits are bounded (SISA_ST_TIMEOUT). */
+int64_t sisa_gemm_workspace(int64_t M, int64_t N, int64_t K, int out_dtype);
 int sisa_gemm(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn, void* c, int64_t ldc,
-              int64_t M, int64_t N, int64_t K, int dtype, int out_dtype, int accumulate, int32_t* status,
-              void* stream);
+              int64_t M, int64_t N, int64_t K, int dtype, int out_dtype, int accumulate, const void* bias,
+              int bias_dtype, void* workspace, int64_t workspace_bytes, int32_t* status, void* stream);
+
+/* The SwiGLU MLP's gate and up projections with the activation in the epilogue (src/sisa/modeling.py:39-49:
+ * w_gate x, w_up x and silu(.) * (.), which the reference runs as two GEMMs and two elementwise kernels).
+ * w (2 d_ff, K): the gate and up weights interleaved in blocks of 8 rows (gate rows 8b .. 8b + 7, then
+ * up rows 8b .. 8b + 7, b = 0 .. d_ff / 8 - 1), K-major like x (rows, K), both in `dtype`. Outputs:
+ * gu (rows, 2 d_ff), the projections in the same interleaved column order rounded to `dtype` (what the
+ * backward reads), and a (rows, d_ff) = silu(g) * u computed in fp32 from the rounded g, u with one
+ * rounding (sisa_swiglu_fwd's arithmetic). d_ff a multiple of 8; 16-byte aligned rows. */
+int sisa_gemm_swiglu(const void* x, int64_t x_ld, const void* w, int64_t w_ld, void* gu, int64_t gu_ld, void* a,
+                     int64_t a_ld, int64_t rows, int64_t d_ff, int64_t K, int dtype, int32_t* status, void* stream);
 
 /* Fused RMSNorm and SwiGLU activation of the model's blocks (src/sisa/modeling.py:25-49). Element
  * types SISA_BF16, SISA_F16 or SISA_F32; row strides (x_ld ...) in elements, unit inner stride.

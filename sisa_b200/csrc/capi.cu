@@ -654,10 +654,61 @@ int sisa_lce_seed_scale(float* x, int64_t n, const float* seed, void* out, int o
   return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_lce_seed_scale launch");
 }
 
+// ------------------------------------------------------------------------------------ SwiGLU gate/up GEMM
+int sisa_gemm_swiglu(const void* x, int64_t x_ld, const void* w, int64_t w_ld, void* gu, int64_t gu_ld, void* a,
+                     int64_t a_ld, int64_t rows, int64_t d_ff, int64_t K, int dtype, int32_t* status, void* stream) {
+  int rc;
+  if ((rc = check_dtype(dtype))) return rc;
+  if (!x || !w || !gu || !a) return fail(SISA_ERR_VALUE, "sisa_gemm_swiglu: null pointer");
+  const int64_t lim = (int64_t)1 << 30;
+  if (rows < 1 || d_ff < 8 || d_ff % 8 || K < 1 || rows > lim || 2 * d_ff > lim || K > lim)
+    return fail(SISA_ERR_VALUE, "sisa_gemm_swiglu: need rows >= 1, d_ff a positive multiple of 8, K >= 1 "
+                "(rows=%lld d_ff=%lld K=%lld)", (long long)rows, (long long)d_ff, (long long)K);
+  if (!aligned16(x) || !aligned16(w) || !aligned16(gu) || !aligned16(a) || x_ld % 8 || w_ld % 8 || gu_ld % 8 ||
+      a_ld % 8 || x_ld < K || w_ld < K || gu_ld < 2 * d_ff || a_ld < d_ff)
+    return fail(SISA_ERR_ALIGN, "sisa_gemm_swiglu: rows must be 16-byte aligned (ld multiple of 8 and >= width)");
+  sisa::DeviceScope scope;
+  if ((rc = scope.bind(x))) return rc;
+  const CUtensorMapDataType dt = dtype == SISA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  sisa::GemmParams p;
+  memset(&p, 0, sizeof(p));
+  if ((rc = map_operand(&p.tm_a, x, x_ld, 0, rows, K, dt, "x"))) return rc;
+  if ((rc = map_operand(&p.tm_b, w, w_ld, 0, 2 * d_ff, K, dt, "w"))) return rc;
+  if ((rc = map_output(&p.tm_c, gu, gu_ld, rows, 2 * d_ff, dtype))) return rc;
+  {
+    EncodeTiledFn enc = encode_fn();
+    cuuint64_t dims[2] = {(cuuint64_t)d_ff, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(a_ld * 2)};
+    cuuint32_t box[2] = {32, 32}, es[2] = {1, 1};
+    if (enc(&p.tm_c2, dt, 2, a, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return fail(SISA_ERR_ALIGN, "a: cuTensorMapEncodeTiled failed");
+  }
+  p.ldc = gu_ld;
+  p.M = (int)rows; p.N = (int)(2 * d_ff); p.K = (int)K;
+  p.num_m = (int)((rows + 255) / 256);
+  p.status = status;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, scope.device());
+  cudaError_t e = sisa::launch_gemm_swiglu(p, dtype, sms, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_gemm_swiglu launch");
+}
+
 // ------------------------------------------------------------------------------------ GEMM
+int64_t sisa_gemm_workspace(int64_t M, int64_t N, int64_t K, int out_dtype) {
+  if (M < 1 || N < 1 || K < 1) return 0;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaGetLastError();
+  const int out = out_dtype == SISA_F32 ? sisa::GEMM_OUT_F32 : out_dtype == SISA_BF16 ? sisa::GEMM_OUT_BF16
+                                                                                        : sisa::GEMM_OUT_F16;
+  return sisa::gemm_workspace_bytes(M, N, K, out, sms);
+}
+
 int sisa_gemm(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn, void* c, int64_t ldc,
-              int64_t M, int64_t N, int64_t K, int dtype, int out_dtype, int accumulate, int32_t* status,
-              void* stream) {
+              int64_t M, int64_t N, int64_t K, int dtype, int out_dtype, int accumulate, const void* bias,
+              int bias_dtype, void* workspace, int64_t workspace_bytes, int32_t* status, void* stream) {
   int rc;
   if ((rc = check_dtype(dtype))) return rc;
   if (!a || !b || !c) return fail(SISA_ERR_VALUE, "sisa_gemm: null pointer");
@@ -676,11 +727,18 @@ int sisa_gemm(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, 
     return fail(SISA_ERR_ALIGN, "sisa_gemm: operands and C must be 16-byte aligned with row strides of whole "
                 "16-byte units covering their rows (lda=%lld ldb=%lld ldc=%lld)", (long long)lda, (long long)ldb,
                 (long long)ldc);
+  if (bias && ((bias_dtype != SISA_BF16 && bias_dtype != SISA_F16 && bias_dtype != SISA_F32) || !aligned16(bias)))
+    return fail(SISA_ERR_VALUE, "sisa_gemm: bias must be 16-byte aligned SISA_BF16, SISA_F16 or SISA_F32");
+  if (workspace && (!aligned16(workspace) || workspace_bytes < 0))
+    return fail(SISA_ERR_VALUE, "sisa_gemm: workspace must be 16-byte aligned");
   sisa::DeviceScope scope;
   if ((rc = scope.bind(a))) return rc;
   const CUtensorMapDataType dt = dtype == SISA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   sisa::GemmParams p;
   memset(&p, 0, sizeof(p));
+  p.bias = bias;
+  p.bias_dtype = bias_dtype == SISA_F32 ? 2 : bias_dtype == SISA_F16 ? 1 : 0;
+  if (workspace && workspace_bytes > 0) { p.sema = static_cast<uint32_t*>(workspace); p.ws_bytes = workspace_bytes; }
   if ((rc = map_operand(&p.tm_a, a, lda, a_mn, M, K, dt, "a"))) return rc;
   if ((rc = map_operand(&p.tm_b, b, ldb, b_mn, N, K, dt, "b"))) return rc;
   if ((rc = map_output(&p.tm_c, c, ldc, M, N, out_dtype))) return rc;
@@ -693,12 +751,12 @@ int sisa_gemm(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, 
                                                                                         : sisa::GEMM_OUT_F16;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, scope.device());
-  int wide = K >= 2048 && N >= 512;
-  if (const char* tile = getenv("SISA_GEMM_TILE")) {
-    if (!strcmp(tile, "wide")) wide = 1;
-    else if (!strcmp(tile, "narrow")) wide = 0;
+  int tile = -1;                             // chosen per problem; the variable forces a shape (tuning, tests)
+  if (const char* t = getenv("SISA_GEMM_TILE")) {
+    if (!strcmp(t, "wide")) tile = 1;
+    else if (!strcmp(t, "narrow")) tile = 0;
   }
-  cudaError_t e = sisa::launch_gemm(p, dtype, a_mn, b_mn, out, wide, sms, static_cast<cudaStream_t>(stream));
+  cudaError_t e = sisa::launch_gemm(p, dtype, a_mn, b_mn, out, tile, sms, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_gemm launch");
 }
 

@@ -45,10 +45,10 @@ constexpr uint32_t TMEM_COLS = 512;
 // stages and 8 epilogue warps (128 columns each): a quarter fewer operand bytes per flop from L2, for
 // long K, where the epilogue (which the next tile's UMMAs into each half wait for) is a small part of a
 // tile.
-template <bool kWide>
+template <bool kWide, int EPI = EPI_STORE>
 struct Cfg {
   static constexpr int BN = kWide ? 512 : 256;             // columns of the pair tile
-  static constexpr int NST = kWide ? 4 : 5;
+  static constexpr int NST = kWide || EPI == EPI_SWIGLU ? 4 : 5;
   static constexpr int NBUF = kWide ? 1 : 2;               // accumulator buffers
   static constexpr int NHALF = kWide ? 2 : 1;              // 256-column parts per buffer
   static constexpr int NEPI = kWide ? 8 : 16;              // epilogue warps
@@ -59,7 +59,9 @@ struct Cfg {
   static constexpr uint32_t SZ_STAGE = SZ_HALF + SZ_B;     // A | B
   static constexpr uint32_t OFF_EPI = NST * SZ_STAGE;      // 160 / 192 KB of stages
   static constexpr uint32_t SZ_EPI = 4096;                 // one staging box: 32 rows x 128 bytes
-  static constexpr uint32_t OFF_BAR = OFF_EPI + NEPI * NBOX * SZ_EPI;
+  static constexpr uint32_t SZ_EPI2 = EPI == EPI_SWIGLU ? 2048 : 0;   // SwiGLU: a box of 32 rows x 64 bytes
+  static constexpr uint32_t OFF_EPI2 = OFF_EPI + NEPI * NBOX * SZ_EPI;
+  static constexpr uint32_t OFF_BAR = OFF_EPI2 + NEPI * SZ_EPI2;
   static_assert(NTHREADS * (kWide ? 168 : 112) <= 65536, "register budget of one CTA per SM");
   static constexpr int B_FULL = 0, B_EMPTY = NST, B_ACCF = 2 * NST, B_ACCE = 2 * NST + 2;
   static constexpr uint32_t TMEM_SLOT = 192;               // byte offset of the TMEM address in the barrier area
@@ -119,6 +121,26 @@ __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
+// Split-K: every K slice of a tile writes its fp32 partial of a warp's 32 rows x 64 columns to its own
+// workspace slot (element i of lane l at slot[i * 32 + l]: each warp store is one coalesced 128-byte
+// line) and counts itself in; the slice that arrives last sums the slots in slice order (a fixed
+// order whoever arrives last: deterministic) and stores C. Slots are read past L1 (other SMs wrote them).
+__device__ __forceinline__ void write_partial(float* slot, const float* v, int lane) {
+#pragma unroll
+  for (int i = 0; i < 64; ++i) __stcg(slot + i * 32 + lane, v[i]);
+}
+__device__ __forceinline__ bool arrive_last(uint32_t* counter, int ns, int lane) {
+  __syncwarp();
+  uint32_t old = 0;
+  if (lane == 0) {
+    __threadfence();
+    old = atomicAdd(counter, 1u);
+    __threadfence();
+  }
+  old = __shfl_sync(0xffffffffu, old, 0);
+  return old + 1 == (uint32_t)ns;
+}
+
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
                : "memory");
@@ -169,25 +191,83 @@ __device__ __forceinline__ uint32_t stage_and_store(const GemmParams& p, const u
   return box;
 }
 
-// Epilogue EPI_STORE: one 128-byte box (32 fp32 or 64 bf16/fp16 columns) of the warp's 32 rows.
-template <int OUT, int NBOX>
-__device__ __forceinline__ void epilogue_store(const GemmParams& p, uint32_t taddr, uint32_t boxes, int lane, int col,
-                                               int row0, int& nbox) {
-  uint32_t w[32];
-  if constexpr (OUT == GEMM_OUT_F32) {
-    tmem_ld32(taddr, reinterpret_cast<float*>(w));
-    tmem_wait_ld();
+// bias[col .. col + 7] as fp32 (0 beyond N); the same address in every lane (a broadcast load).
+__device__ __forceinline__ void load_bias8(const GemmParams& p, int col, float* b) {
+  if (col + 8 <= p.N) {
+    if (p.bias_dtype == 2) {
+      const float4 a = reinterpret_cast<const float4*>(p.bias)[col / 4], c = reinterpret_cast<const float4*>(p.bias)[col / 4 + 1];
+      b[0] = a.x; b[1] = a.y; b[2] = a.z; b[3] = a.w; b[4] = c.x; b[5] = c.y; b[6] = c.z; b[7] = c.w;
+    } else {
+      const uint4 u = reinterpret_cast<const uint4*>(p.bias)[col / 8];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        b[2 * i] = p.bias_dtype == 1 ? unpack_lo<true>(w[i]) : unpack_lo<false>(w[i]);
+        b[2 * i + 1] = p.bias_dtype == 1 ? unpack_hi<true>(w[i]) : unpack_hi<false>(w[i]);
+      }
+    }
   } else {
-    float v[32];
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      tmem_ld32(taddr + 32u * half, v);
-      tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 16; ++i) w[16 * half + i] = pack2<OUT == GEMM_OUT_F16>(v[2 * i], v[2 * i + 1]);
+    for (int i = 0; i < 8; ++i) {
+      const int c = col + i;
+      b[i] = c >= p.N ? 0.f
+             : p.bias_dtype == 2 ? static_cast<const float*>(p.bias)[c]
+             : p.bias_dtype == 1 ? __half2float(static_cast<const __half*>(p.bias)[c])
+                                 : __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[c]);
     }
   }
-  stage_and_store<NBOX>(p, w, boxes, lane, col, row0, nbox, OUT == GEMM_OUT_F32 && p.accumulate);
+}
+
+// Epilogue EPI_STORE of 32 fp32 values per thread already in registers (the summed split-K slices).
+template <int NBOX>
+__device__ __forceinline__ void epilogue_store_values(const GemmParams& p, const float* vin, uint32_t boxes, int lane,
+                                                      int col, int row0, int& nbox, bool reduce, bool add_bias) {
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = vin[i];
+  if (add_bias) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      float b[8];
+      load_bias8(p, col + j, b);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[j + i] += b[i];
+    }
+  }
+  uint32_t w[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(v[i]);
+  stage_and_store<NBOX>(p, w, boxes, lane, col, row0, nbox, reduce);
+}
+
+// Epilogue EPI_STORE: one 128-byte box (32 fp32 or 64 bf16/fp16 columns) of the warp's 32 rows, plus
+// the bias when given; `reduce` adds the box into C (fp32) instead of storing it.
+template <int OUT, int NBOX>
+__device__ __forceinline__ void epilogue_store(const GemmParams& p, uint32_t taddr, uint32_t boxes, int lane, int col,
+                                               int row0, int& nbox, bool reduce, bool add_bias) {
+  constexpr int NV = OUT == GEMM_OUT_F32 ? 32 : 64;
+  float v[NV];
+  tmem_ld32(taddr, v);
+  if constexpr (NV == 64) tmem_ld32(taddr + 32u, v + 32);
+  tmem_wait_ld();
+  if (add_bias) {
+#pragma unroll
+    for (int j = 0; j < NV; j += 8) {
+      float b[8];
+      load_bias8(p, col + j, b);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[j + i] += b[i];
+    }
+  }
+  uint32_t w[32];
+  if constexpr (OUT == GEMM_OUT_F32) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(v[i]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) w[i] = pack2<OUT == GEMM_OUT_F16>(v[2 * i], v[2 * i + 1]);
+  }
+  stage_and_store<NBOX>(p, w, boxes, lane, col, row0, nbox, reduce);
 }
 
 // Maximum of two packed pairs of bf16 / fp16 values, lane by lane, NaN if either is NaN.
@@ -263,9 +343,58 @@ __device__ __forceinline__ void epilogue_lce(const GemmParams& p, uint32_t taddr
   m = mn;
 }
 
+// Epilogue EPI_SWIGLU (the gate and up projections of the SwiGLU MLP, W's rows interleaved in blocks
+// of 8: gate rows 8b .. 8b + 7, then up rows 8b .. 8b + 7, for feature block b): the warp's 64 columns
+// hold 32 features. They are stored (C: g and u in that interleaved order, in the compute dtype, as the
+// backward reads them), and a = silu(g) u is computed in fp32 from the rounded g and u (the arithmetic
+// of the separate SwiGLU kernel, one rounding) and stored to the second output, 32 features x 32 rows
+// through a 64-byte-swizzled box.
+template <bool kHalf, int NBOX>
+__device__ __forceinline__ void epilogue_swiglu(const GemmParams& p, uint32_t taddr, uint32_t boxes, uint32_t box2,
+                                                int lane, int col, int row0, int& nbox) {
+  float v[64];
+  tmem_ld32(taddr, v);
+  tmem_ld32(taddr + 32u, v + 32);
+  tmem_wait_ld();
+  uint32_t w[32], a2[16];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) w[i] = pack2<kHalf>(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    float a[8];
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      const uint32_t gw = w[8 * b + j / 2], uw = w[8 * b + 4 + j / 2];
+      const float g0 = unpack_lo<kHalf>(gw), g1 = unpack_hi<kHalf>(gw);
+      const float u0 = unpack_lo<kHalf>(uw), u1 = unpack_hi<kHalf>(uw);
+      a[j] = g0 * (1.f / (1.f + __expf(-g0))) * u0;
+      a[j + 1] = g1 * (1.f / (1.f + __expf(-g1))) * u1;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) a2[4 * b + j] = pack2<kHalf>(a[2 * j], a[2 * j + 1]);
+  }
+  const uint32_t box = boxes + (uint32_t)(nbox % NBOX) * 4096u;
+  if (lane == 0 && nbox >= NBOX) bulk_wait_read0();
+  __syncwarp();
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    st_shared_v4(box + sw128_off((uint32_t)lane, (uint32_t)q), w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    st_shared_v4(box2 + sw64_off((uint32_t)lane, (uint32_t)q), a2[4 * q], a2[4 * q + 1], a2[4 * q + 2], a2[4 * q + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(&p.tm_c, box, col, row0);
+    tma_store_2d(&p.tm_c2, box2, col / 2, row0);
+    bulk_commit();
+  }
+  ++nbox;
+}
+
 template <int EPI, int OUT, bool kHalf, bool A_MN, bool B_MN, bool kWide>
 __global__ void __launch_bounds__(Cfg<kWide>::NTHREADS, 1) gemm_pair_kernel(const __grid_constant__ GemmParams p) {
-  using C = Cfg<kWide>;
+  using C = Cfg<kWide, EPI>;
   constexpr int NST = C::NST, BN = C::BN, NBUF = C::NBUF, NHALF = C::NHALF, NBOX = C::NBOX, NEPI = C::NEPI;
   constexpr int CW = C::CW;
   constexpr int WP = NEPI, WM = NEPI + 1;                  // producer and UMMA warps
@@ -285,15 +414,25 @@ __global__ void __launch_bounds__(Cfg<kWide>::NTHREADS, 1) gemm_pair_kernel(cons
     fence_barrier_init();
   }
   if (warp == WM) { tmem_alloc_pair(smem_u32(tmem_slot), TMEM_COLS); tmem_relinquish_pair(); }
-  if (warp == WP && lane == 0) { tma_prefetch_desc(&p.tm_a); tma_prefetch_desc(&p.tm_b); tma_prefetch_desc(&p.tm_c); }
+  if (warp == WP && lane == 0) {
+    tma_prefetch_desc(&p.tm_a); tma_prefetch_desc(&p.tm_b); tma_prefetch_desc(&p.tm_c);
+    if constexpr (EPI == EPI_SWIGLU) tma_prefetch_desc(&p.tm_c2);
+  }
   tc_fence_before();
   __syncthreads();
   cluster_sync();          // the leader's barriers exist before the peer's loads and arrivals reach them
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  const int ntiles = p.num_m * p.num_n;
+  // work item w: tile w / k_split, K slice w % k_split (k-blocks [slice kb_split, + kb_split) of nk)
+  const int ns = p.k_split;
+  const int nwork = p.num_m * p.num_n * ns;
   const int cid = (int)blockIdx.x >> 1, ncl = (int)gridDim.x >> 1;
   const int nk = (p.K + BK - 1) / BK;
+  auto kblocks = [&](int w, int& kb0) {
+    kb0 = (w % ns) * p.kb_split;
+    const int kb1 = kb0 + p.kb_split < nk ? kb0 + p.kb_split : nk;
+    return kb1 - kb0;
+  };
 
   if (warp == WP) {
     // ---------------------------------------------------------------- TMA producer (both CTAs)
@@ -301,12 +440,14 @@ __global__ void __launch_bounds__(Cfg<kWide>::NTHREADS, 1) gemm_pair_kernel(cons
       const uint32_t full_leader = map_rank(BAR(C::B_FULL), 0);
       int it = 0;
       bool ok = true;
-      for (int t = cid; ok && t < ntiles; t += ncl) {
-        int mb, nb;
-        tile_coords(p, t, mb, nb);
+      for (int w = cid; ok && w < nwork; w += ncl) {
+        int mb, nb, kb0;
+        tile_coords(p, w / ns, mb, nb);
+        const int nl = kblocks(w, kb0);
+        const int kb1 = kb0 + nl;
         // this CTA's rows: A rows m0 .. m0 + 127; B rows n0 + 256 h .. + 127 for each half h
         const int m0 = mb * 2 * BMC + (int)rank * BMC, n0 = nb * BN + (int)rank * 128;
-        for (int kb = 0; kb < nk; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % NST;
           if (it >= NST && !mbar_wait<true>(BAR(C::B_EMPTY + s), ((it / NST) - 1) & 1, p.status)) { ok = false; break; }
           if (leader) mbar_expect_tx(BAR(C::B_FULL + s), 2 * C::SZ_STAGE);
@@ -360,14 +501,16 @@ __global__ void __launch_bounds__(Cfg<kWide>::NTHREADS, 1) gemm_pair_kernel(cons
       };
       int it = 0, tl = 0;
       bool ok = true;
-      for (int t = cid; ok && t < ntiles; t += ncl, ++tl) {
+      for (int w = cid; ok && w < nwork; w += ncl, ++tl) {
         const int buf = tl % NBUF, round = tl / NBUF;
         const uint32_t acc = tbase + (uint32_t)(buf * NHALF * 256);
+        int kb0;
+        const int nloc = kblocks(w, kb0);
         int kb = 0;
         if constexpr (kWide) {
           // Half 0 runs ahead over the stages already loaded while the epilogue still drains half 1 of
           // the previous tile; the stages are released once half 1 has read them too.
-          const int S = nk < NST ? nk : NST;
+          const int S = nloc < NST ? nloc : NST;
           ok = wait_drained(0, round);
           for (int j = 0; ok && j < S; ++j) {
             if (!(ok = wait_full(it + j))) break;
@@ -383,7 +526,7 @@ __global__ void __launch_bounds__(Cfg<kWide>::NTHREADS, 1) gemm_pair_kernel(cons
         } else {
           ok = wait_drained(buf, round);
         }
-        for (; ok && kb < nk; ++kb, ++it) {
+        for (; ok && kb < nloc; ++kb, ++it) {
           if (!(ok = wait_full(it))) break;
 #pragma unroll
           for (int h = 0; h < NHALF; ++h) issue(acc + 256 * h, it % NST, h, kb == 0);
@@ -396,15 +539,18 @@ __global__ void __launch_bounds__(Cfg<kWide>::NTHREADS, 1) gemm_pair_kernel(cons
   } else {
     // ---------------------------------------------------------------- epilogue warps (both CTAs)
     constexpr int COLS = (EPI == EPI_STORE && OUT == GEMM_OUT_F32) ? 32 : 64;   // columns per 128-byte box row
-    static_assert(EPI == EPI_STORE || CW == 64, "the linear-CE epilogue takes one 64-column box per warp");
+    static_assert(EPI == EPI_STORE || CW == 64, "the linear-CE and SwiGLU epilogues take one 64-column box per warp");
     const int quarter = warp & 3, cgroup = warp >> 2;
     const uint32_t acce_leader = map_rank(BAR(C::B_ACCE), 0);
     const uint32_t boxes = sbase + C::OFF_EPI + (uint32_t)warp * NBOX * C::SZ_EPI;
     int tl = 0, nbox = 0;
-    for (int t = cid; t < ntiles; t += ncl, ++tl) {
+    for (int w = cid; w < nwork; w += ncl, ++tl) {
       int mb, nb;
+      const int t = w / ns, slice = w % ns;
+      (void)slice;
       tile_coords(p, t, mb, nb);
       const int buf = tl % NBUF;
+      const int wslot = (t * 2 + (int)rank) * NEPI + warp;      // this warp's rows and columns of tile t
       const int row0 = mb * 2 * BMC + (int)rank * BMC + quarter * 32;
       int64_t lab = -1;
       if constexpr (EPI == EPI_LCE) {
@@ -419,7 +565,12 @@ __global__ void __launch_bounds__(Cfg<kWide>::NTHREADS, 1) gemm_pair_kernel(cons
         // takes the CW columns from 256 h + CW cgroup
         const int cbase = nb * BN + 256 * h + CW * cgroup;
         const uint32_t tcol = (uint32_t)((buf * NHALF + h) * 256 + CW * cgroup);
-        if constexpr (EPI == EPI_LCE) {
+        if constexpr (EPI == EPI_SWIGLU) {
+          static_assert(CW == 64, "the SwiGLU epilogue takes one 64-column box per warp");
+          if (row0 < p.M && cbase < p.N)
+            epilogue_swiglu<kHalf, NBOX>(p, tlane + tcol, boxes, sbase + C::OFF_EPI2 + (uint32_t)warp * C::SZ_EPI2, lane,
+                                         cbase, row0, nbox);
+        } else if constexpr (EPI == EPI_LCE) {
           const int row = row0 + lane;
           float m = -INFINITY, sum = 0.f, tgt = 0.f;
           bool has_tgt = false;
@@ -430,10 +581,40 @@ __global__ void __launch_bounds__(Cfg<kWide>::NTHREADS, 1) gemm_pair_kernel(cons
             if (has_tgt) p.tgt[row] = tgt;
           }
         } else {
+          bool split_done = false;
+          if constexpr (OUT == GEMM_OUT_F32 && !kWide) {
+            if (ns > 1) {
+              // a K slice: partial to the workspace; the last slice to arrive sums them and stores C
+              float v[64];
+              tmem_ld32(tlane + tcol, v);
+              tmem_ld32(tlane + tcol + 32u, v + 32);
+              tmem_wait_ld();
+              float* slots = p.partials + (size_t)wslot * ns * 2048;
+              write_partial(slots + (size_t)slice * 2048, v, lane);
+              if (arrive_last(p.sema + wslot, ns, lane)) {
+#pragma unroll
+                for (int i = 0; i < 64; ++i) v[i] = 0.f;
+                for (int k = 0; k < ns; ++k) {
+                  const float* sl = slots + (size_t)k * 2048;
+#pragma unroll
+                  for (int i = 0; i < 64; ++i) v[i] += __ldcg(sl + i * 32 + lane);
+                }
+#pragma unroll
+                for (int c0 = 0; c0 < 64; c0 += 32)
+                  if (row0 < p.M && cbase + c0 < p.N)
+                    epilogue_store_values<NBOX>(p, v + c0, boxes, lane, cbase + c0, row0, nbox, p.accumulate != 0,
+                                                p.bias != nullptr);
+              }
+              split_done = true;
+            }
+          }
+          if (!split_done) {
 #pragma unroll 1
-          for (int c0 = 0; c0 < CW; c0 += COLS)
-            if (row0 < p.M && cbase + c0 < p.N)
-              epilogue_store<OUT, NBOX>(p, tlane + tcol + (uint32_t)c0, boxes, lane, cbase + c0, row0, nbox);
+            for (int c0 = 0; c0 < CW; c0 += COLS)
+              if (row0 < p.M && cbase + c0 < p.N)
+                epilogue_store<OUT, NBOX>(p, tlane + tcol + (uint32_t)c0, boxes, lane, cbase + c0, row0, nbox,
+                                          OUT == GEMM_OUT_F32 && p.accumulate, p.bias != nullptr);
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -454,38 +635,57 @@ __global__ void __launch_bounds__(Cfg<kWide>::NTHREADS, 1) gemm_pair_kernel(cons
 
 }  // namespace gemm
 
-// The grid is the number of CTA pairs that can be resident at once (not every GPC holds an even
-// number of SMs), capped by the number of tiles: the tile loop is persistent, so a pair that had to
-// wait for a free SM pair would add a whole tile's time at the end.
-template <int EPI, int OUT, bool H, bool W>
-static cudaError_t launch_majors(GemmParams p, int a_mn, int b_mn, int num_sms, cudaStream_t st) {
+// CTA pairs of the GEMM kernels that can be resident at once on the current device (one CTA per SM,
+// clusters of two; not every GPC holds an even number of SMs), asked once per device.
+static int resident_pairs(int num_sms) {
+  static int cache[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && cache[dev] > 0) return cache[dev];
   using namespace gemm;
-  p.num_n = (p.N + Cfg<W>::BN - 1) / Cfg<W>::BN;
-  auto run = [&](auto kernel) {
-    const uint32_t smem = Cfg<W>::SMEM_BYTES;
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
+  auto kernel = gemm_pair_kernel<EPI_STORE, GEMM_OUT_F32, false, false, false, false>;
+  int pairs = 0;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<false>::SMEM_BYTES) ==
+      cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
-    cfg.blockDim = dim3(Cfg<W>::NTHREADS);
+    cfg.blockDim = dim3(Cfg<false>::NTHREADS);
     cfg.gridDim = dim3(2 * (num_sms / 2));
+    cfg.dynamicSmemBytes = Cfg<false>::SMEM_BYTES;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&pairs, kernel, &cfg) != cudaSuccess) pairs = 0;
+  }
+  cudaGetLastError();
+  if (pairs < 1) pairs = num_sms / 2;
+  if (dev >= 0 && dev < 64) cache[dev] = pairs;
+  return pairs;
+}
+
+// One launch of a persistent grid: min(resident pairs, work items) clusters of two CTAs.
+template <int EPI, int OUT, bool H, bool W>
+static cudaError_t launch_majors(const GemmParams& p, int a_mn, int b_mn, int pairs, cudaStream_t st) {
+  using namespace gemm;
+  auto run = [&](auto kernel) {
+    const uint32_t smem = Cfg<W, EPI>::SMEM_BYTES;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    const int nwork = p.num_m * p.num_n * p.k_split;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(Cfg<W, EPI>::NTHREADS);
+    cfg.gridDim = dim3(2 * (pairs < nwork ? pairs : nwork));
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    int pairs = 0;
-    if (cudaOccupancyMaxActiveClusters(&pairs, kernel, &cfg) != cudaSuccess || pairs < 1) {
-      cudaGetLastError();
-      pairs = num_sms / 2;
-    }
-    const int ntiles = p.num_m * p.num_n;
-    if (pairs > ntiles) pairs = ntiles;
-    cfg.gridDim = dim3(2 * pairs);
     return cudaLaunchKernelEx(&cfg, kernel, p);
   };
-  if constexpr (EPI == EPI_LCE) {
+  if constexpr (EPI != EPI_STORE) {
     return run(gemm_pair_kernel<EPI, OUT, H, false, false, W>);     // X and W rows are K-major
   } else {
     if (a_mn && b_mn) return run(gemm_pair_kernel<EPI, OUT, H, true, true, W>);
@@ -495,26 +695,97 @@ static cudaError_t launch_majors(GemmParams p, int a_mn, int b_mn, int num_sms, 
   }
 }
 
+// Tile shape and K split from a cost model in units of one narrow tile's 64-wide K block (one round of
+// work items takes its longest item's K blocks plus ~3 of pipeline fill and epilogue; a wide tile's K
+// block costs 1.9 narrow ones). A split (narrow tiles, fp32 output, at most 4 rounds of work items) is
+// taken only where the tiles fill less than one wave of CTA pairs and it saves at least 10 %.
+static void choose_shape(int64_t M, int64_t N, int64_t K, int out, int pairs, int tile, bool can_split, int& wide,
+                         int& ns) {
+  const int nk = (int)((K + 63) / 64);
+  const int num_m = (int)((M + 255) / 256);
+  wide = tile > 0 ? 1 : 0;
+  ns = 1;
+  if (tile >= 0) return;
+  double best = 1e300;
+  for (int w = 0; w < 2; ++w) {
+    const int nt = num_m * (int)((N + (w ? 511 : 255)) / (w ? 512 : 256));
+    const double unit = w ? 1.9 : 1.0;
+    const double base = (double)((nt + pairs - 1) / pairs) * (nk + 3.0) * unit;
+    if (base < best) { best = base; wide = w; ns = 1; }
+    if (w || out != GEMM_OUT_F32 || !can_split || nt >= pairs) continue;
+    for (int k = 2; k <= 16 && nk / k >= 4 && nt * k <= 4 * pairs; ++k) {
+      const int kbs = (nk + k - 1) / k;
+      if ((nk + kbs - 1) / kbs != k) continue;           // the same split as a smaller k
+      const double cost = (double)((nt * k + pairs - 1) / pairs) * (kbs + 3.0) * unit;
+      if (cost < 0.9 * base && cost < best) { best = cost; wide = w; ns = k; }
+    }
+  }
+}
+
+// Workspace of a split: counters (one per epilogue warp of each CTA of each tile), then the slots.
+static int64_t split_bytes(int64_t M, int64_t N, int ns) {
+  const int64_t nt = ((M + 255) / 256) * ((N + 255) / 256);
+  const int64_t warps = nt * 2 * gemm::Cfg<false>::NEPI;
+  const int64_t head = ((warps * 4 + 255) / 256) * 256;
+  return ns > 1 ? head + warps * ns * 2048 * 4 : 0;
+}
+
+int64_t gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int out, int num_sms) {
+  int wide, ns;
+  choose_shape(M, N, K, out, resident_pairs(num_sms), -1, true, wide, ns);
+  return split_bytes(M, N, ns);
+}
+
 template <int OUT, bool H>
-static cudaError_t launch_shape(const GemmParams& p, int a_mn, int b_mn, int wide, int num_sms, cudaStream_t st) {
-  return wide ? launch_majors<EPI_STORE, OUT, H, true>(p, a_mn, b_mn, num_sms, st)
-              : launch_majors<EPI_STORE, OUT, H, false>(p, a_mn, b_mn, num_sms, st);
+static cudaError_t launch_shape(const GemmParams& p, int a_mn, int b_mn, int wide, int pairs, cudaStream_t st) {
+  return wide ? launch_majors<EPI_STORE, OUT, H, true>(p, a_mn, b_mn, pairs, st)
+              : launch_majors<EPI_STORE, OUT, H, false>(p, a_mn, b_mn, pairs, st);
 }
 
-cudaError_t launch_gemm(const GemmParams& p, int in_dtype, int a_mn, int b_mn, int out, int wide, int num_sms,
+cudaError_t launch_gemm(const GemmParams& p0, int in_dtype, int a_mn, int b_mn, int out, int tile, int num_sms,
                         cudaStream_t st) {
+  GemmParams p = p0;
+  const int pairs = resident_pairs(num_sms);
+  int wide, ns;
+  choose_shape(p.M, p.N, p.K, out, pairs, tile, true, wide, ns);
+  if (ns > 1 && (p.sema == nullptr || p.ws_bytes < split_bytes(p.M, p.N, ns))) ns = 1;
+  const int nk = (p.K + 63) / 64;
+  p.num_n = (p.N + (wide ? 511 : 255)) / (wide ? 512 : 256);
+  p.k_split = ns;
+  p.kb_split = (nk + ns - 1) / ns;
+  if (ns > 1) {
+    const int64_t warps = (int64_t)p.num_m * p.num_n * 2 * gemm::Cfg<false>::NEPI;
+    p.partials = reinterpret_cast<float*>(reinterpret_cast<char*>(p.sema) + ((warps * 4 + 255) / 256) * 256);
+    cudaError_t e = cudaMemsetAsync(p.sema, 0, (size_t)warps * 4, st);
+    if (e != cudaSuccess) return e;
+  }
   const bool h = in_dtype == 1;
-  if (out == GEMM_OUT_F32) return h ? launch_shape<GEMM_OUT_F32, true>(p, a_mn, b_mn, wide, num_sms, st)
-                                    : launch_shape<GEMM_OUT_F32, false>(p, a_mn, b_mn, wide, num_sms, st);
-  if (out == GEMM_OUT_BF16) return h ? launch_shape<GEMM_OUT_BF16, true>(p, a_mn, b_mn, wide, num_sms, st)
-                                     : launch_shape<GEMM_OUT_BF16, false>(p, a_mn, b_mn, wide, num_sms, st);
-  return h ? launch_shape<GEMM_OUT_F16, true>(p, a_mn, b_mn, wide, num_sms, st)
-           : launch_shape<GEMM_OUT_F16, false>(p, a_mn, b_mn, wide, num_sms, st);
+  if (out == GEMM_OUT_F32) return h ? launch_shape<GEMM_OUT_F32, true>(p, a_mn, b_mn, wide, pairs, st)
+                                    : launch_shape<GEMM_OUT_F32, false>(p, a_mn, b_mn, wide, pairs, st);
+  if (out == GEMM_OUT_BF16) return h ? launch_shape<GEMM_OUT_BF16, true>(p, a_mn, b_mn, wide, pairs, st)
+                                     : launch_shape<GEMM_OUT_BF16, false>(p, a_mn, b_mn, wide, pairs, st);
+  return h ? launch_shape<GEMM_OUT_F16, true>(p, a_mn, b_mn, wide, pairs, st)
+           : launch_shape<GEMM_OUT_F16, false>(p, a_mn, b_mn, wide, pairs, st);
 }
 
-cudaError_t launch_lce_logits_gemm(const GemmParams& p, int in_dtype, int num_sms, cudaStream_t st) {
-  return in_dtype == 1 ? launch_majors<EPI_LCE, GEMM_OUT_F16, true, false>(p, 0, 0, num_sms, st)
-                       : launch_majors<EPI_LCE, GEMM_OUT_BF16, false, false>(p, 0, 0, num_sms, st);
+cudaError_t launch_gemm_swiglu(const GemmParams& p0, int in_dtype, int num_sms, cudaStream_t st) {
+  GemmParams p = p0;
+  p.num_n = (p.N + 255) / 256;
+  p.k_split = 1;
+  p.kb_split = (p.K + 63) / 64;
+  const int pairs = resident_pairs(num_sms);
+  return in_dtype == 1 ? launch_majors<EPI_SWIGLU, GEMM_OUT_F16, true, false>(p, 0, 0, pairs, st)
+                       : launch_majors<EPI_SWIGLU, GEMM_OUT_BF16, false, false>(p, 0, 0, pairs, st);
+}
+
+cudaError_t launch_lce_logits_gemm(const GemmParams& p0, int in_dtype, int num_sms, cudaStream_t st) {
+  GemmParams p = p0;
+  p.num_n = (p.N + 255) / 256;
+  p.k_split = 1;
+  p.kb_split = (p.K + 63) / 64;
+  const int pairs = resident_pairs(num_sms);
+  return in_dtype == 1 ? launch_majors<EPI_LCE, GEMM_OUT_F16, true, false>(p, 0, 0, pairs, st)
+                       : launch_majors<EPI_LCE, GEMM_OUT_BF16, false, false>(p, 0, 0, pairs, st);
 }
 
 }  // namespace sisa

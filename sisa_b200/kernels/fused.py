@@ -9,6 +9,7 @@ from __future__ import annotations
 
 import torch
 
+from .gemm import matmul_t
 from .. import ops
 
 __all__ = ["sisa_fused", "fused_layout", "concat_fused_weights", "fused_projection", "prefill_layer"]
@@ -69,10 +70,10 @@ def _cached_wcat(owner, weights, dtype) -> torch.Tensor:
 class _FusedProjFn(torch.autograd.Function):
     """``proj = x W_cat^T + b_cat`` in the compute dtype from the seven projection weights, ``b_cat`` zero
     except the alpha columns: the call ``F.linear`` makes under autocast (inputs in the compute dtype, bias
-    added in the GEMM epilogue before the one rounding). ``W_cat`` comes from :func:`_cached_wcat` instead of
-    a differentiable ``torch.cat``; the backward runs autograd's two linear-backward GEMMs once for the
-    concatenation, hands each weight its rows of dW as a view, and reduces only the H alpha columns for
-    the bias gradient."""
+    added in the GEMM epilogue before the one rounding), here on the CTA-pair tcgen05 GEMM with its bias
+    epilogue. ``W_cat`` comes from :func:`_cached_wcat` instead of a differentiable ``torch.cat``; the
+    backward runs the two plain linear-backward GEMMs (cuBLAS) once for the concatenation, hands each
+    weight its rows of dW as a view, and reduces only the H alpha columns for the bias gradient."""
 
     @staticmethod
     def forward(ctx, x, b_alpha, owner, dtype, *weights):
@@ -82,8 +83,12 @@ class _FusedProjFn(torch.autograd.Function):
         wc = _cached_wcat(owner, weights, dtype)
         bias = torch.zeros((wc.shape[0],), dtype=dtype, device=x.device)
         bias[col_a:col_a + H] = b_alpha.to(dtype)
-        with torch.autocast(x.device.type, enabled=False):
-            out = torch.nn.functional.linear(xc, wc, bias)
+        d = xc.shape[-1]
+        x2 = xc.reshape(-1, d)
+        out = torch.empty((x2.shape[0], wc.shape[0]), dtype=dtype, device=x.device)
+        if x2.shape[0]:
+            matmul_t(x2 if x2.stride(-1) == 1 else x2.contiguous(), wc, out, bias=bias)
+        out = out.view(*xc.shape[:-1], wc.shape[0])
         ctx.save_for_backward(xc, wc)
         ctx.col_a, ctx.H = col_a, H
         ctx.rows = [w.shape[0] for w in weights]

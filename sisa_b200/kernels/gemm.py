@@ -14,6 +14,20 @@ from .. import _lib, backends
 __all__ = ["matmul_t"]
 
 _OUT_CODES = {torch.float32: 2, torch.bfloat16: 0, torch.float16: 1}
+_WS_BYTES: dict[tuple, int] = {}
+
+
+def _workspace(dev: torch.device, M: int, N: int, K: int, out_code: int) -> Tensor | None:
+    """Split-K workspace for this problem on ``dev`` (None when the kernel would not split it), taken
+    from the caching allocator on the current stream for the one launch."""
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    key = (idx, M, N, K, out_code)
+    nbytes = _WS_BYTES.get(key)
+    if nbytes is None:
+        with torch.cuda.device(idx):
+            nbytes = int(_lib.load().sisa_gemm_workspace(M, N, K, out_code))
+        _WS_BYTES[key] = nbytes
+    return torch.empty(nbytes, dtype=torch.uint8, device=dev) if nbytes > 0 else None
 
 
 def _operand(t: Tensor, name: str) -> tuple[int, int]:
@@ -35,10 +49,11 @@ def _operand(t: Tensor, name: str) -> tuple[int, int]:
 
 
 def matmul_t(a: Tensor, b: Tensor, out: Tensor | None = None, *, accumulate: bool = False,
-             out_dtype: torch.dtype = torch.float32) -> Tensor:
-    """``out (+)= a @ b.T`` for ``a`` (M, K) and ``b`` (N, K) CUDA tensors of one dtype (bf16 or fp16),
-    each with a unit stride along K or along its rows (so ``x.t()`` of a row-major tensor is taken as
-    it lies). ``out`` (M, N) with unit column stride; ``accumulate`` adds to it (fp32 only). Row strides
+             out_dtype: torch.dtype = torch.float32, bias: Tensor | None = None) -> Tensor:
+    """``out (+)= a @ b.T (+ bias)`` for ``a`` (M, K) and ``b`` (N, K) CUDA tensors of one dtype (bf16 or
+    fp16), each with a unit stride along K or along its rows (so ``x.t()`` of a row-major tensor is
+    taken as it lies). ``out`` (M, N) with unit column stride; ``accumulate`` adds to it (fp32 only);
+    ``bias`` (N,) contiguous bf16/fp16/fp32 is added in fp32 before the output's rounding. Row strides
     must be whole 16-byte units and pointers 16-byte aligned (errors come back from the C ABI)."""
     if a.dtype != b.dtype:
         raise TypeError(f"operands differ in dtype: {a.dtype} and {b.dtype}")
@@ -58,10 +73,15 @@ def matmul_t(a: Tensor, b: Tensor, out: Tensor | None = None, *, accumulate: boo
     a_mn, lda = _operand(a, "a")
     b_mn, ldb = _operand(b, "b")
     ldc = out.stride(0) if M > 1 else -(-N // 8) * 8
+    if bias is not None and (bias.shape != (N,) or not bias.is_contiguous() or bias.dtype not in _OUT_CODES):
+        raise ValueError(f"bias must be a contiguous ({N},) bf16/fp16/fp32 tensor, got {tuple(bias.shape)} {bias.dtype}")
     lib = _lib.load()
     dev = a.device
+    ws = _workspace(dev, M, N, K, _OUT_CODES[out.dtype])
     _lib.check(lib.sisa_gemm(a.data_ptr(), lda, a_mn, b.data_ptr(), ldb, b_mn, out.data_ptr(), ldc, M, N, K,
                              _lib.dtype_code(a.dtype), _OUT_CODES[out.dtype], int(accumulate),
+                             None if bias is None else bias.data_ptr(), 0 if bias is None else _OUT_CODES[bias.dtype],
+                             None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(),
                              backends.status_word(dev).data_ptr(), _lib.stream_ptr(dev)), "sisa_gemm")
     backends.after_call(dev)
     return out

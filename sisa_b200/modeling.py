@@ -71,6 +71,13 @@ class SwiGLU(nn.Module):
     def forward(self, x: Tensor) -> Tensor:
         return self.forward_split(x, x)
 
+    def forward_fused(self, h: Tensor, dtype: torch.dtype) -> Tensor:
+        """The forward with the gate and up projections and the activation in one tcgen05 GEMM
+        (kernels/ffn.py), then ``w_down`` under autocast."""
+        from .kernels.ffn import gate_up_swiglu
+
+        return self.w_down(gate_up_swiglu(h, self.w_gate.weight, self.w_up.weight, dtype, self))
+
     def forward_split(self, x_gate: Tensor, x_up: Tensor) -> Tensor:
         """The forward with the gate and up projections fed from separate copies of the input (the fused
         block path hands each its own copy, so that their gradients are summed in fp32)."""
@@ -448,7 +455,10 @@ class SISABlock(nn.Module):
         this block's first norm. Returns ``(x + m + attn, ffn)``: the caller (the next block, or the
         final norm) adds the second term. Each norm also writes its output in the dtype of the linears
         that read it, and the attention norm computes the fp32 forget projection, so neither the casts
-        nor the separate gradient sums of eager PyTorch run (kernels/norm.py ``block_norm``)."""
+        nor the separate gradient sums of eager PyTorch run (kernels/norm.py ``block_norm``). The MLP's
+        gate and up projections and its activation run as one GEMM (kernels/ffn.py) where the widths
+        allow, else as two linears and the activation kernel, each linear fed its own copy of the norm
+        output."""
         from .kernels.norm import block_norm
 
         cd = _compute_dtype(x)
@@ -460,6 +470,11 @@ class SISABlock(nn.Module):
         else:
             xs, h, z = block_norm(x, self.attn_norm.weight, self.attn_norm.eps, res=m, out_dtypes=(cd,), proj=fp)
         a = attn._forward_fused(h, z)
+        from .kernels.ffn import supports
+
+        if supports(x, self.ffn.w_gate.weight.shape[0], cd):
+            xs, f_in = block_norm(xs, self.ffn_norm.weight, self.ffn_norm.eps, res=a, out_dtypes=(cd,))
+            return xs, self.ffn.forward_fused(f_in, cd)
         xs, f_gate, f_up = block_norm(xs, self.ffn_norm.weight, self.ffn_norm.eps, res=a, out_dtypes=(cd, cd))
         return xs, self.ffn.forward_split(f_gate, f_up)
 

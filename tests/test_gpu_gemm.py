@@ -134,3 +134,46 @@ def test_gemm_argument_errors(cuda_dev):
     bb = torch.randn(64, 64, device=cuda_dev).to(torch.bfloat16)
     with pytest.raises(ValueError):
         matmul_t(bb, bb, out, accumulate=True)
+
+
+@pytest.mark.parametrize("M,N,K,a_mn,b_mn", [(1040, 768, 8192, 1, 1), (768, 768, 16384, 1, 1), (300, 200, 5000, 0, 0),
+                                             (520, 300, 3000, 1, 0)])
+def test_gemm_split_k_is_ordered_and_deterministic(cuda_dev, monkeypatch, M, N, K, a_mn, b_mn):
+    """Small fp32 problems with long K split K across CTA pairs; the slices add into C in a fixed order,
+    so repeated runs agree bit for bit, and the result matches fp64 within fp32 summation error."""
+    from sisa_b200.kernels.gemm import matmul_t
+
+    monkeypatch.delenv("SISA_GEMM_TILE", raising=False)
+    a, b, da, db = _operands(M, N, K, a_mn, b_mn, torch.bfloat16, cuda_dev, seed=M + K)
+    c1 = matmul_t(da, db)
+    c2 = matmul_t(da, db)
+    base = torch.randn(M, N, generator=torch.Generator().manual_seed(1)).to(cuda_dev)
+    c3 = base.clone()
+    matmul_t(da, db, c3, accumulate=True)
+    torch.cuda.synchronize()
+    assert torch.equal(c1, c2)
+    _check_f32(c1, a, b)
+    ref = base.double().cpu() + a.double() @ b.double().t()
+    bound = (a.double().abs() @ b.double().abs().t() + base.double().cpu().abs()) * 1e-5
+    assert bool(((c3.double().cpu() - ref).abs() <= bound).all())
+    monkeypatch.setenv("SISA_GEMM_TILE", "narrow")            # one slice: the same product, another order
+    c4 = matmul_t(da, db)
+    torch.cuda.synchronize()
+    _check_f32(c4, a, b)
+    from sisa_b200 import backends
+    assert int(backends.status_word(cuda_dev).item()) == 0
+
+
+@pytest.mark.parametrize("bias_dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("out_dtype", [torch.bfloat16, torch.float32])
+def test_gemm_bias_epilogue(cuda_dev, tile, bias_dtype, out_dtype):
+    from sisa_b200.kernels.gemm import matmul_t
+
+    M, N, K = 600, 3280, 768
+    a, b, da, db = _operands(M, N, K, 0, 0, torch.bfloat16, cuda_dev, seed=21)
+    bias = torch.randn(N, generator=torch.Generator().manual_seed(22)).to(bias_dtype)
+    c = matmul_t(da, db, out_dtype=out_dtype, bias=bias.to(cuda_dev))
+    c32 = matmul_t(da, db)
+    torch.cuda.synchronize()
+    want = c32.cpu() + bias.float()                          # the fp32 result plus the bias, rounded once
+    assert torch.equal(c.cpu(), want.to(out_dtype))
