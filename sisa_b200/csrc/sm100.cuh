@@ -124,7 +124,7 @@ __device__ __forceinline__ void tma_store_3d(const void* map, uint32_t src, int 
                ::"l"(map), "r"(src), "r"(c0), "r"(c1), "r"(c2) : "memory");
 }
 // Untiled bulk copy of `bytes` (a multiple of 16; both addresses 16-byte aligned) from global memory
-// into this CTA's shared memory, completing on an mbarrier. No multicast.
+// into this CTA's shared memory, completing on an mbarrier; this CTA alone receives the bytes.
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
                ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
