@@ -377,7 +377,7 @@ def run_train(args, rank, world, dev):
 
     cfg = sisa.SISAConfig.preset("sisa-152m", attn_impl="cuda")
     model = dp.build_model(cfg, dev, seed=0)
-    trainer = dp.Trainer(model, cuda_graph=True)
+    trainer = dp.Trainer(model, cuda_graph=not args.train_eager)
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     bt, tt = args.train_batch, 2048
     batches = [torch.randint(0, cfg.vocab_size, (bt, tt), device=dev, generator=g) for _ in range(4)]
@@ -409,7 +409,8 @@ def run_train(args, rank, world, dev):
             "mfu_vs_sustained": round(tok_s * TRAIN_FLOP_PER_TOKEN / (world * sustained * 1e12), 4),
             "parallelism": (f"dp{world} (whole step as one CUDA graph per rank: flat fp32 gradients in "
                             f"{len(trainer_buckets)} buckets, each allreduced by NCCL on a side stream as the "
-                            "backward finishes it)" if world > 1 else "dp1 (whole step as one CUDA graph)")}
+                            "backward finishes it)" if world > 1 else
+                            ("dp1 (eager steps)" if args.train_eager else "dp1 (whole step as one CUDA graph)"))}
 
 
 def run_e2e(step, dev, args, world):
@@ -757,6 +758,46 @@ def decode_leg(args, dev, steps=None):
             "config": {"batch": Bd, "prompt": P, "new_tokens": S, "model": "sisa-152m"}}
 
 
+def run_gemm(args):
+    """The CTA-pair tcgen05 GEMM (``sisa_gemm``) on C = A B^T, A and B (n x n) bf16 K-major, bf16 C,
+    in each tile shape and as the cost model chooses, next to cuBLAS (``torch.mm``) on the same
+    operands. TFLOP/s on 2 n^3."""
+    from sisa_b200.kernels.gemm import matmul_t
+
+    dev = torch.device("cuda", 0)
+    n = args.gemm_size
+    g = torch.Generator(device=dev).manual_seed(0)
+    a = torch.randn((n, n), generator=g, device=dev).to(torch.bfloat16)
+    b = torch.randn((n, n), generator=g, device=dev).to(torch.bfloat16)
+    c = torch.empty((n, n), device=dev, dtype=torch.bfloat16)
+    k = max(3, min(args.steps, 50))
+    out = {"metric": "GEMM TFLOP/s (C = A B^T, bf16)", "unit": "TFLOP/s", "config": {"n": n}, "steps": k}
+    with Clocks(0) as clk:
+        for name, tile in (("narrow", "narrow"), ("wide", "wide"), ("auto", None)):
+            if tile:
+                os.environ["SISA_GEMM_TILE"] = tile
+            else:
+                os.environ.pop("SISA_GEMM_TILE", None)
+            ms = _time_cuda(lambda: matmul_t(a, b, c), steps=k, warmup=max(args.warmup, 2))
+            out[name] = round(2 * n ** 3 / (ms * 1e9), 1)
+        os.environ.pop("SISA_GEMM_TILE", None)
+        ms = _time_cuda(lambda: torch.mm(a, b.t(), out=c), steps=k, warmup=max(args.warmup, 2))
+        out["cublas"] = round(2 * n ** 3 / (ms * 1e9), 1)
+    out["value"] = out["auto"]
+    out["clocks"] = clk.summary()
+    print(json.dumps(out))
+
+
+def run_train_only(args):
+    """Only the config 3 training leg (one GPU, the whole step as one CUDA graph)."""
+    dev = torch.device("cuda", 0)
+    with Clocks(0) as clk:
+        with clk.window("train"):
+            out = run_train(args, 0, 1, dev)
+    out["clocks"] = clk.summary("train")
+    print(json.dumps(out))
+
+
 def run_decode(args):
     dev = torch.device("cuda", 0)
     with Clocks(0) as clk:
@@ -804,9 +845,11 @@ def main(argv=None):
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the config 2 / config 4 legs and the reference Triton incumbent of the default run")
     ap.add_argument("--extra-decode-steps", type=int, default=48, help="decode steps of the default run's cfg4 leg")
-    ap.add_argument("--workload", choices=["attn", "lce", "decode", "norm"], default="attn",
+    ap.add_argument("--workload", choices=["attn", "lce", "decode", "norm", "gemm", "train"], default="attn",
                     help="attn (default: config 1 + the config 3 training leg), lce (config 2), decode (config 4), "
-                         "norm (the fused block-boundary norms of config 3)")
+                         "norm (the fused block-boundary norms of config 3), gemm (the CTA-pair GEMM against "
+                         "cuBLAS), train (the config 3 training leg alone)")
+    ap.add_argument("--gemm-size", type=int, default=8192)
     ap.add_argument("--norm-rows", type=int, default=16384)
     ap.add_argument("--lce-tokens", type=int, default=16384, help="hidden rows of the lce workload (cfg2: 16384)")
     ap.add_argument("--decode-batch", type=int, default=64)
@@ -814,6 +857,8 @@ def main(argv=None):
     ap.add_argument("--decode-steps", type=int, default=256)
     ap.add_argument("--train-steps", type=int, default=20)
     ap.add_argument("--train-batch", type=int, default=8)
+    ap.add_argument("--train-eager", action="store_true",
+                    help="train leg without the CUDA graph (for kernel launch lists: ncu cannot follow the capture)")
     ap.add_argument("--B", type=int, default=B, help="batch (default: config 1)")
     ap.add_argument("--T", type=int, default=T, help="sequence length (default: config 1)")
     ap.add_argument("--H", type=int, default=H, help="heads (default: config 1)")
@@ -826,6 +871,10 @@ def main(argv=None):
         run_decode(args)
     elif args.workload == "norm":
         run_norm(args)
+    elif args.workload == "gemm":
+        run_gemm(args)
+    elif args.workload == "train":
+        run_train_only(args)
     else:
         run_cuda(args)
 
