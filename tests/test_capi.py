@@ -115,3 +115,49 @@ def test_selftest_wait_rejects_bad_limits():
     assert lib.sisa_selftest_wait(0, 10, None, None, None) == _lib.ERR_VALUE
     assert "limit_ns" in _lib.last_error()
     assert lib.sisa_selftest_wait(0, 2_000_000_000, None, None, None) == _lib.ERR_VALUE
+
+
+def test_gemm_entry_points_reject_bad_arguments_before_any_cuda_call():
+    """sisa_gemm, sisa_gemm_swiglu and sisa_lce_seed_scale check pointers, layouts and dtypes on the host
+    (fake 16-byte-aligned addresses: no call here reaches the device)."""
+    lib = _lib.load()
+    A, B, C = 0x10000, 0x20000, 0x30000
+    ok = dict(a=A, lda=64, a_mn=0, b=B, ldb=64, b_mn=0, c=C, ldc=64, M=64, N=64, K=64, dtype=_lib.BF16,
+              out=_lib.F32, acc=0, bias=None, bias_dtype=0, ws=None, ws_bytes=0)
+
+    def gemm(**kw):
+        a = dict(ok, **kw)
+        return lib.sisa_gemm(a["a"], a["lda"], a["a_mn"], a["b"], a["ldb"], a["b_mn"], a["c"], a["ldc"], a["M"],
+                             a["N"], a["K"], a["dtype"], a["out"], a["acc"], a["bias"], a["bias_dtype"], a["ws"],
+                             a["ws_bytes"], None, None)
+
+    assert gemm(a=None) == _lib.ERR_VALUE and "null" in _lib.last_error()
+    assert gemm(a_mn=2) == _lib.ERR_VALUE
+    assert gemm(dtype=_lib.F32) == _lib.ERR_TYPE                  # operands are bf16 / fp16
+    assert gemm(out=7) == _lib.ERR_TYPE
+    assert gemm(out=_lib.BF16, acc=1) == _lib.ERR_VALUE and "accumulate" in _lib.last_error()
+    assert gemm(M=0) == _lib.ERR_VALUE
+    assert gemm(K=(1 << 30) + 1) == _lib.ERR_VALUE
+    assert gemm(lda=60) == _lib.ERR_ALIGN                         # not whole 16-byte units
+    assert gemm(lda=56) == _lib.ERR_ALIGN                         # K-major rows shorter than K
+    assert gemm(a=A + 8) == _lib.ERR_ALIGN
+    assert gemm(out=_lib.BF16, ldc=68) == _lib.ERR_ALIGN          # 136-byte rows
+    assert gemm(bias=A + 4, bias_dtype=_lib.F32) == _lib.ERR_VALUE
+    assert gemm(bias=A, bias_dtype=9) == _lib.ERR_VALUE
+    assert gemm(ws=A + 8, ws_bytes=4096) == _lib.ERR_VALUE
+
+    def swiglu(**kw):
+        a = dict(dict(x=A, xld=64, w=B, wld=64, gu=C, guld=80, a=C + 0x8000, ald=40, rows=64, dff=40, K=64,
+                      dtype=_lib.BF16), **kw)
+        return lib.sisa_gemm_swiglu(a["x"], a["xld"], a["w"], a["wld"], a["gu"], a["guld"], a["a"], a["ald"],
+                                    a["rows"], a["dff"], a["K"], a["dtype"], None, None)
+
+    assert swiglu(dff=36) == _lib.ERR_VALUE and "multiple of 8" in _lib.last_error()
+    assert swiglu(gu=None) == _lib.ERR_VALUE
+    assert swiglu(guld=72) == _lib.ERR_ALIGN                      # gu rows must hold 2 d_ff
+    assert swiglu(dtype=_lib.F32) == _lib.ERR_TYPE
+
+    assert lib.sisa_lce_seed_scale(None, 16, A, None, _lib.F32, None, None) == _lib.ERR_VALUE
+    assert lib.sisa_lce_seed_scale(A, 16, A, None, _lib.BF16, None, None) == _lib.ERR_VALUE   # in place is fp32
+    assert lib.sisa_lce_seed_scale(A, 16, A, B, 5, None, None) == _lib.ERR_TYPE
+    assert lib.sisa_lce_seed_scale(A + 4, 16, A, None, _lib.F32, None, None) == _lib.ERR_ALIGN
