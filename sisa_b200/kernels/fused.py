@@ -72,8 +72,9 @@ class _FusedProjFn(torch.autograd.Function):
     except the alpha columns: the call ``F.linear`` makes under autocast (inputs in the compute dtype, bias
     added in the GEMM epilogue before the one rounding), here on the CTA-pair tcgen05 GEMM with its bias
     epilogue. ``W_cat`` comes from :func:`_cached_wcat` instead of a differentiable ``torch.cat``; the
-    backward runs the two plain linear-backward GEMMs (cuBLAS) once for the concatenation, hands each
-    weight its rows of dW as a view, and reduces only the H alpha columns for the bias gradient."""
+    backward runs the two plain linear-backward GEMMs (cuBLAS) once for the concatenation, dW with an
+    fp32 output, hands each weight its rows of dW as a view, and reduces only the H alpha columns for
+    the bias gradient."""
 
     @staticmethod
     def forward(ctx, x, b_alpha, owner, dtype, *weights):
@@ -106,7 +107,8 @@ class _FusedProjFn(torch.autograd.Function):
             db = g2[:, ctx.col_a:ctx.col_a + ctx.H].sum(0).to(ctx.dtypes[1])
         dws = [None] * len(ctx.rows)
         if any(ctx.needs_input_grad[4:]):
-            dw = g2.t() @ xc.reshape(-1, xc.shape[-1])
+            # dW in fp32 straight from the GEMM: each fp32 weight takes its rows as a view, no casts
+            dw = torch.mm(g2.t(), xc.reshape(-1, xc.shape[-1]), out_dtype=torch.float32)
             row = 0
             for i, (n, dt) in enumerate(zip(ctx.rows, ctx.dtypes[2])):
                 if ctx.needs_input_grad[4 + i]:

@@ -75,8 +75,12 @@ class SwiGLU(nn.Module):
         """The forward with the gate and up projections and the activation in one tcgen05 GEMM
         (kernels/ffn.py), then ``w_down`` under autocast."""
         from .kernels.ffn import gate_up_swiglu
+        from .kernels.linear import linear_cast, supports
 
-        return self.w_down(gate_up_swiglu(h, self.w_gate.weight, self.w_up.weight, dtype, self))
+        a = gate_up_swiglu(h, self.w_gate.weight, self.w_up.weight, dtype, self)
+        if supports(a, self.w_down.weight, dtype):
+            return linear_cast(a, self.w_down.weight, dtype, self, "w_down")
+        return self.w_down(a)
 
     def forward_split(self, x_gate: Tensor, x_up: Tensor) -> Tensor:
         """The forward with the gate and up projections fed from separate copies of the input (the fused
@@ -279,6 +283,10 @@ class SISAAttention(nn.Module):
             weight, bias = self.fused_weights()
             proj = F.linear(x, weight, bias)
         y = sisa_fused(proj, self._forget_logits(x) if z is None else z, self.lam(), self.config.n_head)
+        from .kernels.linear import linear_cast, supports
+
+        if supports(y, self.W_O.weight, cd):
+            return linear_cast(y.reshape(bsz, seq_len, d), self.W_O.weight, cd, self, "W_O")
         return self.W_O(y.reshape(bsz, seq_len, d))
 
     def _fused_weights_static(self) -> tuple[Tensor, Tensor]:

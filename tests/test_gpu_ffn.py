@@ -114,3 +114,35 @@ def test_fused_block_uses_the_gate_up_kernel_and_matches_split_block(cuda_dev):
             ffn_mod.supports = orig
     for a, b in zip(outs[0], outs[1]):
         assert rel_err(a, b) <= 2e-2
+
+
+def test_linear_cast_matches_autocast_linear(cuda_dev):
+    """W_O / w_down: the output and dx equal autocast's F.linear bit for bit (the same bf16 GEMM); dW is
+    the same product accumulated to fp32 instead of rounded to bf16 first, and the weight copy is kept
+    while the weight is unchanged."""
+    from types import SimpleNamespace
+
+    from sisa_b200.kernels.linear import linear_cast
+
+    gen = torch.Generator().manual_seed(12)
+    x = torch.randn(4, 300, 768, generator=gen).to(torch.bfloat16).to(cuda_dev)
+    w = (torch.randn(768, 768, generator=gen) * 0.02).to(cuda_dev)
+    dy = torch.randn(4, 300, 768, generator=gen).to(torch.bfloat16).to(cuda_dev)
+    owner = SimpleNamespace()
+    X1, W1 = x.clone().requires_grad_(True), w.clone().requires_grad_(True)
+    y1 = linear_cast(X1, W1, torch.bfloat16, owner, "W")
+    y1.backward(dy)
+    X2, W2 = x.clone().requires_grad_(True), w.clone().requires_grad_(True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y2 = torch.nn.functional.linear(X2, W2)
+    y2.backward(dy)
+    assert y1.dtype == y2.dtype == torch.bfloat16
+    assert torch.equal(y1, y2)
+    assert torch.equal(X1.grad, X2.grad)
+    assert W1.grad.dtype == torch.float32
+    ref = (dy.double().reshape(-1, 768).t() @ x.double().reshape(-1, 768)).float()
+    assert rel_err(W1.grad, ref) <= 1e-5
+    assert rel_err(W2.grad, ref) <= 1e-2                       # autocast's bf16 dW, for scale
+    first = owner._lp_W[1]
+    linear_cast(x, W1, torch.bfloat16, owner, "W")
+    assert owner._lp_W[1] is first

@@ -116,8 +116,9 @@ def test_trainer_cuda_graph_matches_eager(cuda_dev):
 
 
 def test_fused_projection_matches_autocast_linear(cuda_dev):
-    """fused_projection = F.linear(x, W_cat, b_cat) under bf16 autocast: identical output and gradients
-    (the bias gradient from the alpha columns only)."""
+    """fused_projection = F.linear(x, W_cat, b_cat) under bf16 autocast: identical output and input
+    gradient; the weight gradients are the same product kept in fp32 (autocast rounds it to bf16
+    first); the bias gradient from the alpha columns only."""
     from sisa_b200.kernels.fused import concat_fused_weights, fused_projection, fused_layout
 
     H, d = 4, 256
@@ -139,8 +140,13 @@ def test_fused_projection_matches_autocast_linear(cuda_dev):
     yr.backward(go)
     yk.backward(go)
     assert torch.equal(xk.grad, xr.grad)
+    dw32 = torch.mm(go.reshape(-1, go.shape[-1]).t(), x.reshape(-1, d), out_dtype=torch.float32)
+    row = 0
     for a, r in zip(ker[:-1], ref[:-1]):
-        assert torch.equal(a.grad, r.grad)
+        n = a.shape[0]
+        assert a.grad.dtype == torch.float32 and torch.equal(a.grad, dw32[row:row + n])
+        assert torch.allclose(a.grad.to(torch.bfloat16).float(), r.grad, rtol=2 ** -7, atol=0)
+        row += n
     assert torch.allclose(ker[-1].grad, ref[-1].grad, rtol=1e-2, atol=1e-3)
     # the compute-dtype concatenation is kept while the weights are unchanged, rebuilt after an update
     cached = owner.__dict__["_wcat_train"][1]
