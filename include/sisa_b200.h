@@ -182,6 +182,23 @@ int sisa_gemm(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, 
 int sisa_gemm_swiglu(const void* x, int64_t x_ld, const void* w, int64_t w_ld, void* gu, int64_t gu_ld, void* a,
                      int64_t a_ld, int64_t rows, int64_t d_ff, int64_t K, int dtype, int32_t* status, void* stream);
 
+/* AdamW with global-norm gradient clipping over flat fp32 buffers: the training step's
+ * torch.nn.utils.clip_grad_norm_(params, max_norm) followed by torch.optim.AdamW (the reference's
+ * examples/train_minimal.py:253-301; decoupled weight decay, bias-corrected steps), for parameters laid
+ * out in one buffer. param, grad, m, v: n fp32 each (n a multiple of 4), 16-byte aligned. segs: nseg
+ * device records sorted by start, [start, end) multiples of 4, each with its group's lr and weight
+ * decay; elements outside every segment are left alone. step: device float, advanced by 1 (the
+ * bias corrections use the new value). partials: npart doubles of workspace (the norm's fixed-order
+ * partial sums: deterministic). max_norm <= 0 disables clipping. A non-finite norm sets
+ * SISA_ST_NONFINITE. */
+typedef struct sisa_adam_seg {
+  int64_t start, end;
+  float lr, weight_decay;
+} sisa_adam_seg;
+int sisa_adamw_flat(float* param, const float* grad, float* m, float* v, int64_t n, const sisa_adam_seg* segs,
+                    int nseg, float* step, double* partials, int npart, float beta1, float beta2, float eps,
+                    float max_norm, int32_t* status, void* stream);
+
 /* Fused RMSNorm and SwiGLU activation of the model's blocks (src/sisa/modeling.py:25-49). Element
  * types SISA_BF16, SISA_F16 or SISA_F32; row strides (x_ld ...) in elements, unit inner stride.
  * sisa_rmsnorm_fwd: rstd[r] = rsqrt(mean_c x[r,c]^2 + eps), y = (x * rstd) * w, fp32 arithmetic,

@@ -85,6 +85,8 @@ SIGNATURES = {
     "sisa_lce_logits": (_I, [_P, _I64, _I64, _I64, _P, _I64, _I64, _I64, _I, _P, _P, _I64, _P, _P, _P]),
     "sisa_lce_grad": (_I, [_P, _I64, _I64, _I64, _I64, _I, _P, _I64, _P, ctypes.c_float, _I, _P, _P, _P, _P]),
     "sisa_lce_seed_scale": (_I, [_P, _I64, _P, _P, _I, _P, _P]),
+    "sisa_adamw_flat": (_I, [_P, _P, _P, _P, _I64, _P, _I, _P, _P, _I, ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                             ctypes.c_float, _P, _P]),
     "sisa_gemm_swiglu": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _P, _P]),
     "sisa_gemm_workspace": (_I64, [_I64, _I64, _I64, _I]),
     "sisa_gemm": (_I, [_P, _I64, _I, _P, _I64, _I, _P, _I64, _I64, _I64, _I64, _I, _I, _I, _P, _I, _P, _I64, _P, _P]),

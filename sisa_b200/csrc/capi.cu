@@ -17,6 +17,7 @@
 #include "decode.h"
 #include "lce.h"
 #include "gemm.h"
+#include "optim.h"
 #include "norm.h"
 #include "capi_util.h"
 
@@ -652,6 +653,35 @@ int sisa_lce_seed_scale(float* x, int64_t n, const float* seed, void* out, int o
   const int code = out_dtype == SISA_F32 ? 2 : out_dtype == SISA_F16 ? 1 : 0;
   cudaError_t e = sisa::launch_seed_scale(x, n, seed, out, code, sms, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_lce_seed_scale launch");
+}
+
+// ------------------------------------------------------------------------------------ flat AdamW
+int sisa_adamw_flat(float* param, const float* grad, float* m, float* v, int64_t n, const sisa_adam_seg* segs,
+                    int nseg, float* step, double* partials, int npart, float beta1, float beta2, float eps,
+                    float max_norm, int32_t* status, void* stream) {
+  if (!param || !grad || !m || !v || !segs || !step || !partials)
+    return fail(SISA_ERR_VALUE, "sisa_adamw_flat: null pointer");
+  if (n < 0 || n % 4 || nseg < 1 || nseg > 8192 || npart < 1 || npart > 4096)
+    return fail(SISA_ERR_VALUE, "sisa_adamw_flat: need n a multiple of 4, 1 <= nseg <= 8192, 1 <= npart <= 4096 "
+                "(n=%lld nseg=%d npart=%d)", (long long)n, nseg, npart);
+  if (!aligned16(param) || !aligned16(grad) || !aligned16(m) || !aligned16(v) || !aligned16(segs) ||
+      !aligned16(partials))
+    return fail(SISA_ERR_ALIGN, "sisa_adamw_flat: buffers must be 16-byte aligned");
+  if (!(beta1 >= 0.f && beta1 < 1.f && beta2 >= 0.f && beta2 < 1.f && eps > 0.f))
+    return fail(SISA_ERR_VALUE, "sisa_adamw_flat: need 0 <= beta1, beta2 < 1 and eps > 0");
+  static_assert(sizeof(sisa_adam_seg) == sizeof(sisa::AdamSeg), "segment layout");
+  int rc;
+  sisa::DeviceScope scope;
+  if ((rc = scope.bind(param))) return rc;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, scope.device());
+  sisa::AdamParams p{};
+  p.param = param; p.grad = grad; p.m = m; p.v = v; p.n4 = n / 4;
+  p.segs = reinterpret_cast<const sisa::AdamSeg*>(segs); p.nseg = nseg;
+  p.step = step; p.partials = partials; p.npart = npart; p.nblocks = 8 * sms;
+  p.beta1 = beta1; p.beta2 = beta2; p.eps = eps; p.max_norm = max_norm; p.status = status;
+  cudaError_t e = sisa::launch_adamw(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_adamw_flat launch");
 }
 
 // ------------------------------------------------------------------------------------ SwiGLU gate/up GEMM

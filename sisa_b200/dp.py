@@ -81,29 +81,36 @@ class GradBuckets:
     backward in the same way.
     """
 
-    def __init__(self, params: list[torch.nn.Parameter], device: torch.device, cap_mb: float = 40.0):
+    def __init__(self, params: list[torch.nn.Parameter], device: torch.device, cap_mb: float = 40.0,
+                 reduce: bool = True):
         self.device = device
+        self.reduce = reduce
         order = list(reversed(params))
-        self.buffer = torch.zeros(sum(p.numel() for p in order), dtype=torch.float32, device=device)
+        self.order = order
+        # each parameter at an offset of whole 16-byte units (the flat optimizer's float4 chunks)
+        size = lambda p: -(-p.numel() // 4) * 4                       # noqa: E731
+        self.buffer = torch.zeros(sum(size(p) for p in order), dtype=torch.float32, device=device)
         cap = max(1, int(cap_mb * 2**20 / 4))
         self.bounds: list[tuple[int, int]] = []       # [start, end) of each bucket in the buffer
+        self.offset: dict[int, tuple[int, int]] = {}  # id(p) -> (offset, numel)
         self._bucket_of: dict[int, int] = {}
         off, start = 0, 0
         for p in order:
             p.grad = self.buffer[off:off + p.numel()].view_as(p)
-            if off > start and off + p.numel() - start > cap:
+            self.offset[id(p)] = (off, p.numel())
+            if off > start and off + size(p) - start > cap:
                 self.bounds.append((start, off))
                 start = off
             self._bucket_of[id(p)] = len(self.bounds)
-            off += p.numel()
+            off += size(p)
         self.bounds.append((start, off))
         self._size = [0] * len(self.bounds)
         for p in order:
             self._size[self._bucket_of[id(p)]] += 1
         self._left: list[int] = []
         self._next = 0
-        self.side = torch.cuda.Stream(device) if device.type == "cuda" else None
-        self._hooks = [p.register_post_accumulate_grad_hook(self._on_grad) for p in order]
+        self.side = torch.cuda.Stream(device) if (device.type == "cuda" and reduce) else None
+        self._hooks = [p.register_post_accumulate_grad_hook(self._on_grad) for p in order] if reduce else []
 
     def __len__(self) -> int:
         return len(self.bounds)
@@ -111,7 +118,7 @@ class GradBuckets:
     def start_step(self) -> None:
         """Zero the gradients and rearm the bucket counters (call before the backward)."""
         self.buffer.zero_()
-        self._left = list(self._size)
+        self._left = list(self._size) if self.reduce else []
         self._next = 0
 
     def _on_grad(self, p: torch.Tensor) -> None:
@@ -137,6 +144,8 @@ class GradBuckets:
 
     def finish(self) -> None:
         """Start the buckets still pending and order the caller's stream after every allreduce."""
+        if not self.reduce:
+            return
         while self._next < len(self.bounds):
             self._launch(self._next)
             self._next += 1
@@ -160,18 +169,30 @@ class Trainer:
     the launch gaps of its several hundred kernels and the host's dispatch work. The first call runs
     eagerly (it also creates the optimizer state, which a capture must not allocate); the second
     captures and replays; every call is exactly one optimizer step. A new input shape captures again.
+
+    ``flat_optimizer=True`` (CUDA, fp32 parameters, no optimizer given) runs clipping and AdamW as the
+    flat kernels of :class:`sisa_b200.optim.FlatAdamW` over the gradients' flat layout; by default the
+    step uses ``torch.optim.AdamW`` (fused) and ``clip_grad_norm_``.
     """
 
     def __init__(self, model: SISAForCausalLM, optimizer: torch.optim.Optimizer | None = None, *,
                  fused_ce: bool = True, clip: float = 1.0, bucket_cap_mb: float = 40.0, cuda_graph: bool = False,
-                 flat_grads: bool = False):
+                 flat_grads: bool = False, flat_optimizer: bool | None = None):
         self.module = model
         dev = next(model.parameters()).device
         self.device = dev
         self.distributed = dist.is_initialized() and dist.get_world_size() > 1
         self.world = dist.get_world_size() if self.distributed else 1
         self.cuda_graph = cuda_graph and dev.type == "cuda"
-        self.flat = self.distributed and (self.cuda_graph or flat_grads)
+        trainable = [p for p in model.parameters() if p.requires_grad]
+        flat_dp = self.distributed and (self.cuda_graph or flat_grads)
+        # The flat AdamW kernels (sisa_b200.optim) are opt-in: they need the gradients as views of one
+        # buffer, and on one GPU autograd then adds every gradient into its slot instead of handing over
+        # the fresh tensor, which costs about what the kernels save (measured: 29.1 vs 28.4-28.8 ms per
+        # cfg3 step); in the data-parallel flat form they measured no gain either (31.34 vs 31.37 ms).
+        self.flat_opt = bool(flat_optimizer) and optimizer is None and dev.type == "cuda" and \
+            all(p.dtype == torch.float32 for p in trainable)
+        self.flat = flat_dp or self.flat_opt
         self._buckets: GradBuckets | None = None
         if self.flat:
             self.model = model
@@ -182,7 +203,13 @@ class Trainer:
                 bucket_cap_mb=bucket_cap_mb, broadcast_buffers=False)
         else:
             self.model = model
-        self.opt = optimizer or make_optimizer(model, capturable=self.cuda_graph)
+        if self.flat_opt:
+            from .optim import FlatAdamW
+
+            self.opt = FlatAdamW(model.param_groups(6e-4, weight_decay=0.1), self._buckets, betas=(0.9, 0.95),
+                                 max_norm=clip)
+        else:
+            self.opt = optimizer or make_optimizer(model, capturable=self.cuda_graph)
         self.fused_ce = fused_ce and dev.type == "cuda"
         self.clip = clip
         self._graph = None
@@ -195,10 +222,11 @@ class Trainer:
         params = [p for p in self.module.parameters() if p.requires_grad]
         if any(p.dtype != torch.float32 for p in params):
             raise TypeError("flat gradients need fp32 parameters (the master weights)")
-        with torch.no_grad():
-            for p in params:
-                dist.broadcast(p.data, 0)
-        self._buckets = GradBuckets(params, self.device, cap_mb)
+        if self.distributed:
+            with torch.no_grad():
+                for p in params:
+                    dist.broadcast(p.data, 0)
+        self._buckets = GradBuckets(params, self.device, cap_mb, reduce=self.distributed)
 
     def close(self) -> None:
         """Release the captured step. A graph that holds NCCL work must be released before
@@ -256,7 +284,11 @@ class Trainer:
         self._graph = graph
 
     def _update(self) -> None:
-        """Clipping and the optimizer step (in the flat form the allreduces have run during the backward)."""
+        """Clipping and the optimizer step (in the flat form the allreduces have run during the backward;
+        the flat AdamW clips inside its kernels)."""
+        if self.flat_opt:
+            self.opt.step()
+            return
         if self.clip:
             torch.nn.utils.clip_grad_norm_(self.module.parameters(), self.clip)
         self.opt.step()
