@@ -244,3 +244,18 @@ def test_device_position_out_of_range_sets_status(cuda_dev):
         finally:
             st.pos_dev = None
             word.zero_()
+
+
+def test_lm_logits_padded_rows_equal_linear(cuda_dev):
+    """Inference logits through row-padded storage are F.linear's values (a view of padded rows)."""
+    from sisa_b200.modeling import _lm_logits
+
+    gen = torch.Generator().manual_seed(4)
+    h = torch.randn(3, 5, 768, generator=gen).to(torch.bfloat16).to(cuda_dev)
+    w = (torch.randn(50277, 768, generator=gen) * 0.02).to(torch.bfloat16).to(cuda_dev)
+    with torch.no_grad():
+        got = _lm_logits(h, w)
+        want = torch.nn.functional.linear(h, w)
+    assert got.shape == want.shape and got.stride(-2) == 50280
+    assert torch.allclose(got.float(), want.float(), rtol=1e-2, atol=1e-2)
+    assert torch.equal(got.argmax(-1), want.argmax(-1)) or (got.float() - want.float()).abs().max() < 1e-2
