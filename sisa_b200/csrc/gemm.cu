@@ -548,7 +548,6 @@ __global__ void __launch_bounds__(Cfg<kWide>::NTHREADS, 1) gemm_pair_kernel(cons
     for (int w = cid; w < nwork; w += ncl, ++tl) {
       int mb, nb;
       const int t = w / ns, slice = w % ns;
-      (void)slice;
       tile_coords(p, t, mb, nb);
       const int buf = tl % NBUF;
       const int wslot = (t * 2 + (int)rank) * NEPI + warp;      // this warp's rows and columns of tile t

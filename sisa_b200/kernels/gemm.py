@@ -26,6 +26,8 @@ def _workspace(dev: torch.device, M: int, N: int, K: int, out_code: int) -> Tens
     if nbytes is None:
         with torch.cuda.device(idx):
             nbytes = int(_lib.load().sisa_gemm_workspace(M, N, K, out_code))
+        if len(_WS_BYTES) >= 4096:          # shapes of a long-running process with varying sizes
+            _WS_BYTES.clear()
         _WS_BYTES[key] = nbytes
     return torch.empty(nbytes, dtype=torch.uint8, device=dev) if nbytes > 0 else None
 
