@@ -321,6 +321,8 @@ def run_cuda(args):
         torch.cuda.empty_cache()
         extra["decode"] = decode_leg(args, dev, steps=args.extra_decode_steps)
         torch.cuda.empty_cache()
+        extra["gemm"] = gemm_leg(args, dev, n=args.gemm_size, steps=10)
+        torch.cuda.empty_cache()
     else:
         del inputs
     with clk.window("train"):
@@ -758,21 +760,20 @@ def decode_leg(args, dev, steps=None):
             "config": {"batch": Bd, "prompt": P, "new_tokens": S, "model": "sisa-152m"}}
 
 
-def run_gemm(args):
+def gemm_leg(args, dev, n=8192, steps=None):
     """The CTA-pair tcgen05 GEMM (``sisa_gemm``) on C = A B^T, A and B (n x n) bf16 K-major, bf16 C,
     in each tile shape and as the cost model chooses, next to cuBLAS (``torch.mm``) on the same
-    operands. TFLOP/s on 2 n^3."""
+    operands (384 MB at n = 8192, more than L2). TFLOP/s on 2 n^3."""
     from sisa_b200.kernels.gemm import matmul_t
 
-    dev = torch.device("cuda", 0)
-    n = args.gemm_size
     g = torch.Generator(device=dev).manual_seed(0)
     a = torch.randn((n, n), generator=g, device=dev).to(torch.bfloat16)
     b = torch.randn((n, n), generator=g, device=dev).to(torch.bfloat16)
     c = torch.empty((n, n), device=dev, dtype=torch.bfloat16)
-    k = max(3, min(args.steps, 50))
+    k = steps or max(3, min(args.steps, 50))
     out = {"metric": "GEMM TFLOP/s (C = A B^T, bf16)", "unit": "TFLOP/s", "config": {"n": n}, "steps": k}
-    with Clocks(0) as clk:
+    prev = os.environ.get("SISA_GEMM_TILE")
+    try:
         for name, tile in (("narrow", "narrow"), ("wide", "wide"), ("auto", None)):
             if tile:
                 os.environ["SISA_GEMM_TILE"] = tile
@@ -780,10 +781,21 @@ def run_gemm(args):
                 os.environ.pop("SISA_GEMM_TILE", None)
             ms = _time_cuda(lambda: matmul_t(a, b, c), steps=k, warmup=max(args.warmup, 2))
             out[name] = round(2 * n ** 3 / (ms * 1e9), 1)
-        os.environ.pop("SISA_GEMM_TILE", None)
-        ms = _time_cuda(lambda: torch.mm(a, b.t(), out=c), steps=k, warmup=max(args.warmup, 2))
-        out["cublas"] = round(2 * n ** 3 / (ms * 1e9), 1)
+    finally:
+        if prev is None:
+            os.environ.pop("SISA_GEMM_TILE", None)
+        else:
+            os.environ["SISA_GEMM_TILE"] = prev
+    ms = _time_cuda(lambda: torch.mm(a, b.t(), out=c), steps=k, warmup=max(args.warmup, 2))
+    out["cublas"] = round(2 * n ** 3 / (ms * 1e9), 1)
     out["value"] = out["auto"]
+    return out
+
+
+def run_gemm(args):
+    dev = torch.device("cuda", 0)
+    with Clocks(0) as clk:
+        out = gemm_leg(args, dev, n=args.gemm_size)
     out["clocks"] = clk.summary()
     print(json.dumps(out))
 
