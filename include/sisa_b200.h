@@ -135,9 +135,9 @@ int sisa_prep_bwd(const void* proj, int64_t B, int64_t L, int64_t H, int64_t pro
 /* Chunked linear + cross-entropy over a tied LM head (src/sisa/kernels/linear_ce.py:60-196).
  * sisa_lce_logits: logits (R, Vp) = x (R, D) . w (Vp, D)^T on tcgen05 CTA pairs (the sisa_gemm kernel with
  *   a log-sum-exp epilogue), stored in `dtype` (rounded as under autocast) at logits (row stride
- *   logits_ld), plus per (row, 64-column segment) online max/sum-exp over the first V columns and the
+ *   logits_ld), plus per (row, 256-column tile) online max/sum-exp over the first V columns and the
  *   label's logit, kept in `workspace` (sisa_lce_workspace(R, Vp) bytes, 16-byte aligned). D a multiple
- *   of 64, Vp >= V a multiple of 256, w rows [V, Vp) zero.
+ *   of 64, Vp >= V a multiple of 128 (the reference's padding), w rows [V, Vp) zero.
  * sisa_lce_grad: per row lse, loss_rows[r] = lse - logit[label] (0 for ignore_index), and, when
  *   compute_grad, G = (softmax - onehot) * (*inv_n) * grad_scale written over the logits in place
  *   (padding columns 0). inv_n is a device scalar (1 / number of non-ignored rows).

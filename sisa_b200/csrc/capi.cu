@@ -576,7 +576,7 @@ static int map_output(CUtensorMap* m, void* ptr, int64_t ld, int64_t rows, int64
 }
 
 int64_t sisa_lce_workspace(int64_t R, int64_t Vp) {
-  const int64_t nseg = (Vp + 63) / 64;
+  const int64_t nseg = (Vp + 255) / 256;            // one (max, sum) record per row and 256-column tile
   return R * nseg * 8 + ((R * 4 + 255) / 256) * 256;
 }
 
@@ -586,8 +586,8 @@ int sisa_lce_logits(const void* x, int64_t R, int64_t D, int64_t x_ld, const voi
   int rc;
   if ((rc = check_dtype(dtype))) return rc;
   if (!x || !w || !labels || !logits || !workspace) return fail(SISA_ERR_VALUE, "sisa_lce_logits: null pointer");
-  if (R < 1 || D < 64 || D % 64 || V < 1 || Vp % 256 || Vp < V || R > ((int64_t)1 << 30) || Vp > ((int64_t)1 << 30))
-    return fail(SISA_ERR_VALUE, "sisa_lce_logits: need R >= 1, D a multiple of 64, Vp >= V a multiple of 256 "
+  if (R < 1 || D < 64 || D % 64 || V < 1 || Vp % 128 || Vp < V || R > ((int64_t)1 << 30) || Vp > ((int64_t)1 << 30))
+    return fail(SISA_ERR_VALUE, "sisa_lce_logits: need R >= 1, D a multiple of 64, Vp >= V a multiple of 128 "
                 "(R=%lld D=%lld V=%lld Vp=%lld)", (long long)R, (long long)D, (long long)V, (long long)Vp);
   if (!aligned16(x) || !aligned16(w) || !aligned16(logits) || !aligned16(workspace) || x_ld % 8 || w_ld % 8 ||
       logits_ld % 8 || x_ld < D || w_ld < D || logits_ld < Vp)
@@ -600,7 +600,7 @@ int sisa_lce_logits(const void* x, int64_t R, int64_t D, int64_t x_ld, const voi
   if ((rc = map_operand(&p.tm_a, x, x_ld, 0, R, D, dt, "x"))) return rc;
   if ((rc = map_operand(&p.tm_b, w, w_ld, 0, Vp, D, dt, "w"))) return rc;
   if ((rc = map_output(&p.tm_c, logits, logits_ld, R, Vp, dtype == SISA_F16 ? SISA_F16 : SISA_BF16))) return rc;
-  const int64_t nseg = Vp / 64;
+  const int64_t nseg = (Vp + 255) / 256;
   p.ldc = logits_ld;
   p.M = (int)R; p.N = (int)Vp; p.K = (int)D;
   p.num_m = (int)((R + 255) / 256);
@@ -621,9 +621,9 @@ int sisa_lce_grad(void* logits, int64_t logits_ld, int64_t R, int64_t V, int64_t
   int rc;
   if ((rc = check_dtype(dtype))) return rc;
   if (!logits || !labels || !inv_n || !workspace || !loss_rows) return fail(SISA_ERR_VALUE, "sisa_lce_grad: null pointer");
-  if (R < 1 || Vp % 256 || Vp < V || logits_ld < Vp || logits_ld % 8 || !aligned16(logits))
+  if (R < 1 || Vp % 128 || Vp < V || logits_ld < Vp || logits_ld % 8 || !aligned16(logits))
     return fail(SISA_ERR_VALUE, "sisa_lce_grad: bad shape or alignment");
-  const int64_t nseg = Vp / 64;
+  const int64_t nseg = (Vp + 255) / 256;
   sisa::LceGradParams p{};
   p.logits = static_cast<char*>(logits); p.ld = logits_ld;
   p.part = static_cast<const float2*>(workspace);

@@ -65,10 +65,12 @@ struct Cfg {
   static constexpr uint32_t OFF_BAR = OFF_EPI2 + NEPI * SZ_EPI2;
   static_assert(NTHREADS * (kWide ? 168 : 112) <= 65536, "register budget of one CTA per SM");
   static constexpr int B_FULL = 0, B_EMPTY = NST, B_ACCF = 2 * NST, B_ACCE = 2 * NST + 2;
+  // EPI_LCE: per row quarter and tile parity, "the other column groups' (max, sum) are in tensor memory"
+  static constexpr int B_REC = 2 * NST + 4;
   static constexpr uint32_t TMEM_SLOT = 192;               // byte offset of the TMEM address in the barrier area
   static constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
   static_assert(SMEM_BYTES <= 232448, "fits the 227 KB shared-memory limit");
-  static_assert((B_ACCE + 2) * 8 <= (int)TMEM_SLOT, "barriers end below the TMEM slot");
+  static_assert((B_REC + 8) * 8 <= (int)TMEM_SLOT, "barriers end below the TMEM slot");
   static_assert(NBUF * NHALF * 256 == (int)TMEM_COLS, "the accumulators fill the tensor memory");
 };
 
@@ -412,6 +414,8 @@ __global__ void __launch_bounds__(Cfg<kWide>::NTHREADS, 1) gemm_pair_kernel(cons
   if (tid == 0) {
     for (int s = 0; s < NST; ++s) { mbar_init(BAR(C::B_FULL + s), 1); mbar_init(BAR(C::B_EMPTY + s), 1); }
     for (int b = 0; b < 2; ++b) { mbar_init(BAR(C::B_ACCF + b), 1); mbar_init(BAR(C::B_ACCE + b), 2 * NEPI); }
+    if constexpr (EPI == EPI_LCE)
+      for (int b = 0; b < 8; ++b) mbar_init(BAR(C::B_REC + b), NEPI / 4 - 1);
     fence_barrier_init();
   }
   if (warp == WM) { tmem_alloc_pair(smem_u32(tmem_slot), TMEM_COLS); tmem_relinquish_pair(); }
@@ -573,14 +577,43 @@ __global__ void __launch_bounds__(Cfg<kWide>::NTHREADS, 1) gemm_pair_kernel(cons
             epilogue_swiglu<kHalf, NBOX>(p, tlane + tcol, boxes, sbase + C::OFF_EPI2 + (uint32_t)warp * C::SZ_EPI2, lane,
                                          cbase, row0, nbox);
         } else if constexpr (EPI == EPI_LCE) {
+          // One (max, sum) record per row and 256-column tile: the column groups 1..3 of a row quarter
+          // leave theirs in the first two of their own accumulator columns (read already, and not
+          // rewritten before this tile's accumulator-empty barrier, which the merging warp arrives on
+          // last), and column group 0 merges the four in column order.
+          static_assert(NHALF == 1 && CW == 64, "the linear-CE epilogue runs on the narrow tile");
           const int row = row0 + lane;
           float m = -INFINITY, sum = 0.f, tgt = 0.f;
           bool has_tgt = false;
           if (row0 < p.M && cbase < p.N)
             epilogue_lce<kHalf, NBOX>(p, tlane + tcol, boxes, lane, cbase, row0, nbox, lab, m, sum, tgt, has_tgt);
-          if (row < p.M && cbase < p.N) {
-            p.part[(int64_t)row * p.n_part + cbase / 64] = make_float2(m, sum);
-            if (has_tgt) p.tgt[row] = tgt;
+          if (has_tgt && row < p.M) p.tgt[row] = tgt;
+          const uint32_t rec = BAR(C::B_REC + 2 * quarter + (tl & 1));
+          if (cgroup > 0) {
+            tmem_st2(tlane + tcol, make_float2(m, sum));
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(rec);
+          } else {
+            // (a wait that runs out has set the status word's timeout bit; the record is then this
+            // group's alone and the call fails on the host)
+            const bool got = warp_wait(rec, (tl >> 1) & 1, p.status);
+            tc_fence_after();
+            float2 q[NEPI / 4 - 1];
+#pragma unroll
+            for (int c = 1; c < NEPI / 4; ++c) tmem_ld2(tlane + tcol + (uint32_t)(CW * c), q[c - 1]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 1; c < NEPI / 4; ++c) {
+              if (!got) break;
+              const float mc = q[c - 1].x, sc = q[c - 1].y;
+              const float mn = max_nan(m, mc);
+              if (mn != -INFINITY)
+                sum = (m == -INFINITY ? 0.f : sum * ex2_approx(m - mn)) + (mc == -INFINITY ? 0.f : sc * ex2_approx(mc - mn));
+              m = mn;
+            }
+            if (row < p.M) p.part[(int64_t)row * p.n_part + nb * (BN / 256)] = make_float2(m, sum);
           }
         } else {
           bool split_done = false;

@@ -26,8 +26,8 @@ struct GemmParams {
   uint32_t* sema;       // the workspace (counters, then partials); null: no split
   int64_t ws_bytes;
   float* partials;
-  // linear-CE logits epilogue only: per (row, 64-column segment) online {max, sum 2^(x log2 e - max)}
-  // over the columns below V (part[row * n_part + col / 64]), and the label's logit (tgt[row])
+  // linear-CE logits epilogue only: per (row, 256-column tile) online {max, sum 2^(x log2 e - max)}
+  // over the columns below V (part[row * n_part + col / 256]), and the label's logit (tgt[row])
   const int64_t* labels;
   float2* part;
   float* tgt;

@@ -3,7 +3,7 @@
 // Per chunk of R token rows:
 //  1. the logits: the CTA-pair tcgen05 GEMM of gemm.cu with its linear-CE epilogue, logits = X_c W_p^T
 //     rounded to the compute dtype (the autocast rounding point the reference's loss is defined on,
-//     linear_ce.py:26-28), stored as the chunk, with per (row, 64-column segment) the online maximum /
+//     linear_ce.py:26-28), stored as the chunk, with per (row, 256-column tile) the online maximum /
 //     sum of 2^(x log2e - m) over the real vocabulary columns plus the target logit - the first pass of
 //     the reference's row kernel (linear_ce.py:60-89) without re-reading the logits.
 //  2. lce_grad_kernel (here): per row, merge the segment partials into lse, write loss_row = lse - x_label

@@ -270,6 +270,17 @@ __device__ __forceinline__ void tmem_st1(uint32_t taddr, float v) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(__float_as_uint(v)) : "memory");
 }
 
+__device__ __forceinline__ void tmem_ld2(uint32_t taddr, float2& v) {
+  uint32_t a, b;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];" : "=r"(a), "=r"(b) : "r"(taddr));
+  v = make_float2(__uint_as_float(a), __uint_as_float(b));
+}
+
+__device__ __forceinline__ void tmem_st2(uint32_t taddr, float2 v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1,%2};"
+               ::"r"(taddr), "r"(__float_as_uint(v.x)), "r"(__float_as_uint(v.y)) : "memory");
+}
+
 // ------------------------------------------------------------------------------------ packed fp32
 // Two-lane fp32 arithmetic (FADD2 / FMUL2 / FFMA2 on sm_100): one issue slot for two values.
 __device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }

@@ -26,7 +26,7 @@ from .gemm import matmul_t
 
 __all__ = ["linear_cross_entropy", "reference_linear_cross_entropy", "chunk_rows"]
 
-VOCAB_ALIGN = 256          # vocabulary rows of the padded weight copy: the logits kernel's N tile
+VOCAB_ALIGN = 128          # vocabulary rows of the padded weight copy (the reference's padding)
 LOGITS_BUDGET = 1 << 30    # bytes one chunk of logits may take
 ROW_ALIGN = 128            # chunk rows are whole M tiles of the logits kernel
 
@@ -67,19 +67,29 @@ def _lce(x: Tensor, w_pad: Tensor, labels: Tensor, vocab: int, ignore_index: int
     inv_valid = valid.to(torch.float32).reciprocal().reshape(1)
     per_row = torch.empty(N, dtype=torch.float32, device=dev)
     chunk = torch.empty((rows, Vp), dtype=x.dtype, device=dev)
-    ws = torch.empty(lib.sisa_lce_workspace(rows, Vp), dtype=torch.uint8, device=dev)
     dx = torch.empty((N, D) if need_dx else (0,), dtype=torch.float32, device=dev)
     dw = torch.empty((Vp, D) if need_dw else (0,), dtype=torch.float32, device=dev)
+    ws = None
     for start in range(0, N, rows):
         stop = min(N, start + rows)
         g = chunk[:stop - start]
         xs, ls = x[start:stop], labels[start:stop]
+        # The chunk's per-row records (max / sum per 256 logit columns, the label's logit) live in the
+        # chunk's own rows of dX, which its dX GEMM overwrites only after the gradient pass has read them;
+        # when they do not fit there (or no dX is asked for), in a buffer of their own.
+        need = lib.sisa_lce_workspace(stop - start, Vp)
+        if need_dx and need <= (stop - start) * D * 4:
+            ws_ptr = dx[start:stop].data_ptr()
+        else:
+            if ws is None or ws.numel() < need:
+                ws = torch.empty(lib.sisa_lce_workspace(rows, Vp), dtype=torch.uint8, device=dev)
+            ws_ptr = ws.data_ptr()
         _lib.check(lib.sisa_lce_logits(xs.data_ptr(), stop - start, D, xs.stride(0), w_pad.data_ptr(), vocab, Vp,
-                                       w_pad.stride(0), code, ls.data_ptr(), g.data_ptr(), g.stride(0), ws.data_ptr(),
+                                       w_pad.stride(0), code, ls.data_ptr(), g.data_ptr(), g.stride(0), ws_ptr,
                                        st.data_ptr(), sp), "sisa_lce_logits")
         _lib.check(lib.sisa_lce_grad(g.data_ptr(), g.stride(0), stop - start, vocab, Vp, code, ls.data_ptr(),
                                      ignore_index, inv_valid.data_ptr(), grad_scale, int(need_dx or need_dw),
-                                     ws.data_ptr(), per_row[start:stop].data_ptr(), st.data_ptr(), sp),
+                                     ws_ptr, per_row[start:stop].data_ptr(), st.data_ptr(), sp),
                    "sisa_lce_grad")
         if need_dx:
             matmul_t(g, w_pad.t(), dx[start:stop])

@@ -115,3 +115,19 @@ def test_lce_backward_seed_and_dtypes(cuda_dev):
     assert rel_err(H.grad, grads[1.0][0].float() * 2.0) <= 1e-2
     with pytest.raises(RuntimeError, match="retain_graph"):
         loss.backward()
+
+
+@pytest.mark.parametrize("V", [50277, 3000])
+def test_lce_records_outside_dx(cuda_dev, V):
+    """Without a dX gradient the per-row records take a buffer of their own instead of the chunk's dX
+    rows: the loss and dW equal those of the call that also computes dX, bit for bit."""
+    from sisa_b200.kernels.linear_ce import linear_cross_entropy
+
+    h, w, labels = make_case(700, 256, V, seed=V)
+    l_both, _, dw_both = run(h, w, labels, cuda_dev, chunk_tokens=256)
+    W = w.to(cuda_dev).requires_grad_(True)
+    loss = linear_cross_entropy(h.to(cuda_dev), W, labels.to(cuda_dev), chunk_tokens=256)
+    loss.backward()
+    torch.cuda.synchronize()
+    assert torch.equal(loss.detach().cpu(), l_both)
+    assert torch.equal(W.grad.cpu(), dw_both)
