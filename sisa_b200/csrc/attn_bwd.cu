@@ -36,6 +36,7 @@
 // the stage.
 #include <cuda_runtime.h>
 #include <cooperative_groups.h>
+#include <type_traits>
 
 #include "attn_common.cuh"
 #include "attn.h"
@@ -804,33 +805,49 @@ __global__ void __launch_bounds__(NTHREADS, 1) attn_bwd_dkv_kernel(const __grid_
       } else {
         const float gs = qpos[0];                                  // query block start
         const float2 mid2 = bcast2(exp2f(fmin_nan((gs - ge) * kLOG2E, 0.f)));
-        const bool tail = (n0 + 64 * n + 64 > L);
+        // the last query tile of a sequence whose length is not a multiple of 64 masks its columns
+        // past L; every other tile takes the loop without the mask (a tile-uniform branch)
+        const uint32_t qa = sbase + OFF_ST + (uint32_t)s * SZ_STAGE + SZ_Q + SZ_DO + SZ_C + (uint32_t)wg * NCOL * 4;
+        auto ldf4 = [](uint32_t a) {                     // four columns of one plane in one 16-byte load
+          const uint4 v = ld_shared_v4(a);
+          return make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w));
+        };
+        auto offdiag = [&](auto masked) {
+          float4 r4, G4, D4, T4;
 #pragma unroll
-        for (int c = 0; c < NCOL; c += 2) {
-          const float4 r4 = qr4[c / 4], G4 = qG4[c / 4], D4 = qD4[c / 4], T4 = qT4[c / 4];
-          const bool hi = (c & 2) != 0;
-          const float2 rowf2 = hi ? make_float2(r4.z, r4.w) : make_float2(r4.x, r4.y);
-          const float2 G2 = hi ? make_float2(G4.z, G4.w) : make_float2(G4.x, G4.y);
-          const float2 nD2 = hi ? make_float2(D4.z, D4.w) : make_float2(D4.x, D4.y);
-          const float2 nT2 = hi ? make_float2(T4.z, T4.w) : make_float2(T4.x, T4.y);
-          const float2 rq = mul2(rowf2, mid2);                                      // rowf mid
-          const float2 uc = mul2(make_float2(uv[c], uv[c + 1]), rq);
-          const float2 y = fma2(uc, rk2v, add2(G2, nfjl2));                         // ... - lse_i
-          const float2 x = fma2(make_float2(sv[c], sv[c + 1]), c1v, y);
-          float2 pr = make_float2(ex2_approx(x.x), ex2_approx(x.y));
-          if (tail) {
-            if (i0 + c >= L) pr.x = 0.f;
-            if (i0 + c + 1 >= L) pr.y = 0.f;
+          for (int c = 0; c < NCOL; c += 2) {
+            if ((c & 2) == 0) {
+              r4 = ldf4(qa + 512 + c * 4);
+              G4 = ldf4(qa + SZ_POS + c * 4);
+              D4 = ldf4(qa + SZ_POS + 256 + c * 4);
+              T4 = ldf4(qa + SZ_POS + 512 + c * 4);
+            }
+            const bool hi = (c & 2) != 0;
+            const float2 rowf2 = hi ? make_float2(r4.z, r4.w) : make_float2(r4.x, r4.y);
+            const float2 G2 = hi ? make_float2(G4.z, G4.w) : make_float2(G4.x, G4.y);
+            const float2 nD2 = hi ? make_float2(D4.z, D4.w) : make_float2(D4.x, D4.y);
+            const float2 nT2 = hi ? make_float2(T4.z, T4.w) : make_float2(T4.x, T4.y);
+            const float2 rq = mul2(rowf2, mid2);                                      // rowf mid
+            const float2 uc = mul2(make_float2(uv[c], uv[c + 1]), rq);
+            const float2 y = fma2(uc, rk2v, add2(G2, nfjl2));                         // ... - lse_i
+            const float2 x = fma2(make_float2(sv[c], sv[c + 1]), c1v, y);
+            float2 pr = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+            if constexpr (decltype(masked)::value) {
+              if (i0 + c >= L) pr.x = 0.f;
+              if (i0 + c + 1 >= L) pr.y = 0.f;
+            }
+            const float2 dsh = mul2(pr, add2(make_float2(pv[c], pv[c + 1]), nD2));
+            const float2 dsx = fma2(pr, nT2, dsh);                                    // exact dS
+            dgo2 = fma2(dsx, uc, dgo2);
+            dfs2 = add2(dfs2, dsx);
+            const float2 dsb = mul2(dsh, rq);
+            wp[c / 2] = pack2<kHalf>(pr.x, pr.y);
+            wk[c / 2] = pack2<kHalf>(dsx.x, dsx.y);
+            wb[c / 2] = pack2<kHalf>(dsb.x, dsb.y);
           }
-          const float2 dsh = mul2(pr, add2(make_float2(pv[c], pv[c + 1]), nD2));
-          const float2 dsx = fma2(pr, nT2, dsh);                                    // exact dS
-          dgo2 = fma2(dsx, uc, dgo2);
-          dfs2 = add2(dfs2, dsx);
-          const float2 dsb = mul2(dsh, rq);
-          wp[c / 2] = pack2<kHalf>(pr.x, pr.y);
-          wk[c / 2] = pack2<kHalf>(dsx.x, dsx.y);
-          wb[c / 2] = pack2<kHalf>(dsb.x, dsb.y);
-        }
+        };
+        if (n0 + 64 * n + 64 > L) offdiag(std::true_type{});
+        else offdiag(std::false_type{});
       }
       // two operand buffers: the gradient UMMAs of tile n-2 must have read this one
       const int ob = n & 1;

@@ -70,4 +70,13 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, int32_t
   return __all_sync(0xffffffffu, ok);
 }
 
+// The same, testing the phase once without blocking before it waits: for warps whose phases have
+// usually completed by the time they ask, and which have few other warps to hide a wait's latency.
+template <bool kSleep = false>
+__device__ __forceinline__ bool warp_wait_tested(uint32_t bar, uint32_t parity, int32_t* status) {
+  bool ok = mbar_test(bar, parity);
+  if (!ok) ok = mbar_wait<kSleep>(bar, parity, status);
+  return __all_sync(0xffffffffu, ok);
+}
+
 }  // namespace sisa

@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     for (int n = 0; n < ntiles; ++n) {
       const int s = n % NSTAGE;
       const int j0 = key0(n);
-      if (!warp_wait<true>(BAR(B_SUF), n & 1, p.status)) { ok = false; break; }
+      if (!warp_wait_tested<true>(BAR(B_SUF), n & 1, p.status)) { ok = false; break; }
       tc_fence_after();
       // key position planes of this tile: [4][64] floats {g, F, rowf, colf}
       const float* kpos = reinterpret_cast<const float*>(gbase + OFF_ST + s * SZ_STAGE + OFFS_POS);
@@ -266,7 +266,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
       if (any_need && n > 0) {
         // lazy correction of O (including its DT(p) sum column): wait until the previous tile's UMMAs
         // have landed
-        if (!warp_wait<true>(BAR(B_PE), (n - 1) & 1, p.status)) { ok = false; break; }
+        if (!warp_wait_tested<true>(BAR(B_PE), (n - 1) & 1, p.status)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int q = 0; q < 5; ++q) {
@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
         w[c] = pack2<kHalf>(pe.x, pe.y);
       }
       // one P buffer: the previous tile's P V UMMAs must have read it
-      if (n >= 1 && !warp_wait<true>(BAR(B_PE), (n - 1) & 1, p.status)) { ok = false; break; }
+      if (n >= 1 && !warp_wait_tested<true>(BAR(B_PE), (n - 1) & 1, p.status)) { ok = false; break; }
       tmem_st32u(tmem_addr(tbase, warp, COL_P), w);
       tmem_wait_st();
       tc_fence_before();
@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(192, 2) attn_fwd_kernel(const __grid_constant_
     }
     const float2 lsum = add2(add2(lacc[0], lacc[1]), add2(lacc[2], lacc[3]));
     const float l = lsum.x + lsum.y;
-    if (ok && !warp_wait<true>(BAR(B_O), 0, p.status)) ok = false;
+    if (ok && !warp_wait_tested<true>(BAR(B_O), 0, p.status)) ok = false;
     if (ok) {
       tc_fence_after();
       float ov[64], lb;

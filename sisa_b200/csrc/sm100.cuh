@@ -88,6 +88,18 @@ __device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, int
   }
 }
 
+// One non-blocking test of a phase (mbarrier.test_wait returns at once; a try_wait costs a warp some
+// 150 cycles even when the phase has already completed).
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+
 // The library's wait: mbar_wait_for with the SISA_WAIT_NS limit.
 template <bool kSleep = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int32_t* status) {
