@@ -199,6 +199,25 @@ int sisa_adamw_flat(float* param, const float* grad, float* m, float* v, int64_t
                     int nseg, float* step, double* partials, int npart, float beta1, float beta2, float eps,
                     float max_norm, int32_t* status, void* stream);
 
+/* Compute-dtype copies of fp32 weights, many at once (the autocast casts of the weights that the
+ * reference's linears make on every forward, src/sisa/modeling.py:39-49,213-222): job j copies source
+ * rows r = 0 .. rows-1 (cols fp32 values each, row stride src_ld) to destination row
+ * (r / block_rows) * dst_block_stride + r % block_rows (row stride dst_ld) in `dtype`, rounding to
+ * nearest even; a job with src NULL zero-fills its destination rows. cols a multiple of 8, src and dst
+ * 16-byte aligned, src_ld a multiple of 4 and dst_ld of 8, both >= cols, block_rows >= 1.
+ * sisa_row_copy_check: checks one job on the host (no CUDA call).
+ * sisa_copy_rows: `jobs` holds njobs checked jobs in DEVICE memory (so a captured CUDA graph can replay
+ * the launch); max_vectors is the largest rows * cols / 8 among them. */
+typedef struct sisa_row_copy {
+  const float* src;
+  void* dst;
+  int64_t rows, cols, src_ld, dst_ld;
+  int64_t block_rows, dst_block_stride;
+} sisa_row_copy;
+int sisa_row_copy_check(const sisa_row_copy* job);
+int sisa_copy_rows(const sisa_row_copy* jobs, int njobs, int64_t max_vectors, int dtype, int32_t* status,
+                   void* stream);
+
 /* Fused RMSNorm and SwiGLU activation of the model's blocks (src/sisa/modeling.py:25-49). Element
  * types SISA_BF16, SISA_F16 or SISA_F32; row strides (x_ld ...) in elements, unit inner stride.
  * sisa_rmsnorm_fwd: rstd[r] = rsqrt(mean_c x[r,c]^2 + eps), y = (x * rstd) * w, fp32 arithmetic,

@@ -34,6 +34,13 @@ _I = ctypes.c_int
 _VP = ctypes.POINTER(View4)
 
 
+class RowCopy(ctypes.Structure):
+    """``sisa_row_copy``: one row-block copy of fp32 rows into compute-dtype rows (or a zero fill)."""
+
+    _fields_ = [("src", _P), ("dst", _P), ("rows", _I64), ("cols", _I64), ("src_ld", _I64), ("dst_ld", _I64),
+                ("block_rows", _I64), ("dst_block_stride", _I64)]
+
+
 class NormFwdArgs(ctypes.Structure):
     """``sisa_norm_fwd_args``: one RMSNorm at a block boundary (residual add, up to two output copies, an
     optional fp32 projection of the output)."""
@@ -87,6 +94,8 @@ SIGNATURES = {
     "sisa_lce_seed_scale": (_I, [_P, _I64, _P, _P, _I, _P, _P]),
     "sisa_adamw_flat": (_I, [_P, _P, _P, _P, _I64, _P, _I, _P, _P, _I, ctypes.c_float, ctypes.c_float, ctypes.c_float,
                              ctypes.c_float, _P, _P]),
+    "sisa_row_copy_check": (_I, [ctypes.POINTER(RowCopy)]),
+    "sisa_copy_rows": (_I, [_P, _I, _I64, _I, _P, _P]),
     "sisa_gemm_swiglu": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _P, _P]),
     "sisa_gemm_workspace": (_I64, [_I64, _I64, _I64, _I]),
     "sisa_gemm": (_I, [_P, _I64, _I, _P, _I64, _I, _P, _I64, _I64, _I64, _I64, _I, _I, _I, _P, _I, _P, _I64, _P, _P]),

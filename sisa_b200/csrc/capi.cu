@@ -18,6 +18,7 @@
 #include "lce.h"
 #include "gemm.h"
 #include "optim.h"
+#include "copy.h"
 #include "norm.h"
 #include "capi_util.h"
 
@@ -682,6 +683,38 @@ int sisa_adamw_flat(float* param, const float* grad, float* m, float* v, int64_t
   p.beta1 = beta1; p.beta2 = beta2; p.eps = eps; p.max_norm = max_norm; p.status = status;
   cudaError_t e = sisa::launch_adamw(p, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_adamw_flat launch");
+}
+
+// ------------------------------------------------------------------------------------ weight copies
+int sisa_row_copy_check(const sisa_row_copy* j) {
+  if (!j) return fail(SISA_ERR_VALUE, "sisa_row_copy_check: null job");
+  const int64_t lim = (int64_t)1 << 40;
+  if (!j->dst || j->rows < 0 || j->cols < 8 || j->cols % 8 || j->block_rows < 1 || j->dst_block_stride < 0 ||
+      j->rows > lim || j->cols > lim || j->dst_ld > lim || j->src_ld > lim)
+    return fail(SISA_ERR_VALUE, "sisa_row_copy: need dst, rows >= 0, cols a positive multiple of 8, block_rows >= 1 "
+                "(rows=%lld cols=%lld block_rows=%lld)", (long long)j->rows, (long long)j->cols,
+                (long long)j->block_rows);
+  if (!aligned16(j->dst) || j->dst_ld % 8 || j->dst_ld < j->cols ||
+      (j->src && (!aligned16(j->src) || j->src_ld % 4 || j->src_ld < j->cols)))
+    return fail(SISA_ERR_ALIGN, "sisa_row_copy: rows must be 16-byte aligned (dst_ld a multiple of 8, src_ld of 4, "
+                "both >= cols)");
+  return SISA_OK;
+}
+
+int sisa_copy_rows(const sisa_row_copy* jobs, int njobs, int64_t max_vectors, int dtype, int32_t* status,
+                   void* stream) {
+  (void)status;
+  int rc;
+  if ((rc = check_dtype(dtype))) return rc;
+  if (njobs < 0 || njobs > 65535 || max_vectors < 0) return fail(SISA_ERR_VALUE, "sisa_copy_rows: need 0 <= njobs <= 65535");
+  if (njobs == 0) return SISA_OK;
+  if (!jobs || !aligned16(jobs)) return fail(SISA_ERR_ALIGN, "sisa_copy_rows: jobs must be a 16-byte aligned device array");
+  static_assert(sizeof(sisa_row_copy) == sizeof(sisa::RowCopy), "job layout");
+  sisa::DeviceScope scope;
+  if ((rc = scope.bind(jobs))) return rc;
+  cudaError_t e = sisa::launch_copy_rows(reinterpret_cast<const sisa::RowCopy*>(jobs), njobs, max_vectors,
+                                         dtype == SISA_F16 ? 1 : 0, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_copy_rows launch");
 }
 
 // ------------------------------------------------------------------------------------ SwiGLU gate/up GEMM

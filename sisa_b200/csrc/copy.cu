@@ -1,0 +1,51 @@
+// copy.cu - many fp32 -> bf16/fp16 row-block copies in one launch: the compute-dtype copies of a model's
+// weights (the concatenated projection weight, the interleaved gate/up weight, the plain linears), which
+// change after every optimizer step and were otherwise refreshed by one small cast kernel per weight.
+//
+// Job j (one row of the grid's y dimension) copies source rows r = 0 .. rows-1 of `cols` fp32 values to
+// destination row (r / block_rows) * dst_block_stride + r % block_rows, rounding to nearest even; a job
+// without a source zero-fills its destination rows. Each thread moves 8 values at a time (two 16-byte
+// loads, one 16-byte store), grid-striding over its job.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "attn_common.cuh"
+#include "copy.h"
+
+namespace sisa {
+namespace copy {
+
+template <bool kHalf>
+__global__ void __launch_bounds__(256) copy_rows_kernel(const RowCopy* __restrict__ jobs) {
+  const RowCopy jb = jobs[blockIdx.y];
+  const int64_t vpr = jb.cols / 8;                         // 8-value vectors per row
+  const int64_t n = jb.rows * vpr;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const int64_t r = i / vpr, v = i - r * vpr;
+    const int64_t dr = (r / jb.block_rows) * jb.dst_block_stride + r % jb.block_rows;
+    uint4 o = make_uint4(0u, 0u, 0u, 0u);
+    if (jb.src) {
+      const float4* s = reinterpret_cast<const float4*>(jb.src + r * jb.src_ld + 8 * v);
+      const float4 a = s[0], b = s[1];
+      o = make_uint4(pack2<kHalf>(a.x, a.y), pack2<kHalf>(a.z, a.w), pack2<kHalf>(b.x, b.y), pack2<kHalf>(b.z, b.w));
+    }
+    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(jb.dst) + dr * jb.dst_ld + 8 * v) = o;
+  }
+}
+
+}  // namespace copy
+
+cudaError_t launch_copy_rows(const RowCopy* jobs, int njobs, int64_t max_vectors, int dtype, cudaStream_t st) {
+  if (njobs == 0) return cudaSuccess;
+  int64_t gx = (max_vectors + 2047) / 2048;                // about 8 vectors per thread for the largest job
+  if (gx < 1) gx = 1;
+  if (gx > 64) gx = 64;
+  const dim3 grid((unsigned)gx, (unsigned)njobs);
+  if (dtype == 1) copy::copy_rows_kernel<true><<<grid, 256, 0, st>>>(jobs);
+  else copy::copy_rows_kernel<false><<<grid, 256, 0, st>>>(jobs);
+  return cudaGetLastError();
+}
+
+}  // namespace sisa

@@ -1,0 +1,19 @@
+// Host-side launch parameters of the batched weight-copy kernel (copy.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace sisa {
+
+// One row-block copy; the same layout as sisa_row_copy.
+struct RowCopy {
+  const float* src;            // null: zero-fill the destination rows
+  void* dst;
+  int64_t rows, cols, src_ld, dst_ld;
+  int64_t block_rows, dst_block_stride;
+};
+
+// jobs: njobs entries in device memory; max_vectors: the largest rows * cols / 8 among them.
+cudaError_t launch_copy_rows(const RowCopy* jobs, int njobs, int64_t max_vectors, int dtype, cudaStream_t st);
+
+}  // namespace sisa

@@ -179,6 +179,7 @@ class Trainer:
                  fused_ce: bool = True, clip: float = 1.0, bucket_cap_mb: float = 40.0, cuda_graph: bool = False,
                  flat_grads: bool = False, flat_optimizer: bool | None = None):
         self.module = model
+        self._params = list(model.parameters())
         dev = next(model.parameters()).device
         self.device = dev
         self.distributed = dist.is_initialized() and dist.get_world_size() > 1
@@ -254,6 +255,7 @@ class Trainer:
                 return self._eager_step(ids)
         self._static_ids.copy_(ids, non_blocking=True)
         self._graph.replay()
+        self._mark_updated()
         return self._static_loss.clone()
 
     def _capture(self) -> None:
@@ -283,15 +285,22 @@ class Trainer:
                 return
         self._graph = graph
 
+    def _mark_updated(self) -> None:
+        """Advance the parameters' version counters after an update: the fused optimizers (and a graph
+        replay) change the weights in place without doing so, and the compute-dtype weight copies kept
+        for inference are keyed on them."""
+        torch.autograd.graph.increment_version(self._params)
+
     def _update(self) -> None:
         """Clipping and the optimizer step (in the flat form the allreduces have run during the backward;
         the flat AdamW clips inside its kernels)."""
         if self.flat_opt:
             self.opt.step()
-            return
-        if self.clip:
-            torch.nn.utils.clip_grad_norm_(self.module.parameters(), self.clip)
-        self.opt.step()
+        else:
+            if self.clip:
+                torch.nn.utils.clip_grad_norm_(self.module.parameters(), self.clip)
+            self.opt.step()
+        self._mark_updated()
 
     def _loss(self, ids: torch.Tensor) -> torch.Tensor:
         if self.device.type == "cuda":

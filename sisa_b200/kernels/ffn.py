@@ -36,25 +36,32 @@ def interleave_gate_up(w_gate: Tensor, w_up: Tensor, dtype: torch.dtype) -> Tens
     return w.view(2 * d_ff, d)
 
 
-def _cached(owner, w_gate: Tensor, w_up: Tensor, dtype: torch.dtype) -> Tensor:
-    """The interleaved copy, kept on ``owner`` while both weights keep their storage, version and dtype
-    (rebuilt once per optimizer step in training; outside the autograd graph)."""
-    key = (dtype,) + tuple((w.data_ptr(), w._version, w.dtype) for w in (w_gate, w_up))
-    hit = owner.__dict__.get("_gate_up_il")
-    if hit is None or hit[0] != key:
-        hit = (key, interleave_gate_up(w_gate, w_up, dtype))
-        owner.__dict__["_gate_up_il"] = hit
-    return hit[1]
+def gate_up_key(w_gate: Tensor, w_up: Tensor, dtype: torch.dtype) -> tuple:
+    """The key under which the interleaved compute-dtype copy is kept (``_gate_up_il``)."""
+    return (dtype,) + tuple((w.data_ptr(), w._version, w.dtype) for w in (w_gate, w_up))
+
+
+def _cached(owner, w_gate: Tensor, w_up: Tensor, dtype: torch.dtype, train: bool = False) -> Tensor:
+    """The interleaved copy kept on ``owner`` (outside the autograd graph), used as
+    ``kernels.fused.take_fresh`` allows and rebuilt otherwise."""
+    from .fused import take_fresh
+
+    key = gate_up_key(w_gate, w_up, dtype)
+    hit = take_fresh(owner, "_gate_up_il", key, train)
+    if hit is None:
+        hit = interleave_gate_up(w_gate, w_up, dtype)
+        owner.__dict__["_gate_up_il"] = (key, hit, False)
+    return hit
 
 
 class _GateUpFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, h, w_gate, w_up, owner, dtype):
+    def forward(ctx, h, w_gate, w_up, owner, dtype, train):
         d = h.shape[-1]
         d_ff = w_gate.shape[0]
         h2 = h.reshape(-1, d).to(dtype).contiguous()
         rows = h2.shape[0]
-        w_il = _cached(owner, w_gate, w_up, dtype)
+        w_il = _cached(owner, w_gate, w_up, dtype, train)
         gu = torch.empty((rows, 2 * d_ff), dtype=dtype, device=h.device)
         a = torch.empty((rows, d_ff), dtype=dtype, device=h.device)
         if rows:
@@ -96,7 +103,7 @@ class _GateUpFn(torch.autograd.Function):
                 dwg = dw[:, 0].reshape(d_ff, d).to(g_dtype)
             if ctx.needs_input_grad[2]:
                 dwu = dw[:, 1].reshape(d_ff, d).to(u_dtype)
-        return dh, dwg, dwu, None, None
+        return dh, dwg, dwu, None, None, None
 
 
 def gate_up_swiglu(h: Tensor, w_gate: Tensor, w_up: Tensor, dtype: torch.dtype, owner) -> Tensor:
@@ -106,4 +113,4 @@ def gate_up_swiglu(h: Tensor, w_gate: Tensor, w_up: Tensor, dtype: torch.dtype, 
         raise ValueError(f"gate_up_swiglu needs a CUDA input, a bf16/fp16 compute dtype and widths divisible by 8; "
                          f"got {h.device}, {dtype}, d_ff={w_gate.shape[0]}, d={h.shape[-1]}")
     with torch.autocast(h.device.type, enabled=False):
-        return _GateUpFn.apply(h, w_gate, w_up, owner, dtype)
+        return _GateUpFn.apply(h, w_gate, w_up, owner, dtype, torch.is_grad_enabled())

@@ -44,15 +44,35 @@ def concat_fused_weights(W_Q, W_K, W_V, W_B, W_C, W_theta, W_alpha, b_alpha):
     return W, torch.cat(bs, 0)
 
 
-def _cached_wcat(owner, weights, dtype) -> torch.Tensor:
-    """The concatenation of ``weights`` (plus zero padding rows to NPAD) in ``dtype``, kept on ``owner``
-    while every weight keeps its storage, version and dtype. Under training each optimizer step changes the
-    weights, so it is rebuilt once per step and reused by every micro-batch of that step; it never enters
-    the autograd graph."""
-    key = (dtype,) + tuple((w.data_ptr(), w._version, w.dtype) for w in weights)
-    hit = owner.__dict__.get("_wcat_train")
-    if hit is not None and hit[0] == key:
+def take_fresh(owner, slot: str, key: tuple, train: bool):
+    """The compute-dtype weight copy kept on ``owner`` under ``slot`` if it may be used now, else None.
+    Entries are ``(key, tensor, fresh)``. Outside training the key decides. In a training forward
+    (``train``: gradients enabled where the linear was called) the copy must also be fresh, i.e. written
+    by the model's refresh for this forward; the mark is taken with the use."""
+    hit = owner.__dict__.get(slot)
+    if hit is None or hit[0] != key:
+        return None
+    if hit[2]:
+        owner.__dict__[slot] = (hit[0], hit[1], False)
         return hit[1]
+    return None if train else hit[1]
+
+
+def wcat_key(weights, dtype) -> tuple:
+    """The key under which the compute-dtype concatenation of ``weights`` is kept (``_wcat_train``)."""
+    return (dtype,) + tuple((w.data_ptr(), w._version, w.dtype) for w in weights)
+
+
+def _cached_wcat(owner, weights, dtype, train: bool = False) -> torch.Tensor:
+    """The concatenation of ``weights`` (plus zero padding rows to NPAD) in ``dtype``, kept on ``owner``;
+    it never enters the autograd graph. Outside training it is reused while every weight keeps its
+    storage, version and dtype. In a training forward only a copy that the model's one-launch refresh
+    has just written is used (kernels/weights.py), else it is rebuilt: fused optimizers update the
+    weights without advancing their versions."""
+    key = wcat_key(weights, dtype)
+    hit = take_fresh(owner, "_wcat_train", key, train)
+    if hit is not None:
+        return hit
     H = weights[-1].shape[0]
     off = fused_layout(H)
     d = weights[0].shape[1]
@@ -63,7 +83,7 @@ def _cached_wcat(owner, weights, dtype) -> torch.Tensor:
             wc[row:row + w.shape[0]].copy_(w)
             row += w.shape[0]
         wc[row:].zero_()
-    owner.__dict__["_wcat_train"] = (key, wc)
+    owner.__dict__["_wcat_train"] = (key, wc, False)
     return wc
 
 
@@ -77,11 +97,11 @@ class _FusedProjFn(torch.autograd.Function):
     the bias gradient."""
 
     @staticmethod
-    def forward(ctx, x, b_alpha, owner, dtype, *weights):
+    def forward(ctx, x, b_alpha, owner, dtype, train, *weights):
         H = b_alpha.shape[0]
         col_a = fused_layout(H)["A"]
         xc = x.to(dtype)
-        wc = _cached_wcat(owner, weights, dtype)
+        wc = _cached_wcat(owner, weights, dtype, train)
         bias = torch.zeros((wc.shape[0],), dtype=dtype, device=x.device)
         bias[col_a:col_a + H] = b_alpha.to(dtype)
         d = xc.shape[-1]
@@ -106,22 +126,22 @@ class _FusedProjFn(torch.autograd.Function):
         if ctx.needs_input_grad[1]:
             db = g2[:, ctx.col_a:ctx.col_a + ctx.H].sum(0).to(ctx.dtypes[1])
         dws = [None] * len(ctx.rows)
-        if any(ctx.needs_input_grad[4:]):
+        if any(ctx.needs_input_grad[5:]):
             # dW in fp32 straight from the GEMM: each fp32 weight takes its rows as a view, no casts
             dw = torch.mm(g2.t(), xc.reshape(-1, xc.shape[-1]), out_dtype=torch.float32)
             row = 0
             for i, (n, dt) in enumerate(zip(ctx.rows, ctx.dtypes[2])):
-                if ctx.needs_input_grad[4 + i]:
+                if ctx.needs_input_grad[5 + i]:
                     dws[i] = dw[row:row + n].to(dt)
                 row += n
-        return (dx, db, None, None, *dws)
+        return (dx, db, None, None, None, *dws)
 
 
 def fused_projection(x: torch.Tensor, weights, b_alpha: torch.Tensor, dtype: torch.dtype, owner) -> torch.Tensor:
     """``F.linear(x, W_cat, b_cat)`` under autocast to ``dtype`` (fused_prep.py:99-122) from the projection
     weights ``[W_Q, W_K, W_V, W_B, W_C, W_theta, W_alpha]`` and the alpha bias. The compute-dtype
-    concatenation is cached on ``owner`` while the weights are unchanged."""
-    return _FusedProjFn.apply(x, b_alpha, owner, dtype, *weights)
+    concatenation is kept on ``owner`` (see :func:`_cached_wcat`)."""
+    return _FusedProjFn.apply(x, b_alpha, owner, dtype, torch.is_grad_enabled(), *weights)
 
 
 def prep_forward(proj: torch.Tensor, z: torch.Tensor | None, H: int):

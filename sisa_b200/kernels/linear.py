@@ -1,7 +1,8 @@
 """``F.linear(x, W)`` under autocast for the model's plain linears (W_O, w_down): the same bf16/fp16
-product, with the weight's compute-dtype copy kept while the weight is unchanged (instead of a cast on
-every forward) and the weight gradient computed in fp32 by the GEMM (instead of a low-precision
-gradient cast to the fp32 parameter's dtype afterwards). The GEMMs are plain library GEMMs (cuBLAS
+product, with the weight's compute-dtype copy written by the model's one-launch refresh of all its
+weight copies (kernels/weights.py) or kept between inference calls while the weight is unchanged, and
+the weight gradient computed in fp32 by the GEMM (instead of a low-precision gradient cast to the fp32
+parameter's dtype afterwards). The GEMMs are plain library GEMMs (cuBLAS
 through ``torch.mm``); nothing is fused into them.
 """
 from __future__ import annotations
@@ -17,21 +18,30 @@ def supports(x: Tensor, weight: Tensor, dtype: torch.dtype) -> bool:
     return x.is_cuda and dtype in (torch.bfloat16, torch.float16) and weight.dtype != dtype
 
 
-def _cached(owner, name: str, weight: Tensor, dtype: torch.dtype) -> Tensor:
-    key = (dtype, weight.data_ptr(), weight._version, weight.dtype)
+def weight_key(weight: Tensor, dtype: torch.dtype) -> tuple:
+    """The key under which the compute-dtype copy of ``weight`` is kept (``_lp_<name>``)."""
+    return (dtype, weight.data_ptr(), weight._version, weight.dtype)
+
+
+def _cached(owner, name: str, weight: Tensor, dtype: torch.dtype, train: bool = False) -> Tensor:
+    """The compute-dtype copy kept on ``owner`` under ``_lp_<name>``, used as ``kernels.fused.take_fresh``
+    allows and rebuilt otherwise."""
+    from .fused import take_fresh
+
+    key = weight_key(weight, dtype)
     slot = "_lp_" + name
-    hit = owner.__dict__.get(slot)
-    if hit is None or hit[0] != key:
+    hit = take_fresh(owner, slot, key, train)
+    if hit is None:
         with torch.no_grad():
-            hit = (key, weight.to(dtype).contiguous())
-        owner.__dict__[slot] = hit
-    return hit[1]
+            hit = weight.to(dtype).contiguous()
+        owner.__dict__[slot] = (key, hit, False)
+    return hit
 
 
 class _LinearFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, weight, owner, name, dtype):
-        w = _cached(owner, name, weight, dtype)
+    def forward(ctx, x, weight, owner, name, dtype, train):
+        w = _cached(owner, name, weight, dtype, train)
         x2 = x.reshape(-1, x.shape[-1]).to(dtype)
         y = torch.mm(x2, w.t())
         ctx.save_for_backward(x2, w)
@@ -49,10 +59,10 @@ class _LinearFn(torch.autograd.Function):
             dx = torch.mm(dy2, w).view(x_shape).to(x_dtype)
         if ctx.needs_input_grad[1]:
             dw = torch.mm(dy2.t(), x2, out_dtype=torch.float32).to(w_dtype)
-        return dx, dw, None, None, None
+        return dx, dw, None, None, None, None
 
 
 def linear_cast(x: Tensor, weight: Tensor, dtype: torch.dtype, owner, name: str) -> Tensor:
     """``x W^T`` in ``dtype`` (no bias), the weight's ``dtype`` copy kept on ``owner`` under ``name``."""
     with torch.autocast(x.device.type, enabled=False):
-        return _LinearFn.apply(x, weight, owner, name, dtype)
+        return _LinearFn.apply(x, weight, owner, name, dtype, torch.is_grad_enabled())

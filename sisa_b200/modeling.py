@@ -540,6 +540,9 @@ class SISAModel(nn.Module):
         x = self.embed(input_ids)
         use_ckpt = self.config.gradient_checkpointing and self.training and cache is None and torch.is_grad_enabled()
         if cache is None and len(self.layers) and self.layers[0].fused_path(x):
+            from .kernels.weights import refresh
+
+            refresh(self, _compute_dtype(x))        # every stale compute-dtype weight copy, one launch
             m = None
             for layer in self.layers:
                 x, m = (checkpoint(layer.forward_pair, x, m, use_reentrant=False) if use_ckpt

@@ -161,3 +161,33 @@ def test_gemm_entry_points_reject_bad_arguments_before_any_cuda_call():
     assert lib.sisa_lce_seed_scale(A, 16, A, None, _lib.BF16, None, None) == _lib.ERR_VALUE   # in place is fp32
     assert lib.sisa_lce_seed_scale(A, 16, A, B, 5, None, None) == _lib.ERR_TYPE
     assert lib.sisa_lce_seed_scale(A + 4, 16, A, None, _lib.F32, None, None) == _lib.ERR_ALIGN
+
+
+def test_row_copy_jobs_are_checked_on_the_host():
+    """sisa_row_copy_check accepts well-formed jobs and names what is wrong with the others;
+    sisa_copy_rows rejects a bad table pointer or dtype before any CUDA call (fake addresses)."""
+    import ctypes
+
+    lib = _lib.load()
+    ok = dict(src=0x10000, dst=0x20000, rows=64, cols=256, src_ld=256, dst_ld=256, block_rows=64,
+              dst_block_stride=0)
+
+    def check(**kw):
+        job = _lib.RowCopy(**dict(ok, **kw))
+        return lib.sisa_row_copy_check(ctypes.byref(job))
+
+    assert check() == _lib.OK
+    assert check(src=None) == _lib.OK                           # zero fill
+    assert check(block_rows=8, dst_block_stride=16) == _lib.OK  # interleave
+    assert check(dst=None) == _lib.ERR_VALUE
+    assert check(cols=252) == _lib.ERR_VALUE and "multiple of 8" in _lib.last_error()
+    assert check(rows=-1) == _lib.ERR_VALUE
+    assert check(block_rows=0) == _lib.ERR_VALUE
+    assert check(dst=0x20008) == _lib.ERR_ALIGN
+    assert check(src=0x10004) == _lib.ERR_ALIGN
+    assert check(dst_ld=260) == _lib.ERR_ALIGN
+    assert check(src_ld=130) == _lib.ERR_ALIGN                  # shorter than a row
+    assert lib.sisa_copy_rows(0x30008, 4, 100, _lib.BF16, None, None) == _lib.ERR_ALIGN
+    assert lib.sisa_copy_rows(0x30000, 4, 100, 7, None, None) == _lib.ERR_TYPE
+    assert lib.sisa_copy_rows(0x30000, -1, 100, _lib.BF16, None, None) == _lib.ERR_VALUE
+    assert lib.sisa_copy_rows(None, 0, 0, _lib.BF16, None, None) == _lib.OK

@@ -76,14 +76,23 @@ def test_gate_up_weight_cache_follows_the_weights(cuda_dev):
 
     h, wg, wu = _case(256, 128, 64, 7, cuda_dev)
     owner = SimpleNamespace()
-    a1 = gate_up_swiglu(h, wg, wu, torch.bfloat16, owner)
-    first = owner._gate_up_il[1]
-    a2 = gate_up_swiglu(h, wg, wu, torch.bfloat16, owner)
-    assert owner._gate_up_il[1] is first and torch.equal(a1, a2)
-    with torch.no_grad():
+    with torch.no_grad():                                       # inference: the versions decide
+        a1 = gate_up_swiglu(h, wg, wu, torch.bfloat16, owner)
+        first = owner._gate_up_il[1]
+        a2 = gate_up_swiglu(h, wg, wu, torch.bfloat16, owner)
+        assert owner._gate_up_il[1] is first and torch.equal(a1, a2)
         wg.mul_(2.0)                                            # an in-place update bumps the version
-    a3 = gate_up_swiglu(h, wg, wu, torch.bfloat16, owner)
-    assert owner._gate_up_il[1] is not first and not torch.equal(a1, a3)
+        a3 = gate_up_swiglu(h, wg, wu, torch.bfloat16, owner)
+        assert owner._gate_up_il[1] is not first and not torch.equal(a1, a3)
+    # with gradients the copy is rebuilt on every call: an update that leaves the version alone (a fused
+    # optimizer's) is seen too
+    WU = wu.clone().requires_grad_(True)
+    a4 = gate_up_swiglu(h, wg, WU, torch.bfloat16, owner)
+    WU.data.mul_(0.5)
+    a5 = gate_up_swiglu(h, wg, WU, torch.bfloat16, owner)
+    with torch.no_grad():
+        a6 = gate_up_swiglu(h, wg, wu * 0.5, torch.bfloat16, SimpleNamespace())
+    assert torch.equal(a4.detach(), a3) and torch.equal(a5.detach(), a6)
 
 
 def test_fused_block_uses_the_gate_up_kernel_and_matches_split_block(cuda_dev):
@@ -143,6 +152,8 @@ def test_linear_cast_matches_autocast_linear(cuda_dev):
     ref = (dy.double().reshape(-1, 768).t() @ x.double().reshape(-1, 768)).float()
     assert rel_err(W1.grad, ref) <= 1e-5
     assert rel_err(W2.grad, ref) <= 1e-2                       # autocast's bf16 dW, for scale
-    first = owner._lp_W[1]
-    linear_cast(x, W1, torch.bfloat16, owner, "W")
+    with torch.no_grad():                                       # inference: kept while W is unchanged
+        linear_cast(x, W1, torch.bfloat16, owner, "W")
+        first = owner._lp_W[1]
+        linear_cast(x, W1, torch.bfloat16, owner, "W")
     assert owner._lp_W[1] is first

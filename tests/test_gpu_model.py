@@ -148,16 +148,25 @@ def test_fused_projection_matches_autocast_linear(cuda_dev):
         assert torch.allclose(a.grad.to(torch.bfloat16).float(), r.grad, rtol=2 ** -7, atol=0)
         row += n
     assert torch.allclose(ker[-1].grad, ref[-1].grad, rtol=1e-2, atol=1e-3)
-    # the compute-dtype concatenation is kept while the weights are unchanged, rebuilt after an update
+    # without gradients the compute-dtype concatenation is kept while the weights are unchanged and
+    # rebuilt after an update
     cached = owner.__dict__["_wcat_train"][1]
-    with torch.autocast("cuda", dtype=torch.bfloat16):
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
         fused_projection(xk, ker[:-1], ker[-1], torch.bfloat16, owner)
     assert owner.__dict__["_wcat_train"][1] is cached
     with torch.no_grad():
         ker[0].add_(1.0)
-    with torch.autocast("cuda", dtype=torch.bfloat16):
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
         y2 = fused_projection(xk, ker[:-1], ker[-1], torch.bfloat16, owner)
         W2, b2 = concat_fused_weights(*[t.detach() for t in ker])
         y2r = torch.nn.functional.linear(xk.detach(), W2, b2)
     assert owner.__dict__["_wcat_train"][1] is not cached
-    assert torch.equal(y2.detach(), y2r)
+    assert torch.equal(y2, y2r)
+    # with gradients it is rebuilt on every call, so an update that leaves the versions alone (a fused
+    # optimizer's) is seen as well
+    ker[1].data.add_(1.0)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        y3 = fused_projection(xk, ker[:-1], ker[-1], torch.bfloat16, owner)
+        W3, b3 = concat_fused_weights(*[t.detach() for t in ker])
+        y3r = torch.nn.functional.linear(xk.detach(), W3, b3)
+    assert torch.equal(y3.detach(), y3r)
