@@ -105,7 +105,9 @@ def _static(owner: nn.Module, name: str, make, *tensors: Tensor):
     """``make(*tensors)``, kept on ``owner`` under ``name`` while none of ``tensors`` changed (same storage,
     version and dtype). For the decode step, which runs without autograd and would otherwise recompute
     these weight-only values (fp32 copies, concatenations) every token; a captured decode graph reads
-    the kept tensors, which stay valid while the weights are unchanged."""
+    the kept tensors, which stay valid while the weights are unchanged. A fused optimizer changes the
+    weights without advancing their versions: after its steps (our Trainer does this itself) call
+    ``torch.autograd.graph.increment_version`` on the parameters before decoding."""
     key = tuple((t.data_ptr(), t._version, t.dtype) for t in tensors)
     hit = owner.__dict__.get(name)
     if hit is None or hit[0] != key:
