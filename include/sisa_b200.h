@@ -199,6 +199,23 @@ int sisa_adamw_flat(float* param, const float* grad, float* m, float* v, int64_t
                     int nseg, float* step, double* partials, int npart, float beta1, float beta2, float eps,
                     float max_norm, int32_t* status, void* stream);
 
+/* The same AdamW with clipping over separate parameter tensors (the training step's own tensors,
+ * gradients as autograd hands them over): tensors[k] = {param, grad, offset, n, lr, weight_decay}, param
+ * and grad n fp32 values each, 16-byte aligned; offset (a multiple of 4, increasing with k) is the
+ * tensor's first element in the moment buffers m and v (n_state fp32 each, zero-initialised by the
+ * caller). tensors is a HOST array of at most 384 entries: it is passed to the kernels by value, so a
+ * captured CUDA graph replays it. The norm covers the listed gradients; tensors left out (no gradient)
+ * are not updated. Other arguments as for sisa_adamw_flat. */
+typedef struct sisa_adam_tensor {
+  float* param;
+  const float* grad;
+  int64_t offset, n;
+  float lr, weight_decay;
+} sisa_adam_tensor;
+int sisa_adamw_tensors(const sisa_adam_tensor* tensors, int ntensors, float* m, float* v, int64_t n_state,
+                       float* step, double* partials, int npart, float beta1, float beta2, float eps,
+                       float max_norm, int32_t* status, void* stream);
+
 /* Compute-dtype copies of fp32 weights, many at once (the autocast casts of the weights that the
  * reference's linears make on every forward, src/sisa/modeling.py:39-49,213-222): job j copies source
  * rows r = 0 .. rows-1 (cols fp32 values each, row stride src_ld) to destination row

@@ -34,6 +34,13 @@ _I = ctypes.c_int
 _VP = ctypes.POINTER(View4)
 
 
+class AdamTensor(ctypes.Structure):
+    """``sisa_adam_tensor``: one parameter tensor of the tensor-list AdamW."""
+
+    _fields_ = [("param", _P), ("grad", _P), ("offset", _I64), ("n", _I64), ("lr", ctypes.c_float),
+                ("weight_decay", ctypes.c_float)]
+
+
 class RowCopy(ctypes.Structure):
     """``sisa_row_copy``: one row-block copy of fp32 rows into compute-dtype rows (or a zero fill)."""
 
@@ -94,6 +101,8 @@ SIGNATURES = {
     "sisa_lce_seed_scale": (_I, [_P, _I64, _P, _P, _I, _P, _P]),
     "sisa_adamw_flat": (_I, [_P, _P, _P, _P, _I64, _P, _I, _P, _P, _I, ctypes.c_float, ctypes.c_float, ctypes.c_float,
                              ctypes.c_float, _P, _P]),
+    "sisa_adamw_tensors": (_I, [ctypes.POINTER(AdamTensor), _I, _P, _P, _I64, _P, _P, _I, ctypes.c_float,
+                                ctypes.c_float, ctypes.c_float, ctypes.c_float, _P, _P]),
     "sisa_row_copy_check": (_I, [ctypes.POINTER(RowCopy)]),
     "sisa_copy_rows": (_I, [_P, _I, _I64, _I, _P, _P]),
     "sisa_gemm_swiglu": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _P, _P]),

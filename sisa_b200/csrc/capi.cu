@@ -685,6 +685,48 @@ int sisa_adamw_flat(float* param, const float* grad, float* m, float* v, int64_t
   return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_adamw_flat launch");
 }
 
+int sisa_adamw_tensors(const sisa_adam_tensor* tensors, int ntensors, float* m, float* v, int64_t n_state,
+                       float* step, double* partials, int npart, float beta1, float beta2, float eps,
+                       float max_norm, int32_t* status, void* stream) {
+  if (!tensors || !m || !v || !step || !partials) return fail(SISA_ERR_VALUE, "sisa_adamw_tensors: null pointer");
+  if (ntensors < 0 || ntensors > sisa::kMaxAdamTensors || npart < 1 || npart > 4096 || n_state < 0 || n_state % 4)
+    return fail(SISA_ERR_VALUE, "sisa_adamw_tensors: need 0 <= ntensors <= %d, 1 <= npart <= 4096, n_state a "
+                "multiple of 4 (ntensors=%d npart=%d n_state=%lld)", sisa::kMaxAdamTensors, ntensors, npart,
+                (long long)n_state);
+  if (!aligned16(m) || !aligned16(v) || !aligned16(partials))
+    return fail(SISA_ERR_ALIGN, "sisa_adamw_tensors: m, v and partials must be 16-byte aligned");
+  if (!(beta1 >= 0.f && beta1 < 1.f && beta2 >= 0.f && beta2 < 1.f && eps > 0.f))
+    return fail(SISA_ERR_VALUE, "sisa_adamw_tensors: need 0 <= beta1, beta2 < 1 and eps > 0");
+  static_assert(sizeof(sisa_adam_tensor) == sizeof(sisa::AdamTensor), "tensor entry layout");
+  int64_t end = 0;
+  for (int k = 0; k < ntensors; ++k) {
+    const sisa_adam_tensor& t = tensors[k];
+    if (!t.param || !t.grad || t.n < 1 || t.offset % 4 || t.offset < end || t.offset + t.n > n_state)
+      return fail(SISA_ERR_VALUE, "sisa_adamw_tensors: tensor %d: need param, grad, n >= 1 and an offset that is "
+                  "a multiple of 4, past the previous tensor, with offset + n <= n_state", k);
+    if (!aligned16(t.param) || !aligned16(t.grad))
+      return fail(SISA_ERR_ALIGN, "sisa_adamw_tensors: tensor %d: param and grad must be 16-byte aligned", k);
+    end = t.offset + t.n;
+  }
+  if (ntensors == 0) return SISA_OK;
+  int rc;
+  sisa::DeviceScope scope;
+  if ((rc = scope.bind(m))) return rc;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, scope.device());
+  static sisa::AdamListParams p;          // 15 KB: kept off the stack; filled and launched under the lock
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  memset(&p, 0, sizeof(p));
+  memcpy(p.t, tensors, sizeof(sisa::AdamTensor) * (size_t)ntensors);
+  p.nt = ntensors;
+  p.m = m; p.v = v; p.n4 = (end + 3) / 4;
+  p.step = step; p.partials = partials; p.npart = npart; p.nblocks = 8 * sms;
+  p.beta1 = beta1; p.beta2 = beta2; p.eps = eps; p.max_norm = max_norm; p.status = status;
+  cudaError_t e = sisa::launch_adamw_list(p, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_adamw_tensors launch");
+}
+
 // ------------------------------------------------------------------------------------ weight copies
 int sisa_row_copy_check(const sisa_row_copy* j) {
   if (!j) return fail(SISA_ERR_VALUE, "sisa_row_copy_check: null job");

@@ -7,7 +7,8 @@
 // sums the pass-1 partials in the same order, forms the clip factor min(1, max_norm / (norm + 1e-6)),
 // and updates its float4 chunks: decoupled weight decay p *= 1 - lr wd, then m, v and the bias-corrected
 // step, with (lr, wd) of the parameter group the chunk belongs to (segments, binary search in shared
-// memory; every segment is a multiple of 4 elements, so a float4 never straddles two).
+// memory; every segment is a multiple of 4 elements, so a float4 never straddles two). The tensor-list
+// form below runs the same passes over separate parameter tensors.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -103,7 +104,138 @@ __global__ void __launch_bounds__(256) adamw_update_kernel(AdamParams p) {
   }
 }
 
+// ----------------------------------------------------------------------------- tensor-list form
+// The same two passes over parameters that stay separate tensors (gradients as autograd hands them
+// over). The m / v index space is split into 4-element chunks; tensor k owns the chunks from off_k / 4
+// on, and chunks past its n elements (its padding, or a tensor without a gradient left out of the
+// table) belong to no one. A thread walks its grid-stride chunks in increasing order with a cursor
+// into the table.
+__device__ __forceinline__ int find_tensor(const AdamListParams& p, int64_t e) {
+  int lo = 0, hi = p.nt - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.t[mid].off <= e) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(256) adamw_list_sumsq_kernel(const __grid_constant__ AdamListParams p) {
+  __shared__ double red[8];
+  double acc = 0.0;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int k = i < p.n4 ? find_tensor(p, 4 * i) : 0;
+  while (i < p.n4) {
+    while (k + 1 < p.nt && p.t[k + 1].off <= 4 * i) ++k;
+    // tensor k's entry in registers for all of this thread's chunks inside it
+    const int64_t off = p.t[k].off, n = p.t[k].n;
+    if (4 * i < off || 4 * i >= off + n) { i += stride; continue; }   // a chunk nobody owns
+    const float* grad = p.t[k].grad;
+    const int64_t full = (off + (n & ~(int64_t)3)) / 4, end = (off + n + 3) / 4;
+    for (; i < full; i += stride) {
+      const float4 v = *reinterpret_cast<const float4*>(grad + (4 * i - off));
+      acc += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+    }
+    for (; i < end; i += stride) {           // the tensor's last, partial chunk
+      const int64_t loc = 4 * i - off;
+      for (int64_t j = loc; j < n; ++j) acc += (double)grad[j] * grad[j];
+    }
+  }
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int w = 0; w < 8; ++w) t += red[w];
+    p.partials[blockIdx.x] = t;
+    if (blockIdx.x == 0) *p.step += 1.f;
+  }
+}
+
+__global__ void __launch_bounds__(256) adamw_list_update_kernel(const __grid_constant__ AdamListParams p) {
+  __shared__ float s_clip;
+  if (threadIdx.x == 0) {
+    double t = 0.0;
+    for (int i = 0; i < p.npart; ++i) t += p.partials[i];
+    const double norm = sqrt(t);
+    float clip = 1.f;
+    if (p.max_norm > 0.f) {
+      const double c = (double)p.max_norm / (norm + 1e-6);
+      clip = c < 1.0 ? (float)c : 1.f;
+    }
+    if (!isfinite(norm) && p.status) atomicOr(p.status, SISA_ST_NONFINITE);
+    s_clip = clip;
+  }
+  __syncthreads();
+  const float clip = s_clip;
+  const float t = *p.step;
+  const float bc1 = 1.f - powf(p.beta1, t), bc2 = 1.f - powf(p.beta2, t);
+  const float bc2_sqrt = sqrtf(bc2);
+  const float b1 = p.beta1, b2 = p.beta2, omb1 = 1.f - p.beta1, omb2 = 1.f - p.beta2;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  int k = i < p.n4 ? find_tensor(p, 4 * i) : 0;
+  // one chunk of 4 elements (cnt of them real); the arithmetic of the flat kernel
+  auto update = [&](float* pv, const float* gv, int64_t ci, float decay, float step_size) {
+    float4 mv = reinterpret_cast<float4*>(p.m)[ci];
+    float4 vv = reinterpret_cast<float4*>(p.v)[ci];
+    float* mp = &mv.x;
+    float* vp = &vv.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float gr = gv[j] * clip;
+      pv[j] *= decay;
+      mp[j] = b1 * mp[j] + omb1 * gr;
+      vp[j] = b2 * vp[j] + omb2 * gr * gr;
+      const float denom = sqrtf(vp[j]) / bc2_sqrt + p.eps;
+      pv[j] -= step_size * mp[j] / denom;
+    }
+    reinterpret_cast<float4*>(p.m)[ci] = mv;
+    reinterpret_cast<float4*>(p.v)[ci] = vv;
+  };
+  while (i < p.n4) {
+    while (k + 1 < p.nt && p.t[k + 1].off <= 4 * i) ++k;
+    // tensor k's entry in registers for all of this thread's chunks inside it
+    const int64_t off = p.t[k].off, n = p.t[k].n;
+    if (4 * i < off || 4 * i >= off + n) { i += stride; continue; }   // a chunk nobody owns
+    float* param = p.t[k].param;
+    const float* grad = p.t[k].grad;
+    const float decay = 1.f - p.t[k].lr * p.t[k].weight_decay, step_size = p.t[k].lr / bc1;
+    const int64_t full = (off + (n & ~(int64_t)3)) / 4, end = (off + n + 3) / 4;
+    for (; i < full; i += stride) {
+      const int64_t loc = 4 * i - off;
+      const float4 a = *reinterpret_cast<const float4*>(param + loc);
+      const float4 b = *reinterpret_cast<const float4*>(grad + loc);
+      float pv[4] = {a.x, a.y, a.z, a.w};
+      const float gv[4] = {b.x, b.y, b.z, b.w};
+      update(pv, gv, i, decay, step_size);
+      *reinterpret_cast<float4*>(param + loc) = make_float4(pv[0], pv[1], pv[2], pv[3]);
+    }
+    for (; i < end; i += stride) {           // the tensor's last, partial chunk
+      const int64_t loc = 4 * i - off;
+      const int cnt = (int)(n - loc);
+      float pv[4], gv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        pv[j] = j < cnt ? param[loc + j] : 0.f;
+        gv[j] = j < cnt ? grad[loc + j] : 0.f;
+      }
+      update(pv, gv, i, decay, step_size);
+      for (int j = 0; j < cnt; ++j) param[loc + j] = pv[j];
+    }
+  }
+}
+
 }  // namespace optim
+
+cudaError_t launch_adamw_list(const AdamListParams& p, cudaStream_t st) {
+  if (p.n4 == 0 || p.nt == 0) return cudaSuccess;
+  optim::adamw_list_sumsq_kernel<<<p.npart, 256, 0, st>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  optim::adamw_list_update_kernel<<<p.nblocks, 256, 0, st>>>(p);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_adamw(const AdamParams& p, cudaStream_t st) {
   if (p.n4 == 0) return cudaSuccess;

@@ -29,4 +29,29 @@ struct AdamParams {
 
 cudaError_t launch_adamw(const AdamParams& p, cudaStream_t st);
 
+// One parameter tensor of the tensor-list form; the same layout as sisa_adam_tensor.
+struct AdamTensor {
+  float* param;            // n fp32 values, 16-byte aligned
+  const float* grad;       // n fp32 values, 16-byte aligned
+  int64_t off, n;          // its first element in m / v (a multiple of 4) and its size
+  float lr, weight_decay;
+};
+
+// The table travels by value in the kernels' parameters (no device copy, captured with a graph).
+constexpr int kMaxAdamTensors = 384;
+struct AdamListParams {
+  AdamTensor t[kMaxAdamTensors];   // sorted by off
+  int nt;
+  float* m;
+  float* v;
+  int64_t n4;              // 4-element chunks of m / v covered by the table
+  float* step;
+  double* partials;
+  int npart, nblocks;
+  float beta1, beta2, eps, max_norm;
+  int32_t* status;
+};
+
+cudaError_t launch_adamw_list(const AdamListParams& p, cudaStream_t st);
+
 }  // namespace sisa

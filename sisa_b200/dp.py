@@ -177,7 +177,7 @@ class Trainer:
 
     def __init__(self, model: SISAForCausalLM, optimizer: torch.optim.Optimizer | None = None, *,
                  fused_ce: bool = True, clip: float = 1.0, bucket_cap_mb: float = 40.0, cuda_graph: bool = False,
-                 flat_grads: bool = False, flat_optimizer: bool | None = None):
+                 flat_grads: bool = False, flat_optimizer: bool | None = None, tensor_optimizer: bool = True):
         self.module = model
         self._params = list(model.parameters())
         dev = next(model.parameters()).device
@@ -194,6 +194,13 @@ class Trainer:
         self.flat_opt = bool(flat_optimizer) and optimizer is None and dev.type == "cuda" and \
             all(p.dtype == torch.float32 for p in trainable)
         self.flat = flat_dp or self.flat_opt
+        # Otherwise the same kernels over the parameter tensors as they are (sisa_b200.optim.TensorAdamW):
+        # clipping and AdamW in two launches instead of torch's fused AdamW plus clip_grad_norm_.
+        from .optim import TensorAdamW
+
+        self.list_opt = (tensor_optimizer and optimizer is None and not self.flat and dev.type == "cuda"
+                         and all(p.dtype == torch.float32 for p in trainable)
+                         and len(trainable) <= TensorAdamW.MAX_TENSORS)
         self._buckets: GradBuckets | None = None
         if self.flat:
             self.model = model
@@ -209,6 +216,8 @@ class Trainer:
 
             self.opt = FlatAdamW(model.param_groups(6e-4, weight_decay=0.1), self._buckets, betas=(0.9, 0.95),
                                  max_norm=clip)
+        elif self.list_opt:
+            self.opt = TensorAdamW(model.param_groups(6e-4, weight_decay=0.1), betas=(0.9, 0.95), max_norm=clip)
         else:
             self.opt = optimizer or make_optimizer(model, capturable=self.cuda_graph)
         self.fused_ce = fused_ce and dev.type == "cuda"
@@ -294,8 +303,8 @@ class Trainer:
     def _update(self) -> None:
         """Clipping and the optimizer step (in the flat form the allreduces have run during the backward;
         the flat AdamW clips inside its kernels)."""
-        if self.flat_opt:
-            self.opt.step()
+        if self.flat_opt or self.list_opt:
+            self.opt.step()                          # clips inside its kernels
         else:
             if self.clip:
                 torch.nn.utils.clip_grad_norm_(self.module.parameters(), self.clip)

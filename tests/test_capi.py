@@ -191,3 +191,29 @@ def test_row_copy_jobs_are_checked_on_the_host():
     assert lib.sisa_copy_rows(0x30000, 4, 100, 7, None, None) == _lib.ERR_TYPE
     assert lib.sisa_copy_rows(0x30000, -1, 100, _lib.BF16, None, None) == _lib.ERR_VALUE
     assert lib.sisa_copy_rows(None, 0, 0, _lib.BF16, None, None) == _lib.OK
+
+
+def test_adamw_tensor_list_is_checked_on_the_host():
+    """sisa_adamw_tensors checks its host table before any CUDA call (fake 16-byte-aligned addresses;
+    every call here is invalid, so none reaches the device)."""
+    lib = _lib.load()
+    A = 0x10000
+
+    def call(entries, n_state=4096, **kw):
+        tab = (_lib.AdamTensor * max(1, len(entries)))()
+        for e, (param, grad, off, n) in zip(tab, entries):
+            e.param, e.grad, e.offset, e.n, e.lr, e.weight_decay = param, grad, off, n, 1e-3, 0.1
+        a = dict(m=A, v=A + 0x4000, npart=296, b1=0.9, b2=0.95, eps=1e-8)
+        a.update(kw)
+        return lib.sisa_adamw_tensors(tab, len(entries), a["m"], a["v"], n_state, A, A, a["npart"], a["b1"], a["b2"],
+                                      a["eps"], 1.0, None, None)
+
+    assert call([(A, A, 2, 5)]) == _lib.ERR_VALUE                                # offset not a multiple of 4
+    assert call([(A, A, 0, 5), (A, A, 4, 3)]) == _lib.ERR_VALUE                  # overlaps the previous tensor
+    assert call([(A, A, 4092, 8)]) == _lib.ERR_VALUE                             # past n_state
+    assert call([(A + 4, A, 0, 5)]) == _lib.ERR_ALIGN
+    assert call([(A, None, 0, 5)]) == _lib.ERR_VALUE
+    assert call([(A, A, 0, 5)], n_state=4094) == _lib.ERR_VALUE
+    assert call([(A, A, 0, 5)], eps=0.0) == _lib.ERR_VALUE
+    assert call([(A, A, 0, 5)], m=A + 8) == _lib.ERR_ALIGN
+    assert call([(A, A, 4 * k, 1) for k in range(385)], n_state=4 * 385) == _lib.ERR_VALUE

@@ -106,8 +106,8 @@ def test_training_forward_sees_updates_that_keep_the_versions(cuda_dev):
     from sisa_b200 import dp
 
     model = _model(cuda_dev)
-    tr = dp.Trainer(model)
-    assert getattr(tr.opt, "defaults", {}).get("fused")
+    tr = dp.Trainer(model, dp.make_optimizer(model))
+    assert tr.opt.defaults.get("fused")
     ids = torch.randint(0, 512, (2, 192), generator=torch.Generator().manual_seed(2)).to(cuda_dev)
     for _ in range(3):
         tr.step(ids)
@@ -120,7 +120,7 @@ def test_training_forward_sees_updates_that_keep_the_versions(cuda_dev):
             assert torch.equal(owner.__dict__[slot][1], want), slot
     # an inference forward after more steps (eager and graphed) sees them too
     for graph in (False, True):
-        tr2 = dp.Trainer(model, cuda_graph=graph)
+        tr2 = dp.Trainer(model, dp.make_optimizer(model, capturable=graph), cuda_graph=graph)
         for _ in range(3):
             tr2.step(ids)
         with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
