@@ -225,6 +225,14 @@ int sisa_adamw_tensors(const sisa_adam_tensor* tensors, int ntensors, float* m, 
  * sisa_row_copy_check: checks one job on the host (no CUDA call).
  * sisa_copy_rows: `jobs` holds njobs checked jobs in DEVICE memory (so a captured CUDA graph can replay
  * the launch); max_vectors is the largest rows * cols / 8 among them. */
+/* sisa_copy_heads: dst[b, h, t, 0:width] = src[b, h, t, 0:width] for 16-bit elements (bf16 / fp16), b < B,
+ * h < H, t < L, with element strides (sb, sh, sl) on each side: the prompt's keys, values and rotated
+ * B~ (views of the fused projection / the preparation output) into a decode cache's buffers, as
+ * LayerState.append of the reference's generation.py:58-95 does with torch copies. width a multiple of
+ * 8, H * width / 8 <= 256, pointers 16-byte aligned and every stride a multiple of 8. */
+int sisa_copy_heads(const void* src, int64_t src_sb, int64_t src_sh, int64_t src_sl, void* dst, int64_t dst_sb,
+                    int64_t dst_sh, int64_t dst_sl, int64_t B, int64_t H, int64_t L, int64_t width, void* stream);
+
 typedef struct sisa_row_copy {
   const float* src;
   void* dst;

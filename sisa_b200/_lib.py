@@ -104,6 +104,7 @@ SIGNATURES = {
     "sisa_adamw_tensors": (_I, [ctypes.POINTER(AdamTensor), _I, _P, _P, _I64, _P, _P, _I, ctypes.c_float,
                                 ctypes.c_float, ctypes.c_float, ctypes.c_float, _P, _P]),
     "sisa_row_copy_check": (_I, [ctypes.POINTER(RowCopy)]),
+    "sisa_copy_heads": (_I, [_P, _I64, _I64, _I64, _P, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _P]),
     "sisa_copy_rows": (_I, [_P, _I, _I64, _I, _P, _P]),
     "sisa_gemm_swiglu": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _P, _P]),
     "sisa_gemm_workspace": (_I64, [_I64, _I64, _I64, _I]),

@@ -743,6 +743,28 @@ int sisa_row_copy_check(const sisa_row_copy* j) {
   return SISA_OK;
 }
 
+int sisa_copy_heads(const void* src, int64_t src_sb, int64_t src_sh, int64_t src_sl, void* dst, int64_t dst_sb,
+                    int64_t dst_sh, int64_t dst_sl, int64_t B, int64_t H, int64_t L, int64_t width, void* stream) {
+  if (!src || !dst) return fail(SISA_ERR_VALUE, "sisa_copy_heads: null pointer");
+  if (B < 0 || H < 1 || L < 0 || width < 8 || width % 8 || H * (width / 8) > 256 || B > ((int64_t)1 << 31) ||
+      L > ((int64_t)1 << 31))
+    return fail(SISA_ERR_VALUE, "sisa_copy_heads: need B, L >= 0, H >= 1, width a positive multiple of 8 and "
+                "H * width / 8 <= 256 (B=%lld H=%lld L=%lld width=%lld)", (long long)B, (long long)H, (long long)L,
+                (long long)width);
+  if (!aligned16(src) || !aligned16(dst) || src_sb % 8 || src_sh % 8 || src_sl % 8 || dst_sb % 8 || dst_sh % 8 ||
+      dst_sl % 8)
+    return fail(SISA_ERR_ALIGN, "sisa_copy_heads: pointers must be 16-byte aligned and strides multiples of 8");
+  if (B == 0 || L == 0) return SISA_OK;
+  int rc;
+  sisa::DeviceScope scope;
+  if ((rc = scope.bind(dst))) return rc;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, scope.device());
+  const sisa::HeadsCopy p{src, src_sb, src_sh, src_sl, dst, dst_sb, dst_sh, dst_sl, B, H, L, width};
+  cudaError_t e = sisa::launch_copy_heads(p, sms, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_copy_heads launch");
+}
+
 int sisa_copy_rows(const sisa_row_copy* jobs, int njobs, int64_t max_vectors, int dtype, int32_t* status,
                    void* stream) {
   (void)status;

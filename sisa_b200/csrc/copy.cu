@@ -2,6 +2,9 @@
 // weights (the concatenated projection weight, the interleaved gate/up weight, the plain linears), which
 // change after every optimizer step and were otherwise refreshed by one small cast kernel per weight.
 //
+// copy_heads_kernel moves per-head rows of 16-bit elements between two (batch, head, position)
+// layouts: the prompt's keys, values and rotated B~ into a decode cache's buffers.
+//
 // Job j (one row of the grid's y dimension) copies source rows r = 0 .. rows-1 of `cols` fp32 values to
 // destination row (r / block_rows) * dst_block_stride + r % block_rows, rounding to nearest even; a job
 // without a source zero-fills its destination rows. Each thread moves 8 values at a time (two 16-byte
@@ -35,7 +38,35 @@ __global__ void __launch_bounds__(256) copy_rows_kernel(const RowCopy* __restric
   }
 }
 
+// dst[b, h, t, 0:width] = src[b, h, t, 0:width] for 16-bit elements, both sides with their own
+// (batch, head, position) strides and `width` contiguous elements (a multiple of 8): thread (x, y) of a
+// block takes 16-byte vector x of position row y, the vectors of all heads of a position side by side.
+__global__ void __launch_bounds__(256) copy_heads_kernel(HeadsCopy p) {
+  const int nv = (int)(p.width / 8), per_row = (int)p.H * nv;
+  const int j = threadIdx.x;
+  if (j >= per_row) return;
+  const int h = j / nv, v = j - h * nv;
+  const int64_t rows = p.B * p.L;
+  for (int64_t r = (int64_t)blockIdx.x * blockDim.y + threadIdx.y; r < rows; r += (int64_t)gridDim.x * blockDim.y) {
+    const int64_t b = r / p.L, t = r - b * p.L;
+    const uint4 x = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.src) + b * p.ssb + h * p.ssh +
+                                                    t * p.ssl + 8 * v);
+    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.dst) + b * p.dsb + h * p.dsh + t * p.dsl + 8 * v) = x;
+  }
+}
+
 }  // namespace copy
+
+cudaError_t launch_copy_heads(const HeadsCopy& p, int num_sms, cudaStream_t st) {
+  const int64_t rows = p.B * p.L;
+  if (rows == 0 || p.H == 0) return cudaSuccess;
+  const int per_row = (int)(p.H * (p.width / 8));
+  const int tx = (per_row + 31) / 32 * 32, ty = 256 / tx > 0 ? 256 / tx : 1;
+  int64_t grid = (rows + ty - 1) / ty;
+  if (grid > 8 * (int64_t)num_sms) grid = 8 * (int64_t)num_sms;
+  copy::copy_heads_kernel<<<(unsigned)grid, dim3(tx, ty), 0, st>>>(p);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_copy_rows(const RowCopy* jobs, int njobs, int64_t max_vectors, int dtype, cudaStream_t st) {
   if (njobs == 0) return cudaSuccess;

@@ -16,4 +16,14 @@ struct RowCopy {
 // jobs: njobs entries in device memory; max_vectors: the largest rows * cols / 8 among them.
 cudaError_t launch_copy_rows(const RowCopy* jobs, int njobs, int64_t max_vectors, int dtype, cudaStream_t st);
 
+// Per-head rows of 16-bit elements between two (batch, head, position) layouts (element strides).
+struct HeadsCopy {
+  const void* src;
+  int64_t ssb, ssh, ssl;
+  void* dst;
+  int64_t dsb, dsh, dsl;
+  int64_t B, H, L, width;
+};
+cudaError_t launch_copy_heads(const HeadsCopy& p, int num_sms, cudaStream_t st);
+
 }  // namespace sisa

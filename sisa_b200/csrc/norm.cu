@@ -562,8 +562,12 @@ __device__ __forceinline__ int64_t cta_batches(int64_t nb) {
   return nb > (int64_t)blockIdx.x ? (nb - 1 - blockIdx.x) / gridDim.x + 1 : 0;
 }
 
-template <int NP, typename TY>
+// TX: the residual stream's type (fp32 in training, the compute dtype in inference). With a 16-bit stream
+// the sum x + res and the normalised row are rounded to it, as the eager model computes them (the
+// warp-per-row kernel's rnd_to), before the norm and the projection read them.
+template <int NP, typename TY, typename TX>
 __global__ void __launch_bounds__(256) norm_fwd_tma_kernel(const __grid_constant__ NormFwd p) {
+  constexpr bool kLowX = !std::is_same<TX, float>::value;
   constexpr int R = kFwdRows, NPP = NP > 0 ? NP : 1;
   constexpr int NZ = NP > 8 ? 16 : (NP > 0 ? 8 : 1);   // projection entries padded to 2^k
   extern __shared__ __align__(128) unsigned char sbuf[];
@@ -573,10 +577,10 @@ __global__ void __launch_bounds__(256) norm_fwd_tma_kernel(const __grid_constant
   const int d = (int)p.d, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int c = 4 * threadIdx.x;
   const bool on = c < d, has_res = p.res != nullptr;
-  const uint32_t xrow = (uint32_t)d * 4, rrow = has_res ? (uint32_t)d * 2 : 0;
+  const uint32_t xrow = (uint32_t)d * sizeof(TX), rrow = has_res ? (uint32_t)d * 2 : 0;
   const uint32_t stage_bytes = R * (xrow + rrow);
   const int64_t nb = (p.rows + R - 1) / R, my_n = cta_batches(nb);
-  const float* xg = static_cast<const float*>(p.x);
+  const TX* xg = static_cast<const TX*>(p.x);
   const __nv_bfloat16* rg = static_cast<const __nv_bfloat16*>(p.res);
   auto issue = [&](int64_t k) {
     const int s = (int)(k % kStages);
@@ -610,7 +614,7 @@ __global__ void __launch_bounds__(256) norm_fwd_tma_kernel(const __grid_constant
     bool ok = true;
     if (threadIdx.x == 0) ok = mbar_wait(smem_u32(&s_bar[s]), (uint32_t)((k / kStages) & 1), p.status);
     if (__syncthreads_or(!ok)) break;   // every thread leaves together
-    const float* xs = reinterpret_cast<const float*>(sbuf + s * stage_bytes);
+    const TX* xs = reinterpret_cast<const TX*>(sbuf + s * stage_bytes);
     const __nv_bfloat16* rs_ = reinterpret_cast<const __nv_bfloat16*>(sbuf + s * stage_bytes + R * xrow);
     float v[R][4], ss[R];
 #pragma unroll
@@ -623,7 +627,7 @@ __global__ void __launch_bounds__(256) norm_fwd_tma_kernel(const __grid_constant
           float t[4];
           lds4(rs_ + i * d + c, t);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) v[i][q] += t[q];
+          for (int q = 0; q < 4; ++q) v[i][q] = kLowX ? round_lp<false>(v[i][q] + t[q]) : v[i][q] + t[q];
         }
       }
       ss[i] = fmaf(v[i][0], v[i][0], fmaf(v[i][1], v[i][1], fmaf(v[i][2], v[i][2], v[i][3] * v[i][3])));
@@ -636,9 +640,9 @@ __global__ void __launch_bounds__(256) norm_fwd_tma_kernel(const __grid_constant
       const bool live = on && i < nr;
       float h[4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) h[q] = (v[i][q] * rs) * w4[q];
+      for (int q = 0; q < 4; ++q) h[q] = kLowX ? round_lp<false>((v[i][q] * rs) * w4[q]) : (v[i][q] * rs) * w4[q];
       if (live) {
-        if (has_res && p.xsum) stg4(static_cast<float*>(p.xsum) + r * p.xsums + c, v[i]);
+        if (has_res && p.xsum) stg4(static_cast<TX*>(p.xsum) + r * p.xsums + c, v[i]);
         stg4(static_cast<TY*>(p.y[0]) + r * p.ys[0] + c, h);
         if (p.nout > 1) stg4(static_cast<TY*>(p.y[1]) + r * p.ys[1] + c, h);
       }
@@ -995,10 +999,12 @@ bool rows16(const void* ptr, int64_t stride, int dt) {
 int tma_threads(int64_t d) { return (int)((d / 4 + 31) / 32 * 32); }
 
 bool fwd_tma_ok(const NormFwd& p) {
-  if (p.d % 8 || p.d > 1024 || !tma_np_ok(p.np) || p.xdt != 2 || (p.res && p.resdt != 0)) return false;
+  // the stream fp32 (training) or bf16 (inference); a bf16 residual
+  if (p.d % 8 || p.d > 1024 || !tma_np_ok(p.np) || (p.xdt != 2 && p.xdt != 0) || (p.res && p.resdt != 0))
+    return false;
   if (p.ydt[0] != 0 && p.ydt[0] != 2) return false;
   if (p.nout > 1 && p.ydt[1] != p.ydt[0]) return false;
-  return rows16(p.x, p.xs, 2) && rows16(p.res, p.ress, 0) && rows16(p.xsum, p.xsums, 2) &&
+  return rows16(p.x, p.xs, p.xdt) && rows16(p.res, p.ress, 0) && rows16(p.xsum, p.xsums, p.xdt) &&
          rows16(p.y[0], p.ys[0], p.ydt[0]) && (p.nout < 2 || rows16(p.y[1], p.ys[1], p.ydt[1])) &&
          rows16(p.w, 0, 2) && rows16(p.pw, 0, 2);
 }
@@ -1016,8 +1022,9 @@ bool bwd_tma_ok(const NormBwd& p) {
 
 template <int NP, typename TY>
 cudaError_t fwd_tma(const NormFwd& p, cudaStream_t st) {
-  const size_t smem = (size_t)norm::kStages * norm::kFwdRows * p.d * (4 + (p.res ? 2 : 0));
-  auto k = norm::norm_fwd_tma_kernel<NP, TY>;
+  const size_t xb = p.xdt == 2 ? 4 : 2;
+  const size_t smem = (size_t)norm::kStages * norm::kFwdRows * p.d * (xb + (p.res ? 2 : 0));
+  auto k = p.xdt == 2 ? norm::norm_fwd_tma_kernel<NP, TY, float> : norm::norm_fwd_tma_kernel<NP, TY, __nv_bfloat16>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   k<<<(unsigned)tma_grid(p.rows, norm::kFwdRows), tma_threads(p.d), smem, st>>>(p);

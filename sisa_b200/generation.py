@@ -24,6 +24,24 @@ __all__ = ["LayerState", "SISACache", "DecodeGraph", "generate"]
 _ROUND = 256
 
 
+def _copy_heads(dst: Tensor, src: Tensor) -> None:
+    """``dst.copy_(src)`` for (B, H, T, width) tensors. Between 16-bit CUDA tensors whose last dimension is
+    contiguous (the prompt's k and v are head views of the fused projection, strided by its row) one
+    16-byte-vector kernel moves whole rows (``sisa_copy_heads``); anything else is torch's copy."""
+    B, H, T, W = dst.shape
+    ok = (dst.is_cuda and src.is_cuda and dst.dtype == src.dtype and dst.dtype in (torch.bfloat16, torch.float16)
+          and tuple(src.shape) == (B, H, T, W) and dst.stride(-1) == 1 and src.stride(-1) == 1 and W % 8 == 0
+          and H * W // 8 <= 256 and dst.data_ptr() % 16 == 0 and src.data_ptr() % 16 == 0
+          and all(st % 8 == 0 for st in dst.stride()[:3] + src.stride()[:3]))
+    if not ok:
+        dst.copy_(src)
+        return
+    from . import _lib
+
+    _lib.check(_lib.load().sisa_copy_heads(src.data_ptr(), *src.stride()[:3], dst.data_ptr(), *dst.stride()[:3],
+                                           B, H, T, W, _lib.stream_ptr(dst.device)), "sisa_copy_heads")
+
+
 class LayerState:
     """Cached tensors of one layer: k, v ``(B, H, T, d_head)`` and b ``(B, H, T, d_state)`` in the compute
     dtype, g and fgate ``(B, H, T)`` fp32 (views of the first ``length`` positions of the buffers), phi
@@ -72,9 +90,9 @@ class LayerState:
         n = k.shape[2]
         self.reserve(n)
         t0, t1 = self.length, self.length + n
-        self.k_buf[:, :, t0:t1].copy_(k)
-        self.v_buf[:, :, t0:t1].copy_(v)
-        self.b_buf[:, :, t0:t1].copy_(b)
+        _copy_heads(self.k_buf[:, :, t0:t1], k)
+        _copy_heads(self.v_buf[:, :, t0:t1], v)
+        _copy_heads(self.b_buf[:, :, t0:t1], b)
         self.g_buf[:, :, t0:t1].copy_(g)
         self.f_buf[:, :, t0:t1].copy_(fgate)
         self.phi = phi

@@ -109,6 +109,9 @@ def _ref_block(x, res, w, pw, pb, eps, out_dtypes):
     (129, 768, torch.float32, False, 1, 12),    # the first block (no residual add)
     (77, 100, torch.float32, True, 2, 3),       # d not a multiple of 4: scalar path
     (64, 256, torch.bfloat16, True, 1, 16),     # bf16 residual stream
+    (300, 768, torch.bfloat16, True, 1, 12),    # the inference model's attention norm (staged kernel)
+    (300, 768, torch.bfloat16, True, 1, 0),     # and its SwiGLU norm
+    (129, 768, torch.bfloat16, False, 1, 12),   # its first block
     (33, 1280, torch.float32, True, 1, 20),     # row not cached in registers, 32 projection slots
 ])
 def test_block_norm_matches_eager(rows, d, xdt, with_res, n_out, n_proj):
@@ -140,8 +143,16 @@ def test_block_norm_matches_eager(rows, d, xdt, with_res, n_out, n_proj):
     xk, rk, wk, (pwk, pbk) = unpack(ker_in)
     outs = block_norm(xk, wk, 1e-6, res=rk, out_dtypes=out_dtypes, proj=(pwk, pbk) if n_proj else None)
     ref_outs = ([v_ref] if with_res else []) + ys_ref + ([z_ref] if n_proj else [])
+    chk_outs = list(ref_outs)
+    if n_proj and xdt != torch.float32:
+        # a 16-bit stream rounds h to it before the projection; a one-ulp difference of the row's rstd
+        # (summation order) can flip such a rounding, so z is checked against the projection of the
+        # kernel's own rounded h (its last normalised output), and h against the reference at bf16
+        # tolerance
+        chk_outs[-1] = torch.nn.functional.linear(outs[-2].detach().float(), pwr.detach().float(),
+                                                  pbr.detach().float())
     assert len(outs) == len(ref_outs)
-    for o, r in zip(outs, ref_outs):
+    for o, r in zip(outs, chk_outs):
         assert o.dtype == r.dtype and o.shape == r.shape
         tol = 1e-5 if o.dtype == torch.float32 else 1e-2
         assert torch.allclose(o.float(), r.float(), rtol=tol, atol=tol)

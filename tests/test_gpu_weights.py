@@ -1,5 +1,6 @@
 """The one-launch refresh of the compute-dtype weight copies (``sisa_copy_rows``, kernels/weights.py)
-against the per-module builders it stands in for."""
+against the per-module builders it stands in for, and the cache fill's per-head copy
+(``sisa_copy_heads``) against torch's copy."""
 from __future__ import annotations
 
 import pytest
@@ -152,3 +153,23 @@ def test_trainer_losses_follow_the_unfused_path(cuda_dev, graph):
         tr.close()
     for a, b in zip(losses["cuda"], losses["torch"]):
         assert abs(a - b) <= 1e-3 * abs(b), losses
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_copy_heads_equals_torch_copy(cuda_dev, dtype):
+    """The prompt's k (a head view of the fused projection, strided by its row) and b~ (contiguous) into
+    slices of cache buffers with spare capacity: bit for bit torch's copy."""
+    from sisa_b200.generation import _copy_heads
+
+    B, L, H, npad, cap = 3, 517, 12, 3280, 1024
+    gen = torch.Generator(device=cuda_dev).manual_seed(7)
+    proj = torch.randn((B, L, npad), generator=gen, device=cuda_dev).to(dtype)
+    k = proj[..., 768:768 + H * 64].view(B, L, H, 64).transpose(1, 2)
+    b = torch.randn((B, H, L, 32), generator=gen, device=cuda_dev).to(dtype)
+    for src, w in ((k, 64), (b, 32)):
+        dst = torch.zeros((B, H, cap, w), dtype=dtype, device=cuda_dev)
+        want = dst.clone()
+        _copy_heads(dst[:, :, 40:40 + L], src)
+        want[:, :, 40:40 + L].copy_(src)
+        torch.cuda.synchronize()
+        assert torch.equal(dst, want)
