@@ -178,7 +178,8 @@ int sisa_gemm(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, 
  * up rows 8b .. 8b + 7, b = 0 .. d_ff / 8 - 1), K-major like x (rows, K), both in `dtype`. Outputs:
  * gu (rows, 2 d_ff), the projections in the same interleaved column order rounded to `dtype` (what the
  * backward reads), and a (rows, d_ff) = silu(g) * u computed in fp32 from the rounded g, u with one
- * rounding (sisa_swiglu_fwd's arithmetic). d_ff a multiple of 8; 16-byte aligned rows. */
+ * rounding (sisa_swiglu_fwd's arithmetic). d_ff a multiple of 8; 16-byte aligned rows. gu NULL: only a
+ * is stored (inference, where nothing reads the projections again). */
 int sisa_gemm_swiglu(const void* x, int64_t x_ld, const void* w, int64_t w_ld, void* gu, int64_t gu_ld, void* a,
                      int64_t a_ld, int64_t rows, int64_t d_ff, int64_t K, int dtype, int32_t* status, void* stream);
 

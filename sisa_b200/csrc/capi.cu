@@ -786,13 +786,13 @@ int sisa_gemm_swiglu(const void* x, int64_t x_ld, const void* w, int64_t w_ld, v
                      int64_t a_ld, int64_t rows, int64_t d_ff, int64_t K, int dtype, int32_t* status, void* stream) {
   int rc;
   if ((rc = check_dtype(dtype))) return rc;
-  if (!x || !w || !gu || !a) return fail(SISA_ERR_VALUE, "sisa_gemm_swiglu: null pointer");
+  if (!x || !w || !a) return fail(SISA_ERR_VALUE, "sisa_gemm_swiglu: null pointer");
   const int64_t lim = (int64_t)1 << 30;
   if (rows < 1 || d_ff < 8 || d_ff % 8 || K < 1 || rows > lim || 2 * d_ff > lim || K > lim)
     return fail(SISA_ERR_VALUE, "sisa_gemm_swiglu: need rows >= 1, d_ff a positive multiple of 8, K >= 1 "
                 "(rows=%lld d_ff=%lld K=%lld)", (long long)rows, (long long)d_ff, (long long)K);
-  if (!aligned16(x) || !aligned16(w) || !aligned16(gu) || !aligned16(a) || x_ld % 8 || w_ld % 8 || gu_ld % 8 ||
-      a_ld % 8 || x_ld < K || w_ld < K || gu_ld < 2 * d_ff || a_ld < d_ff)
+  if (!aligned16(x) || !aligned16(w) || !aligned16(a) || x_ld % 8 || w_ld % 8 || a_ld % 8 || x_ld < K ||
+      w_ld < K || a_ld < d_ff || (gu && (!aligned16(gu) || gu_ld % 8 || gu_ld < 2 * d_ff)))
     return fail(SISA_ERR_ALIGN, "sisa_gemm_swiglu: rows must be 16-byte aligned (ld multiple of 8 and >= width)");
   sisa::DeviceScope scope;
   if ((rc = scope.bind(x))) return rc;
@@ -801,7 +801,11 @@ int sisa_gemm_swiglu(const void* x, int64_t x_ld, const void* w, int64_t w_ld, v
   memset(&p, 0, sizeof(p));
   if ((rc = map_operand(&p.tm_a, x, x_ld, 0, rows, K, dt, "x"))) return rc;
   if ((rc = map_operand(&p.tm_b, w, w_ld, 0, 2 * d_ff, K, dt, "w"))) return rc;
-  if ((rc = map_output(&p.tm_c, gu, gu_ld, rows, 2 * d_ff, dtype))) return rc;
+  if (gu) {
+    if ((rc = map_output(&p.tm_c, gu, gu_ld, rows, 2 * d_ff, dtype))) return rc;
+  } else {
+    p.skip_c = 1;
+  }
   {
     EncodeTiledFn enc = encode_fn();
     cuuint64_t dims[2] = {(cuuint64_t)d_ff, (cuuint64_t)rows};
@@ -811,7 +815,7 @@ int sisa_gemm_swiglu(const void* x, int64_t x_ld, const void* w, int64_t w_ld, v
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return fail(SISA_ERR_ALIGN, "a: cuTensorMapEncodeTiled failed");
   }
-  p.ldc = gu_ld;
+  p.ldc = gu ? gu_ld : 0;
   p.M = (int)rows; p.N = (int)(2 * d_ff); p.K = (int)K;
   p.num_m = (int)((rows + 255) / 256);
   p.status = status;

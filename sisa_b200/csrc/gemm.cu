@@ -379,16 +379,18 @@ __device__ __forceinline__ void epilogue_swiglu(const GemmParams& p, uint32_t ta
   const uint32_t box = boxes + (uint32_t)(nbox % NBOX) * 4096u;
   if (lane == 0 && nbox >= NBOX) bulk_wait_read0();
   __syncwarp();
+  if (!p.skip_c) {
 #pragma unroll
-  for (int q = 0; q < 8; ++q)
-    st_shared_v4(box + sw128_off((uint32_t)lane, (uint32_t)q), w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+    for (int q = 0; q < 8; ++q)
+      st_shared_v4(box + sw128_off((uint32_t)lane, (uint32_t)q), w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  }
 #pragma unroll
   for (int q = 0; q < 4; ++q)
     st_shared_v4(box2 + sw64_off((uint32_t)lane, (uint32_t)q), a2[4 * q], a2[4 * q + 1], a2[4 * q + 2], a2[4 * q + 3]);
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0) {
-    tma_store_2d(&p.tm_c, box, col, row0);
+    if (!p.skip_c) tma_store_2d(&p.tm_c, box, col, row0);
     tma_store_2d(&p.tm_c2, box2, col / 2, row0);
     bulk_commit();
   }

@@ -32,6 +32,7 @@ struct GemmParams {
   float2* part;
   float* tgt;
   int V, n_part;
+  int skip_c;           // SwiGLU epilogue: store only the activation (inference), not C
 };
 
 enum GemmOut : int { GEMM_OUT_F32 = 0, GEMM_OUT_BF16 = 1, GEMM_OUT_F16 = 2 };

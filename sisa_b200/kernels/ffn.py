@@ -106,11 +106,32 @@ class _GateUpFn(torch.autograd.Function):
         return dh, dwg, dwu, None, None, None
 
 
+def _gate_up_inference(h: Tensor, w_gate: Tensor, w_up: Tensor, dtype: torch.dtype, owner) -> Tensor:
+    """The forward alone: only the activation is stored (the projections are what a backward would read)."""
+    d = h.shape[-1]
+    d_ff = w_gate.shape[0]
+    h2 = h.reshape(-1, d).to(dtype).contiguous()
+    rows = h2.shape[0]
+    w_il = _cached(owner, w_gate, w_up, dtype, False)
+    a = torch.empty((rows, d_ff), dtype=dtype, device=h.device)
+    if rows:
+        dev = h.device
+        _lib.check(_lib.load().sisa_gemm_swiglu(h2.data_ptr(), d, w_il.data_ptr(), d, None, 0, a.data_ptr(), d_ff,
+                                                rows, d_ff, d, _lib.dtype_code(dtype),
+                                                backends.status_word(dev).data_ptr(), _lib.stream_ptr(dev)),
+                   "sisa_gemm_swiglu")
+        backends.after_call(dev)
+    return a.view(*h.shape[:-1], d_ff)
+
+
 def gate_up_swiglu(h: Tensor, w_gate: Tensor, w_up: Tensor, dtype: torch.dtype, owner) -> Tensor:
     """``silu(h W_gate^T) * (h W_up^T)`` in ``dtype`` (the autocast computation of modeling.py:39-49 up to
-    the activation's single rounding), on the fused GEMM. ``owner`` keeps the interleaved weight copy."""
+    the activation's single rounding), on the fused GEMM. ``owner`` keeps the interleaved weight copy.
+    Without a gradient to compute, the projections are not stored at all."""
     if not supports(h, w_gate.shape[0], dtype):
         raise ValueError(f"gate_up_swiglu needs a CUDA input, a bf16/fp16 compute dtype and widths divisible by 8; "
                          f"got {h.device}, {dtype}, d_ff={w_gate.shape[0]}, d={h.shape[-1]}")
     with torch.autocast(h.device.type, enabled=False):
+        if not torch.is_grad_enabled() or not (h.requires_grad or w_gate.requires_grad or w_up.requires_grad):
+            return _gate_up_inference(h, w_gate, w_up, dtype, owner)
         return _GateUpFn.apply(h, w_gate, w_up, owner, dtype, torch.is_grad_enabled())

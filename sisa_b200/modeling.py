@@ -454,10 +454,16 @@ class SISABlock(nn.Module):
             xs, h, z = block_norm(x, wa, self.attn_norm.eps, res=m, proj=(pw, pb))
         a = attn._prefill_fused(h, cache, z) if prefill else attn._decode_fused(h, cache.get(attn.layer_idx), z)
         xs, f_in = block_norm(xs, wf, self.ffn_norm.eps, res=a)
+        from .kernels import ffn as ffn_kernels
+
+        d_ff = ffn.w_gate.weight.shape[0]
+        if prefill and ffn_kernels.supports(f_in, d_ff, f_in.dtype):
+            # the prompt's MLP: gate and up on the CTA-pair GEMM with the activation in its epilogue,
+            # storing only the activation
+            return xs, ffn.w_down(ffn_kernels.gate_up_swiglu(f_in, ffn.w_gate.weight, ffn.w_up.weight, f_in.dtype, ffn))
         # gate and up projections as one GEMM over the concatenated weights, the activation on its halves
         w_gu = _static(ffn, "_gate_up_static", lambda g, u: torch.cat([g, u]), ffn.w_gate.weight, ffn.w_up.weight)
         gu = F.linear(f_in, w_gu)
-        d_ff = ffn.w_gate.weight.shape[0]
         return xs, ffn.w_down(swiglu(gu[..., :d_ff], gu[..., d_ff:]))
 
     def forward_pair(self, x: Tensor, m: Tensor | None) -> tuple[Tensor, Tensor]:

@@ -153,8 +153,9 @@ def test_gemm_entry_points_reject_bad_arguments_before_any_cuda_call():
                                     a["rows"], a["dff"], a["K"], a["dtype"], None, None)
 
     assert swiglu(dff=36) == _lib.ERR_VALUE and "multiple of 8" in _lib.last_error()
-    assert swiglu(gu=None) == _lib.ERR_VALUE
+    assert swiglu(a=None) == _lib.ERR_VALUE                      # gu may be NULL (inference), a may not
     assert swiglu(guld=72) == _lib.ERR_ALIGN                      # gu rows must hold 2 d_ff
+    assert swiglu(gu=None, ald=36) == _lib.ERR_ALIGN              # without gu, a is still checked
     assert swiglu(dtype=_lib.F32) == _lib.ERR_TYPE
 
     assert lib.sisa_lce_seed_scale(None, 16, A, None, _lib.F32, None, None) == _lib.ERR_VALUE

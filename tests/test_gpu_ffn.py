@@ -157,3 +157,17 @@ def test_linear_cast_matches_autocast_linear(cuda_dev):
         first = owner._lp_W[1]
         linear_cast(x, W1, torch.bfloat16, owner, "W")
     assert owner._lp_W[1] is first
+
+
+def test_gate_up_inference_stores_only_the_activation(cuda_dev):
+    """Without a gradient to compute the fused GEMM stores only a: bit for bit the training forward's a."""
+    from types import SimpleNamespace
+
+    from sisa_b200.kernels.ffn import gate_up_swiglu
+
+    h, wg, wu = _case(1000, 768, 2744, 11, cuda_dev)
+    with torch.no_grad():
+        a_inf = gate_up_swiglu(h, wg, wu, torch.bfloat16, SimpleNamespace())
+    a_tr = gate_up_swiglu(h, wg.clone().requires_grad_(True), wu, torch.bfloat16, SimpleNamespace())
+    torch.cuda.synchronize()
+    assert a_tr.requires_grad and torch.equal(a_inf, a_tr.detach())
