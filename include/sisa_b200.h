@@ -327,9 +327,9 @@ int sisa_decode_attn(const sisa_view4* q, const sisa_view4* c, const float* g_q,
  * host programs that bind only this C ABI and have no device allocator, and serving loops held to a
  * fixed, pre-reserved memory budget. The split-K partials live in a fixed 4.3 MB array owned by the
  * library on every GPU that loads it; B*H may not exceed 16384 (SISA_ERR_VALUE otherwise). The first
- * call on a device resolves the array's address with that device current, so it should come before
- * any stream capture; a cudaDeviceReset makes that address stale. Calls that overlap on the GPU share
- * the array and race. The caller's current device is unchanged on return. */
+ * call on a device looks up the array's address (cudaGetSymbolAddress, with that device current) and
+ * keeps it; a cudaDeviceReset makes that address stale. Calls that overlap on the GPU share the array
+ * and race. The caller's current device is unchanged on return. */
 int sisa_decode_attn_noalloc(const sisa_view4* q, const sisa_view4* c, const float* g_q, const float* f_q,
                              const sisa_view4* k_cache, const sisa_view4* v_cache, const sisa_view4* b_cache,
                              const float* g_cache, const float* f_cache, int64_t gf_stride, const float* lam,
