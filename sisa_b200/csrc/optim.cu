@@ -19,6 +19,8 @@
 namespace sisa {
 namespace optim {
 
+constexpr int kSumsqLoads = 4;     // 16-byte gradient loads in flight per thread in the norm passes
+
 __device__ __forceinline__ double warp_sum(double v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -30,7 +32,17 @@ __global__ void __launch_bounds__(256) adamw_sumsq_kernel(const float* __restric
   __shared__ double red[8];
   double acc = 0.0;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+  // kSumsqLoads loads in flight per thread (the fixed grid is small), added in the same chunk order
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + (kSumsqLoads - 1) * stride < n4; i += kSumsqLoads * stride) {
+    float4 v[kSumsqLoads];
+#pragma unroll
+    for (int u = 0; u < kSumsqLoads; ++u) v[u] = reinterpret_cast<const float4*>(g)[i + u * stride];
+#pragma unroll
+    for (int u = 0; u < kSumsqLoads; ++u)
+      acc += (double)v[u].x * v[u].x + (double)v[u].y * v[u].y + (double)v[u].z * v[u].z + (double)v[u].w * v[u].w;
+  }
+  for (; i < n4; i += stride) {
     const float4 v = reinterpret_cast<const float4*>(g)[i];
     acc += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
   }
@@ -132,6 +144,15 @@ __global__ void __launch_bounds__(256) adamw_list_sumsq_kernel(const __grid_cons
     if (4 * i < off || 4 * i >= off + n) { i += stride; continue; }   // a chunk nobody owns
     const float* grad = p.t[k].grad;
     const int64_t full = (off + (n & ~(int64_t)3)) / 4, end = (off + n + 3) / 4;
+    for (; i + (kSumsqLoads - 1) * stride < full; i += kSumsqLoads * stride) {   // loads in flight, chunk order
+      float4 v[kSumsqLoads];
+#pragma unroll
+      for (int u = 0; u < kSumsqLoads; ++u)
+        v[u] = *reinterpret_cast<const float4*>(grad + (4 * (i + u * stride) - off));
+#pragma unroll
+      for (int u = 0; u < kSumsqLoads; ++u)
+        acc += (double)v[u].x * v[u].x + (double)v[u].y * v[u].y + (double)v[u].z * v[u].z + (double)v[u].w * v[u].w;
+    }
     for (; i < full; i += stride) {
       const float4 v = *reinterpret_cast<const float4*>(grad + (4 * i - off));
       acc += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
