@@ -202,7 +202,8 @@ int sisa_adamw_flat(float* param, const float* grad, float* m, float* v, int64_t
 
 /* The same AdamW with clipping over separate parameter tensors (the training step's own tensors,
  * gradients as autograd hands them over): tensors[k] = {param, grad, offset, n, lr, weight_decay}, param
- * and grad n fp32 values each, 16-byte aligned; offset (a multiple of 4, increasing with k) is the
+ * and grad n fp32 values each (16-byte aligned for the fast path; 4-byte aligned, e.g. a gradient in a
+ * DDP bucket, is accepted and read element by element); offset (a multiple of 4, increasing with k) is the
  * tensor's first element in the moment buffers m and v (n_state fp32 each, zero-initialised by the
  * caller). tensors is a HOST array of at most 384 entries: it is passed to the kernels by value, so a
  * captured CUDA graph replays it. The norm covers the listed gradients; tensors left out (no gradient)

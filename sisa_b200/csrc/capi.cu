@@ -704,8 +704,8 @@ int sisa_adamw_tensors(const sisa_adam_tensor* tensors, int ntensors, float* m, 
     if (!t.param || !t.grad || t.n < 1 || t.offset % 4 || t.offset < end || t.offset + t.n > n_state)
       return fail(SISA_ERR_VALUE, "sisa_adamw_tensors: tensor %d: need param, grad, n >= 1 and an offset that is "
                   "a multiple of 4, past the previous tensor, with offset + n <= n_state", k);
-    if (!aligned16(t.param) || !aligned16(t.grad))
-      return fail(SISA_ERR_ALIGN, "sisa_adamw_tensors: tensor %d: param and grad must be 16-byte aligned", k);
+    if ((reinterpret_cast<uintptr_t>(t.param) | reinterpret_cast<uintptr_t>(t.grad)) & 3u)
+      return fail(SISA_ERR_ALIGN, "sisa_adamw_tensors: tensor %d: param and grad must be 4-byte aligned", k);
     end = t.offset + t.n;
   }
   if (ntensors == 0) return SISA_OK;

@@ -27,6 +27,27 @@ __device__ __forceinline__ double warp_sum(double v) {
   return v;
 }
 
+// Warp 0 of an update block: the clipping factor from the norm pass's partial sums, into *s_clip. Lane l
+// adds partials l, l+32, ... in order and the warp folds the lane sums in a fixed butterfly, so every
+// block and every run gets the same bits; the 32 lanes keep the partial loads in flight together instead
+// of one thread reading them one after another while the whole grid waits.
+__device__ __forceinline__ void clip_from_partials(const double* partials, int npart, float max_norm,
+                                                   int32_t* status, float* s_clip) {
+  double t = 0.0;
+  for (int i = threadIdx.x; i < npart; i += 32) t += partials[i];
+  t = warp_sum(t);
+  if (threadIdx.x == 0) {
+    const double norm = sqrt(t);
+    float clip = 1.f;
+    if (max_norm > 0.f) {
+      const double c = (double)max_norm / (norm + 1e-6);
+      clip = c < 1.0 ? (float)c : 1.f;
+    }
+    if (!isfinite(norm) && status) atomicOr(status, SISA_ST_NONFINITE);
+    *s_clip = clip;
+  }
+}
+
 __global__ void __launch_bounds__(256) adamw_sumsq_kernel(const float* __restrict__ g, int64_t n4, double* partials,
                                                           float* step) {
   __shared__ double red[8];
@@ -62,18 +83,7 @@ __global__ void __launch_bounds__(256) adamw_update_kernel(AdamParams p) {
   AdamSeg* segs = reinterpret_cast<AdamSeg*>(smem);
   __shared__ float s_clip;
   for (int i = threadIdx.x; i < p.nseg; i += blockDim.x) segs[i] = p.segs[i];
-  if (threadIdx.x == 0) {
-    double t = 0.0;
-    for (int i = 0; i < p.npart; ++i) t += p.partials[i];
-    const double norm = sqrt(t);
-    float clip = 1.f;
-    if (p.max_norm > 0.f) {
-      const double c = (double)p.max_norm / (norm + 1e-6);
-      clip = c < 1.0 ? (float)c : 1.f;
-    }
-    if (!isfinite(norm) && p.status) atomicOr(p.status, SISA_ST_NONFINITE);
-    s_clip = clip;
-  }
+  if (threadIdx.x < 32) clip_from_partials(p.partials, p.npart, p.max_norm, p.status, &s_clip);
   __syncthreads();
   const float clip = s_clip;
   const float t = *p.step;
@@ -143,7 +153,9 @@ __global__ void __launch_bounds__(256) adamw_list_sumsq_kernel(const __grid_cons
     const int64_t off = p.t[k].off, n = p.t[k].n;
     if (4 * i < off || 4 * i >= off + n) { i += stride; continue; }   // a chunk nobody owns
     const float* grad = p.t[k].grad;
-    const int64_t full = (off + (n & ~(int64_t)3)) / 4, end = (off + n + 3) / 4;
+    // 16-byte loads where the tensor allows them (a gradient inside a DDP bucket may start anywhere)
+    const bool vec = (reinterpret_cast<uintptr_t>(grad) & 15u) == 0;
+    const int64_t end = (off + n + 3) / 4, full = vec ? (off + (n & ~(int64_t)3)) / 4 : off / 4;
     for (; i + (kSumsqLoads - 1) * stride < full; i += kSumsqLoads * stride) {   // loads in flight, chunk order
       float4 v[kSumsqLoads];
 #pragma unroll
@@ -157,9 +169,9 @@ __global__ void __launch_bounds__(256) adamw_list_sumsq_kernel(const __grid_cons
       const float4 v = *reinterpret_cast<const float4*>(grad + (4 * i - off));
       acc += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
     }
-    for (; i < end; i += stride) {           // the tensor's last, partial chunk
-      const int64_t loc = 4 * i - off;
-      for (int64_t j = loc; j < n; ++j) acc += (double)grad[j] * grad[j];
+    for (; i < end; i += stride) {           // the tensor's last, partial chunk (every chunk if unaligned)
+      const int64_t loc = 4 * i - off, stop = loc + 4 < n ? loc + 4 : n;
+      for (int64_t j = loc; j < stop; ++j) acc += (double)grad[j] * grad[j];
     }
   }
   acc = warp_sum(acc);
@@ -175,18 +187,7 @@ __global__ void __launch_bounds__(256) adamw_list_sumsq_kernel(const __grid_cons
 
 __global__ void __launch_bounds__(256) adamw_list_update_kernel(const __grid_constant__ AdamListParams p) {
   __shared__ float s_clip;
-  if (threadIdx.x == 0) {
-    double t = 0.0;
-    for (int i = 0; i < p.npart; ++i) t += p.partials[i];
-    const double norm = sqrt(t);
-    float clip = 1.f;
-    if (p.max_norm > 0.f) {
-      const double c = (double)p.max_norm / (norm + 1e-6);
-      clip = c < 1.0 ? (float)c : 1.f;
-    }
-    if (!isfinite(norm) && p.status) atomicOr(p.status, SISA_ST_NONFINITE);
-    s_clip = clip;
-  }
+  if (threadIdx.x < 32) clip_from_partials(p.partials, p.npart, p.max_norm, p.status, &s_clip);
   __syncthreads();
   const float clip = s_clip;
   const float t = *p.step;
@@ -222,7 +223,8 @@ __global__ void __launch_bounds__(256) adamw_list_update_kernel(const __grid_con
     float* param = p.t[k].param;
     const float* grad = p.t[k].grad;
     const float decay = 1.f - p.t[k].lr * p.t[k].weight_decay, step_size = p.t[k].lr / bc1;
-    const int64_t full = (off + (n & ~(int64_t)3)) / 4, end = (off + n + 3) / 4;
+    const bool vec = ((reinterpret_cast<uintptr_t>(param) | reinterpret_cast<uintptr_t>(grad)) & 15u) == 0;
+    const int64_t end = (off + n + 3) / 4, full = vec ? (off + (n & ~(int64_t)3)) / 4 : off / 4;
     for (; i < full; i += stride) {
       const int64_t loc = 4 * i - off;
       const float4 a = *reinterpret_cast<const float4*>(param + loc);
@@ -232,9 +234,9 @@ __global__ void __launch_bounds__(256) adamw_list_update_kernel(const __grid_con
       update(pv, gv, i, decay, step_size);
       *reinterpret_cast<float4*>(param + loc) = make_float4(pv[0], pv[1], pv[2], pv[3]);
     }
-    for (; i < end; i += stride) {           // the tensor's last, partial chunk
+    for (; i < end; i += stride) {           // the tensor's last, partial chunk (every chunk if unaligned)
       const int64_t loc = 4 * i - off;
-      const int cnt = (int)(n - loc);
+      const int cnt = n - loc < 4 ? (int)(n - loc) : 4;
       float pv[4], gv[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {

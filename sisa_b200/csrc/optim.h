@@ -31,8 +31,8 @@ cudaError_t launch_adamw(const AdamParams& p, cudaStream_t st);
 
 // One parameter tensor of the tensor-list form; the same layout as sisa_adam_tensor.
 struct AdamTensor {
-  float* param;            // n fp32 values, 16-byte aligned
-  const float* grad;       // n fp32 values, 16-byte aligned
+  float* param;            // n fp32 values (16-byte loads where 16-byte aligned)
+  const float* grad;       // n fp32 values
   int64_t off, n;          // its first element in m / v (a multiple of 4) and its size
   float lr, weight_decay;
 };

@@ -18,7 +18,7 @@ from . import _lib, backends
 __all__ = ["FlatAdamW", "TensorAdamW"]
 
 _SEG = np.dtype([("start", "<i8"), ("end", "<i8"), ("lr", "<f4"), ("weight_decay", "<f4")])
-NPART = 296      # fixed grid of the norm pass (its fixed-order partial sums make the norm deterministic)
+NPART = 592      # fixed grid of the norm pass, 4 blocks per SM (fixed-order partial sums: a deterministic norm)
 
 
 class FlatAdamW:

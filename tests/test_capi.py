@@ -212,7 +212,7 @@ def test_adamw_tensor_list_is_checked_on_the_host():
     assert call([(A, A, 2, 5)]) == _lib.ERR_VALUE                                # offset not a multiple of 4
     assert call([(A, A, 0, 5), (A, A, 4, 3)]) == _lib.ERR_VALUE                  # overlaps the previous tensor
     assert call([(A, A, 4092, 8)]) == _lib.ERR_VALUE                             # past n_state
-    assert call([(A + 4, A, 0, 5)]) == _lib.ERR_ALIGN
+    assert call([(A + 2, A, 0, 5)]) == _lib.ERR_ALIGN                            # not even 4-byte aligned
     assert call([(A, None, 0, 5)]) == _lib.ERR_VALUE
     assert call([(A, A, 0, 5)], n_state=4094) == _lib.ERR_VALUE
     assert call([(A, A, 0, 5)], eps=0.0) == _lib.ERR_VALUE

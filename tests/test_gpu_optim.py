@@ -59,15 +59,31 @@ def test_flat_adamw_kernel_matches_fp64(cuda_dev):
     assert int(backends.status_word(cuda_dev).item()) == 0
 
 
-def test_tensor_adamw_matches_fp64(cuda_dev):
-    """TensorAdamW (``sisa_adamw_tensors``) over separate tensors of awkward sizes, two groups, two
-    parameters without a gradient: three steps against the fp64 restatement of clip_grad_norm_ + AdamW."""
+def _packed(arrays, dev):
+    """Views into one buffer, back to back: every tensor after an odd-sized one starts off 16 bytes (as
+    gradients do inside a DDP bucket)."""
+    buf = torch.tensor(np.concatenate(arrays), device=dev)
+    out, o = [], 0
+    for a in arrays:
+        out.append(buf[o:o + a.size])
+        o += a.size
+    return out
+
+
+@pytest.mark.parametrize("packed", [False, True])
+def test_tensor_adamw_matches_fp64(cuda_dev, packed):
+    """TensorAdamW (``sisa_adamw_tensors``) over tensors of awkward sizes, two groups, two parameters
+    without a gradient: three steps against the fp64 restatement of clip_grad_norm_ + AdamW. ``packed``
+    makes parameters and gradients views into one buffer, most of them not 16-byte aligned."""
     from sisa_b200 import backends
     from sisa_b200.optim import TensorAdamW
 
     rng = np.random.default_rng(1)
     sizes = [12, 5, 1003, 40000, 7, 4096]
-    ps = [torch.tensor(rng.standard_normal(n).astype(np.float32), device=cuda_dev) for n in sizes]
+    init = [rng.standard_normal(n).astype(np.float32) for n in sizes]
+    ps = (_packed(init, cuda_dev) if packed else [torch.tensor(a, device=cuda_dev) for a in init])
+    if packed:
+        assert any(p.data_ptr() % 16 for p in ps)
     groups = [{"params": ps[:3], "lr": 1e-3, "weight_decay": 0.1}, {"params": ps[3:], "lr": 5e-4, "weight_decay": 0.0}]
     opt = TensorAdamW(groups, betas=(0.9, 0.95), eps=1e-8, max_norm=1.0)
     p64 = [p.double().cpu().numpy() for p in ps]
@@ -77,8 +93,15 @@ def test_tensor_adamw_matches_fp64(cuda_dev):
     for t in (1, 2, 3):
         grads = [None if k in untouched else (rng.standard_normal(n) * 3).astype(np.float32)
                  for k, n in enumerate(sizes)]
-        for p, g in zip(ps, grads):
-            p.grad = None if g is None else torch.tensor(g, device=cuda_dev)
+        if packed:
+            views = iter(_packed([np.zeros(n, np.float32) if g is None else g for n, g in zip(sizes, grads)],
+                                 cuda_dev))
+            for p, g in zip(ps, grads):
+                view = next(views)
+                p.grad = None if g is None else view
+        else:
+            for p, g in zip(ps, grads):
+                p.grad = None if g is None else torch.tensor(g, device=cuda_dev)
         opt.step()
         norm = np.sqrt(sum((g.astype(np.float64) ** 2).sum() for g in grads if g is not None))
         clip = min(1.0, 1.0 / (norm + 1e-6))
