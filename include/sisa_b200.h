@@ -172,6 +172,19 @@ int sisa_gemm(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, 
               int64_t M, int64_t N, int64_t K, int dtype, int out_dtype, int accumulate, const void* bias,
               int bias_dtype, void* workspace, int64_t workspace_bytes, int32_t* status, void* stream);
 
+/* sisa_gemm with a bias that covers only some columns: bias holds bias_ncols values of bias_dtype for
+ * columns [bias_col0, bias_col0 + bias_ncols) of C, and the other columns get none; output tiles that
+ * do not meet those columns skip the bias entirely. bias_round = 1 rounds each bias value to C's
+ * 16-bit type (which must be `dtype`) before the fp32 add: the cast autocast applies to a linear's
+ * bias. The bias needs only the alignment of its element type (it may be NULL when bias_ncols = 0).
+ * This is the fused projection's F.linear(x, W_cat, b_cat) (src/sisa/modeling.py:213-222,
+ * fused_prep.py:99-122), where b_cat is zero except the H alpha columns: the alpha bias is passed as it
+ * is stored instead of a full b_cat. */
+int sisa_gemm_bias_cols(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn, void* c,
+                        int64_t ldc, int64_t M, int64_t N, int64_t K, int dtype, int out_dtype, int accumulate,
+                        const void* bias, int bias_dtype, int64_t bias_col0, int64_t bias_ncols, int bias_round,
+                        void* workspace, int64_t workspace_bytes, int32_t* status, void* stream);
+
 /* The SwiGLU MLP's gate and up projections with the activation in the epilogue (src/sisa/modeling.py:39-49:
  * w_gate x, w_up x and silu(.) * (.), which the reference runs as two GEMMs and two elementwise kernels).
  * w (2 d_ff, K): the gate and up weights interleaved in blocks of 8 rows (gate rows 8b .. 8b + 7, then

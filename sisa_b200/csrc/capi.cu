@@ -837,31 +837,32 @@ int64_t sisa_gemm_workspace(int64_t M, int64_t N, int64_t K, int out_dtype) {
   return sisa::gemm_workspace_bytes(M, N, K, out, sms);
 }
 
-int sisa_gemm(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn, void* c, int64_t ldc,
-              int64_t M, int64_t N, int64_t K, int dtype, int out_dtype, int accumulate, const void* bias,
-              int bias_dtype, void* workspace, int64_t workspace_bytes, int32_t* status, void* stream) {
+// The checks and the launch shared by sisa_gemm and sisa_gemm_bias_cols; the bias (if any) has been
+// checked by the caller and covers columns [bias_c0, bias_c1).
+static int gemm_impl(const char* name, const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn,
+                     void* c, int64_t ldc, int64_t M, int64_t N, int64_t K, int dtype, int out_dtype, int accumulate,
+                     const void* bias, int bias_dtype, int64_t bias_c0, int64_t bias_c1, int bias_vec,
+                     int bias_round, void* workspace, int64_t workspace_bytes, int32_t* status, void* stream) {
   int rc;
   if ((rc = check_dtype(dtype))) return rc;
-  if (!a || !b || !c) return fail(SISA_ERR_VALUE, "sisa_gemm: null pointer");
+  if (!a || !b || !c) return fail(SISA_ERR_VALUE, "%s: null pointer", name);
   if ((a_mn != 0 && a_mn != 1) || (b_mn != 0 && b_mn != 1))
-    return fail(SISA_ERR_VALUE, "sisa_gemm: a_mn and b_mn are 0 (K-major) or 1 (MN-major)");
+    return fail(SISA_ERR_VALUE, "%s: a_mn and b_mn are 0 (K-major) or 1 (MN-major)", name);
   if (out_dtype != SISA_F32 && out_dtype != SISA_BF16 && out_dtype != SISA_F16)
-    return fail(SISA_ERR_TYPE, "sisa_gemm: out_dtype must be SISA_F32, SISA_BF16 or SISA_F16 (got %d)", out_dtype);
-  if (accumulate && out_dtype != SISA_F32) return fail(SISA_ERR_VALUE, "sisa_gemm: accumulate needs an fp32 output");
+    return fail(SISA_ERR_TYPE, "%s: out_dtype must be SISA_F32, SISA_BF16 or SISA_F16 (got %d)", name, out_dtype);
+  if (accumulate && out_dtype != SISA_F32) return fail(SISA_ERR_VALUE, "%s: accumulate needs an fp32 output", name);
   const int64_t lim = (int64_t)1 << 30;
   if (M < 1 || N < 1 || K < 1 || M > lim || N > lim || K > lim)
-    return fail(SISA_ERR_VALUE, "sisa_gemm: need 1 <= M, N, K <= 2^30 (M=%lld N=%lld K=%lld)", (long long)M,
+    return fail(SISA_ERR_VALUE, "%s: need 1 <= M, N, K <= 2^30 (M=%lld N=%lld K=%lld)", name, (long long)M,
                 (long long)N, (long long)K);
   const int64_t osz = out_dtype == SISA_F32 ? 4 : 2;
   if (!aligned16(a) || !aligned16(b) || !aligned16(c) || lda % 8 || ldb % 8 || (ldc * osz) % 16 ||
       lda < (a_mn ? M : K) || ldb < (b_mn ? N : K) || ldc < N)
-    return fail(SISA_ERR_ALIGN, "sisa_gemm: operands and C must be 16-byte aligned with row strides of whole "
-                "16-byte units covering their rows (lda=%lld ldb=%lld ldc=%lld)", (long long)lda, (long long)ldb,
+    return fail(SISA_ERR_ALIGN, "%s: operands and C must be 16-byte aligned with row strides of whole "
+                "16-byte units covering their rows (lda=%lld ldb=%lld ldc=%lld)", name, (long long)lda, (long long)ldb,
                 (long long)ldc);
-  if (bias && ((bias_dtype != SISA_BF16 && bias_dtype != SISA_F16 && bias_dtype != SISA_F32) || !aligned16(bias)))
-    return fail(SISA_ERR_VALUE, "sisa_gemm: bias must be 16-byte aligned SISA_BF16, SISA_F16 or SISA_F32");
   if (workspace && (!aligned16(workspace) || workspace_bytes < 0))
-    return fail(SISA_ERR_VALUE, "sisa_gemm: workspace must be 16-byte aligned");
+    return fail(SISA_ERR_VALUE, "%s: workspace must be 16-byte aligned", name);
   sisa::DeviceScope scope;
   if ((rc = scope.bind(a))) return rc;
   const CUtensorMapDataType dt = dtype == SISA_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
@@ -869,6 +870,7 @@ int sisa_gemm(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, 
   memset(&p, 0, sizeof(p));
   p.bias = bias;
   p.bias_dtype = bias_dtype == SISA_F32 ? 2 : bias_dtype == SISA_F16 ? 1 : 0;
+  p.bias_c0 = (int)bias_c0; p.bias_c1 = (int)bias_c1; p.bias_vec = bias_vec; p.bias_round = bias_round;
   if (workspace && workspace_bytes > 0) { p.sema = static_cast<uint32_t*>(workspace); p.ws_bytes = workspace_bytes; }
   if ((rc = map_operand(&p.tm_a, a, lda, a_mn, M, K, dt, "a"))) return rc;
   if ((rc = map_operand(&p.tm_b, b, ldb, b_mn, N, K, dt, "b"))) return rc;
@@ -888,7 +890,41 @@ int sisa_gemm(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, 
     else if (!strcmp(t, "narrow")) tile = 0;
   }
   cudaError_t e = sisa::launch_gemm(p, dtype, a_mn, b_mn, out, tile, sms, static_cast<cudaStream_t>(stream));
-  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_gemm launch");
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, name);
+}
+
+
+int sisa_gemm(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn, void* c, int64_t ldc,
+              int64_t M, int64_t N, int64_t K, int dtype, int out_dtype, int accumulate, const void* bias,
+              int bias_dtype, void* workspace, int64_t workspace_bytes, int32_t* status, void* stream) {
+  if (bias && ((bias_dtype != SISA_BF16 && bias_dtype != SISA_F16 && bias_dtype != SISA_F32) || !aligned16(bias)))
+    return fail(SISA_ERR_VALUE, "sisa_gemm: bias must be 16-byte aligned SISA_BF16, SISA_F16 or SISA_F32");
+  return gemm_impl("sisa_gemm", a, lda, a_mn, b, ldb, b_mn, c, ldc, M, N, K, dtype, out_dtype, accumulate, bias,
+                   bias_dtype, 0, N, 1, 0, workspace, workspace_bytes, status, stream);
+}
+
+int sisa_gemm_bias_cols(const void* a, int64_t lda, int a_mn, const void* b, int64_t ldb, int b_mn, void* c,
+                        int64_t ldc, int64_t M, int64_t N, int64_t K, int dtype, int out_dtype, int accumulate,
+                        const void* bias, int bias_dtype, int64_t bias_col0, int64_t bias_ncols, int bias_round,
+                        void* workspace, int64_t workspace_bytes, int32_t* status, void* stream) {
+  if (!bias && bias_ncols > 0) return fail(SISA_ERR_VALUE, "sisa_gemm_bias_cols: null bias");
+  if (bias_dtype != SISA_BF16 && bias_dtype != SISA_F16 && bias_dtype != SISA_F32)
+    return fail(SISA_ERR_TYPE, "sisa_gemm_bias_cols: bias_dtype must be SISA_BF16, SISA_F16 or SISA_F32");
+  const uintptr_t esz = bias_dtype == SISA_F32 ? 4 : 2;
+  if (reinterpret_cast<uintptr_t>(bias) % esz)
+    return fail(SISA_ERR_ALIGN, "sisa_gemm_bias_cols: bias must be aligned to its element size");
+  if (bias_col0 < 0 || bias_ncols < 0 || bias_col0 > N || bias_ncols > N - bias_col0)
+    return fail(SISA_ERR_VALUE, "sisa_gemm_bias_cols: columns [%lld, %lld) lie outside [0, N=%lld)",
+                (long long)bias_col0, (long long)(bias_col0 + bias_ncols), (long long)N);
+  if (bias_round != 0 && bias_round != 1)
+    return fail(SISA_ERR_VALUE, "sisa_gemm_bias_cols: bias_round is 0 or 1");
+  if (bias_round && out_dtype != dtype)
+    return fail(SISA_ERR_VALUE, "sisa_gemm_bias_cols: bias_round needs a 16-bit output of the operands' type");
+  if (bias_ncols == 0) bias = nullptr;      // no column takes a bias
+  const int vec = aligned16(bias) && bias_col0 % 8 == 0;
+  return gemm_impl("sisa_gemm_bias_cols", a, lda, a_mn, b, ldb, b_mn, c, ldc, M, N, K, dtype, out_dtype, accumulate,
+                   bias, bias_dtype, bias_col0, bias_col0 + bias_ncols, vec, bias_round, workspace, workspace_bytes,
+                   status, stream);
 }
 
 // ------------------------------------------------------------------------------------ norm, SwiGLU

@@ -194,31 +194,45 @@ __device__ __forceinline__ uint32_t stage_and_store(const GemmParams& p, const u
   return box;
 }
 
-// bias[col .. col + 7] as fp32 (0 beyond N); the same address in every lane (a broadcast load).
+// The bias of columns col .. col + 7 as fp32: bias[c - bias_c0] inside [bias_c0, bias_c1), 0 outside; the
+// same address in every lane (a broadcast load). The type is branched on once per call, not per value.
+template <bool kRoundHalf>
 __device__ __forceinline__ void load_bias8(const GemmParams& p, int col, float* b) {
-  if (col + 8 <= p.N) {
+  const int i0 = col - p.bias_c0;
+  if (p.bias_vec && i0 >= 0 && col + 8 <= p.bias_c1) {
     if (p.bias_dtype == 2) {
-      const float4 a = reinterpret_cast<const float4*>(p.bias)[col / 4], c = reinterpret_cast<const float4*>(p.bias)[col / 4 + 1];
+      const float4 a = reinterpret_cast<const float4*>(p.bias)[i0 / 4], c = reinterpret_cast<const float4*>(p.bias)[i0 / 4 + 1];
       b[0] = a.x; b[1] = a.y; b[2] = a.z; b[3] = a.w; b[4] = c.x; b[5] = c.y; b[6] = c.z; b[7] = c.w;
     } else {
-      const uint4 u = reinterpret_cast<const uint4*>(p.bias)[col / 8];
+      const uint4 u = reinterpret_cast<const uint4*>(p.bias)[i0 / 8];
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+      if (p.bias_dtype == 1) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        b[2 * i] = p.bias_dtype == 1 ? unpack_lo<true>(w[i]) : unpack_lo<false>(w[i]);
-        b[2 * i + 1] = p.bias_dtype == 1 ? unpack_hi<true>(w[i]) : unpack_hi<false>(w[i]);
+        for (int i = 0; i < 4; ++i) { b[2 * i] = unpack_lo<true>(w[i]); b[2 * i + 1] = unpack_hi<true>(w[i]); }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) { b[2 * i] = unpack_lo<false>(w[i]); b[2 * i + 1] = unpack_hi<false>(w[i]); }
       }
     }
   } else {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       const int c = col + i;
-      b[i] = c >= p.N ? 0.f
-             : p.bias_dtype == 2 ? static_cast<const float*>(p.bias)[c]
-             : p.bias_dtype == 1 ? __half2float(static_cast<const __half*>(p.bias)[c])
-                                 : __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[c]);
+      b[i] = c < p.bias_c0 || c >= p.bias_c1 ? 0.f
+             : p.bias_dtype == 2 ? static_cast<const float*>(p.bias)[c - p.bias_c0]
+             : p.bias_dtype == 1 ? __half2float(static_cast<const __half*>(p.bias)[c - p.bias_c0])
+                                 : __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[c - p.bias_c0]);
     }
   }
+  if (p.bias_round) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) b[i] = round_lp<kRoundHalf>(b[i]);
+  }
+}
+
+// Whether the n columns from col meet the bias's columns (boxes outside them skip the bias).
+__device__ __forceinline__ bool bias_meets(const GemmParams& p, int col, int n) {
+  return col < p.bias_c1 && col + n > p.bias_c0;
 }
 
 // Epilogue EPI_STORE of 32 fp32 values per thread already in registers (the summed split-K slices).
@@ -228,11 +242,11 @@ __device__ __forceinline__ void epilogue_store_values(const GemmParams& p, const
   float v[32];
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = vin[i];
-  if (add_bias) {
+  if (add_bias && bias_meets(p, col, 32)) {
 #pragma unroll
     for (int j = 0; j < 32; j += 8) {
       float b[8];
-      load_bias8(p, col + j, b);
+      load_bias8<false>(p, col + j, b);
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[j + i] += b[i];
     }
@@ -253,11 +267,11 @@ __device__ __forceinline__ void epilogue_store(const GemmParams& p, uint32_t tad
   tmem_ld32(taddr, v);
   if constexpr (NV == 64) tmem_ld32(taddr + 32u, v + 32);
   tmem_wait_ld();
-  if (add_bias) {
+  if (add_bias && bias_meets(p, col, NV)) {
 #pragma unroll
     for (int j = 0; j < NV; j += 8) {
       float b[8];
-      load_bias8(p, col + j, b);
+      load_bias8<OUT == GEMM_OUT_F16>(p, col + j, b);
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[j + i] += b[i];
     }

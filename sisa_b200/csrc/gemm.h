@@ -19,6 +19,10 @@ struct GemmParams {
   int32_t* status;
   const void* bias;     // optional, per column of C, added in fp32 before the output rounding
   int bias_dtype;       // 0 bf16, 1 fp16, 2 fp32
+  // the bias covers columns [bias_c0, bias_c1) (bias[c - bias_c0]; zero elsewhere); bias_vec: 16-byte
+  // loads allowed (aligned pointer, bias_c0 a multiple of 8); bias_round: round each bias value to the
+  // 16-bit output type before the add
+  int bias_c0, bias_c1, bias_vec, bias_round;
   // split-K (fp32 output, narrow tiles): K is cut into k_split slices of kb_split 64-wide blocks; each
   // slice writes its partial to the workspace and the last of a tile's slices (counted in sema, zero at
   // launch) sums them in slice order and stores C

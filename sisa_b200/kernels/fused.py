@@ -102,13 +102,14 @@ class _FusedProjFn(torch.autograd.Function):
         col_a = fused_layout(H)["A"]
         xc = x.to(dtype)
         wc = _cached_wcat(owner, weights, dtype, train)
-        bias = torch.zeros((wc.shape[0],), dtype=dtype, device=x.device)
-        bias[col_a:col_a + H] = b_alpha.to(dtype)
         d = xc.shape[-1]
         x2 = xc.reshape(-1, d)
         out = torch.empty((x2.shape[0], wc.shape[0]), dtype=dtype, device=x.device)
         if x2.shape[0]:
-            matmul_t(x2 if x2.stride(-1) == 1 else x2.contiguous(), wc, out, bias=bias)
+            # b_cat is zero outside the alpha columns: the alpha bias goes to the GEMM as stored, rounded
+            # to the compute dtype in the epilogue (autocast's cast of the bias)
+            matmul_t(x2 if x2.stride(-1) == 1 else x2.contiguous(), wc, out, bias=b_alpha.contiguous(),
+                     bias_col0=col_a, bias_round=True)
         out = out.view(*xc.shape[:-1], wc.shape[0])
         ctx.save_for_backward(xc, wc)
         ctx.col_a, ctx.H = col_a, H

@@ -51,11 +51,15 @@ def _operand(t: Tensor, name: str) -> tuple[int, int]:
 
 
 def matmul_t(a: Tensor, b: Tensor, out: Tensor | None = None, *, accumulate: bool = False,
-             out_dtype: torch.dtype = torch.float32, bias: Tensor | None = None) -> Tensor:
+             out_dtype: torch.dtype = torch.float32, bias: Tensor | None = None, bias_col0: int | None = None,
+             bias_round: bool = False) -> Tensor:
     """``out (+)= a @ b.T (+ bias)`` for ``a`` (M, K) and ``b`` (N, K) CUDA tensors of one dtype (bf16 or
     fp16), each with a unit stride along K or along its rows (so ``x.t()`` of a row-major tensor is
     taken as it lies). ``out`` (M, N) with unit column stride; ``accumulate`` adds to it (fp32 only);
-    ``bias`` (N,) contiguous bf16/fp16/fp32 is added in fp32 before the output's rounding. Row strides
+    ``bias`` (N,) contiguous bf16/fp16/fp32 is added in fp32 before the output's rounding. With
+    ``bias_col0``, ``bias`` (n,) covers only columns [bias_col0, bias_col0 + n) and the others get no bias
+    (``sisa_gemm_bias_cols``: tiles away from those columns skip the bias); ``bias_round`` then rounds
+    each bias value to the output's 16-bit type first, as autocast casts a linear's bias. Row strides
     must be whole 16-byte units and pointers 16-byte aligned (errors come back from the C ABI)."""
     if a.dtype != b.dtype:
         raise TypeError(f"operands differ in dtype: {a.dtype} and {b.dtype}")
@@ -75,15 +79,25 @@ def matmul_t(a: Tensor, b: Tensor, out: Tensor | None = None, *, accumulate: boo
     a_mn, lda = _operand(a, "a")
     b_mn, ldb = _operand(b, "b")
     ldc = out.stride(0) if M > 1 else -(-N // 8) * 8
-    if bias is not None and (bias.shape != (N,) or not bias.is_contiguous() or bias.dtype not in _OUT_CODES):
-        raise ValueError(f"bias must be a contiguous ({N},) bf16/fp16/fp32 tensor, got {tuple(bias.shape)} {bias.dtype}")
     lib = _lib.load()
     dev = a.device
     ws = _workspace(dev, M, N, K, _OUT_CODES[out.dtype])
+    ws_ptr, ws_n = (None, 0) if ws is None else (ws.data_ptr(), ws.numel())
+    if bias_col0 is not None:
+        if bias is None or bias.dim() != 1 or not bias.is_contiguous() or bias.dtype not in _OUT_CODES:
+            raise ValueError("bias_col0 needs a contiguous 1-D bf16/fp16/fp32 bias")
+        _lib.check(lib.sisa_gemm_bias_cols(a.data_ptr(), lda, a_mn, b.data_ptr(), ldb, b_mn, out.data_ptr(), ldc, M, N,
+                                           K, _lib.dtype_code(a.dtype), _OUT_CODES[out.dtype], int(accumulate),
+                                           bias.data_ptr(), _OUT_CODES[bias.dtype], bias_col0, bias.numel(),
+                                           int(bias_round), ws_ptr, ws_n, backends.status_word(dev).data_ptr(),
+                                           _lib.stream_ptr(dev)), "sisa_gemm_bias_cols")
+        backends.after_call(dev)
+        return out
+    if bias is not None and (bias.shape != (N,) or not bias.is_contiguous() or bias.dtype not in _OUT_CODES):
+        raise ValueError(f"bias must be a contiguous ({N},) bf16/fp16/fp32 tensor, got {tuple(bias.shape)} {bias.dtype}")
     _lib.check(lib.sisa_gemm(a.data_ptr(), lda, a_mn, b.data_ptr(), ldb, b_mn, out.data_ptr(), ldc, M, N, K,
                              _lib.dtype_code(a.dtype), _OUT_CODES[out.dtype], int(accumulate),
                              None if bias is None else bias.data_ptr(), 0 if bias is None else _OUT_CODES[bias.dtype],
-                             None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(),
-                             backends.status_word(dev).data_ptr(), _lib.stream_ptr(dev)), "sisa_gemm")
+                             ws_ptr, ws_n, backends.status_word(dev).data_ptr(), _lib.stream_ptr(dev)), "sisa_gemm")
     backends.after_call(dev)
     return out

@@ -152,6 +152,22 @@ def test_gemm_entry_points_reject_bad_arguments_before_any_cuda_call():
         return lib.sisa_gemm_swiglu(a["x"], a["xld"], a["w"], a["wld"], a["gu"], a["guld"], a["a"], a["ald"],
                                     a["rows"], a["dff"], a["K"], a["dtype"], None, None)
 
+    def gemm_cols(bias=A, bias_dtype=_lib.F32, col0=0, n=8, rnd=0, **kw):
+        a = dict(ok, **kw)
+        return lib.sisa_gemm_bias_cols(a["a"], a["lda"], a["a_mn"], a["b"], a["ldb"], a["b_mn"], a["c"], a["ldc"],
+                                       a["M"], a["N"], a["K"], a["dtype"], a["out"], a["acc"], bias, bias_dtype,
+                                       col0, n, rnd, a["ws"], a["ws_bytes"], None, None)
+
+    # each call below fails a host check before anything could reach the device
+    assert gemm_cols(bias=None) == _lib.ERR_VALUE and "null bias" in _lib.last_error()
+    assert gemm_cols(bias_dtype=7) == _lib.ERR_TYPE
+    assert gemm_cols(bias=A + 2) == _lib.ERR_ALIGN                   # fp32 bias off a 4-byte boundary
+    assert gemm_cols(col0=60, n=8) == _lib.ERR_VALUE and "outside" in _lib.last_error()   # past N = 64
+    assert gemm_cols(col0=-1) == _lib.ERR_VALUE
+    assert gemm_cols(rnd=2) == _lib.ERR_VALUE
+    assert gemm_cols(rnd=1) == _lib.ERR_VALUE and "bias_round" in _lib.last_error()       # fp32 output
+    assert gemm_cols(a=None) == _lib.ERR_VALUE and "sisa_gemm_bias_cols" in _lib.last_error()
+
     assert swiglu(dff=36) == _lib.ERR_VALUE and "multiple of 8" in _lib.last_error()
     assert swiglu(a=None) == _lib.ERR_VALUE                      # gu may be NULL (inference), a may not
     assert swiglu(guld=72) == _lib.ERR_ALIGN                      # gu rows must hold 2 d_ff

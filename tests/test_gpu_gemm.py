@@ -177,3 +177,27 @@ def test_gemm_bias_epilogue(cuda_dev, tile, bias_dtype, out_dtype):
     torch.cuda.synchronize()
     want = c32.cpu() + bias.float()                          # the fp32 result plus the bias, rounded once
     assert torch.equal(c.cpu(), want.to(out_dtype))
+
+
+@pytest.mark.parametrize("dtype,bias_dtype,rnd", [(torch.bfloat16, torch.float32, True),
+                                                  (torch.bfloat16, torch.bfloat16, False),
+                                                  (torch.float16, torch.float32, True)])
+@pytest.mark.parametrize("col0,n", [(0, 3280), (3100, 12), (248, 16), (1000, 0)])
+def test_gemm_bias_columns(cuda_dev, tile, dtype, bias_dtype, rnd, col0, n):
+    """``sisa_gemm_bias_cols``: a bias over columns [col0, col0 + n) only (the fused projection's alpha
+    bias), optionally rounded to the output type first, equals the fp32 product plus that bias rounded
+    once; ranges on and off 8-column boundaries, across a tile edge, and empty."""
+    from sisa_b200.kernels.gemm import matmul_t
+
+    M, N, K = 600, 3280, 768
+    a, b, da, db = _operands(M, N, K, 0, 0, dtype, cuda_dev, seed=23)
+    bias = (torch.randn(n, generator=torch.Generator().manual_seed(24)) * 3).to(bias_dtype)
+    c = matmul_t(da, db, out_dtype=dtype, bias=bias.to(cuda_dev), bias_col0=col0, bias_round=rnd)
+    c32 = matmul_t(da, db)
+    torch.cuda.synchronize()
+    full = torch.zeros(N)
+    full[col0:col0 + n] = bias.to(dtype).float() if rnd else bias.float()
+    want = (c32.cpu() + full).to(dtype)
+    assert torch.equal(c.cpu(), want)
+    from sisa_b200 import backends
+    assert int(backends.status_word(cuda_dev).item()) == 0
