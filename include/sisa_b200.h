@@ -248,6 +248,15 @@ int sisa_adamw_tensors(const sisa_adam_tensor* tensors, int ntensors, float* m, 
 int sisa_copy_heads(const void* src, int64_t src_sb, int64_t src_sh, int64_t src_sl, void* dst, int64_t dst_sb,
                     int64_t dst_sh, int64_t dst_sl, int64_t B, int64_t H, int64_t L, int64_t width, void* stream);
 
+/* sisa_split_rows: two fp32 matrices out of one buffer that interleaves them in blocks of `block`
+ * rows (block 0 of matrix 0, block 0 of matrix 1, block 1 of matrix 0, ...): dst_h[r, :] =
+ * src[(r / block) 2 block + h block + r % block, :] for r < rows, h = 0, 1. The gate and up weight
+ * gradients out of the one dW GEMM over their 8-row-interleaved weight (the two weight gradients of
+ * src/sisa/modeling.py:39-49). rows a multiple of block, cols a multiple of 4, pointers 16-byte
+ * aligned, row strides multiples of 4 and >= cols. */
+int sisa_split_rows(const float* src, int64_t src_ld, float* dst0, float* dst1, int64_t dst_ld, int64_t rows,
+                    int64_t cols, int64_t block, void* stream);
+
 typedef struct sisa_row_copy {
   const float* src;
   void* dst;

@@ -765,6 +765,27 @@ int sisa_copy_heads(const void* src, int64_t src_sb, int64_t src_sh, int64_t src
   return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_copy_heads launch");
 }
 
+int sisa_split_rows(const float* src, int64_t src_ld, float* dst0, float* dst1, int64_t dst_ld, int64_t rows,
+                    int64_t cols, int64_t block, void* stream) {
+  if (!src || !dst0 || !dst1) return fail(SISA_ERR_VALUE, "sisa_split_rows: null pointer");
+  if (rows < 0 || cols < 0 || block < 1 || rows % block || cols % 4 || src_ld < cols || dst_ld < cols ||
+      rows > ((int64_t)1 << 40) / (cols > 0 ? cols : 1))
+    return fail(SISA_ERR_VALUE, "sisa_split_rows: need rows a multiple of block >= 1, cols a multiple of 4 and "
+                "row strides >= cols (rows=%lld cols=%lld block=%lld)", (long long)rows, (long long)cols,
+                (long long)block);
+  if (!aligned16(src) || !aligned16(dst0) || !aligned16(dst1) || src_ld % 4 || dst_ld % 4)
+    return fail(SISA_ERR_ALIGN, "sisa_split_rows: pointers must be 16-byte aligned and row strides multiples of 4");
+  if (rows == 0 || cols == 0) return SISA_OK;
+  int rc;
+  sisa::DeviceScope scope;
+  if ((rc = scope.bind(dst0))) return rc;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, scope.device());
+  const sisa::SplitRows p{src, dst0, dst1, rows, cols, src_ld, dst_ld, block};
+  cudaError_t e = sisa::launch_split_rows(p, sms, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_split_rows launch");
+}
+
 int sisa_copy_rows(const sisa_row_copy* jobs, int njobs, int64_t max_vectors, int dtype, int32_t* status,
                    void* stream) {
   (void)status;

@@ -3,7 +3,9 @@
 // change after every optimizer step and were otherwise refreshed by one small cast kernel per weight.
 //
 // copy_heads_kernel moves per-head rows of 16-bit elements between two (batch, head, position)
-// layouts: the prompt's keys, values and rotated B~ into a decode cache's buffers.
+// layouts: the prompt's keys, values and rotated B~ into a decode cache's buffers. split_rows_kernel
+// takes two fp32 matrices out of a buffer that interleaves them in blocks of rows: the weight gradients
+// of the gate and up projections out of the one gradient GEMM over their interleaved weight.
 //
 // Job j (one row of the grid's y dimension) copies source rows r = 0 .. rows-1 of `cols` fp32 values to
 // destination row (r / block_rows) * dst_block_stride + r % block_rows, rounding to nearest even; a job
@@ -55,7 +57,31 @@ __global__ void __launch_bounds__(256) copy_heads_kernel(HeadsCopy p) {
   }
 }
 
+// dst_h[r, :] = src[(r / block) 2 block + h block + r % block, :]: thread i moves 16-byte vector i of
+// the 2 * rows * cols / 4 destination vectors (the two destinations one after the other).
+__global__ void __launch_bounds__(256) split_rows_kernel(SplitRows p) {
+  const int64_t vpr = p.cols / 4;
+  const int64_t n = 2 * p.rows * vpr;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t hr = i / vpr, v = i - hr * vpr;
+    const int h = hr >= p.rows ? 1 : 0;
+    const int64_t r = hr - h * p.rows;
+    const int64_t sr = (r / p.block) * 2 * p.block + h * p.block + r % p.block;
+    const float4 x = *reinterpret_cast<const float4*>(p.src + sr * p.src_ld + 4 * v);
+    *reinterpret_cast<float4*>((h ? p.dst1 : p.dst0) + r * p.dst_ld + 4 * v) = x;
+  }
+}
+
 }  // namespace copy
+
+cudaError_t launch_split_rows(const SplitRows& p, int num_sms, cudaStream_t st) {
+  const int64_t n = 2 * p.rows * (p.cols / 4);
+  if (n == 0) return cudaSuccess;
+  int64_t grid = (n + 255) / 256;
+  if (grid > 8 * (int64_t)num_sms) grid = 8 * (int64_t)num_sms;
+  copy::split_rows_kernel<<<(unsigned)grid, 256, 0, st>>>(p);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_copy_heads(const HeadsCopy& p, int num_sms, cudaStream_t st) {
   const int64_t rows = p.B * p.L;

@@ -26,4 +26,14 @@ struct HeadsCopy {
 };
 cudaError_t launch_copy_heads(const HeadsCopy& p, int num_sms, cudaStream_t st);
 
+// Rows of fp32 values taken out of a buffer that interleaves two matrices in blocks of `block` rows
+// (block of matrix 0, block of matrix 1, ...): dst_h row r = src row (r / block) 2 block + h block + r % block.
+struct SplitRows {
+  const float* src;
+  float* dst0;
+  float* dst1;
+  int64_t rows, cols, src_ld, dst_ld, block;     // rows of each destination
+};
+cudaError_t launch_split_rows(const SplitRows& p, int num_sms, cudaStream_t st);
+
 }  // namespace sisa

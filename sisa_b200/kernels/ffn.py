@@ -99,9 +99,16 @@ class _GateUpFn(torch.autograd.Function):
             dh = torch.mm(dgu, w_il).view(h_shape).to(h_dtype)
         if ctx.needs_input_grad[1] or ctx.needs_input_grad[2]:
             dw = torch.mm(dgu.t(), h2, out_dtype=torch.float32).view(d_ff // BLOCK, 2, BLOCK, d)
-            if ctx.needs_input_grad[1]:
+            if ctx.needs_input_grad[1] and ctx.needs_input_grad[2]:
+                # one launch takes both weights' rows out of the interleaved dW (sisa_split_rows)
+                dwg = torch.empty((d_ff, d), dtype=torch.float32, device=dw.device)
+                dwu = torch.empty_like(dwg)
+                _lib.check(_lib.load().sisa_split_rows(dw.data_ptr(), d, dwg.data_ptr(), dwu.data_ptr(), d, d_ff, d,
+                                                       BLOCK, _lib.stream_ptr(dw.device)), "sisa_split_rows")
+                dwg, dwu = dwg.to(g_dtype), dwu.to(u_dtype)
+            elif ctx.needs_input_grad[1]:
                 dwg = dw[:, 0].reshape(d_ff, d).to(g_dtype)
-            if ctx.needs_input_grad[2]:
+            else:
                 dwu = dw[:, 1].reshape(d_ff, d).to(u_dtype)
         return dh, dwg, dwu, None, None, None
 

@@ -180,6 +180,23 @@ def test_gemm_entry_points_reject_bad_arguments_before_any_cuda_call():
     assert lib.sisa_lce_seed_scale(A + 4, 16, A, None, _lib.F32, None, None) == _lib.ERR_ALIGN
 
 
+def test_split_rows_is_checked_on_the_host():
+    """sisa_split_rows rejects bad shapes and alignment before any CUDA call (fake addresses)."""
+    lib = _lib.load()
+    A, B, C = 0x10000, 0x20000, 0x30000
+
+    def split(src=A, sld=8, d0=B, d1=C, dld=8, rows=16, cols=8, block=8):
+        return lib.sisa_split_rows(src, sld, d0, d1, dld, rows, cols, block, None)
+
+    assert split(src=None) == _lib.ERR_VALUE and "null" in _lib.last_error()
+    assert split(rows=12) == _lib.ERR_VALUE                       # not a multiple of the block
+    assert split(cols=6) == _lib.ERR_VALUE
+    assert split(block=0) == _lib.ERR_VALUE
+    assert split(sld=6, cols=4) == _lib.ERR_ALIGN                  # row stride not a multiple of 4
+    assert split(d1=C + 4) == _lib.ERR_ALIGN
+    assert split(rows=0) == _lib.OK                                # nothing to do, no launch
+
+
 def test_row_copy_jobs_are_checked_on_the_host():
     """sisa_row_copy_check accepts well-formed jobs and names what is wrong with the others;
     sisa_copy_rows rejects a bad table pointer or dtype before any CUDA call (fake addresses)."""

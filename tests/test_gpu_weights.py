@@ -173,3 +173,23 @@ def test_copy_heads_equals_torch_copy(cuda_dev, dtype):
         want[:, :, 40:40 + L].copy_(src)
         torch.cuda.synchronize()
         assert torch.equal(dst, want)
+
+
+@pytest.mark.parametrize("rows,cols,block,pad", [(2744, 768, 8, 0), (64, 12, 8, 4), (6, 4, 1, 0)])
+def test_split_rows_equals_torch_slicing(cuda_dev, rows, cols, block, pad):
+    """sisa_split_rows takes the two matrices out of a block-interleaved buffer (the gate/up weight
+    gradients: blocks of 8 rows) bit for bit as torch's slicing does, with padded row strides too."""
+    from sisa_b200 import _lib
+
+    gen = torch.Generator(device=cuda_dev).manual_seed(9)
+    ld = cols + pad
+    src = torch.randn((2 * rows, ld), generator=gen, device=cuda_dev)
+    d0 = torch.full((rows, ld), -7.0, device=cuda_dev)
+    d1 = torch.full((rows, ld), -7.0, device=cuda_dev)
+    _lib.check(_lib.load().sisa_split_rows(src.data_ptr(), ld, d0.data_ptr(), d1.data_ptr(), ld, rows, cols, block,
+                                           _lib.stream_ptr(cuda_dev)), "sisa_split_rows")
+    torch.cuda.synchronize()
+    blocks = src[:, :cols].view(rows // block, 2, block, cols)
+    assert torch.equal(d0[:, :cols], blocks[:, 0].reshape(rows, cols))
+    assert torch.equal(d1[:, :cols], blocks[:, 1].reshape(rows, cols))
+    assert bool((d0[:, cols:] == -7.0).all()) and bool((d1[:, cols:] == -7.0).all())   # padding untouched
