@@ -257,6 +257,16 @@ int sisa_copy_heads(const void* src, int64_t src_sb, int64_t src_sh, int64_t src
 int sisa_split_rows(const float* src, int64_t src_ld, float* dst0, float* dst1, int64_t dst_ld, int64_t rows,
                     int64_t cols, int64_t block, void* stream);
 
+/* The token embedding's weight gradient (the backward of nn.Embedding in src/sisa/modeling.py, whose
+ * weight the tied LM head shares): dw[v, :] = sum of grad[i, :] over the positions i < n with
+ * ids[i] = v, summed in increasing i (the same bits on every run; no sort, no atomics), every row of
+ * dw written (zero where no id falls). ids outside [0, V) add nothing. Each of the kernel's blocks scans
+ * all ids, so n is bounded: n <= SISA_EMBED_MAX_IDS. grad: n rows of D fp32 values, row stride grad_ld;
+ * dw: V x D fp32 contiguous. D a multiple of 4, dw and grad 16-byte aligned, grad_ld a multiple of 4. */
+#define SISA_EMBED_MAX_IDS 262144
+int sisa_embedding_bwd(const int64_t* ids, int64_t n, const float* grad, int64_t grad_ld, float* dw, int64_t V,
+                       int64_t D, void* stream);
+
 typedef struct sisa_row_copy {
   const float* src;
   void* dst;

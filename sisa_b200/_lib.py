@@ -109,6 +109,7 @@ SIGNATURES = {
     "sisa_gemm_swiglu": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _I64, _I64, _I64, _I, _P, _P]),
     "sisa_gemm_workspace": (_I64, [_I64, _I64, _I64, _I]),
     "sisa_split_rows": (_I, [_P, _I64, _P, _P, _I64, _I64, _I64, _I64, _P]),
+    "sisa_embedding_bwd": (_I, [_P, _I64, _P, _I64, _P, _I64, _I64, _P]),
     "sisa_gemm": (_I, [_P, _I64, _I, _P, _I64, _I, _P, _I64, _I64, _I64, _I64, _I, _I, _I, _P, _I, _P, _I64, _P, _P]),
     "sisa_gemm_bias_cols": (_I, [_P, _I64, _I, _P, _I64, _I, _P, _I64, _I64, _I64, _I64, _I, _I, _I, _P, _I, _I64, _I64,
                                  _I, _P, _I64, _P, _P]),

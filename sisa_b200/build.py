@@ -18,7 +18,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 OUT_DIR = PKG / "_lib"
 LIB = OUT_DIR / "libsisa_b200.so"
-SOURCES = ["prep.cu", "attn_fwd.cu", "attn_bwd.cu", "lce.cu", "gemm.cu", "decode.cu", "norm.cu", "optim.cu", "copy.cu", "selftest.cu", "capi.cu"]
+SOURCES = ["prep.cu", "attn_fwd.cu", "attn_bwd.cu", "lce.cu", "gemm.cu", "decode.cu", "norm.cu", "optim.cu", "copy.cu", "embed.cu", "selftest.cu", "capi.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I", str(ROOT / "include"), "-I", str(CSRC)]
 

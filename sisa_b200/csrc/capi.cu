@@ -19,6 +19,7 @@
 #include "gemm.h"
 #include "optim.h"
 #include "copy.h"
+#include "embed.h"
 #include "norm.h"
 #include "capi_util.h"
 
@@ -763,6 +764,25 @@ int sisa_copy_heads(const void* src, int64_t src_sb, int64_t src_sh, int64_t src
   const sisa::HeadsCopy p{src, src_sb, src_sh, src_sl, dst, dst_sb, dst_sh, dst_sl, B, H, L, width};
   cudaError_t e = sisa::launch_copy_heads(p, sms, static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_copy_heads launch");
+}
+
+int sisa_embedding_bwd(const int64_t* ids, int64_t n, const float* grad, int64_t grad_ld, float* dw, int64_t V,
+                       int64_t D, void* stream) {
+  if ((n > 0 && (!ids || !grad)) || !dw) return fail(SISA_ERR_VALUE, "sisa_embedding_bwd: null pointer");
+  if (n < 0 || n > SISA_EMBED_MAX_IDS || V < 1 || V > ((int64_t)1 << 31) - 1 || D < 4 || D % 4 || grad_ld < D)
+    return fail(SISA_ERR_VALUE, "sisa_embedding_bwd: need 0 <= n <= %d, 1 <= V < 2^31, D a positive multiple of 4 "
+                "and grad_ld >= D (n=%lld V=%lld D=%lld)", SISA_EMBED_MAX_IDS, (long long)n, (long long)V, (long long)D);
+  if (!aligned16(dw) || (n > 0 && (!aligned16(grad) || grad_ld % 4 || reinterpret_cast<uintptr_t>(ids) % 8)))
+    return fail(SISA_ERR_ALIGN, "sisa_embedding_bwd: dw and grad 16-byte aligned, grad_ld a multiple of 4, ids 8-byte "
+                "aligned");
+  int rc;
+  sisa::DeviceScope scope;
+  if ((rc = scope.bind(dw))) return rc;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, scope.device());
+  const sisa::EmbedBwd p{ids, grad, dw, n, V, D, grad_ld, 0};
+  cudaError_t e = sisa::launch_embed_bwd(p, sms, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? SISA_OK : cuda_fail(e, "sisa_embedding_bwd launch");
 }
 
 int sisa_split_rows(const float* src, int64_t src_ld, float* dst0, float* dst1, int64_t dst_ld, int64_t rows,

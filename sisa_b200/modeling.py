@@ -544,8 +544,18 @@ class SISAModel(nn.Module):
         for layer in self.layers:
             layer.reset_parameters()
 
+    def _lookup(self, input_ids: Tensor) -> Tensor:
+        """The token embedding; a plain ``nn.Embedding`` (no padding index, norm limit or frequency
+        scaling) takes its weight gradient from the deterministic CUDA kernel (``kernels.embedding``)."""
+        e = self.embed
+        if e.padding_idx is None and e.max_norm is None and not e.scale_grad_by_freq and not e.sparse:
+            from .kernels.embedding import embedding
+
+            return embedding(input_ids, e.weight)
+        return e(input_ids)
+
     def forward(self, input_ids: Tensor, *, cache: "SISACache | None" = None) -> Tensor:
-        x = self.embed(input_ids)
+        x = self._lookup(input_ids)
         use_ckpt = self.config.gradient_checkpointing and self.training and cache is None and torch.is_grad_enabled()
         if cache is None and len(self.layers) and self.layers[0].fused_path(x):
             from .kernels.weights import refresh

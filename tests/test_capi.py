@@ -197,6 +197,25 @@ def test_split_rows_is_checked_on_the_host():
     assert split(rows=0) == _lib.OK                                # nothing to do, no launch
 
 
+def test_embedding_grad_is_checked_on_the_host():
+    """sisa_embedding_bwd rejects bad sizes and alignment before any CUDA call (fake addresses)."""
+    lib = _lib.load()
+    A, B, C = 0x10000, 0x20000, 0x30000
+
+    def bwd(ids=A, n=16, grad=B, ld=8, dw=C, V=10, D=8):
+        return lib.sisa_embedding_bwd(ids, n, grad, ld, dw, V, D, None)
+
+    assert bwd(dw=None) == _lib.ERR_VALUE and "null" in _lib.last_error()
+    assert bwd(ids=None) == _lib.ERR_VALUE
+    assert bwd(n=262145) == _lib.ERR_VALUE                         # past SISA_EMBED_MAX_IDS
+    assert bwd(D=6, ld=8) == _lib.ERR_VALUE                        # D a multiple of 4
+    assert bwd(ld=4) == _lib.ERR_VALUE                             # row stride below D
+    assert bwd(V=0) == _lib.ERR_VALUE
+    assert bwd(ld=10, D=8) == _lib.ERR_ALIGN
+    assert bwd(grad=B + 8) == _lib.ERR_ALIGN
+    assert bwd(ids=A + 4) == _lib.ERR_ALIGN
+
+
 def test_row_copy_jobs_are_checked_on_the_host():
     """sisa_row_copy_check accepts well-formed jobs and names what is wrong with the others;
     sisa_copy_rows rejects a bad table pointer or dtype before any CUDA call (fake addresses)."""
