@@ -801,13 +801,20 @@ def run_gemm(args):
 
 
 def run_train_only(args):
-    """Only the config 3 training leg (one GPU, the whole step as one CUDA graph)."""
-    dev = torch.device("cuda", 0)
-    with Clocks(0) as clk:
+    """Only the config 3 training leg (the whole step as one CUDA graph per rank); under torchrun one
+    rank per GPU, data-parallel, like the train leg of the default run."""
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    with Clocks(local) as clk:
         with clk.window("train"):
-            out = run_train(args, 0, 1, dev)
+            out = run_train(args, rank, world, dev)
     out["clocks"] = clk.summary("train")
-    print(json.dumps(out))
+    if rank == 0:
+        print(json.dumps(out))
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
 
 
 def run_decode(args):
