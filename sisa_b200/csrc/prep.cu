@@ -116,12 +116,14 @@ __device__ __forceinline__ void load_elems(const PrepArgs& a, int b, int h, int 
   }
 }
 
+// One warp per head (up to 32 heads per block; more take further rounds), so that every head's loads
+// are in flight at once instead of eight warps walking the heads one after another.
 template <bool kHalf>
-__global__ void __launch_bounds__(256) prep_sums_kernel(PrepArgs a) {
+__global__ void __launch_bounds__(1024) prep_sums_kernel(PrepArgs a) {
   const int c = blockIdx.x, b = blockIdx.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   const int t0 = c * kBlk + 2 * lane;
-  for (int h = warp; h < a.H; h += 8) {
+  for (int h = warp; h < a.H; h += nwarps) {
     float la[2], lf[2], th[2][kS2];
     load_elems<kHalf>(a, b, h, t0, la, lf, th);
     float s0, s1, tv[kTot];
@@ -664,10 +666,11 @@ cudaError_t launch_prep_fwd(const PrepFwdLaunch& p, cudaStream_t st) {
   a.tot = p.tot; a.status = p.status;
   dim3 grid(a.nch, a.B);
   dim3 grid_rot((a.H + kHG - 1) / kHG, a.nch, a.B);
+  const int sums_threads = 32 * (a.H < 32 ? a.H : 32);
   if (p.dtype == 1) {
-    prep_sums_kernel<true><<<grid, 256, 0, st>>>(a);
+    prep_sums_kernel<true><<<grid, sums_threads, 0, st>>>(a);
   } else {
-    prep_sums_kernel<false><<<grid, 256, 0, st>>>(a);
+    prep_sums_kernel<false><<<grid, sums_threads, 0, st>>>(a);
   }
   const int64_t nchains = (int64_t)a.B * a.H * kTot;
   block_scan_kernel<float, false><<<(unsigned)((nchains + 7) / 8), 256, 0, st>>>(a.tot, nchains, a.nch);
