@@ -269,9 +269,10 @@ class SISAAttention(nn.Module):
         bsz, h, seq_len, dh = y.shape
         return self.W_O(y.transpose(1, 2).reshape(bsz, seq_len, h * dh))
 
-    def _forward_fused(self, x: Tensor, z: Tensor | None = None) -> Tensor:
+    def _forward_fused(self, x: Tensor, z: Tensor | None = None, lam: Tensor | None = None) -> Tensor:
         """Projection, layer core and output projection (modeling.py:213-222); ``z`` is the forget
-        projection of ``x`` when the caller computed it already (the fused block norm does)."""
+        projection of ``x`` when the caller computed it already (the fused block norm does), ``lam``
+        this layer's softplus(lambda_raw) when the caller computed every layer's at once."""
         from .kernels.fused import sisa_fused
 
         bsz, seq_len, d = x.shape
@@ -284,7 +285,8 @@ class SISAAttention(nn.Module):
         else:
             weight, bias = self.fused_weights()
             proj = F.linear(x, weight, bias)
-        y = sisa_fused(proj, self._forget_logits(x) if z is None else z, self.lam(), self.config.n_head)
+        y = sisa_fused(proj, self._forget_logits(x) if z is None else z, self.lam() if lam is None else lam,
+                       self.config.n_head)
         from .kernels.linear import linear_cast, supports
 
         if supports(y, self.W_O.weight, cd):
@@ -466,7 +468,7 @@ class SISABlock(nn.Module):
         gu = F.linear(f_in, w_gu)
         return xs, ffn.w_down(swiglu(gu[..., :d_ff], gu[..., d_ff:]))
 
-    def forward_pair(self, x: Tensor, m: Tensor | None) -> tuple[Tensor, Tensor]:
+    def forward_pair(self, x: Tensor, m: Tensor | None, lam: Tensor | None = None) -> tuple[Tensor, Tensor]:
         """The block on the fused path, with the previous block's last residual add ``x + m`` folded into
         this block's first norm. Returns ``(x + m + attn, ffn)``: the caller (the next block, or the
         final norm) adds the second term. Each norm also writes its output in the dtype of the linears
@@ -474,7 +476,7 @@ class SISABlock(nn.Module):
         nor the separate gradient sums of eager PyTorch run (kernels/norm.py ``block_norm``). The MLP's
         gate and up projections and its activation run as one GEMM (kernels/ffn.py) where the widths
         allow, else as two linears and the activation kernel, each linear fed its own copy of the norm
-        output."""
+        output. ``lam``: the attention's softplus(lambda_raw), when the caller computed it."""
         from .kernels.norm import block_norm
 
         cd = _compute_dtype(x)
@@ -485,7 +487,7 @@ class SISABlock(nn.Module):
             xs = x
         else:
             xs, h, z = block_norm(x, self.attn_norm.weight, self.attn_norm.eps, res=m, out_dtypes=(cd,), proj=fp)
-        a = attn._forward_fused(h, z)
+        a = attn._forward_fused(h, z, lam)
         from .kernels.ffn import supports
 
         if supports(x, self.ffn.w_gate.weight.shape[0], cd):
@@ -544,6 +546,17 @@ class SISAModel(nn.Module):
         for layer in self.layers:
             layer.reset_parameters()
 
+    def _layer_lams(self) -> tuple[Tensor, ...] | None:
+        """softplus(lambda_raw) of every layer in one launch (a stack and one softplus; one softplus
+        backward for all of them), when the layers' lambda_raw share dtype and device; else None and
+        each layer computes its own. The layers take their rows through ``unbind``, whose backward
+        stacks the rows' gradients in one launch (indexing would zero-fill and add once per layer)."""
+        raws = [layer.attn.lambda_raw for layer in self.layers]
+        if len(raws) < 2 or any(r.dtype != raws[0].dtype or r.device != raws[0].device or r.shape != raws[0].shape
+                                for r in raws):
+            return None
+        return F.softplus(torch.stack(raws)).float().unbind(0)
+
     def _lookup(self, input_ids: Tensor) -> Tensor:
         """The token embedding; a plain ``nn.Embedding`` (no padding index, norm limit or frequency
         scaling) takes its weight gradient from the deterministic CUDA kernel (``kernels.embedding``)."""
@@ -561,10 +574,12 @@ class SISAModel(nn.Module):
             from .kernels.weights import refresh
 
             refresh(self, _compute_dtype(x))        # every stale compute-dtype weight copy, one launch
+            lams = self._layer_lams()
             m = None
-            for layer in self.layers:
-                x, m = (checkpoint(layer.forward_pair, x, m, use_reentrant=False) if use_ckpt
-                        else layer.forward_pair(x, m))
+            for i, layer in enumerate(self.layers):
+                lam = None if lams is None else lams[i]
+                x, m = (checkpoint(layer.forward_pair, x, m, lam, use_reentrant=False) if use_ckpt
+                        else layer.forward_pair(x, m, lam))
             from .kernels.norm import block_norm
 
             return block_norm(x, self.final_norm.weight, self.final_norm.eps, res=m, keep_sum=False)[0]
@@ -649,7 +664,11 @@ class SISAForCausalLM(SISAModel):
                 raise ValueError("fused_ce=True needs CUDA tensors")
             from .kernels.linear_ce import linear_cross_entropy
 
-            loss = linear_cross_entropy(inputs.reshape(-1, inputs.shape[-1]), weight, targets.reshape(-1),
+            # every position with the next token as its label and the last position ignored: the same
+            # rows and loss as hidden[:, :-1] against labels[:, 1:], without copying the sliced hidden
+            # states forward and their gradient back
+            shifted = F.pad(targets, (0, 1), value=IGNORE_INDEX)
+            loss = linear_cross_entropy(hidden.reshape(-1, hidden.shape[-1]), weight, shifted.reshape(-1),
                                         ignore_index=IGNORE_INDEX)
             return SISAOutput(loss=loss)
         if not return_logits:
